@@ -1,0 +1,467 @@
+#!/usr/bin/env python
+"""bench.py -- decode-attention KV GB/s of BASELINE cfg 2 on 1..8 B200s (+ prefill TFLOP/s).
+
+Workload: one batched decode step of a Qwen3-ASR-1.7B-shaped
+decoder over 28 layers -- 256 independent sequences per GPU, KV lengths drawn
+uniformly from [1024, 8192] (seed 0), 16 Q / 8 KV heads, head_dim 128, RoPE theta 1e6,
+bf16 K / fp16 V cache ~N(0,1).  Per layer the step runs the fused QK-RMSNorm + RoPE +
+cache-append kernel for the new token of every sequence and the split-KV decode
+attention over [0, L+1).  Synthetic data; the cache (~135 GB) is far larger than L2,
+so no flush is needed between steps.
+
+Arms
+  default            libsmol_b200 on N GPUs (one process per GPU; weak scaling: every
+                     rank owns its own 256 sequences, no collective on the data path)
+  --impl reference   the reference's own CPU implementation (oracle/_ref, compiled
+                     from the reference sources) on the host cores, rank 0 only
+
+The JSON line carries `value` (device-timed, inputs resident), `e2e` (the same step
+through the C ABI with host buffers: H2D of q/k/v and D2H of the output inside the
+timed region), `roofline` of the decode kernel pair, `cpu_baseline`, `clocks`, and a
+`prefill` block with the cfg 5 causal prefill TFLOP/s (one layer, batch 4 x 32768).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "smol-genius_b200"))
+
+import numpy as np  # noqa: E402
+
+import workload  # noqa: E402
+
+METRIC = "decode attn KV GB/s (% of HBM peak); prefill TFLOP/s; at 1/2/4/8 B200 vs CPU"
+UNIT = "GB/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
+    ap.add_argument("--seqs", type=int, default=workload.CFG2["n_seqs"], help="sequences per GPU")
+    ap.add_argument("--layers", type=int, default=workload.CFG2["layers"])
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return dict(FALLBACK_PEAKS, source="fallback")
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+# ---------------------------------------------------------------------------
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def allreduce_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def gpu_index(local: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = [p for p in vis.split(",") if p.strip()]
+        if local < len(parts) and parts[local].strip().isdigit():
+            return int(parts[local])
+    return local
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's smol_causal_attention on the host cores
+# ---------------------------------------------------------------------------
+def cpu_reference_decode(lens: np.ndarray, seconds: float, threads: int | None = None) -> dict:
+    """Times the compiled reference (oracle/_ref) on cfg-2 decode of the first sequences,
+    one layer each, until `seconds` of work; GB/s counts bf16-equivalent KV bytes so it
+    is the same figure as the GPU's."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ctypes
+
+    import pyoracle
+    path = pyoracle.ref_path()
+    if path is None:
+        return {"unavailable": "compiled reference (oracle/_ref) not present"}
+    lib = ctypes.CDLL(path)
+    nproc = os.cpu_count() or 1
+    threads = threads or min(nproc, 16)
+    lib.smol_set_threads(ctypes.c_int(threads))
+    used = lib.smol_get_thread_count()
+    hq, hkv, hd = 16, 8, 128
+    rng = np.random.default_rng(7)
+    f = lib.smol_causal_attention
+    f.restype = None
+    f.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_int]
+    bufs = []
+    total_bytes, total_t, n_calls = 0, 0.0, 0
+    i = 0
+    while total_t < seconds and i < len(lens):
+        L = int(lens[i]) + 1
+        K = rng.standard_normal((L, hkv * hd), dtype=np.float32)
+        V = rng.standard_normal((L, hkv * hd), dtype=np.float32)
+        q = rng.standard_normal((1, hq * hd), dtype=np.float32)
+        out = np.zeros_like(q)
+        bufs.append((K, V))
+        t0 = time.perf_counter()
+        f(out.ctypes.data, q.ctypes.data, K.ctypes.data, V.ctypes.data, 1, L, hq, hkv, hd, 1 / np.sqrt(hd), L - 1)
+        total_t += time.perf_counter() - t0
+        total_bytes += L * hkv * hd * 2 * 2
+        n_calls += 1
+        i += 1
+        if i == len(lens):   # cycle over the sample again with fresh buffers freed
+            i = 0
+            bufs.clear()
+    return {"value": total_bytes / total_t / 1e9, "unit": UNIT, "cores": int(used), "nproc": nproc,
+            "kind": "reference",
+            "sample": f"{n_calls} single-query decode calls (cfg-2 lengths+1, 16/8 heads, hd 128, one layer each) "
+                      f"of smol_causal_attention from oracle/_ref, fp32 KV; GB/s counts bf16-equivalent KV bytes",
+            "seconds": total_t}
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    lens = workload.decode_lengths(workload.CFG2["n_seqs"], workload.CFG2["len_lo"], workload.CFG2["len_hi"], 0)
+    per_step = max(1.0, min(10.0, 120.0 / max(1, args.steps + args.warmup)))
+    vals = []
+    cb = None
+    for s in range(args.warmup + args.steps):
+        cb = cpu_reference_decode(lens, per_step)
+        if "unavailable" in cb:
+            print(json.dumps({"impl": "reference", "unavailable": cb["unavailable"]}))
+            return
+        if s >= args.warmup:
+            vals.append(cb["value"])
+    v = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "cfg2 batched decode attention (reference CPU, sampled sequences)",
+                       "lengths": "U[1024,8192] seed 0", "heads": "16/8", "head_dim": 128},
+            "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": cb["cores"], "kind": "reference",
+                             "sample": cb["sample"]},
+            "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def fill_randn(t, gen, chunk_rows=1 << 20):
+    import torch
+    for r in range(0, t.shape[0], chunk_rows):
+        seg = t[r:r + chunk_rows]
+        seg.copy_(torch.randn(seg.shape, device=t.device, generator=gen, dtype=torch.float32))
+
+
+def run_prefill(args, world, rank, pk):
+    """cfg 5 causal prefill, one layer: batch 4 x 32768, 16/8 heads, hd 128.  With N
+    GPUs rank r owns KV heads r*8/N.. (and their Q heads) and the per-rank outputs are
+    all-gathered over NCCL once per layer."""
+    import torch
+
+    import smol_b200
+    c = workload.CFG5
+    B, L, hq, hkv, hd = c["batch"], c["seq"], c["n_heads"], c["n_kv_heads"], c["head_dim"]
+    heads = workload.kv_head_groups(hkv, world, rank)
+    hkv_r = len(heads)
+    hq_r = hq // hkv * hkv_r
+    g = torch.Generator(device="cuda").manual_seed(55 + rank)
+    q = torch.randn((B, L, hq_r * hd), device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn((B, L, hkv_r * hd), device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn((B, L, hkv_r * hd), device="cuda", generator=g).to(torch.float16)
+    out = torch.empty((B, L, hq_r * hd), device="cuda")
+    gathered = torch.empty((world,) + tuple(out.shape), device="cuda") if world > 1 else None
+    stream = torch.cuda.current_stream()
+
+    def layer():
+        smol_b200.prefill_attention(out, q, k, v, B, L, L, hq_r, hkv_r, hd, 1 / np.sqrt(hd), stream=stream)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(gathered, out)
+
+    for _ in range(2):
+        layer()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    e0.record()
+    for _ in range(reps):
+        layer()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = allreduce_max(e0.elapsed_time(e1) / reps, world)
+    flops = workload.causal_flops_square(L, hq, hd) * B
+    tf = flops / (ms * 1e-3) / 1e12
+    smol_b200.check(smol_b200.last_error(), "prefill")
+    return {"workload": "cfg5 causal prefill, 1 layer, batch 4 x 32768, GQA 16/8, hd 128"
+                        + (f", KV heads split over {world} GPUs + NCCL all-gather of outputs" if world > 1 else ""),
+            "tflops": round(tf, 1), "ms_per_layer": round(ms, 3), "flops_per_layer": flops,
+            "frac_of_bf16_peak": round(tf / pk["bf16_tflops"], 4),
+            "peak": pk["bf16_tflops"], "peak_source": pk["source"], "kernel": "tcgen05 prefill_kernel<128>"}
+
+
+def run_ours(args):
+    import torch
+
+    import smol_b200
+    world, rank, local = dist_setup(args)
+    pk = peaks()
+    cfg = workload.CFG2
+    hq, hkv, hd, layers = cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"], args.layers
+    kv_dim = hkv * hd
+    n = args.seqs
+    lens = workload.decode_lengths(n, cfg["len_lo"], cfg["len_hi"], seed=0)   # same per rank: equal work
+    lay = workload.pool_layout(lens, layers, reserve=1)
+    max_len = int(lens.max())
+
+    prefill = None
+    if not args.no_prefill:
+        prefill = run_prefill(args, world, rank, pk)
+        torch.cuda.empty_cache()
+
+    # ---- device state: the pooled cache, weights, tables, per-layer indices ----
+    gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    k_pool = torch.empty((lay.rows, kv_dim), dtype=torch.bfloat16, device="cuda")
+    v_pool = torch.empty((lay.rows, kv_dim), dtype=torch.float16, device="cuda")
+    fill_randn(k_pool, gen)
+    fill_randn(v_pool, gen)
+    q_in = torch.randn((n, hq * hd), device="cuda", generator=gen)
+    k_in = torch.randn((n, kv_dim), device="cuda", generator=gen)
+    v_in = torch.randn((n, kv_dim), device="cuda", generator=gen)
+    qn_w = (1 + 0.02 * torch.randn(hd, device="cuda", generator=gen)).contiguous()
+    kn_w = (1 + 0.02 * torch.randn(hd, device="cuda", generator=gen)).contiguous()
+    n_pos = max_len + 2
+    cos_h = np.zeros((n_pos, hd), np.float32)
+    sin_h = np.zeros((n_pos, hd), np.float32)
+    smol_b200.compute_rope(cos_h, sin_h, np.arange(n_pos, dtype=np.int32), n_pos, hd, cfg["theta"])
+    rope_cos = torch.from_numpy(cos_h).cuda()
+    rope_sin = torch.from_numpy(sin_h).cuda()
+    q_rot = torch.empty_like(q_in)
+    out = torch.empty_like(q_in)
+    positions = torch.from_numpy(lens.astype(np.int32)).cuda()
+    kv_next = torch.from_numpy((lens + 1).astype(np.int32)).cuda()
+    row0 = [torch.from_numpy(lay.row0(l)).cuda() for l in range(layers)]
+    slots = [torch.from_numpy(lay.row0(l) + lens).cuda() for l in range(layers)]
+    ws = torch.empty(smol_b200.decode_workspace_bytes(n, max_len + 1, hq, hkv, hd), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+    scale = 1.0 / np.sqrt(hd)
+
+    kv_events = []
+
+    def step(record=False):
+        for l in range(layers):
+            smol_b200.qknorm_rope_append(q_in, k_in, v_in, n, hq, hkv, hd, qn_w, kn_w, 1e-6, rope_cos, rope_sin,
+                                         False, positions, slots[l], q_rot, None, k_pool, v_pool, lay.rows,
+                                         stream=stream)
+            if record:
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+            smol_b200.decode_attention(out, q_rot, k_pool, v_pool, lay.rows, row0[l], kv_next, n, max_len + 1, hq,
+                                       hkv, hd, scale, ws, stream=stream)
+            if record:
+                b.record(stream)
+                kv_events.append((a, b))
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    smol_b200.check(smol_b200.last_error(), "warm-up")
+    barrier(world)
+    clocks = Clocks(gpu_index(local)) if rank == 0 else None
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    t_start.record(stream)
+    for _ in range(args.steps):
+        step(record=True)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop() if clocks else None
+    ms_total = t_start.elapsed_time(t_end)
+    ms_step = allreduce_max(ms_total / args.steps, world)
+    dev_err = smol_b200.device_error()
+    if dev_err or smol_b200.last_error():
+        raise SystemExit(f"kernel error: device word {dev_err}, last error {smol_b200.last_error()}")
+
+    kv_bytes_rank = lay.kv_bytes(kv_dim, extra_tokens=1)          # attends L+1 per layer
+    value = world * kv_bytes_rank / (ms_step * 1e-3) / 1e9
+    # roofline of the decode kernel pair (split-KV + combine), live CUDA events
+    dec_ms = statistics.mean(a.elapsed_time(b) for a, b in kv_events)
+    qo_bytes = n * hq * hd * 4 * 2                                 # fp32 q read + fp32 out write
+    alg_bytes_launch = kv_bytes_rank / layers + qo_bytes
+    achieved = alg_bytes_launch / (dec_ms * 1e-3) / 1e9
+
+    # ---- e2e through the C ABI with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        qh = torch.randn((n, hq * hd), generator=torch.Generator().manual_seed(3)).pin_memory()
+        kh = torch.randn((n, kv_dim), generator=torch.Generator().manual_seed(4)).pin_memory()
+        vh = torch.randn((n, kv_dim), generator=torch.Generator().manual_seed(5)).pin_memory()
+        oh = torch.empty((n, hq * hd)).pin_memory()
+        lens_d = torch.from_numpy(lens.astype(np.int32)).cuda()
+        scratch = torch.empty(smol_b200.decode_step_scratch_bytes(n, max_len, hq, hkv, hd), dtype=torch.uint8,
+                              device="cuda")
+
+        def e2e_step():
+            for l in range(layers):
+                smol_b200.decode_step_host(oh.numpy(), qh.numpy(), kh.numpy(), vh.numpy(), n, hq, hkv, hd, qn_w, kn_w,
+                                           1e-6, rope_cos, rope_sin, False, k_pool, v_pool, lay.rows, row0[l], lens_d,
+                                           max_len, scale, scratch, stream=stream)
+
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = allreduce_max(e0.elapsed_time(e1) / args.steps, world)
+        e2e = {"value": round(world * kv_bytes_rank / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
+               "ms_per_step": round(e2e_ms, 3),
+               "h2d_bytes_per_step": layers * (qh.numel() + kh.numel() + vh.numel()) * 4,
+               "d2h_bytes_per_step": layers * oh.numel() * 4,
+               "api": "smol_b200_decode_step_host (pinned host q/k/v in, host out; 28 calls per step)"}
+        smol_b200.check(smol_b200.last_error(), "e2e")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference_decode(lens, args.cpu_seconds)
+
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "cfg2: batched decode attention step, 28 layers x 256 sequences per GPU, "
+                               "KV len ~U[1024,8192] seed 0, GQA 16/8, hd 128, theta 1e6, QK-norm+RoPE+append fused",
+                   "global_batch": n * world, "layers": layers, "kv_cache": "K bf16 / V fp16, pooled in HBM",
+                   "parallelism": f"dp{world} (sequences sharded, no collective)",
+                   "l2": "cache of %.1f GB per GPU >> 126 MB L2: no flush needed" % (2 * lay.rows * kv_dim * 2 / 1e9)},
+        "kv_bytes_per_step": world * kv_bytes_rank,
+        "hbm_frac": round(value / world / pk["hbm_gbs"], 4),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                     "kernel": "decode_split_kernel<128> + decode_combine_kernel<128> (per layer)",
+                     "alg_bytes_per_launch": int(alg_bytes_launch), "ms_per_launch": round(dec_ms, 4),
+                     "peak_source": pk["source"]},
+        "gpu_launches": args.steps * layers * 3,
+        "e2e": e2e,
+        "cpu_baseline": None if cpu is None else {k: (round(v, 3) if isinstance(v, float) else v)
+                                                  for k, v in cpu.items()},
+        "clocks": clk,
+        "prefill": prefill,
+    }
+    print(json.dumps(line))
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    run_ours(args)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

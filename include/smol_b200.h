@@ -1,0 +1,208 @@
+/*
+ * smol_b200.h -- C ABI of libsmol_b200.so, the B200 (sm_100a) attention hot path
+ * for tmzt/smol-genius.
+ *
+ * Part 1 re-declares, with identical prototypes, the entry points of the three
+ * reference objects this library replaces (attention.o, rope.o, rmsnorm.o of
+ * common/kernels/smol_kernels.h).  A consumer that already includes the
+ * reference's smol_kernels.h links libsmol_b200.so ahead of libsmol.a and the
+ * linker resolves these names here.  Pointers may be host memory (the call
+ * stages through the device and is synchronous on return, as the reference's
+ * callers expect) or device memory (the call runs in place, still synchronous).
+ *
+ * Part 2 is the error interface the reference lacks: the Part-1 functions
+ * return void like their originals and record failures here instead of aborting.
+ *
+ * Part 3 is the device API the fast path uses: a bf16-K / fp16-V KV cache that
+ * stays in HBM, a fused QK-norm + RoPE + cache-append kernel, split-KV batched
+ * decode, and tcgen05 prefill with a mask kind.  All pointers are device pointers
+ * unless a name ends in _host; `stream` is a cudaStream_t (NULL = default stream).
+ * Part-3 calls are asynchronous on `stream` unless stated.
+ *
+ * Reference citations are file:line within tmzt/smol-genius.
+ */
+#ifndef SMOL_B200_H
+#define SMOL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SMOL_B200_API __attribute__((visibility("default")))
+
+/* ======================================================================
+ * Part 1 -- drop-in replacements (common/kernels/smol_kernels.h:86-161)
+ * ====================================================================== */
+
+/* smol_kernels.h:109-113, attention.c:32-77.  MHA; window w covers rows
+ * [window_starts[w], window_starts[w+1]) and attends only to itself. */
+SMOL_B200_API void smol_bidirectional_attention(float *out, const float *Q, const float *K,
+                                                const float *V, int seq, int n_heads,
+                                                int head_dim, float scale,
+                                                const int *window_starts, int n_windows);
+
+/* smol_kernels.h:115-118, attention.c:153-170.  Row i attends keys
+ * [0, min(q_offset+i+1, seq_k)); GQA maps head h to KV head h/(n_heads/n_kv_heads). */
+SMOL_B200_API void smol_causal_attention(float *out, const float *Q, const float *K,
+                                         const float *V, int seq_q, int seq_k, int n_heads,
+                                         int n_kv_heads, int head_dim, float scale,
+                                         int q_offset);
+
+/* smol_kernels.h:120-124, attention.c:254-273.  Keys start at pos-window+1. */
+SMOL_B200_API void smol_sliding_window_attention(float *out, const float *Q, const float *K,
+                                                 const float *V, int seq_q, int seq_k,
+                                                 int n_heads, int n_kv_heads, int head_dim,
+                                                 float scale, int q_offset, int window_size);
+
+/* smol_kernels.h:127-131, attention.c:350-368.  score = cap*tanh(score/cap). */
+SMOL_B200_API void smol_causal_attention_softcap(float *out, const float *Q, const float *K,
+                                                 const float *V, int seq_q, int seq_k,
+                                                 int n_heads, int n_kv_heads, int head_dim,
+                                                 float scale, int q_offset, float cap);
+
+/* smol_kernels.h:133-138, attention.c:443-462. */
+SMOL_B200_API void smol_sliding_window_attention_softcap(float *out, const float *Q,
+                                                         const float *K, const float *V,
+                                                         int seq_q, int seq_k, int n_heads,
+                                                         int n_kv_heads, int head_dim,
+                                                         float scale, int q_offset,
+                                                         int window_size, float cap);
+
+/* smol_kernels.h:144-145, rope.c:12-25.  Table construction, computed on the host
+ * with the reference's libm formula so the values are bit-identical. */
+SMOL_B200_API void smol_sinusoidal_pe(float *pe, int n_pos, int d_model);
+
+/* smol_kernels.h:147-149, rope.c:27-45.  Host-built table (bit-identical values). */
+SMOL_B200_API void smol_compute_rope_neox(float *cos_out, float *sin_out, const int *positions,
+                                          int seq, int head_dim, float theta);
+
+/* smol_kernels.h:151-153, rope.c:99-164.  In place on [seq, n_heads*head_dim]. */
+SMOL_B200_API void smol_apply_rope_neox(float *x, const float *cos_vals, const float *sin_vals,
+                                        int seq, int n_heads, int head_dim);
+
+/* smol_kernels.h:156-158, rope.c:51-66.  Host-built table (bit-identical values). */
+SMOL_B200_API void smol_compute_rope_interleaved(float *cos_out, float *sin_out,
+                                                 const int *positions, int seq, int head_dim,
+                                                 float theta);
+
+/* smol_kernels.h:159-161, rope.c:68-93.  In place. */
+SMOL_B200_API void smol_apply_rope_interleaved(float *x, const float *cos_vals,
+                                               const float *sin_vals, int seq, int n_heads,
+                                               int head_dim);
+
+/* smol_kernels.h:82-84, rmsnorm.c:17-76 (shares rmsnorm.o with the per-head form). */
+SMOL_B200_API void smol_rms_norm(float *out, const float *x, const float *weight, int seq_len,
+                                 int hidden, float eps);
+
+/* smol_kernels.h:86-88, rmsnorm.c:78-140.  In place on each [head_dim] slice. */
+SMOL_B200_API void smol_rms_norm_per_head(float *x, const float *weight, int seq_len,
+                                          int n_heads, int head_dim, float eps);
+
+/* ======================================================================
+ * Part 2 -- status (no reference counterpart: the reference cannot fail,
+ * smol_kernels.h returns void everywhere)
+ * ====================================================================== */
+
+enum {
+    SMOL_B200_OK = 0,
+    SMOL_B200_ERR_ARGS = 1,          /* arguments out of the supported range           */
+    SMOL_B200_ERR_CUDA = 2,          /* a CUDA runtime call failed                     */
+    SMOL_B200_ERR_NO_DEVICE = 3,     /* no sm_100 device visible                       */
+    SMOL_B200_ERR_OOM = 4,           /* device allocation failed                       */
+    SMOL_B200_ERR_WATCHDOG = 5,      /* a kernel's bounded wait ran out (see device word) */
+    SMOL_B200_ERR_WORKSPACE = 6      /* caller's workspace smaller than required        */
+};
+
+/* Last error recorded by any call on this thread's process (sticky until cleared). */
+SMOL_B200_API int smol_cuda_last_error(void);
+SMOL_B200_API const char *smol_cuda_error_string(int code);
+SMOL_B200_API void smol_cuda_clear_error(void);
+/* Device error word of the current device: bits set by kernels whose bounded waits
+ * ran out (0 = none).  Synchronises the device.  Cleared by smol_cuda_clear_error. */
+SMOL_B200_API unsigned smol_cuda_device_error(void);
+
+/* ======================================================================
+ * Part 3 -- device API (new; replaces the host KV cache of
+ * common/decoder/qkn_decoder.c:172-220 and the per-layer attention prologue of
+ * qkn_decoder.c:488-528 / :642-677)
+ * ====================================================================== */
+
+enum {
+    SMOL_MASK_CAUSAL = 0,     /* key j visible to row i iff j <= q_offset+i              */
+    SMOL_MASK_PREFIX_LM = 1,  /* j < max(prefix_len, q_offset+i+1)                        */
+    SMOL_MASK_WINDOWS = 2,    /* bidirectional inside [ws_w, ws_{w+1}) (siglip.c:108)     */
+    SMOL_MASK_FULL = 3        /* every key                                               */
+};
+
+/* Fused prologue of one attention layer (qkn_decoder.c:488-503 prefill, :642-652
+ * decode): for every token t, per-head RMSNorm of q and k (skipped when the weight
+ * is NULL), RoPE from table row positions[t] (skipped when rope_cos is NULL), then
+ * K is stored as bf16 and V as fp16 into cache row slots[t].  The rotated q goes
+ * to q_out_f32 and/or q_out_bf16 (either may be NULL).
+ * Inputs: q_in [n_tokens, n_heads*head_dim], k_in/v_in [n_tokens, n_kv_heads*head_dim]
+ * fp32; cache rows are n_kv_heads*head_dim wide, cache_rows rows long.  A slot
+ * outside [0, cache_rows) is skipped and flagged in the device error word. */
+SMOL_B200_API int smol_b200_qknorm_rope_append(
+    void *stream, const float *q_in, const float *k_in, const float *v_in, int n_tokens,
+    int n_heads, int n_kv_heads, int head_dim, const float *q_norm_w, const float *k_norm_w,
+    float eps, const float *rope_cos, const float *rope_sin, int rope_interleaved,
+    const int *positions, const int64_t *slots, float *q_out_f32, uint16_t *q_out_bf16,
+    uint16_t *k_cache_bf16, uint16_t *v_cache_f16, int64_t cache_rows);
+
+/* Workspace (bytes) that smol_b200_decode_attention needs for these sizes. */
+SMOL_B200_API size_t smol_b200_decode_workspace_bytes(int n_seqs, int max_kv_len, int n_heads,
+                                                      int n_kv_heads, int head_dim);
+
+/* Batched single-query decode, split-KV (qkn_decoder.c:658-677 per sequence):
+ * sequence b attends pool rows [seq_row0[b] + ks, seq_row0[b] + kv_len[b]) where
+ * ks = max(0, kv_len[b]-window) when window > 0, else 0.  q is
+ * [n_seqs, n_heads*head_dim] fp32 (q_is_bf16=0) or bf16 (1); out is fp32 of the same
+ * shape.  k_pool is bf16, v_pool fp16, both [pool_rows, n_kv_heads*head_dim].
+ * max_kv_len bounds kv_len[] (it sizes the grid).  softcap<=0 disables the cap.
+ * head_dim: 64, 128 or 256.  workspace: smol_b200_decode_workspace_bytes() bytes. */
+SMOL_B200_API int smol_b200_decode_attention(
+    void *stream, float *out, const void *q, int q_is_bf16, const uint16_t *k_pool,
+    const uint16_t *v_pool, int64_t pool_rows, const int64_t *seq_row0, const int *kv_len,
+    int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, int head_dim, float scale,
+    int window, float softcap, void *workspace, size_t workspace_bytes);
+
+/* Prefill / encoder attention on tcgen05 tensor cores.  For batch element b, row i
+ * of head h attends the keys the mask allows (see SMOL_MASK_*), further limited to
+ * [pos-window+1, ...] when window > 0 and capped by softcap when softcap > 0.
+ * q, k: bf16; v: fp16; out: fp32.  Strides are in elements; row strides must be
+ * multiples of 8 and pointers 16-byte aligned.  head_dim: 64, 128 or 256.
+ * window_starts (device, n_windows+1 entries) is read for SMOL_MASK_WINDOWS only.
+ * GQA: head h reads KV head h / (n_heads/n_kv_heads). */
+SMOL_B200_API int smol_b200_prefill_attention(
+    void *stream, float *out, int64_t out_row_stride, int64_t out_batch_stride,
+    const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride, const uint16_t *k,
+    int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
+    int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads, int n_kv_heads,
+    int head_dim, float scale, int mask_kind, int q_offset, int prefix_len, int window,
+    float softcap, const int *window_starts, int n_windows);
+
+/* One batched decode step of one layer with host buffers, as a host-driven decoder
+ * issues it: copies q/k/v of the new token of every sequence (fp32, host) to the
+ * device, runs smol_b200_qknorm_rope_append (token of sequence b goes to pool row
+ * seq_row0[b]+kv_len[b] at RoPE position kv_len[b]), attends [0, kv_len[b]+1), and
+ * copies the fp32 result back to out_host.  kv_len is not advanced (the caller
+ * owns it, as qkn_decoder.c:707 owns kv_cache_len).  Synchronous.  `scratch` is a
+ * device buffer of smol_b200_decode_step_scratch_bytes() bytes. */
+SMOL_B200_API size_t smol_b200_decode_step_scratch_bytes(int n_seqs, int max_kv_len, int n_heads,
+                                                         int n_kv_heads, int head_dim);
+SMOL_B200_API int smol_b200_decode_step_host(
+    void *stream, float *out_host, const float *q_host, const float *k_host,
+    const float *v_host, int n_seqs, int n_heads, int n_kv_heads, int head_dim,
+    const float *q_norm_w, const float *k_norm_w, float eps, const float *rope_cos,
+    const float *rope_sin, int rope_interleaved, uint16_t *k_pool, uint16_t *v_pool,
+    int64_t pool_rows, const int64_t *seq_row0, const int *kv_len, int max_kv_len,
+    float scale, void *scratch, size_t scratch_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SMOL_B200_H */

@@ -1,0 +1,464 @@
+// decode_attn.cu -- split-KV flash-decoding over the pooled bf16-K / fp16-V cache.
+//
+// Replaces smol_causal_attention(seq_q=1) as qkn_decoder_forward calls it
+// (qkn_decoder.c:658-677; algorithm attention.c:79-126) for a whole batch of
+// sequences at once.
+//
+// Work split.  One CTA owns (sequence b, KV head, group of <=8 Q heads, chunk of
+// `chunk` keys).  A producer warp streams the chunk's K and V rows of that KV head
+// into shared memory with 2-D TMA tensor copies (64 keys x 64 dims per box,
+// 128-byte swizzle) through a STAGES-deep mbarrier ring.  Four consumer warps each
+// take 16 keys of every 64-key tile and keep their own online-softmax state.
+//
+// Math.  The KV head's keys are the M dimension of warp-level MMAs and the (padded
+// to 8) Q heads the N dimension, so one K/V tile in shared memory serves every Q
+// head of the GQA group (the reference re-reads each KV row once per Q head):
+//   S^T(16 keys x 8 heads)   = K(16 x hd, bf16) . Q^T(hd x 8, bf16; fp32 Q is split
+//                              into bf16 hi + lo terms so scores keep fp32 accuracy)
+//   O^T(hd x 8 heads)       += V^T(hd x 16, fp16) . P^T(16 x 8, fp16)
+// P^T reaches the B-operand layout with one movmatrix transpose per 8 keys.  P and V
+// are fp16 because bf16 probabilities alone put the output ~1.3e-3 (rel-L2) away from
+// an fp32 reference; fp16 keeps it near 1.5e-4.
+//
+// Each CTA merges its 4 warps and writes one partial (O unnormalised, running max,
+// running sum) per Q head; a second kernel merges the chunks of a sequence.
+// Algorithmic traffic: every attended key costs n_kv_heads*hd*2 (K,V) * 2 bytes.
+#include "b200_common.cuh"
+#include "runtime.h"
+
+namespace smolb200 {
+namespace {
+
+constexpr int kKeysPerTile = 64;
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kSubtileBytes = kKeysPerTile * 128;   // 64 rows x 64 halves (128 B)
+
+template <int HD>
+struct DecodeShape {
+    static constexpr int kSubtiles = HD / 64;
+    static constexpr int kTileBytes = kSubtiles * kSubtileBytes;   // K or V of one tile
+    static constexpr int kStageBytes = 2 * kTileBytes;
+    static constexpr int kStages = HD == 256 ? 2 : (HD == 128 ? 3 : 4);
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct DecodeParams {
+    CUtensorMap tmap_k;             // bf16 [pool_rows, kv_dim], box 64x64, SW128
+    CUtensorMap tmap_v;             // fp16 [pool_rows, kv_dim], box 64x64, SW128
+    const void *q;                  // [n_seqs, n_heads*hd] fp32 or bf16
+    const int64_t *seq_row0;
+    const int *kv_len;
+    float *part_o;                  // [n_seqs*n_heads*max_chunks, hd]
+    float *part_ml;                 // [n_seqs*n_heads*max_chunks, 2]
+    unsigned *err;
+    int q_is_bf16;
+    int n_heads, n_kv_heads, group, n_qgroups;
+    int chunk, max_chunks, window;
+    float scale, softcap;
+};
+
+__device__ __forceinline__ float fast_exp2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Splits two fp32 values into packed bf16 hi and lo (x ~= hi + lo).
+__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t &hi, uint32_t &lo)
+{
+    hi = pack_bf16x2(x0, x1);
+    lo = pack_bf16x2(x0 - bf16lo_f32(hi), x1 - bf16hi_f32(hi));
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_constant__ DecodeParams p)
+{
+    using S = DecodeShape<HD>;
+    constexpr int KSTEPS = HD / 16;
+
+    const int b = blockIdx.z;
+    const int kvh = blockIdx.y / p.n_qgroups;
+    const int qg = blockIdx.y % p.n_qgroups;
+    const int c = blockIdx.x;
+
+    const int L = p.kv_len[b];
+    const int ks = (p.window > 0 && L > p.window) ? L - p.window : 0;
+    int n = L - ks;
+    if (n > p.max_chunks * p.chunk) n = p.max_chunks * p.chunk;   // flagged by the combine kernel
+    const int key0 = c * p.chunk;                                  // relative to ks
+    if (n <= 0 || key0 >= n) return;                               // uniform for the CTA
+    const int nkeys = min(p.chunk, n - key0);
+    const int ntiles = (nkeys + kKeysPerTile - 1) / kKeysPerTile;
+    const int h_first = kvh * p.group + qg * 8;
+    const int nh = min(8, p.group - qg * 8);
+    const long long row_base = p.seq_row0[b] + ks + key0;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + S::kStages * S::kStageBytes);
+    uint64_t *empty_bar = full_bar + S::kStages;
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S::kStages; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), kConsumerWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsumerWarps) {
+        // ---------------- producer warp ----------------
+        if (lane == 0) {
+            tma_prefetch_desc(&p.tmap_k);
+            tma_prefetch_desc(&p.tmap_v);
+            int issued = 0;
+            for (int t = 0; t < ntiles; ++t) {
+                const int s = t % S::kStages;
+                if (t >= S::kStages &&
+                    !mbar_wait(smem_u32(&empty_bar[s]), ((t / S::kStages) - 1) & 1, p.err, kErrWaitTmaEmpty))
+                    break;
+                const uint32_t fb = smem_u32(&full_bar[s]);
+                mbar_arrive_expect_tx(fb, S::kStageBytes);
+                const uint32_t kdst = smem_u32(smem + s * S::kStageBytes);
+                const uint32_t vdst = kdst + S::kTileBytes;
+                const int y = static_cast<int>(row_base + t * kKeysPerTile);
+#pragma unroll
+                for (int sub = 0; sub < S::kSubtiles; ++sub) {
+                    const int x = kvh * HD + sub * 64;
+                    tma_load_2d(kdst + sub * kSubtileBytes, &p.tmap_k, fb, x, y);
+                    tma_load_2d(vdst + sub * kSubtileBytes, &p.tmap_v, fb, x, y);
+                }
+                ++issued;
+            }
+            // Drain: every issued tile must have landed before the CTA may exit.
+            for (int t = max(0, issued - S::kStages); t < issued; ++t) {
+                if (!mbar_wait(smem_u32(&full_bar[t % S::kStages]), (t / S::kStages) & 1, p.err, kErrDrain))
+                    break;
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumer warps ----------------
+    const int g = lane >> 2;   // key row (S^T) / head column (B operand)
+    const int tq = lane & 3;
+
+    // Q^T as B fragments (k = head dim, n = head g), bf16 hi (+ lo for fp32 Q).
+    uint32_t qhi[KSTEPS][2], qlo[KSTEPS][2];
+    {
+        const bool valid = g < nh;
+        const long long qrow = (static_cast<long long>(b) * p.n_heads + h_first + (valid ? g : 0)) * HD;
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; ++kk) {
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                const int d = kk * 16 + half * 8 + tq * 2;
+                float x0 = 0.f, x1 = 0.f;
+                if (valid) {
+                    if (p.q_is_bf16) {
+                        const uint32_t v = *reinterpret_cast<const uint32_t *>(
+                            static_cast<const uint16_t *>(p.q) + qrow + d);
+                        x0 = bf16lo_f32(v);
+                        x1 = bf16hi_f32(v);
+                    } else {
+                        const float2 v = *reinterpret_cast<const float2 *>(static_cast<const float *>(p.q) + qrow + d);
+                        x0 = v.x;
+                        x1 = v.y;
+                    }
+                }
+                split_bf16x2(x0, x1, qhi[kk][half], qlo[kk][half]);
+            }
+        }
+    }
+    const bool use_lo = !p.q_is_bf16;
+
+    const float kLog2e = 1.4426950408889634f;
+    const float cap = p.softcap;
+    const float inv_cap = cap > 0.f ? 1.f / cap : 0.f;
+
+    float m_run[2] = {-INFINITY, -INFINITY};   // heads 2tq, 2tq+1 (warp-uniform per column)
+    float l_run[2] = {0.f, 0.f};                // this thread's keys only
+    float o[KSTEPS][4];
+#pragma unroll
+    for (int i = 0; i < KSTEPS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+    bool ok = true;
+    for (int t = 0; t < ntiles; ++t) {
+        const int s = t % S::kStages;
+        if (!mbar_wait(smem_u32(&full_bar[s]), (t / S::kStages) & 1, p.err, kErrWaitTmaFull)) {
+            ok = false;
+            break;
+        }
+        const int kb = t * kKeysPerTile + warp * 16;   // first key of this warp's block
+        const int nv = nkeys - kb;                     // valid keys in the block (may be <=0 or >16)
+        if (nv > 0) {
+            const uint32_t kbase = smem_u32(smem + s * S::kStageBytes);
+            const uint32_t vbase = kbase + S::kTileBytes;
+
+            // ---- S^T = K . Q^T ----
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            {
+                const int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+                for (int kk = 0; kk < KSTEPS; ++kk) {
+                    const int chunk = (kk & 3) * 2 + (lane >> 4);
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4(kbase + (kk >> 2) * kSubtileBytes + sw128_offset(row, chunk), a0, a1, a2, a3);
+                    mma_bf16_16816(acc, a0, a1, a2, a3, qhi[kk][0], qhi[kk][1]);
+                    if (use_lo) mma_bf16_16816(acc, a0, a1, a2, a3, qlo[kk][0], qlo[kk][1]);
+                }
+            }
+            // acc[0]=(key g, head 2tq) acc[1]=(key g, head 2tq+1) acc[2]=(key g+8, 2tq) acc[3]=(key g+8, 2tq+1)
+            float sc[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float x = acc[i] * p.scale;
+                if (cap > 0.f) x = cap * tanhf(x * inv_cap);
+                const int key = g + (i >> 1) * 8;
+                sc[i] = key < nv ? x : -INFINITY;
+            }
+            float mb0 = fmaxf(sc[0], sc[2]);
+            float mb1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, off));
+                mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, off));
+            }
+            const float mn0 = fmaxf(m_run[0], mb0);
+            const float mn1 = fmaxf(m_run[1], mb1);
+            const float corr0 = fast_exp2((m_run[0] - mn0) * kLog2e);
+            const float corr1 = fast_exp2((m_run[1] - mn1) * kLog2e);
+            m_run[0] = mn0;
+            m_run[1] = mn1;
+            const float p0 = fast_exp2((sc[0] - mn0) * kLog2e);
+            const float p1 = fast_exp2((sc[1] - mn1) * kLog2e);
+            const float p2 = fast_exp2((sc[2] - mn0) * kLog2e);
+            const float p3 = fast_exp2((sc[3] - mn1) * kLog2e);
+            l_run[0] = l_run[0] * corr0 + p0 + p2;
+            l_run[1] = l_run[1] * corr1 + p1 + p3;
+#pragma unroll
+            for (int i = 0; i < KSTEPS; ++i) {
+                o[i][0] *= corr0;
+                o[i][1] *= corr1;
+                o[i][2] *= corr0;
+                o[i][3] *= corr1;
+            }
+            const uint32_t pb0 = movmatrix_t(pack_f16x2(p0, p1));   // keys 0-7
+            const uint32_t pb1 = movmatrix_t(pack_f16x2(p2, p3));   // keys 8-15
+
+            // ---- O^T += V^T . P^T ----
+            {
+                const int m = lane >> 3;
+                const int row = warp * 16 + (lane & 7) + (m >> 1) * 8;
+                const bool tail = nv < 16;
+                const int k0 = 2 * tq, k1 = 2 * tq + 8;   // keys held in a0/a1 and a2/a3
+#pragma unroll
+                for (int db = 0; db < KSTEPS; ++db) {
+                    const int chunk = (db & 3) * 2 + (m & 1);
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4_t(vbase + (db >> 2) * kSubtileBytes + sw128_offset(row, chunk), a0, a1, a2, a3);
+                    if (tail) {
+                        const uint32_t mlo = (k0 < nv ? 0x0000ffffu : 0u) | (k0 + 1 < nv ? 0xffff0000u : 0u);
+                        const uint32_t mhi = (k1 < nv ? 0x0000ffffu : 0u) | (k1 + 1 < nv ? 0xffff0000u : 0u);
+                        a0 &= mlo;
+                        a1 &= mlo;
+                        a2 &= mhi;
+                        a3 &= mhi;
+                    }
+                    mma_f16_16816(o[db], a0, a1, a2, a3, pb0, pb1);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+    }
+
+    // ---- merge the 4 consumer warps (stage buffers are free: every tile was consumed) ----
+    // Layout: per warp, per head column: [m, l] then O[hd].
+    float *red = reinterpret_cast<float *>(smem);
+    constexpr int kRowF = HD + 2;
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    {
+        // total l over the 8 key rows (lanes sharing tq)
+        float l0 = l_run[0], l1 = l_run[1];
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+        }
+        float *wbase = red + warp * 8 * kRowF;
+        if (g == 0) {
+            wbase[(2 * tq) * kRowF + 0] = m_run[0];
+            wbase[(2 * tq) * kRowF + 1] = l0;
+            wbase[(2 * tq + 1) * kRowF + 0] = m_run[1];
+            wbase[(2 * tq + 1) * kRowF + 1] = l1;
+        }
+#pragma unroll
+        for (int db = 0; db < KSTEPS; ++db) {
+            const int d0 = db * 16 + g;
+            wbase[(2 * tq) * kRowF + 2 + d0] = o[db][0];
+            wbase[(2 * tq + 1) * kRowF + 2 + d0] = o[db][1];
+            wbase[(2 * tq) * kRowF + 2 + d0 + 8] = o[db][2];
+            wbase[(2 * tq + 1) * kRowF + 2 + d0 + 8] = o[db][3];
+        }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    if (!ok) return;
+    for (int idx = threadIdx.x; idx < nh * HD; idx += kConsumerWarps * 32) {
+        const int h = idx / HD, d = idx % HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, red[(w * 8 + h) * kRowF]);
+        float acc = 0.f, lsum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+            const float mw = red[(w * 8 + h) * kRowF];
+            const float f = mw == -INFINITY ? 0.f : fast_exp2((mw - M) * kLog2e);
+            acc += f * red[(w * 8 + h) * kRowF + 2 + d];
+            lsum += f * red[(w * 8 + h) * kRowF + 1];
+        }
+        const long long item = (static_cast<long long>(b) * p.n_heads + h_first + h) * p.max_chunks + c;
+        p.part_o[item * HD + d] = acc;
+        if (d == 0) {
+            p.part_ml[item * 2 + 0] = M;
+            p.part_ml[item * 2 + 1] = lsum;
+        }
+    }
+}
+
+// out[b, h, :] = merge over the chunks of sequence b.
+template <int HD>
+__global__ void decode_combine_kernel(float *__restrict__ out, const float *__restrict__ part_o,
+                                      const float *__restrict__ part_ml, const int *__restrict__ kv_len,
+                                      int n_heads, int chunk, int max_chunks, int window, unsigned *err)
+{
+    const int b = blockIdx.y, h = blockIdx.x, d = threadIdx.x;
+    const int L = kv_len[b];
+    const int ks = (window > 0 && L > window) ? L - window : 0;
+    const int n = L - ks;
+    int nch = n > 0 ? (n + chunk - 1) / chunk : 0;
+    if (nch > max_chunks) {
+        if (d == 0) atomicOr(err, kErrBadArgs);
+        nch = max_chunks;
+    }
+    const long long item0 = (static_cast<long long>(b) * n_heads + h) * max_chunks;
+    const float kLog2e = 1.4426950408889634f;
+    float M = -INFINITY;
+    for (int c = 0; c < nch; ++c) M = fmaxf(M, part_ml[(item0 + c) * 2]);
+    float acc = 0.f, lsum = 0.f;
+    for (int c = 0; c < nch; ++c) {
+        const float f = fast_exp2((part_ml[(item0 + c) * 2] - M) * kLog2e);
+        acc += f * part_o[(item0 + c) * HD + d];
+        lsum += f * part_ml[(item0 + c) * 2 + 1];
+    }
+    out[(static_cast<long long>(b) * n_heads + h) * HD + d] = lsum > 0.f ? acc / lsum : 0.f;
+}
+
+int decode_chunk_size(int n_seqs, int max_kv_len, int n_kv_heads, int n_qgroups)
+{
+    const long long work = static_cast<long long>(n_seqs) * n_kv_heads * n_qgroups * (max_kv_len > 0 ? max_kv_len : 1);
+    long long c = (work + 148 * 8 - 1) / (148 * 8);
+    c = (c + kKeysPerTile - 1) / kKeysPerTile * kKeysPerTile;
+    if (c < kKeysPerTile) c = kKeysPerTile;
+    if (c > 512) c = 512;
+    return static_cast<int>(c);
+}
+
+template <int HD>
+int launch_decode(cudaStream_t st, float *out, const void *q, int q_is_bf16, const uint16_t *k_pool,
+                  const uint16_t *v_pool, int64_t pool_rows, const int64_t *seq_row0, const int *kv_len,
+                  int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, float scale, int window,
+                  float softcap, void *workspace)
+{
+    using S = DecodeShape<HD>;
+    DecodeParams p;
+    memset(&p, 0, sizeof(p));
+    const int kv_dim = n_kv_heads * HD;
+    if (!make_tmap_2d(&p.tmap_k, k_pool, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kv_dim, pool_rows, 64, kKeysPerTile))
+        return SMOL_B200_ERR_CUDA;
+    if (!make_tmap_2d(&p.tmap_v, v_pool, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kv_dim, pool_rows, 64, kKeysPerTile))
+        return SMOL_B200_ERR_CUDA;
+    p.group = n_heads / n_kv_heads;
+    p.n_qgroups = (p.group + 7) / 8;
+    p.chunk = decode_chunk_size(n_seqs, max_kv_len, n_kv_heads, p.n_qgroups);
+    p.max_chunks = (max_kv_len + p.chunk - 1) / p.chunk;
+    if (p.max_chunks < 1) p.max_chunks = 1;
+    const size_t n_items = static_cast<size_t>(n_seqs) * n_heads * p.max_chunks;
+    p.part_o = static_cast<float *>(workspace);
+    p.part_ml = p.part_o + n_items * HD;
+    p.q = q;
+    p.q_is_bf16 = q_is_bf16;
+    p.seq_row0 = seq_row0;
+    p.kv_len = kv_len;
+    p.err = device_error_word();
+    p.n_heads = n_heads;
+    p.n_kv_heads = n_kv_heads;
+    p.window = window;
+    p.scale = scale;
+    p.softcap = softcap;
+
+    static bool attr_set = false;   // per process; the attribute is per function
+    if (!attr_set) {
+        if (cudaFuncSetAttribute(decode_split_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 S::kSmemBytes) != cudaSuccess)
+            return SMOL_B200_ERR_CUDA;
+        attr_set = true;
+    }
+    dim3 grid(p.max_chunks, n_kv_heads * p.n_qgroups, n_seqs);
+    decode_split_kernel<HD><<<grid, kThreads, S::kSmemBytes, st>>>(p);
+    dim3 cgrid(n_heads, n_seqs);
+    decode_combine_kernel<HD><<<cgrid, HD, 0, st>>>(out, p.part_o, p.part_ml, kv_len, n_heads, p.chunk,
+                                                   p.max_chunks, window, p.err);
+    return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
+}
+
+}  // namespace
+
+size_t decode_workspace_bytes(int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, int head_dim)
+{
+    if (n_seqs <= 0 || n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0) return 0;
+    const int group = n_heads / n_kv_heads;
+    const int nq = (group + 7) / 8;
+    const int chunk = decode_chunk_size(n_seqs, max_kv_len, n_kv_heads, nq);
+    int max_chunks = (max_kv_len + chunk - 1) / chunk;
+    if (max_chunks < 1) max_chunks = 1;
+    const size_t n_items = static_cast<size_t>(n_seqs) * n_heads * max_chunks;
+    return n_items * (static_cast<size_t>(head_dim) + 2) * sizeof(float);
+}
+
+int decode_attention(cudaStream_t st, float *out, const void *q, int q_is_bf16, const uint16_t *k_pool,
+                     const uint16_t *v_pool, int64_t pool_rows, const int64_t *seq_row0, const int *kv_len,
+                     int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, int head_dim, float scale,
+                     int window, float softcap, void *workspace, size_t workspace_bytes)
+{
+    if (n_seqs <= 0) return SMOL_B200_OK;
+    if (!out || !q || !k_pool || !v_pool || !seq_row0 || !kv_len || n_heads <= 0 || n_kv_heads <= 0 ||
+        n_heads % n_kv_heads != 0 || max_kv_len < 0 || pool_rows <= 0 || pool_rows >= (1ll << 31) ||
+        n_seqs > 65535 || n_kv_heads * ((n_heads / n_kv_heads + 7) / 8) > 65535)
+        return SMOL_B200_ERR_ARGS;
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256) return SMOL_B200_ERR_ARGS;
+    if ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool)) & 15) return SMOL_B200_ERR_ARGS;
+    if (q_is_bf16 ? (reinterpret_cast<uintptr_t>(q) & 3) : (reinterpret_cast<uintptr_t>(q) & 7))
+        return SMOL_B200_ERR_ARGS;
+    const size_t need = decode_workspace_bytes(n_seqs, max_kv_len, n_heads, n_kv_heads, head_dim);
+    if (!workspace || workspace_bytes < need) return SMOL_B200_ERR_WORKSPACE;
+    switch (head_dim) {
+    case 64:
+        return launch_decode<64>(st, out, q, q_is_bf16, k_pool, v_pool, pool_rows, seq_row0, kv_len, n_seqs,
+                                 max_kv_len, n_heads, n_kv_heads, scale, window, softcap, workspace);
+    case 128:
+        return launch_decode<128>(st, out, q, q_is_bf16, k_pool, v_pool, pool_rows, seq_row0, kv_len, n_seqs,
+                                  max_kv_len, n_heads, n_kv_heads, scale, window, softcap, workspace);
+    default:
+        return launch_decode<256>(st, out, q, q_is_bf16, k_pool, v_pool, pool_rows, seq_row0, kv_len, n_seqs,
+                                  max_kv_len, n_heads, n_kv_heads, scale, window, softcap, workspace);
+    }
+}
+
+}  // namespace smolb200

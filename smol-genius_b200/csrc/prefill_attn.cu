@@ -1,0 +1,502 @@
+// prefill_attn.cu -- flash attention for prefill and encoders on tcgen05 tensor cores.
+//
+// Replaces smol_causal_attention with seq_q > 1 (attention.c:79-170), its sliding-
+// window and softcap variants (:176-462), smol_bidirectional_attention (:32-77) and
+// the prefix-LM composition PaliGemma needs, as one kernel with a mask kind.
+//
+// One CTA owns a 128-row query tile of one head of one batch element and walks the
+// key range its rows can see in tiles of BN keys.  Warp roles (192 threads):
+//   warps 0-3  softmax: thread t of warp w owns query row 32w+t, which is exactly
+//              TMEM lane 32w+t, so row max / row sum need no shuffles;
+//   warp 4     TMA producer: Q once, then K and V tiles through 2-slot rings;
+//   warp 5     TMEM allocator and single-thread tcgen05.mma issuer.
+// Per key tile j:
+//   S_j = Q K_j^T    kind::f16, bf16 A/B from 128B-swizzled shared memory, fp32 in TMEM
+//                    (two S buffers, so S_{j+1} runs while softmax works on S_j);
+//   P_j = exp2(S_j*scale*log2e - m)  written back over S_j's TMEM columns as fp16;
+//   O  += P_j V_j    A = P from TMEM, B = V (fp16, MN-major) from shared memory.
+// P and V are fp16: with bf16 probabilities alone the result sits ~1.3e-3 (rel-L2)
+// from an fp32 reference, fp16 keeps it near 1.5e-4.  The running maximum used for
+// the exponent only moves when the row maximum grows by more than 2^8, so O is
+// rescaled (TMEM load / scale / store by its owning thread) rarely; values stay
+// below 256 and the final division uses the same maximum for O and the row sum.
+#include <stdio.h>
+
+#include "b200_common.cuh"
+#include "runtime.h"
+
+namespace smolb200 {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kThreads = 192;
+constexpr int kSoftmaxThreads = 128;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr float kRescaleThreshold = 8.0f;   // log2 units
+
+template <int HD>
+struct PrefillShape {
+    static constexpr int BN = HD == 256 ? 64 : 128;
+    static constexpr int kSub = HD / 64;                     // 64-column sub-tiles
+    static constexpr int kQSubBytes = kBM * 128;
+    static constexpr int kQBytes = kSub * kQSubBytes;
+    static constexpr int kKvSubBytes = BN * 128;
+    static constexpr int kKvBytes = kSub * kKvSubBytes;
+    static constexpr int kStages = 2;
+    static constexpr int kOffQ = 0;
+    static constexpr int kOffK = kOffQ + kQBytes;
+    static constexpr int kOffV = kOffK + kStages * kKvBytes;
+    static constexpr int kOffBar = kOffV + kStages * kKvBytes;
+    static constexpr int kUsed = kOffBar + 256 + 1024;
+    // At least ~116 KB so that a single CTA is resident per SM: every CTA
+    // allocates all 512 TMEM columns.
+    static constexpr int kSmemBytes = kUsed > 118 * 1024 ? kUsed : 118 * 1024;
+    static constexpr int kTmS0 = 0, kTmS1 = BN, kTmO = 2 * BN;
+    static constexpr int kTmCols = 512;
+    static_assert(2 * BN + HD <= 512, "TMEM budget");
+};
+
+struct PrefillParams {
+    CUtensorMap tq, tk, tv;
+    float *out;
+    long long out_row_stride, out_batch_stride;
+    const int *window_starts;
+    unsigned *err;
+    int n_windows;
+    int seq_q, seq_k, n_heads, group, mask_kind, q_offset, prefix_len, window;
+    float scale, scale_log2, softcap;
+};
+
+struct Barriers {
+    uint64_t q_full;
+    uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+    uint64_t s_full[2], p_full[2];
+    uint64_t o_done, mma_done;
+    uint32_t tmem_base;
+    int lo_min, hi_max;
+};
+
+__device__ __forceinline__ float fast_exp2(float x)
+{
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Keys [lo, hi) visible to query row i; written=false for rows no window covers
+// (smol_bidirectional_attention leaves those rows untouched, attention.c:39-43).
+__device__ __forceinline__ void row_range(const PrefillParams &p, int i, int &lo, int &hi, bool &written)
+{
+    const int pos = p.q_offset + i;
+    written = true;
+    lo = 0;
+    switch (p.mask_kind) {
+    case SMOL_MASK_CAUSAL: hi = pos + 1; break;
+    case SMOL_MASK_PREFIX_LM: hi = max(pos + 1, p.prefix_len); break;
+    case SMOL_MASK_WINDOWS: {
+        int a = 0, b = p.n_windows;   // find w with ws[w] <= i < ws[w+1]
+        if (p.n_windows <= 0 || i < p.window_starts[0] || i >= p.window_starts[p.n_windows]) {
+            written = false;
+            hi = 0;
+            break;
+        }
+        while (b - a > 1) {
+            const int mid = (a + b) >> 1;
+            if (p.window_starts[mid] <= i) a = mid; else b = mid;
+        }
+        lo = p.window_starts[a];
+        hi = p.window_starts[a + 1];
+        break;
+    }
+    default: hi = p.seq_k; break;
+    }
+    if (hi > p.seq_k) hi = p.seq_k;
+    if (p.window > 0 && pos >= p.window) lo = max(lo, pos - p.window + 1);   // attention.c:194-196
+    if (lo < 0) lo = 0;
+    if (hi < lo) hi = lo;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p)
+{
+    using S = PrefillShape<HD>;
+    constexpr int BN = S::BN;
+
+    const int n_qtiles = gridDim.x;
+    const int qt = n_qtiles - 1 - static_cast<int>(blockIdx.x);   // heaviest (causal) tiles first
+    const int h = blockIdx.y;
+    const int b = blockIdx.z;
+    const int q0 = qt * kBM;
+    const int kvh = h / p.group;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Barriers *bars = reinterpret_cast<Barriers *>(smem + S::kOffBar);
+
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+
+    // ---- set-up: barriers, key range of the tile, TMEM ----
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bars->q_full), 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(smem_u32(&bars->k_full[s]), 1);
+            mbar_init(smem_u32(&bars->k_empty[s]), 1);
+            mbar_init(smem_u32(&bars->v_full[s]), 1);
+            mbar_init(smem_u32(&bars->v_empty[s]), 1);
+            mbar_init(smem_u32(&bars->s_full[s]), 1);
+            mbar_init(smem_u32(&bars->p_full[s]), kSoftmaxThreads);
+        }
+        mbar_init(smem_u32(&bars->o_done), 1);
+        mbar_init(smem_u32(&bars->mma_done), 1);
+        bars->lo_min = 0x7fffffff;
+        bars->hi_max = 0;
+        fence_mbar_init();
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(smem_u32(&bars->tmem_base), S::kTmCols);
+        tmem_relinquish();
+    }
+    int my_lo = 0, my_hi = 0;
+    bool my_written = false;
+    const int row = q0 + threadIdx.x;   // meaningful for softmax threads
+    const bool row_valid = threadIdx.x < kSoftmaxThreads && row < p.seq_q;
+    __syncthreads();
+    if (row_valid) {
+        row_range(p, row, my_lo, my_hi, my_written);
+        if (my_hi > my_lo) {
+            atomicMin(&bars->lo_min, my_lo);
+            atomicMax(&bars->hi_max, my_hi);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    const int lo_min = bars->lo_min;
+    const int hi_max = bars->hi_max;
+    const int n_tiles = hi_max > lo_min ? (hi_max - lo_min + BN - 1) / BN : 0;
+
+    uint8_t *sQ = smem + S::kOffQ;
+    uint8_t *sK = smem + S::kOffK;
+    uint8_t *sV = smem + S::kOffV;
+
+    if (warp == kProducerWarp) {
+        // ================= TMA producer =================
+        if (lane == 0 && n_tiles > 0) {
+            tma_prefetch_desc(&p.tq);
+            tma_prefetch_desc(&p.tk);
+            tma_prefetch_desc(&p.tv);
+            const uint32_t qb = smem_u32(&bars->q_full);
+            mbar_arrive_expect_tx(qb, S::kQBytes);
+#pragma unroll
+            for (int sub = 0; sub < S::kSub; ++sub)
+                tma_load_3d(smem_u32(sQ + sub * S::kQSubBytes), &p.tq, qb, h * HD + sub * 64, q0, b);
+            int kiss = 0, viss = 0;
+            bool ok = true;
+            for (int j = 0; j < n_tiles && ok; ++j) {
+                const int st = j & 1;
+                const int key0 = lo_min + j * BN;
+                if (j >= 2 && !mbar_wait(smem_u32(&bars->k_empty[st]), ((j >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t kb = smem_u32(&bars->k_full[st]);
+                mbar_arrive_expect_tx(kb, S::kKvBytes);
+#pragma unroll
+                for (int sub = 0; sub < S::kSub; ++sub)
+                    tma_load_3d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb,
+                                kvh * HD + sub * 64, key0, b);
+                ++kiss;
+                if (j >= 2 && !mbar_wait(smem_u32(&bars->v_empty[st]), ((j >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t vb = smem_u32(&bars->v_full[st]);
+                mbar_arrive_expect_tx(vb, S::kKvBytes);
+#pragma unroll
+                for (int sub = 0; sub < S::kSub; ++sub)
+                    tma_load_3d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb,
+                                kvh * HD + sub * 64, key0, b);
+                ++viss;
+            }
+            // Drain: whatever was issued must land before the CTA can exit.
+            mbar_wait(smem_u32(&bars->q_full), 0, p.err, kErrDrain);
+            for (int j = max(0, kiss - 2); j < kiss; ++j)
+                if (!mbar_wait(smem_u32(&bars->k_full[j & 1]), (j >> 1) & 1, p.err, kErrDrain)) break;
+            for (int j = max(0, viss - 2); j < viss; ++j)
+                if (!mbar_wait(smem_u32(&bars->v_full[j & 1]), (j >> 1) & 1, p.err, kErrDrain)) break;
+        }
+    } else if (warp == kMmaWarp) {
+        // ================= tcgen05 issuer (one thread) =================
+        if (lane == 0 && n_tiles > 0) {
+            constexpr uint32_t idesc_s = umma_idesc_f16(kBM, BN, true, false);
+            constexpr uint32_t idesc_pv = umma_idesc_f16(kBM, HD, false, true);
+            const uint32_t q_addr = smem_u32(sQ);
+            bool ok = mbar_wait(smem_u32(&bars->q_full), 0, p.err, kErrWaitTmaFull);
+            auto issue_pv = [&](int i) -> bool {
+                const int st = i & 1;
+                if (!mbar_wait(smem_u32(&bars->p_full[st]), (i >> 1) & 1, p.err, kErrWaitSoftmax)) return false;
+                if (!mbar_wait(smem_u32(&bars->v_full[st]), (i >> 1) & 1, p.err, kErrWaitTmaFull)) return false;
+                tc_fence_after();
+                const uint32_t v_addr = smem_u32(sV + st * S::kKvBytes);
+                const uint32_t p_col = tmem + (st ? S::kTmS1 : S::kTmS0);
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; ++kk) {
+                    const uint64_t bdesc = umma_sdesc_sw128(v_addr + kk * 16 * 128, S::kKvSubBytes, 1024);
+                    umma_ts(tmem + S::kTmO, p_col + kk * 8, bdesc, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&bars->o_done));
+                umma_commit(smem_u32(&bars->v_empty[st]));
+                return true;
+            };
+            for (int j = 0; j < n_tiles && ok; ++j) {
+                const int st = j & 1;
+                if (!mbar_wait(smem_u32(&bars->k_full[st]), (j >> 1) & 1, p.err, kErrWaitTmaFull)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(sK + st * S::kKvBytes);
+                const uint32_t s_col = tmem + (st ? S::kTmS1 : S::kTmS0);
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk) {
+                    const uint32_t off = (kk & 3) * 32;   // 16 halves = 32 B along K
+                    const uint64_t adesc = umma_sdesc_sw128(q_addr + (kk >> 2) * S::kQSubBytes + off, 16, 1024);
+                    const uint64_t bdesc = umma_sdesc_sw128(k_addr + (kk >> 2) * S::kKvSubBytes + off, 16, 1024);
+                    umma_ss(s_col, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&bars->s_full[st]));
+                umma_commit(smem_u32(&bars->k_empty[st]));
+                if (j >= 1 && !issue_pv(j - 1)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (ok) issue_pv(n_tiles - 1);
+            // Every MMA must be complete before TMEM is released.
+            umma_commit(smem_u32(&bars->mma_done));
+            mbar_wait(smem_u32(&bars->mma_done), 0, p.err, kErrDrain);
+        }
+    } else {
+        // ================= softmax: thread owns query row `row` =================
+        // tcgen05.ld / tcgen05.st are warp-collective, so every branch around them is
+        // made warp-uniform (votes) and per-row decisions only select values.
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        const float cap = p.softcap;
+        const float inv_cap = cap > 0.f ? 1.f / cap : 0.f;
+        const float kLog2e = 1.4426950408889634f;
+        float m = -INFINITY;   // running maximum in log2 units
+        float l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < n_tiles; ++j) {
+            const int st = j & 1;
+            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->s_full[st]), (j >> 1) & 1, p.err, kErrWaitMma));
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t s_col = lane_base + (st ? S::kTmS1 : S::kTmS0);
+            float t[BN];
+            {
+                uint32_t r[32];
+#pragma unroll
+                for (int c = 0; c < BN / 32; ++c) {
+                    tmem_ld32(s_col + c * 32, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(r[i]);
+                }
+            }
+            const int key0 = lo_min + j * BN;
+            const bool full_tile = row_valid && key0 >= my_lo && key0 + BN <= my_hi;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < BN; ++c) {
+                float x = t[c];
+                if (cap > 0.f) x = cap * tanhf(x * p.scale * inv_cap) * kLog2e;
+                else x = x * p.scale_log2;
+                if (!full_tile) {
+                    const int key = key0 + c;
+                    if (!row_valid || key < my_lo || key >= my_hi) x = -INFINITY;
+                }
+                t[c] = x;
+                mx = fmaxf(mx, x);
+            }
+            // The running maximum moves only when the row maximum grew by > 2^8 (or on the
+            // first tile with a visible key, when O of this row is still zero).
+            const bool need = m != -INFINITY && mx > m + kRescaleThreshold;
+            if (__any_sync(0xffffffffu, need)) {
+                // O holds P_0..P_{j-1} V: wait for PV_{j-1}, then rescale the rows that need it.
+                ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done), (j - 1) & 1, p.err, kErrWaitMma));
+                if (!ok) break;
+                tc_fence_after();
+                const float f = need ? fast_exp2(m - mx) : 1.f;
+                uint32_t r[32];
+#pragma unroll
+                for (int c = 0; c < HD / 32; ++c) {
+                    tmem_ld32(lane_base + S::kTmO + c * 32, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+                    tmem_st32(lane_base + S::kTmO + c * 32, r);
+                }
+                l *= f;
+            }
+            if (need || (m == -INFINITY && mx > -INFINITY)) m = mx;
+            // P = exp2(t - m) as fp16 pairs over the first BN/2 columns of this S buffer.
+            float psum = 0.f;
+            {
+                const bool live = m != -INFINITY;
+                uint32_t r[32];
+#pragma unroll
+                for (int c = 0; c < BN / 64; ++c) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float e0 = live ? fast_exp2(t[c * 64 + 2 * i] - m) : 0.f;
+                        const float e1 = live ? fast_exp2(t[c * 64 + 2 * i + 1] - m) : 0.f;
+                        psum += e0 + e1;
+                        r[i] = pack_f16x2(e0, e1);
+                    }
+                    tmem_st32(s_col + c * 32, r);
+                }
+            }
+            l += psum;
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(smem_u32(&bars->p_full[st]));
+        }
+        // ---- epilogue: O / l -> out (fp32) ----
+        bool have_o = ok && n_tiles > 0;
+        if (have_o)
+            have_o = __all_sync(0xffffffffu,
+                                mbar_wait(smem_u32(&bars->o_done), (n_tiles - 1) & 1, p.err, kErrWaitMma));
+        tc_fence_after();
+        const bool store = ok && row_valid && my_written;
+        float *orow = p.out + static_cast<long long>(b) * p.out_batch_stride +
+                      static_cast<long long>(store ? row : 0) * p.out_row_stride + static_cast<long long>(h) * HD;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+            if (have_o) {
+                tmem_ld32(lane_base + S::kTmO + c * 32, r);
+                tmem_ld_wait();
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) r[i] = 0u;
+            }
+            if (store) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                    float4 v = make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
+                                           __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+                    *reinterpret_cast<float4 *>(orow + c * 32 + i) = v;
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem, S::kTmCols);
+    }
+}
+
+template <int HD>
+int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t out_batch_stride,
+                   const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride, const uint16_t *k,
+                   int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
+                   int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads, int n_kv_heads,
+                   float scale, int mask_kind, int q_offset, int prefix_len, int window, float softcap,
+                   const int *window_starts, int n_windows)
+{
+    using S = PrefillShape<HD>;
+    PrefillParams p;
+    memset(&p, 0, sizeof(p));
+    // A tensor map needs at least one row; with seq_k == 0 no key tile is ever loaded.
+    const int kv_rows = seq_k > 0 ? seq_k : 1;
+    const int64_t qb = batch > 1 ? q_batch_stride : static_cast<int64_t>(seq_q) * q_row_stride;
+    const int64_t kb = batch > 1 ? k_batch_stride : static_cast<int64_t>(kv_rows) * k_row_stride;
+    const int64_t vb = batch > 1 ? v_batch_stride : static_cast<int64_t>(kv_rows) * v_row_stride;
+    if (!make_tmap_3d(&p.tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<int64_t>(n_heads) * HD, seq_q, batch,
+                      q_row_stride, qb, 64, kBM))
+        return SMOL_B200_ERR_CUDA;
+    if (!make_tmap_3d(&p.tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<int64_t>(n_kv_heads) * HD, kv_rows,
+                      batch, k_row_stride, kb, 64, S::BN))
+        return SMOL_B200_ERR_CUDA;
+    if (!make_tmap_3d(&p.tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<int64_t>(n_kv_heads) * HD, kv_rows,
+                      batch, v_row_stride, vb, 64, S::BN))
+        return SMOL_B200_ERR_CUDA;
+    p.out = out;
+    p.out_row_stride = out_row_stride;
+    p.out_batch_stride = out_batch_stride;
+    p.window_starts = window_starts;
+    p.n_windows = n_windows;
+    p.err = device_error_word();
+    p.seq_q = seq_q;
+    p.seq_k = seq_k;
+    p.n_heads = n_heads;
+    p.group = n_heads / n_kv_heads;
+    p.mask_kind = mask_kind;
+    p.q_offset = q_offset;
+    p.prefix_len = prefix_len;
+    p.window = window;
+    p.scale = scale;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.softcap = softcap;
+
+    static bool attr_set[16] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 16 && !attr_set[dev]) {
+        if (cudaFuncSetAttribute(prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes) !=
+            cudaSuccess)
+            return SMOL_B200_ERR_CUDA;
+        attr_set[dev] = true;
+    }
+    const int n_qtiles = (seq_q + kBM - 1) / kBM;
+    dim3 grid(n_qtiles, n_heads, batch);
+    prefill_kernel<HD><<<grid, kThreads, S::kSmemBytes, st>>>(p);
+    return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
+}
+
+}  // namespace
+
+int prefill_attention(cudaStream_t st, float *out, int64_t out_row_stride, int64_t out_batch_stride,
+                      const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride, const uint16_t *k,
+                      int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
+                      int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads, int n_kv_heads,
+                      int head_dim, float scale, int mask_kind, int q_offset, int prefix_len, int window,
+                      float softcap, const int *window_starts, int n_windows)
+{
+    if (batch <= 0 || seq_q <= 0) return SMOL_B200_OK;
+    if (!out || !q || !k || !v || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0 || seq_k < 0 ||
+        batch > 65535 || n_heads > 65535 || mask_kind < 0 || mask_kind > SMOL_MASK_FULL)
+        return SMOL_B200_ERR_ARGS;
+    if (mask_kind == SMOL_MASK_WINDOWS && (!window_starts || n_windows <= 0)) return SMOL_B200_ERR_ARGS;
+    if (head_dim != 64 && head_dim != 128 && head_dim != 256) return SMOL_B200_ERR_ARGS;
+    const uintptr_t align = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
+                            reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out);
+    if (align & 15) return SMOL_B200_ERR_ARGS;
+    if ((q_row_stride | k_row_stride | v_row_stride) & 7) return SMOL_B200_ERR_ARGS;
+    if (batch > 1 && ((q_batch_stride | k_batch_stride | v_batch_stride) & 7)) return SMOL_B200_ERR_ARGS;
+    if ((out_row_stride & 3) || (batch > 1 && (out_batch_stride & 3))) return SMOL_B200_ERR_ARGS;
+    if (q_row_stride < static_cast<int64_t>(n_heads) * head_dim ||
+        k_row_stride < static_cast<int64_t>(n_kv_heads) * head_dim ||
+        v_row_stride < static_cast<int64_t>(n_kv_heads) * head_dim)
+        return SMOL_B200_ERR_ARGS;
+#define SMOL_PREFILL_ARGS                                                                                      \
+    st, out, out_row_stride, out_batch_stride, q, q_row_stride, q_batch_stride, k, k_row_stride, k_batch_stride, \
+        v, v_row_stride, v_batch_stride, batch, seq_q, seq_k, n_heads, n_kv_heads, scale,      \
+        mask_kind, q_offset, prefix_len, window, softcap, window_starts, n_windows
+    switch (head_dim) {
+    case 64: return launch_prefill<64>(SMOL_PREFILL_ARGS);
+    case 128: return launch_prefill<128>(SMOL_PREFILL_ARGS);
+    default: return launch_prefill<256>(SMOL_PREFILL_ARGS);
+    }
+#undef SMOL_PREFILL_ARGS
+}
+
+}  // namespace smolb200

@@ -1,0 +1,79 @@
+// runtime.h -- host-side internals shared by the translation units of libsmol_b200.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "smol_b200.h"
+
+namespace smolb200 {
+
+// ---- error state (process-wide, sticky until smol_cuda_clear_error) ----
+void set_error(int code, const char *what);
+bool cuda_check(cudaError_t e, const char *what);   // records SMOL_B200_ERR_CUDA on failure
+
+// ---- per-device context ----
+// Device error word of the current device (zeroed at creation).
+unsigned *device_error_word();
+// Stream used by the drop-in (Part 1) entry points of the current device.
+cudaStream_t legacy_stream();
+// Grow-only device scratch of the current device for the drop-in entry points.
+// Slot i is an independent buffer.  Returns NULL (error recorded) on failure.
+void *legacy_scratch(int slot, size_t bytes);
+// True when `p` is device or managed memory the current device can address.
+bool is_device_pointer(const void *p);
+// Number of the current device, or -1 (error recorded) when none is usable.
+int current_device();
+
+// ---- TMA descriptors ----
+// 2-D tensor [rows, inner] of 2-byte elements, row stride `row_stride` elements,
+// box = box_rows x box_inner, 128-byte swizzle (box_inner*2 must be 128).
+bool make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int64_t inner,
+                  int64_t rows, int box_inner, int box_rows, int64_t row_stride = -1);
+// 3-D tensor [outer, rows, inner] with strides in elements.
+bool make_tmap_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int64_t inner,
+                  int64_t rows, int64_t outer, int64_t row_stride, int64_t outer_stride, int box_inner,
+                  int box_rows);
+
+// ---- kernels (implemented in the .cu files) ----
+size_t decode_workspace_bytes(int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, int head_dim);
+int decode_attention(cudaStream_t st, float *out, const void *q, int q_is_bf16, const uint16_t *k_pool,
+                     const uint16_t *v_pool, int64_t pool_rows, const int64_t *seq_row0, const int *kv_len,
+                     int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, int head_dim, float scale,
+                     int window, float softcap, void *workspace, size_t workspace_bytes);
+
+int prefill_attention(cudaStream_t st, float *out, int64_t out_row_stride, int64_t out_batch_stride,
+                      const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride, const uint16_t *k,
+                      int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
+                      int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads, int n_kv_heads,
+                      int head_dim, float scale, int mask_kind, int q_offset, int prefix_len, int window,
+                      float softcap, const int *window_starts, int n_windows);
+
+int qknorm_rope_append(cudaStream_t st, const float *q_in, const float *k_in, const float *v_in, int n_tokens,
+                       int n_heads, int n_kv_heads, int head_dim, const float *q_norm_w, const float *k_norm_w,
+                       float eps, const float *rope_cos, const float *rope_sin, int rope_interleaved,
+                       const int *positions, const int64_t *slots, float *q_out_f32, uint16_t *q_out_bf16,
+                       uint16_t *k_cache_bf16, uint16_t *v_cache_f16, int64_t cache_rows);
+
+// In-place fp32 kernels behind the drop-in RoPE / RMSNorm entry points.
+int launch_rms_norm_per_head(cudaStream_t st, float *x, const float *w, int seq_len, int n_heads, int head_dim,
+                             float eps);
+int launch_rms_norm(cudaStream_t st, float *out, const float *x, const float *w, int seq_len, int hidden,
+                    float eps);
+int launch_rope(cudaStream_t st, float *x, const float *cos_vals, const float *sin_vals, int seq, int n_heads,
+                int head_dim, int interleaved);
+
+// Staging kernels of the drop-in attention path: fp32 rows -> padded bf16 / fp16 rows.
+int launch_pack_rows(cudaStream_t st, uint16_t *dst, int64_t dst_stride, int dst_width, const float *src,
+                     int64_t src_stride, int src_heads, int head_dim, int padded_hd, int64_t rows, int to_f16);
+int launch_unpack_rows(cudaStream_t st, float *dst, int64_t dst_stride, const float *src, int64_t src_stride,
+                       int heads, int head_dim, int padded_hd, int64_t rows);
+
+// Per-token (position, slot) of a decode step: positions[b] = kv_len[b],
+// slots[b] = seq_row0[b] + kv_len[b], kv_len_next[b] = kv_len[b] + 1.
+int launch_decode_step_index(cudaStream_t st, int *positions, int64_t *slots, int *kv_len_next,
+                             const int64_t *seq_row0, const int *kv_len, int n_seqs);
+
+}  // namespace smolb200

@@ -1,0 +1,243 @@
+"""smol_b200 -- Python binding of libsmol_b200.so (the C ABI in include/smol_b200.h).
+
+This is the ctypes stub a Python caller of the reference would bind
+(``ctypes.CDLL("libsmol_b200.so")``), with typed wrappers for tests and bench.py.
+Device buffers are passed as torch CUDA tensors (torch is used for allocation and
+streams only); host buffers of the drop-in entry points are numpy float32 arrays.
+
+The product path is the CUDA library: if ``libsmol_b200.so`` is missing this module
+raises instead of computing anything on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libsmol_b200.so")
+HEADER_PATH = os.path.join(os.path.dirname(HERE), "include", "smol_b200.h")
+
+MASK_CAUSAL, MASK_PREFIX_LM, MASK_WINDOWS, MASK_FULL = 0, 1, 2, 3
+
+ERR_NAMES = {0: "ok", 1: "args", 2: "cuda", 3: "no_device", 4: "oom", 5: "watchdog", 6: "workspace"}
+
+
+class SmolB200Error(RuntimeError):
+    """A call into libsmol_b200 returned a non-zero status."""
+
+
+_lib = None
+
+_c_int, _c_float, _c_void = ctypes.c_int, ctypes.c_float, ctypes.c_void_p
+_c_i64, _c_size = ctypes.c_int64, ctypes.c_size_t
+_fp = ctypes.POINTER(ctypes.c_float)
+_ip = ctypes.POINTER(ctypes.c_int)
+
+# name -> (restype, argtypes)
+_SIGNATURES = {
+    # Part 1 (smol_kernels.h)
+    "smol_bidirectional_attention": (None, [_c_void] * 4 + [_c_int, _c_int, _c_int, _c_float, _c_void, _c_int]),
+    "smol_causal_attention": (None, [_c_void] * 4 + [_c_int] * 5 + [_c_float, _c_int]),
+    "smol_sliding_window_attention": (None, [_c_void] * 4 + [_c_int] * 5 + [_c_float, _c_int, _c_int]),
+    "smol_causal_attention_softcap": (None, [_c_void] * 4 + [_c_int] * 5 + [_c_float, _c_int, _c_float]),
+    "smol_sliding_window_attention_softcap": (
+        None, [_c_void] * 4 + [_c_int] * 5 + [_c_float, _c_int, _c_int, _c_float]),
+    "smol_sinusoidal_pe": (None, [_c_void, _c_int, _c_int]),
+    "smol_compute_rope_neox": (None, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_float]),
+    "smol_compute_rope_interleaved": (None, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_float]),
+    "smol_apply_rope_neox": (None, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_int]),
+    "smol_apply_rope_interleaved": (None, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_int]),
+    "smol_rms_norm": (None, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_float]),
+    "smol_rms_norm_per_head": (None, [_c_void, _c_void, _c_int, _c_int, _c_int, _c_float]),
+    # Part 2
+    "smol_cuda_last_error": (_c_int, []),
+    "smol_cuda_error_string": (ctypes.c_char_p, [_c_int]),
+    "smol_cuda_clear_error": (None, []),
+    "smol_cuda_device_error": (ctypes.c_uint, []),
+    # Part 3
+    "smol_b200_qknorm_rope_append": (
+        _c_int, [_c_void, _c_void, _c_void, _c_void, _c_int, _c_int, _c_int, _c_int, _c_void, _c_void, _c_float,
+                 _c_void, _c_void, _c_int, _c_void, _c_void, _c_void, _c_void, _c_void, _c_void, _c_i64]),
+    "smol_b200_decode_workspace_bytes": (_c_size, [_c_int] * 5),
+    "smol_b200_decode_attention": (
+        _c_int, [_c_void, _c_void, _c_void, _c_int, _c_void, _c_void, _c_i64, _c_void, _c_void, _c_int, _c_int,
+                 _c_int, _c_int, _c_int, _c_float, _c_int, _c_float, _c_void, _c_size]),
+    "smol_b200_prefill_attention": (
+        _c_int, [_c_void, _c_void, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void, _c_i64,
+                 _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _c_int, _c_int, _c_int,
+                 _c_float, _c_void, _c_int]),
+    "smol_b200_decode_step_scratch_bytes": (_c_size, [_c_int] * 5),
+    "smol_b200_decode_step_host": (
+        _c_int, [_c_void, _c_void, _c_void, _c_void, _c_void, _c_int, _c_int, _c_int, _c_int, _c_void, _c_void,
+                 _c_float, _c_void, _c_void, _c_int, _c_void, _c_void, _c_i64, _c_void, _c_void, _c_int, _c_float,
+                 _c_void, _c_size]),
+}
+
+
+def header_symbols(path: str = HEADER_PATH) -> list[str]:
+    """Names of every function include/smol_b200.h declares with SMOL_B200_API."""
+    text = open(path).read()
+    return re.findall(r"SMOL_B200_API\s+[\w\s\*]+?\b(\w+)\s*\(", text)
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (raises SmolB200Error when it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise SmolB200Error(f"{LIB_PATH} is missing: build it with `make -C smol-genius_b200` "
+                                "(there is no CPU fallback)")
+        l = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGNATURES.items():
+            f = getattr(l, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = l
+    return _lib
+
+
+def _ptr(x) -> int | None:
+    """Address of a torch tensor / numpy array (None -> NULL)."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if isinstance(x, np.ndarray):
+        if not x.flags["C_CONTIGUOUS"]:
+            raise ValueError("numpy arrays passed to libsmol_b200 must be C-contiguous")
+        return x.ctypes.data
+    return x.data_ptr()
+
+
+def _stream(stream) -> int | None:
+    if stream is None:
+        return None
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise SmolB200Error(f"{what} failed: {ERR_NAMES.get(rc, rc)} "
+                            f"({lib().smol_cuda_error_string(rc).decode()})")
+
+
+def last_error() -> int:
+    return lib().smol_cuda_last_error()
+
+
+def clear_error() -> None:
+    lib().smol_cuda_clear_error()
+
+
+def device_error() -> int:
+    return lib().smol_cuda_device_error()
+
+
+# ---------------------------------------------------------------------------
+# Part 1: drop-in entry points (host numpy or device torch buffers)
+# ---------------------------------------------------------------------------
+def causal_attention(out, Q, K, V, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale, q_offset,
+                     window=0, cap=0.0):
+    L = lib()
+    a = (_ptr(out), _ptr(Q), _ptr(K), _ptr(V), seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale, q_offset)
+    if window > 0 and cap > 0:
+        L.smol_sliding_window_attention_softcap(*a, window, cap)
+    elif window > 0:
+        L.smol_sliding_window_attention(*a, window)
+    elif cap > 0:
+        L.smol_causal_attention_softcap(*a, cap)
+    else:
+        L.smol_causal_attention(*a)
+
+
+def bidirectional_attention(out, Q, K, V, seq, n_heads, head_dim, scale, window_starts):
+    ws = np.ascontiguousarray(window_starts, dtype=np.int32)
+    lib().smol_bidirectional_attention(_ptr(out), _ptr(Q), _ptr(K), _ptr(V), seq, n_heads, head_dim, scale,
+                                       _ptr(ws), len(ws) - 1)
+
+
+def apply_rope(x, cos, sin, seq, n_heads, head_dim, interleaved=False):
+    f = lib().smol_apply_rope_interleaved if interleaved else lib().smol_apply_rope_neox
+    f(_ptr(x), _ptr(cos), _ptr(sin), seq, n_heads, head_dim)
+
+
+def compute_rope(cos_out, sin_out, positions, seq, head_dim, theta, interleaved=False):
+    f = lib().smol_compute_rope_interleaved if interleaved else lib().smol_compute_rope_neox
+    f(_ptr(cos_out), _ptr(sin_out), _ptr(positions), seq, head_dim, theta)
+
+
+def rms_norm_per_head(x, w, seq, n_heads, head_dim, eps):
+    lib().smol_rms_norm_per_head(_ptr(x), _ptr(w), seq, n_heads, head_dim, eps)
+
+
+def rms_norm(out, x, w, seq, hidden, eps):
+    lib().smol_rms_norm(_ptr(out), _ptr(x), _ptr(w), seq, hidden, eps)
+
+
+def sinusoidal_pe(pe, n_pos, d_model):
+    lib().smol_sinusoidal_pe(_ptr(pe), n_pos, d_model)
+
+
+# ---------------------------------------------------------------------------
+# Part 3: device API (torch CUDA tensors)
+# ---------------------------------------------------------------------------
+def qknorm_rope_append(q_in, k_in, v_in, n_tokens, n_heads, n_kv_heads, head_dim, q_norm_w, k_norm_w, eps,
+                       rope_cos, rope_sin, interleaved, positions, slots, q_out_f32, q_out_bf16, k_cache, v_cache,
+                       cache_rows, stream=None):
+    rc = lib().smol_b200_qknorm_rope_append(
+        _stream(stream), _ptr(q_in), _ptr(k_in), _ptr(v_in), n_tokens, n_heads, n_kv_heads, head_dim,
+        _ptr(q_norm_w), _ptr(k_norm_w), eps, _ptr(rope_cos), _ptr(rope_sin), int(interleaved), _ptr(positions),
+        _ptr(slots), _ptr(q_out_f32), _ptr(q_out_bf16), _ptr(k_cache), _ptr(v_cache), cache_rows)
+    check(rc, "smol_b200_qknorm_rope_append")
+
+
+def decode_workspace_bytes(n_seqs, max_kv_len, n_heads, n_kv_heads, head_dim) -> int:
+    return lib().smol_b200_decode_workspace_bytes(n_seqs, max_kv_len, n_heads, n_kv_heads, head_dim)
+
+
+def decode_attention(out, q, k_pool, v_pool, pool_rows, seq_row0, kv_len, n_seqs, max_kv_len, n_heads, n_kv_heads,
+                     head_dim, scale, workspace, window=0, softcap=0.0, stream=None):
+    import torch
+    q_is_bf16 = 1 if q.dtype == torch.bfloat16 else 0
+    rc = lib().smol_b200_decode_attention(
+        _stream(stream), _ptr(out), _ptr(q), q_is_bf16, _ptr(k_pool), _ptr(v_pool), pool_rows, _ptr(seq_row0),
+        _ptr(kv_len), n_seqs, max_kv_len, n_heads, n_kv_heads, head_dim, scale, window, softcap, _ptr(workspace),
+        workspace.numel() * workspace.element_size())
+    check(rc, "smol_b200_decode_attention")
+
+
+def prefill_attention(out, q, k, v, batch, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale, mask_kind=MASK_CAUSAL,
+                      q_offset=0, prefix_len=0, window=0, softcap=0.0, window_starts=None, stream=None,
+                      strides=None):
+    """q/k: bf16 [batch, seq, heads*hd]; v: fp16; out: fp32 [batch, seq_q, n_heads*hd] (contiguous unless
+    `strides` = ((out_row, out_batch), (q_row, q_batch), (k_row, k_batch), (v_row, v_batch)) in elements)."""
+    if strides is None:
+        qw, kw = n_heads * head_dim, n_kv_heads * head_dim
+        strides = ((qw, seq_q * qw), (qw, seq_q * qw), (kw, seq_k * kw), (kw, seq_k * kw))
+    (ors, obs), (qrs, qbs), (krs, kbs), (vrs, vbs) = strides
+    nw = 0 if window_starts is None else window_starts.numel() - 1
+    rc = lib().smol_b200_prefill_attention(
+        _stream(stream), _ptr(out), ors, obs, _ptr(q), qrs, qbs, _ptr(k), krs, kbs, _ptr(v), vrs, vbs, batch, seq_q,
+        seq_k, n_heads, n_kv_heads, head_dim, scale, mask_kind, q_offset, prefix_len, window, softcap,
+        _ptr(window_starts), nw)
+    check(rc, "smol_b200_prefill_attention")
+
+
+def decode_step_scratch_bytes(n_seqs, max_kv_len, n_heads, n_kv_heads, head_dim) -> int:
+    return lib().smol_b200_decode_step_scratch_bytes(n_seqs, max_kv_len, n_heads, n_kv_heads, head_dim)
+
+
+def decode_step_host(out_host, q_host, k_host, v_host, n_seqs, n_heads, n_kv_heads, head_dim, q_norm_w, k_norm_w, eps,
+                     rope_cos, rope_sin, interleaved, k_pool, v_pool, pool_rows, seq_row0, kv_len, max_kv_len, scale,
+                     scratch, stream=None):
+    rc = lib().smol_b200_decode_step_host(
+        _stream(stream), _ptr(out_host), _ptr(q_host), _ptr(k_host), _ptr(v_host), n_seqs, n_heads, n_kv_heads,
+        head_dim, _ptr(q_norm_w), _ptr(k_norm_w), eps, _ptr(rope_cos), _ptr(rope_sin), int(interleaved),
+        _ptr(k_pool), _ptr(v_pool), pool_rows, _ptr(seq_row0), _ptr(kv_len), max_kv_len, scale, _ptr(scratch),
+        scratch.numel() * scratch.element_size())
+    check(rc, "smol_b200_decode_step_host")

@@ -1,0 +1,70 @@
+"""Shared test set-up.
+
+* registers the ``gpu`` marker (tests that need a B200; the CPU suite runs with
+  ``-m "not gpu"``);
+* builds the oracle (oracle/libsmol_oracle.so) and the product library
+  (smol-genius_b200/libsmol_b200.so) when they are missing, so a fresh checkout
+  can run the suite directly;
+* puts the oracle and the binding on sys.path.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ORACLE_DIR = os.path.join(ROOT, "oracle")
+PKG_DIR = os.path.join(ROOT, "smol-genius_b200")
+GOLDEN = os.path.join(ROOT, "tests", "golden", "reference_cases.npz")
+
+for p in (ORACLE_DIR, PKG_DIR):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+# Tolerances of the north star: attention outputs vs the fp32 reference fed the same
+# bf16-rounded inputs.
+REL_L2_TOL = 1e-3
+MAX_ABS_TOL = 1e-2
+
+
+def _ensure_built() -> None:
+    if not os.path.exists(os.path.join(ORACLE_DIR, "libsmol_oracle.so")):
+        subprocess.run(["make", "-C", ORACLE_DIR, "oracle"], check=True, capture_output=True)
+    if not os.path.exists(os.path.join(PKG_DIR, "libsmol_b200.so")):
+        subprocess.run(["make", "-C", PKG_DIR, "-j8"], check=True, capture_output=True)
+
+
+_ensure_built()
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs an sm_100 (B200) CUDA device")
+
+
+@pytest.fixture(scope="session")
+def golden():
+    return np.load(GOLDEN)
+
+
+@pytest.fixture(scope="session")
+def cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch.device("cuda:0")
+
+
+def assert_close(got, want, what=""):
+    import pyoracle
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    assert got.shape == want.shape, f"{what}: shape {got.shape} vs {want.shape}"
+    assert np.all(np.isfinite(got)), f"{what}: non-finite values"
+    e = pyoracle.rel_l2(got, want)
+    m = float(np.abs(got - want).max()) if got.size else 0.0
+    assert e <= REL_L2_TOL and m <= MAX_ABS_TOL, f"{what}: rel-L2 {e:.3e} (tol {REL_L2_TOL}), max-abs {m:.3e}"
+    return e, m

@@ -1,0 +1,110 @@
+"""The C ABI of libsmol_b200.so, checked without a GPU.
+
+* the library loads and exports every function include/smol_b200.h declares;
+* the drop-in prototypes are exactly those of the reference's
+  common/kernels/smol_kernels.h:86-161 (types and order of parameters);
+* without a usable device a drop-in call records SMOL_B200_ERR_NO_DEVICE and
+  zero-fills its output -- it never computes on the CPU.
+"""
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+import smol_b200
+
+# smol_kernels.h:86-161 -- the prototypes attention.o, rope.o and rmsnorm.o export.
+REFERENCE_PROTOTYPES = """
+void smol_rms_norm(float *out, const float *x, const float *weight, int seq_len, int hidden, float eps);
+void smol_rms_norm_per_head(float *x, const float *weight, int seq_len, int n_heads, int head_dim, float eps);
+void smol_bidirectional_attention(float *out, const float *Q, const float *K, const float *V, int seq, int n_heads, int head_dim, float scale, const int *window_starts, int n_windows);
+void smol_causal_attention(float *out, const float *Q, const float *K, const float *V, int seq_q, int seq_k, int n_heads, int n_kv_heads, int head_dim, float scale, int q_offset);
+void smol_sliding_window_attention(float *out, const float *Q, const float *K, const float *V, int seq_q, int seq_k, int n_heads, int n_kv_heads, int head_dim, float scale, int q_offset, int window_size);
+void smol_causal_attention_softcap(float *out, const float *Q, const float *K, const float *V, int seq_q, int seq_k, int n_heads, int n_kv_heads, int head_dim, float scale, int q_offset, float cap);
+void smol_sliding_window_attention_softcap(float *out, const float *Q, const float *K, const float *V, int seq_q, int seq_k, int n_heads, int n_kv_heads, int head_dim, float scale, int q_offset, int window_size, float cap);
+void smol_sinusoidal_pe(float *pe, int n_pos, int d_model);
+void smol_compute_rope_neox(float *cos_out, float *sin_out, const int *positions, int seq, int head_dim, float theta);
+void smol_apply_rope_neox(float *x, const float *cos_vals, const float *sin_vals, int seq, int n_heads, int head_dim);
+void smol_compute_rope_interleaved(float *cos_out, float *sin_out, const int *positions, int seq, int head_dim, float theta);
+void smol_apply_rope_interleaved(float *x, const float *cos_vals, const float *sin_vals, int seq, int n_heads, int head_dim);
+"""
+
+
+def prototypes(text: str) -> dict[str, tuple[str, tuple[str, ...]]]:
+    """name -> (return type, parameter types) for every smol_* prototype in C text."""
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = text.replace('__attribute__((visibility("default")))', "").replace("SMOL_B200_API", "")
+    out = {}
+    for ret, name, params in re.findall(r"(\w[\w\s\*]*?)\s*\b(smol_\w+)\s*\(([^)]*)\)\s*;", text):
+        types = []
+        for prm in params.split(","):
+            prm = " ".join(prm.split())
+            if not prm or prm == "void":
+                continue
+            t = re.sub(r"\b\w+$", "", prm).replace(" ", "")
+            types.append(t)
+        out[name] = (ret.split()[-1], tuple(types))
+    return out
+
+
+def test_library_exports_every_header_symbol():
+    names = smol_b200.header_symbols()
+    assert len(names) >= 22, names
+    lib = smol_b200.lib()
+    for n in names:
+        assert hasattr(lib, n), n
+    dyn = subprocess.run(["nm", "-D", "--defined-only", smol_b200.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in dyn.splitlines() if " T " in line}
+    assert set(names) <= exported, set(names) - exported
+    # nothing but the header's functions leaks out of the library
+    assert {s for s in exported if s.startswith("smol")} == set(names)
+
+
+def test_dropin_prototypes_match_reference():
+    ours = prototypes(open(smol_b200.HEADER_PATH).read())
+    want = prototypes(REFERENCE_PROTOTYPES)
+    assert len(want) == 12
+    for name, sig in want.items():
+        assert ours.get(name) == sig, (name, ours.get(name), sig)
+
+
+@pytest.mark.skipif(not os.path.exists("/root/reference/common/kernels/smol_kernels.h"),
+                    reason="reference checkout not present")
+def test_dropin_prototypes_match_reference_header_file():
+    ref = prototypes(open("/root/reference/common/kernels/smol_kernels.h").read())
+    ours = prototypes(open(smol_b200.HEADER_PATH).read())
+    for name in prototypes(REFERENCE_PROTOTYPES):
+        assert ours[name] == ref[name], name
+
+
+def test_error_strings():
+    lib = smol_b200.lib()
+    for code in range(7):
+        assert lib.smol_cuda_error_string(code)
+    assert lib.smol_cuda_error_string(0) == b"ok"
+
+
+def test_workspace_sizes():
+    a = smol_b200.decode_workspace_bytes(256, 8192, 16, 8, 128)
+    b = smol_b200.decode_workspace_bytes(512, 8192, 16, 8, 128)
+    assert 0 < a < b
+    assert smol_b200.decode_workspace_bytes(1, 0, 16, 8, 128) > 0
+    assert smol_b200.decode_step_scratch_bytes(256, 8192, 16, 8, 128) > a
+
+
+def test_no_device_fails_loudly():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a device is present: the no-device contract is exercised on CPU-only hosts")
+    smol_b200.clear_error()
+    q = np.ones((4, 2 * 64), np.float32)
+    k = np.ones((4, 64), np.float32)
+    out = np.full((4, 2 * 64), 7.0, np.float32)
+    smol_b200.causal_attention(out, q, k, k, 4, 4, 2, 1, 64, 0.125, 0)
+    assert smol_b200.last_error() == 3          # SMOL_B200_ERR_NO_DEVICE
+    assert np.all(out == 0.0)                   # zero-filled, never computed on the CPU
+    smol_b200.clear_error()
+    assert smol_b200.last_error() == 0
