@@ -45,7 +45,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true")
@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
     ap.add_argument("--seqs", type=int, default=workload.CFG2["n_seqs"], help="sequences per GPU")
     ap.add_argument("--layers", type=int, default=workload.CFG2["layers"])
+    ap.add_argument("--no-decode", action="store_true", help="prefill measurement only (profiling helper)")
+    ap.add_argument("--prefill-shape", default=None, help="B,L override of the cfg 5 prefill shape")
     return ap.parse_args()
 
 
@@ -254,6 +256,8 @@ def run_prefill(args, world, rank, pk):
     import smol_b200
     c = workload.CFG5
     B, L, hq, hkv, hd = c["batch"], c["seq"], c["n_heads"], c["n_kv_heads"], c["head_dim"]
+    if args.prefill_shape:
+        B, L = (int(x) for x in args.prefill_shape.split(","))
     heads = workload.kv_head_groups(hkv, world, rank)
     hkv_r = len(heads)
     hq_r = hq // hkv * hkv_r
@@ -286,7 +290,7 @@ def run_prefill(args, world, rank, pk):
     flops = workload.causal_flops_square(L, hq, hd) * B
     tf = flops / (ms * 1e-3) / 1e12
     smol_b200.check(smol_b200.last_error(), "prefill")
-    return {"workload": "cfg5 causal prefill, 1 layer, batch 4 x 32768, GQA 16/8, hd 128"
+    return {"workload": f"cfg5 causal prefill, 1 layer, batch {B} x {L}, GQA 16/8, hd 128"
                         + (f", KV heads split over {world} GPUs + NCCL all-gather of outputs" if world > 1 else ""),
             "tflops": round(tf, 1), "ms_per_layer": round(ms, 3), "flops_per_layer": flops,
             "frac_of_bf16_peak": round(tf / pk["bf16_tflops"], 4),
@@ -311,6 +315,10 @@ def run_ours(args):
     if not args.no_prefill:
         prefill = run_prefill(args, world, rank, pk)
         torch.cuda.empty_cache()
+    if args.no_decode:
+        if rank == 0:
+            print(json.dumps({"prefill": prefill}))
+        return
 
     # ---- device state: the pooled cache, weights, tables, per-layer indices ----
     gen = torch.Generator(device="cuda").manual_seed(1000 + rank)
