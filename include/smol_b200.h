@@ -169,6 +169,33 @@ SMOL_B200_API int smol_b200_decode_attention(
     int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, int head_dim, float scale,
     int window, float softcap, void *workspace, size_t workspace_bytes);
 
+/* smol_b200_decode_attention without a workspace argument.  No counterpart in the
+ * reference (it has no device memory at all).
+ *
+ * For callers that cannot call cudaMalloc: a plugin living inside another
+ * framework's memory manager that owns all device memory, an allocation-free
+ * real-time serving loop, a host that may not allocate between set-up and
+ * teardown.  The per-chunk partial results that smol_b200_decode_attention keeps
+ * in the caller's workspace live instead in one fixed 16 MiB device array inside
+ * the library; every GPU that loads libsmol_b200.so holds that array until the
+ * process exits.  The call itself allocates nothing.
+ *
+ * Limit: the partial results must fit in 16 MiB - 256 bytes.  The call widens its
+ * key chunks until they fit; when even one chunk per sequence needs more
+ * (n_seqs * n_heads * (head_dim + 2) * 4 bytes) it returns SMOL_B200_ERR_ARGS and
+ * says so in the recorded error.
+ * The first call on each device looks up the array's device address (that device
+ * must be current); make that first call before any stream capture.
+ * Every call shares the one array and leaves its contents behind: two calls whose
+ * kernels overlap on the GPU (different streams, or different host threads) race
+ * on it, so serialise them.  Arguments and results are those of
+ * smol_b200_decode_attention. */
+SMOL_B200_API int smol_b200_decode_attention_noalloc(
+    void *stream, float *out, const void *q, int q_is_bf16, const uint16_t *k_pool,
+    const uint16_t *v_pool, int64_t pool_rows, const int64_t *seq_row0, const int *kv_len,
+    int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, int head_dim, float scale,
+    int window, float softcap);
+
 /* Prefill / encoder attention on tcgen05 tensor cores.  For batch element b, row i
  * of head h attends the keys the mask allows (see SMOL_MASK_*), further limited to
  * [pos-window+1, ...] when window > 0 and capped by softcap when softcap > 0.

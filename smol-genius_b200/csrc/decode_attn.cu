@@ -23,6 +23,11 @@
 // Each CTA merges its 4 warps and writes one partial (O unnormalised, running max,
 // running sum) per Q head; a second kernel merges the chunks of a sequence.
 // Algorithmic traffic: every attended key costs n_kv_heads*hd*2 (K,V) * 2 bytes.
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+
 #include "b200_common.cuh"
 #include "runtime.h"
 
@@ -461,4 +466,161 @@ int decode_attention(cudaStream_t st, float *out, const void *q, int q_is_bf16, 
     }
 }
 
+
+// ===========================================================================
+// Allocation-free variant: smol_b200_decode_attention_noalloc
+// ===========================================================================
+// For callers that cannot call cudaMalloc: code that runs inside another
+// framework's memory manager (which owns all device memory and forbids side
+// allocations), allocation-free real-time paths, and hosts that must not allocate
+// between set-up and teardown.  The split-KV partial results, which the regular
+// entry point keeps in a caller-provided workspace, live here in one file-scope
+// device array of fixed size.  Every GPU that loads this library holds the array
+// until the process exits.
+namespace {
+
+constexpr size_t kNoAllocBytes = size_t(16) << 20;        // 16 MiB of partial results
+constexpr size_t kNoAllocHeader = 256;                    // word 0: watchdog bits of this variant
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mutex;
+void *g_noalloc_ptr[16] = {};
+bool g_noalloc_attr[16][3] = {};
+
+// Set-up, once per device and with that device current: the host-side name of a
+// __device__ array is only a stand-in, so its device address is looked up.
+void *noalloc_scratch_for_current(int dev)
+{
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_ptr[dev]) {
+        void *ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+        if (e != cudaSuccess || !ptr) {
+            cudaGetLastError();
+            set_error(SMOL_B200_ERR_CUDA, "cudaGetSymbolAddress(no-alloc scratch) failed");
+            return nullptr;
+        }
+        g_noalloc_ptr[dev] = ptr;
+    }
+    return g_noalloc_ptr[dev];
+}
+
+template <int HD>
+int launch_decode_noalloc(cudaStream_t st, int dev, uint8_t *scratch, float *out, const void *q, int q_is_bf16,
+                          const uint16_t *k_pool, const uint16_t *v_pool, int64_t pool_rows,
+                          const int64_t *seq_row0, const int *kv_len, int n_seqs, int max_kv_len, int n_heads,
+                          int n_kv_heads, float scale, int window, float softcap)
+{
+    using S = DecodeShape<HD>;
+    DecodeParams p;
+    memset(&p, 0, sizeof(p));
+    const int kv_dim = n_kv_heads * HD;
+    p.group = n_heads / n_kv_heads;
+    p.n_qgroups = (p.group + 7) / 8;
+    // Same chunking as the regular entry point, widened until the partials fit.
+    const size_t cap = kNoAllocBytes - kNoAllocHeader;
+    const int max_len = max_kv_len > 0 ? max_kv_len : 1;
+    int chunk = decode_chunk_size(n_seqs, max_kv_len, n_kv_heads, p.n_qgroups);
+    auto need = [&](int c) {
+        const size_t chunks = static_cast<size_t>((max_len + c - 1) / c);
+        return static_cast<size_t>(n_seqs) * n_heads * chunks * (HD + 2) * sizeof(float);
+    };
+    while (need(chunk) > cap && chunk < max_len) chunk *= 2;
+    if (need(chunk) > cap) {
+        char buf[192];
+        snprintf(buf, sizeof(buf),
+                 "smol_b200_decode_attention_noalloc: %d sequences x %d heads need %zu bytes of partials, "
+                 "the static maximum is %zu",
+                 n_seqs, n_heads, need(chunk), cap);
+        set_error(SMOL_B200_ERR_ARGS, buf);
+        return SMOL_B200_ERR_ARGS;
+    }
+    if (!make_tmap_2d(&p.tmap_k, k_pool, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kv_dim, pool_rows, 64, kKeysPerTile))
+        return SMOL_B200_ERR_CUDA;
+    if (!make_tmap_2d(&p.tmap_v, v_pool, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, kv_dim, pool_rows, 64, kKeysPerTile))
+        return SMOL_B200_ERR_CUDA;
+    p.chunk = chunk;
+    p.max_chunks = (max_len + chunk - 1) / chunk;
+    const size_t n_items = static_cast<size_t>(n_seqs) * n_heads * p.max_chunks;
+    p.part_o = reinterpret_cast<float *>(scratch + kNoAllocHeader);
+    p.part_ml = p.part_o + n_items * HD;
+    p.q = q;
+    p.q_is_bf16 = q_is_bf16;
+    p.seq_row0 = seq_row0;
+    p.kv_len = kv_len;
+    // Watchdog bits go to the library's device error word when this device already
+    // has one (read by smol_cuda_device_error), else to word 0 of the static array.
+    unsigned *err = device_error_word_if_created();
+    p.err = err ? err : reinterpret_cast<unsigned *>(scratch);
+    p.n_heads = n_heads;
+    p.n_kv_heads = n_kv_heads;
+    p.window = window;
+    p.scale = scale;
+    p.softcap = softcap;
+    const int ti = HD == 64 ? 0 : (HD == 128 ? 1 : 2);
+    if (!g_noalloc_attr[dev][ti]) {
+        if (cudaFuncSetAttribute(decode_split_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 S::kSmemBytes) != cudaSuccess)
+            return SMOL_B200_ERR_CUDA;
+        g_noalloc_attr[dev][ti] = true;
+    }
+    dim3 grid(p.max_chunks, n_kv_heads * p.n_qgroups, n_seqs);
+    decode_split_kernel<HD><<<grid, kThreads, S::kSmemBytes, st>>>(p);
+    dim3 cgrid(n_heads, n_seqs);
+    decode_combine_kernel<HD><<<cgrid, HD, 0, st>>>(out, p.part_o, p.part_ml, kv_len, n_heads, p.chunk,
+                                                   p.max_chunks, window, p.err);
+    return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
+}
+
+}  // namespace
+
 }  // namespace smolb200
+
+// Part 3 of smol_b200.h: the allocation-free entry point (declared there).
+extern "C" int smol_b200_decode_attention_noalloc(void *stream, float *out, const void *q, int q_is_bf16,
+                                                  const uint16_t *k_pool, const uint16_t *v_pool, int64_t pool_rows,
+                                                  const int64_t *seq_row0, const int *kv_len, int n_seqs,
+                                                  int max_kv_len, int n_heads, int n_kv_heads, int head_dim,
+                                                  float scale, int window, float softcap)
+{
+    using namespace smolb200;
+    if (n_seqs <= 0) return SMOL_B200_OK;
+    int rc = SMOL_B200_OK;
+    if (!out || !q || !k_pool || !v_pool || !seq_row0 || !kv_len || n_heads <= 0 || n_kv_heads <= 0 ||
+        n_heads % n_kv_heads != 0 || max_kv_len < 0 || pool_rows <= 0 || pool_rows >= (1ll << 31) ||
+        n_seqs > 65535 || n_kv_heads * ((n_heads / n_kv_heads + 7) / 8) > 65535 ||
+        (head_dim != 64 && head_dim != 128 && head_dim != 256) ||
+        ((reinterpret_cast<uintptr_t>(k_pool) | reinterpret_cast<uintptr_t>(v_pool)) & 15) ||
+        (q_is_bf16 ? (reinterpret_cast<uintptr_t>(q) & 3) : (reinterpret_cast<uintptr_t>(q) & 7)))
+        rc = SMOL_B200_ERR_ARGS;
+    int dev = -1;
+    if (rc == SMOL_B200_OK && (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16)) {
+        cudaGetLastError();
+        rc = SMOL_B200_ERR_NO_DEVICE;
+    }
+    uint8_t *scratch = nullptr;
+    if (rc == SMOL_B200_OK) {
+        scratch = static_cast<uint8_t *>(noalloc_scratch_for_current(dev));
+        if (!scratch) rc = SMOL_B200_ERR_CUDA;
+    }
+    if (rc == SMOL_B200_OK) {
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        switch (head_dim) {
+        case 64:
+            rc = launch_decode_noalloc<64>(st, dev, scratch, out, q, q_is_bf16, k_pool, v_pool, pool_rows, seq_row0,
+                                           kv_len, n_seqs, max_kv_len, n_heads, n_kv_heads, scale, window, softcap);
+            break;
+        case 128:
+            rc = launch_decode_noalloc<128>(st, dev, scratch, out, q, q_is_bf16, k_pool, v_pool, pool_rows, seq_row0,
+                                            kv_len, n_seqs, max_kv_len, n_heads, n_kv_heads, scale, window, softcap);
+            break;
+        default:
+            rc = launch_decode_noalloc<256>(st, dev, scratch, out, q, q_is_bf16, k_pool, v_pool, pool_rows, seq_row0,
+                                            kv_len, n_seqs, max_kv_len, n_heads, n_kv_heads, scale, window, softcap);
+            break;
+        }
+    }
+    if (rc != SMOL_B200_OK && smol_cuda_last_error() == SMOL_B200_OK)
+        set_error(rc, "smol_b200_decode_attention_noalloc");
+    return rc;
+}

@@ -112,6 +112,16 @@ unsigned *device_error_word()
     return c ? c->err_word : nullptr;
 }
 
+unsigned *device_error_word_if_created()
+{
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return g_ctx[dev].init ? g_ctx[dev].err_word : nullptr;
+}
+
 cudaStream_t legacy_stream()
 {
     DeviceCtx *c = ctx_for_current();

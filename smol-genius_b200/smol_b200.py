@@ -65,6 +65,9 @@ _SIGNATURES = {
     "smol_b200_decode_attention": (
         _c_int, [_c_void, _c_void, _c_void, _c_int, _c_void, _c_void, _c_i64, _c_void, _c_void, _c_int, _c_int,
                  _c_int, _c_int, _c_int, _c_float, _c_int, _c_float, _c_void, _c_size]),
+    "smol_b200_decode_attention_noalloc": (
+        _c_int, [_c_void, _c_void, _c_void, _c_int, _c_void, _c_void, _c_i64, _c_void, _c_void, _c_int, _c_int,
+                 _c_int, _c_int, _c_int, _c_float, _c_int, _c_float]),
     "smol_b200_prefill_attention": (
         _c_int, [_c_void, _c_void, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void, _c_i64,
                  _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _c_int, _c_int, _c_int,
@@ -209,6 +212,17 @@ def decode_attention(out, q, k_pool, v_pool, pool_rows, seq_row0, kv_len, n_seqs
         _ptr(kv_len), n_seqs, max_kv_len, n_heads, n_kv_heads, head_dim, scale, window, softcap, _ptr(workspace),
         workspace.numel() * workspace.element_size())
     check(rc, "smol_b200_decode_attention")
+
+
+def decode_attention_noalloc(out, q, k_pool, v_pool, pool_rows, seq_row0, kv_len, n_seqs, max_kv_len, n_heads,
+                             n_kv_heads, head_dim, scale, window=0, softcap=0.0, stream=None) -> int:
+    """Allocation-free form of decode_attention (partials in the library's static array).
+    Returns the status code instead of raising, so callers can test the size limit."""
+    import torch
+    q_is_bf16 = 1 if q.dtype == torch.bfloat16 else 0
+    return lib().smol_b200_decode_attention_noalloc(
+        _stream(stream), _ptr(out), _ptr(q), q_is_bf16, _ptr(k_pool), _ptr(v_pool), pool_rows, _ptr(seq_row0),
+        _ptr(kv_len), n_seqs, max_kv_len, n_heads, n_kv_heads, head_dim, scale, window, softcap)
 
 
 def prefill_attention(out, q, k, v, batch, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale, mask_kind=MASK_CAUSAL,
