@@ -404,6 +404,391 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     }
 }
 
+// ===========================================================================
+// v2: two 128-row query tiles per CTA (head dims 64 and 128)
+// ===========================================================================
+// Tile pairing: for GQA groups of even size the two tiles are the same rows of two
+// Q heads that share a KV head (identical key ranges); otherwise two consecutive
+// row blocks of one head.  Warps 0-3 run the softmax of tile 0, warps 4-7 that of
+// tile 1, warp 8 is the TMA producer, warp 9 allocates TMEM and issues MMAs.
+// TMEM: tile t owns columns [256t, 256t+128) for S/P and [256t+128, 256t+128+HD) for O.
+// Registers: the block launches with 384 x 168; warps 8-11 give theirs back down to 88
+// (setmaxnreg.dec) and the two softmax warpgroups take 208 each (setmaxnreg.inc):
+// 128*88 + 256*208 = 64512 = 384*168, so the increase never waits on registers the
+// block does not own.  The host checks the compiled count before every launch.
+// The MMA order per key tile j ping-pongs the tiles so that the tensor pipe works on
+// one tile while the other tile's softmax runs:
+//   ... PV0(j)  S0(j+1)  PV1(j)  S1(j+1)  PV0(j+1) ...
+constexpr int kThreads2 = 384;
+constexpr int kProducerWarp2 = 8;
+constexpr int kMmaWarp2 = 9;
+constexpr int kRegsLaunch2 = 168;
+constexpr int kRegsSoftmax2 = 208;
+constexpr int kRegsOther2 = 88;
+static_assert(128 * kRegsOther2 + 256 * kRegsSoftmax2 <= kThreads2 * kRegsLaunch2, "register split");
+
+template <int HD>
+struct Prefill2Shape {
+    static constexpr int BN = 128;
+    static constexpr int kSub = HD / 64;
+    static constexpr int kQSubBytes = kBM * 128;
+    static constexpr int kQBytes = kSub * kQSubBytes;      // one tile
+    static constexpr int kKvSubBytes = BN * 128;
+    static constexpr int kKvBytes = kSub * kKvSubBytes;
+    static constexpr int kOffQ = 0;
+    static constexpr int kOffK = 2 * kQBytes;
+    static constexpr int kOffV = kOffK + 2 * kKvBytes;
+    static constexpr int kOffBar = kOffV + 2 * kKvBytes;
+    static constexpr int kUsed = kOffBar + 256 + 1024;
+    static constexpr int kSmemBytes = kUsed > 118 * 1024 ? kUsed : 118 * 1024;
+    static constexpr int kTileCols = 256;
+    static constexpr int kTmO = 128;
+    static_assert(kTmO + HD <= kTileCols, "TMEM budget");
+};
+
+struct Barriers2 {
+    uint64_t q_full;
+    uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+    uint64_t s_full[2], p_full[2], o_done[2];
+    uint64_t mma_done;
+    uint32_t tmem_base;
+    int lo_min, hi_max;
+};
+
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi)
+{
+    return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_constant__ PrefillParams p, int pair_heads)
+{
+    using S = Prefill2Shape<HD>;
+    constexpr int BN = S::BN;
+
+    const int n_blocks = gridDim.x;
+    const int qb = n_blocks - 1 - static_cast<int>(blockIdx.x);   // heaviest first
+    const int b = blockIdx.z;
+    int head[2], row0[2];
+    if (pair_heads) {
+        head[0] = 2 * blockIdx.y;
+        head[1] = 2 * blockIdx.y + 1;
+        row0[0] = row0[1] = qb * kBM;
+    } else {
+        head[0] = head[1] = blockIdx.y;
+        row0[0] = qb * 2 * kBM;
+        row0[1] = row0[0] + kBM;
+    }
+    const int kvh = head[0] / p.group;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Barriers2 *bars = reinterpret_cast<Barriers2 *>(smem + S::kOffBar);
+    const int warp = threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bars->q_full), 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(smem_u32(&bars->k_full[s]), 1);
+            mbar_init(smem_u32(&bars->k_empty[s]), 1);
+            mbar_init(smem_u32(&bars->v_full[s]), 1);
+            mbar_init(smem_u32(&bars->v_empty[s]), 1);
+            mbar_init(smem_u32(&bars->s_full[s]), 1);
+            mbar_init(smem_u32(&bars->p_full[s]), kSoftmaxThreads);
+            mbar_init(smem_u32(&bars->o_done[s]), 1);
+        }
+        mbar_init(smem_u32(&bars->mma_done), 1);
+        bars->lo_min = 0x7fffffff;
+        bars->hi_max = 0;
+        fence_mbar_init();
+    }
+    if (warp == kMmaWarp2) {
+        tmem_alloc(smem_u32(&bars->tmem_base), 512);
+        tmem_relinquish();
+    }
+    const bool is_softmax = warp < 8;
+    const int tile = warp >> 2;                       // softmax tile of this thread
+    const int row = row0[tile & 1] + (threadIdx.x & 127);
+    const bool row_valid = is_softmax && row < p.seq_q;
+    int my_lo = 0, my_hi = 0;
+    bool my_written = false;
+    __syncthreads();
+    if (row_valid) {
+        row_range(p, row, my_lo, my_hi, my_written);
+        if (my_hi > my_lo) {
+            atomicMin(&bars->lo_min, my_lo);
+            atomicMax(&bars->hi_max, my_hi);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+    const int lo_min = bars->lo_min;
+    const int hi_max = bars->hi_max;
+    const int n_tiles = hi_max > lo_min ? (hi_max - lo_min + BN - 1) / BN : 0;
+
+    uint8_t *sQ = smem + S::kOffQ;
+    uint8_t *sK = smem + S::kOffK;
+    uint8_t *sV = smem + S::kOffV;
+
+    if (warp >= 8) {
+    // warpgroup 2 (producer, MMA issuer, two idle warps) hands registers to the softmax
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsOther2));
+    if (warp == kProducerWarp2) {
+        if (lane == 0 && n_tiles > 0) {
+            tma_prefetch_desc(&p.tq);
+            tma_prefetch_desc(&p.tk);
+            tma_prefetch_desc(&p.tv);
+            const uint32_t qbar = smem_u32(&bars->q_full);
+            mbar_arrive_expect_tx(qbar, 2 * S::kQBytes);
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int sub = 0; sub < S::kSub; ++sub)
+                    tma_load_3d(smem_u32(sQ + t * S::kQBytes + sub * S::kQSubBytes), &p.tq, qbar,
+                                head[t] * HD + sub * 64, row0[t], b);
+            int kiss = 0, viss = 0;
+            for (int j = 0; j < n_tiles; ++j) {
+                const int st = j & 1;
+                const int key0 = lo_min + j * BN;
+                if (j >= 2 && !mbar_wait(smem_u32(&bars->k_empty[st]), ((j >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty))
+                    break;
+                const uint32_t kb = smem_u32(&bars->k_full[st]);
+                mbar_arrive_expect_tx(kb, S::kKvBytes);
+#pragma unroll
+                for (int sub = 0; sub < S::kSub; ++sub)
+                    tma_load_3d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb,
+                                kvh * HD + sub * 64, key0, b);
+                ++kiss;
+                if (j >= 2 && !mbar_wait(smem_u32(&bars->v_empty[st]), ((j >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty))
+                    break;
+                const uint32_t vb = smem_u32(&bars->v_full[st]);
+                mbar_arrive_expect_tx(vb, S::kKvBytes);
+#pragma unroll
+                for (int sub = 0; sub < S::kSub; ++sub)
+                    tma_load_3d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb,
+                                kvh * HD + sub * 64, key0, b);
+                ++viss;
+            }
+            mbar_wait(smem_u32(&bars->q_full), 0, p.err, kErrDrain);
+            for (int j = max(0, kiss - 2); j < kiss; ++j)
+                if (!mbar_wait(smem_u32(&bars->k_full[j & 1]), (j >> 1) & 1, p.err, kErrDrain)) break;
+            for (int j = max(0, viss - 2); j < viss; ++j)
+                if (!mbar_wait(smem_u32(&bars->v_full[j & 1]), (j >> 1) & 1, p.err, kErrDrain)) break;
+        }
+    } else if (warp == kMmaWarp2) {
+        if (lane == 0 && n_tiles > 0) {
+            constexpr uint32_t idesc_s = umma_idesc_f16(kBM, BN, true, false);
+            constexpr uint32_t idesc_pv = umma_idesc_f16(kBM, HD, false, true);
+            auto issue_s = [&](int t, int j) {
+                const uint32_t q_addr = smem_u32(sQ + t * S::kQBytes);
+                const uint32_t k_addr = smem_u32(sK + (j & 1) * S::kKvBytes);
+                const uint32_t s_col = tmem + t * S::kTileCols;
+#pragma unroll
+                for (int kk = 0; kk < HD / 16; ++kk) {
+                    const uint32_t off = (kk & 3) * 32;
+                    const uint64_t adesc = umma_sdesc_sw128(q_addr + (kk >> 2) * S::kQSubBytes + off, 16, 1024);
+                    const uint64_t bdesc = umma_sdesc_sw128(k_addr + (kk >> 2) * S::kKvSubBytes + off, 16, 1024);
+                    umma_ss(s_col, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&bars->s_full[t]));
+            };
+            auto issue_pv = [&](int t, int j) {
+                const uint32_t v_addr = smem_u32(sV + (j & 1) * S::kKvBytes);
+                const uint32_t p_col = tmem + t * S::kTileCols;
+#pragma unroll
+                for (int kk = 0; kk < BN / 16; ++kk) {
+                    const uint64_t bdesc = umma_sdesc_sw128(v_addr + kk * 16 * 128, S::kKvSubBytes, 1024);
+                    umma_ts(p_col + S::kTmO, p_col + kk * 8, bdesc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&bars->o_done[t]));
+            };
+            bool ok = mbar_wait(smem_u32(&bars->q_full), 0, p.err, kErrWaitTmaFull) &&
+                      mbar_wait(smem_u32(&bars->k_full[0]), 0, p.err, kErrWaitTmaFull);
+            if (ok) {
+                tc_fence_after();
+                issue_s(0, 0);
+                issue_s(1, 0);
+                umma_commit(smem_u32(&bars->k_empty[0]));
+            }
+            for (int j = 0; j < n_tiles && ok; ++j) {
+                const int st = j & 1;
+                ok = mbar_wait(smem_u32(&bars->p_full[0]), j & 1, p.err, kErrWaitSoftmax) &&
+                     mbar_wait(smem_u32(&bars->v_full[st]), (j >> 1) & 1, p.err, kErrWaitTmaFull);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(0, j);
+                const bool more = j + 1 < n_tiles;
+                if (more) {
+                    ok = mbar_wait(smem_u32(&bars->k_full[(j + 1) & 1]), ((j + 1) >> 1) & 1, p.err, kErrWaitTmaFull);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_s(0, j + 1);
+                }
+                ok = mbar_wait(smem_u32(&bars->p_full[1]), j & 1, p.err, kErrWaitSoftmax);
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(1, j);
+                umma_commit(smem_u32(&bars->v_empty[st]));
+                if (more) {
+                    issue_s(1, j + 1);
+                    umma_commit(smem_u32(&bars->k_empty[(j + 1) & 1]));
+                }
+            }
+            umma_commit(smem_u32(&bars->mma_done));
+            mbar_wait(smem_u32(&bars->mma_done), 0, p.err, kErrDrain);
+        }
+    }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax2));
+        // ================= softmax of tile `tile`, thread owns query row `row` =================
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + tile * S::kTileCols;
+        const float cap = p.softcap;
+        const float inv_cap = cap > 0.f ? 1.f / cap : 0.f;
+        const float kLog2e = 1.4426950408889634f;
+        const float sl2 = p.scale_log2;
+        float m = -INFINITY;   // running maximum of score*scale*log2(e)
+        float l = 0.f;
+        bool ok = true;
+        const uint32_t s_full = smem_u32(&bars->s_full[tile]);
+        const uint32_t p_full = smem_u32(&bars->p_full[tile]);
+        const uint32_t o_done = smem_u32(&bars->o_done[tile]);
+        for (int j = 0; j < n_tiles; ++j) {
+            ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, p.err, kErrWaitMma));
+            if (!ok) break;
+            tc_fence_after();
+            float t[BN];
+            {
+                uint32_t r[32];
+#pragma unroll
+                for (int c = 0; c < BN / 32; ++c) {
+                    tmem_ld32(lane_base + c * 32, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(r[i]);
+                }
+            }
+            const int key0 = lo_min + j * BN;
+            const bool full_tile = row_valid && key0 >= my_lo && key0 + BN <= my_hi;
+            if (cap > 0.f) {
+#pragma unroll
+                for (int c = 0; c < BN; ++c) t[c] = cap * tanhf(t[c] * p.scale * inv_cap) * kLog2e;
+            }
+            if (!full_tile) {
+#pragma unroll
+                for (int c = 0; c < BN; ++c) {
+                    const int key = key0 + c;
+                    if (!row_valid || key < my_lo || key >= my_hi) t[c] = -INFINITY;
+                }
+            }
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c + 1 < BN; c += 2) mx = max3f(mx, t[c], t[c + 1]);
+            // scores are raw (scale applied below) unless softcapped (already in log2 units)
+            const float mxs = cap > 0.f ? mx : mx * sl2;
+            const bool need = m != -INFINITY && mxs > m + kRescaleThreshold;
+            if (__any_sync(0xffffffffu, need)) {
+                ok = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, p.err, kErrWaitMma));
+                if (!ok) break;
+                tc_fence_after();
+                const float f = need ? fast_exp2(m - mxs) : 1.f;
+                uint32_t r[32];
+#pragma unroll
+                for (int c = 0; c < HD / 32; ++c) {
+                    tmem_ld32(lane_base + S::kTmO + c * 32, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
+                    tmem_st32(lane_base + S::kTmO + c * 32, r);
+                }
+                l *= f;
+            }
+            if (need || (m == -INFINITY && mxs > -INFINITY)) m = mxs;
+            // P = exp2(s*scale_log2 - m): one packed FMA per two scores, then ex2.
+            const bool live = m != -INFINITY;
+            const float mul = cap > 0.f ? 1.f : sl2;
+            const uint64_t vmul = f2_pack(mul, mul);
+            const uint64_t vneg = f2_pack(live ? -m : 0.f, live ? -m : 0.f);
+            uint64_t acc = f2_pack(0.f, 0.f);
+            {
+                uint32_t r[32];
+#pragma unroll
+                for (int c = 0; c < BN / 64; ++c) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const uint64_t x = f2_fma(f2_pack(t[c * 64 + 2 * i], t[c * 64 + 2 * i + 1]), vmul, vneg);
+                        float e0 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x)));
+                        float e1 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x >> 32)));
+                        if (!live) e0 = e1 = 0.f;
+                        acc = f2_add(acc, f2_pack(e0, e1));
+                        r[i] = pack_f16x2(e0, e1);
+                    }
+                    tmem_st32(lane_base + c * 32, r);
+                }
+            }
+            l += __uint_as_float(static_cast<uint32_t>(acc)) + __uint_as_float(static_cast<uint32_t>(acc >> 32));
+            tmem_st_wait();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        bool have_o = ok && n_tiles > 0;
+        if (have_o)
+            have_o = __all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, p.err, kErrWaitMma));
+        tc_fence_after();
+        const bool store = ok && row_valid && my_written;
+        float *orow = p.out + static_cast<long long>(b) * p.out_batch_stride +
+                      static_cast<long long>(store ? row : 0) * p.out_row_stride +
+                      static_cast<long long>(head[tile & 1]) * HD;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+            if (have_o) {
+                tmem_ld32(lane_base + S::kTmO + c * 32, r);
+                tmem_ld_wait();
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) r[i] = 0u;
+            }
+            if (store) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 4) {
+                    float4 v = make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
+                                           __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+                    *reinterpret_cast<float4 *>(orow + c * 32 + i) = v;
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp2) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
 template <int HD>
 int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t out_batch_stride,
                    const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride, const uint16_t *k,
@@ -450,15 +835,40 @@ int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t 
     static bool attr_set[16] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 16 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmemBytes) !=
-            cudaSuccess)
-            return SMOL_B200_ERR_CUDA;
-        attr_set[dev] = true;
+    if constexpr (HD == 256) {
+        if (dev >= 0 && dev < 16 && !attr_set[dev]) {
+            if (cudaFuncSetAttribute(prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     S::kSmemBytes) != cudaSuccess)
+                return SMOL_B200_ERR_CUDA;
+            attr_set[dev] = true;
+        }
+        const int n_qtiles = (seq_q + kBM - 1) / kBM;
+        dim3 grid(n_qtiles, n_heads, batch);
+        prefill_kernel<HD><<<grid, kThreads, S::kSmemBytes, st>>>(p);
+    } else {
+        using S2 = Prefill2Shape<HD>;
+        if (dev >= 0 && dev < 16 && !attr_set[dev]) {
+            // The register split inside the kernel is sized for a launch of exactly
+            // kRegsLaunch2 registers per thread; refuse to run any other build of it.
+            cudaFuncAttributes fa;
+            if (cudaFuncGetAttributes(&fa, prefill2_kernel<HD>) != cudaSuccess) return SMOL_B200_ERR_CUDA;
+            if (fa.numRegs != kRegsLaunch2) {
+                char buf[128];
+                snprintf(buf, sizeof(buf), "prefill2_kernel compiled with %d registers, expected %d", fa.numRegs,
+                         kRegsLaunch2);
+                set_error(SMOL_B200_ERR_CUDA, buf);
+                return SMOL_B200_ERR_CUDA;
+            }
+            if (cudaFuncSetAttribute(prefill2_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     S2::kSmemBytes) != cudaSuccess)
+                return SMOL_B200_ERR_CUDA;
+            attr_set[dev] = true;
+        }
+        const int pair = (p.group % 2 == 0) ? 1 : 0;
+        const int n_blocks = pair ? (seq_q + kBM - 1) / kBM : (seq_q + 2 * kBM - 1) / (2 * kBM);
+        dim3 grid(n_blocks, pair ? n_heads / 2 : n_heads, batch);
+        prefill2_kernel<HD><<<grid, kThreads2, S2::kSmemBytes, st>>>(p, pair);
     }
-    const int n_qtiles = (seq_q + kBM - 1) / kBM;
-    dim3 grid(n_qtiles, n_heads, batch);
-    prefill_kernel<HD><<<grid, kThreads, S::kSmemBytes, st>>>(p);
     return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
 }
 
