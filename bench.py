@@ -45,7 +45,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-prefill", action="store_true")
@@ -55,6 +55,7 @@ def parse_args():
     ap.add_argument("--seqs", type=int, default=workload.CFG2["n_seqs"], help="sequences per GPU")
     ap.add_argument("--layers", type=int, default=workload.CFG2["layers"])
     ap.add_argument("--no-decode", action="store_true", help="prefill measurement only (profiling helper)")
+    ap.add_argument("--no-configs", action="store_true", help="skip the cfg 1/3/4 block")
     ap.add_argument("--prefill-shape", default=None, help="B,L override of the cfg 5 prefill shape")
     return ap.parse_args()
 
@@ -81,7 +82,7 @@ class Clocks:
         self.proc = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -162,51 +163,73 @@ def gpu_index(local: int) -> int:
 # ---------------------------------------------------------------------------
 # CPU baseline: the reference's smol_causal_attention on the host cores
 # ---------------------------------------------------------------------------
-def cpu_reference_decode(lens: np.ndarray, seconds: float, threads: int | None = None) -> dict:
-    """Times the compiled reference (oracle/_ref) on cfg-2 decode of the first sequences,
-    one layer each, until `seconds` of work; GB/s counts bf16-equivalent KV bytes so it
-    is the same figure as the GPU's."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import ctypes
+class CpuReference:
+    """The compiled reference (oracle/_ref) on cfg-2 decode, on the host cores.
 
-    import pyoracle
-    path = pyoracle.ref_path()
-    if path is None:
+    Each call is smol_causal_attention(seq_q=1, seq_k=L+1) of one sequence and one layer
+    (qkn_decoder.c:658-677) over fp32 K/V.  Six distinct full-length K/V buffers
+    (~400 MB, more than a CPU's last-level cache) are generated once and cycled, so the
+    timed calls stream their cache from DRAM like the GPU does; GB/s counts
+    bf16-equivalent KV bytes so it is the same figure as the GPU's."""
+
+    HQ, HKV, HD = 16, 8, 128
+
+    def __init__(self, lens: np.ndarray, threads: int | None = None):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import ctypes
+
+        import pyoracle
+        self.path = pyoracle.ref_path()
+        self.lens = lens
+        if self.path is None:
+            return
+        self.lib = ctypes.CDLL(self.path)
+        self.nproc = os.cpu_count() or 1
+        self.lib.smol_set_threads(ctypes.c_int(threads or min(self.nproc, 16)))
+        self.threads = int(self.lib.smol_get_thread_count())
+        f = self.lib.smol_causal_attention
+        f.restype = None
+        f.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_int]
+        self.f = f
+        rng = np.random.default_rng(7)
+        maxl = int(lens.max()) + 1
+        kv = self.HKV * self.HD
+        self.bufs = [(rng.standard_normal((maxl, kv), dtype=np.float32),
+                      rng.standard_normal((maxl, kv), dtype=np.float32)) for _ in range(6)]
+        self.q = rng.standard_normal((1, self.HQ * self.HD), dtype=np.float32)
+        self.out = np.zeros_like(self.q)
+        self.i = 0
+
+    @property
+    def available(self) -> bool:
+        return self.path is not None
+
+    def run(self, seconds: float) -> dict:
+        total_bytes, total_t, calls = 0, 0.0, 0
+        scale = 1 / np.sqrt(self.HD)
+        while total_t < seconds:
+            L = int(self.lens[self.i % len(self.lens)]) + 1
+            K, V = self.bufs[calls % len(self.bufs)]
+            t0 = time.perf_counter()
+            self.f(self.out.ctypes.data, self.q.ctypes.data, K.ctypes.data, V.ctypes.data, 1, L, self.HQ, self.HKV,
+                   self.HD, scale, L - 1)
+            total_t += time.perf_counter() - t0
+            total_bytes += L * self.HKV * self.HD * 2 * 2
+            calls += 1
+            self.i += 1
+        return {"value": total_bytes / total_t / 1e9, "unit": UNIT, "cores": self.threads, "nproc": self.nproc,
+                "kind": "reference",
+                "sample": f"{calls} single-query decode calls of smol_causal_attention from oracle/_ref (cfg-2 "
+                          f"lengths+1, 16/8 heads, hd 128, one layer each, fp32 KV cycled over 6 buffers); "
+                          f"GB/s counts bf16-equivalent KV bytes",
+                "seconds": round(total_t, 3)}
+
+
+def cpu_reference_decode(lens: np.ndarray, seconds: float) -> dict:
+    ref = CpuReference(lens)
+    if not ref.available:
         return {"unavailable": "compiled reference (oracle/_ref) not present"}
-    lib = ctypes.CDLL(path)
-    nproc = os.cpu_count() or 1
-    threads = threads or min(nproc, 16)
-    lib.smol_set_threads(ctypes.c_int(threads))
-    used = lib.smol_get_thread_count()
-    hq, hkv, hd = 16, 8, 128
-    rng = np.random.default_rng(7)
-    f = lib.smol_causal_attention
-    f.restype = None
-    f.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 5 + [ctypes.c_float, ctypes.c_int]
-    bufs = []
-    total_bytes, total_t, n_calls = 0, 0.0, 0
-    i = 0
-    while total_t < seconds and i < len(lens):
-        L = int(lens[i]) + 1
-        K = rng.standard_normal((L, hkv * hd), dtype=np.float32)
-        V = rng.standard_normal((L, hkv * hd), dtype=np.float32)
-        q = rng.standard_normal((1, hq * hd), dtype=np.float32)
-        out = np.zeros_like(q)
-        bufs.append((K, V))
-        t0 = time.perf_counter()
-        f(out.ctypes.data, q.ctypes.data, K.ctypes.data, V.ctypes.data, 1, L, hq, hkv, hd, 1 / np.sqrt(hd), L - 1)
-        total_t += time.perf_counter() - t0
-        total_bytes += L * hkv * hd * 2 * 2
-        n_calls += 1
-        i += 1
-        if i == len(lens):   # cycle over the sample again with fresh buffers freed
-            i = 0
-            bufs.clear()
-    return {"value": total_bytes / total_t / 1e9, "unit": UNIT, "cores": int(used), "nproc": nproc,
-            "kind": "reference",
-            "sample": f"{n_calls} single-query decode calls (cfg-2 lengths+1, 16/8 heads, hd 128, one layer each) "
-                      f"of smol_causal_attention from oracle/_ref, fp32 KV; GB/s counts bf16-equivalent KV bytes",
-            "seconds": total_t}
+    return ref.run(seconds)
 
 
 def run_reference(args):
@@ -216,13 +239,14 @@ def run_reference(args):
         return
     lens = workload.decode_lengths(workload.CFG2["n_seqs"], workload.CFG2["len_lo"], workload.CFG2["len_hi"], 0)
     per_step = max(1.0, min(10.0, 120.0 / max(1, args.steps + args.warmup)))
+    ref = CpuReference(lens)
+    if not ref.available:
+        print(json.dumps({"impl": "reference", "unavailable": "compiled reference (oracle/_ref) not present"}))
+        return
     vals = []
     cb = None
     for s in range(args.warmup + args.steps):
-        cb = cpu_reference_decode(lens, per_step)
-        if "unavailable" in cb:
-            print(json.dumps({"impl": "reference", "unavailable": cb["unavailable"]}))
-            return
+        cb = ref.run(per_step)
         if s >= args.warmup:
             vals.append(cb["value"])
     v = statistics.median(vals)
@@ -293,8 +317,155 @@ def run_prefill(args, world, rank, pk):
     return {"workload": f"cfg5 causal prefill, 1 layer, batch {B} x {L}, GQA 16/8, hd 128"
                         + (f", KV heads split over {world} GPUs + NCCL all-gather of outputs" if world > 1 else ""),
             "tflops": round(tf, 1), "ms_per_layer": round(ms, 3), "flops_per_layer": flops,
-            "frac_of_bf16_peak": round(tf / pk["bf16_tflops"], 4),
+            "frac_of_bf16_peak": round(tf / world / pk["bf16_tflops"], 4), "per_gpu_tflops": round(tf / world, 1),
             "peak": pk["bf16_tflops"], "peak_source": pk["source"], "kernel": "tcgen05 prefill_kernel<128>"}
+
+
+def run_other_configs(pk) -> dict:
+    """The remaining BASELINE configs on one GPU (latency- or tensor-bound; not the headline)."""
+    import torch
+
+    import smol_b200
+    res = {}
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    g = torch.Generator(device="cuda").manual_seed(11)
+
+    # ---- cfg 1: 1 layer, prefill 512 then 128 decode steps (batch 1, 16/8, hd 128) ----
+    c = workload.CFG1
+    hq, hkv, hd, P, T = c["n_heads"], c["n_kv_heads"], c["head_dim"], c["prefill"], c["decode_steps"]
+    cap = P + T + 8
+    kv = hkv * hd
+    kp = torch.zeros((cap, kv), dtype=torch.bfloat16, device="cuda")
+    vp = torch.zeros((cap, kv), dtype=torch.float16, device="cuda")
+    cos_h = np.zeros((cap, hd), np.float32)
+    sin_h = np.zeros((cap, hd), np.float32)
+    smol_b200.compute_rope(cos_h, sin_h, np.arange(cap, dtype=np.int32), cap, hd, c["theta"])
+    dc, ds = torch.from_numpy(cos_h).cuda(), torch.from_numpy(sin_h).cuda()
+    qn = (1 + 0.02 * torch.randn(hd, device="cuda", generator=g))
+    kn = (1 + 0.02 * torch.randn(hd, device="cuda", generator=g))
+    q = torch.randn((P, hq * hd), device="cuda", generator=g)
+    k = torch.randn((P, kv), device="cuda", generator=g)
+    v = torch.randn((P, kv), device="cuda", generator=g)
+    qb = torch.empty((P, hq * hd), dtype=torch.bfloat16, device="cuda")
+    out = torch.empty((1, P, hq * hd), device="cuda")
+    pos = torch.arange(P, dtype=torch.int32, device="cuda")
+    slots = pos.to(torch.int64)
+    scale = 1 / np.sqrt(hd)
+
+    def prefill():
+        smol_b200.qknorm_rope_append(q, k, v, P, hq, hkv, hd, qn, kn, 1e-6, dc, ds, False, pos, slots, None, qb,
+                                     kp, vp, cap)
+        smol_b200.prefill_attention(out, qb, kp, vp, 1, P, P, hq, hkv, hd, scale,
+                                    strides=((hq * hd, 0), (hq * hd, 0), (kv, 0), (kv, 0)))
+    for _ in range(3):
+        prefill()
+    a, b = ev(), ev()
+    a.record()
+    for _ in range(10):
+        prefill()
+    b.record()
+    torch.cuda.synchronize()
+    pre_ms = a.elapsed_time(b) / 10
+    q1 = torch.randn((1, hq * hd), device="cuda", generator=g)
+    k1 = torch.randn((1, kv), device="cuda", generator=g)
+    v1 = torch.randn((1, kv), device="cuda", generator=g)
+    qr = torch.empty_like(q1)
+    o1 = torch.empty_like(q1)
+    lens = [torch.tensor([P + t], dtype=torch.int32, device="cuda") for t in range(T)]
+    lens1 = [torch.tensor([P + t + 1], dtype=torch.int32, device="cuda") for t in range(T)]
+    slot = [l.to(torch.int64) for l in lens]
+    r0 = torch.zeros(1, dtype=torch.int64, device="cuda")
+    ws = torch.empty(smol_b200.decode_workspace_bytes(1, cap, hq, hkv, hd), dtype=torch.uint8, device="cuda")
+
+    def decode_all():
+        for t in range(T):
+            smol_b200.qknorm_rope_append(q1, k1, v1, 1, hq, hkv, hd, qn, kn, 1e-6, dc, ds, False, lens[t], slot[t],
+                                         qr, None, kp, vp, cap)
+            smol_b200.decode_attention(o1, qr, kp, vp, cap, r0, lens1[t], 1, cap, hq, hkv, hd, scale, ws)
+    decode_all()
+    a.record()
+    decode_all()
+    b.record()
+    torch.cuda.synchronize()
+    dec_ms = a.elapsed_time(b) / T
+    res["cfg1"] = {"prefill_512_ms": round(pre_ms, 4),
+                   "prefill_tflops": round(workload.causal_flops_square(P, hq, hd) / (pre_ms * 1e-3) / 1e12, 1),
+                   "decode_step_us": round(dec_ms * 1e3, 2),
+                   "note": "one layer, batch 1: latency-bound (prologue + attention per step, 2 + 2 launches)"}
+
+    # ---- cfg 3: SigLIP attention, 128 images x 12 layers, 1024 patches, 12 heads, hd 64 ----
+    c = workload.CFG3
+    B, N, h3, hd3 = c["images"], c["patches"], c["n_heads"], c["head_dim"]
+    q3 = torch.randn((B, N, h3 * hd3), device="cuda", generator=g).to(torch.bfloat16)
+    k3 = torch.randn((B, N, h3 * hd3), device="cuda", generator=g).to(torch.bfloat16)
+    v3 = torch.randn((B, N, h3 * hd3), device="cuda", generator=g).to(torch.float16)
+    o3 = torch.empty((B, N, h3 * hd3), device="cuda")
+
+    def siglip():
+        for _ in range(c["layers"]):
+            smol_b200.prefill_attention(o3, q3, k3, v3, B, N, N, h3, h3, hd3, 1 / 8.0, mask_kind=smol_b200.MASK_FULL)
+    siglip()
+    a.record()
+    siglip()
+    b.record()
+    torch.cuda.synchronize()
+    ms3 = a.elapsed_time(b)
+    fl3 = workload.full_flops(N, h3, hd3) * B * c["layers"]
+    res["cfg3"] = {"ms_12_layers_128_images": round(ms3, 3), "tflops": round(fl3 / (ms3 * 1e-3) / 1e12, 1),
+                   "frac_of_bf16_peak": round(fl3 / (ms3 * 1e-3) / 1e12 / pk["bf16_tflops"], 4),
+                   "flops": fl3, "kernel": "prefill2_kernel<64> (full mask)"}
+    del q3, k3, v3, o3
+
+    # ---- cfg 4: PaliGemma prefix-LM, batch 32, 18 layers, MQA 8/1, hd 256 ----
+    c = workload.CFG4
+    B4, P4, S4, h4, hkv4, hd4, L4 = c["batch"], c["prefix"], c["suffix"], c["n_heads"], c["n_kv_heads"], \
+        c["head_dim"], c["layers"]
+    tot = P4 + S4
+    kv4 = hkv4 * hd4
+    q4 = torch.randn((B4, P4, h4 * hd4), device="cuda", generator=g).to(torch.bfloat16)
+    # every layer has its own cache slab (18 x 32 x 448 rows = 264 MB for K+V, more than L2)
+    kp4 = torch.randn((L4 * B4 * tot, kv4), device="cuda", generator=g).to(torch.bfloat16)
+    vp4 = torch.randn((L4 * B4 * tot, kv4), device="cuda", generator=g).to(torch.float16)
+    o4 = torch.empty((B4, P4, h4 * hd4), device="cuda")
+
+    def prefix():
+        for layer in range(L4):
+            base = layer * B4 * tot
+            smol_b200.prefill_attention(o4, q4, kp4[base:], vp4[base:], B4, P4, P4, h4, hkv4, hd4, 1 / 16.0,
+                                        mask_kind=smol_b200.MASK_PREFIX_LM, prefix_len=P4,
+                                        strides=((h4 * hd4, P4 * h4 * hd4), (h4 * hd4, P4 * h4 * hd4),
+                                                 (kv4, tot * kv4), (kv4, tot * kv4)))
+    prefix()
+    a.record()
+    prefix()
+    b.record()
+    torch.cuda.synchronize()
+    ms4 = a.elapsed_time(b)
+    fl4 = workload.prefix_lm_flops(P4, P4, h4, hd4) * B4 * L4
+    qd = torch.randn((B4, h4 * hd4), device="cuda", generator=g)
+    od = torch.empty_like(qd)
+    r04 = [torch.arange(B4, dtype=torch.int64, device="cuda") * tot + layer * B4 * tot for layer in range(L4)]
+    ws4 = torch.empty(smol_b200.decode_workspace_bytes(B4, tot, h4, hkv4, hd4), dtype=torch.uint8, device="cuda")
+    lens4 = [torch.full((B4,), P4 + t + 1, dtype=torch.int32, device="cuda") for t in range(S4)]
+
+    def suffix():
+        for t in range(S4):
+            for layer in range(L4):
+                smol_b200.decode_attention(od, qd, kp4, vp4, L4 * B4 * tot, r04[layer], lens4[t], B4, tot, h4, hkv4,
+                                           hd4, 1 / 16.0, ws4)
+    suffix()
+    a.record()
+    suffix()
+    b.record()
+    torch.cuda.synchronize()
+    ms_s = a.elapsed_time(b)
+    suf_bytes = sum(B4 * (P4 + t + 1) * kv4 * 2 * 2 for t in range(S4)) * L4
+    res["cfg4"] = {"prefix_ms_18_layers": round(ms4, 3), "prefix_tflops": round(fl4 / (ms4 * 1e-3) / 1e12, 1),
+                   "suffix_128_steps_ms": round(ms_s, 2), "suffix_step_us": round(ms_s * 1e3 / S4, 1),
+                   "suffix_kv_gbs": round(suf_bytes / (ms_s * 1e-3) / 1e9, 1),
+                   "kernels": "prefill_kernel<256> (prefix-LM mask) + decode_split_kernel<256> (MQA group 8)"}
+    smol_b200.check(smol_b200.last_error(), "other configs")
+    return res
 
 
 def run_ours(args):
@@ -314,6 +485,10 @@ def run_ours(args):
     prefill = None
     if not args.no_prefill:
         prefill = run_prefill(args, world, rank, pk)
+        torch.cuda.empty_cache()
+    others = None
+    if world == 1 and not args.no_configs and not args.no_decode:
+        others = run_other_configs(pk)
         torch.cuda.empty_cache()
     if args.no_decode:
         if rank == 0:
@@ -456,6 +631,7 @@ def run_ours(args):
                                                   for k, v in cpu.items()},
         "clocks": clk,
         "prefill": prefill,
+        "other_configs": others,
     }
     print(json.dumps(line))
 

@@ -123,6 +123,10 @@ SMOL_B200_API void smol_cuda_clear_error(void);
 /* Device error word of the current device: bits set by kernels whose bounded waits
  * ran out (0 = none).  Synchronises the device.  Cleared by smol_cuda_clear_error. */
 SMOL_B200_API unsigned smol_cuda_device_error(void);
+/* Self test of the bounded waits: launches one kernel that waits on an mbarrier
+ * nothing arrives on.  After about 2 s the wait gives up, sets bit 0 of the device
+ * error word and the kernel returns; the context stays usable.  Asynchronous. */
+SMOL_B200_API int smol_b200_watchdog_selftest(void *stream);
 
 /* ======================================================================
  * Part 3 -- device API (new; replaces the host KV cache of

@@ -435,6 +435,11 @@ int smol_b200_qknorm_rope_append(void *stream, const float *q_in, const float *k
                   "smol_b200_qknorm_rope_append");
 }
 
+int smol_b200_watchdog_selftest(void *stream)
+{
+    return record(launch_watchdog_selftest(static_cast<cudaStream_t>(stream)), "smol_b200_watchdog_selftest");
+}
+
 size_t smol_b200_decode_workspace_bytes(int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, int head_dim)
 {
     return decode_workspace_bytes(n_seqs, max_kv_len, n_heads, n_kv_heads, head_dim);

@@ -229,6 +229,19 @@ __global__ void decode_step_index_kernel(int *positions, int64_t *slots, int *kv
     kv_len_next[b] = L + 1;
 }
 
+// One thread waits on phase 0 of an mbarrier that nothing ever arrives on: the
+// bounded wait runs out after kWaitLimitNs, or-s kErrWaitTmaFull into the device error
+// word and the kernel returns normally (no fault, no trap, no hang).
+__global__ void watchdog_selftest_kernel(unsigned *err)
+{
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        fence_mbar_init();
+        mbar_wait(smem_u32(&bar), 0, err, kErrWaitTmaFull);
+    }
+}
+
 int grid_for(long long total, int per_block)
 {
     long long g = (total + per_block - 1) / per_block;
@@ -305,6 +318,14 @@ int launch_unpack_rows(cudaStream_t st, float *dst, int64_t dst_stride, const fl
     if (rows <= 0 || heads <= 0 || head_dim <= 0) return SMOL_B200_OK;
     unpack_rows_kernel<<<grid_for(rows * heads * head_dim, 256), 256, 0, st>>>(dst, dst_stride, src, src_stride,
                                                                                 heads, head_dim, padded_hd, rows);
+    return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
+}
+
+int launch_watchdog_selftest(cudaStream_t st)
+{
+    unsigned *err = device_error_word();
+    if (!err) return SMOL_B200_ERR_NO_DEVICE;
+    watchdog_selftest_kernel<<<1, 32, 0, st>>>(err);
     return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
 }
 

@@ -75,6 +75,9 @@ int launch_unpack_rows(cudaStream_t st, float *dst, int64_t dst_stride, const fl
 
 // Per-token (position, slot) of a decode step: positions[b] = kv_len[b],
 // slots[b] = seq_row0[b] + kv_len[b], kv_len_next[b] = kv_len[b] + 1.
+// Bounded-wait self test: one kernel whose wait can never succeed (see rope_norm.cu).
+int launch_watchdog_selftest(cudaStream_t st);
+
 int launch_decode_step_index(cudaStream_t st, int *positions, int64_t *slots, int *kv_len_next,
                              const int64_t *seq_row0, const int *kv_len, int n_seqs);
 

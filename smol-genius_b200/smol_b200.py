@@ -57,6 +57,7 @@ _SIGNATURES = {
     "smol_cuda_error_string": (ctypes.c_char_p, [_c_int]),
     "smol_cuda_clear_error": (None, []),
     "smol_cuda_device_error": (ctypes.c_uint, []),
+    "smol_b200_watchdog_selftest": (_c_int, [_c_void]),
     # Part 3
     "smol_b200_qknorm_rope_append": (
         _c_int, [_c_void, _c_void, _c_void, _c_void, _c_int, _c_int, _c_int, _c_int, _c_void, _c_void, _c_float,
@@ -139,6 +140,10 @@ def clear_error() -> None:
 
 def device_error() -> int:
     return lib().smol_cuda_device_error()
+
+
+def watchdog_selftest(stream=None) -> int:
+    return lib().smol_b200_watchdog_selftest(_stream(stream))
 
 
 # ---------------------------------------------------------------------------
