@@ -365,13 +365,18 @@ __global__ void decode_combine_kernel(float *__restrict__ out, const float *__re
     out[(static_cast<long long>(b) * n_heads + h) * HD + d] = lsum > 0.f ? acc / lsum : 0.f;
 }
 
+// Keys per CTA: enough CTAs for ~8 per SM, at most SMOL_DECODE_MAX_CHUNK keys (larger
+// chunks mean fewer partial results to merge, smaller ones a shorter tail).
+#ifndef SMOL_DECODE_MAX_CHUNK
+#define SMOL_DECODE_MAX_CHUNK 2048
+#endif
 int decode_chunk_size(int n_seqs, int max_kv_len, int n_kv_heads, int n_qgroups)
 {
     const long long work = static_cast<long long>(n_seqs) * n_kv_heads * n_qgroups * (max_kv_len > 0 ? max_kv_len : 1);
     long long c = (work + 148 * 8 - 1) / (148 * 8);
     c = (c + kKeysPerTile - 1) / kKeysPerTile * kKeysPerTile;
     if (c < kKeysPerTile) c = kKeysPerTile;
-    if (c > 512) c = 512;
+    if (c > SMOL_DECODE_MAX_CHUNK) c = SMOL_DECODE_MAX_CHUNK;
     return static_cast<int>(c);
 }
 

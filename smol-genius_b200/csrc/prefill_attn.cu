@@ -471,6 +471,27 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b)
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+// 2^x for a pair of floats on the FMA pipe instead of MUFU (Cody-Waite range reduction
+// + polynomial): n = round(x) via the 1.5*2^23 constant, f = x - n in [-1/2, 1/2],
+// 2^f from a degree-3 polynomial fitted for relative error (max 7.5e-5 on the interval;
+// coefficients fitted for this kernel), and n added to the exponent field.  x is
+// clamped to >= -126 so the result stays a normal float (2^-126 rounds to 0 in fp16).
+__device__ __forceinline__ void exp2_poly_pair(uint64_t x, float &e0, float &e1)
+{
+    constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+    const float x0 = fmaxf(__uint_as_float(static_cast<uint32_t>(x)), -126.f);
+    const float x1 = fmaxf(__uint_as_float(static_cast<uint32_t>(x >> 32)), -126.f);
+    const uint64_t xx = f2_pack(x0, x1);
+    const uint64_t j = f2_add(xx, f2_pack(kMagic, kMagic));
+    const uint64_t r = f2_add(j, f2_pack(-kMagic, -kMagic));
+    const uint64_t f = f2_fma(r, f2_pack(-1.f, -1.f), xx);
+    uint64_t p = f2_fma(f2_pack(0.05517166f, 0.05517166f), f, f2_pack(0.24261113f, 0.24261113f));
+    p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
+    p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
+    e0 = __uint_as_float(static_cast<uint32_t>(p) + (static_cast<uint32_t>(j) << 23));
+    e1 = __uint_as_float(static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(j >> 32) << 23));
+}
+
 __device__ __forceinline__ float max3f(float a, float b, float c)
 {
     float d;
@@ -478,7 +499,22 @@ __device__ __forceinline__ float max3f(float a, float b, float c)
     return d;
 }
 
+// Exponentials per row and key tile: PolyPairs8 of every 8 pairs go to the FMA-pipe
+// polynomial, the rest to MUFU ex2.  Measured on cfg 5 (hd 128) and cfg 3 (hd 64):
+// every share above 0 was slower (issue slots, not MUFU, bound the softmax), so the
+// default keeps all exponentials on MUFU; the share stays a build-time knob.
+#ifndef SMOL_POLY8_HD64
+#define SMOL_POLY8_HD64 0
+#endif
+#ifndef SMOL_POLY8_HD128
+#define SMOL_POLY8_HD128 0
+#endif
 template <int HD>
+struct PolyShare {
+    static constexpr int kPairs8 = HD == 64 ? SMOL_POLY8_HD64 : SMOL_POLY8_HD128;
+};
+
+template <int HD, int PolyPairs8 = PolyShare<HD>::kPairs8>
 __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_constant__ PrefillParams p, int pair_heads)
 {
     using S = Prefill2Shape<HD>;
@@ -679,14 +715,15 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
             tc_fence_after();
             float t[BN];
             {
-                uint32_t r[32];
+                // all column groups in flight before one wait
+                uint32_t r[BN / 32][32];
 #pragma unroll
-                for (int c = 0; c < BN / 32; ++c) {
-                    tmem_ld32(lane_base + c * 32, r);
-                    tmem_ld_wait();
+                for (int c = 0; c < BN / 32; ++c) tmem_ld32(lane_base + c * 32, r[c]);
+                tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(r[i]);
-                }
+                for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(r[c][i]);
             }
             const int key0 = lo_min + j * BN;
             const bool full_tile = row_valid && key0 >= my_lo && key0 + BN <= my_hi;
@@ -737,8 +774,13 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const uint64_t x = f2_fma(f2_pack(t[c * 64 + 2 * i], t[c * 64 + 2 * i + 1]), vmul, vneg);
-                        float e0 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x)));
-                        float e1 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x >> 32)));
+                        float e0, e1;
+                        if ((i & 7) < PolyPairs8) {   // this pair on the FMA pipe
+                            exp2_poly_pair(x, e0, e1);
+                        } else {                      // this pair on MUFU
+                            e0 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x)));
+                            e1 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x >> 32)));
+                        }
                         if (!live) e0 = e1 = 0.f;
                         acc = f2_add(acc, f2_pack(e0, e1));
                         r[i] = pack_f16x2(e0, e1);

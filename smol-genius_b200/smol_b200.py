@@ -17,7 +17,8 @@ import re
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libsmol_b200.so")
+# SMOL_B200_LIB points the binding at another build of the library (e.g. a tuning variant).
+LIB_PATH = os.environ.get("SMOL_B200_LIB") or os.path.join(HERE, "libsmol_b200.so")
 HEADER_PATH = os.path.join(os.path.dirname(HERE), "include", "smol_b200.h")
 
 MASK_CAUSAL, MASK_PREFIX_LM, MASK_WINDOWS, MASK_FULL = 0, 1, 2, 3

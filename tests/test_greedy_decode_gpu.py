@@ -93,7 +93,10 @@ def test_greedy_tokens_identical_over_128_steps(cuda):
                                 strides=((HQ * HD, 0), (HQ * HD, 0), (kv_dim, 0), (kv_dim, 0)))
     torch.cuda.synchronize()
     attn_d = out[0].cpu().numpy()
-    assert pyoracle.rel_l2(attn_d, attn_o) < 1e-3
+    # The tensor-core prefill takes Q in bf16: rounding the fp32 rotated q moves this
+    # layer's output ~1.4e-3 (rel-L2) from the oracle fed the unrounded q (on bf16-exact
+    # inputs the same kernels agree to ~2e-4).  The bar for the decoder is token identity.
+    assert pyoracle.rel_l2(attn_d, attn_o) < 5e-3
 
     tok_o, marg = m.next_token(x[-1], attn_o[-1])
     tok_d, _ = m.next_token(x[-1], attn_d[-1])
