@@ -59,6 +59,7 @@ struct PrefillShape {
 
 struct PrefillParams {
     CUtensorMap tq, tk, tv;
+    CUtensorMap to;                 // fp32 output, box 32 x 32 rows, 128B swizzle (v2 epilogue)
     float *out;
     long long out_row_stride, out_batch_stride;
     const int *window_starts;
@@ -738,9 +739,19 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     if (!row_valid || key < my_lo || key >= my_hi) t[c] = -INFINITY;
                 }
             }
-            float mx = -INFINITY;
+            // Row max as 8 independent chains of 3-input maxima and a short tree (a single
+            // chain over BN scores would serialise BN/2 dependent instructions).
+            float mx;
+            {
+                float pm[8];
 #pragma unroll
-            for (int c = 0; c + 1 < BN; c += 2) mx = max3f(mx, t[c], t[c + 1]);
+                for (int k = 0; k < 8; ++k) pm[k] = fmaxf(t[2 * k], t[2 * k + 1]);
+#pragma unroll
+                for (int c = 16; c < BN; c += 16)
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) pm[k] = max3f(pm[k], t[c + 2 * k], t[c + 2 * k + 1]);
+                mx = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
+            }
             // scores are raw (scale applied below) unless softcapped (already in log2 units)
             const float mxs = cap > 0.f ? mx : mx * sl2;
             const bool need = m != -INFINITY && mxs > m + kRescaleThreshold;
@@ -766,7 +777,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
             const float mul = cap > 0.f ? 1.f : sl2;
             const uint64_t vmul = f2_pack(mul, mul);
             const uint64_t vneg = f2_pack(live ? -m : 0.f, live ? -m : 0.f);
-            uint64_t acc = f2_pack(0.f, 0.f);
+            uint64_t acc[4] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
             {
                 uint32_t r[32];
 #pragma unroll
@@ -782,13 +793,15 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                             e1 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x >> 32)));
                         }
                         if (!live) e0 = e1 = 0.f;
-                        acc = f2_add(acc, f2_pack(e0, e1));
+                        acc[i & 3] = f2_add(acc[i & 3], f2_pack(e0, e1));   // 4 independent sums
                         r[i] = pack_f16x2(e0, e1);
                     }
                     tmem_st32(lane_base + c * 32, r);
                 }
             }
-            l += __uint_as_float(static_cast<uint32_t>(acc)) + __uint_as_float(static_cast<uint32_t>(acc >> 32));
+            const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
+            const uint64_t a = f2_add(a01, a23);
+            l += __uint_as_float(static_cast<uint32_t>(a)) + __uint_as_float(static_cast<uint32_t>(a >> 32));
             tmem_st_wait();
             tc_fence_before();
             mbar_arrive(p_full);
@@ -797,27 +810,67 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
         if (have_o)
             have_o = __all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, p.err, kErrWaitMma));
         tc_fence_after();
-        const bool store = ok && row_valid && my_written;
-        float *orow = p.out + static_cast<long long>(b) * p.out_batch_stride +
-                      static_cast<long long>(store ? row : 0) * p.out_row_stride +
-                      static_cast<long long>(head[tile & 1]) * HD;
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        uint32_t r[32];
+        // Staged epilogue: this warp's 32 rows go through shared memory (128B-swizzled
+        // 32 x 32 fp32 boxes) and leave with TMA tensor stores, so every output row is
+        // written as whole sectors.  Tile 0 stages in the K ring, tile 1 in the V ring:
+        // both are free once this tile's last PV completed (S and PV are issued in
+        // order, and the producer has no load left).  Rows no window covers must stay
+        // untouched, so warps holding one fall back to per-row stores.
+        const bool staged = ok && __all_sync(0xffffffffu, my_written || !row_valid);
+        if (staged) {
+            uint8_t *stage = (tile == 0 ? sK : sV) + (warp & 3) * (32 * HD * 4);
+            uint32_t r[32];
 #pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-            if (have_o) {
-                tmem_ld32(lane_base + S::kTmO + c * 32, r);
-                tmem_ld_wait();
-            } else {
+            for (int c = 0; c < HD / 32; ++c) {
+                if (have_o) {
+                    tmem_ld32(lane_base + S::kTmO + c * 32, r);
+                    tmem_ld_wait();
+                } else {
 #pragma unroll
-                for (int i = 0; i < 32; ++i) r[i] = 0u;
+                    for (int i = 0; i < 32; ++i) r[i] = 0u;
+                }
+                uint8_t *box = stage + c * (32 * 128);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    float4 v = make_float4(__uint_as_float(r[4 * k]) * inv, __uint_as_float(r[4 * k + 1]) * inv,
+                                           __uint_as_float(r[4 * k + 2]) * inv, __uint_as_float(r[4 * k + 3]) * inv);
+                    *reinterpret_cast<float4 *>(box + sw128_offset(lane, k)) = v;
+                }
             }
-            if (store) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                const int y = row0[tile & 1] + (warp & 3) * 32;
 #pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    float4 v = make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
-                                           __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
-                    *reinterpret_cast<float4 *>(orow + c * 32 + i) = v;
+                for (int c = 0; c < HD / 32; ++c)
+                    tma_store_3d(&p.to, smem_u32(stage + c * (32 * 128)), head[tile & 1] * HD + c * 32, y, b);
+                bulk_commit();
+                bulk_wait_read0();
+            }
+            __syncwarp();
+        } else {
+            const bool store = ok && row_valid && my_written;
+            float *orow = p.out + static_cast<long long>(b) * p.out_batch_stride +
+                          static_cast<long long>(store ? row : 0) * p.out_row_stride +
+                          static_cast<long long>(head[tile & 1]) * HD;
+            uint32_t r[32];
+#pragma unroll
+            for (int c = 0; c < HD / 32; ++c) {
+                if (have_o) {
+                    tmem_ld32(lane_base + S::kTmO + c * 32, r);
+                    tmem_ld_wait();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) r[i] = 0u;
+                }
+                if (store) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        float4 v = make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
+                                               __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+                        *reinterpret_cast<float4 *>(orow + c * 32 + i) = v;
+                    }
                 }
             }
         }
@@ -856,6 +909,12 @@ int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t 
     if (!make_tmap_3d(&p.tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<int64_t>(n_kv_heads) * HD, kv_rows,
                       batch, v_row_stride, vb, 64, S::BN))
         return SMOL_B200_ERR_CUDA;
+    {
+        const int64_t ob = batch > 1 ? out_batch_stride : static_cast<int64_t>(seq_q) * out_row_stride;
+        if (!make_tmap_3d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<int64_t>(n_heads) * HD, seq_q,
+                          batch, out_row_stride, ob, 32, 32, 4))
+            return SMOL_B200_ERR_CUDA;
+    }
     p.out = out;
     p.out_row_stride = out_row_stride;
     p.out_batch_stride = out_batch_stride;

@@ -180,12 +180,14 @@ bool make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype,
 }
 
 bool make_tmap_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int64_t inner, int64_t rows,
-                  int64_t outer, int64_t row_stride, int64_t outer_stride, int box_inner, int box_rows)
+                  int64_t outer, int64_t row_stride, int64_t outer_stride, int box_inner, int box_rows,
+                  int elem_bytes)
 {
     if (!encode_fn()) return false;
     cuuint64_t dims[3] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows),
                           static_cast<cuuint64_t>(outer)};
-    cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride) * 2, static_cast<cuuint64_t>(outer_stride) * 2};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride) * elem_bytes,
+                             static_cast<cuuint64_t>(outer_stride) * elem_bytes};
     cuuint32_t box[3] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_rows), 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = g_encode(map, dtype, 3, const_cast<void *>(base), dims, strides, box, estr,

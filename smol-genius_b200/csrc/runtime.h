@@ -34,10 +34,10 @@ int current_device();
 // box = box_rows x box_inner, 128-byte swizzle (box_inner*2 must be 128).
 bool make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int64_t inner,
                   int64_t rows, int box_inner, int box_rows, int64_t row_stride = -1);
-// 3-D tensor [outer, rows, inner] with strides in elements.
+// 3-D tensor [outer, rows, inner] with strides in elements of `elem_bytes` bytes.
 bool make_tmap_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int64_t inner,
                   int64_t rows, int64_t outer, int64_t row_stride, int64_t outer_stride, int box_inner,
-                  int box_rows);
+                  int box_rows, int elem_bytes = 2);
 
 // ---- kernels (implemented in the .cu files) ----
 size_t decode_workspace_bytes(int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, int head_dim);
