@@ -56,6 +56,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=workload.CFG2["layers"])
     ap.add_argument("--no-decode", action="store_true", help="prefill measurement only (profiling helper)")
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg 1/3/4 block")
+    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4"], default=None,
+                    help="run one of the cfg 1/3/4 measurements alone (profiling helper)")
+    ap.add_argument("--images", type=int, default=None, help="cfg 3 image count override")
     ap.add_argument("--prefill-shape", default=None, help="B,L override of the cfg 5 prefill shape")
     return ap.parse_args()
 
@@ -318,19 +321,21 @@ def run_prefill(args, world, rank, pk):
                         + (f", KV heads split over {world} GPUs + NCCL all-gather of outputs" if world > 1 else ""),
             "tflops": round(tf, 1), "ms_per_layer": round(ms, 3), "flops_per_layer": flops,
             "frac_of_bf16_peak": round(tf / world / pk["bf16_tflops"], 4), "per_gpu_tflops": round(tf / world, 1),
-            "peak": pk["bf16_tflops"], "peak_source": pk["source"], "kernel": "tcgen05 prefill_kernel<128>"}
+            "peak": pk["bf16_tflops"], "peak_source": pk["source"], "kernel": "tcgen05 prefill2_kernel<128>"}
 
 
-def run_other_configs(pk) -> dict:
-    """The remaining BASELINE configs on one GPU (latency- or tensor-bound; not the headline)."""
+def _ev():
+    import torch
+    return torch.cuda.Event(enable_timing=True)
+
+
+def run_cfg1() -> dict:
+    """cfg 1: one layer, prefill 512 then 128 decode steps (batch 1, 16/8, hd 128)."""
     import torch
 
     import smol_b200
-    res = {}
-    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    ev = _ev
     g = torch.Generator(device="cuda").manual_seed(11)
-
-    # ---- cfg 1: 1 layer, prefill 512 then 128 decode steps (batch 1, 16/8, hd 128) ----
     c = workload.CFG1
     hq, hkv, hd, P, T = c["n_heads"], c["n_kv_heads"], c["head_dim"], c["prefill"], c["decode_steps"]
     cap = P + T + 8
@@ -388,18 +393,31 @@ def run_other_configs(pk) -> dict:
     b.record()
     torch.cuda.synchronize()
     dec_ms = a.elapsed_time(b) / T
-    res["cfg1"] = {"prefill_512_ms": round(pre_ms, 4),
-                   "prefill_tflops": round(workload.causal_flops_square(P, hq, hd) / (pre_ms * 1e-3) / 1e12, 1),
-                   "decode_step_us": round(dec_ms * 1e3, 2),
-                   "note": "one layer, batch 1: latency-bound (prologue + attention per step, 2 + 2 launches)"}
+    return {"prefill_512_ms": round(pre_ms, 4),
+            "prefill_tflops": round(workload.causal_flops_square(P, hq, hd) / (pre_ms * 1e-3) / 1e12, 1),
+            "decode_step_us": round(dec_ms * 1e3, 2),
+            "note": "one layer, batch 1: latency-bound (prologue + attention per step, 2 + 2 launches)"}
 
-    # ---- cfg 3: SigLIP attention, 128 images x 12 layers, 1024 patches, 12 heads, hd 64 ----
-    c = workload.CFG3
+
+def run_cfg3(pk, images: int | None = None, layers: int | None = None) -> dict:
+    """cfg 3: SigLIP attention, 128 images x 12 layers, 1024 patches, 12 heads, hd 64."""
+    import torch
+
+    import smol_b200
+    ev = _ev
+    g = torch.Generator(device="cuda").manual_seed(13)
+    c = dict(workload.CFG3)
+    if images:
+        c["images"] = images
+    if layers:
+        c["layers"] = layers
     B, N, h3, hd3 = c["images"], c["patches"], c["n_heads"], c["head_dim"]
     q3 = torch.randn((B, N, h3 * hd3), device="cuda", generator=g).to(torch.bfloat16)
     k3 = torch.randn((B, N, h3 * hd3), device="cuda", generator=g).to(torch.bfloat16)
     v3 = torch.randn((B, N, h3 * hd3), device="cuda", generator=g).to(torch.float16)
     o3 = torch.empty((B, N, h3 * hd3), device="cuda")
+
+    a, b = ev(), ev()
 
     def siglip():
         for _ in range(c["layers"]):
@@ -411,12 +429,19 @@ def run_other_configs(pk) -> dict:
     torch.cuda.synchronize()
     ms3 = a.elapsed_time(b)
     fl3 = workload.full_flops(N, h3, hd3) * B * c["layers"]
-    res["cfg3"] = {"ms_12_layers_128_images": round(ms3, 3), "tflops": round(fl3 / (ms3 * 1e-3) / 1e12, 1),
-                   "frac_of_bf16_peak": round(fl3 / (ms3 * 1e-3) / 1e12 / pk["bf16_tflops"], 4),
-                   "flops": fl3, "kernel": "prefill2_kernel<64> (full mask)"}
-    del q3, k3, v3, o3
+    return {"workload": f"{B} images x {c['layers']} layers", "ms": round(ms3, 3),
+            "tflops": round(fl3 / (ms3 * 1e-3) / 1e12, 1),
+            "frac_of_bf16_peak": round(fl3 / (ms3 * 1e-3) / 1e12 / pk["bf16_tflops"], 4),
+            "flops": fl3, "kernel": "prefill2_kernel<64> (full mask)"}
 
-    # ---- cfg 4: PaliGemma prefix-LM, batch 32, 18 layers, MQA 8/1, hd 256 ----
+
+def run_cfg4() -> dict:
+    """cfg 4: PaliGemma prefix-LM, batch 32, 18 layers, MQA 8/1, hd 256; 128-step suffix."""
+    import torch
+
+    import smol_b200
+    ev = _ev
+    g = torch.Generator(device="cuda").manual_seed(17)
     c = workload.CFG4
     B4, P4, S4, h4, hkv4, hd4, L4 = c["batch"], c["prefix"], c["suffix"], c["n_heads"], c["n_kv_heads"], \
         c["head_dim"], c["layers"]
@@ -427,6 +452,8 @@ def run_other_configs(pk) -> dict:
     kp4 = torch.randn((L4 * B4 * tot, kv4), device="cuda", generator=g).to(torch.bfloat16)
     vp4 = torch.randn((L4 * B4 * tot, kv4), device="cuda", generator=g).to(torch.float16)
     o4 = torch.empty((B4, P4, h4 * hd4), device="cuda")
+
+    a, b = ev(), ev()
 
     def prefix():
         for layer in range(L4):
@@ -460,10 +487,17 @@ def run_other_configs(pk) -> dict:
     torch.cuda.synchronize()
     ms_s = a.elapsed_time(b)
     suf_bytes = sum(B4 * (P4 + t + 1) * kv4 * 2 * 2 for t in range(S4)) * L4
-    res["cfg4"] = {"prefix_ms_18_layers": round(ms4, 3), "prefix_tflops": round(fl4 / (ms4 * 1e-3) / 1e12, 1),
-                   "suffix_128_steps_ms": round(ms_s, 2), "suffix_step_us": round(ms_s * 1e3 / S4, 1),
-                   "suffix_kv_gbs": round(suf_bytes / (ms_s * 1e-3) / 1e9, 1),
-                   "kernels": "prefill_kernel<256> (prefix-LM mask) + decode_split_kernel<256> (MQA group 8)"}
+    smol_b200.check(smol_b200.last_error(), "cfg4")
+    return {"prefix_ms_18_layers": round(ms4, 3), "prefix_tflops": round(fl4 / (ms4 * 1e-3) / 1e12, 1),
+            "suffix_128_steps_ms": round(ms_s, 2), "suffix_step_us": round(ms_s * 1e3 / S4, 1),
+            "suffix_kv_gbs": round(suf_bytes / (ms_s * 1e-3) / 1e9, 1),
+            "kernels": "prefill_kernel<256> (prefix-LM mask) + decode_split_kernel<256> (MQA group 8)"}
+
+
+def run_other_configs(pk) -> dict:
+    """The remaining BASELINE configs on one GPU (latency- or tensor-bound; not the headline)."""
+    import smol_b200
+    res = {"cfg1": run_cfg1(), "cfg3": run_cfg3(pk), "cfg4": run_cfg4()}
     smol_b200.check(smol_b200.last_error(), "other configs")
     return res
 
@@ -640,6 +674,14 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.only_config:
+        import torch
+        torch.cuda.set_device(0)
+        pk = peaks()
+        fn = {"cfg1": run_cfg1, "cfg3": lambda: run_cfg3(pk, args.images, 1 if args.images else None),
+              "cfg4": run_cfg4}[args.only_config]
+        print(json.dumps({args.only_config: fn()}))
         return
     run_ours(args)
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:

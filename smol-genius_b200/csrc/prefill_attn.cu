@@ -428,9 +428,16 @@ constexpr int kRegsSoftmax2 = 208;
 constexpr int kRegsOther2 = 88;
 static_assert(128 * kRegsOther2 + 256 * kRegsSoftmax2 <= kThreads2 * kRegsLaunch2, "register split");
 
+// Key tile (BN = 128) and K/V ring depth (2) are the same for head dims 64 and 128:
+// TMEM holds S/P (128 columns) and O (head-dim columns) for each of the two Q tiles.
+// Measured alternatives for head dim 64 (cfg 3): 64-key tiles with a 4-deep ring ran
+// 14 % slower; a look-ahead variant with two S buffers per Q tile failed parity on
+// B200 and was left out.
 template <int HD>
 struct Prefill2Shape {
     static constexpr int BN = 128;
+    static constexpr int kNSB = 1;                         // S/P buffers per Q tile
+    static constexpr int kStages = 2;                      // K and V ring depth
     static constexpr int kSub = HD / 64;
     static constexpr int kQSubBytes = kBM * 128;
     static constexpr int kQBytes = kSub * kQSubBytes;      // one tile
@@ -438,19 +445,21 @@ struct Prefill2Shape {
     static constexpr int kKvBytes = kSub * kKvSubBytes;
     static constexpr int kOffQ = 0;
     static constexpr int kOffK = 2 * kQBytes;
-    static constexpr int kOffV = kOffK + 2 * kKvBytes;
-    static constexpr int kOffBar = kOffV + 2 * kKvBytes;
-    static constexpr int kUsed = kOffBar + 256 + 1024;
+    static constexpr int kOffV = kOffK + kStages * kKvBytes;
+    static constexpr int kOffBar = kOffV + kStages * kKvBytes;
+    static constexpr int kUsed = kOffBar + 512 + 1024;
     static constexpr int kSmemBytes = kUsed > 118 * 1024 ? kUsed : 118 * 1024;
     static constexpr int kTileCols = 256;
-    static constexpr int kTmO = 128;
+    static constexpr int kTmO = BN;
     static_assert(kTmO + HD <= kTileCols, "TMEM budget");
+    static_assert(kStages * kKvBytes >= kBM * HD * 4, "epilogue staging must fit a K or V ring");
 };
 
+constexpr int kMaxStages2 = 4;
 struct Barriers2 {
     uint64_t q_full;
-    uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-    uint64_t s_full[2], p_full[2], o_done[2];
+    uint64_t k_full[kMaxStages2], k_empty[kMaxStages2], v_full[kMaxStages2], v_empty[kMaxStages2];
+    uint64_t s_full[2][2], p_full[2][2], o_done[2];
     uint64_t mma_done;
     uint32_t tmem_base;
     int lo_min, hi_max;
@@ -520,6 +529,8 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
 {
     using S = Prefill2Shape<HD>;
     constexpr int BN = S::BN;
+    constexpr int NSB = S::kNSB;
+    constexpr int ST = S::kStages;
 
     const int n_blocks = gridDim.x;
     const int qb = n_blocks - 1 - static_cast<int>(blockIdx.x);   // heaviest first
@@ -544,14 +555,18 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
 
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(&bars->q_full), 1);
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < ST; ++s) {
             mbar_init(smem_u32(&bars->k_full[s]), 1);
             mbar_init(smem_u32(&bars->k_empty[s]), 1);
             mbar_init(smem_u32(&bars->v_full[s]), 1);
             mbar_init(smem_u32(&bars->v_empty[s]), 1);
-            mbar_init(smem_u32(&bars->s_full[s]), 1);
-            mbar_init(smem_u32(&bars->p_full[s]), kSoftmaxThreads);
-            mbar_init(smem_u32(&bars->o_done[s]), 1);
+        }
+        for (int t = 0; t < 2; ++t) {
+            for (int sb = 0; sb < NSB; ++sb) {
+                mbar_init(smem_u32(&bars->s_full[t][sb]), 1);
+                mbar_init(smem_u32(&bars->p_full[t][sb]), kSoftmaxThreads);
+            }
+            mbar_init(smem_u32(&bars->o_done[t]), 1);
         }
         mbar_init(smem_u32(&bars->mma_done), 1);
         bars->lo_min = 0x7fffffff;
@@ -606,9 +621,9 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                                 head[t] * HD + sub * 64, row0[t], b);
             int kiss = 0, viss = 0;
             for (int j = 0; j < n_tiles; ++j) {
-                const int st = j & 1;
+                const int st = j % ST;
                 const int key0 = lo_min + j * BN;
-                if (j >= 2 && !mbar_wait(smem_u32(&bars->k_empty[st]), ((j >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty))
+                if (j >= ST && !mbar_wait(smem_u32(&bars->k_empty[st]), ((j / ST) - 1) & 1, p.err, kErrWaitTmaEmpty))
                     break;
                 const uint32_t kb = smem_u32(&bars->k_full[st]);
                 mbar_arrive_expect_tx(kb, S::kKvBytes);
@@ -617,7 +632,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     tma_load_3d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb,
                                 kvh * HD + sub * 64, key0, b);
                 ++kiss;
-                if (j >= 2 && !mbar_wait(smem_u32(&bars->v_empty[st]), ((j >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty))
+                if (j >= ST && !mbar_wait(smem_u32(&bars->v_empty[st]), ((j / ST) - 1) & 1, p.err, kErrWaitTmaEmpty))
                     break;
                 const uint32_t vb = smem_u32(&bars->v_full[st]);
                 mbar_arrive_expect_tx(vb, S::kKvBytes);
@@ -628,19 +643,20 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                 ++viss;
             }
             mbar_wait(smem_u32(&bars->q_full), 0, p.err, kErrDrain);
-            for (int j = max(0, kiss - 2); j < kiss; ++j)
-                if (!mbar_wait(smem_u32(&bars->k_full[j & 1]), (j >> 1) & 1, p.err, kErrDrain)) break;
-            for (int j = max(0, viss - 2); j < viss; ++j)
-                if (!mbar_wait(smem_u32(&bars->v_full[j & 1]), (j >> 1) & 1, p.err, kErrDrain)) break;
+            for (int j = max(0, kiss - ST); j < kiss; ++j)
+                if (!mbar_wait(smem_u32(&bars->k_full[j % ST]), (j / ST) & 1, p.err, kErrDrain)) break;
+            for (int j = max(0, viss - ST); j < viss; ++j)
+                if (!mbar_wait(smem_u32(&bars->v_full[j % ST]), (j / ST) & 1, p.err, kErrDrain)) break;
         }
     } else if (warp == kMmaWarp2) {
         if (lane == 0 && n_tiles > 0) {
             constexpr uint32_t idesc_s = umma_idesc_f16(kBM, BN, true, false);
             constexpr uint32_t idesc_pv = umma_idesc_f16(kBM, HD, false, true);
+            // S_t(j) lands in S buffer j % NSB of tile t; K/V of key tile j sit in ring slot j % ST.
             auto issue_s = [&](int t, int j) {
                 const uint32_t q_addr = smem_u32(sQ + t * S::kQBytes);
-                const uint32_t k_addr = smem_u32(sK + (j & 1) * S::kKvBytes);
-                const uint32_t s_col = tmem + t * S::kTileCols;
+                const uint32_t k_addr = smem_u32(sK + (j % ST) * S::kKvBytes);
+                const uint32_t s_col = tmem + t * S::kTileCols + (j % NSB) * BN;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk) {
                     const uint32_t off = (kk & 3) * 32;
@@ -648,48 +664,56 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     const uint64_t bdesc = umma_sdesc_sw128(k_addr + (kk >> 2) * S::kKvSubBytes + off, 16, 1024);
                     umma_ss(s_col, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
                 }
-                umma_commit(smem_u32(&bars->s_full[t]));
+                umma_commit(smem_u32(&bars->s_full[t][j % NSB]));
             };
             auto issue_pv = [&](int t, int j) {
-                const uint32_t v_addr = smem_u32(sV + (j & 1) * S::kKvBytes);
-                const uint32_t p_col = tmem + t * S::kTileCols;
+                const uint32_t v_addr = smem_u32(sV + (j % ST) * S::kKvBytes);
+                const uint32_t p_col = tmem + t * S::kTileCols + (j % NSB) * BN;
+                const uint32_t o_col = tmem + t * S::kTileCols + S::kTmO;
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
                     const uint64_t bdesc = umma_sdesc_sw128(v_addr + kk * 16 * 128, S::kKvSubBytes, 1024);
-                    umma_ts(p_col + S::kTmO, p_col + kk * 8, bdesc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                    umma_ts(o_col, p_col + kk * 8, bdesc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(smem_u32(&bars->o_done[t]));
             };
-            bool ok = mbar_wait(smem_u32(&bars->q_full), 0, p.err, kErrWaitTmaFull) &&
-                      mbar_wait(smem_u32(&bars->k_full[0]), 0, p.err, kErrWaitTmaFull);
-            if (ok) {
+            auto wait_k = [&](int j) {
+                return mbar_wait(smem_u32(&bars->k_full[j % ST]), (j / ST) & 1, p.err, kErrWaitTmaFull);
+            };
+            // Prologue: S of the first NSB key tiles for both Q tiles.
+            bool ok = mbar_wait(smem_u32(&bars->q_full), 0, p.err, kErrWaitTmaFull);
+            for (int j = 0; j < NSB && j < n_tiles && ok; ++j) {
+                ok = wait_k(j);
+                if (!ok) break;
                 tc_fence_after();
-                issue_s(0, 0);
-                issue_s(1, 0);
-                umma_commit(smem_u32(&bars->k_empty[0]));
+                issue_s(0, j);
+                issue_s(1, j);
+                umma_commit(smem_u32(&bars->k_empty[j % ST]));
             }
             for (int j = 0; j < n_tiles && ok; ++j) {
-                const int st = j & 1;
-                ok = mbar_wait(smem_u32(&bars->p_full[0]), j & 1, p.err, kErrWaitSoftmax) &&
-                     mbar_wait(smem_u32(&bars->v_full[st]), (j >> 1) & 1, p.err, kErrWaitTmaFull);
+                const int st = j % ST;
+                const int sb = j % NSB;
+                ok = mbar_wait(smem_u32(&bars->p_full[0][sb]), (j / NSB) & 1, p.err, kErrWaitSoftmax) &&
+                     mbar_wait(smem_u32(&bars->v_full[st]), (j / ST) & 1, p.err, kErrWaitTmaFull);
                 if (!ok) break;
                 tc_fence_after();
                 issue_pv(0, j);
-                const bool more = j + 1 < n_tiles;
+                const int jn = j + NSB;                 // S buffer sb is free again after PV0(j)
+                const bool more = jn < n_tiles;
                 if (more) {
-                    ok = mbar_wait(smem_u32(&bars->k_full[(j + 1) & 1]), ((j + 1) >> 1) & 1, p.err, kErrWaitTmaFull);
+                    ok = wait_k(jn);
                     if (!ok) break;
                     tc_fence_after();
-                    issue_s(0, j + 1);
+                    issue_s(0, jn);
                 }
-                ok = mbar_wait(smem_u32(&bars->p_full[1]), j & 1, p.err, kErrWaitSoftmax);
+                ok = mbar_wait(smem_u32(&bars->p_full[1][sb]), (j / NSB) & 1, p.err, kErrWaitSoftmax);
                 if (!ok) break;
                 tc_fence_after();
                 issue_pv(1, j);
                 umma_commit(smem_u32(&bars->v_empty[st]));
                 if (more) {
-                    issue_s(1, j + 1);
-                    umma_commit(smem_u32(&bars->k_empty[(j + 1) & 1]));
+                    issue_s(1, jn);
+                    umma_commit(smem_u32(&bars->k_empty[jn % ST]));
                 }
             }
             umma_commit(smem_u32(&bars->mma_done));
@@ -707,11 +731,13 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
         float m = -INFINITY;   // running maximum of score*scale*log2(e)
         float l = 0.f;
         bool ok = true;
-        const uint32_t s_full = smem_u32(&bars->s_full[tile]);
-        const uint32_t p_full = smem_u32(&bars->p_full[tile]);
         const uint32_t o_done = smem_u32(&bars->o_done[tile]);
         for (int j = 0; j < n_tiles; ++j) {
-            ok = __all_sync(0xffffffffu, mbar_wait(s_full, j & 1, p.err, kErrWaitMma));
+            const int sb = j % NSB;
+            const uint32_t s_full = smem_u32(&bars->s_full[tile][sb]);
+            const uint32_t p_full = smem_u32(&bars->p_full[tile][sb]);
+            const uint32_t s_base = lane_base + sb * BN;   // S of this key tile; P overwrites it
+            ok = __all_sync(0xffffffffu, mbar_wait(s_full, (j / NSB) & 1, p.err, kErrWaitMma));
             if (!ok) break;
             tc_fence_after();
             float t[BN];
@@ -719,7 +745,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                 // all column groups in flight before one wait
                 uint32_t r[BN / 32][32];
 #pragma unroll
-                for (int c = 0; c < BN / 32; ++c) tmem_ld32(lane_base + c * 32, r[c]);
+                for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_base + c * 32, r[c]);
                 tmem_ld_wait();
 #pragma unroll
                 for (int c = 0; c < BN / 32; ++c)
@@ -796,7 +822,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                         acc[i & 3] = f2_add(acc[i & 3], f2_pack(e0, e1));   // 4 independent sums
                         r[i] = pack_f16x2(e0, e1);
                     }
-                    tmem_st32(lane_base + c * 32, r);
+                    tmem_st32(s_base + c * 32, r);
                 }
             }
             const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
@@ -884,6 +910,16 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
     }
 }
 
+// Key-tile height of the kernel that runs for a head dim (v1 for 256, v2 otherwise).
+template <int HD>
+struct KvTileRows {
+    static constexpr int value = Prefill2Shape<HD>::BN;
+};
+template <>
+struct KvTileRows<256> {
+    static constexpr int value = PrefillShape<256>::BN;
+};
+
 template <int HD>
 int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t out_batch_stride,
                    const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride, const uint16_t *k,
@@ -903,11 +939,14 @@ int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t 
     if (!make_tmap_3d(&p.tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<int64_t>(n_heads) * HD, seq_q, batch,
                       q_row_stride, qb, 64, kBM))
         return SMOL_B200_ERR_CUDA;
+    // K/V boxes are one key tile high: the tile height of the kernel that will run
+    // (v1 for head dim 256, v2 otherwise) -- the producer's expect_tx counts on it.
+    constexpr int kv_box_rows = KvTileRows<HD>::value;
     if (!make_tmap_3d(&p.tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<int64_t>(n_kv_heads) * HD, kv_rows,
-                      batch, k_row_stride, kb, 64, S::BN))
+                      batch, k_row_stride, kb, 64, kv_box_rows))
         return SMOL_B200_ERR_CUDA;
     if (!make_tmap_3d(&p.tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<int64_t>(n_kv_heads) * HD, kv_rows,
-                      batch, v_row_stride, vb, 64, S::BN))
+                      batch, v_row_stride, vb, 64, kv_box_rows))
         return SMOL_B200_ERR_CUDA;
     {
         const int64_t ob = batch > 1 ? out_batch_stride : static_cast<int64_t>(seq_q) * out_row_stride;
