@@ -37,6 +37,7 @@ import numpy as np  # noqa: E402
 
 import workload  # noqa: E402
 
+DECODE_TRAFFIC_PER_ALG_BYTE = (304.548352e6 + 4.445440e6) / 304.381952e6
 METRIC = "decode attn KV GB/s (% of HBM peak); prefill TFLOP/s; at 1/2/4/8 B200 vs CPU"
 UNIT = "GB/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -601,6 +602,12 @@ def run_ours(args):
     qo_bytes = n * hq * hd * 4 * 2                                 # fp32 q read + fp32 out write
     alg_bytes_launch = kv_bytes_rank / layers + qo_bytes
     achieved = alg_bytes_launch / (dec_ms * 1e-3) / 1e9
+    # DRAM traffic per launch: ncu (dram__bytes_read.sum + dram__bytes_write.sum) on the
+    # 16-sequence, 1-layer case of this workload read 304.55 MB and wrote 4.45 MB
+    # (partials + output) for 304.38 MB of algorithmic bytes; both grow with the KV
+    # bytes (reads) and the number of 2048-key chunks (partials), so the full launch is
+    # scaled by its algorithmic bytes.
+    traffic_launch = alg_bytes_launch * DECODE_TRAFFIC_PER_ALG_BYTE
 
     # ---- e2e through the C ABI with host buffers ----
     e2e = None
@@ -655,7 +662,8 @@ def run_ours(args):
         "kv_bytes_per_step": world * kv_bytes_rank,
         "hbm_frac": round(value / world / pk["hbm_gbs"], 4),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": int(traffic_launch),
+                     "traffic_source": "ncu dram bytes of the 16-seq 1-layer case x (full / small algorithmic bytes)",
                      "kernel": "decode_split_kernel<128> + decode_combine_kernel<128> (per layer)",
                      "alg_bytes_per_launch": int(alg_bytes_launch), "ms_per_launch": round(dec_ms, 4),
                      "peak_source": pk["source"]},

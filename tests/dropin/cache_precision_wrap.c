@@ -1,0 +1,50 @@
+/*
+ * cache_precision_wrap.c -- CPU emulation of libsmol_b200's storage precision inside
+ * the reference decoder, for choosing the drop-in test's model.
+ *
+ * Linked with -Wl,--wrap=smol_causal_attention, so qkn_decoder.c's calls
+ * (qkn_decoder.c:525, :674) land here.  K is rounded to bf16 and V to fp16 (the
+ * device KV cache formats), and Q to bf16 when seq_q > 1 (the tensor-core prefill's
+ * operand format; decode keeps fp32 Q).  The reference kernel then runs on the
+ * rounded values.  The binary built from this (qkn_dropin_emul) shows how far the
+ * cache precision alone moves each step's logits, which bounds the top-2 margin a
+ * drop-in token-identity test needs.
+ */
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+void __real_smol_causal_attention(float *out, const float *Q, const float *K, const float *V, int seq_q,
+                                  int seq_k, int n_heads, int n_kv_heads, int head_dim, float scale,
+                                  int q_offset);
+
+static float round_bf16(float f)
+{
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    u &= 0xffff0000u;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+static float *rounded(const float *x, size_t n, int fp16)
+{
+    float *y = (float *)malloc(sizeof(float) * (n ? n : 1));
+    for (size_t i = 0; i < n; i++) y[i] = fp16 ? (float)(_Float16)x[i] : round_bf16(x[i]);
+    return y;
+}
+
+void __wrap_smol_causal_attention(float *out, const float *Q, const float *K, const float *V, int seq_q,
+                                  int seq_k, int n_heads, int n_kv_heads, int head_dim, float scale,
+                                  int q_offset)
+{
+    size_t kv_n = (size_t)seq_k * n_kv_heads * head_dim;
+    size_t q_n = (size_t)seq_q * n_heads * head_dim;
+    float *k = rounded(K, kv_n, 0), *v = rounded(V, kv_n, 1);
+    float *q = seq_q > 1 ? rounded(Q, q_n, 0) : NULL;
+    __real_smol_causal_attention(out, q ? q : Q, k, v, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale, q_offset);
+    free(k);
+    free(v);
+    free(q);
+}

@@ -1,9 +1,13 @@
 """Greedy decode parity over 128 steps (BASELINE cfg 1 shape).
 
 A one-layer Qwen3-0.6B-shaped attention decoder with seeded synthetic weights
-(hidden 1024, 16 Q / 8 KV heads, head_dim 128, per-head RMSNorm eps 1e-6 with
-weights ~N(1,0.02), NeoX RoPE theta 1e6, tied embeddings): a 512-token prefill,
-then 129 greedy tokens.  The projections, residual, final norm and argmax run in
+(hidden 1024, 16 Q / 8 KV heads, head_dim 128, per-head RMSNorm eps 1e-6, NeoX
+RoPE theta 1e6, tied embeddings): a 512-token prefill, then 129 greedy tokens.
+The QK-norm weights are ~N(3,0.02) and Wv / Wo carry a gain of 4 so that attention
+is sharp and its read-out, not the token's own embedding, decides the next token:
+with unit gains the stream is one token repeated, which would prove nothing.  With
+these weights the 129 tokens take ~88 distinct values and the test asserts at
+least 32.  The projections, residual, final norm and argmax run in
 numpy for both sides from the same fp32 values, so the only difference between the
 two runs is the hot path: on one side libsmol_b200 (fused QK-norm + RoPE + cache
 append, tcgen05 prefill, split-KV decode through smol_b200_decode_step_host), on the
@@ -22,6 +26,7 @@ pytestmark = pytest.mark.gpu
 
 H, HQ, HKV, HD, VOCAB = 1024, 16, 8, 128, 4096
 PREFILL, STEPS = 512, 129
+QK_GAIN, VO_GAIN = 3.0, 4.0
 
 
 def rms_norm(x, w, eps=1e-6):
@@ -35,10 +40,10 @@ class Model:
         self.E = bf(VOCAB, H)
         self.Wq = bf(HQ * HD, H, sc=1 / np.sqrt(H))
         self.Wk = bf(HKV * HD, H, sc=1 / np.sqrt(H))
-        self.Wv = bf(HKV * HD, H, sc=1 / np.sqrt(H))
-        self.Wo = bf(H, HQ * HD, sc=1 / np.sqrt(HQ * HD))
-        self.qn = (1 + 0.02 * rng.standard_normal(HD)).astype(np.float32)
-        self.kn = (1 + 0.02 * rng.standard_normal(HD)).astype(np.float32)
+        self.Wv = bf(HKV * HD, H, sc=VO_GAIN / np.sqrt(H))
+        self.Wo = bf(H, HQ * HD, sc=VO_GAIN / np.sqrt(HQ * HD))
+        self.qn = (QK_GAIN + 0.02 * rng.standard_normal(HD)).astype(np.float32)
+        self.kn = (QK_GAIN + 0.02 * rng.standard_normal(HD)).astype(np.float32)
         self.norm = (1 + 0.02 * rng.standard_normal(H)).astype(np.float32)
         self.prompt = rng.integers(0, VOCAB, size=PREFILL)
 
@@ -93,10 +98,13 @@ def test_greedy_tokens_identical_over_128_steps(cuda):
                                 strides=((HQ * HD, 0), (HQ * HD, 0), (kv_dim, 0), (kv_dim, 0)))
     torch.cuda.synchronize()
     attn_d = out[0].cpu().numpy()
-    # The tensor-core prefill takes Q in bf16: rounding the fp32 rotated q moves this
-    # layer's output ~1.4e-3 (rel-L2) from the oracle fed the unrounded q (on bf16-exact
-    # inputs the same kernels agree to ~2e-4).  The bar for the decoder is token identity.
-    assert pyoracle.rel_l2(attn_d, attn_o) < 5e-3
+    # The tensor-core prefill takes Q in bf16.  Against the oracle fed the same bf16 Q
+    # the kernel meets the parity bar; against the unrounded fp32 Q of the reference the
+    # layer output moves ~5e-3 (rel-L2) with these sharp QK-norm gains, which the token
+    # stream below absorbs (the first token's top-2 margin is 1.3, the shift 0.17).
+    attn_ob = oracle_attend(pyoracle.round_bf16(q_rot), PREFILL, 0, PREFILL)
+    assert pyoracle.rel_l2(attn_d, attn_ob) < 1e-3
+    assert pyoracle.rel_l2(attn_d, attn_o) < 1e-2
 
     tok_o, marg = m.next_token(x[-1], attn_o[-1])
     tok_d, _ = m.next_token(x[-1], attn_d[-1])
@@ -125,4 +133,5 @@ def test_greedy_tokens_identical_over_128_steps(cuda):
     assert len(toks_o) == STEPS
     assert toks_d == toks_o, (f"diverged at step {len(toks_o) - 1}: device {toks_d[-1]} vs oracle {toks_o[-1]}, "
                               f"oracle top-2 margin {margins[-1]:.4f}")
-    print(f"129 greedy tokens identical; smallest top-1/top-2 margin {min(margins):.4f}")
+    assert len(set(toks_o)) >= 32, f"degenerate token stream: {len(set(toks_o))} distinct tokens"
+    print(f"129 greedy tokens identical ({len(set(toks_o))} distinct); smallest top-1/top-2 margin {min(margins):.4f}")
