@@ -330,12 +330,41 @@ def _ev():
     return torch.cuda.Event(enable_timing=True)
 
 
+def _graph(fn):
+    """Capture fn's launches into a CUDA graph (warm-up on the capture stream first, so
+    one-time set-up such as kernel attributes happens outside the capture)."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
+
+
+def _time_graph(g, reps: int) -> float:
+    """Mean ms per replay of graph g (3 warm-up replays)."""
+    import torch
+    for _ in range(3):
+        g.replay()
+    a, b = _ev(), _ev()
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
 def run_cfg1() -> dict:
     """cfg 1: one layer, prefill 512 then 128 decode steps (batch 1, 16/8, hd 128)."""
     import torch
 
     import smol_b200
-    ev = _ev
     g = torch.Generator(device="cuda").manual_seed(11)
     c = workload.CFG1
     hq, hkv, hd, P, T = c["n_heads"], c["n_kv_heads"], c["head_dim"], c["prefill"], c["decode_steps"]
@@ -363,15 +392,7 @@ def run_cfg1() -> dict:
                                      kp, vp, cap)
         smol_b200.prefill_attention(out, qb, kp, vp, 1, P, P, hq, hkv, hd, scale,
                                     strides=((hq * hd, 0), (hq * hd, 0), (kv, 0), (kv, 0)))
-    for _ in range(3):
-        prefill()
-    a, b = ev(), ev()
-    a.record()
-    for _ in range(10):
-        prefill()
-    b.record()
-    torch.cuda.synchronize()
-    pre_ms = a.elapsed_time(b) / 10
+    pre_ms = _time_graph(_graph(prefill), 20)
     q1 = torch.randn((1, hq * hd), device="cuda", generator=g)
     k1 = torch.randn((1, kv), device="cuda", generator=g)
     v1 = torch.randn((1, kv), device="cuda", generator=g)
@@ -388,16 +409,13 @@ def run_cfg1() -> dict:
             smol_b200.qknorm_rope_append(q1, k1, v1, 1, hq, hkv, hd, qn, kn, 1e-6, dc, ds, False, lens[t], slot[t],
                                          qr, None, kp, vp, cap)
             smol_b200.decode_attention(o1, qr, kp, vp, cap, r0, lens1[t], 1, cap, hq, hkv, hd, scale, ws)
-    decode_all()
-    a.record()
-    decode_all()
-    b.record()
-    torch.cuda.synchronize()
-    dec_ms = a.elapsed_time(b) / T
+    dec_ms = _time_graph(_graph(decode_all), 3) / T
+    smol_b200.check(smol_b200.last_error(), "cfg1")
     return {"prefill_512_ms": round(pre_ms, 4),
             "prefill_tflops": round(workload.causal_flops_square(P, hq, hd) / (pre_ms * 1e-3) / 1e12, 1),
             "decode_step_us": round(dec_ms * 1e3, 2),
-            "note": "one layer, batch 1: latency-bound (prologue + attention per step, 2 + 2 launches)"}
+            "note": "one layer, batch 1: latency-bound; prefill (append + attention) and the 128-step decode "
+                    "loop (append + split + combine per step) each replayed as one CUDA graph"}
 
 
 def run_cfg3(pk, images: int | None = None, layers: int | None = None) -> dict:
@@ -481,18 +499,14 @@ def run_cfg4() -> dict:
             for layer in range(L4):
                 smol_b200.decode_attention(od, qd, kp4, vp4, L4 * B4 * tot, r04[layer], lens4[t], B4, tot, h4, hkv4,
                                            hd4, 1 / 16.0, ws4)
-    suffix()
-    a.record()
-    suffix()
-    b.record()
-    torch.cuda.synchronize()
-    ms_s = a.elapsed_time(b)
+    ms_s = _time_graph(_graph(suffix), 3)
     suf_bytes = sum(B4 * (P4 + t + 1) * kv4 * 2 * 2 for t in range(S4)) * L4
     smol_b200.check(smol_b200.last_error(), "cfg4")
     return {"prefix_ms_18_layers": round(ms4, 3), "prefix_tflops": round(fl4 / (ms4 * 1e-3) / 1e12, 1),
             "suffix_128_steps_ms": round(ms_s, 2), "suffix_step_us": round(ms_s * 1e3 / S4, 1),
             "suffix_kv_gbs": round(suf_bytes / (ms_s * 1e-3) / 1e9, 1),
-            "kernels": "prefill_kernel<256> (prefix-LM mask) + decode_split_kernel<256> (MQA group 8)"}
+            "kernels": "prefill_kernel<256> (prefix-LM mask) + decode_split_kernel<256> (MQA group 8); "
+                       "the 128-step x 18-layer suffix replayed as one CUDA graph"}
 
 
 def run_other_configs(pk) -> dict:

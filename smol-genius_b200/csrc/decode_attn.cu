@@ -20,6 +20,16 @@
 // are fp16 because bf16 probabilities alone put the output ~1.3e-3 (rel-L2) away from
 // an fp32 reference; fp16 keeps it near 1.5e-4.
 //
+// Q.  The consumer warps copy the CTA's (<= 8) Q rows into shared memory with
+// coalesced 16-byte loads, all issued before the first use, while the producer's
+// first TMA is in flight; the MMA fragments are then built from shared memory.  (A
+// CTA of a small batch often owns a single tile, so this prologue is on the critical
+// path: per-thread fragment loads straight from global memory serialise on it.)
+//
+// Stages.  The ring depth is a launch parameter (at most kMaxStages): a chunk of one
+// or two tiles gets one or two stages, so a head-dim-256 CTA of a short chunk needs
+// 73 KB of shared memory instead of 137 KB and two fit on an SM.
+//
 // Each CTA merges its 4 warps and writes one partial (O unnormalised, running max,
 // running sum) per Q head; a second kernel merges the chunks of a sequence.
 // Algorithmic traffic: every attended key costs n_kv_heads*hd*2 (K,V) * 2 bytes.
@@ -44,8 +54,15 @@ struct DecodeShape {
     static constexpr int kSubtiles = HD / 64;
     static constexpr int kTileBytes = kSubtiles * kSubtileBytes;   // K or V of one tile
     static constexpr int kStageBytes = 2 * kTileBytes;
-    static constexpr int kStages = HD == 256 ? 2 : (HD == 128 ? 3 : 4);
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int kMaxStages = HD == 256 ? 2 : (HD == 128 ? 3 : 4);
+    static constexpr int kQRowFloats = HD + 8;                     // padded fp32 Q row
+    static constexpr int kQBytes = 8 * kQRowFloats * 4;
+    static constexpr int kQVecPerThread = 8 * HD * 4 / 16 / (kConsumerWarps * 32);   // 16-byte loads
+    // Layout: [stages x stage][Q rows][barriers], base aligned to 1024 (SW128 tiles).
+    static constexpr size_t smem_bytes(int stages)
+    {
+        return static_cast<size_t>(stages) * kStageBytes + kQBytes + 256 + 1024;
+    }
 };
 
 struct DecodeParams {
@@ -60,6 +77,8 @@ struct DecodeParams {
     int q_is_bf16;
     int n_heads, n_kv_heads, group, n_qgroups;
     int chunk, max_chunks, window;
+    int stages;                     // K/V ring depth, 1..kMaxStages
+    int q_vec16;                    // q base 16-byte aligned: Q rows copied with 16-byte loads
     float scale, softcap;
 };
 
@@ -102,14 +121,16 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + S::kStages * S::kStageBytes);
-    uint64_t *empty_bar = full_bar + S::kStages;
+    const int stages = p.stages;
+    float *qs = reinterpret_cast<float *>(smem + stages * S::kStageBytes);
+    uint64_t *full_bar = reinterpret_cast<uint64_t *>(smem + stages * S::kStageBytes + S::kQBytes);
+    uint64_t *empty_bar = full_bar + S::kMaxStages;
 
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S::kStages; ++s) {
+        for (int s = 0; s < stages; ++s) {
             mbar_init(smem_u32(&full_bar[s]), 1);
             mbar_init(smem_u32(&empty_bar[s]), kConsumerWarps);
         }
@@ -123,10 +144,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_
             tma_prefetch_desc(&p.tmap_k);
             tma_prefetch_desc(&p.tmap_v);
             int issued = 0;
+            int s = 0, phase = 0;
             for (int t = 0; t < ntiles; ++t) {
-                const int s = t % S::kStages;
-                if (t >= S::kStages &&
-                    !mbar_wait(smem_u32(&empty_bar[s]), ((t / S::kStages) - 1) & 1, p.err, kErrWaitTmaEmpty))
+                if (t >= stages && !mbar_wait(smem_u32(&empty_bar[s]), phase ^ 1, p.err, kErrWaitTmaEmpty))
                     break;
                 const uint32_t fb = smem_u32(&full_bar[s]);
                 mbar_arrive_expect_tx(fb, S::kStageBytes);
@@ -140,10 +160,14 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_
                     tma_load_2d(vdst + sub * kSubtileBytes, &p.tmap_v, fb, x, y);
                 }
                 ++issued;
+                if (++s == stages) {
+                    s = 0;
+                    phase ^= 1;
+                }
             }
             // Drain: every issued tile must have landed before the CTA may exit.
-            for (int t = max(0, issued - S::kStages); t < issued; ++t) {
-                if (!mbar_wait(smem_u32(&full_bar[t % S::kStages]), (t / S::kStages) & 1, p.err, kErrDrain))
+            for (int t = max(0, issued - stages); t < issued; ++t) {
+                if (!mbar_wait(smem_u32(&full_bar[t % stages]), (t / stages) & 1, p.err, kErrDrain))
                     break;
             }
         }
@@ -154,30 +178,63 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_
     const int g = lane >> 2;   // key row (S^T) / head column (B operand)
     const int tq = lane & 3;
 
+    // Q rows h_first .. h_first+nh-1 of sequence b (contiguous in global memory) to
+    // shared memory as fp32, one padded row per head.
+    {
+        const int tid = threadIdx.x;   // 0..127
+        const size_t esize = p.q_is_bf16 ? 2 : 4;
+        const uint8_t *qsrc = static_cast<const uint8_t *>(p.q) +
+                              (static_cast<long long>(b) * p.n_heads + h_first) * HD * esize;
+        const int nelem = nh * HD;
+        if (p.q_vec16) {
+            const int nvec = static_cast<int>(nelem * esize / 16);
+            uint4 buf[S::kQVecPerThread];
+#pragma unroll
+            for (int i = 0; i < S::kQVecPerThread; ++i) {
+                const int v = tid + i * kConsumerWarps * 32;
+                if (v < nvec) buf[i] = __ldg(reinterpret_cast<const uint4 *>(qsrc) + v);
+            }
+#pragma unroll
+            for (int i = 0; i < S::kQVecPerThread; ++i) {
+                const int v = tid + i * kConsumerWarps * 32;
+                if (v < nvec) {
+                    if (p.q_is_bf16) {
+                        const int e = v * 8, row = e / HD, col = e % HD;
+                        float *dst = qs + row * S::kQRowFloats + col;
+                        const uint32_t w[4] = {buf[i].x, buf[i].y, buf[i].z, buf[i].w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            dst[2 * j] = bf16lo_f32(w[j]);
+                            dst[2 * j + 1] = bf16hi_f32(w[j]);
+                        }
+                    } else {
+                        const int e = v * 4, row = e / HD, col = e % HD;
+                        *reinterpret_cast<uint4 *>(qs + row * S::kQRowFloats + col) = buf[i];
+                    }
+                }
+            }
+        } else {
+            for (int e = tid; e < nelem; e += kConsumerWarps * 32) {
+                const float x = p.q_is_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(qsrc)[e])
+                                            : reinterpret_cast<const float *>(qsrc)[e];
+                qs[(e / HD) * S::kQRowFloats + e % HD] = x;
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+    }
+
     // Q^T as B fragments (k = head dim, n = head g), bf16 hi (+ lo for fp32 Q).
     uint32_t qhi[KSTEPS][2], qlo[KSTEPS][2];
     {
         const bool valid = g < nh;
-        const long long qrow = (static_cast<long long>(b) * p.n_heads + h_first + (valid ? g : 0)) * HD;
+        const float *qrow = qs + (valid ? g : 0) * S::kQRowFloats;
 #pragma unroll
         for (int kk = 0; kk < KSTEPS; ++kk) {
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 const int d = kk * 16 + half * 8 + tq * 2;
-                float x0 = 0.f, x1 = 0.f;
-                if (valid) {
-                    if (p.q_is_bf16) {
-                        const uint32_t v = *reinterpret_cast<const uint32_t *>(
-                            static_cast<const uint16_t *>(p.q) + qrow + d);
-                        x0 = bf16lo_f32(v);
-                        x1 = bf16hi_f32(v);
-                    } else {
-                        const float2 v = *reinterpret_cast<const float2 *>(static_cast<const float *>(p.q) + qrow + d);
-                        x0 = v.x;
-                        x1 = v.y;
-                    }
-                }
-                split_bf16x2(x0, x1, qhi[kk][half], qlo[kk][half]);
+                const float2 v = *reinterpret_cast<const float2 *>(qrow + d);
+                split_bf16x2(valid ? v.x : 0.f, valid ? v.y : 0.f, qhi[kk][half], qlo[kk][half]);
             }
         }
     }
@@ -194,9 +251,9 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_
     for (int i = 0; i < KSTEPS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
     bool ok = true;
+    int s = 0, phase = 0;
     for (int t = 0; t < ntiles; ++t) {
-        const int s = t % S::kStages;
-        if (!mbar_wait(smem_u32(&full_bar[s]), (t / S::kStages) & 1, p.err, kErrWaitTmaFull)) {
+        if (!mbar_wait(smem_u32(&full_bar[s]), phase, p.err, kErrWaitTmaFull)) {
             ok = false;
             break;
         }
@@ -282,6 +339,10 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+        if (++s == stages) {
+            s = 0;
+            phase ^= 1;
+        }
     }
 
     // ---- merge the 4 consumer warps (stage buffers are free: every tile was consumed) ----
@@ -380,6 +441,48 @@ int decode_chunk_size(int n_seqs, int max_kv_len, int n_kv_heads, int n_qgroups)
     return static_cast<int>(c);
 }
 
+// Raise the dynamic shared-memory limit of decode_split_kernel<HD> on the current
+// device, once per device (the attribute is per function and device).
+template <int HD>
+bool ensure_split_smem_attr()
+{
+    static std::mutex mu;
+    static bool done[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return false;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev]) {
+        if (cudaFuncSetAttribute(decode_split_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(DecodeShape<HD>::smem_bytes(DecodeShape<HD>::kMaxStages))) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+        done[dev] = true;
+    }
+    return true;
+}
+
+// Completes p (ring depth, Q load width) and launches the split and combine kernels.
+template <int HD>
+int launch_split_combine(cudaStream_t st, DecodeParams &p, float *out, int n_seqs)
+{
+    using S = DecodeShape<HD>;
+    const int tiles = (p.chunk + kKeysPerTile - 1) / kKeysPerTile;   // most tiles one CTA streams
+    p.stages = tiles < S::kMaxStages ? tiles : S::kMaxStages;
+    p.q_vec16 = (reinterpret_cast<uintptr_t>(p.q) & 15) == 0;
+    if (!ensure_split_smem_attr<HD>()) return SMOL_B200_ERR_CUDA;
+    dim3 grid(p.max_chunks, p.n_kv_heads * p.n_qgroups, n_seqs);
+    decode_split_kernel<HD><<<grid, kThreads, S::smem_bytes(p.stages), st>>>(p);
+    dim3 cgrid(p.n_heads, n_seqs);
+    decode_combine_kernel<HD><<<cgrid, HD, 0, st>>>(out, p.part_o, p.part_ml, p.kv_len, p.n_heads, p.chunk,
+                                                   p.max_chunks, p.window, p.err);
+    return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
+}
+
 template <int HD>
 int launch_decode(cudaStream_t st, float *out, const void *q, int q_is_bf16, const uint16_t *k_pool,
                   const uint16_t *v_pool, int64_t pool_rows, const int64_t *seq_row0, const int *kv_len,
@@ -413,19 +516,7 @@ int launch_decode(cudaStream_t st, float *out, const void *q, int q_is_bf16, con
     p.scale = scale;
     p.softcap = softcap;
 
-    static bool attr_set = false;   // per process; the attribute is per function
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(decode_split_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 S::kSmemBytes) != cudaSuccess)
-            return SMOL_B200_ERR_CUDA;
-        attr_set = true;
-    }
-    dim3 grid(p.max_chunks, n_kv_heads * p.n_qgroups, n_seqs);
-    decode_split_kernel<HD><<<grid, kThreads, S::kSmemBytes, st>>>(p);
-    dim3 cgrid(n_heads, n_seqs);
-    decode_combine_kernel<HD><<<cgrid, HD, 0, st>>>(out, p.part_o, p.part_ml, kv_len, n_heads, p.chunk,
-                                                   p.max_chunks, window, p.err);
-    return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
+    return launch_split_combine<HD>(st, p, out, n_seqs);
 }
 
 }  // namespace
@@ -490,7 +581,6 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocBytes];
 
 std::mutex g_noalloc_mutex;
 void *g_noalloc_ptr[16] = {};
-bool g_noalloc_attr[16][3] = {};
 
 // Set-up, once per device and with that device current: the host-side name of a
 // __device__ array is only a stand-in, so its device address is looked up.
@@ -562,19 +652,8 @@ int launch_decode_noalloc(cudaStream_t st, int dev, uint8_t *scratch, float *out
     p.window = window;
     p.scale = scale;
     p.softcap = softcap;
-    const int ti = HD == 64 ? 0 : (HD == 128 ? 1 : 2);
-    if (!g_noalloc_attr[dev][ti]) {
-        if (cudaFuncSetAttribute(decode_split_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 S::kSmemBytes) != cudaSuccess)
-            return SMOL_B200_ERR_CUDA;
-        g_noalloc_attr[dev][ti] = true;
-    }
-    dim3 grid(p.max_chunks, n_kv_heads * p.n_qgroups, n_seqs);
-    decode_split_kernel<HD><<<grid, kThreads, S::kSmemBytes, st>>>(p);
-    dim3 cgrid(n_heads, n_seqs);
-    decode_combine_kernel<HD><<<cgrid, HD, 0, st>>>(out, p.part_o, p.part_ml, kv_len, n_heads, p.chunk,
-                                                   p.max_chunks, window, p.err);
-    return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
+    (void)dev;
+    return launch_split_combine<HD>(st, p, out, n_seqs);
 }
 
 }  // namespace

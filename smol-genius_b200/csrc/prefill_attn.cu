@@ -21,6 +21,7 @@
 // rescaled (TMEM load / scale / store by its owning thread) rarely; values stay
 // below 256 and the final division uses the same maximum for O and the row sum.
 #include <stdio.h>
+#include <stdlib.h>
 
 #include "b200_common.cuh"
 #include "runtime.h"
@@ -67,6 +68,8 @@ struct PrefillParams {
     int n_windows;
     int seq_q, seq_k, n_heads, group, mask_kind, q_offset, prefix_len, window;
     float scale, scale_log2, softcap;
+    // v2 work items: n_qblocks x n_ygroups (head pairs or heads) x batch
+    int n_qblocks, n_ygroups, batch, pair_heads, heavy_first;
 };
 
 struct Barriers {
@@ -446,7 +449,12 @@ struct Prefill2Shape {
     static constexpr int kOffQ = 0;
     static constexpr int kOffK = 2 * kQBytes;
     static constexpr int kOffV = kOffK + kStages * kKvBytes;
-    static constexpr int kOffBar = kOffV + kStages * kKvBytes;
+    // Epilogue staging of its own (8 softmax warps x 32 rows x HD fp32) where it fits
+    // beside the rings (head dim 64); head dim 128 stages in the rings after the last item.
+    static constexpr int kEpiBytes = 8 * 32 * HD * 4;
+    static constexpr int kOffEpi = kOffV + kStages * kKvBytes;
+    static constexpr bool kEpiOwn = kOffEpi + kEpiBytes + 512 + 1024 <= 227 * 1024;
+    static constexpr int kOffBar = kOffEpi + (kEpiOwn ? kEpiBytes : 0);
     static constexpr int kUsed = kOffBar + 512 + 1024;
     static constexpr int kSmemBytes = kUsed > 118 * 1024 ? kUsed : 118 * 1024;
     static constexpr int kTileCols = 256;
@@ -457,12 +465,11 @@ struct Prefill2Shape {
 
 constexpr int kMaxStages2 = 4;
 struct Barriers2 {
-    uint64_t q_full;
+    uint64_t q_full, q_empty;
     uint64_t k_full[kMaxStages2], k_empty[kMaxStages2], v_full[kMaxStages2], v_empty[kMaxStages2];
-    uint64_t s_full[2][2], p_full[2][2], o_done[2];
+    uint64_t s_full[2], p_full[2], o_done[2];
     uint64_t mma_done;
     uint32_t tmem_base;
-    int lo_min, hi_max;
 };
 
 __device__ __forceinline__ uint64_t f2_pack(float lo, float hi)
@@ -524,28 +531,75 @@ struct PolyShare {
     static constexpr int kPairs8 = HD == 64 ? SMOL_POLY8_HD64 : SMOL_POLY8_HD128;
 };
 
-template <int HD, int PolyPairs8 = PolyShare<HD>::kPairs8>
-__global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_constant__ PrefillParams p, int pair_heads)
+// Work item k of a launch: (query block, head pair or head, batch element), query
+// blocks fastest -- in decreasing order of work for causal-like masks -- so that the
+// CTAs that run at the same time read the K and V of one (batch, KV head), which
+// stays in L2 (at 32k keys it is 16 MB; spreading concurrent CTAs over many heads
+// measured 8 % slower on cfg 5).  A persistent CTA takes the items of rounds
+// r = 0, 1, ... at positions blockIdx.x (even rounds) and gridDim.x-1-blockIdx.x (odd
+// rounds).
+struct Item2 {
+    int b, head[2], row0[2];
+    int lo_min, n_tiles;   // key tiles [lo_min, lo_min + n_tiles*BN) cover every row's keys
+};
+
+__device__ __forceinline__ int item_index(const PrefillParams &p, int r)
+{
+    const int c = (r & 1) ? static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x)
+                          : static_cast<int>(blockIdx.x);
+    return r * static_cast<int>(gridDim.x) + c;
+}
+
+template <int BN>
+__device__ __forceinline__ Item2 item_geometry(const PrefillParams &p, int k)
+{
+    Item2 it;
+    const int qb = p.heavy_first ? p.n_qblocks - 1 - k % p.n_qblocks : k % p.n_qblocks;
+    const int r = k / p.n_qblocks;
+    const int y = r % p.n_ygroups;
+    it.b = r / p.n_ygroups;
+    if (p.pair_heads) {
+        it.head[0] = 2 * y;
+        it.head[1] = 2 * y + 1;
+        it.row0[0] = it.row0[1] = qb * kBM;
+    } else {
+        it.head[0] = it.head[1] = y;
+        it.row0[0] = qb * 2 * kBM;
+        it.row0[1] = it.row0[0] + kBM;
+    }
+    // Rows of the block, clipped to the query range (and, for window masks, to the
+    // rows some window covers).  Every mask's [lo, hi) is non-decreasing in the row,
+    // so the first row gives the lowest key and the last row the highest.
+    int a = it.row0[0];
+    int z = min(it.row0[1] + kBM, p.seq_q) - 1;
+    if (p.mask_kind == SMOL_MASK_WINDOWS) {
+        a = max(a, p.window_starts[0]);
+        z = min(z, p.window_starts[p.n_windows] - 1);
+    }
+    it.lo_min = 0;
+    it.n_tiles = 0;
+    if (z >= a) {
+        int lo_a, hi_a, lo_z, hi_z;
+        bool w;
+        row_range(p, a, lo_a, hi_a, w);
+        row_range(p, z, lo_z, hi_z, w);
+        if (hi_z > lo_a) {
+            it.lo_min = lo_a;
+            it.n_tiles = (hi_z - lo_a + BN - 1) / BN;
+        }
+    }
+    return it;
+}
+
+template <int HD, bool Persistent, int PolyPairs8 = PolyShare<HD>::kPairs8>
+__global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_constant__ PrefillParams p)
 {
     using S = Prefill2Shape<HD>;
     constexpr int BN = S::BN;
-    constexpr int NSB = S::kNSB;
     constexpr int ST = S::kStages;
-
-    const int n_blocks = gridDim.x;
-    const int qb = n_blocks - 1 - static_cast<int>(blockIdx.x);   // heaviest first
-    const int b = blockIdx.z;
-    int head[2], row0[2];
-    if (pair_heads) {
-        head[0] = 2 * blockIdx.y;
-        head[1] = 2 * blockIdx.y + 1;
-        row0[0] = row0[1] = qb * kBM;
-    } else {
-        head[0] = head[1] = blockIdx.y;
-        row0[0] = qb * 2 * kBM;
-        row0[1] = row0[0] + kBM;
-    }
-    const int kvh = head[0] / p.group;
+    // One item per CTA (grid = items) unless Persistent: then rounds until items run out.
+    const int n_items = p.n_qblocks * p.n_ygroups * p.batch;
+    const int n_rounds = Persistent ? (n_items + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x) : 1;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -555,6 +609,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
 
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(&bars->q_full), 1);
+        mbar_init(smem_u32(&bars->q_empty), 1);
         for (int s = 0; s < ST; ++s) {
             mbar_init(smem_u32(&bars->k_full[s]), 1);
             mbar_init(smem_u32(&bars->k_empty[s]), 1);
@@ -562,101 +617,96 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
             mbar_init(smem_u32(&bars->v_empty[s]), 1);
         }
         for (int t = 0; t < 2; ++t) {
-            for (int sb = 0; sb < NSB; ++sb) {
-                mbar_init(smem_u32(&bars->s_full[t][sb]), 1);
-                mbar_init(smem_u32(&bars->p_full[t][sb]), kSoftmaxThreads);
-            }
+            mbar_init(smem_u32(&bars->s_full[t]), 1);
+            mbar_init(smem_u32(&bars->p_full[t]), kSoftmaxThreads);
             mbar_init(smem_u32(&bars->o_done[t]), 1);
         }
         mbar_init(smem_u32(&bars->mma_done), 1);
-        bars->lo_min = 0x7fffffff;
-        bars->hi_max = 0;
         fence_mbar_init();
     }
     if (warp == kMmaWarp2) {
         tmem_alloc(smem_u32(&bars->tmem_base), 512);
         tmem_relinquish();
     }
-    const bool is_softmax = warp < 8;
-    const int tile = warp >> 2;                       // softmax tile of this thread
-    const int row = row0[tile & 1] + (threadIdx.x & 127);
-    const bool row_valid = is_softmax && row < p.seq_q;
-    int my_lo = 0, my_hi = 0;
-    bool my_written = false;
-    __syncthreads();
-    if (row_valid) {
-        row_range(p, row, my_lo, my_hi, my_written);
-        if (my_hi > my_lo) {
-            atomicMin(&bars->lo_min, my_lo);
-            atomicMax(&bars->hi_max, my_hi);
-        }
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
-    const int lo_min = bars->lo_min;
-    const int hi_max = bars->hi_max;
-    const int n_tiles = hi_max > lo_min ? (hi_max - lo_min + BN - 1) / BN : 0;
 
     uint8_t *sQ = smem + S::kOffQ;
     uint8_t *sK = smem + S::kOffK;
     uint8_t *sV = smem + S::kOffV;
 
+    // Barrier phases run on across items: q_full / q_empty once per item with key
+    // tiles (count qit), the K/V ring and s_full / p_full / o_done once per key tile
+    // (global count g over all items of this CTA).
     if (warp >= 8) {
     // warpgroup 2 (producer, MMA issuer, two idle warps) hands registers to the softmax
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsOther2));
     if (warp == kProducerWarp2) {
-        if (lane == 0 && n_tiles > 0) {
+        if (lane == 0) {
             tma_prefetch_desc(&p.tq);
             tma_prefetch_desc(&p.tk);
             tma_prefetch_desc(&p.tv);
-            const uint32_t qbar = smem_u32(&bars->q_full);
-            mbar_arrive_expect_tx(qbar, 2 * S::kQBytes);
-#pragma unroll
-            for (int t = 0; t < 2; ++t)
-#pragma unroll
-                for (int sub = 0; sub < S::kSub; ++sub)
-                    tma_load_3d(smem_u32(sQ + t * S::kQBytes + sub * S::kQSubBytes), &p.tq, qbar,
-                                head[t] * HD + sub * 64, row0[t], b);
-            int kiss = 0, viss = 0;
-            for (int j = 0; j < n_tiles; ++j) {
-                const int st = j % ST;
-                const int key0 = lo_min + j * BN;
-                if (j >= ST && !mbar_wait(smem_u32(&bars->k_empty[st]), ((j / ST) - 1) & 1, p.err, kErrWaitTmaEmpty))
+            int qit = 0, g = 0;
+            bool ok = true;
+            for (int r = 0; r < n_rounds && ok; ++r) {
+                const int k = item_index(p, r);
+                if (k >= n_items) break;
+                const Item2 it = item_geometry<BN>(p, k);
+                if (it.n_tiles == 0) continue;
+                // Q of this item overwrites the last one's: wait for its final S MMAs.
+                if (qit > 0 && !(ok = mbar_wait(smem_u32(&bars->q_empty), (qit - 1) & 1, p.err, kErrWaitTmaEmpty)))
                     break;
-                const uint32_t kb = smem_u32(&bars->k_full[st]);
-                mbar_arrive_expect_tx(kb, S::kKvBytes);
+                const uint32_t qbar = smem_u32(&bars->q_full);
+                mbar_arrive_expect_tx(qbar, 2 * S::kQBytes);
 #pragma unroll
-                for (int sub = 0; sub < S::kSub; ++sub)
-                    tma_load_3d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb,
-                                kvh * HD + sub * 64, key0, b);
-                ++kiss;
-                if (j >= ST && !mbar_wait(smem_u32(&bars->v_empty[st]), ((j / ST) - 1) & 1, p.err, kErrWaitTmaEmpty))
-                    break;
-                const uint32_t vb = smem_u32(&bars->v_full[st]);
-                mbar_arrive_expect_tx(vb, S::kKvBytes);
+                for (int t = 0; t < 2; ++t)
 #pragma unroll
-                for (int sub = 0; sub < S::kSub; ++sub)
-                    tma_load_3d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb,
-                                kvh * HD + sub * 64, key0, b);
-                ++viss;
+                    for (int sub = 0; sub < S::kSub; ++sub)
+                        tma_load_3d(smem_u32(sQ + t * S::kQBytes + sub * S::kQSubBytes), &p.tq, qbar,
+                                    it.head[t] * HD + sub * 64, it.row0[t], it.b);
+                ++qit;
+                const int kvh = it.head[0] / p.group;
+                for (int j = 0; j < it.n_tiles; ++j, ++g) {
+                    const int st = g % ST;
+                    const int key0 = it.lo_min + j * BN;
+                    if (g >= ST &&
+                        !(ok = mbar_wait(smem_u32(&bars->k_empty[st]), ((g / ST) - 1) & 1, p.err, kErrWaitTmaEmpty)))
+                        break;
+                    const uint32_t kb = smem_u32(&bars->k_full[st]);
+                    mbar_arrive_expect_tx(kb, S::kKvBytes);
+#pragma unroll
+                    for (int sub = 0; sub < S::kSub; ++sub)
+                        tma_load_3d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb,
+                                    kvh * HD + sub * 64, key0, it.b);
+                    if (g >= ST &&
+                        !(ok = mbar_wait(smem_u32(&bars->v_empty[st]), ((g / ST) - 1) & 1, p.err, kErrWaitTmaEmpty)))
+                        break;
+                    const uint32_t vb = smem_u32(&bars->v_full[st]);
+                    mbar_arrive_expect_tx(vb, S::kKvBytes);
+#pragma unroll
+                    for (int sub = 0; sub < S::kSub; ++sub)
+                        tma_load_3d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb,
+                                    kvh * HD + sub * 64, key0, it.b);
+                }
             }
-            mbar_wait(smem_u32(&bars->q_full), 0, p.err, kErrDrain);
-            for (int j = max(0, kiss - ST); j < kiss; ++j)
+            // Drain: the last Q and the last ST key tiles must have landed before exit.
+            if (qit > 0) mbar_wait(smem_u32(&bars->q_full), (qit - 1) & 1, p.err, kErrDrain);
+            for (int j = max(0, g - ST); j < g; ++j) {
                 if (!mbar_wait(smem_u32(&bars->k_full[j % ST]), (j / ST) & 1, p.err, kErrDrain)) break;
-            for (int j = max(0, viss - ST); j < viss; ++j)
                 if (!mbar_wait(smem_u32(&bars->v_full[j % ST]), (j / ST) & 1, p.err, kErrDrain)) break;
+            }
         }
     } else if (warp == kMmaWarp2) {
-        if (lane == 0 && n_tiles > 0) {
+        if (lane == 0) {
             constexpr uint32_t idesc_s = umma_idesc_f16(kBM, BN, true, false);
             constexpr uint32_t idesc_pv = umma_idesc_f16(kBM, HD, false, true);
-            // S_t(j) lands in S buffer j % NSB of tile t; K/V of key tile j sit in ring slot j % ST.
-            auto issue_s = [&](int t, int j) {
+            // S of Q tile t for global key tile g; K/V of key tile g sit in ring slot g % ST.
+            auto issue_s = [&](int t, int g) {
                 const uint32_t q_addr = smem_u32(sQ + t * S::kQBytes);
-                const uint32_t k_addr = smem_u32(sK + (j % ST) * S::kKvBytes);
-                const uint32_t s_col = tmem + t * S::kTileCols + (j % NSB) * BN;
+                const uint32_t k_addr = smem_u32(sK + (g % ST) * S::kKvBytes);
+                const uint32_t s_col = tmem + t * S::kTileCols;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk) {
                     const uint32_t off = (kk & 3) * 32;
@@ -664,57 +714,71 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     const uint64_t bdesc = umma_sdesc_sw128(k_addr + (kk >> 2) * S::kKvSubBytes + off, 16, 1024);
                     umma_ss(s_col, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
                 }
-                umma_commit(smem_u32(&bars->s_full[t][j % NSB]));
+                umma_commit(smem_u32(&bars->s_full[t]));
             };
-            auto issue_pv = [&](int t, int j) {
-                const uint32_t v_addr = smem_u32(sV + (j % ST) * S::kKvBytes);
-                const uint32_t p_col = tmem + t * S::kTileCols + (j % NSB) * BN;
+            // O_t (+)= P_t V for key tile g; `first` starts the accumulation of an item.
+            auto issue_pv = [&](int t, int g, bool first) {
+                const uint32_t v_addr = smem_u32(sV + (g % ST) * S::kKvBytes);
+                const uint32_t p_col = tmem + t * S::kTileCols;
                 const uint32_t o_col = tmem + t * S::kTileCols + S::kTmO;
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
                     const uint64_t bdesc = umma_sdesc_sw128(v_addr + kk * 16 * 128, S::kKvSubBytes, 1024);
-                    umma_ts(o_col, p_col + kk * 8, bdesc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+                    umma_ts(o_col, p_col + kk * 8, bdesc, idesc_pv, (!first || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(smem_u32(&bars->o_done[t]));
             };
-            auto wait_k = [&](int j) {
-                return mbar_wait(smem_u32(&bars->k_full[j % ST]), (j / ST) & 1, p.err, kErrWaitTmaFull);
+            auto wait_k = [&](int g) {
+                return mbar_wait(smem_u32(&bars->k_full[g % ST]), (g / ST) & 1, p.err, kErrWaitTmaFull);
             };
-            // Prologue: S of the first NSB key tiles for both Q tiles.
-            bool ok = mbar_wait(smem_u32(&bars->q_full), 0, p.err, kErrWaitTmaFull);
-            for (int j = 0; j < NSB && j < n_tiles && ok; ++j) {
-                ok = wait_k(j);
+            int qit = 0, g0 = 0;
+            bool ok = true;
+            for (int r = 0; r < n_rounds && ok; ++r) {
+                const int k = item_index(p, r);
+                if (k >= n_items) break;
+                const Item2 it = item_geometry<BN>(p, k);
+                const int n = it.n_tiles;
+                if (n == 0) continue;
+                // Prologue: S of the item's first key tile for both Q tiles.  (The
+                // previous item's last PV read P from the same TMEM columns; MMAs of
+                // this thread run in issue order.)
+                ok = mbar_wait(smem_u32(&bars->q_full), qit & 1, p.err, kErrWaitTmaFull) && wait_k(g0);
                 if (!ok) break;
                 tc_fence_after();
-                issue_s(0, j);
-                issue_s(1, j);
-                umma_commit(smem_u32(&bars->k_empty[j % ST]));
-            }
-            for (int j = 0; j < n_tiles && ok; ++j) {
-                const int st = j % ST;
-                const int sb = j % NSB;
-                ok = mbar_wait(smem_u32(&bars->p_full[0][sb]), (j / NSB) & 1, p.err, kErrWaitSoftmax) &&
-                     mbar_wait(smem_u32(&bars->v_full[st]), (j / ST) & 1, p.err, kErrWaitTmaFull);
-                if (!ok) break;
-                tc_fence_after();
-                issue_pv(0, j);
-                const int jn = j + NSB;                 // S buffer sb is free again after PV0(j)
-                const bool more = jn < n_tiles;
-                if (more) {
-                    ok = wait_k(jn);
+                issue_s(0, g0);
+                issue_s(1, g0);
+                umma_commit(smem_u32(&bars->k_empty[g0 % ST]));
+                if (n == 1) umma_commit(smem_u32(&bars->q_empty));
+                // O_t is overwritten by the item's first PV: its readers (the previous
+                // item's epilogue) are the threads whose p_full arrival that PV waits for.
+                for (int j = 0; j < n && ok; ++j) {
+                    const int g = g0 + j;
+                    const int st = g % ST;
+                    ok = mbar_wait(smem_u32(&bars->p_full[0]), g & 1, p.err, kErrWaitSoftmax) &&
+                         mbar_wait(smem_u32(&bars->v_full[st]), (g / ST) & 1, p.err, kErrWaitTmaFull);
                     if (!ok) break;
                     tc_fence_after();
-                    issue_s(0, jn);
+                    issue_pv(0, g, j == 0);
+                    const bool more = j + 1 < n;   // S buffer of tile 0 is free again after PV0
+                    if (more) {
+                        ok = wait_k(g + 1);
+                        if (!ok) break;
+                        tc_fence_after();
+                        issue_s(0, g + 1);
+                    }
+                    ok = mbar_wait(smem_u32(&bars->p_full[1]), g & 1, p.err, kErrWaitSoftmax);
+                    if (!ok) break;
+                    tc_fence_after();
+                    issue_pv(1, g, j == 0);
+                    umma_commit(smem_u32(&bars->v_empty[st]));
+                    if (more) {
+                        issue_s(1, g + 1);
+                        umma_commit(smem_u32(&bars->k_empty[(g + 1) % ST]));
+                        if (j + 2 == n) umma_commit(smem_u32(&bars->q_empty));   // last S of the item
+                    }
                 }
-                ok = mbar_wait(smem_u32(&bars->p_full[1][sb]), (j / NSB) & 1, p.err, kErrWaitSoftmax);
-                if (!ok) break;
-                tc_fence_after();
-                issue_pv(1, j);
-                umma_commit(smem_u32(&bars->v_empty[st]));
-                if (more) {
-                    issue_s(1, jn);
-                    umma_commit(smem_u32(&bars->k_empty[jn % ST]));
-                }
+                g0 += n;
+                ++qit;
             }
             umma_commit(smem_u32(&bars->mma_done));
             mbar_wait(smem_u32(&bars->mma_done), 0, p.err, kErrDrain);
@@ -723,183 +787,212 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
     } else {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax2));
         // ================= softmax of tile `tile`, thread owns query row `row` =================
+        const int tile = warp >> 2;
         const uint32_t lane_base = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + tile * S::kTileCols;
         const float cap = p.softcap;
         const float inv_cap = cap > 0.f ? 1.f / cap : 0.f;
         const float kLog2e = 1.4426950408889634f;
         const float sl2 = p.scale_log2;
-        float m = -INFINITY;   // running maximum of score*scale*log2(e)
-        float l = 0.f;
-        bool ok = true;
+        const uint32_t s_full = smem_u32(&bars->s_full[tile]);
+        const uint32_t p_full = smem_u32(&bars->p_full[tile]);
         const uint32_t o_done = smem_u32(&bars->o_done[tile]);
-        for (int j = 0; j < n_tiles; ++j) {
-            const int sb = j % NSB;
-            const uint32_t s_full = smem_u32(&bars->s_full[tile][sb]);
-            const uint32_t p_full = smem_u32(&bars->p_full[tile][sb]);
-            const uint32_t s_base = lane_base + sb * BN;   // S of this key tile; P overwrites it
-            ok = __all_sync(0xffffffffu, mbar_wait(s_full, (j / NSB) & 1, p.err, kErrWaitMma));
-            if (!ok) break;
-            tc_fence_after();
-            float t[BN];
-            {
-                // all column groups in flight before one wait
-                uint32_t r[BN / 32][32];
-#pragma unroll
-                for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_base + c * 32, r[c]);
-                tmem_ld_wait();
-#pragma unroll
-                for (int c = 0; c < BN / 32; ++c)
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(r[c][i]);
-            }
-            const int key0 = lo_min + j * BN;
-            const bool full_tile = row_valid && key0 >= my_lo && key0 + BN <= my_hi;
-            if (cap > 0.f) {
-#pragma unroll
-                for (int c = 0; c < BN; ++c) t[c] = cap * tanhf(t[c] * p.scale * inv_cap) * kLog2e;
-            }
-            if (!full_tile) {
-#pragma unroll
-                for (int c = 0; c < BN; ++c) {
-                    const int key = key0 + c;
-                    if (!row_valid || key < my_lo || key >= my_hi) t[c] = -INFINITY;
-                }
-            }
-            // Row max as 8 independent chains of 3-input maxima and a short tree (a single
-            // chain over BN scores would serialise BN/2 dependent instructions).
-            float mx;
-            {
-                float pm[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) pm[k] = fmaxf(t[2 * k], t[2 * k + 1]);
-#pragma unroll
-                for (int c = 16; c < BN; c += 16)
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) pm[k] = max3f(pm[k], t[c + 2 * k], t[c + 2 * k + 1]);
-                mx = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
-            }
-            // scores are raw (scale applied below) unless softcapped (already in log2 units)
-            const float mxs = cap > 0.f ? mx : mx * sl2;
-            const bool need = m != -INFINITY && mxs > m + kRescaleThreshold;
-            if (__any_sync(0xffffffffu, need)) {
-                ok = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, p.err, kErrWaitMma));
+        bool stores_pending = false;   // lane 0: a TMA store from this warp's staging area
+        int g0 = 0;
+        bool ok = true;
+        for (int r = 0; r < n_rounds && ok; ++r) {
+            const int k = item_index(p, r);
+            if (k >= n_items) break;
+            const Item2 it = item_geometry<BN>(p, k);
+            const int n_tiles = it.n_tiles;
+            const int row = it.row0[tile] + (threadIdx.x & 127);
+            const bool row_valid = row < p.seq_q;
+            int my_lo = 0, my_hi = 0;
+            bool my_written = false;
+            if (row_valid) row_range(p, row, my_lo, my_hi, my_written);
+            float m = -INFINITY;   // running maximum of score*scale*log2(e)
+            float l = 0.f;
+            for (int j = 0; j < n_tiles; ++j) {
+                const int g = g0 + j;
+                const uint32_t s_base = lane_base;   // S of this key tile; P overwrites it
+                ok = __all_sync(0xffffffffu, mbar_wait(s_full, g & 1, p.err, kErrWaitMma));
                 if (!ok) break;
                 tc_fence_after();
-                const float f = need ? fast_exp2(m - mxs) : 1.f;
-                uint32_t r[32];
+                float t[BN];
+                {
+                    // all column groups in flight before one wait
+                    uint32_t rr[BN / 32][32];
+#pragma unroll
+                    for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_base + c * 32, rr[c]);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(rr[c][i]);
+                }
+                const int key0 = it.lo_min + j * BN;
+                const bool full_tile = row_valid && key0 >= my_lo && key0 + BN <= my_hi;
+                if (cap > 0.f) {
+#pragma unroll
+                    for (int c = 0; c < BN; ++c) t[c] = cap * tanhf(t[c] * p.scale * inv_cap) * kLog2e;
+                }
+                if (!full_tile) {
+#pragma unroll
+                    for (int c = 0; c < BN; ++c) {
+                        const int key = key0 + c;
+                        if (!row_valid || key < my_lo || key >= my_hi) t[c] = -INFINITY;
+                    }
+                }
+                // Row max as 8 independent chains of 3-input maxima and a short tree (a single
+                // chain over BN scores would serialise BN/2 dependent instructions).
+                float mx;
+                {
+                    float pm[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) pm[q] = fmaxf(t[2 * q], t[2 * q + 1]);
+#pragma unroll
+                    for (int c = 16; c < BN; c += 16)
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) pm[q] = max3f(pm[q], t[c + 2 * q], t[c + 2 * q + 1]);
+                    mx = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
+                }
+                // scores are raw (scale applied below) unless softcapped (already in log2 units)
+                const float mxs = cap > 0.f ? mx : mx * sl2;
+                const bool need = m != -INFINITY && mxs > m + kRescaleThreshold;   // only when j > 0
+                if (__any_sync(0xffffffffu, need)) {
+                    ok = __all_sync(0xffffffffu, mbar_wait(o_done, (g - 1) & 1, p.err, kErrWaitMma));
+                    if (!ok) break;
+                    tc_fence_after();
+                    const float f = need ? fast_exp2(m - mxs) : 1.f;
+                    uint32_t rr[32];
+#pragma unroll
+                    for (int c = 0; c < HD / 32; ++c) {
+                        tmem_ld32(lane_base + S::kTmO + c * 32, rr);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * f);
+                        tmem_st32(lane_base + S::kTmO + c * 32, rr);
+                    }
+                    l *= f;
+                }
+                if (need || (m == -INFINITY && mxs > -INFINITY)) m = mxs;
+                // P = exp2(s*scale_log2 - m): one packed FMA per two scores, then ex2.
+                const bool live = m != -INFINITY;
+                const float mul = cap > 0.f ? 1.f : sl2;
+                const uint64_t vmul = f2_pack(mul, mul);
+                const uint64_t vneg = f2_pack(live ? -m : 0.f, live ? -m : 0.f);
+                uint64_t acc[4] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+                {
+                    uint32_t rr[32];
+#pragma unroll
+                    for (int c = 0; c < BN / 64; ++c) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const uint64_t x = f2_fma(f2_pack(t[c * 64 + 2 * i], t[c * 64 + 2 * i + 1]), vmul, vneg);
+                            float e0, e1;
+                            if ((i & 7) < PolyPairs8) {   // this pair on the FMA pipe
+                                exp2_poly_pair(x, e0, e1);
+                            } else {                      // this pair on MUFU
+                                e0 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x)));
+                                e1 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x >> 32)));
+                            }
+                            if (!live) e0 = e1 = 0.f;
+                            acc[i & 3] = f2_add(acc[i & 3], f2_pack(e0, e1));   // 4 independent sums
+                            rr[i] = pack_f16x2(e0, e1);
+                        }
+                        tmem_st32(s_base + c * 32, rr);
+                    }
+                }
+                const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
+                const uint64_t a = f2_add(a01, a23);
+                l += __uint_as_float(static_cast<uint32_t>(a)) + __uint_as_float(static_cast<uint32_t>(a >> 32));
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(p_full);
+            }
+            if (!ok) break;
+
+            // ---- epilogue: O / l -> out (fp32) ----
+            bool have_o = n_tiles > 0;
+            if (have_o) {
+                have_o = __all_sync(0xffffffffu, mbar_wait(o_done, (g0 + n_tiles - 1) & 1, p.err, kErrWaitMma));
+                ok = have_o;
+            }
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            const int head = it.head[tile];
+            // Staged epilogue: this warp's 32 rows go through shared memory (128B-swizzled
+            // 32 x 32 fp32 boxes) and leave with TMA tensor stores, so every output row is
+            // written as whole sectors.  The staging area is the CTA's own when it fits
+            // beside the rings (head dim 64); otherwise the K ring (tile 0) or V ring
+            // (tile 1), which are free only after the CTA's last item (no load left, and
+            // this tile's last PV completed after every S of the item).  Rows no window
+            // covers must stay untouched, so warps holding one fall back to row stores.
+            const bool last_item = !Persistent || item_index(p, r + 1) >= n_items;
+            const bool staged = ok && (S::kEpiOwn || last_item) && __all_sync(0xffffffffu, my_written || !row_valid);
+            if (staged) {
+                uint8_t *stage = S::kEpiOwn ? smem + S::kOffEpi + warp * (32 * HD * 4)
+                                            : (tile == 0 ? sK : sV) + (warp & 3) * (32 * HD * 4);
+                if (lane == 0 && stores_pending) bulk_wait_read0();   // previous store read its staging
+                __syncwarp();
+                uint32_t rr[32];
 #pragma unroll
                 for (int c = 0; c < HD / 32; ++c) {
-                    tmem_ld32(lane_base + S::kTmO + c * 32, r);
-                    tmem_ld_wait();
+                    if (have_o) {
+                        tmem_ld32(lane_base + S::kTmO + c * 32, rr);
+                        tmem_ld_wait();
+                    } else {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-                    tmem_st32(lane_base + S::kTmO + c * 32, r);
+                        for (int i = 0; i < 32; ++i) rr[i] = 0u;
+                    }
+                    uint8_t *box = stage + c * (32 * 128);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        float4 v = make_float4(__uint_as_float(rr[4 * q]) * inv, __uint_as_float(rr[4 * q + 1]) * inv,
+                                               __uint_as_float(rr[4 * q + 2]) * inv,
+                                               __uint_as_float(rr[4 * q + 3]) * inv);
+                        *reinterpret_cast<float4 *>(box + sw128_offset(lane, q)) = v;
+                    }
                 }
-                l *= f;
-            }
-            if (need || (m == -INFINITY && mxs > -INFINITY)) m = mxs;
-            // P = exp2(s*scale_log2 - m): one packed FMA per two scores, then ex2.
-            const bool live = m != -INFINITY;
-            const float mul = cap > 0.f ? 1.f : sl2;
-            const uint64_t vmul = f2_pack(mul, mul);
-            const uint64_t vneg = f2_pack(live ? -m : 0.f, live ? -m : 0.f);
-            uint64_t acc[4] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
-            {
-                uint32_t r[32];
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    const int y = it.row0[tile] + (warp & 3) * 32;
 #pragma unroll
-                for (int c = 0; c < BN / 64; ++c) {
+                    for (int c = 0; c < HD / 32; ++c)
+                        tma_store_3d(&p.to, smem_u32(stage + c * (32 * 128)), head * HD + c * 32, y, it.b);
+                    bulk_commit();
+                    stores_pending = true;
+                }
+                __syncwarp();
+            } else if (ok) {
+                const bool store = row_valid && my_written;
+                float *orow = p.out + static_cast<long long>(it.b) * p.out_batch_stride +
+                              static_cast<long long>(store ? row : 0) * p.out_row_stride +
+                              static_cast<long long>(head) * HD;
+                uint32_t rr[32];
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const uint64_t x = f2_fma(f2_pack(t[c * 64 + 2 * i], t[c * 64 + 2 * i + 1]), vmul, vneg);
-                        float e0, e1;
-                        if ((i & 7) < PolyPairs8) {   // this pair on the FMA pipe
-                            exp2_poly_pair(x, e0, e1);
-                        } else {                      // this pair on MUFU
-                            e0 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x)));
-                            e1 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x >> 32)));
+                for (int c = 0; c < HD / 32; ++c) {
+                    if (have_o) {
+                        tmem_ld32(lane_base + S::kTmO + c * 32, rr);
+                        tmem_ld_wait();
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) rr[i] = 0u;
+                    }
+                    if (store) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4) {
+                            float4 v = make_float4(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv,
+                                                   __uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
+                            *reinterpret_cast<float4 *>(orow + c * 32 + i) = v;
                         }
-                        if (!live) e0 = e1 = 0.f;
-                        acc[i & 3] = f2_add(acc[i & 3], f2_pack(e0, e1));   // 4 independent sums
-                        r[i] = pack_f16x2(e0, e1);
-                    }
-                    tmem_st32(s_base + c * 32, r);
-                }
-            }
-            const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
-            const uint64_t a = f2_add(a01, a23);
-            l += __uint_as_float(static_cast<uint32_t>(a)) + __uint_as_float(static_cast<uint32_t>(a >> 32));
-            tmem_st_wait();
-            tc_fence_before();
-            mbar_arrive(p_full);
-        }
-        bool have_o = ok && n_tiles > 0;
-        if (have_o)
-            have_o = __all_sync(0xffffffffu, mbar_wait(o_done, (n_tiles - 1) & 1, p.err, kErrWaitMma));
-        tc_fence_after();
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        // Staged epilogue: this warp's 32 rows go through shared memory (128B-swizzled
-        // 32 x 32 fp32 boxes) and leave with TMA tensor stores, so every output row is
-        // written as whole sectors.  Tile 0 stages in the K ring, tile 1 in the V ring:
-        // both are free once this tile's last PV completed (S and PV are issued in
-        // order, and the producer has no load left).  Rows no window covers must stay
-        // untouched, so warps holding one fall back to per-row stores.
-        const bool staged = ok && __all_sync(0xffffffffu, my_written || !row_valid);
-        if (staged) {
-            uint8_t *stage = (tile == 0 ? sK : sV) + (warp & 3) * (32 * HD * 4);
-            uint32_t r[32];
-#pragma unroll
-            for (int c = 0; c < HD / 32; ++c) {
-                if (have_o) {
-                    tmem_ld32(lane_base + S::kTmO + c * 32, r);
-                    tmem_ld_wait();
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) r[i] = 0u;
-                }
-                uint8_t *box = stage + c * (32 * 128);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    float4 v = make_float4(__uint_as_float(r[4 * k]) * inv, __uint_as_float(r[4 * k + 1]) * inv,
-                                           __uint_as_float(r[4 * k + 2]) * inv, __uint_as_float(r[4 * k + 3]) * inv);
-                    *reinterpret_cast<float4 *>(box + sw128_offset(lane, k)) = v;
-                }
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                const int y = row0[tile & 1] + (warp & 3) * 32;
-#pragma unroll
-                for (int c = 0; c < HD / 32; ++c)
-                    tma_store_3d(&p.to, smem_u32(stage + c * (32 * 128)), head[tile & 1] * HD + c * 32, y, b);
-                bulk_commit();
-                bulk_wait_read0();
-            }
-            __syncwarp();
-        } else {
-            const bool store = ok && row_valid && my_written;
-            float *orow = p.out + static_cast<long long>(b) * p.out_batch_stride +
-                          static_cast<long long>(store ? row : 0) * p.out_row_stride +
-                          static_cast<long long>(head[tile & 1]) * HD;
-            uint32_t r[32];
-#pragma unroll
-            for (int c = 0; c < HD / 32; ++c) {
-                if (have_o) {
-                    tmem_ld32(lane_base + S::kTmO + c * 32, r);
-                    tmem_ld_wait();
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) r[i] = 0u;
-                }
-                if (store) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        float4 v = make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
-                                               __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
-                        *reinterpret_cast<float4 *>(orow + c * 32 + i) = v;
                     }
                 }
             }
+            g0 += n_tiles;
         }
+        if (lane == 0 && stores_pending) bulk_wait_read0();
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -919,6 +1012,48 @@ template <>
 struct KvTileRows<256> {
     static constexpr int value = PrefillShape<256>::BN;
 };
+
+// SMOL_PREFILL_PERSISTENT=1 in the environment makes head dim 128 persistent too
+// (measurement knob; head dim 64 always is).
+const bool g_prefill_persistent_all = [] {
+    const char *e = getenv("SMOL_PREFILL_PERSISTENT");
+    return e && e[0] == '1';
+}();
+
+int sm_count()
+{
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+// Once per device and instantiation: check the register count the in-kernel split is
+// sized for (the block launches with kRegsLaunch2 per thread; any other build is
+// refused) and raise the dynamic shared-memory limit.
+template <int HD, bool Persistent>
+int prepare_v2(int dev)
+{
+    static bool done[16] = {};
+    if (dev < 0 || dev >= 16) return SMOL_B200_ERR_CUDA;
+    if (done[dev]) return SMOL_B200_OK;
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, prefill2_kernel<HD, Persistent>) != cudaSuccess) return SMOL_B200_ERR_CUDA;
+    if (fa.numRegs != kRegsLaunch2) {
+        char buf[128];
+        snprintf(buf, sizeof(buf), "prefill2_kernel compiled with %d registers, expected %d", fa.numRegs,
+                 kRegsLaunch2);
+        set_error(SMOL_B200_ERR_CUDA, buf);
+        return SMOL_B200_ERR_CUDA;
+    }
+    if (cudaFuncSetAttribute(prefill2_kernel<HD, Persistent>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Prefill2Shape<HD>::kSmemBytes) != cudaSuccess)
+        return SMOL_B200_ERR_CUDA;
+    done[dev] = true;
+    return SMOL_B200_OK;
+}
 
 template <int HD>
 int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t out_batch_stride,
@@ -987,27 +1122,28 @@ int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t 
         prefill_kernel<HD><<<grid, kThreads, S::kSmemBytes, st>>>(p);
     } else {
         using S2 = Prefill2Shape<HD>;
-        if (dev >= 0 && dev < 16 && !attr_set[dev]) {
-            // The register split inside the kernel is sized for a launch of exactly
-            // kRegsLaunch2 registers per thread; refuse to run any other build of it.
-            cudaFuncAttributes fa;
-            if (cudaFuncGetAttributes(&fa, prefill2_kernel<HD>) != cudaSuccess) return SMOL_B200_ERR_CUDA;
-            if (fa.numRegs != kRegsLaunch2) {
-                char buf[128];
-                snprintf(buf, sizeof(buf), "prefill2_kernel compiled with %d registers, expected %d", fa.numRegs,
-                         kRegsLaunch2);
-                set_error(SMOL_B200_ERR_CUDA, buf);
-                return SMOL_B200_ERR_CUDA;
-            }
-            if (cudaFuncSetAttribute(prefill2_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     S2::kSmemBytes) != cudaSuccess)
-                return SMOL_B200_ERR_CUDA;
-            attr_set[dev] = true;
+        p.pair_heads = (p.group % 2 == 0) ? 1 : 0;
+        p.n_qblocks = p.pair_heads ? (seq_q + kBM - 1) / kBM : (seq_q + 2 * kBM - 1) / (2 * kBM);
+        p.n_ygroups = p.pair_heads ? n_heads / 2 : n_heads;
+        p.batch = batch;
+        // Query blocks of causal-like masks carry more keys the later they start.
+        p.heavy_first = (mask_kind == SMOL_MASK_CAUSAL || mask_kind == SMOL_MASK_PREFIX_LM) ? 1 : 0;
+        const long long n_items = static_cast<long long>(p.n_qblocks) * p.n_ygroups * batch;
+        if (n_items > 0x7fffffffLL) return SMOL_B200_ERR_ARGS;
+        // Persistent CTAs (one per SM) for head dim 64, where items are short and a
+        // CTA's fill and drain would otherwise be exposed; one CTA per item otherwise.
+        int grid = static_cast<int>(n_items);
+        if (HD == 64 || g_prefill_persistent_all) {
+            const int sms = sm_count();
+            if (sms > 0 && grid > sms) grid = sms;
+            const int rc = prepare_v2<HD, true>(dev);
+            if (rc != SMOL_B200_OK) return rc;
+            prefill2_kernel<HD, true><<<grid, kThreads2, S2::kSmemBytes, st>>>(p);
+        } else {
+            const int rc = prepare_v2<HD, false>(dev);
+            if (rc != SMOL_B200_OK) return rc;
+            prefill2_kernel<HD, false><<<grid, kThreads2, S2::kSmemBytes, st>>>(p);
         }
-        const int pair = (p.group % 2 == 0) ? 1 : 0;
-        const int n_blocks = pair ? (seq_q + kBM - 1) / kBM : (seq_q + 2 * kBM - 1) / (2 * kBM);
-        dim3 grid(n_blocks, pair ? n_heads / 2 : n_heads, batch);
-        prefill2_kernel<HD><<<grid, kThreads2, S2::kSmemBytes, st>>>(p, pair);
     }
     return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
 }

@@ -13,6 +13,7 @@ from __future__ import annotations
 import ctypes
 import os
 import re
+import sys
 
 import numpy as np
 
@@ -118,7 +119,14 @@ def _ptr(x) -> int | None:
 
 
 def _stream(stream) -> int | None:
+    """The CUDA stream handle to launch on.  None means torch's current stream when
+    torch has initialised CUDA in this process (so calls inside `torch.cuda.stream(s)`
+    or `torch.cuda.graph(g)` land on that stream and can be captured), else the
+    legacy default stream (NULL)."""
     if stream is None:
+        torch = sys.modules.get("torch")
+        if torch is not None and torch.cuda.is_initialized():
+            return torch.cuda.current_stream().cuda_stream or None
         return None
     if isinstance(stream, int):
         return stream
