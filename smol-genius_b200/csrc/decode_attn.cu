@@ -34,6 +34,7 @@
 // running sum) per Q head; a second kernel merges the chunks of a sequence.
 // Algorithmic traffic: every attended key costs n_kv_heads*hd*2 (K,V) * 2 bytes.
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -58,6 +59,10 @@ struct DecodeShape {
     static constexpr int kQRowFloats = HD + 8;                     // padded fp32 Q row
     static constexpr int kQBytes = 8 * kQRowFloats * 4;
     static constexpr int kQVecPerThread = 8 * HD * 4 / 16 / (kConsumerWarps * 32);   // 16-byte loads
+    // After the K/V tiles: the 4-warp merge area, then the CTA's partial [8][m, l, O[HD]].
+    static constexpr int kRedBytes = kConsumerWarps * 8 * (HD + 2) * 4;
+    static constexpr int kCpartOff = kRedBytes;
+    static_assert(kRedBytes + 8 * (HD + 2) * 4 <= kStageBytes, "merge areas must fit one stage");
     // Layout: [stages x stage][Q rows][barriers], base aligned to 1024 (SW128 tiles).
     static constexpr size_t smem_bytes(int stages)
     {
@@ -77,6 +82,7 @@ struct DecodeParams {
     int q_is_bf16;
     int n_heads, n_kv_heads, group, n_qgroups;
     int chunk, max_chunks, window;
+    float *out;                     // [n_seqs, n_heads*hd] fp32 (cluster form writes it directly)
     int stages;                     // K/V ring depth, 1..kMaxStages
     int q_vec16;                    // q base 16-byte aligned: Q rows copied with 16-byte loads
     float scale, softcap;
@@ -96,7 +102,15 @@ __device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t &hi, u
     lo = pack_bf16x2(x0 - bf16lo_f32(hi), x1 - bf16hi_f32(hi));
 }
 
-template <int HD>
+// Cluster form (InCluster): the max_chunks CTAs of one (sequence, KV head, Q-head
+// group) form a thread-block cluster along x.  Each leaves its partial in its own
+// shared memory; after a cluster barrier every CTA merges a slice of the outputs by
+// reading the partials of the others through distributed shared memory and writes
+// `out` directly, and a second cluster barrier keeps every CTA resident until the
+// others finished reading it.  Every thread of every CTA, idle chunks included,
+// passes both barriers.  Used for small batches, whose grid fits one wave and whose
+// separate merge launch would otherwise cost as much as the split itself.
+template <int HD, bool InCluster>
 __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_constant__ DecodeParams p)
 {
     using S = DecodeShape<HD>;
@@ -110,10 +124,11 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_
     const int L = p.kv_len[b];
     const int ks = (p.window > 0 && L > p.window) ? L - p.window : 0;
     int n = L - ks;
-    if (n > p.max_chunks * p.chunk) n = p.max_chunks * p.chunk;   // flagged by the combine kernel
+    if (n > p.max_chunks * p.chunk) n = p.max_chunks * p.chunk;   // flagged by the merge
     const int key0 = c * p.chunk;                                  // relative to ks
-    if (n <= 0 || key0 >= n) return;                               // uniform for the CTA
-    const int nkeys = min(p.chunk, n - key0);
+    const bool active = n > 0 && key0 < n;                         // uniform for the CTA
+    if (!InCluster && !active) return;
+    const int nkeys = active ? min(p.chunk, n - key0) : 0;
     const int ntiles = (nkeys + kKeysPerTile - 1) / kKeysPerTile;
     const int h_first = kvh * p.group + qg * 8;
     const int nh = min(8, p.group - qg * 8);
@@ -140,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_
 
     if (warp == kConsumerWarps) {
         // ---------------- producer warp ----------------
-        if (lane == 0) {
+        if (lane == 0 && ntiles > 0) {
             tma_prefetch_desc(&p.tmap_k);
             tma_prefetch_desc(&p.tmap_v);
             int issued = 0;
@@ -171,230 +186,274 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_
                     break;
             }
         }
-        return;
-    }
+        if (!InCluster) return;
+    } else if (active) {
+        // ---------------- consumer warps ----------------
+        const int g = lane >> 2;   // key row (S^T) / head column (B operand)
+        const int tq = lane & 3;
 
-    // ---------------- consumer warps ----------------
-    const int g = lane >> 2;   // key row (S^T) / head column (B operand)
-    const int tq = lane & 3;
-
-    // Q rows h_first .. h_first+nh-1 of sequence b (contiguous in global memory) to
-    // shared memory as fp32, one padded row per head.
-    {
-        const int tid = threadIdx.x;   // 0..127
-        const size_t esize = p.q_is_bf16 ? 2 : 4;
-        const uint8_t *qsrc = static_cast<const uint8_t *>(p.q) +
-                              (static_cast<long long>(b) * p.n_heads + h_first) * HD * esize;
-        const int nelem = nh * HD;
-        if (p.q_vec16) {
-            const int nvec = static_cast<int>(nelem * esize / 16);
-            uint4 buf[S::kQVecPerThread];
-#pragma unroll
-            for (int i = 0; i < S::kQVecPerThread; ++i) {
-                const int v = tid + i * kConsumerWarps * 32;
-                if (v < nvec) buf[i] = __ldg(reinterpret_cast<const uint4 *>(qsrc) + v);
-            }
-#pragma unroll
-            for (int i = 0; i < S::kQVecPerThread; ++i) {
-                const int v = tid + i * kConsumerWarps * 32;
-                if (v < nvec) {
-                    if (p.q_is_bf16) {
-                        const int e = v * 8, row = e / HD, col = e % HD;
-                        float *dst = qs + row * S::kQRowFloats + col;
-                        const uint32_t w[4] = {buf[i].x, buf[i].y, buf[i].z, buf[i].w};
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            dst[2 * j] = bf16lo_f32(w[j]);
-                            dst[2 * j + 1] = bf16hi_f32(w[j]);
+        // Q rows h_first .. h_first+nh-1 of sequence b (contiguous in global memory) to
+        // shared memory as fp32, one padded row per head.
+        {
+            const int tid = threadIdx.x;   // 0..127
+            const size_t esize = p.q_is_bf16 ? 2 : 4;
+            const uint8_t *qsrc = static_cast<const uint8_t *>(p.q) +
+                                  (static_cast<long long>(b) * p.n_heads + h_first) * HD * esize;
+            const int nelem = nh * HD;
+            if (p.q_vec16) {
+                const int nvec = static_cast<int>(nelem * esize / 16);
+                uint4 buf[S::kQVecPerThread];
+    #pragma unroll
+                for (int i = 0; i < S::kQVecPerThread; ++i) {
+                    const int v = tid + i * kConsumerWarps * 32;
+                    if (v < nvec) buf[i] = __ldg(reinterpret_cast<const uint4 *>(qsrc) + v);
+                }
+    #pragma unroll
+                for (int i = 0; i < S::kQVecPerThread; ++i) {
+                    const int v = tid + i * kConsumerWarps * 32;
+                    if (v < nvec) {
+                        if (p.q_is_bf16) {
+                            const int e = v * 8, row = e / HD, col = e % HD;
+                            float *dst = qs + row * S::kQRowFloats + col;
+                            const uint32_t w[4] = {buf[i].x, buf[i].y, buf[i].z, buf[i].w};
+    #pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                dst[2 * j] = bf16lo_f32(w[j]);
+                                dst[2 * j + 1] = bf16hi_f32(w[j]);
+                            }
+                        } else {
+                            const int e = v * 4, row = e / HD, col = e % HD;
+                            *reinterpret_cast<uint4 *>(qs + row * S::kQRowFloats + col) = buf[i];
                         }
-                    } else {
-                        const int e = v * 4, row = e / HD, col = e % HD;
-                        *reinterpret_cast<uint4 *>(qs + row * S::kQRowFloats + col) = buf[i];
+                    }
+                }
+            } else {
+                for (int e = tid; e < nelem; e += kConsumerWarps * 32) {
+                    const float x = p.q_is_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(qsrc)[e])
+                                                : reinterpret_cast<const float *>(qsrc)[e];
+                    qs[(e / HD) * S::kQRowFloats + e % HD] = x;
+                }
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+        }
+
+        // Q^T as B fragments (k = head dim, n = head g), bf16 hi (+ lo for fp32 Q).
+        uint32_t qhi[KSTEPS][2], qlo[KSTEPS][2];
+        {
+            const bool valid = g < nh;
+            const float *qrow = qs + (valid ? g : 0) * S::kQRowFloats;
+    #pragma unroll
+            for (int kk = 0; kk < KSTEPS; ++kk) {
+    #pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const int d = kk * 16 + half * 8 + tq * 2;
+                    const float2 v = *reinterpret_cast<const float2 *>(qrow + d);
+                    split_bf16x2(valid ? v.x : 0.f, valid ? v.y : 0.f, qhi[kk][half], qlo[kk][half]);
+                }
+            }
+        }
+        const bool use_lo = !p.q_is_bf16;
+
+        const float kLog2e = 1.4426950408889634f;
+        const float cap = p.softcap;
+        const float inv_cap = cap > 0.f ? 1.f / cap : 0.f;
+
+        float m_run[2] = {-INFINITY, -INFINITY};   // heads 2tq, 2tq+1 (warp-uniform per column)
+        float l_run[2] = {0.f, 0.f};                // this thread's keys only
+        float o[KSTEPS][4];
+    #pragma unroll
+        for (int i = 0; i < KSTEPS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+        bool ok = true;
+        int s = 0, phase = 0;
+        for (int t = 0; t < ntiles; ++t) {
+            if (!mbar_wait(smem_u32(&full_bar[s]), phase, p.err, kErrWaitTmaFull)) {
+                ok = false;
+                break;
+            }
+            const int kb = t * kKeysPerTile + warp * 16;   // first key of this warp's block
+            const int nv = nkeys - kb;                     // valid keys in the block (may be <=0 or >16)
+            if (nv > 0) {
+                const uint32_t kbase = smem_u32(smem + s * S::kStageBytes);
+                const uint32_t vbase = kbase + S::kTileBytes;
+
+                // ---- S^T = K . Q^T ----
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};
+                {
+                    const int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+    #pragma unroll
+                    for (int kk = 0; kk < KSTEPS; ++kk) {
+                        const int chunk = (kk & 3) * 2 + (lane >> 4);
+                        uint32_t a0, a1, a2, a3;
+                        ldsm_x4(kbase + (kk >> 2) * kSubtileBytes + sw128_offset(row, chunk), a0, a1, a2, a3);
+                        mma_bf16_16816(acc, a0, a1, a2, a3, qhi[kk][0], qhi[kk][1]);
+                        if (use_lo) mma_bf16_16816(acc, a0, a1, a2, a3, qlo[kk][0], qlo[kk][1]);
+                    }
+                }
+                // acc[0]=(key g, head 2tq) acc[1]=(key g, head 2tq+1) acc[2]=(key g+8, 2tq) acc[3]=(key g+8, 2tq+1)
+                float sc[4];
+    #pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float x = acc[i] * p.scale;
+                    if (cap > 0.f) x = cap * tanhf(x * inv_cap);
+                    const int key = g + (i >> 1) * 8;
+                    sc[i] = key < nv ? x : -INFINITY;
+                }
+                float mb0 = fmaxf(sc[0], sc[2]);
+                float mb1 = fmaxf(sc[1], sc[3]);
+    #pragma unroll
+                for (int off = 4; off < 32; off <<= 1) {
+                    mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, off));
+                    mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, off));
+                }
+                const float mn0 = fmaxf(m_run[0], mb0);
+                const float mn1 = fmaxf(m_run[1], mb1);
+                const float corr0 = fast_exp2((m_run[0] - mn0) * kLog2e);
+                const float corr1 = fast_exp2((m_run[1] - mn1) * kLog2e);
+                m_run[0] = mn0;
+                m_run[1] = mn1;
+                const float p0 = fast_exp2((sc[0] - mn0) * kLog2e);
+                const float p1 = fast_exp2((sc[1] - mn1) * kLog2e);
+                const float p2 = fast_exp2((sc[2] - mn0) * kLog2e);
+                const float p3 = fast_exp2((sc[3] - mn1) * kLog2e);
+                l_run[0] = l_run[0] * corr0 + p0 + p2;
+                l_run[1] = l_run[1] * corr1 + p1 + p3;
+    #pragma unroll
+                for (int i = 0; i < KSTEPS; ++i) {
+                    o[i][0] *= corr0;
+                    o[i][1] *= corr1;
+                    o[i][2] *= corr0;
+                    o[i][3] *= corr1;
+                }
+                const uint32_t pb0 = movmatrix_t(pack_f16x2(p0, p1));   // keys 0-7
+                const uint32_t pb1 = movmatrix_t(pack_f16x2(p2, p3));   // keys 8-15
+
+                // ---- O^T += V^T . P^T ----
+                {
+                    const int m = lane >> 3;
+                    const int row = warp * 16 + (lane & 7) + (m >> 1) * 8;
+                    const bool tail = nv < 16;
+                    const int k0 = 2 * tq, k1 = 2 * tq + 8;   // keys held in a0/a1 and a2/a3
+    #pragma unroll
+                    for (int db = 0; db < KSTEPS; ++db) {
+                        const int chunk = (db & 3) * 2 + (m & 1);
+                        uint32_t a0, a1, a2, a3;
+                        ldsm_x4_t(vbase + (db >> 2) * kSubtileBytes + sw128_offset(row, chunk), a0, a1, a2, a3);
+                        if (tail) {
+                            const uint32_t mlo = (k0 < nv ? 0x0000ffffu : 0u) | (k0 + 1 < nv ? 0xffff0000u : 0u);
+                            const uint32_t mhi = (k1 < nv ? 0x0000ffffu : 0u) | (k1 + 1 < nv ? 0xffff0000u : 0u);
+                            a0 &= mlo;
+                            a1 &= mlo;
+                            a2 &= mhi;
+                            a3 &= mhi;
+                        }
+                        mma_f16_16816(o[db], a0, a1, a2, a3, pb0, pb1);
                     }
                 }
             }
-        } else {
-            for (int e = tid; e < nelem; e += kConsumerWarps * 32) {
-                const float x = p.q_is_bf16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16 *>(qsrc)[e])
-                                            : reinterpret_cast<const float *>(qsrc)[e];
-                qs[(e / HD) * S::kQRowFloats + e % HD] = x;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
+            if (++s == stages) {
+                s = 0;
+                phase ^= 1;
+            }
+        }
+
+        // ---- merge the 4 consumer warps (stage buffers are free: every tile was consumed) ----
+        // Layout: per warp, per head column: [m, l] then O[hd].
+        float *red = reinterpret_cast<float *>(smem);
+        constexpr int kRowF = HD + 2;
+        asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+        {
+            // total l over the 8 key rows (lanes sharing tq)
+            float l0 = l_run[0], l1 = l_run[1];
+    #pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+                l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+            }
+            float *wbase = red + warp * 8 * kRowF;
+            if (g == 0) {
+                wbase[(2 * tq) * kRowF + 0] = m_run[0];
+                wbase[(2 * tq) * kRowF + 1] = l0;
+                wbase[(2 * tq + 1) * kRowF + 0] = m_run[1];
+                wbase[(2 * tq + 1) * kRowF + 1] = l1;
+            }
+    #pragma unroll
+            for (int db = 0; db < KSTEPS; ++db) {
+                const int d0 = db * 16 + g;
+                wbase[(2 * tq) * kRowF + 2 + d0] = o[db][0];
+                wbase[(2 * tq + 1) * kRowF + 2 + d0] = o[db][1];
+                wbase[(2 * tq) * kRowF + 2 + d0 + 8] = o[db][2];
+                wbase[(2 * tq + 1) * kRowF + 2 + d0 + 8] = o[db][3];
             }
         }
         asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-    }
-
-    // Q^T as B fragments (k = head dim, n = head g), bf16 hi (+ lo for fp32 Q).
-    uint32_t qhi[KSTEPS][2], qlo[KSTEPS][2];
-    {
-        const bool valid = g < nh;
-        const float *qrow = qs + (valid ? g : 0) * S::kQRowFloats;
-#pragma unroll
-        for (int kk = 0; kk < KSTEPS; ++kk) {
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                const int d = kk * 16 + half * 8 + tq * 2;
-                const float2 v = *reinterpret_cast<const float2 *>(qrow + d);
-                split_bf16x2(valid ? v.x : 0.f, valid ? v.y : 0.f, qhi[kk][half], qlo[kk][half]);
+        if (!InCluster && !ok) return;
+        for (int idx = threadIdx.x; idx < nh * HD; idx += kConsumerWarps * 32) {
+            const int h = idx / HD, d = idx % HD;
+            float M = -INFINITY;
+    #pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, red[(w * 8 + h) * kRowF]);
+            float acc = 0.f, lsum = 0.f;
+    #pragma unroll
+            for (int w = 0; w < kConsumerWarps; ++w) {
+                const float mw = red[(w * 8 + h) * kRowF];
+                const float f = mw == -INFINITY ? 0.f : fast_exp2((mw - M) * kLog2e);
+                acc += f * red[(w * 8 + h) * kRowF + 2 + d];
+                lsum += f * red[(w * 8 + h) * kRowF + 1];
             }
-        }
-    }
-    const bool use_lo = !p.q_is_bf16;
-
-    const float kLog2e = 1.4426950408889634f;
-    const float cap = p.softcap;
-    const float inv_cap = cap > 0.f ? 1.f / cap : 0.f;
-
-    float m_run[2] = {-INFINITY, -INFINITY};   // heads 2tq, 2tq+1 (warp-uniform per column)
-    float l_run[2] = {0.f, 0.f};                // this thread's keys only
-    float o[KSTEPS][4];
-#pragma unroll
-    for (int i = 0; i < KSTEPS; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-
-    bool ok = true;
-    int s = 0, phase = 0;
-    for (int t = 0; t < ntiles; ++t) {
-        if (!mbar_wait(smem_u32(&full_bar[s]), phase, p.err, kErrWaitTmaFull)) {
-            ok = false;
-            break;
-        }
-        const int kb = t * kKeysPerTile + warp * 16;   // first key of this warp's block
-        const int nv = nkeys - kb;                     // valid keys in the block (may be <=0 or >16)
-        if (nv > 0) {
-            const uint32_t kbase = smem_u32(smem + s * S::kStageBytes);
-            const uint32_t vbase = kbase + S::kTileBytes;
-
-            // ---- S^T = K . Q^T ----
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            {
-                const int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-#pragma unroll
-                for (int kk = 0; kk < KSTEPS; ++kk) {
-                    const int chunk = (kk & 3) * 2 + (lane >> 4);
-                    uint32_t a0, a1, a2, a3;
-                    ldsm_x4(kbase + (kk >> 2) * kSubtileBytes + sw128_offset(row, chunk), a0, a1, a2, a3);
-                    mma_bf16_16816(acc, a0, a1, a2, a3, qhi[kk][0], qhi[kk][1]);
-                    if (use_lo) mma_bf16_16816(acc, a0, a1, a2, a3, qlo[kk][0], qlo[kk][1]);
+            if constexpr (InCluster) {
+                float *cp = reinterpret_cast<float *>(smem + S::kCpartOff) + h * (HD + 2);
+                cp[2 + d] = acc;
+                if (d == 0) {
+                    cp[0] = M;
+                    cp[1] = lsum;
                 }
-            }
-            // acc[0]=(key g, head 2tq) acc[1]=(key g, head 2tq+1) acc[2]=(key g+8, 2tq) acc[3]=(key g+8, 2tq+1)
-            float sc[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float x = acc[i] * p.scale;
-                if (cap > 0.f) x = cap * tanhf(x * inv_cap);
-                const int key = g + (i >> 1) * 8;
-                sc[i] = key < nv ? x : -INFINITY;
-            }
-            float mb0 = fmaxf(sc[0], sc[2]);
-            float mb1 = fmaxf(sc[1], sc[3]);
-#pragma unroll
-            for (int off = 4; off < 32; off <<= 1) {
-                mb0 = fmaxf(mb0, __shfl_xor_sync(0xffffffffu, mb0, off));
-                mb1 = fmaxf(mb1, __shfl_xor_sync(0xffffffffu, mb1, off));
-            }
-            const float mn0 = fmaxf(m_run[0], mb0);
-            const float mn1 = fmaxf(m_run[1], mb1);
-            const float corr0 = fast_exp2((m_run[0] - mn0) * kLog2e);
-            const float corr1 = fast_exp2((m_run[1] - mn1) * kLog2e);
-            m_run[0] = mn0;
-            m_run[1] = mn1;
-            const float p0 = fast_exp2((sc[0] - mn0) * kLog2e);
-            const float p1 = fast_exp2((sc[1] - mn1) * kLog2e);
-            const float p2 = fast_exp2((sc[2] - mn0) * kLog2e);
-            const float p3 = fast_exp2((sc[3] - mn1) * kLog2e);
-            l_run[0] = l_run[0] * corr0 + p0 + p2;
-            l_run[1] = l_run[1] * corr1 + p1 + p3;
-#pragma unroll
-            for (int i = 0; i < KSTEPS; ++i) {
-                o[i][0] *= corr0;
-                o[i][1] *= corr1;
-                o[i][2] *= corr0;
-                o[i][3] *= corr1;
-            }
-            const uint32_t pb0 = movmatrix_t(pack_f16x2(p0, p1));   // keys 0-7
-            const uint32_t pb1 = movmatrix_t(pack_f16x2(p2, p3));   // keys 8-15
-
-            // ---- O^T += V^T . P^T ----
-            {
-                const int m = lane >> 3;
-                const int row = warp * 16 + (lane & 7) + (m >> 1) * 8;
-                const bool tail = nv < 16;
-                const int k0 = 2 * tq, k1 = 2 * tq + 8;   // keys held in a0/a1 and a2/a3
-#pragma unroll
-                for (int db = 0; db < KSTEPS; ++db) {
-                    const int chunk = (db & 3) * 2 + (m & 1);
-                    uint32_t a0, a1, a2, a3;
-                    ldsm_x4_t(vbase + (db >> 2) * kSubtileBytes + sw128_offset(row, chunk), a0, a1, a2, a3);
-                    if (tail) {
-                        const uint32_t mlo = (k0 < nv ? 0x0000ffffu : 0u) | (k0 + 1 < nv ? 0xffff0000u : 0u);
-                        const uint32_t mhi = (k1 < nv ? 0x0000ffffu : 0u) | (k1 + 1 < nv ? 0xffff0000u : 0u);
-                        a0 &= mlo;
-                        a1 &= mlo;
-                        a2 &= mhi;
-                        a3 &= mhi;
-                    }
-                    mma_f16_16816(o[db], a0, a1, a2, a3, pb0, pb1);
+            } else {
+                const long long item = (static_cast<long long>(b) * p.n_heads + h_first + h) * p.max_chunks + c;
+                p.part_o[item * HD + d] = acc;
+                if (d == 0) {
+                    p.part_ml[item * 2 + 0] = M;
+                    p.part_ml[item * 2 + 1] = lsum;
                 }
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&empty_bar[s]));
-        if (++s == stages) {
-            s = 0;
-            phase ^= 1;
-        }
+    } else {
+        // idle chunk of a cluster (InCluster only): an empty partial
+        float *cp = reinterpret_cast<float *>(smem + S::kCpartOff);
+        for (int idx = threadIdx.x; idx < 8 * (HD + 2); idx += kConsumerWarps * 32)
+            cp[idx] = (idx % (HD + 2)) == 0 ? -INFINITY : 0.f;
     }
 
-    // ---- merge the 4 consumer warps (stage buffers are free: every tile was consumed) ----
-    // Layout: per warp, per head column: [m, l] then O[hd].
-    float *red = reinterpret_cast<float *>(smem);
-    constexpr int kRowF = HD + 2;
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-    {
-        // total l over the 8 key rows (lanes sharing tq)
-        float l0 = l_run[0], l1 = l_run[1];
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-            l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-            l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    if constexpr (InCluster) {
+        // ---- merge the chunks of this cluster; CTA rank r takes elements r, r+C, ... ----
+        cluster_sync_all();
+        const int C = static_cast<int>(gridDim.x);   // cluster size = chunks
+        int nact = n > 0 ? (n + p.chunk - 1) / p.chunk : 0;
+        if ((L - ks) > p.max_chunks * p.chunk) {
+            if (c == 0 && threadIdx.x == 0) atomicOr(p.err, kErrBadArgs);
+            nact = p.max_chunks;
         }
-        float *wbase = red + warp * 8 * kRowF;
-        if (g == 0) {
-            wbase[(2 * tq) * kRowF + 0] = m_run[0];
-            wbase[(2 * tq) * kRowF + 1] = l0;
-            wbase[(2 * tq + 1) * kRowF + 0] = m_run[1];
-            wbase[(2 * tq + 1) * kRowF + 1] = l1;
+        const uint32_t cp0 = smem_u32(smem + S::kCpartOff);
+        const float kLog2e = 1.4426950408889634f;
+        for (int e = c * kThreads + threadIdx.x; e < nh * HD; e += C * kThreads) {
+            const int h = e / HD, d = e % HD;
+            const uint32_t hoff = static_cast<uint32_t>(h * (HD + 2)) * 4u;
+            float M = -INFINITY;
+            for (int r = 0; r < nact; ++r)
+                M = fmaxf(M, ld_shared_cluster_f32(map_shared_rank(cp0 + hoff, r)));
+            float acc = 0.f, lsum = 0.f;
+            for (int r = 0; r < nact; ++r) {
+                const uint32_t base = map_shared_rank(cp0 + hoff, r);
+                const float mr = ld_shared_cluster_f32(base);
+                const float f = mr == -INFINITY ? 0.f : fast_exp2((mr - M) * kLog2e);
+                lsum += f * ld_shared_cluster_f32(base + 4);
+                acc += f * ld_shared_cluster_f32(base + 8 + 4 * d);
+            }
+            p.out[(static_cast<long long>(b) * p.n_heads + h_first + h) * HD + d] = lsum > 0.f ? acc / lsum : 0.f;
         }
-#pragma unroll
-        for (int db = 0; db < KSTEPS; ++db) {
-            const int d0 = db * 16 + g;
-            wbase[(2 * tq) * kRowF + 2 + d0] = o[db][0];
-            wbase[(2 * tq + 1) * kRowF + 2 + d0] = o[db][1];
-            wbase[(2 * tq) * kRowF + 2 + d0 + 8] = o[db][2];
-            wbase[(2 * tq + 1) * kRowF + 2 + d0 + 8] = o[db][3];
-        }
-    }
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
-    if (!ok) return;
-    for (int idx = threadIdx.x; idx < nh * HD; idx += kConsumerWarps * 32) {
-        const int h = idx / HD, d = idx % HD;
-        float M = -INFINITY;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, red[(w * 8 + h) * kRowF]);
-        float acc = 0.f, lsum = 0.f;
-#pragma unroll
-        for (int w = 0; w < kConsumerWarps; ++w) {
-            const float mw = red[(w * 8 + h) * kRowF];
-            const float f = mw == -INFINITY ? 0.f : fast_exp2((mw - M) * kLog2e);
-            acc += f * red[(w * 8 + h) * kRowF + 2 + d];
-            lsum += f * red[(w * 8 + h) * kRowF + 1];
-        }
-        const long long item = (static_cast<long long>(b) * p.n_heads + h_first + h) * p.max_chunks + c;
-        p.part_o[item * HD + d] = acc;
-        if (d == 0) {
-            p.part_ml[item * 2 + 0] = M;
-            p.part_ml[item * 2 + 1] = lsum;
-        }
+        cluster_sync_all();
     }
 }
 
@@ -431,6 +490,11 @@ __global__ void decode_combine_kernel(float *__restrict__ out, const float *__re
 #ifndef SMOL_DECODE_MAX_CHUNK
 #define SMOL_DECODE_MAX_CHUNK 2048
 #endif
+// SMOL_DECODE_CLUSTER=0 in the environment forces the two-kernel form (measurement knob).
+const bool g_decode_cluster = [] {
+    const char *e = getenv("SMOL_DECODE_CLUSTER");
+    return !(e && e[0] == '0');
+}();
 int decode_chunk_size(int n_seqs, int max_kv_len, int n_kv_heads, int n_qgroups)
 {
     const long long work = static_cast<long long>(n_seqs) * n_kv_heads * n_qgroups * (max_kv_len > 0 ? max_kv_len : 1);
@@ -441,9 +505,9 @@ int decode_chunk_size(int n_seqs, int max_kv_len, int n_kv_heads, int n_qgroups)
     return static_cast<int>(c);
 }
 
-// Raise the dynamic shared-memory limit of decode_split_kernel<HD> on the current
-// device, once per device (the attribute is per function and device).
-template <int HD>
+// Raise the dynamic shared-memory limit of decode_split_kernel<HD, InCluster> on the
+// current device, once per device (the attribute is per function and device).
+template <int HD, bool InCluster>
 bool ensure_split_smem_attr()
 {
     static std::mutex mu;
@@ -455,7 +519,7 @@ bool ensure_split_smem_attr()
     }
     std::lock_guard<std::mutex> lock(mu);
     if (!done[dev]) {
-        if (cudaFuncSetAttribute(decode_split_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(decode_split_kernel<HD, InCluster>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(DecodeShape<HD>::smem_bytes(DecodeShape<HD>::kMaxStages))) !=
             cudaSuccess) {
             cudaGetLastError();
@@ -466,17 +530,89 @@ bool ensure_split_smem_attr()
     return true;
 }
 
-// Completes p (ring depth, Q load width) and launches the split and combine kernels.
+int device_sm_count()
+{
+    static int cached[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (!cached[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+// Cluster form when the whole grid fits one wave with at most 8 chunks per
+// (sequence, KV head, Q-head group): the smallest chunk (multiple of 64 keys) that
+// satisfies both, i.e. the most CTAs that still run at once.  Returns the chunk, or 0
+// for the two-kernel form.
 template <int HD>
-int launch_split_combine(cudaStream_t st, DecodeParams &p, float *out, int n_seqs)
+int cluster_chunk(int units, int max_kv_len)
 {
     using S = DecodeShape<HD>;
+    const int sms = device_sm_count();
+    if (sms <= 0 || max_kv_len <= 0 || units <= 0) return 0;
+    constexpr size_t kSmPerSm = 228 * 1024;   // shared memory per SM on sm_100
+    for (int chunk = kKeysPerTile; chunk <= SMOL_DECODE_MAX_CHUNK; chunk += kKeysPerTile) {
+        const int nch = (max_kv_len + chunk - 1) / chunk;
+        if (nch > 8) continue;
+        const int tiles = chunk / kKeysPerTile;
+        const int stages = tiles < S::kMaxStages ? tiles : S::kMaxStages;
+        size_t per_sm = kSmPerSm / (S::smem_bytes(stages) + 1024);
+        if (per_sm > 2) per_sm = 2;   // __launch_bounds__(kThreads, 2)
+        if (static_cast<long long>(units) * nch <= static_cast<long long>(sms) * static_cast<long long>(per_sm))
+            return chunk;
+    }
+    return 0;
+}
+
+// Completes p (ring depth, Q load width) and launches the split and merge: one
+// cluster kernel for single-wave problems, else the split kernel and the combine
+// kernel over the partials in the workspace.
+template <int HD>
+int launch_split_combine(cudaStream_t st, DecodeParams &p, float *out, int n_seqs, int max_kv_len)
+{
+    using S = DecodeShape<HD>;
+    p.out = out;
+    p.q_vec16 = (reinterpret_cast<uintptr_t>(p.q) & 15) == 0;
+    const int units = n_seqs * p.n_kv_heads * p.n_qgroups;
+    const int cchunk = g_decode_cluster ? cluster_chunk<HD>(units, max_kv_len) : 0;
+    if (cchunk > 0) {
+        p.chunk = cchunk;
+        p.max_chunks = (max_kv_len + cchunk - 1) / cchunk;
+        const int tiles = cchunk / kKeysPerTile;
+        p.stages = tiles < S::kMaxStages ? tiles : S::kMaxStages;
+        if (!ensure_split_smem_attr<HD, true>()) return SMOL_B200_ERR_CUDA;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(p.max_chunks, p.n_kv_heads * p.n_qgroups, n_seqs);
+        cfg.blockDim = dim3(kThreads, 1, 1);
+        cfg.dynamicSmemBytes = S::smem_bytes(p.stages);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = p.max_chunks;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaLaunchKernelEx(&cfg, decode_split_kernel<HD, true>, p) != cudaSuccess) {
+            cudaGetLastError();
+            return SMOL_B200_ERR_CUDA;
+        }
+        return SMOL_B200_OK;
+    }
     const int tiles = (p.chunk + kKeysPerTile - 1) / kKeysPerTile;   // most tiles one CTA streams
     p.stages = tiles < S::kMaxStages ? tiles : S::kMaxStages;
-    p.q_vec16 = (reinterpret_cast<uintptr_t>(p.q) & 15) == 0;
-    if (!ensure_split_smem_attr<HD>()) return SMOL_B200_ERR_CUDA;
+    if (!ensure_split_smem_attr<HD, false>()) return SMOL_B200_ERR_CUDA;
     dim3 grid(p.max_chunks, p.n_kv_heads * p.n_qgroups, n_seqs);
-    decode_split_kernel<HD><<<grid, kThreads, S::smem_bytes(p.stages), st>>>(p);
+    decode_split_kernel<HD, false><<<grid, kThreads, S::smem_bytes(p.stages), st>>>(p);
     dim3 cgrid(p.n_heads, n_seqs);
     decode_combine_kernel<HD><<<cgrid, HD, 0, st>>>(out, p.part_o, p.part_ml, p.kv_len, p.n_heads, p.chunk,
                                                    p.max_chunks, p.window, p.err);
@@ -516,7 +652,7 @@ int launch_decode(cudaStream_t st, float *out, const void *q, int q_is_bf16, con
     p.scale = scale;
     p.softcap = softcap;
 
-    return launch_split_combine<HD>(st, p, out, n_seqs);
+    return launch_split_combine<HD>(st, p, out, n_seqs, max_kv_len);
 }
 
 }  // namespace
@@ -653,7 +789,7 @@ int launch_decode_noalloc(cudaStream_t st, int dev, uint8_t *scratch, float *out
     p.scale = scale;
     p.softcap = softcap;
     (void)dev;
-    return launch_split_combine<HD>(st, p, out, n_seqs);
+    return launch_split_combine<HD>(st, p, out, n_seqs, max_kv_len);
 }
 
 }  // namespace
