@@ -232,6 +232,75 @@ SMOL_B200_API int smol_b200_decode_step_host(
     int64_t pool_rows, const int64_t *seq_row0, const int *kv_len, int max_kv_len,
     float scale, void *scratch, size_t scratch_bytes);
 
+/* ===========================================================================
+ * Part 4 -- device-resident decoder step (Qwen3-style qkn_decoder).
+ *
+ * One greedy token for each of n_seqs sequences, entirely on the device: the whole of
+ * qkn_decoder_forward (qkn_decoder.c:570-714) for the configuration with per-head
+ * QK-RMSNorm, SwiGLU MLP and tied embeddings -- embedding lookup, per layer input
+ * RMSNorm, Q/K/V projections, QK-norm + RoPE + cache append, attention over the
+ * pooled cache, output projection + residual, post-attention RMSNorm, fused
+ * gate/up projection with SiLU(gate)*up, down projection + residual; final RMSNorm
+ * and the greedy argmax over the tied embedding matrix (smol_argmax_matvec_bf16,
+ * matmul.c:371-398: the lowest index among equal maxima).  Weights use the
+ * reference's layouts: bf16 [out][in] matrices, gate/up rows interleaved
+ * (qkn_decoder.c:140-154), fp32 norm weights.  Projections compute in fp32 from the
+ * bf16 weights (bf16_matvec_fused); the cache holds K bf16 / V fp16 as in Part 3.
+ * Every pointer below is device memory except `layers` (a host array).  The step is
+ * asynchronous on `stream` and allocation-free, so a decode loop can be captured
+ * once in a CUDA graph and replayed.
+ * =========================================================================== */
+typedef struct smol_b200_qkn_layer {
+    const uint16_t *wq;              /* [n_heads*head_dim][hidden]           */
+    const uint16_t *wk, *wv;         /* [n_kv_heads*head_dim][hidden]        */
+    const uint16_t *wo;              /* [hidden][n_heads*head_dim]           */
+    const uint16_t *gate_up;         /* [2*intermediate][hidden], interleaved */
+    const uint16_t *down;            /* [hidden][intermediate]              */
+    const float *input_norm, *post_attn_norm;   /* [hidden]   */
+    const float *q_norm, *k_norm;               /* [head_dim] */
+} smol_b200_qkn_layer;
+
+typedef struct smol_b200_qkn_model {
+    int hidden, n_layers, n_heads, n_kv_heads, head_dim, intermediate, vocab;
+    float eps;                        /* RMSNorm epsilon (all norms)            */
+    int rope_interleaved;             /* 0: NeoX halves, 1: interleaved pairs  */
+    const uint16_t *tok_embeddings;   /* [vocab][hidden] bf16, also the lm_head */
+    const float *final_norm;          /* [hidden]                               */
+    const smol_b200_qkn_layer *layers;   /* host array of n_layers              */
+} smol_b200_qkn_model;
+
+/* Device workspace one step needs for n_seqs sequences of at most max_kv_len cached
+ * tokens (before the step). */
+SMOL_B200_API size_t smol_b200_qkn_step_workspace_bytes(const smol_b200_qkn_model *model, int n_seqs,
+                                                        int max_kv_len);
+
+/* tokens_in[b]: the token each sequence feeds (may alias tokens_out).
+ * layer_row0[l*n_seqs + b]: pool row of position 0 of sequence b in layer l.
+ * kv_len[b]: tokens already cached; the new token goes to position / row offset
+ * kv_len[b] and attention covers [0, kv_len[b]+1).  advance != 0 increments kv_len
+ * on the device at the end of the step (so a captured step replays as a loop).
+ * rope_cos / rope_sin: [>= max_kv_len+1][head_dim] tables (row = position).
+ * tokens_out[b]: the greedy next token. */
+SMOL_B200_API int smol_b200_qkn_decode_step(
+    void *stream, const smol_b200_qkn_model *model, int n_seqs, const int *tokens_in,
+    int *tokens_out, uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows,
+    const int64_t *layer_row0, int *kv_len, int max_kv_len, const float *rope_cos,
+    const float *rope_sin, int advance, void *workspace, size_t workspace_bytes);
+
+/* The building blocks of the step, for callers that orchestrate their own decoder:
+ *   y[b][n] (+)= sum_k x[b][k] * W[n][k]    mode 0: store, 1: add into y (residual),
+ *   2: SiLU-gated pairs, y[b][r] = silu(s[2r]) * s[2r+1] over W's 2*n_out rows
+ *   (smol_swiglu_multiply, activation.c:55-86), n_out = rows of y.
+ * W bf16 [rows][k_dim] with k_dim a multiple of 8 and 16-byte aligned rows.
+ * x fp32 with row stride ldx (multiple of 4), y fp32 with row stride ldy. */
+SMOL_B200_API int smol_b200_gemv_bf16(void *stream, float *y, int64_t ldy, const float *x, int64_t ldx,
+                                      const uint16_t *w, int n_out, int k_dim, int n_seqs, int mode);
+/* tokens_out[b] = argmax_v sum_k x[b][k] * E[v][k] (lowest v among equal maxima). */
+SMOL_B200_API int smol_b200_argmax_bf16(void *stream, int *tokens_out, const float *x, int64_t ldx,
+                                        const uint16_t *emb, int vocab, int k_dim, int n_seqs,
+                                        void *workspace, size_t workspace_bytes);
+SMOL_B200_API size_t smol_b200_argmax_workspace_bytes(int n_seqs);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,119 @@
+"""CPU restatement of the reference decoder step -- TEST INFRASTRUCTURE ONLY.
+
+numpy (fp32) restatement of qkn_decoder_prefill (qkn_decoder.c:369-564) and
+qkn_decoder_forward (qkn_decoder.c:570-714) for the Qwen3 configuration the device
+decoder step implements: per-head QK-RMSNorm, NeoX RoPE, no softcap or sliding
+window, SwiGLU MLP with interleaved gate/up rows, tied embeddings, greedy argmax.
+The attention, QK-norm, RoPE and cache append go through the C restatement
+(pyoracle: smol_oracle.c) over a cache that holds the device formats (K bf16, V
+fp16), so both sides attend over identical values.  Weights are bf16 (kept as the
+rounded fp32 values and as the raw bits to upload).
+
+Only tests/ import this module.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+import pyoracle
+
+
+def rms_norm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """smol_rms_norm (rmsnorm.c:17-70): (x * w) * 1/sqrtf(mean(x^2) + eps), per row."""
+    ss = np.sum(x.astype(np.float32) ** 2, axis=-1, keepdims=True, dtype=np.float32)
+    inv = (np.float32(1.0) / np.sqrt(ss / np.float32(x.shape[-1]) + np.float32(eps))).astype(np.float32)
+    return ((x * w).astype(np.float32) * inv).astype(np.float32)
+
+
+def swiglu(gate_up: np.ndarray) -> np.ndarray:
+    """smol_swiglu_multiply (activation.c:55-86): silu(g[2j]) * g[2j+1]."""
+    g = gate_up[..., 0::2]
+    u = gate_up[..., 1::2]
+    return ((g / (np.float32(1.0) + np.exp(-g, dtype=np.float32))) * u).astype(np.float32)
+
+
+def argmax_first(logits: np.ndarray) -> int:
+    """smol_argmax_matvec_bf16 (matmul.c:371-398): the lowest index among equal maxima."""
+    return int(np.argmax(logits))
+
+
+class QknOracle:
+    """A seeded Qwen3-shaped model and its reference forward passes."""
+
+    def __init__(self, hidden=1024, layers=2, n_heads=16, n_kv_heads=8, head_dim=128, intermediate=3072,
+                 vocab=4096, theta=1e6, eps=1e-6, qk_gain=3.0, vo_gain=4.0, seed=0, cap=1024):
+        rng = np.random.default_rng(seed)
+        self.H, self.L, self.HQ, self.HKV, self.HD = hidden, layers, n_heads, n_kv_heads, head_dim
+        self.I, self.V, self.eps, self.cap = intermediate, vocab, eps, cap
+        qd, kvd = n_heads * head_dim, n_kv_heads * head_dim
+
+        def bf(*shape, sc=1.0):
+            return pyoracle.round_bf16((rng.standard_normal(shape) * sc).astype(np.float32))
+
+        def near(n, mean, sd=0.02):
+            return (mean + sd * rng.standard_normal(n)).astype(np.float32)
+
+        self.E = bf(vocab, hidden)
+        self.final_norm = near(hidden, 1.0)
+        self.layers = []
+        for _ in range(layers):
+            self.layers.append({
+                "wq": bf(qd, hidden, sc=1 / np.sqrt(hidden)),
+                "wk": bf(kvd, hidden, sc=1 / np.sqrt(hidden)),
+                "wv": bf(kvd, hidden, sc=vo_gain / np.sqrt(hidden)),
+                "wo": bf(hidden, qd, sc=vo_gain / np.sqrt(qd)),
+                "gate_up": bf(2 * intermediate, hidden, sc=1 / np.sqrt(hidden)),
+                "down": bf(hidden, intermediate, sc=1 / np.sqrt(intermediate)),
+                "input_norm": near(hidden, 1.0),
+                "post_attn_norm": near(hidden, 1.0),
+                "q_norm": near(head_dim, qk_gain),
+                "k_norm": near(head_dim, qk_gain),
+            })
+        self.cos, self.sin = pyoracle.fill_rope_table(cap, head_dim, theta)
+        self.kc = [np.zeros((cap, kvd), np.uint16) for _ in range(layers)]   # bf16 bits
+        self.vc = [np.zeros((cap, kvd), np.uint16) for _ in range(layers)]   # fp16 bits
+        self.len = 0
+        self.o = pyoracle.oracle()
+        self.scale = np.float32(1.0 / np.sqrt(np.float32(head_dim)))
+
+    def _layer(self, l: int, x: np.ndarray, pos0: int) -> np.ndarray:
+        """One decoder layer over tokens at positions pos0.. (qkn_decoder.c:431-563 / :622-705)."""
+        lw, n = self.layers[l], x.shape[0]
+        xn = rms_norm(x, lw["input_norm"], self.eps)
+        q, k, v = xn @ lw["wq"].T, xn @ lw["wk"].T, xn @ lw["wv"].T
+        pos = np.arange(pos0, pos0 + n, dtype=np.int32)
+        q_rot = pyoracle.qknorm_rope_append(q, k, v, self.HQ, self.HKV, self.HD, lw["q_norm"], lw["k_norm"], self.eps,
+                                            self.cos, self.sin, False, pos, pos.astype(np.int64), self.kc[l],
+                                            self.vc[l])
+        total = pos0 + n
+        K = pyoracle.bf16_to_f32(self.kc[l][:total])
+        Vv = self.vc[l][:total].view(np.float16).astype(np.float32)
+        attn = self.o.causal_attention(q_rot, K, Vv, n, total, self.HQ, self.HKV, self.HD, self.scale, pos0)
+        x = (x + attn @ lw["wo"].T).astype(np.float32)
+        xn = rms_norm(x, lw["post_attn_norm"], self.eps)
+        act = swiglu(xn @ lw["gate_up"].T)
+        return (x + act @ lw["down"].T).astype(np.float32)
+
+    def prefill(self, tokens) -> None:
+        """qkn_decoder_prefill over `tokens` (no logits, as the reference)."""
+        x = self.E[np.asarray(tokens)].astype(np.float32)
+        for l in range(self.L):
+            x = self._layer(l, x, self.len)
+        self.len += len(tokens)
+
+    def forward(self, token: int) -> tuple[int, float, np.ndarray]:
+        """qkn_decoder_forward for one token: (greedy token, top-1/top-2 margin, final normed x)."""
+        x = self.E[[token]].astype(np.float32)
+        for l in range(self.L):
+            x = self._layer(l, x, self.len)
+        self.len += 1
+        xf = rms_norm(x, self.final_norm, self.eps)[0]
+        logits = self.E @ xf
+        top = np.argsort(logits)[-2:]
+        return argmax_first(logits), float(logits[top[1]] - logits[top[0]]), xf
+
+    def device_weights(self, to_device):
+        """Upload helper: to_device(np array) -> device tensor; bf16 matrices go as raw bits."""
+        bits = lambda a: to_device(pyoracle.bf16_bits(a))   # noqa: E731
+        layers = [{name: (bits(w) if w.ndim == 2 else to_device(w)) for name, w in lw.items()} for lw in self.layers]
+        return bits(self.E), to_device(self.final_norm), layers

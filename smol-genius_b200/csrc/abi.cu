@@ -543,4 +543,43 @@ int smol_b200_decode_step_host(void *stream, float *out_host, const float *q_hos
     return SMOL_B200_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Part 4
+// ---------------------------------------------------------------------------
+size_t smol_b200_qkn_step_workspace_bytes(const smol_b200_qkn_model *model, int n_seqs, int max_kv_len)
+{
+    return qkn_step_workspace_bytes(model, n_seqs, max_kv_len);
+}
+
+int smol_b200_qkn_decode_step(void *stream, const smol_b200_qkn_model *model, int n_seqs, const int *tokens_in,
+                              int *tokens_out, uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows,
+                              const int64_t *layer_row0, int *kv_len, int max_kv_len, const float *rope_cos,
+                              const float *rope_sin, int advance, void *workspace, size_t workspace_bytes)
+{
+    return record(qkn_decode_step(static_cast<cudaStream_t>(stream), model, n_seqs, tokens_in, tokens_out, k_pool,
+                                  v_pool, pool_rows, layer_row0, kv_len, max_kv_len, rope_cos, rope_sin, advance,
+                                  workspace, workspace_bytes),
+                  "smol_b200_qkn_decode_step");
+}
+
+int smol_b200_gemv_bf16(void *stream, float *y, int64_t ldy, const float *x, int64_t ldx, const uint16_t *w,
+                        int n_out, int k_dim, int n_seqs, int mode)
+{
+    return record(gemv_bf16(static_cast<cudaStream_t>(stream), y, ldy, x, ldx, w, n_out, k_dim, n_seqs, mode),
+                  "smol_b200_gemv_bf16");
+}
+
+int smol_b200_argmax_bf16(void *stream, int *tokens_out, const float *x, int64_t ldx, const uint16_t *emb,
+                          int vocab, int k_dim, int n_seqs, void *workspace, size_t workspace_bytes)
+{
+    return record(argmax_bf16(static_cast<cudaStream_t>(stream), tokens_out, x, ldx, emb, vocab, k_dim, n_seqs,
+                              workspace, workspace_bytes),
+                  "smol_b200_argmax_bf16");
+}
+
+size_t smol_b200_argmax_workspace_bytes(int n_seqs)
+{
+    return argmax_workspace_bytes(n_seqs);
+}
+
 }  // extern "C"

@@ -78,6 +78,18 @@ int launch_unpack_rows(cudaStream_t st, float *dst, int64_t dst_stride, const fl
 // Bounded-wait self test: one kernel whose wait can never succeed (see rope_norm.cu).
 int launch_watchdog_selftest(cudaStream_t st);
 
+// decoder.cu: the device-resident decode step (Part 4 of smol_b200.h)
+int gemv_bf16(cudaStream_t st, float *y, int64_t ldy, const float *x, int64_t ldx, const uint16_t *w, int n_out,
+              int k_dim, int n_seqs, int mode);
+int argmax_bf16(cudaStream_t st, int *tokens_out, const float *x, int64_t ldx, const uint16_t *emb, int vocab,
+                int k_dim, int n_seqs, void *ws, size_t ws_bytes);
+size_t argmax_workspace_bytes(int n_seqs);
+size_t qkn_step_workspace_bytes(const smol_b200_qkn_model *m, int n_seqs, int max_kv_len);
+int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *m, int n_seqs, const int *tokens_in,
+                    int *tokens_out, uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows,
+                    const int64_t *layer_row0, int *kv_len, int max_kv_len, const float *rope_cos,
+                    const float *rope_sin, int advance, void *workspace, size_t workspace_bytes);
+
 int launch_decode_step_index(cudaStream_t st, int *positions, int64_t *slots, int *kv_len_next,
                              const int64_t *seq_row0, const int *kv_len, int n_seqs);
 

@@ -80,6 +80,16 @@ _SIGNATURES = {
         _c_int, [_c_void, _c_void, _c_void, _c_void, _c_void, _c_int, _c_int, _c_int, _c_int, _c_void, _c_void,
                  _c_float, _c_void, _c_void, _c_int, _c_void, _c_void, _c_i64, _c_void, _c_void, _c_int, _c_float,
                  _c_void, _c_size]),
+    # Part 4 (device-resident decoder step)
+    "smol_b200_qkn_step_workspace_bytes": (_c_size, [_c_void, _c_int, _c_int]),
+    "smol_b200_qkn_decode_step": (
+        _c_int, [_c_void, _c_void, _c_int, _c_void, _c_void, _c_void, _c_void, _c_i64, _c_void, _c_void, _c_int,
+                 _c_void, _c_void, _c_int, _c_void, _c_size]),
+    "smol_b200_gemv_bf16": (_c_int, [_c_void, _c_void, _c_i64, _c_void, _c_i64, _c_void, _c_int, _c_int, _c_int,
+                                     _c_int]),
+    "smol_b200_argmax_bf16": (_c_int, [_c_void, _c_void, _c_void, _c_i64, _c_void, _c_int, _c_int, _c_int, _c_void,
+                                       _c_size]),
+    "smol_b200_argmax_workspace_bytes": (_c_size, [_c_int]),
 }
 
 
@@ -269,3 +279,63 @@ def decode_step_host(out_host, q_host, k_host, v_host, n_seqs, n_heads, n_kv_hea
         _ptr(k_pool), _ptr(v_pool), pool_rows, _ptr(seq_row0), _ptr(kv_len), max_kv_len, scale, _ptr(scratch),
         scratch.numel() * scratch.element_size())
     check(rc, "smol_b200_decode_step_host")
+
+
+# ---------------------------------------------------------------------------
+# Part 4: device-resident decoder step
+# ---------------------------------------------------------------------------
+class QknLayer(ctypes.Structure):
+    """smol_b200_qkn_layer: device pointers of one layer's weights."""
+    _fields_ = [("wq", ctypes.c_void_p), ("wk", ctypes.c_void_p), ("wv", ctypes.c_void_p), ("wo", ctypes.c_void_p),
+                ("gate_up", ctypes.c_void_p), ("down", ctypes.c_void_p), ("input_norm", ctypes.c_void_p),
+                ("post_attn_norm", ctypes.c_void_p), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p)]
+
+
+class QknModel(ctypes.Structure):
+    """smol_b200_qkn_model (the layers array stays referenced by the Python object)."""
+    _fields_ = [("hidden", ctypes.c_int), ("n_layers", ctypes.c_int), ("n_heads", ctypes.c_int),
+                ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("intermediate", ctypes.c_int),
+                ("vocab", ctypes.c_int), ("eps", ctypes.c_float), ("rope_interleaved", ctypes.c_int),
+                ("tok_embeddings", ctypes.c_void_p), ("final_norm", ctypes.c_void_p),
+                ("layers", ctypes.POINTER(QknLayer))]
+
+
+def qkn_model(hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab, eps, tok_embeddings, final_norm, layers,
+              rope_interleaved=False) -> QknModel:
+    """layers: list of dicts with the QknLayer field names mapped to device tensors."""
+    arr = (QknLayer * len(layers))()
+    for i, lw in enumerate(layers):
+        for name, _ in QknLayer._fields_:
+            setattr(arr[i], name, _ptr(lw[name]))
+    m = QknModel(hidden, len(layers), n_heads, n_kv_heads, head_dim, intermediate, vocab, eps, int(rope_interleaved),
+                 _ptr(tok_embeddings), _ptr(final_norm), ctypes.cast(arr, ctypes.POINTER(QknLayer)))
+    m._layers = arr   # keep the array alive with the struct
+    return m
+
+
+def qkn_step_workspace_bytes(model: QknModel, n_seqs: int, max_kv_len: int) -> int:
+    return lib().smol_b200_qkn_step_workspace_bytes(ctypes.byref(model), n_seqs, max_kv_len)
+
+
+def qkn_decode_step(model: QknModel, n_seqs, tokens_in, tokens_out, k_pool, v_pool, pool_rows, layer_row0, kv_len,
+                    max_kv_len, rope_cos, rope_sin, workspace, advance=False, stream=None):
+    rc = lib().smol_b200_qkn_decode_step(
+        _stream(stream), ctypes.byref(model), n_seqs, _ptr(tokens_in), _ptr(tokens_out), _ptr(k_pool), _ptr(v_pool),
+        pool_rows, _ptr(layer_row0), _ptr(kv_len), max_kv_len, _ptr(rope_cos), _ptr(rope_sin), int(advance),
+        _ptr(workspace), workspace.numel() * workspace.element_size())
+    check(rc, "smol_b200_qkn_decode_step")
+
+
+def gemv_bf16(y, ldy, x, ldx, w, n_out, k_dim, n_seqs, mode=0, stream=None):
+    check(lib().smol_b200_gemv_bf16(_stream(stream), _ptr(y), ldy, _ptr(x), ldx, _ptr(w), n_out, k_dim, n_seqs, mode),
+          "smol_b200_gemv_bf16")
+
+
+def argmax_workspace_bytes(n_seqs: int) -> int:
+    return lib().smol_b200_argmax_workspace_bytes(n_seqs)
+
+
+def argmax_bf16(tokens_out, x, ldx, emb, vocab, k_dim, n_seqs, workspace, stream=None):
+    check(lib().smol_b200_argmax_bf16(_stream(stream), _ptr(tokens_out), _ptr(x), ldx, _ptr(emb), vocab, k_dim, n_seqs,
+                                      _ptr(workspace), workspace.numel() * workspace.element_size()),
+          "smol_b200_argmax_bf16")
