@@ -57,7 +57,7 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=workload.CFG2["layers"])
     ap.add_argument("--no-decode", action="store_true", help="prefill measurement only (profiling helper)")
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg 1/3/4 block")
-    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4"], default=None,
+    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4", "decoder"], default=None,
                     help="run one of the cfg 1/3/4 measurements alone (profiling helper)")
     ap.add_argument("--images", type=int, default=None, help="cfg 3 image count override")
     ap.add_argument("--prefill-shape", default=None, help="B,L override of the cfg 5 prefill shape")
@@ -509,10 +509,63 @@ def run_cfg4() -> dict:
                        "the 128-step x 18-layer suffix replayed as one CUDA graph"}
 
 
+def run_decoder(pk, batch: int = 1, steps: int = 50) -> dict:
+    """The device-resident decoder step (smol_b200_qkn_decode_step) at Qwen3-0.6B size:
+    28 layers, hidden 1024, 16/8 heads, head_dim 128, SwiGLU 3072, vocab 151936 (tied
+    lm_head), random bf16 weights, `batch` sequences with 512 cached tokens each.  One
+    step = one greedy token per sequence, replayed from a CUDA graph.  Bytes per step =
+    every weight once (the products stream them) + the attended K/V."""
+    import torch
+
+    import smol_b200
+    g = torch.Generator(device="cuda").manual_seed(21)
+    H, Lr, HQ, HKV, HD, I, V = 1024, 28, 16, 8, 128, 3072, 151936
+    qd, kvd, P, cap = HQ * HD, HKV * HD, 512, 1024
+
+    def bf(rows, cols):
+        return (torch.randn((rows, cols), device="cuda", generator=g) / np.sqrt(cols)).to(torch.bfloat16)
+
+    def near(n, mean):
+        return (mean + 0.02 * torch.randn(n, device="cuda", generator=g)).contiguous()
+
+    emb = torch.randn((V, H), device="cuda", generator=g).to(torch.bfloat16)
+    layers = [{"wq": bf(qd, H), "wk": bf(kvd, H), "wv": bf(kvd, H), "wo": bf(H, qd), "gate_up": bf(2 * I, H),
+               "down": bf(H, I), "input_norm": near(H, 1.0), "post_attn_norm": near(H, 1.0),
+               "q_norm": near(HD, 1.0), "k_norm": near(HD, 1.0)} for _ in range(Lr)]
+    model = smol_b200.qkn_model(H, HQ, HKV, HD, I, V, 1e-6, emb, near(H, 1.0), layers)
+    rows = Lr * batch * cap
+    k_pool = torch.randn((rows, kvd), device="cuda", generator=g).to(torch.bfloat16)
+    v_pool = torch.randn((rows, kvd), device="cuda", generator=g).to(torch.float16)
+    row0 = (torch.arange(Lr * batch, device="cuda", dtype=torch.int64) * cap).contiguous()   # [layer][seq]
+    kv_len = torch.full((batch,), P, dtype=torch.int32, device="cuda")
+    cos_h = np.zeros((cap, HD), np.float32)
+    sin_h = np.zeros((cap, HD), np.float32)
+    smol_b200.compute_rope(cos_h, sin_h, np.arange(cap, dtype=np.int32), cap, HD, 1e6)
+    cos_d, sin_d = torch.from_numpy(cos_h).cuda(), torch.from_numpy(sin_h).cuda()
+    ws = torch.empty(smol_b200.qkn_step_workspace_bytes(model, batch, cap - 1), dtype=torch.uint8, device="cuda")
+    tokens = torch.randint(0, V, (batch,), dtype=torch.int32, device="cuda", generator=g)
+
+    def step():
+        smol_b200.qkn_decode_step(model, batch, tokens, tokens, k_pool, v_pool, rows, row0, kv_len, cap - 1, cos_d,
+                                  sin_d, ws, advance=True)
+    ms = _time_graph(_graph(step), steps)
+    smol_b200.check(smol_b200.last_error(), "decoder step")
+    weight_bytes = (Lr * (qd * H + 2 * kvd * H + H * qd + 2 * I * H + H * I) + V * H) * 2
+    mean_len = P + 4 + steps / 2 + 1          # cached tokens attended on average over the timed replays
+    kv_bytes = int(Lr * batch * mean_len * kvd * 2 * 2)
+    gbs = (weight_bytes + kv_bytes) / (ms * 1e-3) / 1e9
+    return {"workload": f"Qwen3-0.6B-size decode step (28 layers, vocab 151936), batch {batch}, ~{P} cached tokens",
+            "us_per_step": round(ms * 1e3, 1), "tokens_per_s": round(batch / (ms * 1e-3), 1),
+            "bytes_per_step": weight_bytes + kv_bytes, "gbs": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
+            "kernels": "gemv_bf16_kernel, qknorm_rope_append, decode_split_kernel (cluster), argmax_rows_kernel; "
+                       "one CUDA graph per step"}
+
+
 def run_other_configs(pk) -> dict:
     """The remaining BASELINE configs on one GPU (latency- or tensor-bound; not the headline)."""
     import smol_b200
-    res = {"cfg1": run_cfg1(), "cfg3": run_cfg3(pk), "cfg4": run_cfg4()}
+    res = {"cfg1": run_cfg1(), "cfg3": run_cfg3(pk), "cfg4": run_cfg4(),
+           "decoder_step_b1": run_decoder(pk, 1), "decoder_step_b8": run_decoder(pk, 8)}
     smol_b200.check(smol_b200.last_error(), "other configs")
     return res
 
@@ -702,7 +755,7 @@ def main():
         torch.cuda.set_device(0)
         pk = peaks()
         fn = {"cfg1": run_cfg1, "cfg3": lambda: run_cfg3(pk, args.images, 1 if args.images else None),
-              "cfg4": run_cfg4}[args.only_config]
+              "cfg4": run_cfg4, "decoder": lambda: [run_decoder(pk, 1), run_decoder(pk, 8)]}[args.only_config]
         print(json.dumps({args.only_config: fn()}))
         return
     run_ours(args)

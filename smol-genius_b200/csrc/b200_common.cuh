@@ -332,6 +332,17 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialisation may start while its predecessor still runs: it must call
+// griddep_wait() before it reads anything an earlier kernel wrote or writes any
+// global memory (after the wait every earlier kernel of the stream has completed
+// and its writes are visible).  griddep_trigger() lets the successor launch; both
+// are no-ops for a kernel launched without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // Thread-block clusters: barrier and distributed shared memory (DSMEM) loads.
 // (No TMA multicast anywhere: clusters are used only to read a peer CTA's partials.)
 // ---------------------------------------------------------------------------

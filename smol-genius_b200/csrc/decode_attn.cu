@@ -116,6 +116,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_
     using S = DecodeShape<HD>;
     constexpr int KSTEPS = HD / 16;
 
+    griddep_trigger();
+    griddep_wait();   // q, kv_len and the appended cache rows come from earlier kernels
     const int b = blockIdx.z;
     const int kvh = blockIdx.y / p.n_qgroups;
     const int qg = blockIdx.y % p.n_qgroups;
@@ -463,6 +465,8 @@ __global__ void decode_combine_kernel(float *__restrict__ out, const float *__re
                                       const float *__restrict__ part_ml, const int *__restrict__ kv_len,
                                       int n_heads, int chunk, int max_chunks, int window, unsigned *err)
 {
+    griddep_trigger();
+    griddep_wait();
     const int b = blockIdx.y, h = blockIdx.x, d = threadIdx.x;
     const int L = kv_len[b];
     const int ks = (window > 0 && L > window) ? L - window : 0;
@@ -595,13 +599,15 @@ int launch_split_combine(cudaStream_t st, DecodeParams &p, float *out, int n_seq
         cfg.blockDim = dim3(kThreads, 1, 1);
         cfg.dynamicSmemBytes = S::smem_bytes(p.stages);
         cfg.stream = st;
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = p.max_chunks;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = g_pdl_scope ? 2 : 1;
         if (cudaLaunchKernelEx(&cfg, decode_split_kernel<HD, true>, p) != cudaSuccess) {
             cudaGetLastError();
             return SMOL_B200_ERR_CUDA;
@@ -612,11 +618,15 @@ int launch_split_combine(cudaStream_t st, DecodeParams &p, float *out, int n_seq
     p.stages = tiles < S::kMaxStages ? tiles : S::kMaxStages;
     if (!ensure_split_smem_attr<HD, false>()) return SMOL_B200_ERR_CUDA;
     dim3 grid(p.max_chunks, p.n_kv_heads * p.n_qgroups, n_seqs);
-    decode_split_kernel<HD, false><<<grid, kThreads, S::smem_bytes(p.stages), st>>>(p);
+    if (launch_kernel(decode_split_kernel<HD, false>, grid, dim3(kThreads), S::smem_bytes(p.stages), st, p) !=
+        cudaSuccess)
+        return SMOL_B200_ERR_CUDA;
     dim3 cgrid(p.n_heads, n_seqs);
-    decode_combine_kernel<HD><<<cgrid, HD, 0, st>>>(out, p.part_o, p.part_ml, p.kv_len, p.n_heads, p.chunk,
-                                                   p.max_chunks, p.window, p.err);
-    return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
+    return launch_kernel(decode_combine_kernel<HD>, cgrid, dim3(HD), 0, st, out,
+                         static_cast<const float *>(p.part_o), static_cast<const float *>(p.part_ml), p.kv_len,
+                         p.n_heads, p.chunk, p.max_chunks, p.window, p.err) == cudaSuccess
+               ? SMOL_B200_OK
+               : SMOL_B200_ERR_CUDA;
 }
 
 template <int HD>

@@ -27,6 +27,7 @@ namespace {
 constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kMaxBatch = 8;   // sequences per launch (larger batches loop)
+constexpr int kMaxXsBytes = 200 * 1024;   // staged activations: kMaxBatch x k_dim fp32 (k_dim <= 6400)
 
 struct GemvSeg {
     const uint16_t *w;
@@ -41,6 +42,8 @@ struct GemvParams {
     int total_rows;
     const float *x;
     long long ldx;
+    const float *norm_w;   // non-null: x is RMS-normalised with these weights first
+    float eps;
     int k_dim;
     int nb;     // sequences in this launch (<= NB)
     int mode;   // 0 store, 1 add, 2 gated pairs
@@ -93,24 +96,86 @@ __device__ __forceinline__ void fma8(float (&acc)[NB], const uint4 &w, const flo
 }
 
 // Stage x[b][0..k_dim) of the launch's sequences in shared memory (float4 pieces).
-__device__ __forceinline__ void stage_x(float *xs, const float *x, long long ldx, int k_dim, int nb)
+// With norm_w, each row becomes smol_rms_norm's (x * w) * 1/sqrtf(mean(x^2) + eps)
+// (rmsnorm.c:17-70), so the normalised activations never go through global memory.
+template <int NB>
+__device__ __forceinline__ void stage_x(float *xs, const float *x, long long ldx, int k_dim, int nb,
+                                        const float *norm_w, float eps)
 {
     const int n4 = nb * k_dim / 4;
+    float ss[NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) ss[b] = 0.f;
     for (int i = threadIdx.x; i < n4; i += blockDim.x) {
         const int e = i * 4, b = e / k_dim, k = e % k_dim;
-        *reinterpret_cast<float4 *>(xs + e) = *reinterpret_cast<const float4 *>(x + b * ldx + k);
+        const float4 v = *reinterpret_cast<const float4 *>(x + b * ldx + k);
+        *reinterpret_cast<float4 *>(xs + e) = v;
+        if (norm_w) {
+#pragma unroll
+            for (int bb = 0; bb < NB; ++bb)
+                if (bb == b) ss[bb] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        }
+    }
+    if (norm_w) {
+        __shared__ float part[kGemvWarps][NB];
+        __shared__ float rinv[NB];
+        const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const float t = warp_sum(ss[b]);
+            if (lane == 0) part[warp][b] = t;
+        }
+        __syncthreads();
+        if (threadIdx.x < nb) {
+            float t = 0.f;
+            for (int w = 0; w < kGemvWarps; ++w) t += part[w][threadIdx.x];
+            rinv[threadIdx.x] = 1.0f / sqrtf(t / static_cast<float>(k_dim) + eps);
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+            const int e = i * 4, b = e / k_dim, k = e % k_dim;
+            float4 v = *reinterpret_cast<float4 *>(xs + e);
+            const float4 w = *reinterpret_cast<const float4 *>(norm_w + k);
+            const float r = rinv[b];
+            v.x = v.x * w.x * r;
+            v.y = v.y * w.y * r;
+            v.z = v.z * w.z * r;
+            v.w = v.w * w.w * r;
+            *reinterpret_cast<float4 *>(xs + e) = v;
+        }
     }
     __syncthreads();
+}
+
+// Pull a weight row into L2 ahead of the dependency wait (weights never change).
+__device__ __forceinline__ void prefetch_row_l2(const uint16_t *row, int k_dim, int lane)
+{
+    const char *p = reinterpret_cast<const char *>(row);
+    for (int off = lane * 128; off < k_dim * 2; off += 32 * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
 }
 
 template <int NB>
 __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_constant__ GemvParams p)
 {
     extern __shared__ float xs[];   // [nb][k_dim]
-    stage_x(xs, p.x, p.ldx, p.k_dim, p.nb);
+    griddep_trigger();
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int rpw = p.mode == 2 ? 2 : 1;   // weight rows per warp
     const int k_dim = p.k_dim;
+    {   // this warp's first rows stream from HBM while the previous kernel finishes
+        const int r0 = (blockIdx.x * kGemvWarps + warp) * rpw;
+        if (r0 < p.total_rows) {
+            int s = 0, r = r0;
+            while (s + 1 < p.nseg && r >= p.seg[s].rows) {
+                r -= p.seg[s].rows;
+                ++s;
+            }
+            for (int i = 0; i < rpw; ++i) prefetch_row_l2(p.seg[s].w + static_cast<size_t>(r + i) * k_dim, k_dim, lane);
+        }
+    }
+    griddep_wait();
+    stage_x<NB>(xs, p.x, p.ldx, p.k_dim, p.nb, p.norm_w, p.eps);
     for (int r0 = (blockIdx.x * kGemvWarps + warp) * rpw; r0 < p.total_rows; r0 += gridDim.x * kGemvWarps * rpw) {
         int s = 0, r = r0;
         while (s + 1 < p.nseg && r >= p.seg[s].rows) {
@@ -176,10 +241,21 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_co
 template <int NB>
 __global__ void __launch_bounds__(kGemvThreads) argmax_rows_kernel(float *part_val, int *part_idx, const float *x,
                                                                     long long ldx, const uint16_t *emb, int vocab,
-                                                                    int k_dim, int nb)
+                                                                    int k_dim, int nb, const float *norm_w, float eps,
+                                                                    float *x_normed)
 {
     extern __shared__ float xs[];
-    stage_x(xs, x, ldx, k_dim, nb);
+    griddep_trigger();
+    {
+        const int r = blockIdx.x * kGemvWarps + threadIdx.x / 32;
+        if (r < vocab) prefetch_row_l2(emb + static_cast<size_t>(r) * k_dim, k_dim, threadIdx.x % 32);
+    }
+    griddep_wait();
+    stage_x<NB>(xs, x, ldx, k_dim, nb, norm_w, eps);
+    if (x_normed && blockIdx.x == 0) {   // the normalised final state, for callers that read it
+        for (int i = threadIdx.x; i < nb * k_dim; i += blockDim.x)
+            x_normed[(i / k_dim) * ldx + i % k_dim] = xs[i];
+    }
     __shared__ float wbest[kGemvWarps][NB];
     __shared__ int wbidx[kGemvWarps][NB];
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -238,6 +314,8 @@ __global__ void __launch_bounds__(kGemvThreads) argmax_rows_kernel(float *part_v
 
 __global__ void argmax_final_kernel(int *tokens_out, const float *part_val, const int *part_idx, int nparts)
 {
+    griddep_trigger();
+    griddep_wait();
     // one warp per sequence (blockIdx.x)
     const int b = blockIdx.x, lane = threadIdx.x;
     float bv = -1e30f;
@@ -265,6 +343,8 @@ __global__ void argmax_final_kernel(int *tokens_out, const float *part_val, cons
 // x[b][:] = E[tokens[b]][:] (bf16 -> fp32)
 __global__ void embed_kernel(float *x, const int *tokens, const uint16_t *emb, int hidden, int vocab, unsigned *err)
 {
+    griddep_trigger();
+    griddep_wait();
     const int b = blockIdx.x;
     int t = tokens[b];
     if (t < 0 || t >= vocab) {
@@ -280,6 +360,8 @@ __global__ void embed_kernel(float *x, const int *tokens, const uint16_t *emb, i
 __global__ void step_index_kernel(int *positions, int *kv_next, int64_t *slots, const int64_t *layer_row0,
                                   const int *kv_len, int n_seqs, int n_layers)
 {
+    griddep_trigger();
+    griddep_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_seqs * n_layers) return;
     const int b = i % n_seqs;
@@ -293,6 +375,8 @@ __global__ void step_index_kernel(int *positions, int *kv_next, int64_t *slots, 
 
 __global__ void advance_kernel(int *kv_len, int n_seqs)
 {
+    griddep_trigger();
+    griddep_wait();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b < n_seqs) kv_len[b] += 1;
 }
@@ -311,8 +395,9 @@ int launch_gemv_nb(cudaStream_t st, GemvParams &p)
         const int dev = current_device();
         if (dev < 0 || dev >= 64) return SMOL_B200_ERR_CUDA;
         if (!raised[dev]) {
+            // dynamic + static (the norm partials) must stay within the 227 KB per block
             if (cudaFuncSetAttribute(gemv_bf16_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     227 * 1024) != cudaSuccess)
+                                     kMaxXsBytes) != cudaSuccess)
                 return SMOL_B200_ERR_CUDA;
             raised[dev] = true;
         }
@@ -321,15 +406,17 @@ int launch_gemv_nb(cudaStream_t st, GemvParams &p)
     const long long warps = (p.total_rows + rpw - 1) / rpw;
     long long grid = (warps + kGemvWarps - 1) / kGemvWarps;
     if (grid > 148LL * 16) grid = 148LL * 16;
-    gemv_bf16_kernel<NB><<<static_cast<unsigned>(grid), kGemvThreads, smem, st>>>(p);
-    return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
+    return launch_kernel(gemv_bf16_kernel<NB>, dim3(static_cast<unsigned>(grid)), dim3(kGemvThreads), smem, st, p) ==
+                   cudaSuccess
+               ? SMOL_B200_OK
+               : SMOL_B200_ERR_CUDA;
 }
 
 // Runs the segmented product for every sequence, kMaxBatch sequences per launch.
 int run_gemv(cudaStream_t st, GemvParams p, int n_seqs)
 {
     if (p.k_dim <= 0 || p.k_dim % 8 || (p.ldx & 3) || p.total_rows <= 0) return SMOL_B200_ERR_ARGS;
-    if (gemv_smem_bytes(kMaxBatch, p.k_dim) > 227 * 1024) return SMOL_B200_ERR_ARGS;
+    if (gemv_smem_bytes(kMaxBatch, p.k_dim) > kMaxXsBytes) return SMOL_B200_ERR_ARGS;
     for (int s = 0; s < p.nseg; ++s)
         if (!p.seg[s].w || !p.seg[s].y || (reinterpret_cast<uintptr_t>(p.seg[s].w) & 15)) return SMOL_B200_ERR_ARGS;
     if (!p.x || (reinterpret_cast<uintptr_t>(p.x) & 15)) return SMOL_B200_ERR_ARGS;
@@ -359,7 +446,7 @@ size_t argmax_ws_bytes(int n_seqs)
 
 template <int NB>
 int launch_argmax_nb(cudaStream_t st, float *pv, int *pi, const float *x, long long ldx, const uint16_t *emb,
-                     int vocab, int k_dim, int nb)
+                     int vocab, int k_dim, int nb, const float *norm_w, float eps, float *x_normed)
 {
     const int smem = gemv_smem_bytes(nb, k_dim);
     if (smem > 48 * 1024) {
@@ -368,37 +455,42 @@ int launch_argmax_nb(cudaStream_t st, float *pv, int *pi, const float *x, long l
         if (dev < 0 || dev >= 64) return SMOL_B200_ERR_CUDA;
         if (!raised[dev]) {
             if (cudaFuncSetAttribute(argmax_rows_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     200 * 1024) != cudaSuccess)
+                                     kMaxXsBytes) != cudaSuccess)
                 return SMOL_B200_ERR_CUDA;
             raised[dev] = true;
         }
     }
-    argmax_rows_kernel<NB><<<kArgmaxBlocks, kGemvThreads, smem, st>>>(pv, pi, x, ldx, emb, vocab, k_dim, nb);
-    return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
+    return launch_kernel(argmax_rows_kernel<NB>, dim3(kArgmaxBlocks), dim3(kGemvThreads), smem, st, pv, pi, x, ldx,
+                         emb, vocab, k_dim, nb, norm_w, eps, x_normed) == cudaSuccess
+               ? SMOL_B200_OK
+               : SMOL_B200_ERR_CUDA;
 }
 
 int run_argmax(cudaStream_t st, int *tokens_out, const float *x, long long ldx, const uint16_t *emb, int vocab,
-               int k_dim, int n_seqs, void *ws, size_t ws_bytes)
+               int k_dim, int n_seqs, void *ws, size_t ws_bytes, const float *norm_w = nullptr, float eps = 0.f,
+               float *x_normed = nullptr)
 {
     if (n_seqs <= 0) return SMOL_B200_OK;
     if (!tokens_out || !x || !emb || vocab <= 0 || k_dim <= 0 || k_dim % 8 || (ldx & 3) ||
         (reinterpret_cast<uintptr_t>(emb) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
         return SMOL_B200_ERR_ARGS;
     if (!ws || ws_bytes < argmax_ws_bytes(n_seqs)) return SMOL_B200_ERR_WORKSPACE;
-    if (gemv_smem_bytes(kMaxBatch, k_dim) > 200 * 1024) return SMOL_B200_ERR_ARGS;
+    if (gemv_smem_bytes(kMaxBatch, k_dim) > kMaxXsBytes) return SMOL_B200_ERR_ARGS;
     float *pv = static_cast<float *>(ws);
     int *pi = reinterpret_cast<int *>(pv + kArgmaxBlocks * kMaxBatch);
     for (int b0 = 0; b0 < n_seqs; b0 += kMaxBatch) {
         const int nb = n_seqs - b0 < kMaxBatch ? n_seqs - b0 : kMaxBatch;
         const float *xb = x + static_cast<long long>(b0) * ldx;
+        float *xo = x_normed ? x_normed + static_cast<long long>(b0) * ldx : nullptr;
         int rc;
-        if (nb == 1) rc = launch_argmax_nb<1>(st, pv, pi, xb, ldx, emb, vocab, k_dim, nb);
-        else if (nb == 2) rc = launch_argmax_nb<2>(st, pv, pi, xb, ldx, emb, vocab, k_dim, nb);
-        else if (nb <= 4) rc = launch_argmax_nb<4>(st, pv, pi, xb, ldx, emb, vocab, k_dim, nb);
-        else rc = launch_argmax_nb<8>(st, pv, pi, xb, ldx, emb, vocab, k_dim, nb);
+        if (nb == 1) rc = launch_argmax_nb<1>(st, pv, pi, xb, ldx, emb, vocab, k_dim, nb, norm_w, eps, xo);
+        else if (nb == 2) rc = launch_argmax_nb<2>(st, pv, pi, xb, ldx, emb, vocab, k_dim, nb, norm_w, eps, xo);
+        else if (nb <= 4) rc = launch_argmax_nb<4>(st, pv, pi, xb, ldx, emb, vocab, k_dim, nb, norm_w, eps, xo);
+        else rc = launch_argmax_nb<8>(st, pv, pi, xb, ldx, emb, vocab, k_dim, nb, norm_w, eps, xo);
         if (rc != SMOL_B200_OK) return rc;
-        argmax_final_kernel<<<nb, 32, 0, st>>>(tokens_out + b0, pv, pi, kArgmaxBlocks);
-        if (cudaGetLastError() != cudaSuccess) return SMOL_B200_ERR_CUDA;
+        if (launch_kernel(argmax_final_kernel, dim3(nb), dim3(32), 0, st, tokens_out + b0, pv, pi, kArgmaxBlocks) !=
+            cudaSuccess)
+            return SMOL_B200_ERR_CUDA;
     }
     return SMOL_B200_OK;
 }
@@ -456,8 +548,8 @@ bool model_ok(const smol_b200_qkn_model *m)
 
 }  // namespace
 
-int gemv_bf16(cudaStream_t st, float *y, int64_t ldy, const float *x, int64_t ldx, const uint16_t *w, int n_out,
-              int k_dim, int n_seqs, int mode)
+int gemv_norm_bf16(cudaStream_t st, float *y, int64_t ldy, const float *x, int64_t ldx, const uint16_t *w,
+                   int n_out, int k_dim, int n_seqs, int mode, const float *norm_w, float eps)
 {
     if (n_seqs <= 0 || n_out <= 0) return SMOL_B200_OK;
     if (mode < 0 || mode > 2 || (ldy < n_out)) return SMOL_B200_ERR_ARGS;
@@ -468,9 +560,17 @@ int gemv_bf16(cudaStream_t st, float *y, int64_t ldy, const float *x, int64_t ld
     p.total_rows = p.seg[0].rows;
     p.x = x;
     p.ldx = ldx;
+    p.norm_w = norm_w;
+    p.eps = eps;
     p.k_dim = k_dim;
     p.mode = mode;
     return run_gemv(st, p, n_seqs);
+}
+
+int gemv_bf16(cudaStream_t st, float *y, int64_t ldy, const float *x, int64_t ldx, const uint16_t *w, int n_out,
+              int k_dim, int n_seqs, int mode)
+{
+    return gemv_norm_bf16(st, y, ldy, x, ldx, w, n_out, k_dim, n_seqs, mode, nullptr, 0.f);
 }
 
 int argmax_bf16(cudaStream_t st, int *tokens_out, const float *x, int64_t ldx, const uint16_t *emb, int vocab,
@@ -507,18 +607,20 @@ int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *mp, int n_seqs, 
     const int H = m.hidden, qd = m.n_heads * m.head_dim, kvd = m.n_kv_heads * m.head_dim;
     const float scale = 1.0f / sqrtf(static_cast<float>(m.head_dim));   // qkn_decoder.c:620
 
+    // Every kernel of the step launches with programmatic dependent launch: it starts
+    // while its predecessor runs and streams its (constant) weights before waiting.
+    PdlScope pdl;
     const int n_idx = n_seqs * m.n_layers;
-    step_index_kernel<<<(n_idx + 255) / 256, 256, 0, st>>>(w.positions, w.kv_next, w.slots, layer_row0, kv_len,
-                                                          n_seqs, m.n_layers);
-    embed_kernel<<<n_seqs, 256, 0, st>>>(w.x, tokens_in, m.tok_embeddings, H, m.vocab, err);
-    if (cudaGetLastError() != cudaSuccess) return SMOL_B200_ERR_CUDA;
+    if (launch_kernel(step_index_kernel, dim3((n_idx + 255) / 256), dim3(256), 0, st, w.positions, w.kv_next, w.slots,
+                      layer_row0, static_cast<const int *>(kv_len), n_seqs, m.n_layers) != cudaSuccess ||
+        launch_kernel(embed_kernel, dim3(n_seqs), dim3(256), 0, st, w.x, tokens_in, m.tok_embeddings, H, m.vocab,
+                      err) != cudaSuccess)
+        return SMOL_B200_ERR_CUDA;
 
     int rc = SMOL_B200_OK;
     for (int l = 0; l < m.n_layers && rc == SMOL_B200_OK; ++l) {
         const smol_b200_qkn_layer &L = m.layers[l];
-        rc = launch_rms_norm(st, w.xn, w.x, L.input_norm, n_seqs, H, m.eps);
-        if (rc != SMOL_B200_OK) break;
-        {   // Q, K, V in one launch (smol_linear_nobias_bf16_qkv, matmul.c:308-334)
+        {   // input RMSNorm + Q, K, V in one launch (smol_linear_nobias_bf16_qkv, matmul.c:308-334)
             GemvParams p;
             memset(&p, 0, sizeof(p));
             p.seg[0] = {L.wq, w.q, qd, qd};
@@ -526,8 +628,10 @@ int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *mp, int n_seqs, 
             p.seg[2] = {L.wv, w.v, kvd, kvd};
             p.nseg = 3;
             p.total_rows = qd + 2 * kvd;
-            p.x = w.xn;
+            p.x = w.x;
             p.ldx = H;
+            p.norm_w = L.input_norm;
+            p.eps = m.eps;
             p.k_dim = H;
             p.mode = 0;
             rc = run_gemv(st, p, n_seqs);
@@ -541,23 +645,23 @@ int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *mp, int n_seqs, 
                               layer_row0 + static_cast<size_t>(l) * n_seqs, w.kv_next, n_seqs, max_kv_len + 1,
                               m.n_heads, m.n_kv_heads, m.head_dim, scale, 0, 0.f, w.attn_ws, w.attn_ws_bytes);
         if (rc != SMOL_B200_OK) break;
-        rc = gemv_bf16(st, w.x, H, w.attn, qd, L.wo, H, qd, n_seqs, 1);                  // x += o_proj(attn)
+        rc = gemv_norm_bf16(st, w.x, H, w.attn, qd, L.wo, H, qd, n_seqs, 1, nullptr, 0.f);   // x += o_proj(attn)
         if (rc != SMOL_B200_OK) break;
-        rc = launch_rms_norm(st, w.xn, w.x, L.post_attn_norm, n_seqs, H, m.eps);
+        // post-attention RMSNorm + gate/up + SiLU gate
+        rc = gemv_norm_bf16(st, w.act, m.intermediate, w.x, H, L.gate_up, m.intermediate, H, n_seqs, 2,
+                            L.post_attn_norm, m.eps);
         if (rc != SMOL_B200_OK) break;
-        rc = gemv_bf16(st, w.act, m.intermediate, w.xn, H, L.gate_up, m.intermediate, H, n_seqs, 2);   // SwiGLU
-        if (rc != SMOL_B200_OK) break;
-        rc = gemv_bf16(st, w.x, H, w.act, m.intermediate, L.down, H, m.intermediate, n_seqs, 1);       // x += down
+        rc = gemv_norm_bf16(st, w.x, H, w.act, m.intermediate, L.down, H, m.intermediate, n_seqs, 1, nullptr,
+                            0.f);   // x += down(act)
     }
     if (rc != SMOL_B200_OK) return rc;
-    rc = launch_rms_norm(st, w.x, w.x, m.final_norm, n_seqs, H, m.eps);   // qkn_decoder.c:710
+    // final RMSNorm (qkn_decoder.c:710) folded into the argmax; the normalised state lands in xn
+    rc = run_argmax(st, tokens_out, w.x, H, m.tok_embeddings, m.vocab, H, n_seqs, w.argmax_ws, w.argmax_ws_bytes,
+                    m.final_norm, m.eps, w.xn);
     if (rc != SMOL_B200_OK) return rc;
-    rc = run_argmax(st, tokens_out, w.x, H, m.tok_embeddings, m.vocab, H, n_seqs, w.argmax_ws, w.argmax_ws_bytes);
-    if (rc != SMOL_B200_OK) return rc;
-    if (advance) {
-        advance_kernel<<<(n_seqs + 255) / 256, 256, 0, st>>>(kv_len, n_seqs);
-        if (cudaGetLastError() != cudaSuccess) return SMOL_B200_ERR_CUDA;
-    }
+    if (advance && launch_kernel(advance_kernel, dim3((n_seqs + 255) / 256), dim3(256), 0, st, kv_len, n_seqs) !=
+                       cudaSuccess)
+        return SMOL_B200_ERR_CUDA;
     return SMOL_B200_OK;
 }
 

@@ -108,6 +108,8 @@ __global__ void qknorm_rope_append_kernel(const float *__restrict__ q_in, const 
                                           float *q_out_f32, uint16_t *q_out_bf16, uint16_t *k_cache,
                                           uint16_t *v_cache, long long cache_rows, unsigned *err)
 {
+    griddep_trigger();
+    griddep_wait();
     const long long wid = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const long long nq = static_cast<long long>(n_tokens) * n_heads;
@@ -297,10 +299,11 @@ int qknorm_rope_append(cudaStream_t st, const float *q_in, const float *k_in, co
     const long long warps = static_cast<long long>(n_tokens) * (n_heads + n_kv_heads);
     const long long blocks = (warps + kWarpsPerBlock - 1) / kWarpsPerBlock;
     if (blocks > 0x7fffffffLL) return SMOL_B200_ERR_ARGS;
-    qknorm_rope_append_kernel<<<static_cast<unsigned>(blocks), kWarpsPerBlock * 32, 0, st>>>(
-        q_in, k_in, v_in, n_tokens, n_heads, n_kv_heads, head_dim, q_norm_w, k_norm_w, eps, rope_cos, rope_sin,
-        rope_interleaved, positions, slots, q_out_f32, q_out_bf16, k_cache_bf16, v_cache_f16, cache_rows, err);
-    return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
+    const cudaError_t e = launch_kernel(
+        qknorm_rope_append_kernel, dim3(static_cast<unsigned>(blocks)), dim3(kWarpsPerBlock * 32), 0, st, q_in, k_in,
+        v_in, n_tokens, n_heads, n_kv_heads, head_dim, q_norm_w, k_norm_w, eps, rope_cos, rope_sin, rope_interleaved,
+        positions, slots, q_out_f32, q_out_bf16, k_cache_bf16, v_cache_f16, static_cast<long long>(cache_rows), err);
+    return e == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
 }
 
 int launch_pack_rows(cudaStream_t st, uint16_t *dst, int64_t dst_stride, int dst_width, const float *src,

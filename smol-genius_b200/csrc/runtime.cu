@@ -12,6 +12,8 @@
 
 namespace smolb200 {
 
+thread_local bool g_pdl_scope = false;
+
 namespace {
 
 constexpr int kMaxDevices = 16;

@@ -78,6 +78,34 @@ int launch_unpack_rows(cudaStream_t st, float *dst, int64_t dst_stride, const fl
 // Bounded-wait self test: one kernel whose wait can never succeed (see rope_norm.cu).
 int launch_watchdog_selftest(cudaStream_t st);
 
+// Launches with programmatic dependent launch when the calling thread is inside a
+// PdlScope (the device decoder step); otherwise a plain launch.  The kernels that
+// go through it call griddep_wait() before touching data of earlier kernels.
+extern thread_local bool g_pdl_scope;
+struct PdlScope {
+    bool prev;
+    PdlScope() : prev(g_pdl_scope) { g_pdl_scope = true; }
+    ~PdlScope() { g_pdl_scope = prev; }
+};
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                          Args &&...args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    if (g_pdl_scope) {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+    }
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // decoder.cu: the device-resident decode step (Part 4 of smol_b200.h)
 int gemv_bf16(cudaStream_t st, float *y, int64_t ldy, const float *x, int64_t ldx, const uint16_t *w, int n_out,
               int k_dim, int n_seqs, int mode);
