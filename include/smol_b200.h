@@ -295,11 +295,12 @@ SMOL_B200_API int smol_b200_qkn_decode_step(
  * x fp32 with row stride ldx (multiple of 4), y fp32 with row stride ldy. */
 SMOL_B200_API int smol_b200_gemv_bf16(void *stream, float *y, int64_t ldy, const float *x, int64_t ldx,
                                       const uint16_t *w, int n_out, int k_dim, int n_seqs, int mode);
-/* tokens_out[b] = argmax_v sum_k x[b][k] * E[v][k] (lowest v among equal maxima). */
+/* tokens_out[b] = argmax_v sum_k x[b][k] * E[v][k] (lowest v among equal maxima); the
+ * workspace holds the n_seqs x vocab fp32 logits. */
 SMOL_B200_API int smol_b200_argmax_bf16(void *stream, int *tokens_out, const float *x, int64_t ldx,
                                         const uint16_t *emb, int vocab, int k_dim, int n_seqs,
                                         void *workspace, size_t workspace_bytes);
-SMOL_B200_API size_t smol_b200_argmax_workspace_bytes(int n_seqs);
+SMOL_B200_API size_t smol_b200_argmax_workspace_bytes(int n_seqs, int vocab);
 
 #ifdef __cplusplus
 }

@@ -577,9 +577,9 @@ int smol_b200_argmax_bf16(void *stream, int *tokens_out, const float *x, int64_t
                   "smol_b200_argmax_bf16");
 }
 
-size_t smol_b200_argmax_workspace_bytes(int n_seqs)
+size_t smol_b200_argmax_workspace_bytes(int n_seqs, int vocab)
 {
-    return argmax_workspace_bytes(n_seqs);
+    return argmax_workspace_bytes(n_seqs, vocab);
 }
 
 }  // extern "C"

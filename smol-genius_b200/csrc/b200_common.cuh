@@ -336,8 +336,10 @@ __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.
 // serialisation may start while its predecessor still runs: it must call
 // griddep_wait() before it reads anything an earlier kernel wrote or writes any
 // global memory (after the wait every earlier kernel of the stream has completed
-// and its writes are visible).  griddep_trigger() lets the successor launch; both
-// are no-ops for a kernel launched without the attribute.
+// and its writes are visible).  griddep_trigger() lets the successor launch; the
+// kernels here trigger after their own wait, so at most one grid waits ahead of the
+// running one (triggering on entry lets a chain of waiting grids fill the SMs).
+// Both are no-ops for a kernel launched without the attribute.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

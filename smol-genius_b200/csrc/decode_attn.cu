@@ -116,8 +116,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_split_kernel(const __grid_
     using S = DecodeShape<HD>;
     constexpr int KSTEPS = HD / 16;
 
-    griddep_trigger();
     griddep_wait();   // q, kv_len and the appended cache rows come from earlier kernels
+    griddep_trigger();
     const int b = blockIdx.z;
     const int kvh = blockIdx.y / p.n_qgroups;
     const int qg = blockIdx.y % p.n_qgroups;
@@ -465,8 +465,8 @@ __global__ void decode_combine_kernel(float *__restrict__ out, const float *__re
                                       const float *__restrict__ part_ml, const int *__restrict__ kv_len,
                                       int n_heads, int chunk, int max_chunks, int window, unsigned *err)
 {
-    griddep_trigger();
     griddep_wait();
+    griddep_trigger();
     const int b = blockIdx.y, h = blockIdx.x, d = threadIdx.x;
     const int L = kv_len[b];
     const int ks = (window > 0 && L > window) ? L - window : 0;

@@ -14,6 +14,7 @@
 // launch's sequences sit in shared memory.  Algorithmic bytes per launch: rows *
 // k_dim * 2 (weights) + n_seqs * (k_dim + rows) * 4 (activations).
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <vector>
@@ -27,7 +28,13 @@ namespace {
 constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kMaxBatch = 8;   // sequences per launch (larger batches loop)
-constexpr int kMaxXsBytes = 200 * 1024;   // staged activations: kMaxBatch x k_dim fp32 (k_dim <= 6400)
+constexpr int kMaxXsBytes = 200 * 1024;
+// Warps per SM the K split aims for (SMOL_GEMV_WARPS_PER_SM, measurement knob).
+const int g_gemv_warps_per_sm = [] {
+    const char *e = getenv("SMOL_GEMV_WARPS_PER_SM");
+    const int v = e ? atoi(e) : 0;
+    return v > 0 ? v : 8;
+}();   // staged activations: kMaxBatch x k_dim fp32 (k_dim <= 6400)
 
 struct GemvSeg {
     const uint16_t *w;
@@ -44,9 +51,11 @@ struct GemvParams {
     long long ldx;
     const float *norm_w;   // non-null: x is RMS-normalised with these weights first
     float eps;
+    float *x_normed;       // non-null: CTA 0 also writes the staged (normalised) x here
     int k_dim;
-    int nb;     // sequences in this launch (<= NB)
-    int mode;   // 0 store, 1 add, 2 gated pairs
+    int nb;       // sequences in this launch (<= NB)
+    int mode;     // 0 store, 1 add, 2 gated pairs
+    int ksplit;   // warps of a CTA that share one row group, each a slice of K (1, 2, 4, 8)
 };
 
 __device__ __forceinline__ uint4 ldg_stream(const void *p)
@@ -155,196 +164,232 @@ __device__ __forceinline__ void prefetch_row_l2(const uint16_t *row, int k_dim, 
         asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
 }
 
-template <int NB>
+// Row `r` of the concatenated segments: its weights and its output column.
+struct RowRef {
+    const uint16_t *w;
+    float *y;
+    long long ldy;
+    int col;
+};
+
+__device__ __forceinline__ RowRef row_ref(const GemvParams &p, int r, int k_dim)
+{
+    int s = 0;
+    while (s + 1 < p.nseg && r >= p.seg[s].rows) {
+        r -= p.seg[s].rows;
+        ++s;
+    }
+    return {p.seg[s].w + static_cast<size_t>(r) * k_dim, p.seg[s].y, p.seg[s].ldy, r};
+}
+
+// A warp owns R consecutive weight rows (R even for the gated form: gate, up pairs),
+// so each 16-byte piece of the staged activations read from shared memory serves R
+// rows: with 8 sequences and R = 4 the shared-memory traffic is 4x the weight
+// traffic instead of 16x.  With ksplit = S the CTA's 8 warps form 8/S row groups of S
+// warps, each warp streaming every S-th 256-element piece of K, and the S partial
+// sums meet in shared memory -- so a projection with few rows still spreads over
+// enough warps to keep HBM busy.
+template <int NB, int R>
 __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_constant__ GemvParams p)
 {
     extern __shared__ float xs[];   // [nb][k_dim]
-    griddep_trigger();
+    __shared__ float part[kGemvWarps][R][NB];
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int rpw = p.mode == 2 ? 2 : 1;   // weight rows per warp
     const int k_dim = p.k_dim;
+    const int S = p.ksplit, G = kGemvWarps / S;
+    const int slice = warp % S, grp = warp / S;
+    const int n_groups = (p.total_rows + R - 1) / R;
     {   // this warp's first rows stream from HBM while the previous kernel finishes
-        const int r0 = (blockIdx.x * kGemvWarps + warp) * rpw;
-        if (r0 < p.total_rows) {
-            int s = 0, r = r0;
-            while (s + 1 < p.nseg && r >= p.seg[s].rows) {
-                r -= p.seg[s].rows;
-                ++s;
+        const int rg = blockIdx.x * G + grp;
+        if (rg < n_groups) {
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                if (rg * R + i >= p.total_rows) break;
+                const char *row = reinterpret_cast<const char *>(row_ref(p, rg * R + i, k_dim).w);
+                for (int off = (slice * 32 + lane) * 512; off < k_dim * 2; off += S * 32 * 512)
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(row + off));
             }
-            for (int i = 0; i < rpw; ++i) prefetch_row_l2(p.seg[s].w + static_cast<size_t>(r + i) * k_dim, k_dim, lane);
         }
     }
     griddep_wait();
-    stage_x<NB>(xs, p.x, p.ldx, p.k_dim, p.nb, p.norm_w, p.eps);
-    for (int r0 = (blockIdx.x * kGemvWarps + warp) * rpw; r0 < p.total_rows; r0 += gridDim.x * kGemvWarps * rpw) {
-        int s = 0, r = r0;
-        while (s + 1 < p.nseg && r >= p.seg[s].rows) {
-            r -= p.seg[s].rows;
-            ++s;
-        }
-        const uint16_t *w0 = p.seg[s].w + static_cast<size_t>(r) * k_dim;
-        float acc0[NB], acc1[NB];
+    griddep_trigger();   // one successor may start (and prefetch) while this one works
+    stage_x<NB>(xs, p.x, p.ldx, k_dim, p.nb, p.norm_w, p.eps);
+    if (p.x_normed && blockIdx.x == 0)
+        for (int i = threadIdx.x; i < p.nb * k_dim; i += blockDim.x) p.x_normed[(i / k_dim) * p.ldx + i % k_dim] = xs[i];
+    // every warp runs the same number of rounds (the CTA meets at the partial-sum barriers)
+    for (int base = blockIdx.x * G; base < n_groups; base += gridDim.x * G) {
+        const int rg = base + grp;
+        const int r0 = rg * R;
+        RowRef rr[R];
+        bool valid[R];
 #pragma unroll
-        for (int b = 0; b < NB; ++b) acc0[b] = acc1[b] = 0.f;
-        if (rpw == 1) {
-            int k = lane * 8;
-            // four 16-byte pieces in flight per lane
-            for (; k + 3 * 256 < k_dim; k += 4 * 256) {
-                const uint4 a = ldg_stream(w0 + k), b1 = ldg_stream(w0 + k + 256), c = ldg_stream(w0 + k + 512),
-                            d = ldg_stream(w0 + k + 768);
-                fma8<NB>(acc0, a, xs, k_dim, k, p.nb);
-                fma8<NB>(acc0, b1, xs, k_dim, k + 256, p.nb);
-                fma8<NB>(acc0, c, xs, k_dim, k + 512, p.nb);
-                fma8<NB>(acc0, d, xs, k_dim, k + 768, p.nb);
-            }
-            for (; k < k_dim; k += 256) fma8<NB>(acc0, ldg_stream(w0 + k), xs, k_dim, k, p.nb);
-        } else {
-            const uint16_t *w1 = w0 + k_dim;
-            int k = lane * 8;
-            for (; k + 256 < k_dim; k += 2 * 256) {
-                const uint4 a = ldg_stream(w0 + k), b1 = ldg_stream(w1 + k), c = ldg_stream(w0 + k + 256),
-                            d = ldg_stream(w1 + k + 256);
-                fma8<NB>(acc0, a, xs, k_dim, k, p.nb);
-                fma8<NB>(acc1, b1, xs, k_dim, k, p.nb);
-                fma8<NB>(acc0, c, xs, k_dim, k + 256, p.nb);
-                fma8<NB>(acc1, d, xs, k_dim, k + 256, p.nb);
-            }
-            for (; k < k_dim; k += 256) {
-                fma8<NB>(acc0, ldg_stream(w0 + k), xs, k_dim, k, p.nb);
-                fma8<NB>(acc1, ldg_stream(w1 + k), xs, k_dim, k, p.nb);
-            }
+        for (int i = 0; i < R; ++i) {
+            valid[i] = rg < n_groups && r0 + i < p.total_rows;
+            rr[i] = row_ref(p, valid[i] ? r0 + i : 0, k_dim);
         }
+        float acc[R][NB];
 #pragma unroll
-        for (int b = 0; b < NB; ++b) {
-            if (b < p.nb) {
-                const float s0 = warp_sum(acc0[b]);
-                const float s1 = rpw == 2 ? warp_sum(acc1[b]) : 0.f;
-                if (lane == 0) {
-                    float *y = p.seg[s].y + b * p.seg[s].ldy;
-                    if (p.mode == 0) {
-                        y[r] = s0;
-                    } else if (p.mode == 1) {
-                        y[r] = y[r] + s0;
-                    } else {
-                        const float g = s0 / (1.0f + expf(-s0));   // SiLU, activation.c:81
-                        y[r / 2] = g * s1;
+        for (int i = 0; i < R; ++i)
+#pragma unroll
+            for (int b = 0; b < NB; ++b) acc[i][b] = 0.f;
+#pragma unroll 2
+        for (int k = (slice * 32 + lane) * 8; k < k_dim; k += S * 256) {
+            float wf[R][8];
+#pragma unroll
+            for (int i = 0; i < R; ++i) {
+                const uint4 w = valid[i] ? ldg_stream(rr[i].w + k) : make_uint4(0, 0, 0, 0);
+                const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    wf[i][2 * j] = bf16lo_f32(u[j]);
+                    wf[i][2 * j + 1] = bf16hi_f32(u[j]);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (b < p.nb) {
+                    const float4 xa = *reinterpret_cast<const float4 *>(xs + b * k_dim + k);
+                    const float4 xb = *reinterpret_cast<const float4 *>(xs + b * k_dim + k + 4);
+                    const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+                    for (int i = 0; i < R; ++i) {
+                        float a = acc[i][b];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) a = fmaf(wf[i][j], xv[j], a);
+                        acc[i][b] = a;
                     }
                 }
             }
         }
+        if (S == 1) {   // the warp holds whole rows: write from lane 0, no CTA barrier
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (b >= p.nb) continue;
+                float sums[R];
+#pragma unroll
+                for (int i = 0; i < R; ++i) sums[i] = warp_sum(acc[i][b]);
+                if (lane == 0) {
+#pragma unroll
+                    for (int i = 0; i < R; ++i) {
+                        if (!valid[i]) continue;
+                        float *y = rr[i].y + b * rr[i].ldy;
+                        if (p.mode == 0) {
+                            y[rr[i].col] = sums[i];
+                        } else if (p.mode == 1) {
+                            y[rr[i].col] = y[rr[i].col] + sums[i];
+                        } else if ((i & 1) == 0) {
+                            const float g = sums[i] / (1.0f + expf(-sums[i]));   // SiLU, activation.c:81
+                            y[rr[i].col / 2] = g * sums[i + 1];
+                        }
+                    }
+                }
+            }
+            continue;
+        }
+#pragma unroll
+        for (int i = 0; i < R; ++i)
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                const float v = warp_sum(acc[i][b]);
+                if (lane == 0) part[warp][i][b] = v;
+            }
+        __syncthreads();
+        if (slice == 0 && lane < R * NB) {
+            const int i = lane / NB, b = lane % NB;
+            if (valid[i] && b < p.nb) {
+                float v = 0.f;
+                for (int sl = 0; sl < S; ++sl) v += part[grp * S + sl][i][b];
+                const RowRef r = row_ref(p, r0 + i, k_dim);
+                float *y = r.y + b * r.ldy;
+                if (p.mode == 0) {
+                    y[r.col] = v;
+                } else if (p.mode == 1) {
+                    y[r.col] = y[r.col] + v;
+                } else if ((i & 1) == 0) {   // gate row i, up row i+1 (pairs never straddle a warp)
+                    float u = 0.f;
+                    for (int sl = 0; sl < S; ++sl) u += part[grp * S + sl][i + 1][b];
+                    const float g = v / (1.0f + expf(-v));   // SiLU, activation.c:81
+                    y[r.col / 2] = g * u;
+                }
+            }
+        }
+        __syncthreads();
     }
 }
 
-// Greedy argmax over the rows of E: per CTA the best (value, row) of each sequence.
-// A row wins over another when its value is larger, or equal with a lower index
-// (the reference's strict '>' scan from row 0 keeps the first maximum).
-template <int NB>
-__global__ void __launch_bounds__(kGemvThreads) argmax_rows_kernel(float *part_val, int *part_idx, const float *x,
-                                                                    long long ldx, const uint16_t *emb, int vocab,
-                                                                    int k_dim, int nb, const float *norm_w, float eps,
-                                                                    float *x_normed)
+// Greedy argmax over the logits of each sequence: the largest value, the lowest index
+// among equal ones -- the reference's strict '>' scan from row 0 with best = -1e30
+// (bf16_matvec_avx.c:156-250, matmul.c:371-398).  Stage 1: kArgmaxParts CTAs per
+// sequence each reduce a contiguous part; stage 2: one warp per sequence.
+constexpr int kArgmaxParts = 64;
+
+__device__ __forceinline__ void better(float &bv, int &bi, float v, int i)
 {
-    extern __shared__ float xs[];
-    griddep_trigger();
-    {
-        const int r = blockIdx.x * kGemvWarps + threadIdx.x / 32;
-        if (r < vocab) prefetch_row_l2(emb + static_cast<size_t>(r) * k_dim, k_dim, threadIdx.x % 32);
-    }
-    griddep_wait();
-    stage_x<NB>(xs, x, ldx, k_dim, nb, norm_w, eps);
-    if (x_normed && blockIdx.x == 0) {   // the normalised final state, for callers that read it
-        for (int i = threadIdx.x; i < nb * k_dim; i += blockDim.x)
-            x_normed[(i / k_dim) * ldx + i % k_dim] = xs[i];
-    }
-    __shared__ float wbest[kGemvWarps][NB];
-    __shared__ int wbidx[kGemvWarps][NB];
-    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    float best[NB];
-    int bidx[NB];
-#pragma unroll
-    for (int b = 0; b < NB; ++b) {
-        best[b] = -1e30f;   // the reference's initial best value (bf16_matvec_avx.c:160)
-        bidx[b] = 0;
-    }
-    for (int r = blockIdx.x * kGemvWarps + warp; r < vocab; r += gridDim.x * kGemvWarps) {
-        const uint16_t *w0 = emb + static_cast<size_t>(r) * k_dim;
-        float acc[NB];
-#pragma unroll
-        for (int b = 0; b < NB; ++b) acc[b] = 0.f;
-        int k = lane * 8;
-        for (; k + 256 < k_dim; k += 2 * 256) {
-            const uint4 a = ldg_stream(w0 + k), c = ldg_stream(w0 + k + 256);
-            fma8<NB>(acc, a, xs, k_dim, k, nb);
-            fma8<NB>(acc, c, xs, k_dim, k + 256, nb);
-        }
-        for (; k < k_dim; k += 256) fma8<NB>(acc, ldg_stream(w0 + k), xs, k_dim, k, nb);
-#pragma unroll
-        for (int b = 0; b < NB; ++b) {
-            const float v = warp_sum(acc[b]);   // identical in every lane
-            if (v > best[b] || (v == best[b] && r < bidx[b])) {
-                best[b] = v;
-                bidx[b] = r;
-            }
-        }
-    }
-    if (lane == 0) {
-#pragma unroll
-        for (int b = 0; b < NB; ++b) {
-            wbest[warp][b] = best[b];
-            wbidx[warp][b] = bidx[b];
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x < nb) {
-        const int b = threadIdx.x;
-        float bv = wbest[0][b];
-        int bi = wbidx[0][b];
-        for (int w = 1; w < kGemvWarps; ++w) {
-            const float v = wbest[w][b];
-            const int i = wbidx[w][b];
-            if (v > bv || (v == bv && i < bi)) {
-                bv = v;
-                bi = i;
-            }
-        }
-        part_val[blockIdx.x * kMaxBatch + b] = bv;
-        part_idx[blockIdx.x * kMaxBatch + b] = bi;
+    if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
     }
 }
 
-__global__ void argmax_final_kernel(int *tokens_out, const float *part_val, const int *part_idx, int nparts)
+__device__ __forceinline__ void warp_best(float &bv, int &bi)
 {
-    griddep_trigger();
-    griddep_wait();
-    // one warp per sequence (blockIdx.x)
-    const int b = blockIdx.x, lane = threadIdx.x;
-    float bv = -1e30f;
-    int bi = 0;
-    for (int i = lane; i < nparts; i += 32) {
-        const float v = part_val[i * kMaxBatch + b];
-        const int ix = part_idx[i * kMaxBatch + b];
-        if (v > bv || (v == bv && ix < bi)) {
-            bv = v;
-            bi = ix;
-        }
-    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float v = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int ix = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (v > bv || (v == bv && ix < bi)) {
-            bv = v;
-            bi = ix;
+        const int i = __shfl_xor_sync(0xffffffffu, bi, o);
+        better(bv, bi, v, i);
+    }
+}
+
+__global__ void __launch_bounds__(256) argmax_part_kernel(float *part_val, int *part_idx, const float *logits,
+                                                          long long ld, int vocab)
+{
+    griddep_wait();
+    griddep_trigger();
+    const int b = blockIdx.y, part = blockIdx.x;
+    const int per = (vocab + kArgmaxParts - 1) / kArgmaxParts;
+    const int lo = part * per, hi = min(vocab, lo + per);
+    const float *lg = logits + b * ld;
+    float bv = -1e30f;
+    int bi = lo < vocab ? lo : 0;
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) better(bv, bi, lg[i], i);
+    warp_best(bv, bi);
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    if (threadIdx.x % 32 == 0) {
+        sv[threadIdx.x / 32] = bv;
+        si[threadIdx.x / 32] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        bv = threadIdx.x < 8 ? sv[threadIdx.x] : -1e30f;
+        bi = threadIdx.x < 8 ? si[threadIdx.x] : si[0];
+        warp_best(bv, bi);
+        if (threadIdx.x == 0) {
+            part_val[b * kArgmaxParts + part] = bv;
+            part_idx[b * kArgmaxParts + part] = bi;
         }
     }
-    if (lane == 0) tokens_out[b] = bi;
+}
+
+__global__ void argmax_final_kernel(int *tokens_out, const float *part_val, const int *part_idx)
+{
+    griddep_wait();
+    griddep_trigger();
+    const int b = blockIdx.x;
+    float bv = -1e30f;
+    int bi = 0;
+    for (int i = threadIdx.x; i < kArgmaxParts; i += 32)
+        better(bv, bi, part_val[b * kArgmaxParts + i], part_idx[b * kArgmaxParts + i]);
+    warp_best(bv, bi);
+    if (threadIdx.x == 0) tokens_out[b] = bi;
 }
 
 // x[b][:] = E[tokens[b]][:] (bf16 -> fp32)
 __global__ void embed_kernel(float *x, const int *tokens, const uint16_t *emb, int hidden, int vocab, unsigned *err)
 {
-    griddep_trigger();
     griddep_wait();
+    griddep_trigger();
     const int b = blockIdx.x;
     int t = tokens[b];
     if (t < 0 || t >= vocab) {
@@ -360,8 +405,8 @@ __global__ void embed_kernel(float *x, const int *tokens, const uint16_t *emb, i
 __global__ void step_index_kernel(int *positions, int *kv_next, int64_t *slots, const int64_t *layer_row0,
                                   const int *kv_len, int n_seqs, int n_layers)
 {
-    griddep_trigger();
     griddep_wait();
+    griddep_trigger();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n_seqs * n_layers) return;
     const int b = i % n_seqs;
@@ -375,8 +420,8 @@ __global__ void step_index_kernel(int *positions, int *kv_next, int64_t *slots, 
 
 __global__ void advance_kernel(int *kv_len, int n_seqs)
 {
-    griddep_trigger();
     griddep_wait();
+    griddep_trigger();
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b < n_seqs) kv_len[b] += 1;
 }
@@ -386,7 +431,7 @@ int gemv_smem_bytes(int nb, int k_dim)
     return nb * k_dim * static_cast<int>(sizeof(float));
 }
 
-template <int NB>
+template <int NB, int R>
 int launch_gemv_nb(cudaStream_t st, GemvParams &p)
 {
     const int smem = gemv_smem_bytes(p.nb, p.k_dim);
@@ -396,20 +441,36 @@ int launch_gemv_nb(cudaStream_t st, GemvParams &p)
         if (dev < 0 || dev >= 64) return SMOL_B200_ERR_CUDA;
         if (!raised[dev]) {
             // dynamic + static (the norm partials) must stay within the 227 KB per block
-            if (cudaFuncSetAttribute(gemv_bf16_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            if (cudaFuncSetAttribute(gemv_bf16_kernel<NB, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kMaxXsBytes) != cudaSuccess)
                 return SMOL_B200_ERR_CUDA;
             raised[dev] = true;
         }
     }
-    const int rpw = p.mode == 2 ? 2 : 1;
-    const long long warps = (p.total_rows + rpw - 1) / rpw;
-    long long grid = (warps + kGemvWarps - 1) / kGemvWarps;
+    // K slices per row group: enough warps in flight for HBM (~16 per SM), while each
+    // slice keeps at least one 256-element piece per lane.
+    const long long groups = (p.total_rows + R - 1) / R;
+    const long long want_warps = 148LL * g_gemv_warps_per_sm;
+    int S = 1;
+    while (S < kGemvWarps && groups * S < want_warps && p.k_dim >= 256 * 2 * S) S *= 2;
+    p.ksplit = S;
+    const int G = kGemvWarps / S;
+    long long grid = (groups + G - 1) / G;
     if (grid > 148LL * 16) grid = 148LL * 16;
-    return launch_kernel(gemv_bf16_kernel<NB>, dim3(static_cast<unsigned>(grid)), dim3(kGemvThreads), smem, st, p) ==
-                   cudaSuccess
+    return launch_kernel(gemv_bf16_kernel<NB, R>, dim3(static_cast<unsigned>(grid)), dim3(kGemvThreads), smem, st,
+                         p) == cudaSuccess
                ? SMOL_B200_OK
                : SMOL_B200_ERR_CUDA;
+}
+
+// Rows per warp: 1 for a single sequence (most warps in flight), 2 for two, 4 from four
+// sequences on; the gated form needs an even count (gate, up).
+template <int NB>
+int launch_gemv_rows(cudaStream_t st, GemvParams &p)
+{
+    if (NB >= 4) return launch_gemv_nb<NB, 4>(st, p);
+    if (NB == 2 || p.mode == 2) return launch_gemv_nb<NB, 2>(st, p);
+    return launch_gemv_nb<NB, 1>(st, p);
 }
 
 // Runs the segmented product for every sequence, kMaxBatch sequences per launch.
@@ -418,80 +479,68 @@ int run_gemv(cudaStream_t st, GemvParams p, int n_seqs)
     if (p.k_dim <= 0 || p.k_dim % 8 || (p.ldx & 3) || p.total_rows <= 0) return SMOL_B200_ERR_ARGS;
     if (gemv_smem_bytes(kMaxBatch, p.k_dim) > kMaxXsBytes) return SMOL_B200_ERR_ARGS;
     for (int s = 0; s < p.nseg; ++s)
-        if (!p.seg[s].w || !p.seg[s].y || (reinterpret_cast<uintptr_t>(p.seg[s].w) & 15)) return SMOL_B200_ERR_ARGS;
+        if (!p.seg[s].w || !p.seg[s].y || (reinterpret_cast<uintptr_t>(p.seg[s].w) & 15) ||
+            (p.mode == 2 && (p.seg[s].rows & 1)))
+            return SMOL_B200_ERR_ARGS;
     if (!p.x || (reinterpret_cast<uintptr_t>(p.x) & 15)) return SMOL_B200_ERR_ARGS;
     for (int b0 = 0; b0 < n_seqs; b0 += kMaxBatch) {
         GemvParams q = p;
         q.nb = n_seqs - b0 < kMaxBatch ? n_seqs - b0 : kMaxBatch;
         q.x = p.x + static_cast<long long>(b0) * p.ldx;
+        if (p.x_normed) q.x_normed = p.x_normed + static_cast<long long>(b0) * p.ldx;
         for (int s = 0; s < p.nseg; ++s) q.seg[s].y = p.seg[s].y + static_cast<long long>(b0) * p.seg[s].ldy;
         int rc;
-        if (q.nb == 1) rc = launch_gemv_nb<1>(st, q);
-        else if (q.nb == 2) rc = launch_gemv_nb<2>(st, q);
-        else if (q.nb <= 4) rc = launch_gemv_nb<4>(st, q);
-        else rc = launch_gemv_nb<8>(st, q);
+        if (q.nb == 1) rc = launch_gemv_rows<1>(st, q);
+        else if (q.nb == 2) rc = launch_gemv_rows<2>(st, q);
+        else if (q.nb <= 4) rc = launch_gemv_rows<4>(st, q);
+        else rc = launch_gemv_rows<8>(st, q);
         if (rc != SMOL_B200_OK) return rc;
     }
     return SMOL_B200_OK;
 }
 
-constexpr int kArgmaxBlocks = 148 * 4;
-
-size_t argmax_ws_bytes(int n_seqs)
+// Logits of every sequence (fp32, [n_seqs][vocab]) between the lm_head product and the
+// reduction.
+size_t argmax_ws_bytes(int n_seqs, int vocab)
 {
-    const int launches = (n_seqs + kMaxBatch - 1) / kMaxBatch;
-    (void)launches;
-    return static_cast<size_t>(kArgmaxBlocks) * kMaxBatch * (sizeof(float) + sizeof(int));
+    const size_t logits = (static_cast<size_t>(n_seqs) * static_cast<size_t>(vocab) * sizeof(float) + 255) / 256 * 256;
+    return logits + static_cast<size_t>(n_seqs) * kArgmaxParts * (sizeof(float) + sizeof(int));
 }
 
-template <int NB>
-int launch_argmax_nb(cudaStream_t st, float *pv, int *pi, const float *x, long long ldx, const uint16_t *emb,
-                     int vocab, int k_dim, int nb, const float *norm_w, float eps, float *x_normed)
-{
-    const int smem = gemv_smem_bytes(nb, k_dim);
-    if (smem > 48 * 1024) {
-        static bool raised[64] = {};
-        const int dev = current_device();
-        if (dev < 0 || dev >= 64) return SMOL_B200_ERR_CUDA;
-        if (!raised[dev]) {
-            if (cudaFuncSetAttribute(argmax_rows_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kMaxXsBytes) != cudaSuccess)
-                return SMOL_B200_ERR_CUDA;
-            raised[dev] = true;
-        }
-    }
-    return launch_kernel(argmax_rows_kernel<NB>, dim3(kArgmaxBlocks), dim3(kGemvThreads), smem, st, pv, pi, x, ldx,
-                         emb, vocab, k_dim, nb, norm_w, eps, x_normed) == cudaSuccess
-               ? SMOL_B200_OK
-               : SMOL_B200_ERR_CUDA;
-}
-
+// tokens_out[b] = argmax_v sum_k norm(x)[b][k] * E[v][k]: the tied lm_head as a GEMV into
+// the logits, then the lowest-index maximum.  norm_w (optional) applies the final RMSNorm
+// while x is staged; x_normed (optional) receives the normalised rows.
 int run_argmax(cudaStream_t st, int *tokens_out, const float *x, long long ldx, const uint16_t *emb, int vocab,
                int k_dim, int n_seqs, void *ws, size_t ws_bytes, const float *norm_w = nullptr, float eps = 0.f,
                float *x_normed = nullptr)
 {
     if (n_seqs <= 0) return SMOL_B200_OK;
-    if (!tokens_out || !x || !emb || vocab <= 0 || k_dim <= 0 || k_dim % 8 || (ldx & 3) ||
-        (reinterpret_cast<uintptr_t>(emb) & 15) || (reinterpret_cast<uintptr_t>(x) & 15))
-        return SMOL_B200_ERR_ARGS;
-    if (!ws || ws_bytes < argmax_ws_bytes(n_seqs)) return SMOL_B200_ERR_WORKSPACE;
-    if (gemv_smem_bytes(kMaxBatch, k_dim) > kMaxXsBytes) return SMOL_B200_ERR_ARGS;
-    float *pv = static_cast<float *>(ws);
-    int *pi = reinterpret_cast<int *>(pv + kArgmaxBlocks * kMaxBatch);
-    for (int b0 = 0; b0 < n_seqs; b0 += kMaxBatch) {
-        const int nb = n_seqs - b0 < kMaxBatch ? n_seqs - b0 : kMaxBatch;
-        const float *xb = x + static_cast<long long>(b0) * ldx;
-        float *xo = x_normed ? x_normed + static_cast<long long>(b0) * ldx : nullptr;
-        int rc;
-        if (nb == 1) rc = launch_argmax_nb<1>(st, pv, pi, xb, ldx, emb, vocab, k_dim, nb, norm_w, eps, xo);
-        else if (nb == 2) rc = launch_argmax_nb<2>(st, pv, pi, xb, ldx, emb, vocab, k_dim, nb, norm_w, eps, xo);
-        else if (nb <= 4) rc = launch_argmax_nb<4>(st, pv, pi, xb, ldx, emb, vocab, k_dim, nb, norm_w, eps, xo);
-        else rc = launch_argmax_nb<8>(st, pv, pi, xb, ldx, emb, vocab, k_dim, nb, norm_w, eps, xo);
-        if (rc != SMOL_B200_OK) return rc;
-        if (launch_kernel(argmax_final_kernel, dim3(nb), dim3(32), 0, st, tokens_out + b0, pv, pi, kArgmaxBlocks) !=
-            cudaSuccess)
-            return SMOL_B200_ERR_CUDA;
-    }
+    if (!tokens_out || !x || !emb || vocab <= 0) return SMOL_B200_ERR_ARGS;
+    if (!ws || ws_bytes < argmax_ws_bytes(n_seqs, vocab)) return SMOL_B200_ERR_WORKSPACE;
+    float *logits = static_cast<float *>(ws);
+    GemvParams p;
+    memset(&p, 0, sizeof(p));
+    p.seg[0] = {emb, logits, vocab, vocab};
+    p.nseg = 1;
+    p.total_rows = vocab;
+    p.x = x;
+    p.ldx = ldx;
+    p.norm_w = norm_w;
+    p.eps = eps;
+    p.x_normed = x_normed;
+    p.k_dim = k_dim;
+    p.mode = 0;
+    int rc = run_gemv(st, p, n_seqs);
+    if (rc != SMOL_B200_OK) return rc;
+    uint8_t *rest = static_cast<uint8_t *>(ws) +
+                    (static_cast<size_t>(n_seqs) * static_cast<size_t>(vocab) * sizeof(float) + 255) / 256 * 256;
+    float *pv = reinterpret_cast<float *>(rest);
+    int *pi = reinterpret_cast<int *>(pv + static_cast<size_t>(n_seqs) * kArgmaxParts);
+    if (launch_kernel(argmax_part_kernel, dim3(kArgmaxParts, n_seqs), dim3(256), 0, st, pv, pi,
+                      static_cast<const float *>(logits), static_cast<long long>(vocab), vocab) != cudaSuccess ||
+        launch_kernel(argmax_final_kernel, dim3(n_seqs), dim3(32), 0, st, tokens_out,
+                      static_cast<const float *>(pv), static_cast<const int *>(pi)) != cudaSuccess)
+        return SMOL_B200_ERR_CUDA;
     return SMOL_B200_OK;
 }
 
@@ -532,7 +581,7 @@ StepWs carve(const smol_b200_qkn_model &m, int n_seqs, int max_kv_len, uint8_t *
     w.slots = reinterpret_cast<int64_t *>(take(B * m.n_layers * 8));
     w.attn_ws_bytes = decode_workspace_bytes(n_seqs, max_kv_len + 1, m.n_heads, m.n_kv_heads, m.head_dim);
     w.attn_ws = take(w.attn_ws_bytes);
-    w.argmax_ws_bytes = argmax_ws_bytes(n_seqs);
+    w.argmax_ws_bytes = argmax_ws_bytes(n_seqs, m.vocab);
     w.argmax_ws = take(w.argmax_ws_bytes);
     w.total = off;
     return w;
@@ -579,9 +628,9 @@ int argmax_bf16(cudaStream_t st, int *tokens_out, const float *x, int64_t ldx, c
     return run_argmax(st, tokens_out, x, ldx, emb, vocab, k_dim, n_seqs, ws, ws_bytes);
 }
 
-size_t argmax_workspace_bytes(int n_seqs)
+size_t argmax_workspace_bytes(int n_seqs, int vocab)
 {
-    return argmax_ws_bytes(n_seqs);
+    return argmax_ws_bytes(n_seqs, vocab);
 }
 
 size_t qkn_step_workspace_bytes(const smol_b200_qkn_model *m, int n_seqs, int max_kv_len)

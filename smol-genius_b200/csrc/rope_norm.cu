@@ -108,8 +108,8 @@ __global__ void qknorm_rope_append_kernel(const float *__restrict__ q_in, const 
                                           float *q_out_f32, uint16_t *q_out_bf16, uint16_t *k_cache,
                                           uint16_t *v_cache, long long cache_rows, unsigned *err)
 {
-    griddep_trigger();
     griddep_wait();
+    griddep_trigger();
     const long long wid = static_cast<long long>(blockIdx.x) * kWarpsPerBlock + threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
     const long long nq = static_cast<long long>(n_tokens) * n_heads;

@@ -6,6 +6,7 @@
 // points stage through, plus the device error word that bounded waits write.
 #include <mutex>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "runtime.h"
@@ -13,6 +14,11 @@
 namespace smolb200 {
 
 thread_local bool g_pdl_scope = false;
+// SMOL_PDL=0 in the environment turns programmatic dependent launch off (measurement knob).
+const bool g_pdl_enabled = [] {
+    const char *e = getenv("SMOL_PDL");
+    return !(e && e[0] == '0');
+}();
 
 namespace {
 

@@ -82,9 +82,10 @@ int launch_watchdog_selftest(cudaStream_t st);
 // PdlScope (the device decoder step); otherwise a plain launch.  The kernels that
 // go through it call griddep_wait() before touching data of earlier kernels.
 extern thread_local bool g_pdl_scope;
+extern const bool g_pdl_enabled;
 struct PdlScope {
     bool prev;
-    PdlScope() : prev(g_pdl_scope) { g_pdl_scope = true; }
+    PdlScope() : prev(g_pdl_scope) { g_pdl_scope = g_pdl_enabled; }
     ~PdlScope() { g_pdl_scope = prev; }
 };
 template <typename... KArgs, typename... Args>
@@ -111,7 +112,7 @@ int gemv_bf16(cudaStream_t st, float *y, int64_t ldy, const float *x, int64_t ld
               int k_dim, int n_seqs, int mode);
 int argmax_bf16(cudaStream_t st, int *tokens_out, const float *x, int64_t ldx, const uint16_t *emb, int vocab,
                 int k_dim, int n_seqs, void *ws, size_t ws_bytes);
-size_t argmax_workspace_bytes(int n_seqs);
+size_t argmax_workspace_bytes(int n_seqs, int vocab);
 size_t qkn_step_workspace_bytes(const smol_b200_qkn_model *m, int n_seqs, int max_kv_len);
 int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *m, int n_seqs, const int *tokens_in,
                     int *tokens_out, uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows,

@@ -89,7 +89,7 @@ _SIGNATURES = {
                                      _c_int]),
     "smol_b200_argmax_bf16": (_c_int, [_c_void, _c_void, _c_void, _c_i64, _c_void, _c_int, _c_int, _c_int, _c_void,
                                        _c_size]),
-    "smol_b200_argmax_workspace_bytes": (_c_size, [_c_int]),
+    "smol_b200_argmax_workspace_bytes": (_c_size, [_c_int, _c_int]),
 }
 
 
@@ -331,8 +331,8 @@ def gemv_bf16(y, ldy, x, ldx, w, n_out, k_dim, n_seqs, mode=0, stream=None):
           "smol_b200_gemv_bf16")
 
 
-def argmax_workspace_bytes(n_seqs: int) -> int:
-    return lib().smol_b200_argmax_workspace_bytes(n_seqs)
+def argmax_workspace_bytes(n_seqs: int, vocab: int) -> int:
+    return lib().smol_b200_argmax_workspace_bytes(n_seqs, vocab)
 
 
 def argmax_bf16(tokens_out, x, ldx, emb, vocab, k_dim, n_seqs, workspace, stream=None):

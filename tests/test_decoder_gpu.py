@@ -58,7 +58,7 @@ def test_argmax_bf16_lowest_index_on_ties(cuda):
     E[4000] = E[17]
     X = np.stack([E[t_] * 3 + 0.01 * rng.standard_normal(H).astype(np.float32) for t_ in targets]).astype(np.float32)
     out = torch.full((nb,), -1, dtype=torch.int32, device=cuda)
-    ws = torch.empty(smol_b200.argmax_workspace_bytes(nb), dtype=torch.uint8, device=cuda)
+    ws = torch.empty(smol_b200.argmax_workspace_bytes(nb, V), dtype=torch.uint8, device=cuda)
     smol_b200.argmax_bf16(out, t(X), H, t(pyoracle.bf16_bits(E)), V, H, nb, ws)
     torch.cuda.synchronize()
     assert out.cpu().tolist() == targets
