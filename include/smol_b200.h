@@ -242,7 +242,7 @@ SMOL_B200_API int smol_b200_decode_step_host(
  * pooled cache, output projection + residual, post-attention RMSNorm, fused
  * gate/up projection with SiLU(gate)*up, down projection + residual; final RMSNorm
  * and the greedy argmax over the tied embedding matrix (smol_argmax_matvec_bf16,
- * matmul.c:371-398: the lowest index among equal maxima).  Weights use the
+ * matmul.c:392-417: the lowest index among equal maxima).  Weights use the
  * reference's layouts: bf16 [out][in] matrices, gate/up rows interleaved
  * (qkn_decoder.c:140-154), fp32 norm weights.  Projections compute in fp32 from the
  * bf16 weights (bf16_matvec_fused); the cache holds K bf16 / V fp16 as in Part 3.

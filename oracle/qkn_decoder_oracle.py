@@ -33,7 +33,7 @@ def swiglu(gate_up: np.ndarray) -> np.ndarray:
 
 
 def argmax_first(logits: np.ndarray) -> int:
-    """smol_argmax_matvec_bf16 (matmul.c:371-398): the lowest index among equal maxima."""
+    """smol_argmax_matvec_bf16 (matmul.c:392-417): the lowest index among equal maxima."""
     return int(np.argmax(logits))
 
 

@@ -5,7 +5,7 @@
 // bf16_matvec_avx.c:24-150: fp32 activations times bf16 weights widened to fp32,
 // fp32 accumulation), the SwiGLU gate (activation.c:55-86), residual adds
 // (matmul.c:33-35), RMSNorm (rmsnorm.c:17-70) and the greedy argmax over the tied
-// embedding matrix (matmul.c:371-398, bf16_matvec_avx.c:156-250).
+// embedding matrix (matmul.c:392-417, bf16_matvec_avx.c:156-250).
 //
 // The products are HBM-bound for a batch of a few sequences: every weight is read
 // once per step and reused for all (<= 8) sequences of a launch.  One warp owns one
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_co
 
 // Greedy argmax over the logits of each sequence: the largest value, the lowest index
 // among equal ones -- the reference's strict '>' scan from row 0 with best = -1e30
-// (bf16_matvec_avx.c:156-250, matmul.c:371-398).  Stage 1: kArgmaxParts CTAs per
+// (bf16_matvec_avx.c:156-250, matmul.c:392-417).  Stage 1: kArgmaxParts CTAs per
 // sequence each reduce a contiguous part; stage 2: one warp per sequence.
 constexpr int kArgmaxParts = 64;
 
