@@ -523,23 +523,53 @@ int smol_b200_decode_step_host(void *stream, float *out_host, const float *q_hos
     int *pos = reinterpret_cast<int *>(base + L.pos);
     int64_t *slot = reinterpret_cast<int64_t *>(base + L.slot);
     int *next = reinterpret_cast<int *>(base + L.next);
-    const size_t qn = static_cast<size_t>(n_seqs) * n_heads * head_dim * 4;
-    const size_t kn = static_cast<size_t>(n_seqs) * n_kv_heads * head_dim * 4;
-    if (!cuda_check(cudaMemcpyAsync(q, q_host, qn, cudaMemcpyHostToDevice, st), "copy q") ||
-        !cuda_check(cudaMemcpyAsync(k, k_host, kn, cudaMemcpyHostToDevice, st), "copy k") ||
-        !cuda_check(cudaMemcpyAsync(v, v_host, kn, cudaMemcpyHostToDevice, st), "copy v"))
-        return SMOL_B200_ERR_CUDA;
-    int rc = launch_decode_step_index(st, pos, slot, next, seq_row0, kv_len, n_seqs);
-    if (rc == SMOL_B200_OK)
-        rc = qknorm_rope_append(st, q, k, v, n_seqs, n_heads, n_kv_heads, head_dim, q_norm_w, k_norm_w, eps, rope_cos,
-                                rope_sin, rope_interleaved, pos, slot, qr, nullptr, k_pool, v_pool, pool_rows);
-    if (rc == SMOL_B200_OK)
-        rc = decode_attention(st, out, qr, 0, k_pool, v_pool, pool_rows, seq_row0, next, n_seqs, max_kv_len + 1,
-                              n_heads, n_kv_heads, head_dim, scale, 0, 0.f, base + L.ws, L.total - L.ws);
+    StepPipe *P = step_pipe();
+    if (!P) return record(SMOL_B200_ERR_CUDA, "smol_b200_decode_step_host");
+    std::lock_guard<std::mutex> lock(*P->mu);
+    // The batch goes in up to four chunks of sequences: the inputs of chunk c+1 copy in
+    // and the result of chunk c-1 copies out while chunk c computes (three streams).
+    const int chunks = n_seqs >= 128 ? 4 : (n_seqs >= 64 ? 2 : 1);
+    const size_t qw = static_cast<size_t>(n_heads) * head_dim, kw = static_cast<size_t>(n_kv_heads) * head_dim;
+    bool ok = cuda_check(cudaEventRecord(P->start, st), "record") &&          // after the caller's prior work
+              cuda_check(cudaStreamWaitEvent(P->h2d, P->start, 0), "wait") &&
+              cuda_check(cudaStreamWaitEvent(P->compute, P->start, 0), "wait");
+    int rc = SMOL_B200_OK;
+    for (int c = 0; c < chunks && ok && rc == SMOL_B200_OK; ++c) {
+        const int s0 = static_cast<int>(static_cast<long long>(n_seqs) * c / chunks);
+        const int s1 = static_cast<int>(static_cast<long long>(n_seqs) * (c + 1) / chunks);
+        const int nc = s1 - s0;
+        ok = cuda_check(cudaMemcpyAsync(q + s0 * qw, q_host + s0 * qw, nc * qw * 4, cudaMemcpyHostToDevice, P->h2d),
+                        "copy q") &&
+             cuda_check(cudaMemcpyAsync(k + s0 * kw, k_host + s0 * kw, nc * kw * 4, cudaMemcpyHostToDevice, P->h2d),
+                        "copy k") &&
+             cuda_check(cudaMemcpyAsync(v + s0 * kw, v_host + s0 * kw, nc * kw * 4, cudaMemcpyHostToDevice, P->h2d),
+                        "copy v") &&
+             cuda_check(cudaEventRecord(P->in[c], P->h2d), "record") &&
+             cuda_check(cudaStreamWaitEvent(P->compute, P->in[c], 0), "wait");
+        if (!ok) break;
+        rc = launch_decode_step_index(P->compute, pos + s0, slot + s0, next + s0, seq_row0 + s0, kv_len + s0, nc);
+        if (rc == SMOL_B200_OK)
+            rc = qknorm_rope_append(P->compute, q + s0 * qw, k + s0 * kw, v + s0 * kw, nc, n_heads, n_kv_heads,
+                                    head_dim, q_norm_w, k_norm_w, eps, rope_cos, rope_sin, rope_interleaved, pos + s0,
+                                    slot + s0, qr + s0 * qw, nullptr, k_pool, v_pool, pool_rows);
+        if (rc == SMOL_B200_OK)
+            rc = decode_attention(P->compute, out + s0 * qw, qr + s0 * qw, 0, k_pool, v_pool, pool_rows,
+                                  seq_row0 + s0, next + s0, nc, max_kv_len + 1, n_heads, n_kv_heads, head_dim, scale,
+                                  0, 0.f, base + L.ws, L.total - L.ws);
+        if (rc != SMOL_B200_OK) break;
+        ok = cuda_check(cudaEventRecord(P->done[c], P->compute), "record") &&
+             cuda_check(cudaStreamWaitEvent(P->d2h, P->done[c], 0), "wait") &&
+             cuda_check(cudaMemcpyAsync(out_host + s0 * qw, out + s0 * qw, nc * qw * 4, cudaMemcpyDeviceToHost,
+                                        P->d2h),
+                        "copy out");
+    }
+    // Drain all three streams before returning (also on failure: nothing of this call
+    // may still be in flight when the caller reuses its buffers).
+    const bool drained = cuda_check(cudaStreamSynchronize(P->h2d), "synchronize") &
+                         cuda_check(cudaStreamSynchronize(P->compute), "synchronize") &
+                         cuda_check(cudaStreamSynchronize(P->d2h), "synchronize");
     if (rc != SMOL_B200_OK) return record(rc, "smol_b200_decode_step_host");
-    if (!cuda_check(cudaMemcpyAsync(out_host, out, qn, cudaMemcpyDeviceToHost, st), "copy out") ||
-        !cuda_check(cudaStreamSynchronize(st), "synchronize"))
-        return SMOL_B200_ERR_CUDA;
+    if (!ok || !drained) return SMOL_B200_ERR_CUDA;
     return SMOL_B200_OK;
 }
 

@@ -31,6 +31,9 @@ struct DeviceCtx {
     cudaStream_t stream = nullptr;
     void *scratch[kScratchSlots] = {};
     size_t scratch_bytes[kScratchSlots] = {};
+    bool pipe_init = false;
+    StepPipe pipe;
+    std::mutex pipe_mu;
 };
 
 std::mutex g_mutex;
@@ -78,6 +81,29 @@ bool encode_fn()
 }
 
 }  // namespace
+
+StepPipe *step_pipe()
+{
+    DeviceCtx *c = ctx_for_current();
+    if (!c) return nullptr;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (!c->pipe_init) {
+        StepPipe &P = c->pipe;
+        cudaStream_t *streams[3] = {&P.h2d, &P.compute, &P.d2h};
+        for (cudaStream_t *sp : streams)
+            if (!cuda_check(cudaStreamCreateWithFlags(sp, cudaStreamNonBlocking), "cudaStreamCreate(pipe)"))
+                return nullptr;
+        if (!cuda_check(cudaEventCreateWithFlags(&P.start, cudaEventDisableTiming), "cudaEventCreate(pipe)"))
+            return nullptr;
+        for (int i = 0; i < StepPipe::kMaxChunks; ++i)
+            if (!cuda_check(cudaEventCreateWithFlags(&P.in[i], cudaEventDisableTiming), "cudaEventCreate(pipe)") ||
+                !cuda_check(cudaEventCreateWithFlags(&P.done[i], cudaEventDisableTiming), "cudaEventCreate(pipe)"))
+                return nullptr;
+        P.mu = &c->pipe_mu;
+        c->pipe_init = true;
+    }
+    return &c->pipe;
+}
 
 void set_error(int code, const char *what)
 {

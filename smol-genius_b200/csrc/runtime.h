@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "smol_b200.h"
 
 namespace smolb200 {
@@ -77,6 +79,17 @@ int launch_unpack_rows(cudaStream_t st, float *dst, int64_t dst_stride, const fl
 // slots[b] = seq_row0[b] + kv_len[b], kv_len_next[b] = kv_len[b] + 1.
 // Bounded-wait self test: one kernel whose wait can never succeed (see rope_norm.cu).
 int launch_watchdog_selftest(cudaStream_t st);
+
+// Three streams and their events for calls that pipeline host copies with compute
+// (smol_b200_decode_step_host): inputs in on h2d, kernels on compute, results out on
+// d2h.  One per device, created on first use; `mu` serialises its users.
+struct StepPipe {
+    static constexpr int kMaxChunks = 4;
+    cudaStream_t h2d = nullptr, compute = nullptr, d2h = nullptr;
+    cudaEvent_t start = nullptr, in[kMaxChunks] = {}, done[kMaxChunks] = {};
+    std::mutex *mu = nullptr;
+};
+StepPipe *step_pipe();
 
 // Launches with programmatic dependent launch when the calling thread is inside a
 // PdlScope (the device decoder step); otherwise a plain launch.  The kernels that

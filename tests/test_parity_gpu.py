@@ -458,10 +458,12 @@ def test_prefill_cfg5_full_length_sampled(cuda):
 # ---------------------------------------------------------------------------
 # The host-buffer decode step (the call bench.py's end-to-end number goes through)
 # ---------------------------------------------------------------------------
-def test_decode_step_host_vs_oracle(cuda):
-    rng = np.random.default_rng(12)
-    hq, hkv, hd, n = 16, 8, 128, 6
-    lens = np.array([1, 100, 512, 513, 700, 64], np.int32)
+@pytest.mark.parametrize("n", [6, 70, 130])   # 1, 2 and 4 pipelined chunks of sequences
+def test_decode_step_host_vs_oracle(cuda, n):
+    rng = np.random.default_rng(12 + n)
+    hq, hkv, hd = 16, 8, 128
+    lens = (np.array([1, 100, 512, 513, 700, 64], np.int32) if n == 6
+            else rng.integers(1, 700, size=n).astype(np.int32))
     cap_rows = lens + 1
     row0 = np.concatenate([[0], np.cumsum(cap_rows)[:-1]]).astype(np.int64)
     rows = int(cap_rows.sum())
@@ -475,6 +477,9 @@ def test_decode_step_host_vs_oracle(cuda):
     kh = rnd_bf16(rng, n, hkv * hd)
     vh = rnd_bf16(rng, n, hkv * hd)
     out = np.zeros((n, hq * hd), np.float32)
+    if n > 6:   # pinned host memory, so the chunks' copies overlap their compute
+        pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory().numpy()  # noqa: E731
+        out, qh, kh, vh = pin(out), pin(qh), pin(kh), pin(vh)
     scratch = torch.empty(smol_b200.decode_step_scratch_bytes(n, int(lens.max()), hq, hkv, hd), dtype=torch.uint8,
                           device=cuda)
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)  # noqa: E731
