@@ -49,6 +49,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--prefill-nccl", action="store_true",
+                    help="N>1: all-gather the prefill outputs with NCCL after the kernel instead of inside it")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -278,7 +280,9 @@ def fill_randn(t, gen, chunk_rows=1 << 20):
 def run_prefill(args, world, rank, pk):
     """cfg 5 causal prefill, one layer: batch 4 x 32768, 16/8 heads, hd 128.  With N
     GPUs rank r owns KV heads r*8/N.. (and their Q heads) and the per-rank outputs are
-    all-gathered over NCCL once per layer."""
+    all-gathered once per layer: by the prefill kernel itself, which stores every output
+    tile to its slot in each peer's gather buffer (CUDA IPC mappings, NVLink), or with
+    --prefill-nccl by a separate NCCL all-gather."""
     import torch
 
     import smol_b200
@@ -296,13 +300,52 @@ def run_prefill(args, world, rank, pk):
     out = torch.empty((B, L, hq_r * hd), device="cuda")
     gathered = torch.empty((world,) + tuple(out.shape), device="cuda") if world > 1 else None
     stream = torch.cuda.current_stream()
+    scale = 1 / np.sqrt(hd)
+    fused = world > 1 and not args.prefill_nccl
+    opened, outs, check = [], None, None
+    if world > 1:
+        import torch.distributed as dist
+        sync_t = torch.zeros(1, device="cuda")
+    if fused:
+        # Every rank maps every peer's gather buffer (CUDA IPC) and its prefill writes each
+        # output tile to its own slot in all of them: the all-gather runs inside the kernel.
+        handle, off = smol_b200.ipc_handle(gathered)
+        meta = torch.tensor(list(handle) + list(off.to_bytes(8, "little")), dtype=torch.uint8, device="cuda")
+        allmeta = torch.empty(world * 72, dtype=torch.uint8, device="cuda")
+        dist.all_gather_into_tensor(allmeta, meta)
+        allmeta = allmeta.cpu().numpy().reshape(world, 72)
+        slot = out.numel() * 4
+        bases = []
+        for peer in range(world):
+            if peer == rank:
+                bases.append(gathered.data_ptr())
+            else:
+                b0 = smol_b200.ipc_open(bytes(allmeta[peer, :64]))
+                opened.append(b0)
+                bases.append(b0 + int.from_bytes(bytes(allmeta[peer, 64:]), "little"))
+        outs = [bases[rank] + rank * slot] + [bases[peer] + rank * slot for peer in range(world) if peer != rank]
 
     def layer():
-        smol_b200.prefill_attention(out, q, k, v, B, L, L, hq_r, hkv_r, hd, 1 / np.sqrt(hd), stream=stream)
-        if world > 1:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(gathered, out)
+        if fused:
+            smol_b200.prefill_attention_multi(outs, hq_r * hd, L * hq_r * hd, q, k, v, B, L, L, hq_r, hkv_r, hd, scale,
+                                              stream=stream)
+            dist.all_reduce(sync_t)   # device-side barrier: every rank's stores have landed
+        else:
+            smol_b200.prefill_attention(out, q, k, v, B, L, L, hq_r, hkv_r, hd, scale, stream=stream)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, out)
 
+    if fused:   # the fused result equals prefill + NCCL all-gather, bit for bit
+        layer()
+        torch.cuda.synchronize()
+        fused_copy = gathered.clone()
+        smol_b200.prefill_attention(out, q, k, v, B, L, L, hq_r, hkv_r, hd, scale, stream=stream)
+        dist.all_gather_into_tensor(gathered, out)
+        torch.cuda.synchronize()
+        check = bool(torch.equal(fused_copy, gathered))
+        del fused_copy
+        if not check:
+            raise SystemExit(f"rank {rank}: fused prefill all-gather differs from prefill + NCCL all-gather")
     for _ in range(2):
         layer()
     torch.cuda.synchronize()
@@ -318,8 +361,14 @@ def run_prefill(args, world, rank, pk):
     flops = workload.causal_flops_square(L, hq, hd) * B
     tf = flops / (ms * 1e-3) / 1e12
     smol_b200.check(smol_b200.last_error(), "prefill")
-    return {"workload": f"cfg5 causal prefill, 1 layer, batch {B} x {L}, GQA 16/8, hd 128"
-                        + (f", KV heads split over {world} GPUs + NCCL all-gather of outputs" if world > 1 else ""),
+    for b0 in opened:
+        smol_b200.ipc_close(b0)
+    gather = ("" if world == 1 else
+              (f", KV heads split over {world} GPUs; outputs all-gathered inside the prefill kernel (every output "
+               "row stored to each peer's buffer over NVLink, CUDA IPC)" if fused
+               else f", KV heads split over {world} GPUs + NCCL all-gather"))
+    return {"workload": f"cfg5 causal prefill, 1 layer, batch {B} x {L}, GQA 16/8, hd 128" + gather,
+            "gather_matches_nccl": check,
             "tflops": round(tf, 1), "ms_per_layer": round(ms, 3), "flops_per_layer": flops,
             "frac_of_bf16_peak": round(tf / world / pk["bf16_tflops"], 4), "per_gpu_tflops": round(tf / world, 1),
             "peak": pk["bf16_tflops"], "peak_source": pk["source"], "kernel": "tcgen05 prefill2_kernel<128>"}

@@ -215,6 +215,31 @@ SMOL_B200_API int smol_b200_prefill_attention(
     int head_dim, float scale, int mask_kind, int q_offset, int prefix_len, int window,
     float softcap, const int *window_starts, int n_windows);
 
+/* The same prefill with its output written to several places at once: out_list[i]
+ * (device pointers, n_out <= 8, all with the same row / batch strides) each receive
+ * the full result.  With CUDA IPC mappings of other GPUs' buffers in the list (the
+ * slot of this rank in each peer's gather buffer), the KV-head-split prefill and the
+ * all-gather of its output become one kernel: every output row leaves the CTA for this
+ * GPU (TMA store) and, as plain stores over NVLink, for every peer, while later tiles
+ * compute.
+ * out_list is a host array.  Head dims 64 and 128 (the tcgen05 two-tile kernel). */
+SMOL_B200_API int smol_b200_prefill_attention_multi(
+    void *stream, float *const *out_list, int n_out, int64_t out_row_stride,
+    int64_t out_batch_stride, const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride,
+    const uint16_t *k, int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v,
+    int64_t v_row_stride, int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads,
+    int n_kv_heads, int head_dim, float scale, int mask_kind, int q_offset, int prefix_len,
+    int window, float softcap, const int *window_starts, int n_windows);
+
+/* CUDA IPC for the above: a 64-byte handle of the device allocation that contains
+ * dev_ptr (cudaIpcGetMemHandle) and dev_ptr's byte offset inside it, so the peer adds
+ * the offset to the base its open returns (allocators sub-allocate); the mapping in
+ * another process (cudaIpcOpenMemHandle, peer access enabled on first use); close
+ * unmaps. */
+SMOL_B200_API int smol_b200_ipc_get_handle(const void *dev_ptr, void *handle64, size_t *offset);
+SMOL_B200_API int smol_b200_ipc_open_handle(const void *handle64, void **dev_ptr);
+SMOL_B200_API int smol_b200_ipc_close(void *dev_ptr);
+
 /* One batched decode step of one layer with host buffers, as a host-driven decoder
  * issues it: copies q/k/v of the new token of every sequence (fp32, host) to the
  * device, runs smol_b200_qknorm_rope_append (token of sequence b goes to pool row

@@ -573,6 +573,54 @@ int smol_b200_decode_step_host(void *stream, float *out_host, const float *q_hos
     return SMOL_B200_OK;
 }
 
+int smol_b200_prefill_attention_multi(void *stream, float *const *out_list, int n_out, int64_t out_row_stride,
+                                      int64_t out_batch_stride, const uint16_t *q, int64_t q_row_stride,
+                                      int64_t q_batch_stride, const uint16_t *k, int64_t k_row_stride,
+                                      int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
+                                      int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads,
+                                      int n_kv_heads, int head_dim, float scale, int mask_kind, int q_offset,
+                                      int prefix_len, int window, float softcap, const int *window_starts,
+                                      int n_windows)
+{
+    if (!out_list || n_out < 1 || n_out > 8) return record(SMOL_B200_ERR_ARGS, "smol_b200_prefill_attention_multi");
+    return record(prefill_attention(static_cast<cudaStream_t>(stream), out_list[0], out_row_stride, out_batch_stride,
+                                    q, q_row_stride, q_batch_stride, k, k_row_stride, k_batch_stride, v, v_row_stride,
+                                    v_batch_stride, batch, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale,
+                                    mask_kind, q_offset, prefix_len, window, softcap, window_starts, n_windows,
+                                    out_list + 1, n_out - 1),
+                  "smol_b200_prefill_attention_multi");
+}
+
+int smol_b200_ipc_get_handle(const void *dev_ptr, void *handle64, size_t *offset)
+{
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    if (!dev_ptr || !handle64 || !offset) return record(SMOL_B200_ERR_ARGS, "smol_b200_ipc_get_handle");
+    cudaIpcMemHandle_t h;
+    if (!cuda_check(cudaIpcGetMemHandle(&h, const_cast<void *>(dev_ptr)), "cudaIpcGetMemHandle"))
+        return SMOL_B200_ERR_CUDA;
+    uintptr_t base = 0;
+    if (!allocation_base(dev_ptr, &base)) return record(SMOL_B200_ERR_CUDA, "smol_b200_ipc_get_handle");
+    memcpy(handle64, &h, sizeof(h));
+    *offset = reinterpret_cast<uintptr_t>(dev_ptr) - base;
+    return SMOL_B200_OK;
+}
+
+int smol_b200_ipc_open_handle(const void *handle64, void **dev_ptr)
+{
+    if (!handle64 || !dev_ptr) return record(SMOL_B200_ERR_ARGS, "smol_b200_ipc_open_handle");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle64, sizeof(h));
+    if (!cuda_check(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle"))
+        return SMOL_B200_ERR_CUDA;
+    return SMOL_B200_OK;
+}
+
+int smol_b200_ipc_close(void *dev_ptr)
+{
+    if (!dev_ptr) return SMOL_B200_OK;
+    return cuda_check(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle") ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
+}
+
 // ---------------------------------------------------------------------------
 // Part 4
 // ---------------------------------------------------------------------------

@@ -58,9 +58,16 @@ struct PrefillShape {
     static_assert(2 * BN + HD <= 512, "TMEM budget");
 };
 
+constexpr int kMaxExtraOuts = 7;   // further copies of the output (peers of an all-gather)
+
 struct PrefillParams {
     CUtensorMap tq, tk, tv;
     CUtensorMap to;                 // fp32 output, box 32 x 32 rows, 128B swizzle (v2 epilogue)
+    // Further destinations of every output row (v2), same strides as `out`: plain
+    // 16-byte stores, so a peer GPU's buffer mapped through CUDA IPC receives its copy
+    // over NVLink while later tiles compute.
+    float *out_more[kMaxExtraOuts];
+    int n_more;
     float *out;
     long long out_row_stride, out_batch_stride;
     const int *window_starts;
@@ -945,12 +952,19 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                         for (int i = 0; i < 32; ++i) rr[i] = 0u;
                     }
                     uint8_t *box = stage + c * (32 * 128);
+                    const bool peers = p.n_more > 0 && row_valid;   // rows past seq_q exist only in the staging
+                    const long long off = static_cast<long long>(it.b) * p.out_batch_stride +
+                                          static_cast<long long>(peers ? row : 0) * p.out_row_stride +
+                                          static_cast<long long>(head) * HD + c * 32;
 #pragma unroll
                     for (int q = 0; q < 8; ++q) {
                         float4 v = make_float4(__uint_as_float(rr[4 * q]) * inv, __uint_as_float(rr[4 * q + 1]) * inv,
                                                __uint_as_float(rr[4 * q + 2]) * inv,
                                                __uint_as_float(rr[4 * q + 3]) * inv);
                         *reinterpret_cast<float4 *>(box + sw128_offset(lane, q)) = v;
+                        if (peers)
+                            for (int o = 0; o < p.n_more; ++o)
+                                *reinterpret_cast<float4 *>(p.out_more[o] + off + 4 * q) = v;
                     }
                 }
                 fence_proxy_async_smem();
@@ -980,11 +994,15 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                         for (int i = 0; i < 32; ++i) rr[i] = 0u;
                     }
                     if (store) {
+                        const long long off = static_cast<long long>(it.b) * p.out_batch_stride +
+                                              static_cast<long long>(row) * p.out_row_stride +
+                                              static_cast<long long>(head) * HD + c * 32;
 #pragma unroll
                         for (int i = 0; i < 32; i += 4) {
                             float4 v = make_float4(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv,
                                                    __uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
                             *reinterpret_cast<float4 *>(orow + c * 32 + i) = v;
+                            for (int o = 0; o < p.n_more; ++o) *reinterpret_cast<float4 *>(p.out_more[o] + off + i) = v;
                         }
                     }
                 }
@@ -1061,7 +1079,7 @@ int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t 
                    int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
                    int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads, int n_kv_heads,
                    float scale, int mask_kind, int q_offset, int prefix_len, int window, float softcap,
-                   const int *window_starts, int n_windows)
+                   const int *window_starts, int n_windows, float *const *more_outs, int n_more)
 {
     using S = PrefillShape<HD>;
     PrefillParams p;
@@ -1088,6 +1106,8 @@ int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t 
         if (!make_tmap_3d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<int64_t>(n_heads) * HD, seq_q,
                           batch, out_row_stride, ob, 32, 32, 4))
             return SMOL_B200_ERR_CUDA;
+        p.n_more = n_more;
+        for (int i = 0; i < n_more; ++i) p.out_more[i] = more_outs[i];
     }
     p.out = out;
     p.out_row_stride = out_row_stride;
@@ -1155,9 +1175,13 @@ int prefill_attention(cudaStream_t st, float *out, int64_t out_row_stride, int64
                       int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
                       int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads, int n_kv_heads,
                       int head_dim, float scale, int mask_kind, int q_offset, int prefix_len, int window,
-                      float softcap, const int *window_starts, int n_windows)
+                      float softcap, const int *window_starts, int n_windows, float *const *more_outs, int n_more)
 {
     if (batch <= 0 || seq_q <= 0) return SMOL_B200_OK;
+    if (n_more < 0 || n_more > kMaxExtraOuts || (n_more > 0 && (!more_outs || head_dim == 256)))
+        return SMOL_B200_ERR_ARGS;
+    for (int i = 0; i < n_more; ++i)
+        if (!more_outs[i] || (reinterpret_cast<uintptr_t>(more_outs[i]) & 15)) return SMOL_B200_ERR_ARGS;
     if (!out || !q || !k || !v || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads != 0 || seq_k < 0 ||
         batch > 65535 || n_heads > 65535 || mask_kind < 0 || mask_kind > SMOL_MASK_FULL)
         return SMOL_B200_ERR_ARGS;
@@ -1176,7 +1200,7 @@ int prefill_attention(cudaStream_t st, float *out, int64_t out_row_stride, int64
 #define SMOL_PREFILL_ARGS                                                                                      \
     st, out, out_row_stride, out_batch_stride, q, q_row_stride, q_batch_stride, k, k_row_stride, k_batch_stride, \
         v, v_row_stride, v_batch_stride, batch, seq_q, seq_k, n_heads, n_kv_heads, scale,      \
-        mask_kind, q_offset, prefix_len, window, softcap, window_starts, n_windows
+        mask_kind, q_offset, prefix_len, window, softcap, window_starts, n_windows, more_outs, n_more
     switch (head_dim) {
     case 64: return launch_prefill<64>(SMOL_PREFILL_ARGS);
     case 128: return launch_prefill<128>(SMOL_PREFILL_ARGS);

@@ -66,6 +66,10 @@ DeviceCtx *ctx_for_current()
     return &c;
 }
 
+// cuMemGetAddressRange (cuda.h), also resolved through the runtime.
+typedef CUresult (*AddressRangeFn)(CUdeviceptr *, size_t *, CUdeviceptr);
+AddressRangeFn g_address_range = nullptr;
+
 bool encode_fn()
 {
     if (g_encode) return true;
@@ -103,6 +107,29 @@ StepPipe *step_pipe()
         c->pipe_init = true;
     }
     return &c->pipe;
+}
+
+bool allocation_base(const void *ptr, uintptr_t *base)
+{
+    if (!g_address_range) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !fn) {
+            cudaGetLastError();
+            set_error(SMOL_B200_ERR_CUDA, "cuMemGetAddressRange entry point not found");
+            return false;
+        }
+        g_address_range = reinterpret_cast<AddressRangeFn>(fn);
+    }
+    CUdeviceptr b = 0;
+    size_t sz = 0;
+    if (g_address_range(&b, &sz, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) {
+        set_error(SMOL_B200_ERR_CUDA, "cuMemGetAddressRange failed");
+        return false;
+    }
+    *base = static_cast<uintptr_t>(b);
+    return true;
 }
 
 void set_error(int code, const char *what)

@@ -28,6 +28,8 @@ cudaStream_t legacy_stream();
 void *legacy_scratch(int slot, size_t bytes);
 // True when `p` is device or managed memory the current device can address.
 bool is_device_pointer(const void *p);
+// Base address of the device allocation that contains ptr (cuMemGetAddressRange).
+bool allocation_base(const void *ptr, uintptr_t *base);
 // Number of the current device, or -1 (error recorded) when none is usable.
 int current_device();
 
@@ -53,7 +55,8 @@ int prefill_attention(cudaStream_t st, float *out, int64_t out_row_stride, int64
                       int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
                       int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads, int n_kv_heads,
                       int head_dim, float scale, int mask_kind, int q_offset, int prefix_len, int window,
-                      float softcap, const int *window_starts, int n_windows);
+                      float softcap, const int *window_starts, int n_windows, float *const *more_outs = nullptr,
+                      int n_more = 0);
 
 int qknorm_rope_append(cudaStream_t st, const float *q_in, const float *k_in, const float *v_in, int n_tokens,
                        int n_heads, int n_kv_heads, int head_dim, const float *q_norm_w, const float *k_norm_w,

@@ -90,6 +90,13 @@ _SIGNATURES = {
     "smol_b200_argmax_bf16": (_c_int, [_c_void, _c_void, _c_void, _c_i64, _c_void, _c_int, _c_int, _c_int, _c_void,
                                        _c_size]),
     "smol_b200_argmax_workspace_bytes": (_c_size, [_c_int, _c_int]),
+    "smol_b200_prefill_attention_multi": (
+        _c_int, [_c_void, _c_void, _c_int, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void,
+                 _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _c_int, _c_int,
+                 _c_int, _c_float, _c_void, _c_int]),
+    "smol_b200_ipc_get_handle": (_c_int, [_c_void, _c_void, ctypes.POINTER(ctypes.c_size_t)]),
+    "smol_b200_ipc_open_handle": (_c_int, [_c_void, ctypes.POINTER(ctypes.c_void_p)]),
+    "smol_b200_ipc_close": (_c_int, [_c_void]),
 }
 
 
@@ -339,3 +346,41 @@ def argmax_bf16(tokens_out, x, ldx, emb, vocab, k_dim, n_seqs, workspace, stream
     check(lib().smol_b200_argmax_bf16(_stream(stream), _ptr(tokens_out), _ptr(x), ldx, _ptr(emb), vocab, k_dim, n_seqs,
                                       _ptr(workspace), workspace.numel() * workspace.element_size()),
           "smol_b200_argmax_bf16")
+
+
+# ---------------------------------------------------------------------------
+# Prefill with several output destinations (fused all-gather) and CUDA IPC
+# ---------------------------------------------------------------------------
+def prefill_attention_multi(out_ptrs, row_stride, batch_stride, q, k, v, batch, seq_q, seq_k, n_heads, n_kv_heads,
+                            head_dim, scale, mask_kind=MASK_CAUSAL, q_offset=0, prefix_len=0, window=0, softcap=0.0,
+                            strides=None, stream=None):
+    """out_ptrs: device addresses (ints) of every destination, same strides (elements)."""
+    if strides is None:
+        strides = ((n_heads * head_dim, seq_q * n_heads * head_dim), (n_kv_heads * head_dim, seq_k * n_kv_heads * head_dim),
+                   (n_kv_heads * head_dim, seq_k * n_kv_heads * head_dim))
+    (qs, qb), (ks, kb), (vs, vb) = strides
+    arr = (ctypes.c_void_p * len(out_ptrs))(*out_ptrs)
+    rc = lib().smol_b200_prefill_attention_multi(
+        _stream(stream), ctypes.cast(arr, ctypes.c_void_p), len(out_ptrs), row_stride, batch_stride, _ptr(q), qs, qb,
+        _ptr(k), ks, kb, _ptr(v), vs, vb, batch, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale, mask_kind,
+        q_offset, prefix_len, window, softcap, None, 0)
+    check(rc, "smol_b200_prefill_attention_multi")
+
+
+def ipc_handle(t) -> tuple[bytes, int]:
+    """(64-byte handle of the allocation holding t, t's byte offset inside it)."""
+    buf = ctypes.create_string_buffer(64)
+    off = ctypes.c_size_t()
+    check(lib().smol_b200_ipc_get_handle(_ptr(t), buf, ctypes.byref(off)), "smol_b200_ipc_get_handle")
+    return buf.raw, off.value
+
+
+def ipc_open(handle: bytes) -> int:
+    ptr = ctypes.c_void_p()
+    buf = ctypes.create_string_buffer(handle, 64)
+    check(lib().smol_b200_ipc_open_handle(buf, ctypes.byref(ptr)), "smol_b200_ipc_open_handle")
+    return ptr.value
+
+
+def ipc_close(ptr: int) -> None:
+    check(lib().smol_b200_ipc_close(ptr), "smol_b200_ipc_close")
