@@ -80,12 +80,11 @@ struct PrefillParams {
 };
 
 struct Barriers {
-    uint64_t q_full;
+    uint64_t q_full, q_empty;
     uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
     uint64_t s_full[2], p_full[2];
     uint64_t o_done, mma_done;
     uint32_t tmem_base;
-    int lo_min, hi_max;
 };
 
 __device__ __forceinline__ float fast_exp2(float x)
@@ -128,18 +127,64 @@ __device__ __forceinline__ void row_range(const PrefillParams &p, int i, int &lo
     if (hi < lo) hi = lo;
 }
 
+// Work item k of a v1 launch: (query tile qt, head h, batch b), query tiles fastest --
+// in decreasing order of work for causal-like masks -- so that CTAs running at the same
+// time share one (batch, KV head)'s K and V in L2.  A persistent CTA takes the items
+// of rounds r = 0, 1, ... at positions blockIdx.x (even rounds) and gridDim.x-1-blockIdx.x
+// (odd rounds).
+struct Item1 {
+    int qt, h, b, q0;
+    int lo_min, n_tiles;   // key tiles [lo_min, lo_min + n_tiles*BN) cover every row's keys
+};
+
+template <int BN>
+__device__ __forceinline__ Item1 item1_geometry(const PrefillParams &p, int k)
+{
+    Item1 it;
+    const int nq = p.n_qblocks;
+    it.qt = p.heavy_first ? nq - 1 - k % nq : k % nq;
+    const int r = k / nq;
+    it.h = r % p.n_ygroups;
+    it.b = r / p.n_ygroups;
+    it.q0 = it.qt * kBM;
+    // every mask's [lo, hi) is non-decreasing in the row: first row -> lowest key, last row -> highest
+    int a = it.q0, z = min(it.q0 + kBM, p.seq_q) - 1;
+    if (p.mask_kind == SMOL_MASK_WINDOWS) {
+        a = max(a, p.window_starts[0]);
+        z = min(z, p.window_starts[p.n_windows] - 1);
+    }
+    it.lo_min = 0;
+    it.n_tiles = 0;
+    if (z >= a) {
+        int lo_a, hi_a, lo_z, hi_z;
+        bool w;
+        row_range(p, a, lo_a, hi_a, w);
+        row_range(p, z, lo_z, hi_z, w);
+        if (hi_z > lo_a) {
+            it.lo_min = lo_a;
+            it.n_tiles = (hi_z - lo_a + BN - 1) / BN;
+        }
+    }
+    return it;
+}
+
+__device__ __forceinline__ int item1_index(int r)
+{
+    const int c = (r & 1) ? static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x)
+                          : static_cast<int>(blockIdx.x);
+    return r * static_cast<int>(gridDim.x) + c;
+}
+
+// v1 (head dim 256): one 128-row query tile per work item; CTAs are persistent -- TMEM
+// is allocated once and every barrier's phase runs on across items (q_full / q_empty
+// once per item with key tiles, the K/V ring, S buffers and o_done once per key tile).
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p)
 {
     using S = PrefillShape<HD>;
     constexpr int BN = S::BN;
-
-    const int n_qtiles = gridDim.x;
-    const int qt = n_qtiles - 1 - static_cast<int>(blockIdx.x);   // heaviest (causal) tiles first
-    const int h = blockIdx.y;
-    const int b = blockIdx.z;
-    const int q0 = qt * kBM;
-    const int kvh = h / p.group;
+    const int n_items = p.n_qblocks * p.n_ygroups * p.batch;
+    const int n_rounds = (n_items + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -148,9 +193,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
     const int warp = threadIdx.x / 32;
     const int lane = threadIdx.x % 32;
 
-    // ---- set-up: barriers, key range of the tile, TMEM ----
     if (threadIdx.x == 0) {
         mbar_init(smem_u32(&bars->q_full), 1);
+        mbar_init(smem_u32(&bars->q_empty), 1);
         for (int s = 0; s < 2; ++s) {
             mbar_init(smem_u32(&bars->k_full[s]), 1);
             mbar_init(smem_u32(&bars->k_empty[s]), 1);
@@ -161,33 +206,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
         mbar_init(smem_u32(&bars->o_done), 1);
         mbar_init(smem_u32(&bars->mma_done), 1);
-        bars->lo_min = 0x7fffffff;
-        bars->hi_max = 0;
         fence_mbar_init();
     }
     if (warp == kMmaWarp) {
         tmem_alloc(smem_u32(&bars->tmem_base), S::kTmCols);
         tmem_relinquish();
     }
-    int my_lo = 0, my_hi = 0;
-    bool my_written = false;
-    const int row = q0 + threadIdx.x;   // meaningful for softmax threads
-    const bool row_valid = threadIdx.x < kSoftmaxThreads && row < p.seq_q;
-    __syncthreads();
-    if (row_valid) {
-        row_range(p, row, my_lo, my_hi, my_written);
-        if (my_hi > my_lo) {
-            atomicMin(&bars->lo_min, my_lo);
-            atomicMax(&bars->hi_max, my_hi);
-        }
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
-    const int lo_min = bars->lo_min;
-    const int hi_max = bars->hi_max;
-    const int n_tiles = hi_max > lo_min ? (hi_max - lo_min + BN - 1) / BN : 0;
 
     uint8_t *sQ = smem + S::kOffQ;
     uint8_t *sK = smem + S::kOffK;
@@ -195,97 +223,114 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 
     if (warp == kProducerWarp) {
         // ================= TMA producer =================
-        if (lane == 0 && n_tiles > 0) {
+        if (lane == 0) {
             tma_prefetch_desc(&p.tq);
             tma_prefetch_desc(&p.tk);
             tma_prefetch_desc(&p.tv);
-            const uint32_t qb = smem_u32(&bars->q_full);
-            mbar_arrive_expect_tx(qb, S::kQBytes);
-#pragma unroll
-            for (int sub = 0; sub < S::kSub; ++sub)
-                tma_load_3d(smem_u32(sQ + sub * S::kQSubBytes), &p.tq, qb, h * HD + sub * 64, q0, b);
-            int kiss = 0, viss = 0;
+            int qit = 0, g = 0;
             bool ok = true;
-            for (int j = 0; j < n_tiles && ok; ++j) {
-                const int st = j & 1;
-                const int key0 = lo_min + j * BN;
-                if (j >= 2 && !mbar_wait(smem_u32(&bars->k_empty[st]), ((j >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty)) {
-                    ok = false;
+            for (int r = 0; r < n_rounds && ok; ++r) {
+                const int k = item1_index(r);
+                if (k >= n_items) break;
+                const Item1 it = item1_geometry<BN>(p, k);
+                if (it.n_tiles == 0) continue;
+                // this item's Q overwrites the last one's: wait for its final S MMA
+                if (qit > 0 && !(ok = mbar_wait(smem_u32(&bars->q_empty), (qit - 1) & 1, p.err, kErrWaitTmaEmpty)))
                     break;
-                }
-                const uint32_t kb = smem_u32(&bars->k_full[st]);
-                mbar_arrive_expect_tx(kb, S::kKvBytes);
+                const uint32_t qb = smem_u32(&bars->q_full);
+                mbar_arrive_expect_tx(qb, S::kQBytes);
 #pragma unroll
                 for (int sub = 0; sub < S::kSub; ++sub)
-                    tma_load_3d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb,
-                                kvh * HD + sub * 64, key0, b);
-                ++kiss;
-                if (j >= 2 && !mbar_wait(smem_u32(&bars->v_empty[st]), ((j >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t vb = smem_u32(&bars->v_full[st]);
-                mbar_arrive_expect_tx(vb, S::kKvBytes);
+                    tma_load_3d(smem_u32(sQ + sub * S::kQSubBytes), &p.tq, qb, it.h * HD + sub * 64, it.q0, it.b);
+                ++qit;
+                const int kvh = it.h / p.group;
+                for (int j = 0; j < it.n_tiles; ++j, ++g) {
+                    const int st = g & 1;
+                    const int key0 = it.lo_min + j * BN;
+                    if (g >= 2 &&
+                        !(ok = mbar_wait(smem_u32(&bars->k_empty[st]), ((g >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty)))
+                        break;
+                    const uint32_t kb = smem_u32(&bars->k_full[st]);
+                    mbar_arrive_expect_tx(kb, S::kKvBytes);
 #pragma unroll
-                for (int sub = 0; sub < S::kSub; ++sub)
-                    tma_load_3d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb,
-                                kvh * HD + sub * 64, key0, b);
-                ++viss;
+                    for (int sub = 0; sub < S::kSub; ++sub)
+                        tma_load_3d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb,
+                                    kvh * HD + sub * 64, key0, it.b);
+                    if (g >= 2 &&
+                        !(ok = mbar_wait(smem_u32(&bars->v_empty[st]), ((g >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty)))
+                        break;
+                    const uint32_t vb = smem_u32(&bars->v_full[st]);
+                    mbar_arrive_expect_tx(vb, S::kKvBytes);
+#pragma unroll
+                    for (int sub = 0; sub < S::kSub; ++sub)
+                        tma_load_3d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb,
+                                    kvh * HD + sub * 64, key0, it.b);
+                }
             }
             // Drain: whatever was issued must land before the CTA can exit.
-            mbar_wait(smem_u32(&bars->q_full), 0, p.err, kErrDrain);
-            for (int j = max(0, kiss - 2); j < kiss; ++j)
+            if (qit > 0) mbar_wait(smem_u32(&bars->q_full), (qit - 1) & 1, p.err, kErrDrain);
+            for (int j = max(0, g - 2); j < g; ++j) {
                 if (!mbar_wait(smem_u32(&bars->k_full[j & 1]), (j >> 1) & 1, p.err, kErrDrain)) break;
-            for (int j = max(0, viss - 2); j < viss; ++j)
                 if (!mbar_wait(smem_u32(&bars->v_full[j & 1]), (j >> 1) & 1, p.err, kErrDrain)) break;
+            }
         }
     } else if (warp == kMmaWarp) {
         // ================= tcgen05 issuer (one thread) =================
-        if (lane == 0 && n_tiles > 0) {
+        if (lane == 0) {
             constexpr uint32_t idesc_s = umma_idesc_f16(kBM, BN, true, false);
             constexpr uint32_t idesc_pv = umma_idesc_f16(kBM, HD, false, true);
             const uint32_t q_addr = smem_u32(sQ);
-            bool ok = mbar_wait(smem_u32(&bars->q_full), 0, p.err, kErrWaitTmaFull);
-            auto issue_pv = [&](int i) -> bool {
-                const int st = i & 1;
-                if (!mbar_wait(smem_u32(&bars->p_full[st]), (i >> 1) & 1, p.err, kErrWaitSoftmax)) return false;
-                if (!mbar_wait(smem_u32(&bars->v_full[st]), (i >> 1) & 1, p.err, kErrWaitTmaFull)) return false;
+            // O += P(g) V(g); `first` starts the accumulation of an item
+            auto issue_pv = [&](int g, bool first) -> bool {
+                const int st = g & 1;
+                if (!mbar_wait(smem_u32(&bars->p_full[st]), (g >> 1) & 1, p.err, kErrWaitSoftmax)) return false;
+                if (!mbar_wait(smem_u32(&bars->v_full[st]), (g >> 1) & 1, p.err, kErrWaitTmaFull)) return false;
                 tc_fence_after();
                 const uint32_t v_addr = smem_u32(sV + st * S::kKvBytes);
                 const uint32_t p_col = tmem + (st ? S::kTmS1 : S::kTmS0);
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
                     const uint64_t bdesc = umma_sdesc_sw128(v_addr + kk * 16 * 128, S::kKvSubBytes, 1024);
-                    umma_ts(tmem + S::kTmO, p_col + kk * 8, bdesc, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+                    umma_ts(tmem + S::kTmO, p_col + kk * 8, bdesc, idesc_pv, (!first || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(smem_u32(&bars->o_done));
                 umma_commit(smem_u32(&bars->v_empty[st]));
                 return true;
             };
-            for (int j = 0; j < n_tiles && ok; ++j) {
-                const int st = j & 1;
-                if (!mbar_wait(smem_u32(&bars->k_full[st]), (j >> 1) & 1, p.err, kErrWaitTmaFull)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t k_addr = smem_u32(sK + st * S::kKvBytes);
-                const uint32_t s_col = tmem + (st ? S::kTmS1 : S::kTmS0);
+            int qit = 0, g0 = 0;
+            bool ok = true;
+            for (int r = 0; r < n_rounds && ok; ++r) {
+                const int k = item1_index(r);
+                if (k >= n_items) break;
+                const Item1 it = item1_geometry<BN>(p, k);
+                const int n = it.n_tiles;
+                if (n == 0) continue;
+                ok = mbar_wait(smem_u32(&bars->q_full), qit & 1, p.err, kErrWaitTmaFull);
+                // O is overwritten by the item's first PV: its readers (the previous item's
+                // epilogue) are the threads whose p_full arrival that PV waits for.
+                for (int j = 0; j < n && ok; ++j) {
+                    const int g = g0 + j;
+                    const int st = g & 1;
+                    if (!(ok = mbar_wait(smem_u32(&bars->k_full[st]), (g >> 1) & 1, p.err, kErrWaitTmaFull))) break;
+                    tc_fence_after();
+                    const uint32_t k_addr = smem_u32(sK + st * S::kKvBytes);
+                    const uint32_t s_col = tmem + (st ? S::kTmS1 : S::kTmS0);
 #pragma unroll
-                for (int kk = 0; kk < HD / 16; ++kk) {
-                    const uint32_t off = (kk & 3) * 32;   // 16 halves = 32 B along K
-                    const uint64_t adesc = umma_sdesc_sw128(q_addr + (kk >> 2) * S::kQSubBytes + off, 16, 1024);
-                    const uint64_t bdesc = umma_sdesc_sw128(k_addr + (kk >> 2) * S::kKvSubBytes + off, 16, 1024);
-                    umma_ss(s_col, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+                    for (int kk = 0; kk < HD / 16; ++kk) {
+                        const uint32_t off = (kk & 3) * 32;   // 16 halves = 32 B along K
+                        const uint64_t adesc = umma_sdesc_sw128(q_addr + (kk >> 2) * S::kQSubBytes + off, 16, 1024);
+                        const uint64_t bdesc = umma_sdesc_sw128(k_addr + (kk >> 2) * S::kKvSubBytes + off, 16, 1024);
+                        umma_ss(s_col, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+                    }
+                    umma_commit(smem_u32(&bars->s_full[st]));
+                    umma_commit(smem_u32(&bars->k_empty[st]));
+                    if (j + 1 == n) umma_commit(smem_u32(&bars->q_empty));   // the item's last S read Q
+                    if (j >= 1 && !(ok = issue_pv(g - 1, j == 1))) break;
                 }
-                umma_commit(smem_u32(&bars->s_full[st]));
-                umma_commit(smem_u32(&bars->k_empty[st]));
-                if (j >= 1 && !issue_pv(j - 1)) {
-                    ok = false;
-                    break;
-                }
+                if (ok) ok = issue_pv(g0 + n - 1, n == 1);
+                g0 += n;
+                ++qit;
             }
-            if (ok) issue_pv(n_tiles - 1);
             // Every MMA must be complete before TMEM is released.
             umma_commit(smem_u32(&bars->mma_done));
             mbar_wait(smem_u32(&bars->mma_done), 0, p.err, kErrDrain);
@@ -298,112 +343,129 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         const float cap = p.softcap;
         const float inv_cap = cap > 0.f ? 1.f / cap : 0.f;
         const float kLog2e = 1.4426950408889634f;
-        float m = -INFINITY;   // running maximum in log2 units
-        float l = 0.f;
+        int g0 = 0;
         bool ok = true;
-        for (int j = 0; j < n_tiles; ++j) {
-            const int st = j & 1;
-            ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->s_full[st]), (j >> 1) & 1, p.err, kErrWaitMma));
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t s_col = lane_base + (st ? S::kTmS1 : S::kTmS0);
-            float t[BN];
-            {
-                uint32_t r[32];
-#pragma unroll
-                for (int c = 0; c < BN / 32; ++c) {
-                    tmem_ld32(s_col + c * 32, r);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(r[i]);
-                }
-            }
-            const int key0 = lo_min + j * BN;
-            const bool full_tile = row_valid && key0 >= my_lo && key0 + BN <= my_hi;
-            float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                float x = t[c];
-                if (cap > 0.f) x = cap * tanhf(x * p.scale * inv_cap) * kLog2e;
-                else x = x * p.scale_log2;
-                if (!full_tile) {
-                    const int key = key0 + c;
-                    if (!row_valid || key < my_lo || key >= my_hi) x = -INFINITY;
-                }
-                t[c] = x;
-                mx = fmaxf(mx, x);
-            }
-            // The running maximum moves only when the row maximum grew by > 2^8 (or on the
-            // first tile with a visible key, when O of this row is still zero).
-            const bool need = m != -INFINITY && mx > m + kRescaleThreshold;
-            if (__any_sync(0xffffffffu, need)) {
-                // O holds P_0..P_{j-1} V: wait for PV_{j-1}, then rescale the rows that need it.
-                ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done), (j - 1) & 1, p.err, kErrWaitMma));
+        for (int r = 0; r < n_rounds && ok; ++r) {
+            const int k = item1_index(r);
+            if (k >= n_items) break;
+            const Item1 it = item1_geometry<BN>(p, k);
+            const int n_tiles = it.n_tiles;
+            const int row = it.q0 + threadIdx.x;
+            const bool row_valid = row < p.seq_q;
+            int my_lo = 0, my_hi = 0;
+            bool my_written = false;
+            if (row_valid) row_range(p, row, my_lo, my_hi, my_written);
+            float m = -INFINITY;   // running maximum in log2 units
+            float l = 0.f;
+            for (int j = 0; j < n_tiles; ++j) {
+                const int g = g0 + j;
+                const int st = g & 1;
+                ok = __all_sync(0xffffffffu,
+                                mbar_wait(smem_u32(&bars->s_full[st]), (g >> 1) & 1, p.err, kErrWaitMma));
                 if (!ok) break;
                 tc_fence_after();
-                const float f = need ? fast_exp2(m - mx) : 1.f;
-                uint32_t r[32];
+                const uint32_t s_col = lane_base + (st ? S::kTmS1 : S::kTmS0);
+                float t[BN];
+                {
+                    uint32_t rr[32];
 #pragma unroll
-                for (int c = 0; c < HD / 32; ++c) {
-                    tmem_ld32(lane_base + S::kTmO + c * 32, r);
-                    tmem_ld_wait();
+                    for (int c = 0; c < BN / 32; ++c) {
+                        tmem_ld32(s_col + c * 32, rr);
+                        tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * f);
-                    tmem_st32(lane_base + S::kTmO + c * 32, r);
-                }
-                l *= f;
-            }
-            if (need || (m == -INFINITY && mx > -INFINITY)) m = mx;
-            // P = exp2(t - m) as fp16 pairs over the first BN/2 columns of this S buffer.
-            float psum = 0.f;
-            {
-                const bool live = m != -INFINITY;
-                uint32_t r[32];
-#pragma unroll
-                for (int c = 0; c < BN / 64; ++c) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const float e0 = live ? fast_exp2(t[c * 64 + 2 * i] - m) : 0.f;
-                        const float e1 = live ? fast_exp2(t[c * 64 + 2 * i + 1] - m) : 0.f;
-                        psum += e0 + e1;
-                        r[i] = pack_f16x2(e0, e1);
+                        for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(rr[i]);
                     }
-                    tmem_st32(s_col + c * 32, r);
+                }
+                const int key0 = it.lo_min + j * BN;
+                const bool full_tile = row_valid && key0 >= my_lo && key0 + BN <= my_hi;
+                float mx = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < BN; ++c) {
+                    float x = t[c];
+                    if (cap > 0.f) x = cap * tanhf(x * p.scale * inv_cap) * kLog2e;
+                    else x = x * p.scale_log2;
+                    if (!full_tile) {
+                        const int key = key0 + c;
+                        if (!row_valid || key < my_lo || key >= my_hi) x = -INFINITY;
+                    }
+                    t[c] = x;
+                    mx = fmaxf(mx, x);
+                }
+                // The running maximum moves only when the row maximum grew by > 2^8 (or on the
+                // first tile with a visible key, when O of this row is still zero).
+                const bool need = m != -INFINITY && mx > m + kRescaleThreshold;
+                if (__any_sync(0xffffffffu, need)) {
+                    // O holds P_0..P_{j-1} V: wait for the item's previous PV, then rescale.
+                    ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done), (g - 1) & 1, p.err, kErrWaitMma));
+                    if (!ok) break;
+                    tc_fence_after();
+                    const float f = need ? fast_exp2(m - mx) : 1.f;
+                    uint32_t rr[32];
+#pragma unroll
+                    for (int c = 0; c < HD / 32; ++c) {
+                        tmem_ld32(lane_base + S::kTmO + c * 32, rr);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * f);
+                        tmem_st32(lane_base + S::kTmO + c * 32, rr);
+                    }
+                    l *= f;
+                }
+                if (need || (m == -INFINITY && mx > -INFINITY)) m = mx;
+                // P = exp2(t - m) as fp16 pairs over the first BN/2 columns of this S buffer.
+                float psum = 0.f;
+                {
+                    const bool live = m != -INFINITY;
+                    uint32_t rr[32];
+#pragma unroll
+                    for (int c = 0; c < BN / 64; ++c) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            const float e0 = live ? fast_exp2(t[c * 64 + 2 * i] - m) : 0.f;
+                            const float e1 = live ? fast_exp2(t[c * 64 + 2 * i + 1] - m) : 0.f;
+                            psum += e0 + e1;
+                            rr[i] = pack_f16x2(e0, e1);
+                        }
+                        tmem_st32(s_col + c * 32, rr);
+                    }
+                }
+                l += psum;
+                tmem_st_wait();
+                tc_fence_before();
+                mbar_arrive(smem_u32(&bars->p_full[st]));
+            }
+            if (!ok) break;
+            // ---- epilogue: O / l -> out (fp32) ----
+            bool have_o = n_tiles > 0;
+            if (have_o)
+                have_o = ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done), (g0 + n_tiles - 1) & 1,
+                                                                 p.err, kErrWaitMma));
+            tc_fence_after();
+            const bool store = ok && row_valid && my_written;
+            float *orow = p.out + static_cast<long long>(it.b) * p.out_batch_stride +
+                          static_cast<long long>(store ? row : 0) * p.out_row_stride +
+                          static_cast<long long>(it.h) * HD;
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            uint32_t rr[32];
+#pragma unroll
+            for (int c = 0; c < HD / 32; ++c) {
+                if (have_o) {
+                    tmem_ld32(lane_base + S::kTmO + c * 32, rr);
+                    tmem_ld_wait();
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) rr[i] = 0u;
+                }
+                if (store) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4) {
+                        float4 v = make_float4(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv,
+                                               __uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
+                        *reinterpret_cast<float4 *>(orow + c * 32 + i) = v;
+                    }
                 }
             }
-            l += psum;
-            tmem_st_wait();
-            tc_fence_before();
-            mbar_arrive(smem_u32(&bars->p_full[st]));
-        }
-        // ---- epilogue: O / l -> out (fp32) ----
-        bool have_o = ok && n_tiles > 0;
-        if (have_o)
-            have_o = __all_sync(0xffffffffu,
-                                mbar_wait(smem_u32(&bars->o_done), (n_tiles - 1) & 1, p.err, kErrWaitMma));
-        tc_fence_after();
-        const bool store = ok && row_valid && my_written;
-        float *orow = p.out + static_cast<long long>(b) * p.out_batch_stride +
-                      static_cast<long long>(store ? row : 0) * p.out_row_stride + static_cast<long long>(h) * HD;
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        uint32_t r[32];
-#pragma unroll
-        for (int c = 0; c < HD / 32; ++c) {
-            if (have_o) {
-                tmem_ld32(lane_base + S::kTmO + c * 32, r);
-                tmem_ld_wait();
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) r[i] = 0u;
-            }
-            if (store) {
-#pragma unroll
-                for (int i = 0; i < 32; i += 4) {
-                    float4 v = make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
-                                           __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
-                    *reinterpret_cast<float4 *>(orow + c * 32 + i) = v;
-                }
-            }
+            g0 += n_tiles;
         }
     }
 
@@ -1137,8 +1199,16 @@ int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t 
                 return SMOL_B200_ERR_CUDA;
             attr_set[dev] = true;
         }
-        const int n_qtiles = (seq_q + kBM - 1) / kBM;
-        dim3 grid(n_qtiles, n_heads, batch);
+        // work items (query tile, head, batch), query tiles fastest; persistent CTAs
+        p.n_qblocks = (seq_q + kBM - 1) / kBM;
+        p.n_ygroups = n_heads;
+        p.batch = batch;
+        p.heavy_first = (mask_kind == SMOL_MASK_CAUSAL || mask_kind == SMOL_MASK_PREFIX_LM) ? 1 : 0;
+        const long long n_items = static_cast<long long>(p.n_qblocks) * n_heads * batch;
+        if (n_items > 0x7fffffffLL) return SMOL_B200_ERR_ARGS;
+        int grid = static_cast<int>(n_items);
+        const int sms = sm_count();
+        if (sms > 0 && grid > sms) grid = sms;
         prefill_kernel<HD><<<grid, kThreads, S::kSmemBytes, st>>>(p);
     } else {
         using S2 = Prefill2Shape<HD>;
