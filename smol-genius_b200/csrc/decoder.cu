@@ -17,8 +17,6 @@
 #include <stdlib.h>
 #include <string.h>
 
-#include <vector>
-
 #include "b200_common.cuh"
 #include "runtime.h"
 
