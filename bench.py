@@ -609,8 +609,8 @@ def run_decoder(pk, batch: int = 1, steps: int = 50) -> dict:
     return {"workload": f"Qwen3-0.6B-size decode step (28 layers, vocab 151936), batch {batch}, ~{P} cached tokens",
             "us_per_step": round(ms * 1e3, 1), "tokens_per_s": round(batch / (ms * 1e-3), 1),
             "bytes_per_step": weight_bytes + kv_bytes, "gbs": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
-            "kernels": "gemv_bf16_kernel, qknorm_rope_append, decode_split_kernel (cluster), argmax_rows_kernel; "
-                       "one CUDA graph per step"}
+            "kernels": "gemv_bf16_kernel, qknorm_rope_append, decode_split_kernel (cluster), "
+                       "argmax_part/final_kernel; one CUDA graph per step"}
 
 
 def run_other_configs(pk) -> dict:
