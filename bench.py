@@ -49,9 +49,9 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--prefill-gather", choices=["auto", "kernel", "nccl"], default="auto",
+    ap.add_argument("--prefill-gather", choices=["kernel", "nccl"], default="kernel",
                     help="N>1: all-gather the prefill outputs inside the kernel (stores to every peer) or with NCCL "
-                         "after it; auto = inside for 2 GPUs, NCCL beyond (measured faster at each)")
+                         "after it (measured: the in-kernel form is faster at 2, 4 and 8 GPUs)")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -283,7 +283,7 @@ def run_prefill(args, world, rank, pk):
     GPUs rank r owns KV heads r*8/N.. (and their Q heads) and the per-rank outputs are
     all-gathered once per layer: by the prefill kernel itself, which stores every output
     tile to its slot in each peer's gather buffer (CUDA IPC mappings, NVLink), or by a
-    separate NCCL all-gather (--prefill-gather; auto picks the faster for N)."""
+    separate NCCL all-gather (--prefill-gather nccl)."""
     import torch
 
     import smol_b200
@@ -302,9 +302,8 @@ def run_prefill(args, world, rank, pk):
     gathered = torch.empty((world,) + tuple(out.shape), device="cuda") if world > 1 else None
     stream = torch.cuda.current_stream()
     scale = 1 / np.sqrt(hd)
-    # Measured on one box: 2 GPUs 8.92 ms fused vs 9.34 ms NCCL; 8 GPUs 6.90 ms fused vs
-    # 3.67 ms NCCL (the per-thread stores to 7 peers stall the softmax warps).
-    fused = world > 1 and (args.prefill_gather == "kernel" or (args.prefill_gather == "auto" and world <= 2))
+    # Measured on one box (ms per layer, fused vs NCCL): 4 GPUs 4.37 vs 5.56, 8 GPUs 2.72 vs 3.71.
+    fused = world > 1 and args.prefill_gather == "kernel"
     opened, outs, check = [], None, None
     if world > 1:
         import torch.distributed as dist

@@ -563,11 +563,17 @@ int smol_b200_decode_step_host(void *stream, float *out_host, const float *q_hos
                                         P->d2h),
                         "copy out");
     }
-    // Drain all three streams before returning (also on failure: nothing of this call
-    // may still be in flight when the caller reuses its buffers).
-    const bool drained = cuda_check(cudaStreamSynchronize(P->h2d), "synchronize") &
-                         cuda_check(cudaStreamSynchronize(P->compute), "synchronize") &
-                         cuda_check(cudaStreamSynchronize(P->d2h), "synchronize");
+    // Nothing of this call may still be in flight when the caller reuses its buffers.
+    // On success the last copy-out waited (through events) for every chunk's compute,
+    // which waited for its copy-in, so draining the copy-out stream drains all three;
+    // after a failure part of that chain may be missing, so each stream is drained.
+    bool drained;
+    if (ok && rc == SMOL_B200_OK)
+        drained = cuda_check(cudaStreamSynchronize(P->d2h), "synchronize");
+    else
+        drained = cuda_check(cudaStreamSynchronize(P->h2d), "synchronize") &
+                  cuda_check(cudaStreamSynchronize(P->compute), "synchronize") &
+                  cuda_check(cudaStreamSynchronize(P->d2h), "synchronize");
     if (rc != SMOL_B200_OK) return record(rc, "smol_b200_decode_step_host");
     if (!ok || !drained) return SMOL_B200_ERR_CUDA;
     return SMOL_B200_OK;

@@ -1014,19 +1014,33 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                         for (int i = 0; i < 32; ++i) rr[i] = 0u;
                     }
                     uint8_t *box = stage + c * (32 * 128);
-                    const bool peers = p.n_more > 0 && row_valid;   // rows past seq_q exist only in the staging
-                    const long long off = static_cast<long long>(it.b) * p.out_batch_stride +
-                                          static_cast<long long>(peers ? row : 0) * p.out_row_stride +
-                                          static_cast<long long>(head) * HD + c * 32;
 #pragma unroll
                     for (int q = 0; q < 8; ++q) {
                         float4 v = make_float4(__uint_as_float(rr[4 * q]) * inv, __uint_as_float(rr[4 * q + 1]) * inv,
                                                __uint_as_float(rr[4 * q + 2]) * inv,
                                                __uint_as_float(rr[4 * q + 3]) * inv);
                         *reinterpret_cast<float4 *>(box + sw128_offset(lane, q)) = v;
-                        if (peers)
-                            for (int o = 0; o < p.n_more; ++o)
-                                *reinterpret_cast<float4 *>(p.out_more[o] + off + 4 * q) = v;
+                    }
+                }
+                __syncwarp();
+                if (p.n_more > 0) {
+                    // Further destinations (a peer GPU's buffer over NVLink): the warp copies its
+                    // 32 staged rows one row per instruction -- lane l takes the 16 bytes at
+                    // column 4l (16-byte unit l%8 of box l/8) -- so each store is a contiguous
+                    // run of the row, not 32 scattered 16-byte pieces.
+                    const int y0 = it.row0[tile] + (warp & 3) * 32;
+                    constexpr int kLanesPerRow = HD / 4;          // 16 (hd 64) or 32 (hd 128)
+                    constexpr int kRowsPerStep = 32 / kLanesPerRow;
+                    const int sub = lane / kLanesPerRow, col4 = lane % kLanesPerRow;
+                    for (int r0 = 0; r0 < 32; r0 += kRowsPerStep) {
+                        const int rr_ = r0 + sub, grow = y0 + rr_;
+                        if (grow >= p.seq_q) break;   // rows past the end exist only in the staging
+                        const float4 v = *reinterpret_cast<const float4 *>(stage + (col4 / 8) * (32 * 128) +
+                                                                           sw128_offset(rr_, col4 % 8));
+                        const long long off = static_cast<long long>(it.b) * p.out_batch_stride +
+                                              static_cast<long long>(grow) * p.out_row_stride +
+                                              static_cast<long long>(head) * HD + col4 * 4;
+                        for (int o = 0; o < p.n_more; ++o) *reinterpret_cast<float4 *>(p.out_more[o] + off) = v;
                     }
                 }
                 fence_proxy_async_smem();
