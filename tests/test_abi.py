@@ -108,3 +108,25 @@ def test_no_device_fails_loudly():
     assert np.all(out == 0.0)                   # zero-filled, never computed on the CPU
     smol_b200.clear_error()
     assert smol_b200.last_error() == 0
+
+
+def test_binding_signatures_match_header():
+    """Every prototype of include/smol_b200.h has a ctypes signature in the binding with
+    the same number of arguments and a matching return kind, so a changed C prototype
+    cannot silently mis-marshal calls (which only a GPU run would otherwise reveal)."""
+    import ctypes
+    import re
+    text = re.sub(r"/\*.*?\*/", "", open(smol_b200.HEADER_PATH).read(), flags=re.S)
+    protos = re.findall(r"SMOL_B200_API\s+([\w\s\*]+?)\b(\w+)\s*\(([^;]*?)\)\s*;", text, flags=re.S)
+    assert len(protos) == len(smol_b200.header_symbols())
+    kinds = {"void": None, "int": ctypes.c_int, "size_t": ctypes.c_size_t, "unsigned": ctypes.c_uint,
+             "const char *": ctypes.c_char_p}
+    for ret, name, args in protos:
+        args = args.strip()
+        n_args = 0 if args in ("", "void") else len(args.split(","))
+        assert name in smol_b200._SIGNATURES, name
+        res, argtypes = smol_b200._SIGNATURES[name]
+        assert len(argtypes) == n_args, (name, n_args, len(argtypes))
+        ret = " ".join(ret.split())
+        assert ret in kinds, (name, ret)
+        assert res == kinds[ret], (name, ret, res)
