@@ -4,11 +4,15 @@
 // window and softcap variants (:176-462), smol_bidirectional_attention (:32-77) and
 // the prefix-LM composition PaliGemma needs, as one kernel with a mask kind.
 //
-// One CTA owns a 128-row query tile of one head of one batch element and walks the
-// key range its rows can see in tiles of BN keys.  Warp roles (192 threads):
+// Two kernels.  v2 (head dims 64 and 128, below) computes two 128-row query tiles per
+// work item and ping-pongs the tensor pipe between them.  v1 (head dim 256, whose O
+// needs 256 TMEM columns) computes one: a work item is a 128-row query tile of one
+// head of one batch element, and the CTA walks the key range its rows can see in
+// tiles of BN keys.  Both run persistent CTAs over their work items (v2 for head dim
+// 64; head dim 128 launches one CTA per item).  v1 warp roles (192 threads):
 //   warps 0-3  softmax: thread t of warp w owns query row 32w+t, which is exactly
 //              TMEM lane 32w+t, so row max / row sum need no shuffles;
-//   warp 4     TMA producer: Q once, then K and V tiles through 2-slot rings;
+//   warp 4     TMA producer: each item's Q, then K and V tiles through 2-slot rings;
 //   warp 5     TMEM allocator and single-thread tcgen05.mma issuer.
 // Per key tile j:
 //   S_j = Q K_j^T    kind::f16, bf16 A/B from 128B-swizzled shared memory, fp32 in TMEM
