@@ -203,8 +203,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_co
 #pragma unroll
             for (int i = 0; i < R; ++i) {
                 if (rg * R + i >= p.total_rows) break;
+                // this warp reads the 512-byte pieces slice, slice+S, ... of the row: lane l
+                // takes 128-byte line l%4 of piece slice + (l/4)*S, 8 pieces per pass
                 const char *row = reinterpret_cast<const char *>(row_ref(p, rg * R + i, k_dim).w);
-                for (int off = (slice * 32 + lane) * 512; off < k_dim * 2; off += S * 32 * 512)
+                for (int off = (slice + (lane / 4) * S) * 512 + (lane % 4) * 128; off < k_dim * 2;
+                     off += 8 * S * 512)
                     asm volatile("prefetch.global.L2 [%0];" ::"l"(row + off));
             }
         }
