@@ -3,12 +3,15 @@
  * of tmzt/smol-genius) through qkn_decoder_prefill / qkn_decoder_forward with a seeded,
  * synthetic Qwen3-shaped model, and prints the greedy tokens.
  *
- * oracle/Makefile links this file twice:
+ * oracle/Makefile links this file three times:
  *   qkn_dropin_ref   -- with every reference kernel object (the baseline);
  *   qkn_dropin_b200  -- with the reference objects minus attention.o, rope.o and
  *                       rmsnorm.o, and with libsmol_b200.so in their place, exactly as
- *                       INTEGRATION.md tells a maintainer to link the exports.
- * The test compares the two token streams.  Nothing in the reference changes.
+ *                       a maintainer links the exports (those three sources
+ *                       filtered out of libsmol.a's list, -lsmol_b200 added);
+ *   qkn_dropin_emul  -- with every reference object and smol_causal_attention wrapped
+ *                       (cache_precision_wrap.c) to attend over bf16 K / fp16 V values.
+ * The tests compare the token streams.  Nothing in the reference changes.
  *
  * Usage: qkn_dropin_xxx [prefill_len=512] [steps=128] [seed=2] [qk_gain=4] [vo_gain=2] [layers=1] [copy=1]
  *

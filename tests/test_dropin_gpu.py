@@ -6,7 +6,7 @@ and kernels three times:
 
   qkn_dropin_ref   every reference kernel, fp32 host KV cache (the unmodified path);
   qkn_dropin_b200  attention.c, rope.c and rmsnorm.c left out and -lsmol_b200 linked
-                   instead (the recipe INTEGRATION.md gives maintainers): every
+                   instead (the recipe a maintainer uses for the exports): every
                    attention, RoPE and RMSNorm call of the decoder runs on the GPU;
   qkn_dropin_emul  the reference kernels, with smol_causal_attention wrapped
                    (cache_precision_wrap.c) to round K to bf16, V to fp16 and prefill Q
