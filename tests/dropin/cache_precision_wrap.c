@@ -9,6 +9,10 @@
  * rounded values.  The binary built from this (qkn_dropin_emul) shows how far the
  * cache precision alone moves each step's logits, which bounds the top-2 margin a
  * drop-in token-identity test needs.
+ *
+ * Built with -DSMOL_WRAP_FP32_Q, prefill Q stays fp32 as well: that is the precision
+ * of the decoder-step oracle's prefill (oracle/qkn_decoder_oracle.py), which the
+ * qkn_weights_emul binary pins to the reference.
  */
 #include <stdint.h>
 #include <stdlib.h>
@@ -42,7 +46,12 @@ void __wrap_smol_causal_attention(float *out, const float *Q, const float *K, co
     size_t kv_n = (size_t)seq_k * n_kv_heads * head_dim;
     size_t q_n = (size_t)seq_q * n_heads * head_dim;
     float *k = rounded(K, kv_n, 0), *v = rounded(V, kv_n, 1);
+#ifdef SMOL_WRAP_FP32_Q
+    float *q = NULL;
+    (void)q_n;
+#else
     float *q = seq_q > 1 ? rounded(Q, q_n, 0) : NULL;
+#endif
     __real_smol_causal_attention(out, q ? q : Q, k, v, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale, q_offset);
     free(k);
     free(v);

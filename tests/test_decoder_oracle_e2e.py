@@ -1,0 +1,92 @@
+"""Pins the whole decoder-step restatement (oracle/qkn_decoder_oracle.py) to the reference decoder.
+
+The oracle's seeded model is written to a file and run by oracle/_ref/qkn_weights_emul:
+the reference's own qkn_decoder_prefill / qkn_decoder_forward (qkn_decoder.c:369-714)
+with its kernels, attention over the cache formats the oracle also keeps (K bf16, V
+fp16).  Both sides are teacher-forced on the same tokens, so every step is compared
+on the same history: the greedy token wherever the top-2 logit margin exceeds the
+difference the hidden states allow, and the final normalised hidden state within
+rel-L2 3e-3 at every step and 1e-4 / 1e-3 (one / two layers) at the median.
+
+The tolerance is that of storage rounding, not of the restatement: a cache element
+whose fp32 value lies within the accumulation-order difference (~1e-6) of a bf16
+rounding boundary is stored one bf16 unit (2^-8) apart, and the sharp attention of
+this model (QK-norm gain 3) carries that to the output.  The oracle against itself
+with float64 instead of float32 accumulation in its matrix products differs by the
+same amount: up to 1.4e-4 (one layer) and 1.5e-3 (two layers, where layer 1's cache
+is fed by layer 0's prefill attention), median 8e-6 / 5e-4.  CPU only; skipped where
+the binary was not built.
+"""
+import os
+import struct
+import subprocess
+
+import numpy as np
+import pytest
+
+import pyoracle
+from qkn_decoder_oracle import QknOracle
+
+BIN = os.path.join(os.path.dirname(pyoracle.__file__), "_ref", "qkn_weights_emul")
+pytestmark = pytest.mark.skipif(not os.path.exists(BIN), reason="oracle/_ref/qkn_weights_emul not built")
+
+THETA, EPS = 1e6, 1e-6
+
+
+def _write_model(path, m: QknOracle, prompt, feed):
+    bits = lambda a: np.ascontiguousarray(pyoracle.bf16_bits(a)).tobytes()        # noqa: E731
+    f32 = lambda a: np.ascontiguousarray(a, dtype=np.float32).tobytes()              # noqa: E731
+    with open(path, "wb") as f:
+        f.write(b"QKNW")
+        f.write(struct.pack("<9i", m.H, m.L, m.HQ, m.HKV, m.HD, m.I, m.V, len(prompt), len(feed)))
+        f.write(struct.pack("<2f", EPS, THETA))
+        f.write(bits(m.E))
+        f.write(f32(m.final_norm))
+        for lw in m.layers:
+            for name in ("wq", "wk", "wv", "wo", "gate_up", "down"):
+                f.write(bits(lw[name]))
+            for name in ("input_norm", "post_attn_norm", "q_norm", "k_norm"):
+                f.write(f32(lw[name]))
+        f.write(np.asarray(prompt, "<i4").tobytes())
+        f.write(np.asarray(feed, "<i4").tobytes())
+
+
+def _read_steps(path, n_steps, hidden):
+    raw = np.fromfile(path, dtype=np.uint8).reshape(n_steps, 4 + 4 * hidden)
+    tokens = raw[:, :4].copy().view("<i4")[:, 0]
+    xs = raw[:, 4:].copy().view("<f4")
+    return tokens, xs
+
+
+@pytest.mark.parametrize("layers,prompt_len,steps,seed", [(1, 96, 24, 11), (2, 64, 24, 12)])
+def test_oracle_decoder_matches_reference_decoder(tmp_path, layers, prompt_len, steps, seed):
+    m = QknOracle(layers=layers, seed=seed, qk_gain=3.0, vo_gain=4.0, cap=prompt_len + steps + 8,
+                  theta=THETA, eps=EPS)
+    rng = np.random.default_rng(seed)
+    prompt = rng.integers(0, m.V, prompt_len).tolist()
+    m.prefill(prompt[:-1])
+    feed, tokens, margins, xs = [prompt[-1]], [], [], []
+    for _ in range(steps):
+        tok, margin, xf = m.forward(feed[-1])
+        tokens.append(tok)
+        margins.append(margin)
+        xs.append(xf)
+        feed.append(tok)
+    feed = feed[:steps]
+
+    inp, out = tmp_path / "model.bin", tmp_path / "steps.bin"
+    _write_model(inp, m, prompt, feed)
+    subprocess.run([BIN, str(inp), str(out)], check=True, timeout=300)
+    ref_tokens, ref_xs = _read_steps(out, steps, m.H)
+
+    e_norm = float(np.max(np.linalg.norm(m.E, axis=1)))
+    errs = [pyoracle.rel_l2(xs[s], ref_xs[s]) for s in range(steps)]
+    assert max(errs) < 3e-3, errs
+    assert float(np.median(errs)) < (1e-4 if layers == 1 else 1e-3), errs
+    for s in range(steps):
+        # |logit difference| <= |E_v| * |x - x_ref| for every v: a token may differ only
+        # where the oracle's own top-2 margin is within twice that bound.
+        bound = 2 * e_norm * float(np.linalg.norm(xs[s] - ref_xs[s]))
+        if margins[s] > bound:
+            assert ref_tokens[s] == tokens[s], (s, margins[s], bound)
+    assert len(set(tokens)) > steps // 3          # the history is not one repeated token
