@@ -104,6 +104,21 @@ def test_dropin_bidirectional_leaves_uncovered_rows(cuda):
     assert_close(out[5:60], want[5:60], "windows")
 
 
+def test_dropin_bidirectional_audio_encoder_windows(cuda):
+    # Qwen3-ASR audio encoder shape (encoder.c:426-465): 104-token windows, 16 heads,
+    # hd 64, a ragged last window; every 128-row query tile spans two or three windows
+    rng = np.random.default_rng(6)
+    h, hd = 16, 64
+    ws = list(range(0, 9 * 104 + 1, 104)) + [9 * 104 + 50]
+    seq = ws[-1]
+    q, k, v = (rnd_bf16(rng, seq, h * hd) for _ in range(3))
+    out = np.zeros((seq, h * hd), np.float32)
+    smol_b200.bidirectional_attention(out, q, k, v, seq, h, hd, 0.125, ws)
+    no_error()
+    want = pyoracle.oracle().bidirectional_attention(q, k, v, seq, h, hd, 0.125, ws)
+    assert_close(out, want, "audio encoder windows")
+
+
 def test_dropin_rope_and_norm_golden(golden, cuda):
     for name in ("rope_neox", "rope_interleaved", "rope_neox_odd"):
         hd, inter = (int(x) for x in golden[f"{name}/meta"])
