@@ -55,7 +55,7 @@ def parse_args():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget in seconds (--impl reference: the cap per step)")
     ap.add_argument("--seqs", type=int, default=workload.CFG2["n_seqs"], help="sequences per GPU")
     ap.add_argument("--layers", type=int, default=workload.CFG2["layers"])
     ap.add_argument("--no-decode", action="store_true", help="prefill measurement only (profiling helper)")
@@ -245,7 +245,8 @@ def run_reference(args):
     if rank != 0:
         return
     lens = workload.decode_lengths(workload.CFG2["n_seqs"], workload.CFG2["len_lo"], workload.CFG2["len_hi"], 0)
-    per_step = max(1.0, min(10.0, 120.0 / max(1, args.steps + args.warmup)))
+    # each step a bounded sample: the whole run stays near two minutes of CPU time
+    per_step = max(0.1, min(args.cpu_seconds, 120.0 / max(1, args.steps + args.warmup)))
     ref = CpuReference(lens)
     if not ref.available:
         print(json.dumps({"impl": "reference", "unavailable": "compiled reference (oracle/_ref) not present"}))
