@@ -1,9 +1,12 @@
 """CPU restatement of the reference decoder step -- TEST INFRASTRUCTURE ONLY.
 
 numpy (fp32) restatement of qkn_decoder_prefill (qkn_decoder.c:369-564) and
-qkn_decoder_forward (qkn_decoder.c:570-714) for the Qwen3 configuration the device
-decoder step implements: per-head QK-RMSNorm, NeoX RoPE, no softcap or sliding
-window, SwiGLU MLP with interleaved gate/up rows, tied embeddings, greedy argmax.
+qkn_decoder_forward (qkn_decoder.c:570-714) in the configurations the device decoder
+step implements: Qwen3 (per-head QK-RMSNorm, NeoX RoPE, SwiGLU, residual then norm)
+and Gemma (the exports' settings, paligemma.c:206-230: embedding scale, interleaved
+RoPE, GeGLU, a norm on each sublayer's output before its residual add
+(qkn_decoder.c:681-701), attention softcap, sliding-window layers with their own
+RoPE theta, QK-norm optional); interleaved gate/up rows, tied embeddings, greedy argmax.
 The attention, QK-norm, RoPE and cache append go through the C restatement
 (pyoracle: smol_oracle.c) over a cache that holds the device formats (K bf16, V
 fp16), so both sides attend over identical values.  Weights are bf16 (kept as the
@@ -32,6 +35,16 @@ def swiglu(gate_up: np.ndarray) -> np.ndarray:
     return ((g / (np.float32(1.0) + np.exp(-g, dtype=np.float32))) * u).astype(np.float32)
 
 
+def geglu(gate_up: np.ndarray) -> np.ndarray:
+    """smol_geglu_multiply (activation.c:104-126): gelu_tanh(g[2j]) * g[2j+1]."""
+    g = gate_up[..., 0::2]
+    u = gate_up[..., 1::2]
+    x3 = (g * g * g).astype(np.float32)
+    inner = (np.float32(0.7978845608028654) * (g + np.float32(0.044715) * x3)).astype(np.float32)
+    gl = (np.float32(0.5) * g * (np.float32(1.0) + np.tanh(inner, dtype=np.float32))).astype(np.float32)
+    return (gl * u).astype(np.float32)
+
+
 def argmax_first(logits: np.ndarray) -> int:
     """smol_argmax_matvec_bf16 (matmul.c:392-417): the lowest index among equal maxima."""
     return int(np.argmax(logits))
@@ -41,10 +54,23 @@ class QknOracle:
     """A seeded Qwen3-shaped model and its reference forward passes."""
 
     def __init__(self, hidden=1024, layers=2, n_heads=16, n_kv_heads=8, head_dim=128, intermediate=3072,
-                 vocab=4096, theta=1e6, eps=1e-6, qk_gain=3.0, vo_gain=4.0, seed=0, cap=1024):
+                 vocab=4096, theta=1e6, eps=1e-6, qk_gain=3.0, vo_gain=4.0, seed=0, cap=1024, gemma=None):
+        """gemma (None for Qwen3): dict of the Gemma settings -- embed_normalizer, attn_softcap,
+        sliding_window, sliding (per-layer flags), local_theta, qk_norm (bool), interleaved (bool),
+        sublayer_gain.  Gemma models carry pre/post-FFN norms and use GeGLU."""
         rng = np.random.default_rng(seed)
         self.H, self.L, self.HQ, self.HKV, self.HD = hidden, layers, n_heads, n_kv_heads, head_dim
         self.I, self.V, self.eps, self.cap = intermediate, vocab, eps, cap
+        self.theta = theta
+        g = dict(gemma or {})
+        self.gemma = gemma is not None
+        self.embed_normalizer = np.float32(g.get("embed_normalizer", 0.0))
+        self.attn_softcap = float(g.get("attn_softcap", 0.0))
+        self.sliding_window = int(g.get("sliding_window", 0))
+        self.sliding = [bool(x) for x in g.get("sliding", [False] * layers)]
+        self.local_theta = float(g.get("local_theta", 0.0))
+        self.qk_norm = bool(g.get("qk_norm", True))
+        self.interleaved = bool(g.get("interleaved", False))
         qd, kvd = n_heads * head_dim, n_kv_heads * head_dim
 
         def bf(*shape, sc=1.0):
@@ -53,7 +79,8 @@ class QknOracle:
         def near(n, mean, sd=0.02):
             return (mean + sd * rng.standard_normal(n)).astype(np.float32)
 
-        self.E = bf(vocab, hidden)
+        # Gemma's embedding rows are small and scaled up by embed_normalizer on lookup
+        self.E = bf(vocab, hidden, sc=1 / float(self.embed_normalizer) if self.embed_normalizer > 0 else 1.0)
         self.final_norm = near(hidden, 1.0)
         self.layers = []
         for _ in range(layers):
@@ -69,7 +96,20 @@ class QknOracle:
                 "q_norm": near(head_dim, qk_gain),
                 "k_norm": near(head_dim, qk_gain),
             })
-        self.cos, self.sin = pyoracle.fill_rope_table(cap, head_dim, theta)
+            if self.gemma:
+                # the sublayer-output norms scale each sublayer's contribution against the
+                # embedding (sublayer_gain, so that the next token is not the fed one)
+                gain = np.float32(g.get("sublayer_gain", 4.0))
+                self.layers[-1]["post_attn_norm"] = (self.layers[-1]["post_attn_norm"] * gain).astype(np.float32)
+                self.layers[-1]["pre_ffn_norm"] = near(hidden, 1.0)
+                self.layers[-1]["post_ffn_norm"] = (near(hidden, 1.0) * gain).astype(np.float32)
+                if not self.qk_norm:
+                    del self.layers[-1]["q_norm"], self.layers[-1]["k_norm"]
+        self.cos, self.sin = pyoracle.fill_rope_table(cap, head_dim, theta, self.interleaved)
+        # sliding layers use their own table when the theta differs (qkn_decoder.c:313-340, :462-468)
+        self.has_local = self.local_theta > 0 and self.local_theta != theta
+        if self.has_local:
+            self.cos_local, self.sin_local = pyoracle.fill_rope_table(cap, head_dim, self.local_theta, self.interleaved)
         self.kc = [np.zeros((cap, kvd), np.uint16) for _ in range(layers)]   # bf16 bits
         self.vc = [np.zeros((cap, kvd), np.uint16) for _ in range(layers)]   # fp16 bits
         self.len = 0
@@ -79,31 +119,50 @@ class QknOracle:
     def _layer(self, l: int, x: np.ndarray, pos0: int) -> np.ndarray:
         """One decoder layer over tokens at positions pos0.. (qkn_decoder.c:431-563 / :622-705)."""
         lw, n = self.layers[l], x.shape[0]
+        sliding = self.sliding[l] and self.sliding_window > 0
+        cos, sin = (self.cos_local, self.sin_local) if self.has_local and self.sliding[l] else (self.cos, self.sin)
         xn = rms_norm(x, lw["input_norm"], self.eps)
         q, k, v = xn @ lw["wq"].T, xn @ lw["wk"].T, xn @ lw["wv"].T
         pos = np.arange(pos0, pos0 + n, dtype=np.int32)
-        q_rot = pyoracle.qknorm_rope_append(q, k, v, self.HQ, self.HKV, self.HD, lw["q_norm"], lw["k_norm"], self.eps,
-                                            self.cos, self.sin, False, pos, pos.astype(np.int64), self.kc[l],
-                                            self.vc[l])
+        q_rot = pyoracle.qknorm_rope_append(q, k, v, self.HQ, self.HKV, self.HD, lw.get("q_norm"), lw.get("k_norm"),
+                                            self.eps, cos, sin, self.interleaved, pos, pos.astype(np.int64),
+                                            self.kc[l], self.vc[l])
         total = pos0 + n
         K = pyoracle.bf16_to_f32(self.kc[l][:total])
         Vv = self.vc[l][:total].view(np.float16).astype(np.float32)
-        attn = self.o.causal_attention(q_rot, K, Vv, n, total, self.HQ, self.HKV, self.HD, self.scale, pos0)
-        x = (x + attn @ lw["wo"].T).astype(np.float32)
-        xn = rms_norm(x, lw["post_attn_norm"], self.eps)
-        act = swiglu(xn @ lw["gate_up"].T)
-        return (x + act @ lw["down"].T).astype(np.float32)
+        attn = self.o.causal_attention(q_rot, K, Vv, n, total, self.HQ, self.HKV, self.HD, self.scale, pos0,
+                                       window=self.sliding_window if sliding else 0, cap=self.attn_softcap)
+        proj = (attn @ lw["wo"].T).astype(np.float32)
+        if "pre_ffn_norm" in lw:   # Gemma: norm the sublayer output, add, norm for the MLP (:681-685)
+            x = (x + rms_norm(proj, lw["post_attn_norm"], self.eps)).astype(np.float32)
+            xn = rms_norm(x, lw["pre_ffn_norm"], self.eps)
+        else:                      # Qwen3: add, then norm (:688-689)
+            x = (x + proj).astype(np.float32)
+            xn = rms_norm(x, lw["post_attn_norm"], self.eps)
+        gu = xn @ lw["gate_up"].T
+        act = geglu(gu) if self.gemma else swiglu(gu)
+        ffn = (act @ lw["down"].T).astype(np.float32)
+        if "post_ffn_norm" in lw:
+            ffn = rms_norm(ffn, lw["post_ffn_norm"], self.eps)
+        return (x + ffn).astype(np.float32)
+
+    def _embed(self, tokens) -> np.ndarray:
+        """Embedding rows, scaled by embed_normalizer when it is set (qkn_decoder.c:415-419, :596-599)."""
+        x = self.E[np.asarray(tokens)].astype(np.float32)
+        if self.embed_normalizer > 0:
+            x = (x * self.embed_normalizer).astype(np.float32)
+        return x
 
     def prefill(self, tokens) -> None:
         """qkn_decoder_prefill over `tokens` (no logits, as the reference)."""
-        x = self.E[np.asarray(tokens)].astype(np.float32)
+        x = self._embed(tokens)
         for l in range(self.L):
             x = self._layer(l, x, self.len)
         self.len += len(tokens)
 
     def forward(self, token: int) -> tuple[int, float, np.ndarray]:
         """qkn_decoder_forward for one token: (greedy token, top-1/top-2 margin, final normed x)."""
-        x = self.E[[token]].astype(np.float32)
+        x = self._embed([token])
         for l in range(self.L):
             x = self._layer(l, x, self.len)
         self.len += 1

@@ -10,10 +10,13 @@
  * device cache and the tensor-core prefill hold, which the oracle also uses).
  *
  * Input (little-endian): "QKNW", int32 hidden, layers, heads, kv_heads, head_dim,
- * intermediate, vocab, n_prompt, n_steps; float32 eps, rope_theta; uint16 bf16
- * E[vocab][hidden]; float32 final_norm[hidden]; per layer: bf16 wq, wk, wv, wo,
- * gate_up (rows interleaved), down; float32 input_norm, post_attn_norm, q_norm,
- * k_norm; int32 prompt[n_prompt]; int32 feed[n_steps] (the token fed at each step).
+ * intermediate, vocab, n_prompt, n_steps, activation (qkn_activation_t), rope_interleaved,
+ * sliding_window, has_qk_norm, has_ffn_norms; float32 eps, rope_theta, rope_local_theta,
+ * embed_normalizer, attn_logit_softcap; uint16 bf16 E[vocab][hidden]; float32
+ * final_norm[hidden]; per layer: int32 is_sliding, bf16 wq, wk, wv, wo, gate_up (rows
+ * interleaved), down; float32 input_norm, post_attn_norm, then q_norm, k_norm when
+ * has_qk_norm, then pre_ffn_norm, post_ffn_norm when has_ffn_norms; int32
+ * prompt[n_prompt]; int32 feed[n_steps] (the token fed at each step).
  * Output: per step int32 token, float32 x[hidden].
  *
  * Usage: qkn_weights_xxx <in> <out>
@@ -54,9 +57,10 @@ int main(int argc, char **argv)
     if (!g_in || !out) return 2;
     char magic[4];
     if (fread(magic, 1, 4, g_in) != 4 || memcmp(magic, "QKNW", 4)) return 2;
-    int32_t *h = (int32_t *)take(9 * sizeof(int32_t));
+    int32_t *h = (int32_t *)take(14 * sizeof(int32_t));
     const int H = h[0], L = h[1], HQ = h[2], HKV = h[3], HD = h[4], I = h[5], V = h[6], NP = h[7], NS = h[8];
-    float *fh = (float *)take(2 * sizeof(float));
+    const int has_qk_norm = h[12], has_ffn_norms = h[13];
+    float *fh = (float *)take(5 * sizeof(float));
     if (L < 1 || L > QKN_MAX_DEC_LAYERS || NP < 2) return 2;
     const size_t qd = (size_t)HQ * HD, kvd = (size_t)HKV * HD;
 
@@ -69,15 +73,20 @@ int main(int argc, char **argv)
     c->dec_head_dim = HD;
     c->dec_intermediate = I;
     c->vocab_size = V;
+    c->activation = h[9] ? QKN_ACT_GEGLU : QKN_ACT_SWIGLU;
+    c->rope_type = h[10] ? QKN_ROPE_INTERLEAVED : QKN_ROPE_NEOX;
+    c->sliding_window = h[11];
     c->dec_rms_norm_eps = fh[0];
     c->dec_rope_theta = fh[1];
-    c->activation = QKN_ACT_SWIGLU;
-    c->rope_type = QKN_ROPE_NEOX;
+    c->dec_rope_local_theta = fh[2];
+    c->embed_normalizer = fh[3];
+    c->attn_logit_softcap = fh[4];
     qkn_decoder_t *d = &ctx->decoder;
     d->tok_embeddings_bf16 = (uint16_t *)take((size_t)V * H * 2);
     d->norm = (float *)take((size_t)H * 4);
     for (int l = 0; l < L; l++) {
         qkn_dec_layer_t *ly = &d->layers[l];
+        ly->is_sliding = *(int32_t *)take(4);
         ly->wq_weight_bf16 = (uint16_t *)take(qd * H * 2);
         ly->wk_weight_bf16 = (uint16_t *)take(kvd * H * 2);
         ly->wv_weight_bf16 = (uint16_t *)take(kvd * H * 2);
@@ -86,8 +95,14 @@ int main(int argc, char **argv)
         ly->down_weight_bf16 = (uint16_t *)take((size_t)H * I * 2);
         ly->input_norm = (float *)take((size_t)H * 4);
         ly->post_attn_norm = (float *)take((size_t)H * 4);
-        ly->q_norm_weight = (float *)take((size_t)HD * 4);
-        ly->k_norm_weight = (float *)take((size_t)HD * 4);
+        if (has_qk_norm) {
+            ly->q_norm_weight = (float *)take((size_t)HD * 4);
+            ly->k_norm_weight = (float *)take((size_t)HD * 4);
+        }
+        if (has_ffn_norms) {
+            ly->pre_ffn_norm = (float *)take((size_t)H * 4);
+            ly->post_ffn_norm = (float *)take((size_t)H * 4);
+        }
     }
     int32_t *prompt = (int32_t *)take((size_t)NP * 4);
     int32_t *feed = (int32_t *)take((size_t)NS * 4);

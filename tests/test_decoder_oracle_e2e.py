@@ -3,8 +3,8 @@
 The oracle's seeded model is written to a file and run by oracle/_ref/qkn_weights_emul:
 the reference's own qkn_decoder_prefill / qkn_decoder_forward (qkn_decoder.c:369-714)
 with its kernels, attention over the cache formats the oracle also keeps (K bf16, V
-fp16).  Both sides are teacher-forced on the same tokens, so every step is compared
-on the same history: the greedy token wherever the top-2 logit margin exceeds the
+fp16).  Both sides are teacher-forced on the same tokens (a seeded random stream), so
+every step is compared on the same history: the greedy token wherever the top-2 logit margin exceeds the
 difference the hidden states allow, and the final normalised hidden state within
 rel-L2 3e-3 at every step and 1e-4 / 1e-3 (one / two layers) at the median.
 
@@ -36,16 +36,21 @@ THETA, EPS = 1e6, 1e-6
 def _write_model(path, m: QknOracle, prompt, feed):
     bits = lambda a: np.ascontiguousarray(pyoracle.bf16_bits(a)).tobytes()        # noqa: E731
     f32 = lambda a: np.ascontiguousarray(a, dtype=np.float32).tobytes()              # noqa: E731
+    has_ffn_norms = int("pre_ffn_norm" in m.layers[0])
     with open(path, "wb") as f:
         f.write(b"QKNW")
-        f.write(struct.pack("<9i", m.H, m.L, m.HQ, m.HKV, m.HD, m.I, m.V, len(prompt), len(feed)))
-        f.write(struct.pack("<2f", EPS, THETA))
+        f.write(struct.pack("<14i", m.H, m.L, m.HQ, m.HKV, m.HD, m.I, m.V, len(prompt), len(feed), int(m.gemma),
+                            int(m.interleaved), m.sliding_window, int(m.qk_norm), has_ffn_norms))
+        f.write(struct.pack("<5f", EPS, m.theta, m.local_theta, float(m.embed_normalizer), m.attn_softcap))
         f.write(bits(m.E))
         f.write(f32(m.final_norm))
-        for lw in m.layers:
+        for l, lw in enumerate(m.layers):
+            f.write(struct.pack("<i", int(m.sliding[l])))
             for name in ("wq", "wk", "wv", "wo", "gate_up", "down"):
                 f.write(bits(lw[name]))
-            for name in ("input_norm", "post_attn_norm", "q_norm", "k_norm"):
+            names = ["input_norm", "post_attn_norm"] + (["q_norm", "k_norm"] if m.qk_norm else []) + \
+                (["pre_ffn_norm", "post_ffn_norm"] if has_ffn_norms else [])
+            for name in names:
                 f.write(f32(lw[name]))
         f.write(np.asarray(prompt, "<i4").tobytes())
         f.write(np.asarray(feed, "<i4").tobytes())
@@ -58,21 +63,35 @@ def _read_steps(path, n_steps, hidden):
     return tokens, xs
 
 
-@pytest.mark.parametrize("layers,prompt_len,steps,seed", [(1, 96, 24, 11), (2, 64, 24, 12)])
-def test_oracle_decoder_matches_reference_decoder(tmp_path, layers, prompt_len, steps, seed):
+# Gemma settings as the exports set them (paligemma.c:206-230), at test scale: Gemma 2
+# (no QK-norm, attention softcap, alternating sliding layers with their own RoPE theta)
+# and Gemma 3 (QK-norm, no softcap); the window is short enough to bind in the test.
+GEMMA2 = {"embed_normalizer": 32.0, "interleaved": True, "attn_softcap": 3.0, "sliding_window": 16,
+          "sliding": [True, False], "local_theta": 1e4, "qk_norm": False}
+GEMMA3 = {"embed_normalizer": 32.0, "interleaved": True, "attn_softcap": 0.0, "sliding_window": 16,
+          "sliding": [True, False], "local_theta": 1e4, "qk_norm": True}
+GEMMA_SHAPE = {"n_heads": 8, "n_kv_heads": 1, "head_dim": 256, "intermediate": 2048}
+
+
+@pytest.mark.parametrize("layers,prompt_len,steps,seed,gemma", [(1, 96, 24, 11, None), (2, 64, 24, 12, None),
+                                                                 (2, 64, 24, 13, GEMMA2), (2, 64, 24, 14, GEMMA3)],
+                         ids=["qwen3-1", "qwen3-2", "gemma2-2", "gemma3-2"])
+def test_oracle_decoder_matches_reference_decoder(tmp_path, layers, prompt_len, steps, seed, gemma):
+    shape = GEMMA_SHAPE if gemma else {}
     m = QknOracle(layers=layers, seed=seed, qk_gain=3.0, vo_gain=4.0, cap=prompt_len + steps + 8,
-                  theta=THETA, eps=EPS)
+                  theta=THETA, eps=EPS, gemma=gemma, **shape)
     rng = np.random.default_rng(seed)
     prompt = rng.integers(0, m.V, prompt_len).tolist()
     m.prefill(prompt[:-1])
-    feed, tokens, margins, xs = [prompt[-1]], [], [], []
-    for _ in range(steps):
-        tok, margin, xf = m.forward(feed[-1])
+    # teacher forcing on the prompt's last token, then a seeded random stream: random
+    # models' own greedy streams tend to settle on one token, a random history does not
+    feed = [prompt[-1]] + rng.integers(0, m.V, steps - 1).tolist()
+    tokens, margins, xs = [], [], []
+    for s in range(steps):
+        tok, margin, xf = m.forward(feed[s])
         tokens.append(tok)
         margins.append(margin)
         xs.append(xf)
-        feed.append(tok)
-    feed = feed[:steps]
 
     inp, out = tmp_path / "model.bin", tmp_path / "steps.bin"
     _write_model(inp, m, prompt, feed)
@@ -89,4 +108,4 @@ def test_oracle_decoder_matches_reference_decoder(tmp_path, layers, prompt_len, 
         bound = 2 * e_norm * float(np.linalg.norm(xs[s] - ref_xs[s]))
         if margins[s] > bound:
             assert ref_tokens[s] == tokens[s], (s, margins[s], bound)
-    assert len(set(tokens)) > steps // 3          # the history is not one repeated token
+    assert len(set(tokens)) > steps // 3          # the outputs are not one repeated token
