@@ -258,19 +258,24 @@ SMOL_B200_API int smol_b200_decode_step_host(
     float scale, void *scratch, size_t scratch_bytes);
 
 /* ===========================================================================
- * Part 4 -- device-resident decoder step (Qwen3-style qkn_decoder).
+ * Part 4 -- device-resident decoder step (qkn_decoder).
  *
  * One greedy token for each of n_seqs sequences, entirely on the device: the whole of
- * qkn_decoder_forward (qkn_decoder.c:570-714) for the configuration with per-head
- * QK-RMSNorm, SwiGLU MLP and tied embeddings -- embedding lookup, per layer input
+ * qkn_decoder_forward (qkn_decoder.c:570-714) -- embedding lookup, per layer input
  * RMSNorm, Q/K/V projections, QK-norm + RoPE + cache append, attention over the
- * pooled cache, output projection + residual, post-attention RMSNorm, fused
- * gate/up projection with SiLU(gate)*up, down projection + residual; final RMSNorm
- * and the greedy argmax over the tied embedding matrix (smol_argmax_matvec_bf16,
+ * pooled cache, output projection + residual, post-attention RMSNorm, fused gate/up
+ * projection with the gated activation, down projection + residual; final RMSNorm and
+ * the greedy argmax over the tied embedding matrix (smol_argmax_matvec_bf16,
  * matmul.c:392-417: the lowest index among equal maxima).  Weights use the
  * reference's layouts: bf16 [out][in] matrices, gate/up rows interleaved
  * (qkn_decoder.c:140-154), fp32 norm weights.  Projections compute in fp32 from the
  * bf16 weights (bf16_matvec_fused); the cache holds K bf16 / V fp16 as in Part 3.
+ *
+ * Two configurations, as qkn_decoder.c selects them: Qwen3 (the Gemma fields zero /
+ * NULL) and Gemma as the exports set it (paligemma.c:206-230): embedding scale,
+ * GeGLU, a norm on each sublayer's output before its residual add, attention softcap,
+ * sliding-window layers with their own RoPE tables; QK-norm is optional in both.
+ *
  * Every pointer below is device memory except `layers` (a host array).  The step is
  * asynchronous on `stream` and allocation-free, so a decode loop can be captured
  * once in a CUDA graph and replayed.
@@ -282,7 +287,15 @@ typedef struct smol_b200_qkn_layer {
     const uint16_t *gate_up;         /* [2*intermediate][hidden], interleaved */
     const uint16_t *down;            /* [hidden][intermediate]              */
     const float *input_norm, *post_attn_norm;   /* [hidden]   */
-    const float *q_norm, *k_norm;               /* [head_dim] */
+    const float *q_norm, *k_norm;               /* [head_dim]; NULL: no QK-norm */
+    /* Gemma (NULL / 0 in the Qwen3 configuration): */
+    const float *pre_ffn_norm;       /* [hidden]; set: post_attn_norm normalises the
+                                        attention output before its residual add and
+                                        this normalises x for the MLP (:681-685)   */
+    const float *post_ffn_norm;      /* [hidden]; set: normalises the MLP output before
+                                        its residual add (:701-702)                */
+    int is_sliding;                  /* attends the last sliding_window positions, with
+                                        the local RoPE tables (:626-632, :659-667)  */
 } smol_b200_qkn_layer;
 
 typedef struct smol_b200_qkn_model {
@@ -292,6 +305,13 @@ typedef struct smol_b200_qkn_model {
     const uint16_t *tok_embeddings;   /* [vocab][hidden] bf16, also the lm_head */
     const float *final_norm;          /* [hidden]                               */
     const smol_b200_qkn_layer *layers;   /* host array of n_layers              */
+    /* Gemma (0 / NULL in the Qwen3 configuration): */
+    int activation;                   /* 0: SwiGLU, 1: GeGLU (GELU-tanh gate)    */
+    float embed_normalizer;           /* > 0: embedding rows are scaled by it    */
+    float attn_softcap;               /* > 0: scores become cap*tanh(score/cap)  */
+    int sliding_window;               /* > 0: window of the is_sliding layers    */
+    const float *rope_cos_local;      /* tables of the is_sliding layers, as the */
+    const float *rope_sin_local;      /* step's; NULL: the step's tables         */
 } smol_b200_qkn_model;
 
 /* Device workspace one step needs for n_seqs sequences of at most max_kv_len cached
@@ -304,7 +324,8 @@ SMOL_B200_API size_t smol_b200_qkn_step_workspace_bytes(const smol_b200_qkn_mode
  * kv_len[b]: tokens already cached; the new token goes to position / row offset
  * kv_len[b] and attention covers [0, kv_len[b]+1).  advance != 0 increments kv_len
  * on the device at the end of the step (so a captured step replays as a loop).
- * rope_cos / rope_sin: [>= max_kv_len+1][head_dim] tables (row = position).
+ * rope_cos / rope_sin: [>= max_kv_len+1][head_dim] tables (row = position); the
+ * model's local tables, when given, have the same shape.
  * tokens_out[b]: the greedy next token. */
 SMOL_B200_API int smol_b200_qkn_decode_step(
     void *stream, const smol_b200_qkn_model *model, int n_seqs, const int *tokens_in,
@@ -315,7 +336,8 @@ SMOL_B200_API int smol_b200_qkn_decode_step(
 /* The building blocks of the step, for callers that orchestrate their own decoder:
  *   y[b][n] (+)= sum_k x[b][k] * W[n][k]    mode 0: store, 1: add into y (residual),
  *   2: SiLU-gated pairs, y[b][r] = silu(s[2r]) * s[2r+1] over W's 2*n_out rows
- *   (smol_swiglu_multiply, activation.c:55-86), n_out = rows of y.
+ *   (smol_swiglu_multiply, activation.c:55-86), 3: GELU-tanh-gated pairs
+ *   (smol_geglu_multiply, activation.c:104-126); n_out = rows of y.
  * W bf16 [rows][k_dim] with k_dim a multiple of 8 and 16-byte aligned rows.
  * x fp32 with row stride ldx (multiple of 4), y fp32 with row stride ldy. */
 SMOL_B200_API int smol_b200_gemv_bf16(void *stream, float *y, int64_t ldy, const float *x, int64_t ldx,

@@ -5,7 +5,7 @@ qkn_decoder_forward (qkn_decoder.c:570-714) in the configurations the device dec
 step implements: Qwen3 (per-head QK-RMSNorm, NeoX RoPE, SwiGLU, residual then norm)
 and Gemma (the exports' settings, paligemma.c:206-230: embedding scale, interleaved
 RoPE, GeGLU, a norm on each sublayer's output before its residual add
-(qkn_decoder.c:681-701), attention softcap, sliding-window layers with their own
+(qkn_decoder.c:681-704), attention softcap, sliding-window layers with their own
 RoPE theta, QK-norm optional); interleaved gate/up rows, tied embeddings, greedy argmax.
 The attention, QK-norm, RoPE and cache append go through the C restatement
 (pyoracle: smol_oracle.c) over a cache that holds the device formats (K bf16, V
@@ -51,7 +51,7 @@ def argmax_first(logits: np.ndarray) -> int:
 
 
 class QknOracle:
-    """A seeded Qwen3-shaped model and its reference forward passes."""
+    """A seeded decoder (Qwen3 or Gemma configuration) and its reference forward passes."""
 
     def __init__(self, hidden=1024, layers=2, n_heads=16, n_kv_heads=8, head_dim=128, intermediate=3072,
                  vocab=4096, theta=1e6, eps=1e-6, qk_gain=3.0, vo_gain=4.0, seed=0, cap=1024, gemma=None):

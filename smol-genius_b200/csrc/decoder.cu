@@ -3,9 +3,10 @@
 // Replaces what qkn_decoder_forward (qkn_decoder.c:570-714) runs on the host between
 // the attention calls: bf16 matrix-vector products (bf16_matvec_fused,
 // bf16_matvec_avx.c:24-150: fp32 activations times bf16 weights widened to fp32,
-// fp32 accumulation), the SwiGLU gate (activation.c:55-86), residual adds
-// (matmul.c:33-35), RMSNorm (rmsnorm.c:17-70) and the greedy argmax over the tied
-// embedding matrix (matmul.c:392-417, bf16_matvec_avx.c:156-250).
+// fp32 accumulation), the SwiGLU / GeGLU gates (activation.c:55-126), residual adds
+// (matmul.c:33-35), RMSNorm (rmsnorm.c:17-70), Gemma's embedding scale and
+// sublayer-output norms (qkn_decoder.c:596-599, :681-702) and the greedy argmax over
+// the tied embedding matrix (matmul.c:392-417, bf16_matvec_avx.c:156-250).
 //
 // The products are HBM-bound for a batch of a few sequences: every weight is read
 // once per step and reused for all (<= 8) sequences of a launch.  One warp owns one
@@ -52,7 +53,7 @@ struct GemvParams {
     float *x_normed;       // non-null: CTA 0 also writes the staged (normalised) x here
     int k_dim;
     int nb;       // sequences in this launch (<= NB)
-    int mode;     // 0 store, 1 add, 2 gated pairs
+    int mode;     // 0 store, 1 add, 2 SiLU-gated pairs, 3 GELU-tanh-gated pairs
     int ksplit;   // warps of a CTA that share one row group, each a slice of K (1, 2, 4, 8)
 };
 
@@ -152,6 +153,19 @@ __device__ __forceinline__ void stage_x(float *xs, const float *x, long long ldx
         }
     }
     __syncthreads();
+}
+
+// The gate of a gated pair: SiLU g/(1+exp(-g)) (mode 2, activation.c:81) or GELU with
+// the tanh approximation 0.5*g*(1+tanh(sqrt(2/pi)*(g+0.044715*g^3))) (mode 3,
+// activation.c:119-123).
+__device__ __forceinline__ float gate_act(float g, int mode)
+{
+    if (mode == 3) {
+        const float x3 = g * g * g;
+        const float inner = 0.7978845608028654f * (g + 0.044715f * x3);
+        return 0.5f * g * (1.0f + tanhf(inner));
+    }
+    return g / (1.0f + expf(-g));
 }
 
 // Pull a weight row into L2 ahead of the dependency wait (weights never change).
@@ -279,8 +293,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_co
                         } else if (p.mode == 1) {
                             y[rr[i].col] = y[rr[i].col] + sums[i];
                         } else if ((i & 1) == 0) {
-                            const float g = sums[i] / (1.0f + expf(-sums[i]));   // SiLU, activation.c:81
-                            y[rr[i].col / 2] = g * sums[i + 1];
+                            y[rr[i].col / 2] = gate_act(sums[i], p.mode) * sums[i + 1];
                         }
                     }
                 }
@@ -309,8 +322,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_co
                 } else if ((i & 1) == 0) {   // gate row i, up row i+1 (pairs never straddle a warp)
                     float u = 0.f;
                     for (int sl = 0; sl < S; ++sl) u += part[grp * S + sl][i + 1][b];
-                    const float g = v / (1.0f + expf(-v));   // SiLU, activation.c:81
-                    y[r.col / 2] = g * u;
+                    y[r.col / 2] = gate_act(v, p.mode) * u;
                 }
             }
         }
@@ -386,8 +398,10 @@ __global__ void argmax_final_kernel(int *tokens_out, const float *part_val, cons
     if (threadIdx.x == 0) tokens_out[b] = bi;
 }
 
-// x[b][:] = E[tokens[b]][:] (bf16 -> fp32)
-__global__ void embed_kernel(float *x, const int *tokens, const uint16_t *emb, int hidden, int vocab, unsigned *err)
+// x[b][:] = E[tokens[b]][:] (bf16 -> fp32), times `scale` when it is positive (Gemma's
+// embed_normalizer, qkn_decoder.c:596-599)
+__global__ void embed_kernel(float *x, const int *tokens, const uint16_t *emb, int hidden, int vocab, float scale,
+                             unsigned *err)
 {
     griddep_wait();
     griddep_trigger();
@@ -398,8 +412,39 @@ __global__ void embed_kernel(float *x, const int *tokens, const uint16_t *emb, i
         t = 0;
     }
     const uint16_t *e = emb + static_cast<size_t>(t) * hidden;
-    for (int i = threadIdx.x; i < hidden; i += blockDim.x)
-        x[static_cast<size_t>(b) * hidden + i] = __uint_as_float(static_cast<uint32_t>(e[i]) << 16);
+    for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+        float v = __uint_as_float(static_cast<uint32_t>(e[i]) << 16);
+        if (scale > 0.f) v *= scale;
+        x[static_cast<size_t>(b) * hidden + i] = v;
+    }
+}
+
+// x[b][:] += rmsnorm(y[b][:]) with weights w: smol_rms_norm of a sublayer's output
+// followed by smol_add_inplace (qkn_decoder.c:683-684, :701-704; rmsnorm.c:17-70:
+// (y * w) * 1/sqrtf(mean(y^2) + eps)).  One CTA of kNormAddThreads per sequence.
+constexpr int kNormAddThreads = 256;
+
+__global__ void __launch_bounds__(kNormAddThreads) norm_add_kernel(float *x, const float *y, const float *w,
+                                                                  int hidden, float eps)
+{
+    griddep_wait();
+    griddep_trigger();
+    const size_t row = static_cast<size_t>(blockIdx.x) * hidden;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < hidden; i += kNormAddThreads) ss += y[row + i] * y[row + i];
+    ss = warp_sum(ss);
+    __shared__ float part[kNormAddThreads / 32];
+    __shared__ float rinv;
+    if (threadIdx.x % 32 == 0) part[threadIdx.x / 32] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int i = 0; i < kNormAddThreads / 32; ++i) t += part[i];
+        rinv = 1.0f / sqrtf(t / static_cast<float>(hidden) + eps);
+    }
+    __syncthreads();
+    const float r = rinv;
+    for (int i = threadIdx.x; i < hidden; i += kNormAddThreads) x[row + i] = x[row + i] + y[row + i] * w[i] * r;
 }
 
 // positions[b] = kv_len[b]; kv_next[b] = kv_len[b] + 1; slots[l][b] = row0[l][b] + kv_len[b]
@@ -465,12 +510,12 @@ int launch_gemv_nb(cudaStream_t st, GemvParams &p)
 }
 
 // Rows per warp: 1 for a single sequence (most warps in flight), 2 for two, 4 from four
-// sequences on; the gated form needs an even count (gate, up).
+// sequences on; the gated forms need an even count (gate, up).
 template <int NB>
 int launch_gemv_rows(cudaStream_t st, GemvParams &p)
 {
     if (NB >= 4) return launch_gemv_nb<NB, 4>(st, p);
-    if (NB == 2 || p.mode == 2) return launch_gemv_nb<NB, 2>(st, p);
+    if (NB == 2 || p.mode >= 2) return launch_gemv_nb<NB, 2>(st, p);
     return launch_gemv_nb<NB, 1>(st, p);
 }
 
@@ -481,7 +526,7 @@ int run_gemv(cudaStream_t st, GemvParams p, int n_seqs)
     if (gemv_smem_bytes(kMaxBatch, p.k_dim) > kMaxXsBytes) return SMOL_B200_ERR_ARGS;
     for (int s = 0; s < p.nseg; ++s)
         if (!p.seg[s].w || !p.seg[s].y || (reinterpret_cast<uintptr_t>(p.seg[s].w) & 15) ||
-            (p.mode == 2 && (p.seg[s].rows & 1)))
+            (p.mode >= 2 && (p.seg[s].rows & 1)))
             return SMOL_B200_ERR_ARGS;
     if (!p.x || (reinterpret_cast<uintptr_t>(p.x) & 15)) return SMOL_B200_ERR_ARGS;
     for (int b0 = 0; b0 < n_seqs; b0 += kMaxBatch) {
@@ -547,7 +592,7 @@ int run_argmax(cudaStream_t st, int *tokens_out, const float *x, long long ldx, 
 
 // Workspace of one decoder step, carved in 256-byte aligned pieces.
 struct StepWs {
-    float *x, *xn, *q, *k, *v, *qr, *attn, *act;
+    float *x, *xn, *q, *k, *v, *qr, *attn, *act, *sub;   // sub: a sublayer's output before its norm
     int *positions, *kv_next;
     int64_t *slots;
     void *attn_ws;
@@ -584,6 +629,7 @@ StepWs carve(const smol_b200_qkn_model &m, int n_seqs, int max_kv_len, uint8_t *
     w.attn_ws = take(w.attn_ws_bytes);
     w.argmax_ws_bytes = argmax_ws_bytes(n_seqs, m.vocab);
     w.argmax_ws = take(w.argmax_ws_bytes);
+    w.sub = reinterpret_cast<float *>(take(B * m.hidden * 4));
     w.total = off;
     return w;
 }
@@ -593,7 +639,8 @@ bool model_ok(const smol_b200_qkn_model *m)
     return m && m->hidden > 0 && m->n_layers > 0 && m->n_heads > 0 && m->n_kv_heads > 0 && m->head_dim > 0 &&
            m->n_heads % m->n_kv_heads == 0 && m->intermediate > 0 && m->vocab > 0 && m->tok_embeddings &&
            m->final_norm && m->layers && m->hidden % 8 == 0 && m->intermediate % 8 == 0 &&
-           (m->n_heads * m->head_dim) % 8 == 0;
+           (m->n_heads * m->head_dim) % 8 == 0 && (m->activation == 0 || m->activation == 1) &&
+           m->sliding_window >= 0 && !m->rope_cos_local == !m->rope_sin_local;
 }
 
 }  // namespace
@@ -602,10 +649,10 @@ int gemv_norm_bf16(cudaStream_t st, float *y, int64_t ldy, const float *x, int64
                    int n_out, int k_dim, int n_seqs, int mode, const float *norm_w, float eps)
 {
     if (n_seqs <= 0 || n_out <= 0) return SMOL_B200_OK;
-    if (mode < 0 || mode > 2 || (ldy < n_out)) return SMOL_B200_ERR_ARGS;
+    if (mode < 0 || mode > 3 || (ldy < n_out)) return SMOL_B200_ERR_ARGS;
     GemvParams p;
     memset(&p, 0, sizeof(p));
-    p.seg[0] = {w, y, ldy, mode == 2 ? 2 * n_out : n_out};
+    p.seg[0] = {w, y, ldy, mode >= 2 ? 2 * n_out : n_out};
     p.nseg = 1;
     p.total_rows = p.seg[0].rows;
     p.x = x;
@@ -664,12 +711,26 @@ int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *mp, int n_seqs, 
     if (launch_kernel(step_index_kernel, dim3((n_idx + 255) / 256), dim3(256), 0, st, w.positions, w.kv_next, w.slots,
                       layer_row0, static_cast<const int *>(kv_len), n_seqs, m.n_layers) != cudaSuccess ||
         launch_kernel(embed_kernel, dim3(n_seqs), dim3(256), 0, st, w.x, tokens_in, m.tok_embeddings, H, m.vocab,
-                      err) != cudaSuccess)
+                      m.embed_normalizer, err) != cudaSuccess)
         return SMOL_B200_ERR_CUDA;
 
+    const int gate_mode = m.activation == 1 ? 3 : 2;   // GeGLU / SwiGLU (qkn_decoder.c:695-698)
+    // x[b] += rmsnorm(sub[b]) (Gemma's sublayer-output norm before the residual add)
+    auto norm_add = [&](const float *w_norm) {
+        if (!w_norm) return SMOL_B200_ERR_ARGS;
+        return launch_kernel(norm_add_kernel, dim3(n_seqs), dim3(kNormAddThreads), 0, st, w.x,
+                             static_cast<const float *>(w.sub), w_norm, H, m.eps) == cudaSuccess
+                   ? SMOL_B200_OK
+                   : SMOL_B200_ERR_CUDA;
+    };
     int rc = SMOL_B200_OK;
     for (int l = 0; l < m.n_layers && rc == SMOL_B200_OK; ++l) {
         const smol_b200_qkn_layer &L = m.layers[l];
+        // sliding layers: their own RoPE tables when given, the window when set
+        // (qkn_decoder.c:626-632, :659-667)
+        const bool local_rope = L.is_sliding && m.rope_cos_local;
+        const int window = L.is_sliding && m.sliding_window > 0 ? m.sliding_window : 0;
+        const float softcap = m.attn_softcap > 0.f ? m.attn_softcap : 0.f;
         {   // input RMSNorm + Q, K, V in one launch (smol_linear_nobias_bf16_qkv, matmul.c:308-334)
             GemvParams p;
             memset(&p, 0, sizeof(p));
@@ -688,21 +749,39 @@ int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *mp, int n_seqs, 
         }
         if (rc != SMOL_B200_OK) break;
         rc = qknorm_rope_append(st, w.q, w.k, w.v, n_seqs, m.n_heads, m.n_kv_heads, m.head_dim, L.q_norm, L.k_norm,
-                                m.eps, rope_cos, rope_sin, m.rope_interleaved, w.positions,
+                                m.eps, local_rope ? m.rope_cos_local : rope_cos,
+                                local_rope ? m.rope_sin_local : rope_sin, m.rope_interleaved, w.positions,
                                 w.slots + static_cast<size_t>(l) * n_seqs, w.qr, nullptr, k_pool, v_pool, pool_rows);
         if (rc != SMOL_B200_OK) break;
         rc = decode_attention(st, w.attn, w.qr, 0, k_pool, v_pool, pool_rows,
                               layer_row0 + static_cast<size_t>(l) * n_seqs, w.kv_next, n_seqs, max_kv_len + 1,
-                              m.n_heads, m.n_kv_heads, m.head_dim, scale, 0, 0.f, w.attn_ws, w.attn_ws_bytes);
+                              m.n_heads, m.n_kv_heads, m.head_dim, scale, window, softcap, w.attn_ws,
+                              w.attn_ws_bytes);
         if (rc != SMOL_B200_OK) break;
-        rc = gemv_norm_bf16(st, w.x, H, w.attn, qd, L.wo, H, qd, n_seqs, 1, nullptr, 0.f);   // x += o_proj(attn)
+        if (L.pre_ffn_norm) {
+            // Gemma (qkn_decoder.c:681-685): x += rmsnorm(o_proj(attn)); the MLP input is
+            // rmsnorm(x) with pre_ffn_norm
+            rc = gemv_norm_bf16(st, w.sub, H, w.attn, qd, L.wo, H, qd, n_seqs, 0, nullptr, 0.f);
+            if (rc == SMOL_B200_OK) rc = norm_add(L.post_attn_norm);
+            if (rc == SMOL_B200_OK)
+                rc = gemv_norm_bf16(st, w.act, m.intermediate, w.x, H, L.gate_up, m.intermediate, H, n_seqs,
+                                    gate_mode, L.pre_ffn_norm, m.eps);
+        } else {
+            rc = gemv_norm_bf16(st, w.x, H, w.attn, qd, L.wo, H, qd, n_seqs, 1, nullptr, 0.f);   // x += o_proj(attn)
+            // post-attention RMSNorm + gate/up + gate
+            if (rc == SMOL_B200_OK)
+                rc = gemv_norm_bf16(st, w.act, m.intermediate, w.x, H, L.gate_up, m.intermediate, H, n_seqs,
+                                    gate_mode, L.post_attn_norm, m.eps);
+        }
         if (rc != SMOL_B200_OK) break;
-        // post-attention RMSNorm + gate/up + SiLU gate
-        rc = gemv_norm_bf16(st, w.act, m.intermediate, w.x, H, L.gate_up, m.intermediate, H, n_seqs, 2,
-                            L.post_attn_norm, m.eps);
-        if (rc != SMOL_B200_OK) break;
-        rc = gemv_norm_bf16(st, w.x, H, w.act, m.intermediate, L.down, H, m.intermediate, n_seqs, 1, nullptr,
-                            0.f);   // x += down(act)
+        if (L.post_ffn_norm) {   // Gemma (qkn_decoder.c:701-704): x += rmsnorm(down(act))
+            rc = gemv_norm_bf16(st, w.sub, H, w.act, m.intermediate, L.down, H, m.intermediate, n_seqs, 0, nullptr,
+                                0.f);
+            if (rc == SMOL_B200_OK) rc = norm_add(L.post_ffn_norm);
+        } else {
+            rc = gemv_norm_bf16(st, w.x, H, w.act, m.intermediate, L.down, H, m.intermediate, n_seqs, 1, nullptr,
+                                0.f);   // x += down(act)
+        }
     }
     if (rc != SMOL_B200_OK) return rc;
     // final RMSNorm (qkn_decoder.c:710) folded into the argmax; the normalised state lands in xn

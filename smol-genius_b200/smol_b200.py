@@ -292,10 +292,11 @@ def decode_step_host(out_host, q_host, k_host, v_host, n_seqs, n_heads, n_kv_hea
 # Part 4: device-resident decoder step
 # ---------------------------------------------------------------------------
 class QknLayer(ctypes.Structure):
-    """smol_b200_qkn_layer: device pointers of one layer's weights."""
+    """smol_b200_qkn_layer: device pointers of one layer's weights (Gemma fields NULL / 0 for Qwen3)."""
     _fields_ = [("wq", ctypes.c_void_p), ("wk", ctypes.c_void_p), ("wv", ctypes.c_void_p), ("wo", ctypes.c_void_p),
                 ("gate_up", ctypes.c_void_p), ("down", ctypes.c_void_p), ("input_norm", ctypes.c_void_p),
-                ("post_attn_norm", ctypes.c_void_p), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p)]
+                ("post_attn_norm", ctypes.c_void_p), ("q_norm", ctypes.c_void_p), ("k_norm", ctypes.c_void_p),
+                ("pre_ffn_norm", ctypes.c_void_p), ("post_ffn_norm", ctypes.c_void_p), ("is_sliding", ctypes.c_int)]
 
 
 class QknModel(ctypes.Structure):
@@ -304,18 +305,30 @@ class QknModel(ctypes.Structure):
                 ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int), ("intermediate", ctypes.c_int),
                 ("vocab", ctypes.c_int), ("eps", ctypes.c_float), ("rope_interleaved", ctypes.c_int),
                 ("tok_embeddings", ctypes.c_void_p), ("final_norm", ctypes.c_void_p),
-                ("layers", ctypes.POINTER(QknLayer))]
+                ("layers", ctypes.POINTER(QknLayer)), ("activation", ctypes.c_int),
+                ("embed_normalizer", ctypes.c_float), ("attn_softcap", ctypes.c_float),
+                ("sliding_window", ctypes.c_int), ("rope_cos_local", ctypes.c_void_p),
+                ("rope_sin_local", ctypes.c_void_p)]
+
+
+ACT_SWIGLU, ACT_GEGLU = 0, 1
 
 
 def qkn_model(hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab, eps, tok_embeddings, final_norm, layers,
-              rope_interleaved=False) -> QknModel:
-    """layers: list of dicts with the QknLayer field names mapped to device tensors."""
+              rope_interleaved=False, activation=ACT_SWIGLU, embed_normalizer=0.0, attn_softcap=0.0,
+              sliding_window=0, rope_cos_local=None, rope_sin_local=None, sliding=None) -> QknModel:
+    """layers: list of dicts mapping QknLayer pointer field names to device tensors (absent
+    names -> NULL); sliding: per-layer is_sliding flags (default all 0)."""
     arr = (QknLayer * len(layers))()
     for i, lw in enumerate(layers):
-        for name, _ in QknLayer._fields_:
-            setattr(arr[i], name, _ptr(lw[name]))
+        for name, ctype in QknLayer._fields_:
+            if ctype is ctypes.c_void_p:
+                setattr(arr[i], name, _ptr(lw.get(name)))
+        arr[i].is_sliding = int(bool(sliding[i])) if sliding is not None else 0
     m = QknModel(hidden, len(layers), n_heads, n_kv_heads, head_dim, intermediate, vocab, eps, int(rope_interleaved),
-                 _ptr(tok_embeddings), _ptr(final_norm), ctypes.cast(arr, ctypes.POINTER(QknLayer)))
+                 _ptr(tok_embeddings), _ptr(final_norm), ctypes.cast(arr, ctypes.POINTER(QknLayer)), int(activation),
+                 float(embed_normalizer), float(attn_softcap), int(sliding_window), _ptr(rope_cos_local),
+                 _ptr(rope_sin_local))
     m._layers = arr   # keep the array alive with the struct
     return m
 

@@ -1,7 +1,8 @@
 """Shared test set-up.
 
 * registers the ``gpu`` marker (tests that need a B200; the CPU suite runs with
-  ``-m "not gpu"``);
+  ``-m "not gpu"``) and the ``new_on_gpu`` marker (GPU tests not yet run on a B200,
+  ordered after the rest);
 * builds the oracle (oracle/libsmol_oracle.so) and the product library
   (smol-genius_b200/libsmol_b200.so) when they are missing, so a fresh checkout
   can run the suite directly;
@@ -43,6 +44,13 @@ _ensure_built()
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs an sm_100 (B200) CUDA device")
+    config.addinivalue_line("markers", "new_on_gpu: a GPU test not yet run on a B200; runs after the rest")
+
+
+def pytest_collection_modifyitems(config, items):
+    """Tests marked new_on_gpu run last (the sort is stable), so that under -x a failure
+    in one of them cannot keep the established tests from running."""
+    items.sort(key=lambda item: item.get_closest_marker("new_on_gpu") is not None)
 
 
 @pytest.fixture(scope="session")

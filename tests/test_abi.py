@@ -130,3 +130,31 @@ def test_binding_signatures_match_header():
         ret = " ".join(ret.split())
         assert ret in kinds, (name, ret)
         assert res == kinds[ret], (name, ret, res)
+
+
+def test_binding_structs_match_header(tmp_path):
+    """The ctypes mirrors of the Part-4 structs have the C layout: field names in header
+    order, and every offset and the size as gcc lays them out for include/smol_b200.h."""
+    import ctypes
+    import re
+    text = re.sub(r"/\*.*?\*/", "", open(smol_b200.HEADER_PATH).read(), flags=re.S)
+    for cname, pystruct in (("smol_b200_qkn_layer", smol_b200.QknLayer), ("smol_b200_qkn_model", smol_b200.QknModel)):
+        body = re.search(r"typedef struct " + cname + r"\s*\{(.*?)\}\s*" + cname + r"\s*;", text, flags=re.S).group(1)
+        names = []
+        for decl in body.split(";"):
+            decl = " ".join(decl.split())
+            if not decl:
+                continue
+            # "const float *a, *b" / "int x, y": the names are the last word of each declarator
+            names += [re.findall(r"\w+", d)[-1] for d in decl.split(",")]
+        assert names == [f[0] for f in pystruct._fields_], (cname, names)
+        src = tmp_path / f"{cname}.c"
+        src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"smol_b200.h\"\nint main(void){\n" +
+                       "".join(f'printf("%zu\\n", offsetof({cname}, {n}));\n' for n in names) +
+                       f'printf("%zu\\n", sizeof({cname}));\nreturn 0;\n}}\n')
+        exe = tmp_path / cname
+        subprocess.run(["gcc", "-std=c11", "-I", os.path.dirname(smol_b200.HEADER_PATH), "-o", str(exe), str(src)],
+                       check=True)
+        got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+        want = [getattr(pystruct, n).offset for n in names] + [ctypes.sizeof(pystruct)]
+        assert got == want, (cname, got, want)

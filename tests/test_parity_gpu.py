@@ -104,6 +104,7 @@ def test_dropin_bidirectional_leaves_uncovered_rows(cuda):
     assert_close(out[5:60], want[5:60], "windows")
 
 
+@pytest.mark.new_on_gpu
 def test_dropin_bidirectional_audio_encoder_windows(cuda):
     # Qwen3-ASR audio encoder shape (encoder.c:426-465): 104-token windows, 16 heads,
     # hd 64, a ragged last window; every 128-row query tile spans two or three windows
