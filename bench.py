@@ -614,11 +614,22 @@ def run_decoder(pk, batch: int = 1, steps: int = 50) -> dict:
 
 
 def run_other_configs(pk) -> dict:
-    """The remaining BASELINE configs on one GPU (latency- or tensor-bound; not the headline)."""
+    """The remaining BASELINE configs on one GPU (latency- or tensor-bound; not the headline).
+
+    Each runs on its own: a library error in one is reported in its entry ("error")
+    and does not stop the others or the headline measurement."""
     import smol_b200
-    res = {"cfg1": run_cfg1(), "cfg3": run_cfg3(pk), "cfg4": run_cfg4(),
-           "decoder_step_b1": run_decoder(pk, 1), "decoder_step_b8": run_decoder(pk, 8)}
-    smol_b200.check(smol_b200.last_error(), "other configs")
+    runs = {"cfg1": run_cfg1, "cfg3": lambda: run_cfg3(pk), "cfg4": run_cfg4,
+            "decoder_step_b1": lambda: run_decoder(pk, 1), "decoder_step_b8": lambda: run_decoder(pk, 8)}
+    res = {}
+    for name, fn in runs.items():
+        smol_b200.clear_error()
+        try:
+            res[name] = fn()
+            smol_b200.check(smol_b200.last_error(), name)
+        except smol_b200.SmolB200Error as e:
+            res[name] = {"error": str(e)}
+            smol_b200.clear_error()
     return res
 
 
