@@ -16,6 +16,8 @@ Only tests/ import this module.
 """
 from __future__ import annotations
 
+import struct
+
 import numpy as np
 
 import pyoracle
@@ -176,3 +178,74 @@ class QknOracle:
         bits = lambda a: to_device(pyoracle.bf16_bits(a))   # noqa: E731
         layers = [{name: (bits(w) if w.ndim == 2 else to_device(w)) for name, w in lw.items()} for lw in self.layers]
         return bits(self.E), to_device(self.final_norm), layers
+
+
+# ---------------------------------------------------------------------------
+# Cases that pin this restatement to the reference decoder (qkn_decoder.c run on the
+# same weights by oracle/_ref/qkn_weights_emul, built from tests/dropin/qkn_weights_main.c)
+# ---------------------------------------------------------------------------
+# Gemma settings as the exports set them (paligemma.c:206-230), at test scale: Gemma 2
+# (no QK-norm, attention softcap, alternating sliding layers with their own RoPE theta)
+# and Gemma 3 (QK-norm, no softcap); the window is short enough to bind.
+GEMMA2_SMALL = {"embed_normalizer": 32.0, "interleaved": True, "attn_softcap": 3.0, "sliding_window": 16,
+                "sliding": [True, False], "local_theta": 1e4, "qk_norm": False}
+GEMMA3_SMALL = {"embed_normalizer": 32.0, "interleaved": True, "attn_softcap": 0.0, "sliding_window": 16,
+                "sliding": [True, False], "local_theta": 1e4, "qk_norm": True}
+GEMMA_SHAPE = {"n_heads": 8, "n_kv_heads": 1, "head_dim": 256, "intermediate": 2048}
+PIN_CASES = {
+    "qwen3-1": {"layers": 1, "prompt_len": 96, "steps": 24, "seed": 11, "gemma": None},
+    "qwen3-2": {"layers": 2, "prompt_len": 64, "steps": 24, "seed": 12, "gemma": None},
+    "gemma2-2": {"layers": 2, "prompt_len": 64, "steps": 24, "seed": 13, "gemma": GEMMA2_SMALL},
+    "gemma3-2": {"layers": 2, "prompt_len": 64, "steps": 24, "seed": 14, "gemma": GEMMA3_SMALL},
+}
+
+
+def pin_case(name: str):
+    """(model, prompt, feed) of a pin case: the seeded model (not prefilled), its prompt,
+    and the tokens fed at each teacher-forced step -- the prompt's last token, then a
+    seeded random stream (random models' own greedy streams tend to settle on one token)."""
+    c = PIN_CASES[name]
+    shape = GEMMA_SHAPE if c["gemma"] else {}
+    m = QknOracle(layers=c["layers"], seed=c["seed"], qk_gain=3.0, vo_gain=4.0,
+                  cap=c["prompt_len"] + c["steps"] + 8, theta=1e6, eps=1e-6, gemma=c["gemma"], **shape)
+    rng = np.random.default_rng(c["seed"])
+    prompt = rng.integers(0, m.V, c["prompt_len"]).tolist()
+    feed = [prompt[-1]] + rng.integers(0, m.V, c["steps"] - 1).tolist()
+    return m, prompt, feed
+
+
+def run_teacher_forced(m: QknOracle, prompt, feed):
+    """Prefill prompt[:-1], then one forward per fed token: (tokens, margins, final normed states)."""
+    m.prefill(prompt[:-1])
+    out = [m.forward(t) for t in feed]
+    return [o[0] for o in out], [o[1] for o in out], np.stack([o[2] for o in out])
+
+
+def write_weights_file(path, m: QknOracle, prompt, feed) -> None:
+    """The input file of qkn_weights_main.c (its header comment gives the format)."""
+    bits = lambda a: np.ascontiguousarray(pyoracle.bf16_bits(a)).tobytes()        # noqa: E731
+    f32 = lambda a: np.ascontiguousarray(a, dtype=np.float32).tobytes()              # noqa: E731
+    has_ffn_norms = int("pre_ffn_norm" in m.layers[0])
+    with open(path, "wb") as f:
+        f.write(b"QKNW")
+        f.write(struct.pack("<14i", m.H, m.L, m.HQ, m.HKV, m.HD, m.I, m.V, len(prompt), len(feed), int(m.gemma),
+                            int(m.interleaved), m.sliding_window, int(m.qk_norm), has_ffn_norms))
+        f.write(struct.pack("<5f", m.eps, m.theta, m.local_theta, float(m.embed_normalizer), m.attn_softcap))
+        f.write(bits(m.E))
+        f.write(f32(m.final_norm))
+        for l, lw in enumerate(m.layers):
+            f.write(struct.pack("<i", int(m.sliding[l])))
+            for name in ("wq", "wk", "wv", "wo", "gate_up", "down"):
+                f.write(bits(lw[name]))
+            names = ["input_norm", "post_attn_norm"] + (["q_norm", "k_norm"] if m.qk_norm else []) + \
+                (["pre_ffn_norm", "post_ffn_norm"] if has_ffn_norms else [])
+            for name in names:
+                f.write(f32(lw[name]))
+        f.write(np.asarray(prompt, "<i4").tobytes())
+        f.write(np.asarray(feed, "<i4").tobytes())
+
+
+def read_reference_steps(path, n_steps: int, hidden: int):
+    """qkn_weights_main.c's output: per step the greedy token and the final normed state."""
+    raw = np.fromfile(path, dtype=np.uint8).reshape(n_steps, 4 + 4 * hidden)
+    return raw[:, :4].copy().view("<i4")[:, 0], raw[:, 4:].copy().view("<f4")

@@ -19,15 +19,13 @@ import torch
 
 import pyoracle
 import smol_b200
-from qkn_decoder_oracle import QknOracle, geglu
+from qkn_decoder_oracle import GEMMA2_SMALL, GEMMA3_SMALL, GEMMA_SHAPE, QknOracle, geglu
 
 pytestmark = [pytest.mark.gpu, pytest.mark.new_on_gpu]
 
-GEMMA_SHAPE = {"n_heads": 8, "n_kv_heads": 1, "head_dim": 256, "intermediate": 2048}
-GEMMA2 = {"embed_normalizer": 32.0, "interleaved": True, "attn_softcap": 3.0, "sliding_window": 64,
-          "sliding": [True, False], "local_theta": 1e4, "qk_norm": False}
-GEMMA3 = {"embed_normalizer": 32.0, "interleaved": True, "attn_softcap": 0.0, "sliding_window": 64,
-          "sliding": [True, False], "local_theta": 1e4, "qk_norm": True}
+# the pinned Gemma settings with a window that binds over a 300-token prompt
+GEMMA2 = {**GEMMA2_SMALL, "sliding_window": 64}
+GEMMA3 = {**GEMMA3_SMALL, "sliding_window": 64}
 
 
 def _dev(cuda):

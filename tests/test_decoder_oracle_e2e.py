@@ -1,12 +1,16 @@
 """Pins the whole decoder-step restatement (oracle/qkn_decoder_oracle.py) to the reference decoder.
 
-The oracle's seeded model is written to a file and run by oracle/_ref/qkn_weights_emul:
-the reference's own qkn_decoder_prefill / qkn_decoder_forward (qkn_decoder.c:369-714)
-with its kernels, attention over the cache formats the oracle also keeps (K bf16, V
-fp16).  Both sides are teacher-forced on the same tokens (a seeded random stream), so
-every step is compared on the same history: the greedy token wherever the top-2 logit margin exceeds the
-difference the hidden states allow, and the final normalised hidden state within
-rel-L2 3e-3 at every step and 1e-4 / 1e-3 (one / two layers) at the median.
+The oracle's seeded model goes through a file to oracle/_ref/qkn_weights_emul: the
+reference's own qkn_decoder_prefill / qkn_decoder_forward (qkn_decoder.c:369-714) with
+its kernels, attention over the cache formats the oracle also keeps (K bf16, V fp16).
+Both sides are teacher-forced on the same tokens (a seeded random stream), so every
+step is compared on the same history: the greedy token wherever the top-2 margin
+exceeds the difference the hidden states allow, and the final normalised hidden state
+within rel-L2 3e-3 at every step and 1e-4 / 1e-3 (one / two layers) at the median.
+The cases (oracle PIN_CASES) cover Qwen3 with one and two layers and the Gemma 2 /
+Gemma 3 settings.  Where the reference binary is built the comparison runs live;
+everywhere it also runs against the reference's outputs committed in
+tests/golden/decoder_cases.npz (tests/golden/make_decoder_golden.py).
 
 The tolerance is that of storage rounding, not of the restatement: a cache element
 whose fp32 value lies within the accumulation-order difference (~1e-6) of a bf16
@@ -14,94 +18,27 @@ rounding boundary is stored one bf16 unit (2^-8) apart, and the sharp attention 
 this model (QK-norm gain 3) carries that to the output.  The oracle against itself
 with float64 instead of float32 accumulation in its matrix products differs by the
 same amount: up to 1.4e-4 (one layer) and 1.5e-3 (two layers, where layer 1's cache
-is fed by layer 0's prefill attention), median 8e-6 / 5e-4.  CPU only; skipped where
-the binary was not built.
+is fed by layer 0's prefill attention), median 8e-6 / 5e-4.  CPU only.
 """
 import os
-import struct
 import subprocess
 
 import numpy as np
 import pytest
 
 import pyoracle
-from qkn_decoder_oracle import QknOracle
+from qkn_decoder_oracle import PIN_CASES, pin_case, read_reference_steps, run_teacher_forced, write_weights_file
 
 BIN = os.path.join(os.path.dirname(pyoracle.__file__), "_ref", "qkn_weights_emul")
-pytestmark = pytest.mark.skipif(not os.path.exists(BIN), reason="oracle/_ref/qkn_weights_emul not built")
-
-THETA, EPS = 1e6, 1e-6
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "decoder_cases.npz")
 
 
-def _write_model(path, m: QknOracle, prompt, feed):
-    bits = lambda a: np.ascontiguousarray(pyoracle.bf16_bits(a)).tobytes()        # noqa: E731
-    f32 = lambda a: np.ascontiguousarray(a, dtype=np.float32).tobytes()              # noqa: E731
-    has_ffn_norms = int("pre_ffn_norm" in m.layers[0])
-    with open(path, "wb") as f:
-        f.write(b"QKNW")
-        f.write(struct.pack("<14i", m.H, m.L, m.HQ, m.HKV, m.HD, m.I, m.V, len(prompt), len(feed), int(m.gemma),
-                            int(m.interleaved), m.sliding_window, int(m.qk_norm), has_ffn_norms))
-        f.write(struct.pack("<5f", EPS, m.theta, m.local_theta, float(m.embed_normalizer), m.attn_softcap))
-        f.write(bits(m.E))
-        f.write(f32(m.final_norm))
-        for l, lw in enumerate(m.layers):
-            f.write(struct.pack("<i", int(m.sliding[l])))
-            for name in ("wq", "wk", "wv", "wo", "gate_up", "down"):
-                f.write(bits(lw[name]))
-            names = ["input_norm", "post_attn_norm"] + (["q_norm", "k_norm"] if m.qk_norm else []) + \
-                (["pre_ffn_norm", "post_ffn_norm"] if has_ffn_norms else [])
-            for name in names:
-                f.write(f32(lw[name]))
-        f.write(np.asarray(prompt, "<i4").tobytes())
-        f.write(np.asarray(feed, "<i4").tobytes())
-
-
-def _read_steps(path, n_steps, hidden):
-    raw = np.fromfile(path, dtype=np.uint8).reshape(n_steps, 4 + 4 * hidden)
-    tokens = raw[:, :4].copy().view("<i4")[:, 0]
-    xs = raw[:, 4:].copy().view("<f4")
-    return tokens, xs
-
-
-# Gemma settings as the exports set them (paligemma.c:206-230), at test scale: Gemma 2
-# (no QK-norm, attention softcap, alternating sliding layers with their own RoPE theta)
-# and Gemma 3 (QK-norm, no softcap); the window is short enough to bind in the test.
-GEMMA2 = {"embed_normalizer": 32.0, "interleaved": True, "attn_softcap": 3.0, "sliding_window": 16,
-          "sliding": [True, False], "local_theta": 1e4, "qk_norm": False}
-GEMMA3 = {"embed_normalizer": 32.0, "interleaved": True, "attn_softcap": 0.0, "sliding_window": 16,
-          "sliding": [True, False], "local_theta": 1e4, "qk_norm": True}
-GEMMA_SHAPE = {"n_heads": 8, "n_kv_heads": 1, "head_dim": 256, "intermediate": 2048}
-
-
-@pytest.mark.parametrize("layers,prompt_len,steps,seed,gemma", [(1, 96, 24, 11, None), (2, 64, 24, 12, None),
-                                                                 (2, 64, 24, 13, GEMMA2), (2, 64, 24, 14, GEMMA3)],
-                         ids=["qwen3-1", "qwen3-2", "gemma2-2", "gemma3-2"])
-def test_oracle_decoder_matches_reference_decoder(tmp_path, layers, prompt_len, steps, seed, gemma):
-    shape = GEMMA_SHAPE if gemma else {}
-    m = QknOracle(layers=layers, seed=seed, qk_gain=3.0, vo_gain=4.0, cap=prompt_len + steps + 8,
-                  theta=THETA, eps=EPS, gemma=gemma, **shape)
-    rng = np.random.default_rng(seed)
-    prompt = rng.integers(0, m.V, prompt_len).tolist()
-    m.prefill(prompt[:-1])
-    # teacher forcing on the prompt's last token, then a seeded random stream: random
-    # models' own greedy streams tend to settle on one token, a random history does not
-    feed = [prompt[-1]] + rng.integers(0, m.V, steps - 1).tolist()
-    tokens, margins, xs = [], [], []
-    for s in range(steps):
-        tok, margin, xf = m.forward(feed[s])
-        tokens.append(tok)
-        margins.append(margin)
-        xs.append(xf)
-
-    inp, out = tmp_path / "model.bin", tmp_path / "steps.bin"
-    _write_model(inp, m, prompt, feed)
-    subprocess.run([BIN, str(inp), str(out)], check=True, timeout=300)
-    ref_tokens, ref_xs = _read_steps(out, steps, m.H)
-
+def _check(m, tokens, margins, xs, ref_tokens, ref_xs):
+    steps = len(tokens)
     e_norm = float(np.max(np.linalg.norm(m.E, axis=1)))
     errs = [pyoracle.rel_l2(xs[s], ref_xs[s]) for s in range(steps)]
     assert max(errs) < 3e-3, errs
-    assert float(np.median(errs)) < (1e-4 if layers == 1 else 1e-3), errs
+    assert float(np.median(errs)) < (1e-4 if m.L == 1 else 1e-3), errs
     for s in range(steps):
         # |logit difference| <= |E_v| * |x - x_ref| for every v: a token may differ only
         # where the oracle's own top-2 margin is within twice that bound.
@@ -109,3 +46,25 @@ def test_oracle_decoder_matches_reference_decoder(tmp_path, layers, prompt_len, 
         if margins[s] > bound:
             assert ref_tokens[s] == tokens[s], (s, margins[s], bound)
     assert len(set(tokens)) > steps // 3          # the outputs are not one repeated token
+
+
+@pytest.mark.skipif(not os.path.exists(BIN), reason="oracle/_ref/qkn_weights_emul not built")
+@pytest.mark.parametrize("case", list(PIN_CASES))
+def test_oracle_decoder_matches_reference_decoder(tmp_path, case):
+    m, prompt, feed = pin_case(case)
+    inp, out = tmp_path / "model.bin", tmp_path / "steps.bin"
+    write_weights_file(inp, m, prompt, feed)
+    tokens, margins, xs = run_teacher_forced(m, prompt, feed)
+    subprocess.run([BIN, str(inp), str(out)], check=True, timeout=300)
+    ref_tokens, ref_xs = read_reference_steps(out, len(feed), m.H)
+    _check(m, tokens, margins, xs, ref_tokens, ref_xs)
+
+
+@pytest.mark.skipif(not os.path.exists(GOLDEN), reason="tests/golden/decoder_cases.npz not generated")
+@pytest.mark.parametrize("case", list(PIN_CASES))
+def test_oracle_decoder_matches_reference_golden(case):
+    g = np.load(GOLDEN)
+    m, prompt, feed = pin_case(case)
+    assert g[f"{case}/feed"].tolist() == feed and g[f"{case}/prompt"].tolist() == prompt
+    tokens, margins, xs = run_teacher_forced(m, prompt, feed)
+    _check(m, tokens, margins, xs, g[f"{case}/tokens"], g[f"{case}/x"])
