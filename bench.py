@@ -60,8 +60,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=workload.CFG2["layers"])
     ap.add_argument("--no-decode", action="store_true", help="prefill measurement only (profiling helper)")
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg 1/3/4 block")
-    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4", "decoder"], default=None,
-                    help="run one of the cfg 1/3/4 measurements alone (profiling helper)")
+    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4", "decoder", "audio"], default=None,
+                    help="run one of the other measurements alone: cfg 1/3/4, the decoder step, or the audio-encoder "
+                         "windows (not in the default run yet)")
     ap.add_argument("--images", type=int, default=None, help="cfg 3 image count override")
     ap.add_argument("--prefill-shape", default=None, help="B,L override of the cfg 5 prefill shape")
     return ap.parse_args()
@@ -506,6 +507,40 @@ def run_cfg3(pk, images: int | None = None, layers: int | None = None) -> dict:
             "flops": fl3, "kernel": "prefill2_kernel<64> (full mask)"}
 
 
+def run_audio_windows(pk, segments: int = 64) -> dict:
+    """Windowed bidirectional attention of the Qwen3-ASR audio encoder (encoder.c:426-465):
+    ten 104-token windows per segment, 16 heads, hd 64, one layer; FLOPs count only the
+    pairs inside a window (4 * hd per pair and head)."""
+    import torch
+
+    import smol_b200
+    g = torch.Generator(device="cuda").manual_seed(19)
+    win, n_win, h, hd = 104, 10, 16, 64
+    N = win * n_win
+    q = torch.randn((segments, N, h * hd), device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn((segments, N, h * hd), device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn((segments, N, h * hd), device="cuda", generator=g).to(torch.float16)
+    o = torch.empty((segments, N, h * hd), device="cuda")
+    ws = torch.arange(0, N + 1, win, dtype=torch.int32, device="cuda")
+
+    def layer():
+        smol_b200.prefill_attention(o, q, k, v, segments, N, N, h, h, hd, 1 / 8.0, mask_kind=smol_b200.MASK_WINDOWS,
+                                    window_starts=ws)
+    layer()
+    a, b = _ev(), _ev()
+    a.record()
+    for _ in range(5):
+        layer()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / 5
+    fl = 4 * hd * h * n_win * win * win * segments
+    return {"workload": f"{segments} segments x {n_win} windows of {win} tokens, 16 heads, hd 64, one layer",
+            "ms": round(ms, 4), "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
+            "frac_of_bf16_peak": round(fl / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 4), "flops": fl,
+            "kernel": "prefill2_kernel<64> (window mask)"}
+
+
 def run_cfg4() -> dict:
     """cfg 4: PaliGemma prefix-LM, batch 32, 18 layers, MQA 8/1, hd 256; 128-step suffix."""
     import torch
@@ -818,7 +853,8 @@ def main():
         torch.cuda.set_device(0)
         pk = peaks()
         fn = {"cfg1": run_cfg1, "cfg3": lambda: run_cfg3(pk, args.images, 1 if args.images else None),
-              "cfg4": run_cfg4, "decoder": lambda: [run_decoder(pk, 1), run_decoder(pk, 8)]}[args.only_config]
+              "cfg4": run_cfg4, "decoder": lambda: [run_decoder(pk, 1), run_decoder(pk, 8)],
+              "audio": lambda: run_audio_windows(pk)}[args.only_config]
         print(json.dumps({args.only_config: fn()}))
         return
     run_ours(args)
