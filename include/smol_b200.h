@@ -349,6 +349,69 @@ SMOL_B200_API int smol_b200_argmax_bf16(void *stream, int *tokens_out, const flo
                                         void *workspace, size_t workspace_bytes);
 SMOL_B200_API size_t smol_b200_argmax_workspace_bytes(int n_seqs, int vocab);
 
+/* ===========================================================================
+ * Part 5 -- SigLIP vision encoder on the device (siglip_forward, siglip.c:71-156).
+ *
+ * Patch embedding (the kernel = stride = patch convolution of siglip.c:24-65 as a
+ * GEMM over unfolded patches, conv2d.c:13-95), position embeddings, the encoder
+ * layers (LayerNorm -> Q/K/V with bias -> bidirectional attention over all patches
+ * -> output projection + residual; LayerNorm -> fc1 + bias -> GELU (tanh form) -> fc2
+ * + bias + residual) and the post-LayerNorm, for a batch of images.  The linear layers
+ * run as tcgen05 GEMMs with bf16 operands and fp32 accumulation; the residual stream
+ * stays fp32; LayerNorm, attention and GELU outputs are rounded to bf16 (V to fp16)
+ * where they become GEMM / attention operands.  head_dim must be 64, 128 or 256.
+ * Every pointer is device memory except `layers` (a host array).
+ * =========================================================================== */
+#define SMOL_B200_GEMM_OUT_F32 0      /* C = result (fp32)                       */
+#define SMOL_B200_GEMM_OUT_BF16 1     /* C = bf16(result)                        */
+#define SMOL_B200_GEMM_OUT_F16 2      /* C = fp16(result)                        */
+#define SMOL_B200_GEMM_OUT_F32_ADD 3  /* C += result (fp32, the residual stream) */
+
+typedef struct smol_b200_siglip_layer {
+    const float *ln1_w, *ln1_b;                   /* [hidden]                     */
+    const uint16_t *wq, *wk, *wv, *wo;            /* [hidden][hidden] bf16        */
+    const float *bq, *bk, *bv, *bo;               /* [hidden]                     */
+    const float *ln2_w, *ln2_b;                   /* [hidden]                     */
+    const uint16_t *fc1;                          /* [ffn][hidden] bf16           */
+    const float *b1;                              /* [ffn]                        */
+    const uint16_t *fc2;                          /* [hidden][ffn] bf16           */
+    const float *b2;                              /* [hidden]                     */
+} smol_b200_siglip_layer;
+
+typedef struct smol_b200_siglip_model {
+    int hidden, heads, ffn, n_layers, patch, image_size, num_positions;
+    float eps;                                    /* LayerNorm epsilon            */
+    const uint16_t *patch_w;                      /* [hidden][patch_ld] bf16, columns
+                                                     (channel, ky, kx) of 3*patch^2 */
+    int patch_ld;                                 /* >= 3*patch^2, multiple of 8  */
+    const float *patch_b;                         /* [hidden]                     */
+    const float *pos;                             /* [num_positions][hidden]      */
+    const float *post_w, *post_b;                 /* [hidden]                     */
+    const smol_b200_siglip_layer *layers;         /* host array of n_layers       */
+} smol_b200_siglip_model;
+
+/* Device workspace of smol_b200_siglip_forward for n_images images. */
+SMOL_B200_API size_t smol_b200_siglip_workspace_bytes(const smol_b200_siglip_model *model, int n_images);
+
+/* images: [n_images][3][image_size][image_size] fp32; out: [n_images][n_patches][hidden]
+ * fp32 with n_patches = (image_size/patch)^2 <= num_positions. */
+SMOL_B200_API int smol_b200_siglip_forward(void *stream, float *out, const float *images, int n_images,
+                                           const smol_b200_siglip_model *model, void *workspace,
+                                           size_t workspace_bytes);
+
+/* The building blocks:
+ *   C[m][n] (+)= sum_k A[m][k] * W[n][k] + bias[n] + add[m % add_rows][n], then GELU-tanh
+ *   when gelu != 0; stored as out_kind says.  A bf16 [M][lda], W bf16 [N][ldw] (K-major,
+ *   16-byte aligned, lda / ldw multiples of 8); bias, add optional. */
+SMOL_B200_API int smol_b200_gemm_bf16(void *stream, void *out, int64_t ldo, int out_kind, const uint16_t *a,
+                                      int64_t lda, const uint16_t *w, int64_t ldw, const float *bias,
+                                      const float *add, int64_t ld_add, int add_rows, int m, int n, int k,
+                                      int gelu);
+/* out[r] = (x[r] - mean) / sqrtf(var + eps) * w + b per row (smol_layer_norm,
+ * layernorm.c:17-124); out bf16 when out_bf16 != 0, else fp32 (may alias x). */
+SMOL_B200_API int smol_b200_layer_norm(void *stream, void *out, int out_bf16, const float *x, const float *w,
+                                       const float *b, int rows, int hidden, float eps);
+
 #ifdef __cplusplus
 }
 #endif

@@ -628,6 +628,38 @@ int smol_b200_ipc_close(void *dev_ptr)
 }
 
 // ---------------------------------------------------------------------------
+// Part 5
+// ---------------------------------------------------------------------------
+size_t smol_b200_siglip_workspace_bytes(const smol_b200_siglip_model *model, int n_images)
+{
+    return siglip_workspace_bytes(model, n_images);
+}
+
+int smol_b200_siglip_forward(void *stream, float *out, const float *images, int n_images,
+                             const smol_b200_siglip_model *model, void *workspace, size_t workspace_bytes)
+{
+    return record(siglip_forward(static_cast<cudaStream_t>(stream), out, images, n_images, model, workspace,
+                                 workspace_bytes),
+                  "smol_b200_siglip_forward");
+}
+
+int smol_b200_gemm_bf16(void *stream, void *out, int64_t ldo, int out_kind, const uint16_t *a, int64_t lda,
+                        const uint16_t *w, int64_t ldw, const float *bias, const float *add, int64_t ld_add,
+                        int add_rows, int m, int n, int k, int gelu)
+{
+    return record(gemm_bf16(static_cast<cudaStream_t>(stream), out, ldo, out_kind, a, lda, w, ldw, bias, add, ld_add,
+                            add_rows, m, n, k, gelu),
+                  "smol_b200_gemm_bf16");
+}
+
+int smol_b200_layer_norm(void *stream, void *out, int out_bf16, const float *x, const float *w, const float *b,
+                         int rows, int hidden, float eps)
+{
+    return record(layer_norm(static_cast<cudaStream_t>(stream), out, out_bf16, x, w, b, rows, hidden, eps),
+                  "smol_b200_layer_norm");
+}
+
+// ---------------------------------------------------------------------------
 // Part 4
 // ---------------------------------------------------------------------------
 size_t smol_b200_qkn_step_workspace_bytes(const smol_b200_qkn_model *model, int n_seqs, int max_kv_len)

@@ -1,0 +1,283 @@
+// gemm.cu -- bf16 GEMM on the 5th-generation tensor cores, with the epilogues the
+// SigLIP encoder's linear layers need.
+//
+//   C[m][n] = sum_k A[m][k] * W[n][k]  (+ bias[n]) (+ add[m % add_rows][n]) (GELU-tanh)
+//   stored as fp32, bf16 or fp16, or added into an fp32 C (the residual stream)
+//
+// This is smol_linear (matmul.c:70-100: y = x W^T + b) and the bias + GELU / residual
+// steps around it in siglip_forward (siglip.c:116-146), with A and W in bf16 and fp32
+// accumulation.  Both operands are K-major, as the reference stores them (x rows, W
+// rows), so TMA copies 128-row x 64-column boxes straight into 128-byte-swizzled
+// shared memory and tcgen05.mma reads them through matrix descriptors.  Rows past M or
+// N and columns past K are outside the tensor maps and arrive as zeros; the epilogue
+// writes only rows < M and columns < N.
+//
+// One CTA computes one 128 x 128 tile of C: warp 0 issues the TMA loads of a 3-stage
+// ring of A / W boxes, warp 1 allocates 128 TMEM columns and issues the MMAs (4 per
+// 64-wide k block, K = 16 each), warps 2-5 read the fp32 accumulator back from TMEM
+// (each warp the 32 lanes its index allows) and apply the epilogue.  96 KB of shared
+// memory, so two CTAs share an SM and one's epilogue overlaps the other's MMAs.
+// Every wait is bounded (2 s), reports through the device error word and lets the CTA
+// drain its copies and MMAs before it exits.
+#include <stdio.h>
+#include <string.h>
+
+#include "b200_common.cuh"
+#include "runtime.h"
+
+namespace smolb200 {
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 64;
+constexpr int kStages = 3;
+constexpr int kGemmThreads = 192;
+constexpr int kProducerWarp = 0, kMmaWarp = 1;
+constexpr int kABytes = kBM * kBK * 2;   // 16 KB
+constexpr int kWBytes = kBN * kBK * 2;   // 16 KB
+constexpr int kStageBytes = kABytes + kWBytes;
+constexpr int kTmemCols = kBN;
+constexpr uint32_t kIdesc = umma_idesc_f16(kBM, kBN, true, false);   // bf16 x bf16 -> f32, both K-major
+
+struct GemmBarriers {
+    uint64_t full[kStages], empty[kStages];
+    uint64_t acc_full, mma_done;
+    uint32_t tmem_base;
+    int abort;
+};
+
+constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;   // alignment slack, ring, barriers
+
+struct GemmParams {
+    CUtensorMap ta, tw;
+    void *out;
+    long long ldo;
+    const float *bias;        // [N] or null
+    const float *add;         // [add_rows][ld_add] or null
+    long long ld_add;
+    int add_rows;
+    int M, N, K;
+    int out_kind;             // SMOL_B200_GEMM_OUT_*
+    int gelu;
+    int vec_ok;               // rows of `out` (and `add`) are 16-byte aligned
+    unsigned *err;
+};
+
+__device__ __forceinline__ float gelu_tanh(float x)
+{
+    // smol_gelu (activation.c:29-36)
+    const float x3 = x * x * x;
+    const float inner = 0.7978845608028654f * (x + 0.044715f * x3);
+    return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 2) gemm_bf16_kernel(const __grid_constant__ GemmParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    GemmBarriers *bars = reinterpret_cast<GemmBarriers *>(smem + kStages * kStageBytes);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int n0 = blockIdx.x * kBN, m0 = blockIdx.y * kBM;
+    const int n_kb = (p.K + kBK - 1) / kBK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_u32(&bars->full[s]), 1);
+            mbar_init(smem_u32(&bars->empty[s]), 1);
+        }
+        mbar_init(smem_u32(&bars->acc_full), 1);
+        mbar_init(smem_u32(&bars->mma_done), 1);
+        bars->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(smem_u32(&bars->tmem_base), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            tma_prefetch_desc(&p.ta);
+            tma_prefetch_desc(&p.tw);
+            int issued = 0;
+            for (int kb = 0; kb < n_kb; ++kb) {
+                const int st = kb % kStages;
+                if (kb >= kStages &&
+                    !mbar_wait(smem_u32(&bars->empty[st]), ((kb / kStages) - 1) & 1, p.err, kErrWaitTmaEmpty)) {
+                    atomicExch(&bars->abort, 1);
+                    break;
+                }
+                if (atomicAdd(&bars->abort, 0)) break;
+                const uint32_t full = smem_u32(&bars->full[st]);
+                const uint32_t sa = smem_u32(smem + st * kStageBytes);
+                mbar_arrive_expect_tx(full, kStageBytes);
+                tma_load_2d(sa, &p.ta, full, kb * kBK, m0);
+                tma_load_2d(sa + kABytes, &p.tw, full, kb * kBK, n0);
+                ++issued;
+            }
+            // every issued copy lands before the CTA may exit
+            for (int kb = issued > kStages ? issued - kStages : 0; kb < issued; ++kb)
+                mbar_wait(smem_u32(&bars->full[kb % kStages]), (kb / kStages) & 1, p.err, kErrDrain);
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            for (int kb = 0; kb < n_kb; ++kb) {
+                const int st = kb % kStages;
+                if (!mbar_wait(smem_u32(&bars->full[st]), (kb / kStages) & 1, p.err, kErrWaitTmaFull) ||
+                    atomicAdd(&bars->abort, 0)) {
+                    atomicExch(&bars->abort, 1);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + st * kStageBytes);
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk) {   // 16 bf16 = 32 bytes along K inside the swizzled row
+                    const uint64_t adesc = umma_sdesc_sw128(sa + kk * 32, 16, 1024);
+                    const uint64_t bdesc = umma_sdesc_sw128(sa + kABytes + kk * 32, 16, 1024);
+                    umma_ss(tmem, adesc, bdesc, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(smem_u32(&bars->empty[st]));
+            }
+            // the epilogue waits for this (it checks `abort` before it reads TMEM)
+            umma_commit(smem_u32(&bars->acc_full));
+            // every MMA completes before TMEM is released
+            umma_commit(smem_u32(&bars->mma_done));
+            mbar_wait(smem_u32(&bars->mma_done), 0, p.err, kErrDrain);
+        }
+    } else {
+        // ================= epilogue: thread = one row of the tile =================
+        const int quarter = warp & 3;                       // TMEM lanes this warp may read
+        const int row = m0 + quarter * 32 + lane;
+        const bool waited = mbar_wait(smem_u32(&bars->acc_full), 0, p.err, kErrWaitMma);
+        tc_fence_after();
+        // warp-uniform: tcgen05.ld is a warp-collective instruction
+        if (__all_sync(0xffffffffu, waited && atomicAdd(&bars->abort, 0) == 0)) {
+            const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+            for (int c = 0; c < kBN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(taddr + c * 32, r);
+                tmem_ld_wait();
+                const int nb = n0 + c * 32;
+                if (row >= p.M || nb >= p.N) continue;
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int n = nb + i;
+                    float x = __uint_as_float(r[i]);
+                    if (n < p.N) {
+                        if (p.bias) x += p.bias[n];
+                        if (p.add) x += p.add[static_cast<long long>(row % p.add_rows) * p.ld_add + n];
+                        if (p.gelu) x = gelu_tanh(x);
+                    }
+                    v[i] = x;
+                }
+                const bool full = p.vec_ok && nb + 32 <= p.N;
+                if (p.out_kind == SMOL_B200_GEMM_OUT_BF16 || p.out_kind == SMOL_B200_GEMM_OUT_F16) {
+                    uint16_t *o = static_cast<uint16_t *>(p.out) + static_cast<long long>(row) * p.ldo + nb;
+                    const bool h = p.out_kind == SMOL_B200_GEMM_OUT_F16;
+                    if (full) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            uint4 w;
+                            uint32_t *wp = reinterpret_cast<uint32_t *>(&w);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                const float a = v[q * 8 + 2 * j], b = v[q * 8 + 2 * j + 1];
+                                wp[j] = h ? pack_f16x2(a, b) : pack_bf16x2(a, b);
+                            }
+                            *reinterpret_cast<uint4 *>(o + q * 8) = w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {   // unrolled: v stays in registers
+                            if (nb + i >= p.N) continue;
+                            const uint32_t w = h ? pack_f16x2(v[i], 0.f) : pack_bf16x2(v[i], 0.f);
+                            o[i] = static_cast<uint16_t>(w & 0xffffu);
+                        }
+                    }
+                } else {
+                    float *o = static_cast<float *>(p.out) + static_cast<long long>(row) * p.ldo + nb;
+                    const bool acc = p.out_kind == SMOL_B200_GEMM_OUT_F32_ADD;
+                    if (full) {
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            float4 w = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                            if (acc) {
+                                const float4 o4 = *reinterpret_cast<const float4 *>(o + 4 * q);
+                                w.x += o4.x;
+                                w.y += o4.y;
+                                w.z += o4.z;
+                                w.w += o4.w;
+                            }
+                            *reinterpret_cast<float4 *>(o + 4 * q) = w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (nb + i < p.N) o[i] = acc ? o[i] + v[i] : v[i];
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace
+
+int gemm_bf16(cudaStream_t st, void *out, int64_t ldo, int out_kind, const uint16_t *a, int64_t lda,
+              const uint16_t *w, int64_t ldw, const float *bias, const float *add, int64_t ld_add, int add_rows,
+              int M, int N, int K, int gelu)
+{
+    if (M <= 0 || N <= 0) return SMOL_B200_OK;
+    if (!out || !a || !w || K <= 0 || lda < K || ldw < K || lda % 8 || ldw % 8 || ldo < N ||
+        (reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
+        out_kind < SMOL_B200_GEMM_OUT_F32 || out_kind > SMOL_B200_GEMM_OUT_F32_ADD || (add && (add_rows <= 0 || ld_add < N)))
+        return SMOL_B200_ERR_ARGS;
+    if ((M + kBM - 1) / kBM > 65535 || (N + kBN - 1) / kBN > 65535) return SMOL_B200_ERR_ARGS;   // grid limits
+    unsigned *err = device_error_word();
+    if (!err) return SMOL_B200_ERR_NO_DEVICE;
+    const int dev = current_device();
+    if (dev < 0 || dev >= 64) return SMOL_B200_ERR_CUDA;
+    static bool raised[64] = {};
+    if (!raised[dev]) {
+        if (cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) !=
+            cudaSuccess)
+            return SMOL_B200_ERR_CUDA;
+        raised[dev] = true;
+    }
+    GemmParams p;
+    memset(&p, 0, sizeof(p));
+    if (!make_tmap_2d(&p.ta, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, kBK, kBM, lda) ||
+        !make_tmap_2d(&p.tw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, N, kBK, kBN, ldw))
+        return SMOL_B200_ERR_CUDA;
+    const int esz = out_kind == SMOL_B200_GEMM_OUT_BF16 || out_kind == SMOL_B200_GEMM_OUT_F16 ? 2 : 4;
+    p.out = out;
+    p.ldo = ldo;
+    p.bias = bias;
+    p.add = add;
+    p.ld_add = ld_add;
+    p.add_rows = add_rows > 0 ? add_rows : 1;
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.out_kind = out_kind;
+    p.gelu = gelu ? 1 : 0;
+    p.vec_ok = (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (ldo * esz) % 16 == 0;
+    p.err = err;
+    const dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
+    return launch_kernel(gemm_bf16_kernel, grid, dim3(kGemmThreads), kSmemBytes, st, p) == cudaSuccess
+               ? SMOL_B200_OK
+               : SMOL_B200_ERR_CUDA;
+}
+
+}  // namespace smolb200

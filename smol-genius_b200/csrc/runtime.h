@@ -138,4 +138,14 @@ int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *m, int n_seqs, c
 int launch_decode_step_index(cudaStream_t st, int *positions, int64_t *slots, int *kv_len_next,
                              const int64_t *seq_row0, const int *kv_len, int n_seqs);
 
+// gemm.cu / siglip.cu: the SigLIP encoder (Part 5 of smol_b200.h)
+int gemm_bf16(cudaStream_t st, void *out, int64_t ldo, int out_kind, const uint16_t *a, int64_t lda,
+              const uint16_t *w, int64_t ldw, const float *bias, const float *add, int64_t ld_add, int add_rows,
+              int M, int N, int K, int gelu);
+int layer_norm(cudaStream_t st, void *out, int out_bf16, const float *x, const float *w, const float *b, int rows,
+               int hidden, float eps);
+size_t siglip_workspace_bytes(const smol_b200_siglip_model *m, int n_images);
+int siglip_forward(cudaStream_t st, float *out, const float *images, int n_images, const smol_b200_siglip_model *m,
+                   void *workspace, size_t workspace_bytes);
+
 }  // namespace smolb200

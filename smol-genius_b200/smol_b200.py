@@ -97,6 +97,13 @@ _SIGNATURES = {
     "smol_b200_ipc_get_handle": (_c_int, [_c_void, _c_void, ctypes.POINTER(ctypes.c_size_t)]),
     "smol_b200_ipc_open_handle": (_c_int, [_c_void, ctypes.POINTER(ctypes.c_void_p)]),
     "smol_b200_ipc_close": (_c_int, [_c_void]),
+    # Part 5 (SigLIP encoder)
+    "smol_b200_siglip_workspace_bytes": (_c_size, [_c_void, _c_int]),
+    "smol_b200_siglip_forward": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_void, _c_void, _c_size]),
+    "smol_b200_gemm_bf16": (_c_int, [_c_void, _c_void, _c_i64, _c_int, _c_void, _c_i64, _c_void, _c_i64, _c_void,
+                                     _c_void, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int]),
+    "smol_b200_layer_norm": (_c_int, [_c_void, _c_void, _c_int, _c_void, _c_void, _c_void, _c_int, _c_int,
+                                      _c_float]),
 }
 
 
@@ -397,3 +404,60 @@ def ipc_open(handle: bytes) -> int:
 
 def ipc_close(ptr: int) -> None:
     check(lib().smol_b200_ipc_close(ptr), "smol_b200_ipc_close")
+
+
+# ---------------------------------------------------------------------------
+# Part 5: SigLIP encoder
+# ---------------------------------------------------------------------------
+GEMM_OUT_F32, GEMM_OUT_BF16, GEMM_OUT_F16, GEMM_OUT_F32_ADD = 0, 1, 2, 3
+
+
+class SiglipLayer(ctypes.Structure):
+    """smol_b200_siglip_layer: device pointers of one encoder layer."""
+    _fields_ = [(n, ctypes.c_void_p) for n in ("ln1_w", "ln1_b", "wq", "wk", "wv", "wo", "bq", "bk", "bv", "bo",
+                                               "ln2_w", "ln2_b", "fc1", "b1", "fc2", "b2")]
+
+
+class SiglipModel(ctypes.Structure):
+    """smol_b200_siglip_model (the layers array stays referenced by the Python object)."""
+    _fields_ = [("hidden", ctypes.c_int), ("heads", ctypes.c_int), ("ffn", ctypes.c_int), ("n_layers", ctypes.c_int),
+                ("patch", ctypes.c_int), ("image_size", ctypes.c_int), ("num_positions", ctypes.c_int),
+                ("eps", ctypes.c_float), ("patch_w", ctypes.c_void_p), ("patch_ld", ctypes.c_int),
+                ("patch_b", ctypes.c_void_p), ("pos", ctypes.c_void_p), ("post_w", ctypes.c_void_p),
+                ("post_b", ctypes.c_void_p), ("layers", ctypes.POINTER(SiglipLayer))]
+
+
+def siglip_model(hidden, heads, ffn, patch, image_size, num_positions, eps, patch_w, patch_ld, patch_b, pos, post_w,
+                 post_b, layers) -> SiglipModel:
+    """layers: list of dicts mapping the SiglipLayer field names to device tensors."""
+    arr = (SiglipLayer * len(layers))()
+    for i, lw in enumerate(layers):
+        for name, _ in SiglipLayer._fields_:
+            setattr(arr[i], name, _ptr(lw[name]))
+    m = SiglipModel(hidden, heads, ffn, len(layers), patch, image_size, num_positions, eps, _ptr(patch_w), patch_ld,
+                    _ptr(patch_b), _ptr(pos), _ptr(post_w), _ptr(post_b), ctypes.cast(arr, ctypes.POINTER(SiglipLayer)))
+    m._layers = arr
+    return m
+
+
+def siglip_workspace_bytes(model: SiglipModel, n_images: int) -> int:
+    return lib().smol_b200_siglip_workspace_bytes(ctypes.byref(model), n_images)
+
+
+def siglip_forward(out, images, n_images, model: SiglipModel, workspace, stream=None):
+    check(lib().smol_b200_siglip_forward(_stream(stream), _ptr(out), _ptr(images), n_images, ctypes.byref(model),
+                                         _ptr(workspace), workspace.numel() * workspace.element_size()),
+          "smol_b200_siglip_forward")
+
+
+def gemm_bf16(out, ldo, out_kind, a, lda, w, ldw, m, n, k, bias=None, add=None, ld_add=0, add_rows=0, gelu=False,
+              stream=None):
+    check(lib().smol_b200_gemm_bf16(_stream(stream), _ptr(out), ldo, out_kind, _ptr(a), lda, _ptr(w), ldw, _ptr(bias),
+                                    _ptr(add), ld_add, add_rows, m, n, k, int(gelu)),
+          "smol_b200_gemm_bf16")
+
+
+def layer_norm(out, x, w, b, rows, hidden, eps, out_bf16=False, stream=None):
+    check(lib().smol_b200_layer_norm(_stream(stream), _ptr(out), int(out_bf16), _ptr(x), _ptr(w), _ptr(b), rows,
+                                     hidden, eps),
+          "smol_b200_layer_norm")

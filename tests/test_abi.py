@@ -133,12 +133,14 @@ def test_binding_signatures_match_header():
 
 
 def test_binding_structs_match_header(tmp_path):
-    """The ctypes mirrors of the Part-4 structs have the C layout: field names in header
-    order, and every offset and the size as gcc lays them out for include/smol_b200.h."""
+    """The ctypes mirrors of the Part-4 / Part-5 structs have the C layout: field names in
+    header order, and every offset and the size as gcc lays them out for include/smol_b200.h."""
     import ctypes
     import re
     text = re.sub(r"/\*.*?\*/", "", open(smol_b200.HEADER_PATH).read(), flags=re.S)
-    for cname, pystruct in (("smol_b200_qkn_layer", smol_b200.QknLayer), ("smol_b200_qkn_model", smol_b200.QknModel)):
+    for cname, pystruct in (("smol_b200_qkn_layer", smol_b200.QknLayer), ("smol_b200_qkn_model", smol_b200.QknModel),
+                            ("smol_b200_siglip_layer", smol_b200.SiglipLayer),
+                            ("smol_b200_siglip_model", smol_b200.SiglipModel)):
         body = re.search(r"typedef struct " + cname + r"\s*\{(.*?)\}\s*" + cname + r"\s*;", text, flags=re.S).group(1)
         names = []
         for decl in body.split(";"):
