@@ -60,9 +60,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=workload.CFG2["layers"])
     ap.add_argument("--no-decode", action="store_true", help="prefill measurement only (profiling helper)")
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg 1/3/4 block")
-    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4", "decoder", "audio"], default=None,
-                    help="run one of the other measurements alone: cfg 1/3/4, the decoder step, or the audio-encoder "
-                         "windows (not in the default run yet)")
+    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4", "decoder", "audio", "siglip"], default=None,
+                    help="run one of the other measurements alone: cfg 1/3/4, the decoder step, or (not in the "
+                         "default run yet) the audio-encoder windows or the whole SigLIP encoder")
     ap.add_argument("--images", type=int, default=None, help="cfg 3 image count override")
     ap.add_argument("--prefill-shape", default=None, help="B,L override of the cfg 5 prefill shape")
     return ap.parse_args()
@@ -541,6 +541,53 @@ def run_audio_windows(pk, segments: int = 64) -> dict:
             "kernel": "prefill2_kernel<64> (window mask)"}
 
 
+def run_siglip_encoder(pk, images: int | None = None) -> dict:
+    """The whole SigLIP-base encoder on the device (siglip_forward, Part 5): cfg 3's 128
+    images of 512 x 512 (1024 patches of 16 x 16), 12 layers, hidden 768, 12 heads, ffn
+    3072; random weights.  FLOPs: the GEMMs (patch embedding and per layer Q, K, V, O,
+    fc1, fc2) plus the attention's 4 * hd per pair and head."""
+    import torch
+
+    import smol_b200
+    g = torch.Generator(device="cuda").manual_seed(23)
+    n_img = images or workload.CFG3["images"]
+    H, NH, F, L, P, S = 768, 12, 3072, workload.CFG3["layers"], 16, 512
+    NP = (S // P) ** 2
+    kin = 3 * P * P
+
+    def mat(r, c):
+        return (torch.randn((r, c), device="cuda", generator=g) / c ** 0.5).to(torch.bfloat16)
+
+    def vec(n, mean=0.0):
+        return mean + 0.02 * torch.randn(n, device="cuda", generator=g)
+
+    layers = [{"ln1_w": vec(H, 1.0), "ln1_b": vec(H), "wq": mat(H, H), "wk": mat(H, H), "wv": mat(H, H),
+               "wo": mat(H, H), "bq": vec(H), "bk": vec(H), "bv": vec(H), "bo": vec(H), "ln2_w": vec(H, 1.0),
+               "ln2_b": vec(H), "fc1": mat(F, H), "b1": vec(F), "fc2": mat(H, F), "b2": vec(H)} for _ in range(L)]
+    keep = dict(patch_w=mat(H, kin), patch_b=vec(H), pos=vec(NP * H), post_w=vec(H, 1.0), post_b=vec(H))
+    model = smol_b200.siglip_model(H, NH, F, P, S, NP, 1e-6, keep["patch_w"], kin, keep["patch_b"], keep["pos"],
+                                   keep["post_w"], keep["post_b"], layers)
+    imgs = torch.rand((n_img, 3, S, S), device="cuda", generator=g) * 2 - 1
+    out = torch.empty((n_img, NP, H), device="cuda")
+    ws = torch.empty(smol_b200.siglip_workspace_bytes(model, n_img), dtype=torch.uint8, device="cuda")
+    smol_b200.siglip_forward(out, imgs, n_img, model, ws)
+    a, b = _ev(), _ev()
+    a.record()
+    smol_b200.siglip_forward(out, imgs, n_img, model, ws)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    T = n_img * NP
+    gemm = 2 * T * H * kin + L * 2 * T * H * (4 * H + 2 * F)
+    attn = L * workload.full_flops(NP, NH, H // NH) * n_img
+    fl = gemm + attn
+    return {"workload": f"SigLIP-base encoder, {n_img} images x {L} layers, 1024 patches, hidden 768, ffn 3072",
+            "ms": round(ms, 3), "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
+            "frac_of_bf16_peak": round(fl / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 4), "flops": fl,
+            "gemm_flops": gemm, "attention_flops": attn,
+            "kernels": "gemm_bf16_kernel (tcgen05), prefill2_kernel<64>, layer_norm_kernel, unfold / convert"}
+
+
 def run_cfg4() -> dict:
     """cfg 4: PaliGemma prefix-LM, batch 32, 18 layers, MQA 8/1, hd 256; 128-step suffix."""
     import torch
@@ -854,7 +901,8 @@ def main():
         pk = peaks()
         fn = {"cfg1": run_cfg1, "cfg3": lambda: run_cfg3(pk, args.images, 1 if args.images else None),
               "cfg4": run_cfg4, "decoder": lambda: [run_decoder(pk, 1), run_decoder(pk, 8)],
-              "audio": lambda: run_audio_windows(pk)}[args.only_config]
+              "audio": lambda: run_audio_windows(pk),
+              "siglip": lambda: run_siglip_encoder(pk, args.images)}[args.only_config]
         print(json.dumps({args.only_config: fn()}))
         return
     run_ours(args)
