@@ -95,6 +95,33 @@ def test_workspace_sizes():
     assert smol_b200.decode_step_scratch_bytes(256, 8192, 16, 8, 128) > a
 
 
+def _siglip_model(**over):
+    """A model struct with dummy (never dereferenced) device addresses: the workspace
+    query only validates the shape and pointer presence."""
+    fake = 1 << 20
+    layer = {name: fake for name, _ in smol_b200.SiglipLayer._fields_}
+    kw = dict(hidden=768, heads=12, ffn=3072, patch=16, image_size=512, num_positions=1024, eps=1e-6, patch_w=fake,
+              patch_ld=768, patch_b=fake, pos=fake, post_w=fake, post_b=fake, layers=[layer, layer])
+    kw.update(over)
+    return smol_b200.siglip_model(**kw)
+
+
+def test_siglip_workspace_sizes_and_shape_checks():
+    """Host-side shape rules of Part 5: the workspace grows with the batch and is 0 (the
+    call would return SMOL_B200_ERR_ARGS) for shapes the device path does not take."""
+    one = smol_b200.siglip_workspace_bytes(_siglip_model(), 1)
+    assert one > 0 and smol_b200.siglip_workspace_bytes(_siglip_model(), 4) > 3 * one
+    # per image: unfolded patches, 4 bf16 activations and a bf16 copy of the attention
+    # output, the fp32 attention output, the bf16 fc1 output (1024 patches)
+    T = 1024
+    assert one >= T * (768 * 2 + 5 * 768 * 2 + 768 * 4 + 3072 * 2)
+    assert smol_b200.siglip_workspace_bytes(_siglip_model(heads=16), 1) == 0           # head dim 48
+    assert smol_b200.siglip_workspace_bytes(_siglip_model(num_positions=1000), 1) == 0  # fewer positions than patches
+    assert smol_b200.siglip_workspace_bytes(_siglip_model(patch_ld=770), 1) == 0       # stride not a multiple of 8
+    assert smol_b200.siglip_workspace_bytes(_siglip_model(ffn=3070), 1) == 0
+    assert smol_b200.siglip_workspace_bytes(_siglip_model(patch_w=None), 1) == 0
+
+
 def test_no_device_fails_loudly():
     import torch
     if torch.cuda.is_available():
