@@ -27,13 +27,16 @@ namespace {
 constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * 32;
 constexpr int kMaxBatch = 8;   // sequences per launch (larger batches loop)
+// Shared memory for the staged activations of one launch: launches carry up to
+// kMaxBatch sequences, fewer when k_dim is large (8 x 6400 fp32 fill it; a 16384-wide
+// down projection takes 3 sequences per launch).
 constexpr int kMaxXsBytes = 200 * 1024;
 // Warps per SM the K split aims for (SMOL_GEMV_WARPS_PER_SM, measurement knob).
 const int g_gemv_warps_per_sm = [] {
     const char *e = getenv("SMOL_GEMV_WARPS_PER_SM");
     const int v = e ? atoi(e) : 0;
     return v > 0 ? v : 8;
-}();   // staged activations: kMaxBatch x k_dim fp32 (k_dim <= 6400)
+}();
 
 struct GemvSeg {
     const uint16_t *w;
@@ -523,15 +526,18 @@ int launch_gemv_rows(cudaStream_t st, GemvParams &p)
 int run_gemv(cudaStream_t st, GemvParams p, int n_seqs)
 {
     if (p.k_dim <= 0 || p.k_dim % 8 || (p.ldx & 3) || p.total_rows <= 0) return SMOL_B200_ERR_ARGS;
-    if (gemv_smem_bytes(kMaxBatch, p.k_dim) > kMaxXsBytes) return SMOL_B200_ERR_ARGS;
+    const int per_launch = kMaxXsBytes / gemv_smem_bytes(1, p.k_dim) < kMaxBatch
+                               ? kMaxXsBytes / gemv_smem_bytes(1, p.k_dim)
+                               : kMaxBatch;
+    if (per_launch < 1) return SMOL_B200_ERR_ARGS;   // k_dim > 51200
     for (int s = 0; s < p.nseg; ++s)
         if (!p.seg[s].w || !p.seg[s].y || (reinterpret_cast<uintptr_t>(p.seg[s].w) & 15) ||
             (p.mode >= 2 && (p.seg[s].rows & 1)))
             return SMOL_B200_ERR_ARGS;
     if (!p.x || (reinterpret_cast<uintptr_t>(p.x) & 15)) return SMOL_B200_ERR_ARGS;
-    for (int b0 = 0; b0 < n_seqs; b0 += kMaxBatch) {
+    for (int b0 = 0; b0 < n_seqs; b0 += per_launch) {
         GemvParams q = p;
-        q.nb = n_seqs - b0 < kMaxBatch ? n_seqs - b0 : kMaxBatch;
+        q.nb = n_seqs - b0 < per_launch ? n_seqs - b0 : per_launch;
         q.x = p.x + static_cast<long long>(b0) * p.ldx;
         if (p.x_normed) q.x_normed = p.x_normed + static_cast<long long>(b0) * p.ldx;
         for (int s = 0; s < p.nseg; ++s) q.seg[s].y = p.seg[s].y + static_cast<long long>(b0) * p.seg[s].ldy;

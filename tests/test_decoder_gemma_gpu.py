@@ -7,7 +7,8 @@ RoPE tables, QK-norm optional.  The oracle (oracle/qkn_decoder_oracle.py, pinned
 the reference decoder on the same settings by tests/test_decoder_oracle_e2e.py)
 prefills the prompt and the device pool gets its cache rows; then both sides run the
 same teacher-forced steps.  Checked:
-  * the GELU-tanh-gated matrix-vector product (mode 3) against fp32 numpy;
+  * the GELU-tanh-gated matrix-vector product (mode 3) against fp32 numpy, and the
+    product with a 16384-wide input (fewer sequences per launch);
   * 2-layer Gemma 2 / Gemma 3 style decoders (MQA 8/1, head dim 256, one sliding layer
     with a 64-token window over a 300-token prompt): every step's final normalised
     state within rel-L2 1e-3 of the oracle's and the same token wherever the oracle's
@@ -43,6 +44,24 @@ def test_gemv_bf16_geglu(cuda, n_out, k_dim, nb):
     torch.cuda.synchronize()
     assert smol_b200.last_error() == 0
     want = geglu((X.astype(np.float64) @ W.T.astype(np.float64)).astype(np.float32))
+    assert pyoracle.rel_l2(y.cpu().numpy(), want) < 1e-5
+
+
+@pytest.mark.parametrize("nb", [1, 3, 5])
+def test_gemv_bf16_wide_k(cuda, nb):
+    """A 16384-wide input (Gemma 2B's down projection): fewer sequences per launch, so
+    the staged activations still fit shared memory."""
+    rng = np.random.default_rng(40 + nb)
+    t = _dev(cuda)
+    n_out, k_dim = 512, 16384
+    X = rng.standard_normal((nb, k_dim)).astype(np.float32)
+    W = pyoracle.round_bf16((rng.standard_normal((n_out, k_dim)) / np.sqrt(k_dim)).astype(np.float32))
+    y0 = rng.standard_normal((nb, n_out)).astype(np.float32)
+    y = t(y0)
+    smol_b200.gemv_bf16(y, n_out, t(X), k_dim, t(pyoracle.bf16_bits(W)), n_out, k_dim, nb, 1)
+    torch.cuda.synchronize()
+    assert smol_b200.last_error() == 0
+    want = y0 + (X.astype(np.float64) @ W.T.astype(np.float64)).astype(np.float32)
     assert pyoracle.rel_l2(y.cpu().numpy(), want) < 1e-5
 
 
