@@ -60,9 +60,11 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=workload.CFG2["layers"])
     ap.add_argument("--no-decode", action="store_true", help="prefill measurement only (profiling helper)")
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg 1/3/4 block")
-    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4", "decoder", "audio", "siglip"], default=None,
+    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4", "decoder", "audio", "siglip", "gemma"],
+                    default=None,
                     help="run one of the other measurements alone: cfg 1/3/4, the decoder step, or (not in the "
-                         "default run yet) the audio-encoder windows or the whole SigLIP encoder")
+                         "default run yet) the audio-encoder windows, the whole SigLIP encoder or the Gemma-"
+                         "configured decoder step")
     ap.add_argument("--images", type=int, default=None, help="cfg 3 image count override")
     ap.add_argument("--prefill-shape", default=None, help="B,L override of the cfg 5 prefill shape")
     return ap.parse_args()
@@ -695,6 +697,62 @@ def run_decoder(pk, batch: int = 1, steps: int = 50) -> dict:
                        "argmax_part/final_kernel; one CUDA graph per step"}
 
 
+def run_gemma_decoder(pk, batch: int = 1, steps: int = 30) -> dict:
+    """The device decoder step in the Gemma configuration at PaliGemma's Gemma-2B size
+    (paligemma.c:206-222 settings): 18 layers, hidden 2048, 8 heads / 1 KV head, head_dim
+    256, GeGLU 16384, vocab 257216, embedding scale sqrt(2048), interleaved RoPE,
+    attention softcap 50, every other layer sliding (window 4096, local theta 1e4),
+    pre/post-FFN norms, no QK-norm; random bf16 weights, 512 cached tokens per sequence,
+    replayed from a CUDA graph.  Bytes per step = every weight once + the attended K/V."""
+    import torch
+
+    import smol_b200
+    g = torch.Generator(device="cuda").manual_seed(29)
+    H, Lr, HQ, HKV, HD, I, V = 2048, 18, 8, 1, 256, 16384, 257216
+    qd, kvd, P, cap = HQ * HD, HKV * HD, 512, 1024
+
+    def bf(rows, cols):
+        return (torch.randn((rows, cols), device="cuda", generator=g) / np.sqrt(cols)).to(torch.bfloat16)
+
+    def near(n, mean):
+        return (mean + 0.02 * torch.randn(n, device="cuda", generator=g)).contiguous()
+
+    emb = (torch.randn((V, H), device="cuda", generator=g) / np.sqrt(H)).to(torch.bfloat16)
+    layers = [{"wq": bf(qd, H), "wk": bf(kvd, H), "wv": bf(kvd, H), "wo": bf(H, qd), "gate_up": bf(2 * I, H),
+               "down": bf(H, I), "input_norm": near(H, 1.0), "post_attn_norm": near(H, 1.0),
+               "pre_ffn_norm": near(H, 1.0), "post_ffn_norm": near(H, 1.0)} for _ in range(Lr)]
+    tabs = {}
+    for theta in (1e6, 1e4):
+        c = np.zeros((cap, HD), np.float32)
+        s_ = np.zeros((cap, HD), np.float32)
+        smol_b200.compute_rope(c, s_, np.arange(cap, dtype=np.int32), cap, HD, theta, interleaved=True)
+        tabs[theta] = (torch.from_numpy(c).cuda(), torch.from_numpy(s_).cuda())
+    model = smol_b200.qkn_model(H, HQ, HKV, HD, I, V, 1e-6, emb, near(H, 1.0), layers, rope_interleaved=True,
+                                activation=smol_b200.ACT_GEGLU, embed_normalizer=float(np.sqrt(H)),
+                                attn_softcap=50.0, sliding_window=4096, rope_cos_local=tabs[1e4][0],
+                                rope_sin_local=tabs[1e4][1], sliding=[l % 2 == 0 for l in range(Lr)])
+    rows = Lr * batch * cap
+    k_pool = torch.randn((rows, kvd), device="cuda", generator=g).to(torch.bfloat16)
+    v_pool = torch.randn((rows, kvd), device="cuda", generator=g).to(torch.float16)
+    row0 = (torch.arange(Lr * batch, device="cuda", dtype=torch.int64) * cap).contiguous()   # [layer][seq]
+    kv_len = torch.full((batch,), P, dtype=torch.int32, device="cuda")
+    ws = torch.empty(smol_b200.qkn_step_workspace_bytes(model, batch, cap - 1), dtype=torch.uint8, device="cuda")
+    tokens = torch.randint(0, V, (batch,), dtype=torch.int32, device="cuda", generator=g)
+
+    def step():
+        smol_b200.qkn_decode_step(model, batch, tokens, tokens, k_pool, v_pool, rows, row0, kv_len, cap - 1,
+                                  tabs[1e6][0], tabs[1e6][1], ws, advance=True)
+    ms = _time_graph(_graph(step), steps)
+    smol_b200.check(smol_b200.last_error(), "gemma decoder step")
+    weight_bytes = (Lr * (qd * H + 2 * kvd * H + H * qd + 2 * I * H + H * I) + V * H) * 2
+    mean_len = P + 4 + steps / 2 + 1
+    kv_bytes = int(Lr * batch * mean_len * kvd * 2 * 2)
+    gbs = (weight_bytes + kv_bytes) / (ms * 1e-3) / 1e9
+    return {"workload": f"Gemma-2B-size decode step (PaliGemma settings, 18 layers, vocab 257216), batch {batch}",
+            "us_per_step": round(ms * 1e3, 1), "tokens_per_s": round(batch / (ms * 1e-3), 1),
+            "bytes_per_step": weight_bytes + kv_bytes, "gbs": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 4)}
+
+
 def run_other_configs(pk) -> dict:
     """The remaining BASELINE configs on one GPU (latency- or tensor-bound; not the headline).
 
@@ -902,7 +960,8 @@ def main():
         fn = {"cfg1": run_cfg1, "cfg3": lambda: run_cfg3(pk, args.images, 1 if args.images else None),
               "cfg4": run_cfg4, "decoder": lambda: [run_decoder(pk, 1), run_decoder(pk, 8)],
               "audio": lambda: run_audio_windows(pk),
-              "siglip": lambda: run_siglip_encoder(pk, args.images)}[args.only_config]
+              "siglip": lambda: run_siglip_encoder(pk, args.images),
+              "gemma": lambda: [run_gemma_decoder(pk, 1), run_gemma_decoder(pk, 8)]}[args.only_config]
         print(json.dumps({args.only_config: fn()}))
         return
     run_ours(args)
