@@ -6,6 +6,7 @@
 * without a usable device a drop-in call records SMOL_B200_ERR_NO_DEVICE and
   zero-fills its output -- it never computes on the CPU.
 """
+import ctypes
 import os
 import re
 import subprocess
@@ -104,6 +105,30 @@ def _siglip_model(**over):
               patch_ld=768, patch_b=fake, pos=fake, post_w=fake, post_b=fake, layers=[layer, layer])
     kw.update(over)
     return smol_b200.siglip_model(**kw)
+
+
+def test_qkn_model_configuration_checks():
+    """Host-side rules of the Part-4 model struct: the Qwen3 and Gemma configurations are
+    accepted (non-zero workspace), malformed ones are not (0: the step would return
+    SMOL_B200_ERR_ARGS)."""
+    fake = 1 << 20
+    layer = {name: fake for name, t in smol_b200.QknLayer._fields_ if t is ctypes.c_void_p}
+
+    def ws(**over):
+        kw = dict(hidden=1024, n_heads=16, n_kv_heads=8, head_dim=128, intermediate=3072, vocab=4096, eps=1e-6,
+                  tok_embeddings=fake, final_norm=fake, layers=[layer, layer])
+        kw.update(over)
+        return smol_b200.qkn_step_workspace_bytes(smol_b200.qkn_model(**kw), 2, 511)
+
+    qwen = ws()
+    assert qwen > 0
+    assert ws(activation=smol_b200.ACT_GEGLU, embed_normalizer=32.0, attn_softcap=50.0, sliding_window=4096,
+              rope_cos_local=fake, rope_sin_local=fake, sliding=[True, False], rope_interleaved=True) == qwen
+    assert ws(activation=2) == 0
+    assert ws(sliding_window=-1) == 0
+    assert ws(rope_cos_local=fake) == 0              # one local table without the other
+    assert ws(n_kv_heads=5) == 0                     # 16 heads do not split into 5 groups
+    assert ws(intermediate=3070) == 0
 
 
 def test_siglip_workspace_sizes_and_shape_checks():
