@@ -333,6 +333,21 @@ SMOL_B200_API int smol_b200_qkn_decode_step(
     const int64_t *layer_row0, int *kv_len, int max_kv_len, const float *rope_cos,
     const float *rope_sin, int advance, void *workspace, size_t workspace_bytes);
 
+/* Prefill of one sequence (qkn_decoder_prefill, qkn_decoder.c:369-564) on the device:
+ * tokens[0..n_tokens) (device) at positions start.. .  Per layer the projections run as
+ * tcgen05 GEMMs over bf16 activations (the RMSNorm outputs, the attention output and
+ * the gated activation are rounded to bf16 as GEMM operands; the residual stream stays
+ * fp32), K / V go to the pool rows layer_row0_host[l] + position (a HOST array of
+ * n_layers rows), and the causal prefill attention covers positions [0, start +
+ * n_tokens) (sliding layers their window).  No logits, as the reference; a decode step
+ * with kv_len = start + n_tokens continues from it.  rope tables: >= start + n_tokens
+ * rows.  head_dim 64, 128 or 256. */
+SMOL_B200_API size_t smol_b200_qkn_prefill_workspace_bytes(const smol_b200_qkn_model *model, int n_tokens);
+SMOL_B200_API int smol_b200_qkn_prefill(void *stream, const smol_b200_qkn_model *model, const int *tokens,
+                                        int n_tokens, int start, uint16_t *k_pool, uint16_t *v_pool,
+                                        int64_t pool_rows, const int64_t *layer_row0_host, const float *rope_cos,
+                                        const float *rope_sin, void *workspace, size_t workspace_bytes);
+
 /* The building blocks of the step, for callers that orchestrate their own decoder:
  *   y[b][n] (+)= sum_k x[b][k] * W[n][k]    mode 0: store, 1: add into y (residual),
  *   2: SiLU-gated pairs, y[b][r] = silu(s[2r]) * s[2r+1] over W's 2*n_out rows
@@ -400,13 +415,19 @@ SMOL_B200_API int smol_b200_siglip_forward(void *stream, float *out, const float
                                            size_t workspace_bytes);
 
 /* The building blocks:
- *   C[m][n] (+)= sum_k A[m][k] * W[n][k] + bias[n] + add[m % add_rows][n], then GELU-tanh
- *   when gelu != 0; stored as out_kind says.  A bf16 [M][lda], W bf16 [N][ldw] (K-major,
- *   16-byte aligned, lda / ldw multiples of 8); bias, add optional. */
+ *   C[m][n] (+)= sum_k A[m][k] * W[n][k] + bias[n] + add[m % add_rows][n], stored as
+ *   out_kind says.  A bf16 [M][lda], W bf16 [N][ldw] (K-major, 16-byte aligned, lda / ldw
+ *   multiples of 8); bias, add optional.  act: SMOL_B200_ACT_NONE, _GELU (GELU-tanh of
+ *   every element), or _SWIGLU / _GEGLU: W's rows are interleaved gate/up pairs and
+ *   C[m][j] = act(c[2j]) * c[2j+1] for j < n/2 (bf16 or fp32 out, no `add`). */
+#define SMOL_B200_ACT_NONE 0
+#define SMOL_B200_ACT_GELU 1
+#define SMOL_B200_ACT_SWIGLU 2
+#define SMOL_B200_ACT_GEGLU 3
 SMOL_B200_API int smol_b200_gemm_bf16(void *stream, void *out, int64_t ldo, int out_kind, const uint16_t *a,
                                       int64_t lda, const uint16_t *w, int64_t ldw, const float *bias,
                                       const float *add, int64_t ld_add, int add_rows, int m, int n, int k,
-                                      int gelu);
+                                      int act);
 /* out[r] = (x[r] - mean) / sqrtf(var + eps) * w + b per row (smol_layer_norm,
  * layernorm.c:17-124); out bf16 when out_bf16 != 0, else fp32 (may alias x). */
 SMOL_B200_API int smol_b200_layer_norm(void *stream, void *out, int out_bf16, const float *x, const float *w,

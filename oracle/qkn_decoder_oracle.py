@@ -118,12 +118,16 @@ class QknOracle:
         self.o = pyoracle.oracle()
         self.scale = np.float32(1.0 / np.sqrt(np.float32(head_dim)))
 
-    def _layer(self, l: int, x: np.ndarray, pos0: int) -> np.ndarray:
-        """One decoder layer over tokens at positions pos0.. (qkn_decoder.c:431-563 / :622-705)."""
+    def _layer(self, l: int, x: np.ndarray, pos0: int, device_formats: bool = False) -> np.ndarray:
+        """One decoder layer over tokens at positions pos0.. (qkn_decoder.c:431-563 / :622-705).
+        device_formats: round what the device prefill keeps in bf16 -- the RMSNorm outputs,
+        the rotated Q, the attention output and the gated activation (GEMM / attention
+        operands) -- the same way."""
+        r16 = pyoracle.round_bf16 if device_formats else (lambda a: a)
         lw, n = self.layers[l], x.shape[0]
         sliding = self.sliding[l] and self.sliding_window > 0
         cos, sin = (self.cos_local, self.sin_local) if self.has_local and self.sliding[l] else (self.cos, self.sin)
-        xn = rms_norm(x, lw["input_norm"], self.eps)
+        xn = r16(rms_norm(x, lw["input_norm"], self.eps))
         q, k, v = xn @ lw["wq"].T, xn @ lw["wk"].T, xn @ lw["wv"].T
         pos = np.arange(pos0, pos0 + n, dtype=np.int32)
         q_rot = pyoracle.qknorm_rope_append(q, k, v, self.HQ, self.HKV, self.HD, lw.get("q_norm"), lw.get("k_norm"),
@@ -132,17 +136,17 @@ class QknOracle:
         total = pos0 + n
         K = pyoracle.bf16_to_f32(self.kc[l][:total])
         Vv = self.vc[l][:total].view(np.float16).astype(np.float32)
-        attn = self.o.causal_attention(q_rot, K, Vv, n, total, self.HQ, self.HKV, self.HD, self.scale, pos0,
+        attn = self.o.causal_attention(r16(q_rot), K, Vv, n, total, self.HQ, self.HKV, self.HD, self.scale, pos0,
                                        window=self.sliding_window if sliding else 0, cap=self.attn_softcap)
-        proj = (attn @ lw["wo"].T).astype(np.float32)
+        proj = (r16(attn) @ lw["wo"].T).astype(np.float32)
         if "pre_ffn_norm" in lw:   # Gemma: norm the sublayer output, add, norm for the MLP (:681-685)
             x = (x + rms_norm(proj, lw["post_attn_norm"], self.eps)).astype(np.float32)
-            xn = rms_norm(x, lw["pre_ffn_norm"], self.eps)
+            xn = r16(rms_norm(x, lw["pre_ffn_norm"], self.eps))
         else:                      # Qwen3: add, then norm (:688-689)
             x = (x + proj).astype(np.float32)
-            xn = rms_norm(x, lw["post_attn_norm"], self.eps)
+            xn = r16(rms_norm(x, lw["post_attn_norm"], self.eps))
         gu = xn @ lw["gate_up"].T
-        act = geglu(gu) if self.gemma else swiglu(gu)
+        act = r16(geglu(gu) if self.gemma else swiglu(gu))
         ffn = (act @ lw["down"].T).astype(np.float32)
         if "post_ffn_norm" in lw:
             ffn = rms_norm(ffn, lw["post_ffn_norm"], self.eps)
@@ -155,11 +159,12 @@ class QknOracle:
             x = (x * self.embed_normalizer).astype(np.float32)
         return x
 
-    def prefill(self, tokens) -> None:
-        """qkn_decoder_prefill over `tokens` (no logits, as the reference)."""
+    def prefill(self, tokens, device_formats: bool = False) -> None:
+        """qkn_decoder_prefill over `tokens` (no logits, as the reference); device_formats:
+        the operand roundings of the device prefill (smol_b200_qkn_prefill)."""
         x = self._embed(tokens)
         for l in range(self.L):
-            x = self._layer(l, x, self.len)
+            x = self._layer(l, x, self.len, device_formats)
         self.len += len(tokens)
 
     def forward(self, token: int) -> tuple[int, float, np.ndarray]:

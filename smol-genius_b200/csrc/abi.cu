@@ -645,10 +645,11 @@ int smol_b200_siglip_forward(void *stream, float *out, const float *images, int 
 
 int smol_b200_gemm_bf16(void *stream, void *out, int64_t ldo, int out_kind, const uint16_t *a, int64_t lda,
                         const uint16_t *w, int64_t ldw, const float *bias, const float *add, int64_t ld_add,
-                        int add_rows, int m, int n, int k, int gelu)
+                        int add_rows, int m, int n, int k, int act)
 {
+    if (act < SMOL_B200_ACT_NONE || act > SMOL_B200_ACT_GEGLU) return record(SMOL_B200_ERR_ARGS, "smol_b200_gemm_bf16");
     return record(gemm_bf16(static_cast<cudaStream_t>(stream), out, ldo, out_kind, a, lda, w, ldw, bias, add, ld_add,
-                            add_rows, m, n, k, gelu),
+                            add_rows, m, n, k, act == SMOL_B200_ACT_GELU, act >= SMOL_B200_ACT_SWIGLU ? act : 0),
                   "smol_b200_gemm_bf16");
 }
 
@@ -662,6 +663,20 @@ int smol_b200_layer_norm(void *stream, void *out, int out_bf16, const float *x, 
 // ---------------------------------------------------------------------------
 // Part 4
 // ---------------------------------------------------------------------------
+size_t smol_b200_qkn_prefill_workspace_bytes(const smol_b200_qkn_model *model, int n_tokens)
+{
+    return qkn_prefill_workspace_bytes(model, n_tokens);
+}
+
+int smol_b200_qkn_prefill(void *stream, const smol_b200_qkn_model *model, const int *tokens, int n_tokens, int start,
+                          uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows, const int64_t *layer_row0_host,
+                          const float *rope_cos, const float *rope_sin, void *workspace, size_t workspace_bytes)
+{
+    return record(qkn_prefill(static_cast<cudaStream_t>(stream), model, tokens, n_tokens, start, k_pool, v_pool,
+                              pool_rows, layer_row0_host, rope_cos, rope_sin, workspace, workspace_bytes),
+                  "smol_b200_qkn_prefill");
+}
+
 size_t smol_b200_qkn_step_workspace_bytes(const smol_b200_qkn_model *model, int n_seqs, int max_kv_len)
 {
     return qkn_step_workspace_bytes(model, n_seqs, max_kv_len);

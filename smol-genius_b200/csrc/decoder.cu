@@ -467,6 +467,37 @@ __global__ void step_index_kernel(int *positions, int *kv_next, int64_t *slots, 
     }
 }
 
+// Prefill: out[t][:] = bf16(smol_rms_norm(x[t][:])) -- (x * w) * 1/sqrtf(mean(x^2) + eps)
+// (rmsnorm.c:17-70), one warp per row, as the operand of the next GEMM.
+constexpr int kRowNormWarps = 8;
+
+__global__ void __launch_bounds__(kRowNormWarps * 32) rms_norm_rows_bf16_kernel(uint16_t *out, const float *x,
+                                                                                const float *w, int rows, int hidden,
+                                                                                float eps)
+{
+    const int row = blockIdx.x * kRowNormWarps + threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (row >= rows) return;
+    const float *xr = x + static_cast<long long>(row) * hidden;
+    float ss = 0.f;
+    for (int i = lane; i < hidden; i += 32) ss += xr[i] * xr[i];
+    const float r = 1.0f / sqrtf(warp_sum(ss) / static_cast<float>(hidden) + eps);
+    uint16_t *o = out + static_cast<long long>(row) * hidden;
+    for (int i = lane; i < hidden; i += 32) {
+        __nv_bfloat16 b = __float2bfloat16_rn(xr[i] * w[i] * r);
+        o[i] = *reinterpret_cast<uint16_t *>(&b);
+    }
+}
+
+// Prefill positions and pool rows of one layer: positions[t] = start + t,
+// slots[t] = row0 + start + t.
+__global__ void prefill_index_kernel(int *positions, int64_t *slots, int64_t row0, int start, int n)
+{
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= n) return;
+    if (positions) positions[t] = start + t;
+    slots[t] = row0 + start + t;
+}
+
 __global__ void advance_kernel(int *kv_len, int n_seqs)
 {
     griddep_wait();
@@ -685,6 +716,153 @@ int argmax_bf16(cudaStream_t st, int *tokens_out, const float *x, int64_t ldx, c
 size_t argmax_workspace_bytes(int n_seqs, int vocab)
 {
     return argmax_ws_bytes(n_seqs, vocab);
+}
+
+// Workspace of one prefill of n tokens, carved in 256-byte aligned pieces.
+struct PrefillWs {
+    float *x, *q, *k, *v, *attn, *sub;
+    uint16_t *xn, *qb, *attn16, *act;
+    int *positions;
+    int64_t *slots;
+    size_t total;
+};
+
+static PrefillWs carve_prefill(const smol_b200_qkn_model &m, int n, uint8_t *base)
+{
+    PrefillWs w;
+    memset(&w, 0, sizeof(w));
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        uint8_t *p = base ? base + off : nullptr;
+        off += (bytes + 255) / 256 * 256;
+        return p;
+    };
+    const size_t T = static_cast<size_t>(n), H = m.hidden, I = m.intermediate;
+    const size_t qd = static_cast<size_t>(m.n_heads) * m.head_dim, kvd = static_cast<size_t>(m.n_kv_heads) * m.head_dim;
+    w.x = reinterpret_cast<float *>(take(T * H * 4));
+    w.q = reinterpret_cast<float *>(take(T * qd * 4));
+    w.k = reinterpret_cast<float *>(take(T * kvd * 4));
+    w.v = reinterpret_cast<float *>(take(T * kvd * 4));
+    w.attn = reinterpret_cast<float *>(take(T * qd * 4));
+    w.sub = reinterpret_cast<float *>(take(T * H * 4));
+    w.xn = reinterpret_cast<uint16_t *>(take(T * H * 2));
+    w.qb = reinterpret_cast<uint16_t *>(take(T * qd * 2));
+    w.attn16 = reinterpret_cast<uint16_t *>(take(T * qd * 2));
+    w.act = reinterpret_cast<uint16_t *>(take(T * I * 2));
+    w.positions = reinterpret_cast<int *>(take(T * 4));
+    w.slots = reinterpret_cast<int64_t *>(take(T * 8));
+    w.total = off;
+    return w;
+}
+
+size_t qkn_prefill_workspace_bytes(const smol_b200_qkn_model *m, int n_tokens)
+{
+    if (!model_ok(m) || n_tokens <= 0) return 0;
+    return carve_prefill(*m, n_tokens, nullptr).total;
+}
+
+int qkn_prefill(cudaStream_t st, const smol_b200_qkn_model *mp, const int *tokens, int n, int start,
+                uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows, const int64_t *layer_row0,
+                const float *rope_cos, const float *rope_sin, void *workspace, size_t workspace_bytes)
+{
+    if (n <= 0) return SMOL_B200_OK;
+    if (!model_ok(mp) || !tokens || !k_pool || !v_pool || !layer_row0 || !rope_cos || !rope_sin || start < 0)
+        return SMOL_B200_ERR_ARGS;
+    const smol_b200_qkn_model &m = *mp;
+    const int hd = m.head_dim;
+    if (hd != 64 && hd != 128 && hd != 256) return SMOL_B200_ERR_ARGS;   // the prefill kernel's head dims
+    for (int l = 0; l < m.n_layers; ++l)
+        if (layer_row0[l] < 0 || layer_row0[l] + start + n > pool_rows) return SMOL_B200_ERR_ARGS;
+    const PrefillWs w = carve_prefill(m, n, static_cast<uint8_t *>(workspace));
+    if (!workspace || workspace_bytes < w.total) return SMOL_B200_ERR_WORKSPACE;
+    unsigned *err = device_error_word();
+    if (!err) return SMOL_B200_ERR_NO_DEVICE;
+    const int H = m.hidden, I = m.intermediate, qd = m.n_heads * hd, kvd = m.n_kv_heads * hd;
+    const int L_k = start + n;                                          // keys attended by the last token
+    const float scale = 1.0f / sqrtf(static_cast<float>(hd));            // qkn_decoder.c:430
+    const int gate = m.activation == 1 ? 3 : 2;                         // GeGLU / SwiGLU (:548-551)
+    const unsigned rows_grid = static_cast<unsigned>((n + kRowNormWarps - 1) / kRowNormWarps);
+    auto rms_bf16 = [&](const float *norm_w) {
+        if (!norm_w) return SMOL_B200_ERR_ARGS;
+        return launch_kernel(rms_norm_rows_bf16_kernel, dim3(rows_grid), dim3(kRowNormWarps * 32), 0, st, w.xn,
+                             static_cast<const float *>(w.x), norm_w, n, H, m.eps) == cudaSuccess
+                   ? SMOL_B200_OK
+                   : SMOL_B200_ERR_CUDA;
+    };
+    auto norm_add = [&](const float *norm_w) {   // x += rmsnorm(sub) (Gemma, :535-537, :555-558)
+        if (!norm_w) return SMOL_B200_ERR_ARGS;
+        return launch_kernel(norm_add_kernel, dim3(n), dim3(kNormAddThreads), 0, st, w.x,
+                             static_cast<const float *>(w.sub), norm_w, H, m.eps) == cudaSuccess
+                   ? SMOL_B200_OK
+                   : SMOL_B200_ERR_CUDA;
+    };
+    // embedding rows, scaled by the Gemma normaliser when set (qkn_decoder.c:408-419)
+    if (launch_kernel(embed_kernel, dim3(n), dim3(256), 0, st, w.x, tokens, m.tok_embeddings, H, m.vocab,
+                      m.embed_normalizer, err) != cudaSuccess)
+        return SMOL_B200_ERR_CUDA;
+    int rc = SMOL_B200_OK;
+    for (int l = 0; l < m.n_layers && rc == SMOL_B200_OK; ++l) {
+        const smol_b200_qkn_layer &L = m.layers[l];
+        const bool local_rope = L.is_sliding && m.rope_cos_local;
+        const int window = L.is_sliding && m.sliding_window > 0 ? m.sliding_window : 0;
+        const float softcap = m.attn_softcap > 0.f ? m.attn_softcap : 0.f;
+        const int64_t row0 = layer_row0[l];
+        // input RMSNorm, Q / K / V projections (qkn_decoder.c:470-476)
+        rc = rms_bf16(L.input_norm);
+        if (rc == SMOL_B200_OK)
+            rc = gemm_bf16(st, w.q, qd, SMOL_B200_GEMM_OUT_F32, w.xn, H, L.wq, H, nullptr, nullptr, 0, 0, n, qd, H, 0);
+        if (rc == SMOL_B200_OK)
+            rc = gemm_bf16(st, w.k, kvd, SMOL_B200_GEMM_OUT_F32, w.xn, H, L.wk, H, nullptr, nullptr, 0, 0, n, kvd, H, 0);
+        if (rc == SMOL_B200_OK)
+            rc = gemm_bf16(st, w.v, kvd, SMOL_B200_GEMM_OUT_F32, w.xn, H, L.wv, H, nullptr, nullptr, 0, 0, n, kvd, H, 0);
+        // QK-norm, RoPE at positions start.., K / V into the pool (qkn_decoder.c:486-503)
+        if (rc == SMOL_B200_OK &&
+            launch_kernel(prefill_index_kernel, dim3((n + 255) / 256), dim3(256), 0, st, l == 0 ? w.positions : nullptr,
+                          w.slots, row0, start, n) != cudaSuccess)
+            rc = SMOL_B200_ERR_CUDA;
+        if (rc == SMOL_B200_OK)
+            rc = qknorm_rope_append(st, w.q, w.k, w.v, n, m.n_heads, m.n_kv_heads, hd, L.q_norm, L.k_norm, m.eps,
+                                    local_rope ? m.rope_cos_local : rope_cos, local_rope ? m.rope_sin_local : rope_sin,
+                                    m.rope_interleaved, w.positions, w.slots, nullptr, w.qb, k_pool, v_pool,
+                                    pool_rows);
+        // causal attention over the layer's cached rows [0, start + n) (qkn_decoder.c:505-531)
+        if (rc == SMOL_B200_OK) {
+            const uint16_t *kl = k_pool + row0 * kvd, *vl = v_pool + row0 * kvd;
+            rc = prefill_attention(st, w.attn, qd, static_cast<int64_t>(n) * qd, w.qb, qd, static_cast<int64_t>(n) * qd,
+                                   kl, kvd, static_cast<int64_t>(L_k) * kvd, vl, kvd, static_cast<int64_t>(L_k) * kvd,
+                                   1, n, L_k, m.n_heads, m.n_kv_heads, hd, scale, SMOL_MASK_CAUSAL, start, 0, window,
+                                   softcap, nullptr, 0);
+        }
+        if (rc == SMOL_B200_OK) rc = convert_f32_to_bf16(st, w.attn16, w.attn, static_cast<long long>(n) * qd);
+        // output projection and residual, then the MLP input norm (qkn_decoder.c:530-543)
+        if (rc == SMOL_B200_OK) {
+            if (L.pre_ffn_norm) {
+                rc = gemm_bf16(st, w.sub, H, SMOL_B200_GEMM_OUT_F32, w.attn16, qd, L.wo, qd, nullptr, nullptr, 0, 0, n,
+                               H, qd, 0);
+                if (rc == SMOL_B200_OK) rc = norm_add(L.post_attn_norm);
+                if (rc == SMOL_B200_OK) rc = rms_bf16(L.pre_ffn_norm);
+            } else {
+                rc = gemm_bf16(st, w.x, H, SMOL_B200_GEMM_OUT_F32_ADD, w.attn16, qd, L.wo, qd, nullptr, nullptr, 0, 0,
+                               n, H, qd, 0);
+                if (rc == SMOL_B200_OK) rc = rms_bf16(L.post_attn_norm);
+            }
+        }
+        // gate/up with the gated activation, down projection and residual (qkn_decoder.c:546-560)
+        if (rc == SMOL_B200_OK)
+            rc = gemm_bf16(st, w.act, I, SMOL_B200_GEMM_OUT_BF16, w.xn, H, L.gate_up, H, nullptr, nullptr, 0, 0, n,
+                           2 * I, H, 0, gate);
+        if (rc == SMOL_B200_OK) {
+            if (L.post_ffn_norm) {
+                rc = gemm_bf16(st, w.sub, H, SMOL_B200_GEMM_OUT_F32, w.act, I, L.down, I, nullptr, nullptr, 0, 0, n, H,
+                               I, 0);
+                if (rc == SMOL_B200_OK) rc = norm_add(L.post_ffn_norm);
+            } else {
+                rc = gemm_bf16(st, w.x, H, SMOL_B200_GEMM_OUT_F32_ADD, w.act, I, L.down, I, nullptr, nullptr, 0, 0, n,
+                               H, I, 0);
+            }
+        }
+    }
+    return rc;
 }
 
 size_t qkn_step_workspace_bytes(const smol_b200_qkn_model *m, int n_seqs, int max_kv_len)

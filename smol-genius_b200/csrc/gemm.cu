@@ -2,7 +2,8 @@
 // SigLIP encoder's linear layers need.
 //
 //   C[m][n] = sum_k A[m][k] * W[n][k]  (+ bias[n]) (+ add[m % add_rows][n]) (GELU-tanh)
-//   stored as fp32, bf16 or fp16, or added into an fp32 C (the residual stream)
+//   stored as fp32, bf16 or fp16, or added into an fp32 C (the residual stream); or,
+//   for an interleaved gate/up weight, C[m][j] = act(c[2j]) * c[2j+1] (SwiGLU / GeGLU)
 //
 // This is smol_linear (matmul.c:70-100: y = x W^T + b) and the bias + GELU / residual
 // steps around it in siglip_forward (siglip.c:116-146), with A and W in bf16 and fp32
@@ -58,6 +59,7 @@ struct GemmParams {
     int M, N, K;
     int out_kind;             // SMOL_B200_GEMM_OUT_*
     int gelu;
+    int gate;                 // 0, or 2 / 3: columns (2j, 2j+1) -> out[j] = act(c[2j]) * c[2j+1], act SiLU / GELU-tanh
     int vec_ok;               // rows of `out` (and `add`) are 16-byte aligned
     unsigned *err;
 };
@@ -68,6 +70,13 @@ __device__ __forceinline__ float gelu_tanh(float x)
     const float x3 = x * x * x;
     const float inner = 0.7978845608028654f * (x + 0.044715f * x3);
     return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+// The gated forms of smol_swiglu_multiply / smol_geglu_multiply (activation.c:55-126):
+// gate g = column 2j, up u = column 2j+1 of the interleaved gate/up product.
+__device__ __forceinline__ float gated(float g, float u, int gate)
+{
+    return (gate == 3 ? gelu_tanh(g) : g / (1.0f + expf(-g))) * u;
 }
 
 __global__ void __launch_bounds__(kGemmThreads, 2) gemm_bf16_kernel(const __grid_constant__ GemmParams p)
@@ -175,6 +184,35 @@ __global__ void __launch_bounds__(kGemmThreads, 2) gemm_bf16_kernel(const __grid
                     v[i] = x;
                 }
                 const bool full = p.vec_ok && nb + 32 <= p.N;
+                if (p.gate) {   // 16 outputs from the 32 columns: out[nb/2 + j]
+                    float gv[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) gv[j] = gated(v[2 * j], v[2 * j + 1], p.gate);
+                    const long long ob = static_cast<long long>(row) * p.ldo + nb / 2;
+                    if (p.out_kind == SMOL_B200_GEMM_OUT_BF16) {
+                        uint16_t *o = static_cast<uint16_t *>(p.out) + ob;
+                        if (full) {
+#pragma unroll
+                            for (int q = 0; q < 2; ++q) {
+                                uint4 w;
+                                uint32_t *wp = reinterpret_cast<uint32_t *>(&w);
+#pragma unroll
+                                for (int j = 0; j < 4; ++j) wp[j] = pack_bf16x2(gv[q * 8 + 2 * j], gv[q * 8 + 2 * j + 1]);
+                                *reinterpret_cast<uint4 *>(o + q * 8) = w;
+                            }
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                if (nb + 2 * j + 1 < p.N) o[j] = static_cast<uint16_t>(pack_bf16x2(gv[j], 0.f) & 0xffffu);
+                        }
+                    } else {
+                        float *o = static_cast<float *>(p.out) + ob;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (nb + 2 * j + 1 < p.N) o[j] = gv[j];
+                    }
+                    continue;
+                }
                 if (p.out_kind == SMOL_B200_GEMM_OUT_BF16 || p.out_kind == SMOL_B200_GEMM_OUT_F16) {
                     uint16_t *o = static_cast<uint16_t *>(p.out) + static_cast<long long>(row) * p.ldo + nb;
                     const bool h = p.out_kind == SMOL_B200_GEMM_OUT_F16;
@@ -236,10 +274,13 @@ __global__ void __launch_bounds__(kGemmThreads, 2) gemm_bf16_kernel(const __grid
 
 int gemm_bf16(cudaStream_t st, void *out, int64_t ldo, int out_kind, const uint16_t *a, int64_t lda,
               const uint16_t *w, int64_t ldw, const float *bias, const float *add, int64_t ld_add, int add_rows,
-              int M, int N, int K, int gelu)
+              int M, int N, int K, int gelu, int gate)
 {
     if (M <= 0 || N <= 0) return SMOL_B200_OK;
-    if (!out || !a || !w || K <= 0 || lda < K || ldw < K || lda % 8 || ldw % 8 || ldo < N ||
+    if (gate && (gate < 2 || gate > 3 || (N & 1) || gelu || add ||
+                 (out_kind != SMOL_B200_GEMM_OUT_BF16 && out_kind != SMOL_B200_GEMM_OUT_F32) || ldo < N / 2))
+        return SMOL_B200_ERR_ARGS;
+    if (!out || !a || !w || K <= 0 || lda < K || ldw < K || lda % 8 || ldw % 8 || (!gate && ldo < N) ||
         (reinterpret_cast<uintptr_t>(a) & 15) || (reinterpret_cast<uintptr_t>(w) & 15) ||
         out_kind < SMOL_B200_GEMM_OUT_F32 || out_kind > SMOL_B200_GEMM_OUT_F32_ADD || (add && (add_rows <= 0 || ld_add < N)))
         return SMOL_B200_ERR_ARGS;
@@ -272,6 +313,7 @@ int gemm_bf16(cudaStream_t st, void *out, int64_t ldo, int out_kind, const uint1
     p.K = K;
     p.out_kind = out_kind;
     p.gelu = gelu ? 1 : 0;
+    p.gate = gate;
     p.vec_ok = (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (ldo * esz) % 16 == 0;
     p.err = err;
     const dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);

@@ -135,13 +135,19 @@ int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *m, int n_seqs, c
                     const int64_t *layer_row0, int *kv_len, int max_kv_len, const float *rope_cos,
                     const float *rope_sin, int advance, void *workspace, size_t workspace_bytes);
 
+size_t qkn_prefill_workspace_bytes(const smol_b200_qkn_model *m, int n_tokens);
+int qkn_prefill(cudaStream_t st, const smol_b200_qkn_model *m, const int *tokens, int n_tokens, int start,
+                uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows, const int64_t *layer_row0,
+                const float *rope_cos, const float *rope_sin, void *workspace, size_t workspace_bytes);
+
 int launch_decode_step_index(cudaStream_t st, int *positions, int64_t *slots, int *kv_len_next,
                              const int64_t *seq_row0, const int *kv_len, int n_seqs);
 
 // gemm.cu / siglip.cu: the SigLIP encoder (Part 5 of smol_b200.h)
 int gemm_bf16(cudaStream_t st, void *out, int64_t ldo, int out_kind, const uint16_t *a, int64_t lda,
               const uint16_t *w, int64_t ldw, const float *bias, const float *add, int64_t ld_add, int add_rows,
-              int M, int N, int K, int gelu);
+              int M, int N, int K, int gelu, int gate = 0);
+int convert_f32_to_bf16(cudaStream_t st, uint16_t *dst, const float *src, long long n);
 int layer_norm(cudaStream_t st, void *out, int out_bf16, const float *x, const float *w, const float *b, int rows,
                int hidden, float eps);
 size_t siglip_workspace_bytes(const smol_b200_siglip_model *m, int n_images);

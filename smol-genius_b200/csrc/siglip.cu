@@ -153,6 +153,17 @@ bool model_ok(const smol_b200_siglip_model *m)
 
 }  // namespace
 
+int convert_f32_to_bf16(cudaStream_t st, uint16_t *dst, const float *src, long long n)
+{
+    if (n <= 0) return SMOL_B200_OK;
+    if (!dst || !src || (n & 3) || (reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 7))
+        return SMOL_B200_ERR_ARGS;
+    const long long n4 = n / 4;
+    return launch_kernel(f32_to_bf16_kernel, dim3(grid_for(n4, 256)), dim3(256), 0, st, dst, src, n4) == cudaSuccess
+               ? SMOL_B200_OK
+               : SMOL_B200_ERR_CUDA;
+}
+
 int layer_norm(cudaStream_t st, void *out, int out_bf16, const float *x, const float *w, const float *b, int rows,
                int hidden, float eps)
 {
@@ -208,12 +219,7 @@ int siglip_forward(cudaStream_t st, float *out, const float *images, int n_image
                                    w.k, H, static_cast<int64_t>(NP) * H, w.v, H, static_cast<int64_t>(NP) * H,
                                    n_images, NP, NP, m.heads, m.heads, hd, scale, SMOL_MASK_FULL, 0, 0, 0, 0.f,
                                    nullptr, 0);
-        if (rc == SMOL_B200_OK) {
-            const long long n4 = static_cast<long long>(T) * H / 4;
-            if (launch_kernel(f32_to_bf16_kernel, dim3(grid_for(n4, 256)), dim3(256), 0, st, w.attn16,
-                              static_cast<const float *>(w.attn), n4) != cudaSuccess)
-                rc = SMOL_B200_ERR_CUDA;
-        }
+        if (rc == SMOL_B200_OK) rc = convert_f32_to_bf16(st, w.attn16, w.attn, static_cast<long long>(T) * H);
         if (rc == SMOL_B200_OK)
             rc = gemm_bf16(st, x, H, SMOL_B200_GEMM_OUT_F32_ADD, w.attn16, H, L.wo, H, L.bo, nullptr, 0, 0, T, H, H, 0);
         if (rc == SMOL_B200_OK) rc = layer_norm(st, w.xn, 1, x, L.ln2_w, L.ln2_b, T, H, m.eps);

@@ -82,6 +82,9 @@ _SIGNATURES = {
                  _c_void, _c_size]),
     # Part 4 (device-resident decoder step)
     "smol_b200_qkn_step_workspace_bytes": (_c_size, [_c_void, _c_int, _c_int]),
+    "smol_b200_qkn_prefill_workspace_bytes": (_c_size, [_c_void, _c_int]),
+    "smol_b200_qkn_prefill": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_void, _c_void, _c_i64, _c_void,
+                                       _c_void, _c_void, _c_void, _c_size]),
     "smol_b200_qkn_decode_step": (
         _c_int, [_c_void, _c_void, _c_int, _c_void, _c_void, _c_void, _c_void, _c_i64, _c_void, _c_void, _c_int,
                  _c_void, _c_void, _c_int, _c_void, _c_size]),
@@ -340,6 +343,20 @@ def qkn_model(hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab, eps, t
     return m
 
 
+def qkn_prefill_workspace_bytes(model: QknModel, n_tokens: int) -> int:
+    return lib().smol_b200_qkn_prefill_workspace_bytes(ctypes.byref(model), n_tokens)
+
+
+def qkn_prefill(model: QknModel, tokens, n_tokens, start, k_pool, v_pool, pool_rows, layer_row0_host, rope_cos,
+                rope_sin, workspace, stream=None):
+    """layer_row0_host: numpy int64 [n_layers] (host); tokens, pools, tables, workspace on the device."""
+    row0 = np.ascontiguousarray(layer_row0_host, dtype=np.int64)
+    rc = lib().smol_b200_qkn_prefill(_stream(stream), ctypes.byref(model), _ptr(tokens), n_tokens, start, _ptr(k_pool),
+                                     _ptr(v_pool), pool_rows, _ptr(row0), _ptr(rope_cos), _ptr(rope_sin),
+                                     _ptr(workspace), workspace.numel() * workspace.element_size())
+    check(rc, "smol_b200_qkn_prefill")
+
+
 def qkn_step_workspace_bytes(model: QknModel, n_seqs: int, max_kv_len: int) -> int:
     return lib().smol_b200_qkn_step_workspace_bytes(ctypes.byref(model), n_seqs, max_kv_len)
 
@@ -410,6 +427,7 @@ def ipc_close(ptr: int) -> None:
 # Part 5: SigLIP encoder
 # ---------------------------------------------------------------------------
 GEMM_OUT_F32, GEMM_OUT_BF16, GEMM_OUT_F16, GEMM_OUT_F32_ADD = 0, 1, 2, 3
+ACT_NONE, ACT_GELU, ACT_SWIGLU_PAIRS, ACT_GEGLU_PAIRS = 0, 1, 2, 3
 
 
 class SiglipLayer(ctypes.Structure):
@@ -451,9 +469,11 @@ def siglip_forward(out, images, n_images, model: SiglipModel, workspace, stream=
 
 
 def gemm_bf16(out, ldo, out_kind, a, lda, w, ldw, m, n, k, bias=None, add=None, ld_add=0, add_rows=0, gelu=False,
-              stream=None):
+              act=None, stream=None):
+    """act: ACT_* (gelu=True is ACT_GELU)."""
+    a_code = act if act is not None else (ACT_GELU if gelu else ACT_NONE)
     check(lib().smol_b200_gemm_bf16(_stream(stream), _ptr(out), ldo, out_kind, _ptr(a), lda, _ptr(w), ldw, _ptr(bias),
-                                    _ptr(add), ld_add, add_rows, m, n, k, int(gelu)),
+                                    _ptr(add), ld_add, add_rows, m, n, k, a_code),
           "smol_b200_gemm_bf16")
 
 

@@ -44,13 +44,17 @@ _ensure_built()
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs an sm_100 (B200) CUDA device")
-    config.addinivalue_line("markers", "new_on_gpu: a GPU test not yet run on a B200; runs after the rest")
+    config.addinivalue_line("markers", "new_on_gpu(stage=0): a GPU test not yet run on a B200; runs after the rest")
 
 
 def pytest_collection_modifyitems(config, items):
     """Tests marked new_on_gpu run last (the sort is stable), so that under -x a failure
-    in one of them cannot keep the established tests from running."""
-    items.sort(key=lambda item: item.get_closest_marker("new_on_gpu") is not None)
+    in one of them cannot keep the established tests from running; among them by
+    `stage` (default 0): unit tests of a new kernel before the tests built on it."""
+    def key(item):
+        mark = item.get_closest_marker("new_on_gpu")
+        return (0, 0) if mark is None else (1, mark.kwargs.get("stage", 0))
+    items.sort(key=key)
 
 
 @pytest.fixture(scope="session")

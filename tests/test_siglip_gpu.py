@@ -21,7 +21,7 @@ import pyoracle
 import smol_b200
 from siglip_oracle import SIGLIP_PIN_CASES, gelu_tanh, layer_norm, siglip_pin_case
 
-pytestmark = [pytest.mark.gpu, pytest.mark.new_on_gpu]
+pytestmark = [pytest.mark.gpu, pytest.mark.new_on_gpu(stage=2)]
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "siglip_cases.npz")
 
 
@@ -34,6 +34,7 @@ def _no_error():
     assert smol_b200.device_error() == 0
 
 
+@pytest.mark.new_on_gpu(stage=1)
 @pytest.mark.parametrize("M,N,K", [(256, 256, 128), (200, 136, 200), (1000, 768, 768), (130, 520, 588)])
 def test_gemm_bf16_output_kinds(cuda, M, N, K):
     rng = np.random.default_rng(M + N + K)
@@ -78,6 +79,31 @@ def test_gemm_bf16_output_kinds(cuda, M, N, K):
     _no_error()
 
 
+@pytest.mark.new_on_gpu(stage=1)
+@pytest.mark.parametrize("M,I,K", [(300, 1536, 1024), (77, 200, 256)])
+def test_gemm_bf16_gated_pairs(cuda, M, I, K):
+    """Interleaved gate/up weight rows: out[m][j] = act(c[2j]) * c[2j+1] (the decoder
+    prefill's MLP, activation.c:55-126), SiLU and GELU-tanh, fp32 and bf16 out."""
+    from qkn_decoder_oracle import geglu, swiglu
+    rng = np.random.default_rng(M + I)
+    t = _dev(cuda)
+    A = pyoracle.round_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    W = pyoracle.round_bf16((rng.standard_normal((2 * I, K)) / np.sqrt(K)).astype(np.float32))
+    c = (A.astype(np.float64) @ W.T.astype(np.float64)).astype(np.float32)
+    for act, fn in ((smol_b200.ACT_SWIGLU_PAIRS, swiglu), (smol_b200.ACT_GEGLU_PAIRS, geglu)):
+        y = torch.zeros((M, I), device=cuda)
+        smol_b200.gemm_bf16(y, I, smol_b200.GEMM_OUT_F32, t(pyoracle.bf16_bits(A)), K, t(pyoracle.bf16_bits(W)), K, M,
+                            2 * I, K, act=act)
+        yb = torch.zeros((M, I), dtype=torch.bfloat16, device=cuda)
+        smol_b200.gemm_bf16(yb, I, smol_b200.GEMM_OUT_BF16, t(pyoracle.bf16_bits(A)), K, t(pyoracle.bf16_bits(W)), K,
+                            M, 2 * I, K, act=act)
+        torch.cuda.synchronize()
+        _no_error()
+        assert pyoracle.rel_l2(y.cpu().numpy(), fn(c)) < 1e-5
+        assert pyoracle.rel_l2(yb.float().cpu().numpy(), fn(c)) < 4e-3
+
+
+@pytest.mark.new_on_gpu(stage=1)
 def test_layer_norm_fp32_bf16_in_place(cuda):
     rng = np.random.default_rng(3)
     t = _dev(cuda)
