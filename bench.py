@@ -60,11 +60,12 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=workload.CFG2["layers"])
     ap.add_argument("--no-decode", action="store_true", help="prefill measurement only (profiling helper)")
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg 1/3/4 block")
-    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4", "decoder", "audio", "siglip", "gemma"],
+    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4", "decoder", "audio", "siglip", "gemma",
+                                              "prefill"],
                     default=None,
                     help="run one of the other measurements alone: cfg 1/3/4, the decoder step, or (not in the "
-                         "default run yet) the audio-encoder windows, the whole SigLIP encoder or the Gemma-"
-                         "configured decoder step")
+                         "default run yet) the audio-encoder windows, the whole SigLIP encoder, the Gemma-"
+                         "configured decoder step or the device prefill")
     ap.add_argument("--images", type=int, default=None, help="cfg 3 image count override")
     ap.add_argument("--prefill-shape", default=None, help="B,L override of the cfg 5 prefill shape")
     return ap.parse_args()
@@ -753,6 +754,59 @@ def run_gemma_decoder(pk, batch: int = 1, steps: int = 30) -> dict:
             "bytes_per_step": weight_bytes + kv_bytes, "gbs": round(gbs, 1), "hbm_frac": round(gbs / pk["hbm_gbs"], 4)}
 
 
+def run_decoder_prefill(pk, n_tokens: int = 2048) -> dict:
+    """The device prefill (smol_b200_qkn_prefill) at Qwen3-0.6B size: one sequence of
+    n_tokens, 28 layers, hidden 1024, 16/8 heads, head_dim 128, SwiGLU 3072; random bf16
+    weights.  FLOPs: the projections (2 * weights per token) plus the causal attention
+    (4 * hd per visible pair and head)."""
+    import torch
+
+    import smol_b200
+    g = torch.Generator(device="cuda").manual_seed(37)
+    H, Lr, HQ, HKV, HD, I, V = 1024, 28, 16, 8, 128, 3072, 151936
+    qd, kvd = HQ * HD, HKV * HD
+
+    def bf(rows, cols):
+        return (torch.randn((rows, cols), device="cuda", generator=g) / np.sqrt(cols)).to(torch.bfloat16)
+
+    def near(n, mean):
+        return (mean + 0.02 * torch.randn(n, device="cuda", generator=g)).contiguous()
+
+    emb = torch.randn((V, H), device="cuda", generator=g).to(torch.bfloat16)
+    layers = [{"wq": bf(qd, H), "wk": bf(kvd, H), "wv": bf(kvd, H), "wo": bf(H, qd), "gate_up": bf(2 * I, H),
+               "down": bf(H, I), "input_norm": near(H, 1.0), "post_attn_norm": near(H, 1.0),
+               "q_norm": near(HD, 1.0), "k_norm": near(HD, 1.0)} for _ in range(Lr)]
+    model = smol_b200.qkn_model(H, HQ, HKV, HD, I, V, 1e-6, emb, near(H, 1.0), layers)
+    cap = n_tokens
+    rows = Lr * cap
+    k_pool = torch.zeros((rows, kvd), dtype=torch.bfloat16, device="cuda")
+    v_pool = torch.zeros((rows, kvd), dtype=torch.float16, device="cuda")
+    row0 = np.arange(Lr, dtype=np.int64) * cap
+    c = np.zeros((cap, HD), np.float32)
+    s_ = np.zeros((cap, HD), np.float32)
+    smol_b200.compute_rope(c, s_, np.arange(cap, dtype=np.int32), cap, HD, 1e6)
+    cos_d, sin_d = torch.from_numpy(c).cuda(), torch.from_numpy(s_).cuda()
+    tokens = torch.randint(0, V, (n_tokens,), dtype=torch.int32, device="cuda", generator=g)
+    ws = torch.empty(smol_b200.qkn_prefill_workspace_bytes(model, n_tokens), dtype=torch.uint8, device="cuda")
+
+    def run():
+        smol_b200.qkn_prefill(model, tokens, n_tokens, 0, k_pool, v_pool, rows, row0, cos_d, sin_d, ws)
+    run()
+    a, b = _ev(), _ev()
+    a.record()
+    run()
+    b.record()
+    torch.cuda.synchronize()
+    smol_b200.check(smol_b200.last_error(), "decoder prefill")
+    ms = a.elapsed_time(b)
+    gemm = 2 * n_tokens * Lr * (qd * H + 2 * kvd * H + H * qd + 2 * I * H + H * I)
+    attn = Lr * workload.causal_flops_square(n_tokens, HQ, HD)
+    fl = gemm + attn
+    return {"workload": f"Qwen3-0.6B-size prefill of {n_tokens} tokens (28 layers)", "ms": round(ms, 3),
+            "tokens_per_s": round(n_tokens / (ms * 1e-3), 1), "tflops": round(fl / (ms * 1e-3) / 1e12, 1),
+            "frac_of_bf16_peak": round(fl / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 4)}
+
+
 def run_other_configs(pk) -> dict:
     """The remaining BASELINE configs on one GPU (latency- or tensor-bound; not the headline).
 
@@ -961,7 +1015,8 @@ def main():
               "cfg4": run_cfg4, "decoder": lambda: [run_decoder(pk, 1), run_decoder(pk, 8)],
               "audio": lambda: run_audio_windows(pk),
               "siglip": lambda: run_siglip_encoder(pk, args.images),
-              "gemma": lambda: [run_gemma_decoder(pk, 1), run_gemma_decoder(pk, 8)]}[args.only_config]
+              "gemma": lambda: [run_gemma_decoder(pk, 1), run_gemma_decoder(pk, 8)],
+              "prefill": lambda: run_decoder_prefill(pk)}[args.only_config]
         print(json.dumps({args.only_config: fn()}))
         return
     run_ours(args)
