@@ -21,6 +21,7 @@
 // Every wait is bounded (2 s), reports through the device error word and lets the CTA
 // drain its copies and MMAs before it exits.
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include "b200_common.cuh"
@@ -77,6 +78,99 @@ __device__ __forceinline__ float gelu_tanh(float x)
 __device__ __forceinline__ float gated(float g, float u, int gate)
 {
     return (gate == 3 ? gelu_tanh(g) : g / (1.0f + expf(-g))) * u;
+}
+
+// Epilogue of one 32-column chunk of one row: bias, addend, activation, store.
+__device__ __forceinline__ void store_chunk(const GemmParams &p, int row, int nb, const uint32_t (&r)[32])
+{
+    if (row >= p.M || nb >= p.N) return;
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const int n = nb + i;
+        float x = __uint_as_float(r[i]);
+        if (n < p.N) {
+            if (p.bias) x += p.bias[n];
+            if (p.add) x += p.add[static_cast<long long>(row % p.add_rows) * p.ld_add + n];
+            if (p.gelu) x = gelu_tanh(x);
+        }
+        v[i] = x;
+    }
+    const bool full = p.vec_ok && nb + 32 <= p.N;
+    if (p.gate) {   // 16 outputs from the 32 columns: out[nb/2 + j]
+        float gv[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) gv[j] = gated(v[2 * j], v[2 * j + 1], p.gate);
+        const long long ob = static_cast<long long>(row) * p.ldo + nb / 2;
+        if (p.out_kind == SMOL_B200_GEMM_OUT_BF16) {
+            uint16_t *o = static_cast<uint16_t *>(p.out) + ob;
+            if (full) {
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    uint4 w;
+                    uint32_t *wp = reinterpret_cast<uint32_t *>(&w);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) wp[j] = pack_bf16x2(gv[q * 8 + 2 * j], gv[q * 8 + 2 * j + 1]);
+                    *reinterpret_cast<uint4 *>(o + q * 8) = w;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (nb + 2 * j + 1 < p.N) o[j] = static_cast<uint16_t>(pack_bf16x2(gv[j], 0.f) & 0xffffu);
+            }
+        } else {
+            float *o = static_cast<float *>(p.out) + ob;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (nb + 2 * j + 1 < p.N) o[j] = gv[j];
+        }
+        return;
+    }
+    if (p.out_kind == SMOL_B200_GEMM_OUT_BF16 || p.out_kind == SMOL_B200_GEMM_OUT_F16) {
+        uint16_t *o = static_cast<uint16_t *>(p.out) + static_cast<long long>(row) * p.ldo + nb;
+        const bool h = p.out_kind == SMOL_B200_GEMM_OUT_F16;
+        if (full) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint4 w;
+                uint32_t *wp = reinterpret_cast<uint32_t *>(&w);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float a = v[q * 8 + 2 * j], b = v[q * 8 + 2 * j + 1];
+                    wp[j] = h ? pack_f16x2(a, b) : pack_bf16x2(a, b);
+                }
+                *reinterpret_cast<uint4 *>(o + q * 8) = w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {   // unrolled: v stays in registers
+                if (nb + i >= p.N) continue;
+                const uint32_t w = h ? pack_f16x2(v[i], 0.f) : pack_bf16x2(v[i], 0.f);
+                o[i] = static_cast<uint16_t>(w & 0xffffu);
+            }
+        }
+    } else {
+        float *o = static_cast<float *>(p.out) + static_cast<long long>(row) * p.ldo + nb;
+        const bool acc = p.out_kind == SMOL_B200_GEMM_OUT_F32_ADD;
+        if (full) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                float4 w = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                if (acc) {
+                    const float4 o4 = *reinterpret_cast<const float4 *>(o + 4 * q);
+                    w.x += o4.x;
+                    w.y += o4.y;
+                    w.z += o4.z;
+                    w.w += o4.w;
+                }
+                *reinterpret_cast<float4 *>(o + 4 * q) = w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (nb + i < p.N) o[i] = acc ? o[i] + v[i] : v[i];
+        }
+    }
 }
 
 __global__ void __launch_bounds__(kGemmThreads, 2) gemm_bf16_kernel(const __grid_constant__ GemmParams p)
@@ -169,95 +263,7 @@ __global__ void __launch_bounds__(kGemmThreads, 2) gemm_bf16_kernel(const __grid
                 uint32_t r[32];
                 tmem_ld32(taddr + c * 32, r);
                 tmem_ld_wait();
-                const int nb = n0 + c * 32;
-                if (row >= p.M || nb >= p.N) continue;
-                float v[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int n = nb + i;
-                    float x = __uint_as_float(r[i]);
-                    if (n < p.N) {
-                        if (p.bias) x += p.bias[n];
-                        if (p.add) x += p.add[static_cast<long long>(row % p.add_rows) * p.ld_add + n];
-                        if (p.gelu) x = gelu_tanh(x);
-                    }
-                    v[i] = x;
-                }
-                const bool full = p.vec_ok && nb + 32 <= p.N;
-                if (p.gate) {   // 16 outputs from the 32 columns: out[nb/2 + j]
-                    float gv[16];
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) gv[j] = gated(v[2 * j], v[2 * j + 1], p.gate);
-                    const long long ob = static_cast<long long>(row) * p.ldo + nb / 2;
-                    if (p.out_kind == SMOL_B200_GEMM_OUT_BF16) {
-                        uint16_t *o = static_cast<uint16_t *>(p.out) + ob;
-                        if (full) {
-#pragma unroll
-                            for (int q = 0; q < 2; ++q) {
-                                uint4 w;
-                                uint32_t *wp = reinterpret_cast<uint32_t *>(&w);
-#pragma unroll
-                                for (int j = 0; j < 4; ++j) wp[j] = pack_bf16x2(gv[q * 8 + 2 * j], gv[q * 8 + 2 * j + 1]);
-                                *reinterpret_cast<uint4 *>(o + q * 8) = w;
-                            }
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 16; ++j)
-                                if (nb + 2 * j + 1 < p.N) o[j] = static_cast<uint16_t>(pack_bf16x2(gv[j], 0.f) & 0xffffu);
-                        }
-                    } else {
-                        float *o = static_cast<float *>(p.out) + ob;
-#pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            if (nb + 2 * j + 1 < p.N) o[j] = gv[j];
-                    }
-                    continue;
-                }
-                if (p.out_kind == SMOL_B200_GEMM_OUT_BF16 || p.out_kind == SMOL_B200_GEMM_OUT_F16) {
-                    uint16_t *o = static_cast<uint16_t *>(p.out) + static_cast<long long>(row) * p.ldo + nb;
-                    const bool h = p.out_kind == SMOL_B200_GEMM_OUT_F16;
-                    if (full) {
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            uint4 w;
-                            uint32_t *wp = reinterpret_cast<uint32_t *>(&w);
-#pragma unroll
-                            for (int j = 0; j < 4; ++j) {
-                                const float a = v[q * 8 + 2 * j], b = v[q * 8 + 2 * j + 1];
-                                wp[j] = h ? pack_f16x2(a, b) : pack_bf16x2(a, b);
-                            }
-                            *reinterpret_cast<uint4 *>(o + q * 8) = w;
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {   // unrolled: v stays in registers
-                            if (nb + i >= p.N) continue;
-                            const uint32_t w = h ? pack_f16x2(v[i], 0.f) : pack_bf16x2(v[i], 0.f);
-                            o[i] = static_cast<uint16_t>(w & 0xffffu);
-                        }
-                    }
-                } else {
-                    float *o = static_cast<float *>(p.out) + static_cast<long long>(row) * p.ldo + nb;
-                    const bool acc = p.out_kind == SMOL_B200_GEMM_OUT_F32_ADD;
-                    if (full) {
-#pragma unroll
-                        for (int q = 0; q < 8; ++q) {
-                            float4 w = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                            if (acc) {
-                                const float4 o4 = *reinterpret_cast<const float4 *>(o + 4 * q);
-                                w.x += o4.x;
-                                w.y += o4.y;
-                                w.z += o4.z;
-                                w.w += o4.w;
-                            }
-                            *reinterpret_cast<float4 *>(o + 4 * q) = w;
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (nb + i < p.N) o[i] = acc ? o[i] + v[i] : v[i];
-                    }
-                }
+                store_chunk(p, row, n0 + c * 32, r);
             }
         }
     }
@@ -268,6 +274,170 @@ __global__ void __launch_bounds__(kGemmThreads, 2) gemm_bf16_kernel(const __grid
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+}
+
+// ---------------------------------------------------------------------------
+// Persistent form (SMOL_GEMM_PERSISTENT=1): one CTA per SM walks the output tiles
+// (N fastest, so CTAs running together share A rows in L2), a 4-stage ring runs on
+// across tiles, and two TMEM accumulators (2 x 128 columns) let the MMAs of the next
+// tile run while the epilogue warps drain the previous one.
+// ---------------------------------------------------------------------------
+constexpr int kPStages = 4;
+
+struct PersistentBarriers {
+    uint64_t full[kPStages], empty[kPStages];
+    uint64_t acc_full[2], acc_empty[2];
+    uint64_t mma_done;
+    uint32_t tmem_base;
+    int abort;
+};
+
+constexpr int kPSmemBytes = 1024 + kPStages * kStageBytes + 256;
+
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_persistent_kernel(const __grid_constant__ GemmParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    PersistentBarriers *bars = reinterpret_cast<PersistentBarriers *>(smem + kPStages * kStageBytes);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int n_kb = (p.K + kBK - 1) / kBK;
+    const int tiles_n = (p.N + kBN - 1) / kBN;
+    const int n_tiles = tiles_n * ((p.M + kBM - 1) / kBM);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kPStages; ++s) {
+            mbar_init(smem_u32(&bars->full[s]), 1);
+            mbar_init(smem_u32(&bars->empty[s]), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&bars->acc_full[b]), 1);
+            mbar_init(smem_u32(&bars->acc_empty[b]), 128);   // every epilogue thread
+        }
+        mbar_init(smem_u32(&bars->mma_done), 1);
+        bars->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == kMmaWarp) {
+        tmem_alloc(smem_u32(&bars->tmem_base), 2 * kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            tma_prefetch_desc(&p.ta);
+            tma_prefetch_desc(&p.tw);
+            int g = 0;   // k blocks issued so far (the ring's running index)
+            bool ok = true;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kBN;
+                for (int kb = 0; kb < n_kb; ++kb, ++g) {
+                    const int st = g % kPStages;
+                    if ((g >= kPStages &&
+                         !mbar_wait(smem_u32(&bars->empty[st]), ((g / kPStages) - 1) & 1, p.err, kErrWaitTmaEmpty)) ||
+                        atomicAdd(&bars->abort, 0)) {
+                        atomicExch(&bars->abort, 1);
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t full = smem_u32(&bars->full[st]);
+                    const uint32_t sa = smem_u32(smem + st * kStageBytes);
+                    mbar_arrive_expect_tx(full, kStageBytes);
+                    tma_load_2d(sa, &p.ta, full, kb * kBK, m0);
+                    tma_load_2d(sa + kABytes, &p.tw, full, kb * kBK, n0);
+                }
+            }
+            // every issued copy lands before the CTA may exit
+            for (int q = g > kPStages ? g - kPStages : 0; q < g; ++q)
+                mbar_wait(smem_u32(&bars->full[q % kPStages]), (q / kPStages) & 1, p.err, kErrDrain);
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            int g = 0, i = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++i) {
+                const int b = i & 1;
+                const uint32_t acc = tmem + b * kTmemCols;
+                // the epilogue has drained this accumulator (tile i - 2)
+                if (i >= 2 && !mbar_wait(smem_u32(&bars->acc_empty[b]), ((i >> 1) - 1) & 1, p.err, kErrWaitSoftmax)) {
+                    atomicExch(&bars->abort, 1);
+                    break;
+                }
+                tc_fence_after();
+                for (int kb = 0; kb < n_kb; ++kb, ++g) {
+                    const int st = g % kPStages;
+                    if (!mbar_wait(smem_u32(&bars->full[st]), (g / kPStages) & 1, p.err, kErrWaitTmaFull) ||
+                        atomicAdd(&bars->abort, 0)) {
+                        atomicExch(&bars->abort, 1);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + st * kStageBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const uint64_t adesc = umma_sdesc_sw128(sa + kk * 32, 16, 1024);
+                        const uint64_t bdesc = umma_sdesc_sw128(sa + kABytes + kk * 32, 16, 1024);
+                        umma_ss(acc, adesc, bdesc, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    umma_commit(smem_u32(&bars->empty[st]));
+                }
+                umma_commit(smem_u32(&bars->acc_full[b]));   // also after an abort: wakes the epilogue
+            }
+            umma_commit(smem_u32(&bars->mma_done));
+            mbar_wait(smem_u32(&bars->mma_done), 0, p.err, kErrDrain);
+        }
+    } else {
+        const int quarter = warp & 3;
+        int i = 0;
+        for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
+            const int b = i & 1;
+            const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kBN;
+            const int row = m0 + quarter * 32 + lane;
+            const bool waited = mbar_wait(smem_u32(&bars->acc_full[b]), (i >> 1) & 1, p.err, kErrWaitMma);
+            tc_fence_after();
+            if (!__all_sync(0xffffffffu, waited && atomicAdd(&bars->abort, 0) == 0)) break;
+            const uint32_t taddr = tmem + b * kTmemCols + (static_cast<uint32_t>(quarter * 32) << 16);
+            for (int c = 0; c < kBN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(taddr + c * 32, r);
+                tmem_ld_wait();
+                if (c == kBN / 32 - 1) {   // the accumulator is free for tile i + 2
+                    tc_fence_before();
+                    mbar_arrive(smem_u32(&bars->acc_empty[b]));
+                }
+                store_chunk(p, row, n0 + c * 32, r);
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == kMmaWarp) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * kTmemCols);
+    }
+}
+
+const bool g_gemm_persistent = [] {
+    const char *e = getenv("SMOL_GEMM_PERSISTENT");
+    return e && atoi(e) != 0;
+}();
+
+int sm_count()
+{
+    static int cached[64] = {};
+    const int dev = current_device();
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cached[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        cached[dev] = n;
+    }
+    return cached[dev];
 }
 
 }  // namespace
@@ -316,6 +486,21 @@ int gemm_bf16(cudaStream_t st, void *out, int64_t ldo, int out_kind, const uint1
     p.gate = gate;
     p.vec_ok = (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (ldo * esz) % 16 == 0;
     p.err = err;
+    if (g_gemm_persistent) {
+        static bool raised_p[64] = {};
+        if (!raised_p[dev]) {
+            if (cudaFuncSetAttribute(gemm_bf16_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kPSmemBytes) != cudaSuccess)
+                return SMOL_B200_ERR_CUDA;
+            raised_p[dev] = true;
+        }
+        const long long tiles = static_cast<long long>((N + kBN - 1) / kBN) * ((M + kBM - 1) / kBM);
+        const unsigned grid = static_cast<unsigned>(tiles < sm_count() ? tiles : sm_count());
+        return launch_kernel(gemm_bf16_persistent_kernel, dim3(grid), dim3(kGemmThreads), kPSmemBytes, st, p) ==
+                       cudaSuccess
+                   ? SMOL_B200_OK
+                   : SMOL_B200_ERR_CUDA;
+    }
     const dim3 grid((N + kBN - 1) / kBN, (M + kBM - 1) / kBM);
     return launch_kernel(gemm_bf16_kernel, grid, dim3(kGemmThreads), kSmemBytes, st, p) == cudaSuccess
                ? SMOL_B200_OK

@@ -103,6 +103,47 @@ def test_gemm_bf16_gated_pairs(cuda, M, I, K):
         assert pyoracle.rel_l2(yb.float().cpu().numpy(), fn(c)) < 4e-3
 
 
+_PERSISTENT_CHECK = """
+import sys, numpy as np, torch
+sys.path[:0] = [{oracle!r}, {pkg!r}]
+import pyoracle, smol_b200
+rng = np.random.default_rng(5)
+for M, N, K in ((1000, 768, 768), (4500, 640, 200), (8192, 1024, 256), (130, 520, 588)):
+    lda = (K + 7) // 8 * 8
+    A = pyoracle.round_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    W = pyoracle.round_bf16((rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float32))
+    Ap = np.zeros((M, lda), np.float32); Ap[:, :K] = A
+    Wp = np.zeros((N, lda), np.float32); Wp[:, :K] = W
+    bias = rng.standard_normal(N).astype(np.float32)
+    y = torch.zeros((M, N), device="cuda")
+    smol_b200.gemm_bf16(y, N, smol_b200.GEMM_OUT_F32, torch.from_numpy(pyoracle.bf16_bits(Ap)).cuda(), lda,
+                        torch.from_numpy(pyoracle.bf16_bits(Wp)).cuda(), lda, M, N, K, bias=torch.from_numpy(bias).cuda(),
+                        gelu=True)
+    torch.cuda.synchronize()
+    assert smol_b200.last_error() == 0 and smol_b200.device_error() == 0
+    from siglip_oracle import gelu_tanh
+    want = gelu_tanh(((A.astype(np.float64) @ W.T.astype(np.float64)) + bias).astype(np.float32))
+    e = pyoracle.rel_l2(y.cpu().numpy(), want)
+    assert e < 1e-5, (M, N, K, e)
+print("persistent ok")
+"""
+
+
+@pytest.mark.new_on_gpu(stage=1)
+def test_gemm_bf16_persistent_form(cuda):
+    """The persistent GEMM (SMOL_GEMM_PERSISTENT=1, read when the library loads, so it
+    runs in a child process): more tiles than SMs (up to 4 per CTA, so both accumulators
+    are reused), ragged tails, bias + GELU."""
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    root = os.path.dirname(here)
+    code = _PERSISTENT_CHECK.format(oracle=os.path.join(root, "oracle"), pkg=os.path.join(root, "smol-genius_b200"))
+    env = dict(os.environ, SMOL_GEMM_PERSISTENT="1")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0 and "persistent ok" in r.stdout, r.stdout + r.stderr
+
+
 @pytest.mark.new_on_gpu(stage=1)
 def test_layer_norm_fp32_bf16_in_place(cuda):
     rng = np.random.default_rng(3)
