@@ -315,7 +315,7 @@ typedef struct smol_b200_qkn_model {
 } smol_b200_qkn_model;
 
 /* Device workspace one step needs for n_seqs sequences of at most max_kv_len cached
- * tokens (before the step). */
+ * tokens (before the step); 0 when the model is malformed. */
 SMOL_B200_API size_t smol_b200_qkn_step_workspace_bytes(const smol_b200_qkn_model *model, int n_seqs,
                                                         int max_kv_len);
 
@@ -342,6 +342,7 @@ SMOL_B200_API int smol_b200_qkn_decode_step(
  * n_tokens) (sliding layers their window).  No logits, as the reference; a decode step
  * with kv_len = start + n_tokens continues from it.  rope tables: >= start + n_tokens
  * rows.  head_dim 64, 128 or 256. */
+/* 0 when the model is malformed (the call would return SMOL_B200_ERR_ARGS). */
 SMOL_B200_API size_t smol_b200_qkn_prefill_workspace_bytes(const smol_b200_qkn_model *model, int n_tokens);
 SMOL_B200_API int smol_b200_qkn_prefill(void *stream, const smol_b200_qkn_model *model, const int *tokens,
                                         int n_tokens, int start, uint16_t *k_pool, uint16_t *v_pool,
@@ -405,7 +406,8 @@ typedef struct smol_b200_siglip_model {
     const smol_b200_siglip_layer *layers;         /* host array of n_layers       */
 } smol_b200_siglip_model;
 
-/* Device workspace of smol_b200_siglip_forward for n_images images. */
+/* Device workspace of smol_b200_siglip_forward for n_images images (0: a shape the
+ * device path does not take -- the call would return SMOL_B200_ERR_ARGS). */
 SMOL_B200_API size_t smol_b200_siglip_workspace_bytes(const smol_b200_siglip_model *model, int n_images);
 
 /* images: [n_images][3][image_size][image_size] fp32; out: [n_images][n_patches][hidden]
