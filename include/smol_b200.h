@@ -275,6 +275,8 @@ SMOL_B200_API int smol_b200_decode_step_host(
  * NULL) and Gemma as the exports set it (paligemma.c:206-230): embedding scale,
  * GeGLU, a norm on each sublayer's output before its residual add, attention softcap,
  * sliding-window layers with their own RoPE tables; QK-norm is optional in both.
+ * SmolVLM's decoder (smolvlm_decoder_forward, exports/smolvlm/decoder.c:391-476) is
+ * the Qwen3 configuration without QK-norm and with an untied `lm_head`.
  *
  * Every pointer below is device memory except `layers` (a host array).  The step is
  * asynchronous on `stream` and allocation-free, so a decode loop can be captured
@@ -312,6 +314,8 @@ typedef struct smol_b200_qkn_model {
     int sliding_window;               /* > 0: window of the is_sliding layers    */
     const float *rope_cos_local;      /* tables of the is_sliding layers, as the */
     const float *rope_sin_local;      /* step's; NULL: the step's tables         */
+    /* Untied output head (SmolVLM's decoder, exports/smolvlm/decoder.c:473-475): */
+    const uint16_t *lm_head;          /* [vocab][hidden] bf16; NULL: tok_embeddings */
 } smol_b200_qkn_model;
 
 /* Device workspace one step needs for n_seqs sequences of at most max_kv_len cached

@@ -56,10 +56,13 @@ class QknOracle:
     """A seeded decoder (Qwen3 or Gemma configuration) and its reference forward passes."""
 
     def __init__(self, hidden=1024, layers=2, n_heads=16, n_kv_heads=8, head_dim=128, intermediate=3072,
-                 vocab=4096, theta=1e6, eps=1e-6, qk_gain=3.0, vo_gain=4.0, seed=0, cap=1024, gemma=None):
+                 vocab=4096, theta=1e6, eps=1e-6, qk_gain=3.0, vo_gain=4.0, seed=0, cap=1024, gemma=None,
+                 qk_norm=True, tied=True):
         """gemma (None for Qwen3): dict of the Gemma settings -- embed_normalizer, attn_softcap,
         sliding_window, sliding (per-layer flags), local_theta, qk_norm (bool), interleaved (bool),
-        sublayer_gain.  Gemma models carry pre/post-FFN norms and use GeGLU."""
+        sublayer_gain.  Gemma models carry pre/post-FFN norms and use GeGLU.
+        qk_norm=False, tied=False: SmolVLM's decoder (exports/smolvlm/decoder.c:391-476) --
+        no per-head QK-norm, an lm_head of its own."""
         rng = np.random.default_rng(seed)
         self.H, self.L, self.HQ, self.HKV, self.HD = hidden, layers, n_heads, n_kv_heads, head_dim
         self.I, self.V, self.eps, self.cap = intermediate, vocab, eps, cap
@@ -71,7 +74,7 @@ class QknOracle:
         self.sliding_window = int(g.get("sliding_window", 0))
         self.sliding = [bool(x) for x in g.get("sliding", [False] * layers)]
         self.local_theta = float(g.get("local_theta", 0.0))
-        self.qk_norm = bool(g.get("qk_norm", True))
+        self.qk_norm = bool(g.get("qk_norm", qk_norm))
         self.interleaved = bool(g.get("interleaved", False))
         qd, kvd = n_heads * head_dim, n_kv_heads * head_dim
 
@@ -98,6 +101,8 @@ class QknOracle:
                 "q_norm": near(head_dim, qk_gain),
                 "k_norm": near(head_dim, qk_gain),
             })
+            if not self.gemma and not self.qk_norm:
+                del self.layers[-1]["q_norm"], self.layers[-1]["k_norm"]
             if self.gemma:
                 # the sublayer-output norms scale each sublayer's contribution against the
                 # embedding (sublayer_gain, so that the next token is not the fed one)
@@ -107,6 +112,8 @@ class QknOracle:
                 self.layers[-1]["post_ffn_norm"] = (near(hidden, 1.0) * gain).astype(np.float32)
                 if not self.qk_norm:
                     del self.layers[-1]["q_norm"], self.layers[-1]["k_norm"]
+        # an untied output head is drawn last, so the tied models' weights do not move
+        self.lm_head = None if tied else bf(vocab, hidden)
         self.cos, self.sin = pyoracle.fill_rope_table(cap, head_dim, theta, self.interleaved)
         # sliding layers use their own table when the theta differs (qkn_decoder.c:313-340, :462-468)
         self.has_local = self.local_theta > 0 and self.local_theta != theta
@@ -174,7 +181,7 @@ class QknOracle:
             x = self._layer(l, x, self.len)
         self.len += 1
         xf = rms_norm(x, self.final_norm, self.eps)[0]
-        logits = self.E @ xf
+        logits = (self.E if self.lm_head is None else self.lm_head) @ xf
         top = np.argsort(logits)[-2:]
         return argmax_first(logits), float(logits[top[1]] - logits[top[0]]), xf
 
@@ -202,7 +209,12 @@ PIN_CASES = {
     "qwen3-2": {"layers": 2, "prompt_len": 64, "steps": 24, "seed": 12, "gemma": None},
     "gemma2-2": {"layers": 2, "prompt_len": 64, "steps": 24, "seed": 13, "gemma": GEMMA2_SMALL},
     "gemma3-2": {"layers": 2, "prompt_len": 64, "steps": 24, "seed": 14, "gemma": GEMMA3_SMALL},
+    # SmolVLM's decoder (run by oracle/_ref/smolvlm_weights_ref): MHA with head dim 64,
+    # no QK-norm, an untied lm_head, its RoPE theta and epsilon
+    "smolvlm-2": {"layers": 2, "prompt_len": 64, "steps": 24, "seed": 15, "gemma": None, "smolvlm": True},
 }
+SMOLVLM_SHAPE = {"hidden": 512, "n_heads": 8, "n_kv_heads": 8, "head_dim": 64, "intermediate": 1536,
+                 "theta": 273768.0, "eps": 1e-5, "qk_norm": False, "tied": False}
 
 
 def pin_case(name: str):
@@ -210,9 +222,10 @@ def pin_case(name: str):
     and the tokens fed at each teacher-forced step -- the prompt's last token, then a
     seeded random stream (random models' own greedy streams tend to settle on one token)."""
     c = PIN_CASES[name]
-    shape = GEMMA_SHAPE if c["gemma"] else {}
+    shape = dict(theta=1e6, eps=1e-6)
+    shape.update(GEMMA_SHAPE if c["gemma"] else (SMOLVLM_SHAPE if c.get("smolvlm") else {}))
     m = QknOracle(layers=c["layers"], seed=c["seed"], qk_gain=3.0, vo_gain=4.0,
-                  cap=c["prompt_len"] + c["steps"] + 8, theta=1e6, eps=1e-6, gemma=c["gemma"], **shape)
+                  cap=c["prompt_len"] + c["steps"] + 8, gemma=c["gemma"], **shape)
     rng = np.random.default_rng(c["seed"])
     prompt = rng.integers(0, m.V, c["prompt_len"]).tolist()
     feed = [prompt[-1]] + rng.integers(0, m.V, c["steps"] - 1).tolist()
@@ -248,6 +261,8 @@ def write_weights_file(path, m: QknOracle, prompt, feed) -> None:
                 f.write(f32(lw[name]))
         f.write(np.asarray(prompt, "<i4").tobytes())
         f.write(np.asarray(feed, "<i4").tobytes())
+        if m.lm_head is not None:   # read by the SmolVLM driver only
+            f.write(bits(m.lm_head))
 
 
 def read_reference_steps(path, n_steps: int, hidden: int):

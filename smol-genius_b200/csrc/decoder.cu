@@ -969,8 +969,9 @@ int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *mp, int n_seqs, 
     }
     if (rc != SMOL_B200_OK) return rc;
     // final RMSNorm (qkn_decoder.c:710) folded into the argmax; the normalised state lands in xn
-    rc = run_argmax(st, tokens_out, w.x, H, m.tok_embeddings, m.vocab, H, n_seqs, w.argmax_ws, w.argmax_ws_bytes,
-                    m.final_norm, m.eps, w.xn);
+    // the greedy token over the output head: tied embeddings, or SmolVLM's lm_head (decoder.c:473-475)
+    rc = run_argmax(st, tokens_out, w.x, H, m.lm_head ? m.lm_head : m.tok_embeddings, m.vocab, H, n_seqs, w.argmax_ws,
+                    w.argmax_ws_bytes, m.final_norm, m.eps, w.xn);
     if (rc != SMOL_B200_OK) return rc;
     if (advance && launch_kernel(advance_kernel, dim3((n_seqs + 255) / 256), dim3(256), 0, st, kv_len, n_seqs) !=
                        cudaSuccess)

@@ -318,7 +318,7 @@ class QknModel(ctypes.Structure):
                 ("layers", ctypes.POINTER(QknLayer)), ("activation", ctypes.c_int),
                 ("embed_normalizer", ctypes.c_float), ("attn_softcap", ctypes.c_float),
                 ("sliding_window", ctypes.c_int), ("rope_cos_local", ctypes.c_void_p),
-                ("rope_sin_local", ctypes.c_void_p)]
+                ("rope_sin_local", ctypes.c_void_p), ("lm_head", ctypes.c_void_p)]
 
 
 ACT_SWIGLU, ACT_GEGLU = 0, 1
@@ -326,7 +326,7 @@ ACT_SWIGLU, ACT_GEGLU = 0, 1
 
 def qkn_model(hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab, eps, tok_embeddings, final_norm, layers,
               rope_interleaved=False, activation=ACT_SWIGLU, embed_normalizer=0.0, attn_softcap=0.0,
-              sliding_window=0, rope_cos_local=None, rope_sin_local=None, sliding=None) -> QknModel:
+              sliding_window=0, rope_cos_local=None, rope_sin_local=None, sliding=None, lm_head=None) -> QknModel:
     """layers: list of dicts mapping QknLayer pointer field names to device tensors (absent
     names -> NULL); sliding: per-layer is_sliding flags (default all 0)."""
     arr = (QknLayer * len(layers))()
@@ -338,7 +338,7 @@ def qkn_model(hidden, n_heads, n_kv_heads, head_dim, intermediate, vocab, eps, t
     m = QknModel(hidden, len(layers), n_heads, n_kv_heads, head_dim, intermediate, vocab, eps, int(rope_interleaved),
                  _ptr(tok_embeddings), _ptr(final_norm), ctypes.cast(arr, ctypes.POINTER(QknLayer)), int(activation),
                  float(embed_normalizer), float(attn_softcap), int(sliding_window), _ptr(rope_cos_local),
-                 _ptr(rope_sin_local))
+                 _ptr(rope_sin_local), _ptr(lm_head))
     m._layers = arr   # keep the array alive with the struct
     return m
 

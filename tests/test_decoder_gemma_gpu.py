@@ -10,9 +10,10 @@ same teacher-forced steps.  Checked:
   * the GELU-tanh-gated matrix-vector product (mode 3) against fp32 numpy, and the
     product with a 16384-wide input (fewer sequences per launch);
   * 2-layer Gemma 2 / Gemma 3 style decoders (MQA 8/1, head dim 256, one sliding layer
-    with a 64-token window over a 300-token prompt): every step's final normalised
-    state within rel-L2 1e-3 of the oracle's and the same token wherever the oracle's
-    top-2 margin exceeds 0.05.
+    with a 64-token window over a 300-token prompt), and SmolVLM's decoder (MHA with head
+    dim 64, no QK-norm, an untied lm_head): every step's final normalised state within
+    rel-L2 1e-3 of the oracle's and the same token wherever the oracle's top-2 margin
+    exceeds 0.05.
 """
 import numpy as np
 import pytest
@@ -20,7 +21,7 @@ import torch
 
 import pyoracle
 import smol_b200
-from qkn_decoder_oracle import GEMMA2_SMALL, GEMMA3_SMALL, GEMMA_SHAPE, QknOracle, geglu
+from qkn_decoder_oracle import GEMMA2_SMALL, GEMMA3_SMALL, GEMMA_SHAPE, SMOLVLM_SHAPE, QknOracle, geglu
 
 pytestmark = [pytest.mark.gpu, pytest.mark.new_on_gpu]
 
@@ -112,3 +113,45 @@ def test_gemma_decoder_step_teacher_forced(cuda, gemma, seed):
     assert int(kv_len.item()) == 299 + steps
     assert checked >= steps // 2
     print(f"{steps} teacher-forced Gemma steps: worst hidden-state rel-L2 {worst:.2e}; {checked} clear tokens equal")
+
+
+def test_smolvlm_decoder_step_teacher_forced(cuda):
+    """SmolVLM's decoder (exports/smolvlm/decoder.c:391-476): the Qwen3 step without
+    QK-norm, greedy over an untied lm_head."""
+    cap, steps = 512, 32
+    m = QknOracle(layers=2, seed=23, qk_gain=3.0, vo_gain=4.0, cap=cap, **SMOLVLM_SHAPE)
+    rng = np.random.default_rng(23)
+    prompt = rng.integers(0, m.V, 300)
+    feed = [int(prompt[-1])] + rng.integers(0, m.V, steps - 1).tolist()
+    t = _dev(cuda)
+    m.prefill(prompt[:-1])
+    emb, fnorm, layers = m.device_weights(t)
+    head = t(pyoracle.bf16_bits(m.lm_head))
+    model = smol_b200.qkn_model(m.H, m.HQ, m.HKV, m.HD, m.I, m.V, m.eps, emb, fnorm, layers, lm_head=head)
+    kvd = m.HKV * m.HD
+    k_pool = torch.zeros((m.L * cap, kvd), dtype=torch.int16, device=cuda)
+    v_pool = torch.zeros((m.L * cap, kvd), dtype=torch.int16, device=cuda)
+    for l in range(m.L):
+        k_pool[l * cap:(l + 1) * cap] = torch.from_numpy(m.kc[l].view(np.int16)).to(cuda)
+        v_pool[l * cap:(l + 1) * cap] = torch.from_numpy(m.vc[l].view(np.int16)).to(cuda)
+    row0 = torch.tensor([l * cap for l in range(m.L)], dtype=torch.int64, device=cuda)
+    kv_len = torch.tensor([m.len], dtype=torch.int32, device=cuda)
+    ws = torch.zeros(smol_b200.qkn_step_workspace_bytes(model, 1, cap - 1), dtype=torch.uint8, device=cuda)
+    cos, sin = t(m.cos), t(m.sin)
+    tok_in = torch.zeros(1, dtype=torch.int32, device=cuda)
+    tok_out = torch.zeros(1, dtype=torch.int32, device=cuda)
+    xn_off = (m.H * 4 + 255) // 256 * 256
+    checked = 0
+    for s in range(steps):
+        tok_in.fill_(feed[s])
+        smol_b200.qkn_decode_step(model, 1, tok_in, tok_out, k_pool, v_pool, m.L * cap, row0, kv_len, cap - 1, cos,
+                                  sin, ws, advance=True)
+        want, margin, xf = m.forward(feed[s])
+        torch.cuda.synchronize()
+        assert smol_b200.last_error() == 0 and smol_b200.device_error() == 0
+        err = pyoracle.rel_l2(ws[xn_off:xn_off + m.H * 4].view(torch.float32).cpu().numpy(), xf)
+        assert err < 1e-3, (s, err)
+        if margin > 0.05:
+            checked += 1
+            assert int(tok_out.item()) == want, (s, int(tok_out.item()), want, margin)
+    assert checked >= steps // 2

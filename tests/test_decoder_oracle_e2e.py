@@ -7,10 +7,12 @@ Both sides are teacher-forced on the same tokens (a seeded random stream), so ev
 step is compared on the same history: the greedy token wherever the top-2 margin
 exceeds the difference the hidden states allow, and the final normalised hidden state
 within rel-L2 3e-3 at every step and 1e-4 / 1e-3 (one / two layers) at the median.
-The cases (oracle PIN_CASES) cover Qwen3 with one and two layers and the Gemma 2 /
-Gemma 3 settings.  Where the reference binary is built the comparison runs live;
-everywhere it also runs against the reference's outputs committed in
-tests/golden/decoder_cases.npz (tests/golden/make_decoder_golden.py).
+The cases (oracle PIN_CASES) cover Qwen3 with one and two layers, the Gemma 2 /
+Gemma 3 settings, and SmolVLM's own decoder (exports/smolvlm/decoder.c:269-476, run by
+oracle/_ref/smolvlm_weights_emul: no QK-norm, an untied lm_head).  Where the reference
+binaries are built the comparison runs live; everywhere it also runs against the
+reference's outputs committed in tests/golden/decoder_cases.npz
+(tests/golden/make_decoder_golden.py).
 
 The tolerance is that of storage rounding, not of the restatement: a cache element
 whose fp32 value lies within the accumulation-order difference (~1e-6) of a bf16
@@ -29,13 +31,21 @@ import pytest
 import pyoracle
 from qkn_decoder_oracle import PIN_CASES, pin_case, read_reference_steps, run_teacher_forced, write_weights_file
 
-BIN = os.path.join(os.path.dirname(pyoracle.__file__), "_ref", "qkn_weights_emul")
+REF_DIR = os.path.join(os.path.dirname(pyoracle.__file__), "_ref")
+
+
+def _binary(case):
+    """The reference decoder a case runs on: qkn_decoder.c, or SmolVLM's decoder.c."""
+    return os.path.join(REF_DIR, "smolvlm_weights_emul" if PIN_CASES[case].get("smolvlm") else "qkn_weights_emul")
+
+
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "decoder_cases.npz")
 
 
 def _check(m, tokens, margins, xs, ref_tokens, ref_xs):
     steps = len(tokens)
-    e_norm = float(np.max(np.linalg.norm(m.E, axis=1)))
+    head = m.E if m.lm_head is None else m.lm_head
+    e_norm = float(np.max(np.linalg.norm(head, axis=1)))
     errs = [pyoracle.rel_l2(xs[s], ref_xs[s]) for s in range(steps)]
     assert max(errs) < 3e-3, errs
     assert float(np.median(errs)) < (1e-4 if m.L == 1 else 1e-3), errs
@@ -48,14 +58,15 @@ def _check(m, tokens, margins, xs, ref_tokens, ref_xs):
     assert len(set(tokens)) > steps // 3          # the outputs are not one repeated token
 
 
-@pytest.mark.skipif(not os.path.exists(BIN), reason="oracle/_ref/qkn_weights_emul not built")
 @pytest.mark.parametrize("case", list(PIN_CASES))
 def test_oracle_decoder_matches_reference_decoder(tmp_path, case):
+    if not os.path.exists(_binary(case)):
+        pytest.skip(f"{_binary(case)} not built")
     m, prompt, feed = pin_case(case)
     inp, out = tmp_path / "model.bin", tmp_path / "steps.bin"
     write_weights_file(inp, m, prompt, feed)
     tokens, margins, xs = run_teacher_forced(m, prompt, feed)
-    subprocess.run([BIN, str(inp), str(out)], check=True, timeout=300)
+    subprocess.run([_binary(case), str(inp), str(out)], check=True, timeout=300)
     ref_tokens, ref_xs = read_reference_steps(out, len(feed), m.H)
     _check(m, tokens, margins, xs, ref_tokens, ref_xs)
 
