@@ -420,6 +420,18 @@ SMOL_B200_API int smol_b200_siglip_forward(void *stream, float *out, const float
                                            const smol_b200_siglip_model *model, void *workspace,
                                            size_t workspace_bytes);
 
+/* The pre-LayerNorm encoder layers on their own (siglip.c:112-147; the Qwen3-ASR audio
+ * encoder's layers, exports/qwen_asr/encoder.c:449-484, have the same form): x
+ * [batch][seq][hidden] fp32 in place; window_starts (device, n_windows + 1 entries, as
+ * smol_bidirectional_attention takes them) limits attention to windows within every
+ * batch element, NULL lets every token attend to its whole batch element.  eps: the
+ * LayerNorm epsilon (SigLIP 1e-6, the audio encoder 1e-5). */
+SMOL_B200_API size_t smol_b200_encoder_workspace_bytes(int n_tokens, int hidden, int ffn);
+SMOL_B200_API int smol_b200_encoder_layers(void *stream, float *x, int batch, int seq,
+                                           const smol_b200_siglip_layer *layers, int n_layers, int hidden,
+                                           int heads, int ffn, float eps, const int *window_starts, int n_windows,
+                                           void *workspace, size_t workspace_bytes);
+
 /* The building blocks:
  *   C[m][n] (+)= sum_k A[m][k] * W[n][k] + bias[n] + add[m % add_rows][n], stored as
  *   out_kind says.  A bf16 [M][lda], W bf16 [N][ldw] (K-major, 16-byte aligned, lda / ldw

@@ -103,8 +103,10 @@ class SiglipOracle:
             out.append((u @ self.patch_w.T + self.patch_b + self.pos).astype(np.float32))
         return np.stack(out)
 
-    def layer(self, x: np.ndarray, l: int, device_formats: bool) -> np.ndarray:
-        """One encoder layer over [n_img, seq, hidden] (siglip.c:112-147)."""
+    def layer(self, x: np.ndarray, l: int, device_formats: bool, window_starts=None) -> np.ndarray:
+        """One encoder layer over [n_img, seq, hidden] (siglip.c:112-147); window_starts
+        limits the attention to windows, as the Qwen3-ASR audio encoder's layers do
+        (encoder.c:449-484)."""
         lw = self.layers[l]
         r16 = pyoracle.round_bf16 if device_formats else (lambda a: a)
         v16 = f16 if device_formats else (lambda a: a)
@@ -117,13 +119,20 @@ class SiglipOracle:
             q = r16((xn @ lw["wq"].T + lw["bq"]).astype(np.float32))
             k = r16((xn @ lw["wk"].T + lw["bk"]).astype(np.float32))
             v = v16((xn @ lw["wv"].T + lw["bv"]).astype(np.float32))
-            a = self.o.bidirectional_attention(q, k, v, seq, self.NH, self.HD, scale, [0, seq])
+            a = self.o.bidirectional_attention(q, k, v, seq, self.NH, self.HD, scale,
+                                               [0, seq] if window_starts is None else window_starts)
             a = r16(a)
             xi = (xi + (a @ lw["wo"].T + lw["bo"])).astype(np.float32)
             xn = r16(layer_norm(xi, lw["ln2_w"], lw["ln2_b"], self.eps))
             h = r16(gelu_tanh((xn @ lw["fc1"].T + lw["b1"]).astype(np.float32)))
             out[i] = (xi + (h @ lw["fc2"].T + lw["b2"])).astype(np.float32)
         return out
+
+    def encoder_layers(self, x: np.ndarray, device_formats: bool = True, window_starts=None) -> np.ndarray:
+        """The layer stack alone over [batch, seq, hidden] (no patch embedding, no post-LN)."""
+        for l in range(self.L):
+            x = self.layer(x, l, device_formats, window_starts)
+        return x
 
     def forward(self, images: np.ndarray, device_formats: bool = True) -> np.ndarray:
         """siglip_forward for a batch of [3, image, image] images: [n_img, n_pos, hidden]."""

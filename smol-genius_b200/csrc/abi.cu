@@ -643,6 +643,20 @@ int smol_b200_siglip_forward(void *stream, float *out, const float *images, int 
                   "smol_b200_siglip_forward");
 }
 
+size_t smol_b200_encoder_workspace_bytes(int n_tokens, int hidden, int ffn)
+{
+    return encoder_workspace_bytes(n_tokens, hidden, ffn);
+}
+
+int smol_b200_encoder_layers(void *stream, float *x, int batch, int seq, const smol_b200_siglip_layer *layers,
+                             int n_layers, int hidden, int heads, int ffn, float eps, const int *window_starts,
+                             int n_windows, void *workspace, size_t workspace_bytes)
+{
+    return record(encoder_layers(static_cast<cudaStream_t>(stream), x, batch, seq, layers, n_layers, hidden, heads,
+                                 ffn, eps, window_starts, n_windows, workspace, workspace_bytes),
+                  "smol_b200_encoder_layers");
+}
+
 int smol_b200_gemm_bf16(void *stream, void *out, int64_t ldo, int out_kind, const uint16_t *a, int64_t lda,
                         const uint16_t *w, int64_t ldw, const float *bias, const float *add, int64_t ld_add,
                         int add_rows, int m, int n, int k, int act)

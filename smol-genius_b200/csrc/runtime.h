@@ -150,6 +150,10 @@ int gemm_bf16(cudaStream_t st, void *out, int64_t ldo, int out_kind, const uint1
 int convert_f32_to_bf16(cudaStream_t st, uint16_t *dst, const float *src, long long n);
 int layer_norm(cudaStream_t st, void *out, int out_bf16, const float *x, const float *w, const float *b, int rows,
                int hidden, float eps);
+size_t encoder_workspace_bytes(int n_tokens, int hidden, int ffn);
+int encoder_layers(cudaStream_t st, float *x, int batch, int seq, const smol_b200_siglip_layer *layers, int n_layers,
+                   int hidden, int heads, int ffn, float eps, const int *window_starts, int n_windows,
+                   void *workspace, size_t workspace_bytes);
 size_t siglip_workspace_bytes(const smol_b200_siglip_model *m, int n_images);
 int siglip_forward(cudaStream_t st, float *out, const float *images, int n_images, const smol_b200_siglip_model *m,
                    void *workspace, size_t workspace_bytes);

@@ -1,4 +1,6 @@
-// siglip.cu -- the SigLIP vision encoder (siglip_forward, siglip.c:71-156) on the device.
+// siglip.cu -- the SigLIP vision encoder (siglip_forward, siglip.c:71-156) and the
+// pre-LayerNorm encoder layers it shares with the Qwen3-ASR audio encoder
+// (encoder.c:449-484, attention within the windows of :426-435) on the device.
 //
 // Per batch of images: the patches are unfolded into bf16 rows (the im2col of the
 // kernel = stride = patch convolution, conv2d.c:13-50, one row per patch) and the patch
@@ -98,17 +100,16 @@ unsigned grid_for(long long work, int block)
     return static_cast<unsigned>(g < 148LL * 32 ? (g > 0 ? g : 1) : 148LL * 32);
 }
 
-// Workspace pieces (256-byte aligned).
-struct SiglipWs {
-    uint16_t *patches, *xn, *q, *k, *v, *attn16, *h;
+// Workspace of the encoder layers for T tokens (256-byte aligned pieces).
+struct EncoderWs {
+    uint16_t *xn, *q, *k, *v, *attn16, *h;
     float *attn;
-    int lda, n_patches;
     size_t total;
 };
 
-SiglipWs carve(const smol_b200_siglip_model &m, int n_images, uint8_t *base)
+EncoderWs carve_encoder(size_t T, size_t H, size_t F, uint8_t *base)
 {
-    SiglipWs w;
+    EncoderWs w;
     memset(&w, 0, sizeof(w));
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -116,11 +117,6 @@ SiglipWs carve(const smol_b200_siglip_model &m, int n_images, uint8_t *base)
         off += (bytes + 255) / 256 * 256;
         return p;
     };
-    const int pw = m.image_size / m.patch;
-    w.n_patches = pw * pw;
-    w.lda = (3 * m.patch * m.patch + 7) / 8 * 8;
-    const size_t T = static_cast<size_t>(n_images) * w.n_patches, H = m.hidden, F = m.ffn;
-    w.patches = reinterpret_cast<uint16_t *>(take(T * w.lda * 2));
     w.xn = reinterpret_cast<uint16_t *>(take(T * H * 2));
     w.q = reinterpret_cast<uint16_t *>(take(T * H * 2));
     w.k = reinterpret_cast<uint16_t *>(take(T * H * 2));
@@ -132,23 +128,59 @@ SiglipWs carve(const smol_b200_siglip_model &m, int n_images, uint8_t *base)
     return w;
 }
 
-bool model_ok(const smol_b200_siglip_model *m)
+// SigLIP: the unfolded patches, then the encoder pieces.
+struct SiglipWs {
+    uint16_t *patches;
+    uint8_t *enc;
+    size_t enc_bytes;
+    int lda, n_patches;
+    size_t total;
+};
+
+SiglipWs carve(const smol_b200_siglip_model &m, int n_images, uint8_t *base)
 {
-    if (!m || m->hidden <= 0 || m->heads <= 0 || m->hidden % m->heads || m->ffn <= 0 || m->n_layers <= 0 ||
-        m->patch <= 0 || m->image_size < m->patch || m->hidden % 8 || m->ffn % 8 || !m->patch_w || !m->patch_b ||
-        !m->pos || !m->post_w || !m->post_b || !m->layers || m->patch_ld < 3 * m->patch * m->patch ||
-        m->patch_ld % 8)
-        return false;
-    const int hd = m->hidden / m->heads, pw = m->image_size / m->patch;
-    if (hd != 64 && hd != 128 && hd != 256) return false;
-    if (pw * pw > m->num_positions) return false;
-    for (int l = 0; l < m->n_layers; ++l) {
-        const smol_b200_siglip_layer &L = m->layers[l];
+    SiglipWs w;
+    memset(&w, 0, sizeof(w));
+    const int pw = m.image_size / m.patch;
+    w.n_patches = pw * pw;
+    w.lda = (3 * m.patch * m.patch + 7) / 8 * 8;
+    const size_t T = static_cast<size_t>(n_images) * w.n_patches;
+    const size_t patch_bytes = (T * w.lda * 2 + 255) / 256 * 256;
+    w.patches = base ? reinterpret_cast<uint16_t *>(base) : nullptr;
+    w.enc = base ? base + patch_bytes : nullptr;
+    w.enc_bytes = carve_encoder(T, m.hidden, m.ffn, nullptr).total;
+    w.total = patch_bytes + w.enc_bytes;
+    return w;
+}
+
+bool layers_ok(const smol_b200_siglip_layer *layers, int n_layers)
+{
+    if (!layers || n_layers <= 0) return false;
+    for (int l = 0; l < n_layers; ++l) {
+        const smol_b200_siglip_layer &L = layers[l];
         if (!L.ln1_w || !L.ln1_b || !L.wq || !L.wk || !L.wv || !L.wo || !L.bq || !L.bk || !L.bv || !L.bo ||
             !L.ln2_w || !L.ln2_b || !L.fc1 || !L.b1 || !L.fc2 || !L.b2)
             return false;
     }
     return true;
+}
+
+bool encoder_shape_ok(int hidden, int heads, int ffn)
+{
+    if (hidden <= 0 || heads <= 0 || hidden % heads || ffn <= 0 || hidden % 8 || ffn % 8) return false;
+    const int hd = hidden / heads;
+    return hd == 64 || hd == 128 || hd == 256;
+}
+
+bool model_ok(const smol_b200_siglip_model *m)
+{
+    if (!m || !encoder_shape_ok(m->hidden, m->heads, m->ffn) || m->patch <= 0 || m->image_size < m->patch ||
+        !m->patch_w || !m->patch_b || !m->pos || !m->post_w || !m->post_b ||
+        m->patch_ld < 3 * m->patch * m->patch || m->patch_ld % 8)
+        return false;
+    const int pw = m->image_size / m->patch;
+    if (pw * pw > m->num_positions) return false;
+    return layers_ok(m->layers, m->n_layers);
 }
 
 }  // namespace
@@ -176,6 +208,53 @@ int layer_norm(cudaStream_t st, void *out, int out_bf16, const float *x, const f
                : SMOL_B200_ERR_CUDA;
 }
 
+size_t encoder_workspace_bytes(int n_tokens, int hidden, int ffn)
+{
+    if (n_tokens <= 0 || hidden <= 0 || ffn <= 0) return 0;
+    return carve_encoder(static_cast<size_t>(n_tokens), hidden, ffn, nullptr).total;
+}
+
+int encoder_layers(cudaStream_t st, float *x, int batch, int seq, const smol_b200_siglip_layer *layers, int n_layers,
+                   int hidden, int heads, int ffn, float eps, const int *window_starts, int n_windows,
+                   void *workspace, size_t workspace_bytes)
+{
+    if (batch <= 0 || seq <= 0) return SMOL_B200_OK;
+    if (!x || !encoder_shape_ok(hidden, heads, ffn) || !layers_ok(layers, n_layers) ||
+        (window_starts && n_windows <= 0))
+        return SMOL_B200_ERR_ARGS;
+    const int H = hidden, F = ffn, T = batch * seq, hd = H / heads;
+    const EncoderWs w = carve_encoder(static_cast<size_t>(T), H, F, static_cast<uint8_t *>(workspace));
+    if (!workspace || workspace_bytes < w.total) return SMOL_B200_ERR_WORKSPACE;
+    const float scale = 1.0f / sqrtf(static_cast<float>(hd));   // siglip.c:108, encoder.c:447
+    const int64_t bs = static_cast<int64_t>(seq) * H;           // elements between batch elements
+    const int mask = window_starts ? SMOL_MASK_WINDOWS : SMOL_MASK_FULL;
+    int rc = SMOL_B200_OK;
+    for (int l = 0; l < n_layers && rc == SMOL_B200_OK; ++l) {
+        const smol_b200_siglip_layer &L = layers[l];
+        rc = layer_norm(st, w.xn, 1, x, L.ln1_w, L.ln1_b, T, H, eps);
+        if (rc == SMOL_B200_OK)
+            rc = gemm_bf16(st, w.q, H, SMOL_B200_GEMM_OUT_BF16, w.xn, H, L.wq, H, L.bq, nullptr, 0, 0, T, H, H, 0);
+        if (rc == SMOL_B200_OK)
+            rc = gemm_bf16(st, w.k, H, SMOL_B200_GEMM_OUT_BF16, w.xn, H, L.wk, H, L.bk, nullptr, 0, 0, T, H, H, 0);
+        if (rc == SMOL_B200_OK)
+            rc = gemm_bf16(st, w.v, H, SMOL_B200_GEMM_OUT_F16, w.xn, H, L.wv, H, L.bv, nullptr, 0, 0, T, H, H, 0);
+        // bidirectional attention: all tokens of a batch element (siglip.c:104-127) or the
+        // tokens of each window (encoder.c:426-435, :462-464)
+        if (rc == SMOL_B200_OK)
+            rc = prefill_attention(st, w.attn, H, bs, w.q, H, bs, w.k, H, bs, w.v, H, bs, batch, seq, seq, heads, heads,
+                                   hd, scale, mask, 0, 0, 0, 0.f, window_starts, n_windows);
+        if (rc == SMOL_B200_OK) rc = convert_f32_to_bf16(st, w.attn16, w.attn, static_cast<long long>(T) * H);
+        if (rc == SMOL_B200_OK)
+            rc = gemm_bf16(st, x, H, SMOL_B200_GEMM_OUT_F32_ADD, w.attn16, H, L.wo, H, L.bo, nullptr, 0, 0, T, H, H, 0);
+        if (rc == SMOL_B200_OK) rc = layer_norm(st, w.xn, 1, x, L.ln2_w, L.ln2_b, T, H, eps);
+        if (rc == SMOL_B200_OK)
+            rc = gemm_bf16(st, w.h, F, SMOL_B200_GEMM_OUT_BF16, w.xn, H, L.fc1, H, L.b1, nullptr, 0, 0, T, F, H, 1);
+        if (rc == SMOL_B200_OK)
+            rc = gemm_bf16(st, x, H, SMOL_B200_GEMM_OUT_F32_ADD, w.h, F, L.fc2, F, L.b2, nullptr, 0, 0, T, H, F, 0);
+    }
+    return rc;
+}
+
 size_t siglip_workspace_bytes(const smol_b200_siglip_model *m, int n_images)
 {
     if (!model_ok(m) || n_images <= 0) return 0;
@@ -190,10 +269,9 @@ int siglip_forward(cudaStream_t st, float *out, const float *images, int n_image
     const smol_b200_siglip_model &m = *mp;
     const SiglipWs w = carve(m, n_images, static_cast<uint8_t *>(workspace));
     if (!workspace || workspace_bytes < w.total) return SMOL_B200_ERR_WORKSPACE;
-    const int H = m.hidden, F = m.ffn, NP = w.n_patches, T = n_images * NP, hd = H / m.heads;
+    const int H = m.hidden, NP = w.n_patches, T = n_images * NP;
     const int kin = 3 * m.patch * m.patch;
-    const float scale = 1.0f / sqrtf(static_cast<float>(hd));   // siglip.c:108
-    float *x = out;                                             // the fp32 residual stream
+    float *x = out;   // the fp32 residual stream
 
     // patch embedding: conv bias and position embedding in the GEMM epilogue (siglip.c:80-89)
     {
@@ -204,30 +282,10 @@ int siglip_forward(cudaStream_t st, float *out, const float *images, int n_image
     }
     int rc = gemm_bf16(st, x, H, SMOL_B200_GEMM_OUT_F32, w.patches, w.lda, m.patch_w, m.patch_ld, m.patch_b, m.pos,
                        H, NP, T, H, kin, 0);
-    for (int l = 0; l < m.n_layers && rc == SMOL_B200_OK; ++l) {
-        const smol_b200_siglip_layer &L = m.layers[l];
-        rc = layer_norm(st, w.xn, 1, x, L.ln1_w, L.ln1_b, T, H, m.eps);
-        if (rc == SMOL_B200_OK)
-            rc = gemm_bf16(st, w.q, H, SMOL_B200_GEMM_OUT_BF16, w.xn, H, L.wq, H, L.bq, nullptr, 0, 0, T, H, H, 0);
-        if (rc == SMOL_B200_OK)
-            rc = gemm_bf16(st, w.k, H, SMOL_B200_GEMM_OUT_BF16, w.xn, H, L.wk, H, L.bk, nullptr, 0, 0, T, H, H, 0);
-        if (rc == SMOL_B200_OK)
-            rc = gemm_bf16(st, w.v, H, SMOL_B200_GEMM_OUT_F16, w.xn, H, L.wv, H, L.bv, nullptr, 0, 0, T, H, H, 0);
-        // all patches attend to all patches of their image (window {0, n_patches}, siglip.c:104-127)
-        if (rc == SMOL_B200_OK)
-            rc = prefill_attention(st, w.attn, H, static_cast<int64_t>(NP) * H, w.q, H, static_cast<int64_t>(NP) * H,
-                                   w.k, H, static_cast<int64_t>(NP) * H, w.v, H, static_cast<int64_t>(NP) * H,
-                                   n_images, NP, NP, m.heads, m.heads, hd, scale, SMOL_MASK_FULL, 0, 0, 0, 0.f,
-                                   nullptr, 0);
-        if (rc == SMOL_B200_OK) rc = convert_f32_to_bf16(st, w.attn16, w.attn, static_cast<long long>(T) * H);
-        if (rc == SMOL_B200_OK)
-            rc = gemm_bf16(st, x, H, SMOL_B200_GEMM_OUT_F32_ADD, w.attn16, H, L.wo, H, L.bo, nullptr, 0, 0, T, H, H, 0);
-        if (rc == SMOL_B200_OK) rc = layer_norm(st, w.xn, 1, x, L.ln2_w, L.ln2_b, T, H, m.eps);
-        if (rc == SMOL_B200_OK)
-            rc = gemm_bf16(st, w.h, F, SMOL_B200_GEMM_OUT_BF16, w.xn, H, L.fc1, H, L.b1, nullptr, 0, 0, T, F, H, 1);
-        if (rc == SMOL_B200_OK)
-            rc = gemm_bf16(st, x, H, SMOL_B200_GEMM_OUT_F32_ADD, w.h, F, L.fc2, F, L.b2, nullptr, 0, 0, T, H, F, 0);
-    }
+    // the encoder layers, every patch attending to every patch of its image (siglip.c:112-147)
+    if (rc == SMOL_B200_OK)
+        rc = encoder_layers(st, x, n_images, NP, m.layers, m.n_layers, H, m.heads, m.ffn, m.eps, nullptr, 0, w.enc,
+                            w.enc_bytes);
     // post-LayerNorm in place (siglip.c:150-151)
     if (rc == SMOL_B200_OK) rc = layer_norm(st, x, 0, x, m.post_w, m.post_b, T, H, m.eps);
     return rc;

@@ -103,6 +103,9 @@ _SIGNATURES = {
     # Part 5 (SigLIP encoder)
     "smol_b200_siglip_workspace_bytes": (_c_size, [_c_void, _c_int]),
     "smol_b200_siglip_forward": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_void, _c_void, _c_size]),
+    "smol_b200_encoder_workspace_bytes": (_c_size, [_c_int, _c_int, _c_int]),
+    "smol_b200_encoder_layers": (_c_int, [_c_void, _c_void, _c_int, _c_int, _c_void, _c_int, _c_int, _c_int, _c_int,
+                                          _c_float, _c_void, _c_int, _c_void, _c_size]),
     "smol_b200_gemm_bf16": (_c_int, [_c_void, _c_void, _c_i64, _c_int, _c_void, _c_i64, _c_void, _c_i64, _c_void,
                                      _c_void, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int]),
     "smol_b200_layer_norm": (_c_int, [_c_void, _c_void, _c_int, _c_void, _c_void, _c_void, _c_int, _c_int,
@@ -456,6 +459,29 @@ def siglip_model(hidden, heads, ffn, patch, image_size, num_positions, eps, patc
                     _ptr(patch_b), _ptr(pos), _ptr(post_w), _ptr(post_b), ctypes.cast(arr, ctypes.POINTER(SiglipLayer)))
     m._layers = arr
     return m
+
+
+def siglip_layers(layers) -> ctypes.Array:
+    """A SiglipLayer array from a list of dicts of device tensors (keep it referenced)."""
+    arr = (SiglipLayer * len(layers))()
+    for i, lw in enumerate(layers):
+        for name, _ in SiglipLayer._fields_:
+            setattr(arr[i], name, _ptr(lw[name]))
+    return arr
+
+
+def encoder_workspace_bytes(n_tokens: int, hidden: int, ffn: int) -> int:
+    return lib().smol_b200_encoder_workspace_bytes(n_tokens, hidden, ffn)
+
+
+def encoder_layers(x, batch, seq, layer_array, hidden, heads, ffn, eps, workspace, window_starts=None, stream=None):
+    """window_starts: device int32 tensor of n_windows + 1 entries, or None (whole sequence)."""
+    nw = 0 if window_starts is None else window_starts.numel() - 1
+    check(lib().smol_b200_encoder_layers(_stream(stream), _ptr(x), batch, seq,
+                                         ctypes.addressof(layer_array), len(layer_array), hidden,
+                                         heads, ffn, eps, _ptr(window_starts), nw, _ptr(workspace),
+                                         workspace.numel() * workspace.element_size()),
+          "smol_b200_encoder_layers")
 
 
 def siglip_workspace_bytes(model: SiglipModel, n_images: int) -> int:

@@ -9,7 +9,9 @@ Checked:
     within rel-L2 5e-3 of oracle/siglip_oracle.py with the device's 16-bit operands
     (bf16 rounding of LayerNorm / attention / GELU outputs turns the attention kernel's
     ~3e-4 difference into a few 1e-3), and within 1e-2 of the reference's own outputs
-    (tests/golden/siglip_cases.npz).
+    (tests/golden/siglip_cases.npz);
+  * the layer stack alone with attention windows (the audio encoder's form), against the
+    same oracle.
 """
 import os
 
@@ -19,7 +21,7 @@ import torch
 
 import pyoracle
 import smol_b200
-from siglip_oracle import SIGLIP_PIN_CASES, gelu_tanh, layer_norm, siglip_pin_case
+from siglip_oracle import SIGLIP_PIN_CASES, SiglipOracle, gelu_tanh, layer_norm, siglip_pin_case
 
 pytestmark = [pytest.mark.gpu, pytest.mark.new_on_gpu(stage=2)]
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "siglip_cases.npz")
@@ -199,3 +201,30 @@ def test_siglip_forward_matches_oracle_and_reference(cuda, case):
     ref = np.load(GOLDEN)[f"{case}/out"]
     assert pyoracle.rel_l2(got, ref) < 1e-2
     print(f"{case}: rel-L2 {e:.2e} vs the device-format oracle, {pyoracle.rel_l2(got, ref):.2e} vs the reference")
+
+
+def test_encoder_layers_with_windows(cuda):
+    """The layer stack alone with attention windows -- the Qwen3-ASR audio encoder's form
+    (encoder.c:449-484, eps 1e-5): ten 104-token windows, the last ragged, 4 heads of 64
+    (tests/test_encoder_layers_oracle.py pins the windowed oracle to the reference)."""
+    m = SiglipOracle(hidden=256, heads=4, ffn=512, layers=2, eps=1e-5, seed=8)
+    ws = list(range(0, 9 * 104 + 1, 104)) + [9 * 104 + 50]
+    T = ws[-1]
+    x = np.random.default_rng(9).standard_normal((T, m.H)).astype(np.float32)
+    t = _dev(cuda)
+    bits = lambda a: t(pyoracle.bf16_bits(a))   # noqa: E731
+    keep = [{"ln1_w": t(lw["ln1_w"]), "ln1_b": t(lw["ln1_b"]), "wq": bits(lw["wq"]), "wk": bits(lw["wk"]),
+             "wv": bits(lw["wv"]), "wo": bits(lw["wo"]), "bq": t(lw["bq"]), "bk": t(lw["bk"]), "bv": t(lw["bv"]),
+             "bo": t(lw["bo"]), "ln2_w": t(lw["ln2_w"]), "ln2_b": t(lw["ln2_b"]), "fc1": bits(lw["fc1"]),
+             "b1": t(lw["b1"]), "fc2": bits(lw["fc2"]), "b2": t(lw["b2"])} for lw in m.layers]
+    arr = smol_b200.siglip_layers(keep)
+    xd = t(x)
+    ws_d = t(np.asarray(ws, np.int32))
+    work = torch.zeros(smol_b200.encoder_workspace_bytes(T, m.H, m.F), dtype=torch.uint8, device=cuda)
+    smol_b200.encoder_layers(xd, 1, T, arr, m.H, m.NH, m.F, m.eps, work, window_starts=ws_d)
+    torch.cuda.synchronize()
+    _no_error()
+    got = xd.cpu().numpy()
+    e = pyoracle.rel_l2(got, m.encoder_layers(x[None], device_formats=True, window_starts=ws)[0])
+    assert e < 5e-3, e
+    assert pyoracle.rel_l2(got, m.encoder_layers(x[None], device_formats=False, window_starts=ws)[0]) < 1e-2
