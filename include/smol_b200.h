@@ -353,6 +353,30 @@ SMOL_B200_API int smol_b200_qkn_prefill(void *stream, const smol_b200_qkn_model 
                                         int64_t pool_rows, const int64_t *layer_row0_host, const float *rope_cos,
                                         const float *rope_sin, void *workspace, size_t workspace_bytes);
 
+/* The same two calls with the caller's input embeddings instead of token ids, as
+ * qkn_decoder_prefill / qkn_decoder_forward take them (an export passes image or audio
+ * features as embeddings): embeds fp32 [n][hidden] on the device, scaled by
+ * embed_normalizer when it is set, as the reference does (qkn_decoder.c:415-419,
+ * :596-599). */
+SMOL_B200_API int smol_b200_qkn_prefill_embeds(void *stream, const smol_b200_qkn_model *model,
+                                               const float *embeds, int n_tokens, int start, uint16_t *k_pool,
+                                               uint16_t *v_pool, int64_t pool_rows,
+                                               const int64_t *layer_row0_host, const float *rope_cos,
+                                               const float *rope_sin, void *workspace, size_t workspace_bytes);
+SMOL_B200_API int smol_b200_qkn_decode_step_embeds(
+    void *stream, const smol_b200_qkn_model *model, int n_seqs, const float *embeds, int *tokens_out,
+    uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows, const int64_t *layer_row0, int *kv_len,
+    int max_kv_len, const float *rope_cos, const float *rope_sin, int advance, void *workspace,
+    size_t workspace_bytes, float *x_normed_out /* optional [n_seqs][hidden]: the final normalised
+                                                   state (the reference's ctx->dec_x) */);
+
+/* Device memory for C callers that do not link the CUDA runtime themselves (the
+ * decoder-level drop-in): allocation (NULL on failure, recorded), release, and a
+ * synchronous copy in any direction between host and device pointers. */
+SMOL_B200_API void *smol_b200_device_alloc(size_t bytes);
+SMOL_B200_API void smol_b200_device_free(void *ptr);
+SMOL_B200_API int smol_b200_copy(void *dst, const void *src, size_t bytes);
+
 /* The building blocks of the step, for callers that orchestrate their own decoder:
  *   y[b][n] (+)= sum_k x[b][k] * W[n][k]    mode 0: store, 1: add into y (residual),
  *   2: SiLU-gated pairs, y[b][r] = silu(s[2r]) * s[2r+1] over W's 2*n_out rows

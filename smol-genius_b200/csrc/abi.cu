@@ -686,7 +686,7 @@ int smol_b200_qkn_prefill(void *stream, const smol_b200_qkn_model *model, const 
                           uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows, const int64_t *layer_row0_host,
                           const float *rope_cos, const float *rope_sin, void *workspace, size_t workspace_bytes)
 {
-    return record(qkn_prefill(static_cast<cudaStream_t>(stream), model, tokens, n_tokens, start, k_pool, v_pool,
+    return record(qkn_prefill(static_cast<cudaStream_t>(stream), model, tokens, nullptr, n_tokens, start, k_pool, v_pool,
                               pool_rows, layer_row0_host, rope_cos, rope_sin, workspace, workspace_bytes),
                   "smol_b200_qkn_prefill");
 }
@@ -696,12 +696,57 @@ size_t smol_b200_qkn_step_workspace_bytes(const smol_b200_qkn_model *model, int 
     return qkn_step_workspace_bytes(model, n_seqs, max_kv_len);
 }
 
+int smol_b200_qkn_prefill_embeds(void *stream, const smol_b200_qkn_model *model, const float *embeds, int n_tokens,
+                                 int start, uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows,
+                                 const int64_t *layer_row0_host, const float *rope_cos, const float *rope_sin,
+                                 void *workspace, size_t workspace_bytes)
+{
+    if (!embeds) return record(SMOL_B200_ERR_ARGS, "smol_b200_qkn_prefill_embeds");
+    return record(qkn_prefill(static_cast<cudaStream_t>(stream), model, nullptr, embeds, n_tokens, start, k_pool,
+                              v_pool, pool_rows, layer_row0_host, rope_cos, rope_sin, workspace, workspace_bytes),
+                  "smol_b200_qkn_prefill_embeds");
+}
+
+int smol_b200_qkn_decode_step_embeds(void *stream, const smol_b200_qkn_model *model, int n_seqs, const float *embeds,
+                                     int *tokens_out, uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows,
+                                     const int64_t *layer_row0, int *kv_len, int max_kv_len, const float *rope_cos,
+                                     const float *rope_sin, int advance, void *workspace, size_t workspace_bytes,
+                                     float *x_normed_out)
+{
+    if (!embeds) return record(SMOL_B200_ERR_ARGS, "smol_b200_qkn_decode_step_embeds");
+    return record(qkn_decode_step(static_cast<cudaStream_t>(stream), model, n_seqs, nullptr, embeds, tokens_out, k_pool,
+                                  v_pool, pool_rows, layer_row0, kv_len, max_kv_len, rope_cos, rope_sin, advance,
+                                  workspace, workspace_bytes, x_normed_out),
+                  "smol_b200_qkn_decode_step_embeds");
+}
+
+void *smol_b200_device_alloc(size_t bytes)
+{
+    if (bytes == 0) return nullptr;
+    void *p = nullptr;
+    if (!cuda_check(cudaMalloc(&p, bytes), "cudaMalloc")) return nullptr;
+    return p;
+}
+
+void smol_b200_device_free(void *p)
+{
+    if (p) cuda_check(cudaFree(p), "cudaFree");
+}
+
+int smol_b200_copy(void *dst, const void *src, size_t bytes)
+{
+    if (bytes == 0) return SMOL_B200_OK;
+    if (!dst || !src) return record(SMOL_B200_ERR_ARGS, "smol_b200_copy");
+    return cuda_check(cudaMemcpy(dst, src, bytes, cudaMemcpyDefault), "cudaMemcpy") ? SMOL_B200_OK
+                                                                                     : SMOL_B200_ERR_CUDA;
+}
+
 int smol_b200_qkn_decode_step(void *stream, const smol_b200_qkn_model *model, int n_seqs, const int *tokens_in,
                               int *tokens_out, uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows,
                               const int64_t *layer_row0, int *kv_len, int max_kv_len, const float *rope_cos,
                               const float *rope_sin, int advance, void *workspace, size_t workspace_bytes)
 {
-    return record(qkn_decode_step(static_cast<cudaStream_t>(stream), model, n_seqs, tokens_in, tokens_out, k_pool,
+    return record(qkn_decode_step(static_cast<cudaStream_t>(stream), model, n_seqs, tokens_in, nullptr, tokens_out, k_pool,
                                   v_pool, pool_rows, layer_row0, kv_len, max_kv_len, rope_cos, rope_sin, advance,
                                   workspace, workspace_bytes),
                   "smol_b200_qkn_decode_step");

@@ -401,14 +401,23 @@ __global__ void argmax_final_kernel(int *tokens_out, const float *part_val, cons
     if (threadIdx.x == 0) tokens_out[b] = bi;
 }
 
-// x[b][:] = E[tokens[b]][:] (bf16 -> fp32), times `scale` when it is positive (Gemma's
-// embed_normalizer, qkn_decoder.c:596-599)
+// x[b][:] = E[tokens[b]][:] (bf16 -> fp32) -- or x_in[b][:] when the caller passes its
+// own embeddings -- times `scale` when it is positive (Gemma's embed_normalizer,
+// qkn_decoder.c:596-599)
 __global__ void embed_kernel(float *x, const int *tokens, const uint16_t *emb, int hidden, int vocab, float scale,
-                             unsigned *err)
+                             unsigned *err, const float *x_in)
 {
     griddep_wait();
     griddep_trigger();
     const int b = blockIdx.x;
+    if (x_in) {   // the caller's embeddings (qkn_decoder_forward's input_embed), scaled the same way
+        for (int i = threadIdx.x; i < hidden; i += blockDim.x) {
+            float v = x_in[static_cast<size_t>(b) * hidden + i];
+            if (scale > 0.f) v *= scale;
+            x[static_cast<size_t>(b) * hidden + i] = v;
+        }
+        return;
+    }
     int t = tokens[b];
     if (t < 0 || t >= vocab) {
         if (threadIdx.x == 0) atomicOr(err, kErrBadArgs);
@@ -761,12 +770,12 @@ size_t qkn_prefill_workspace_bytes(const smol_b200_qkn_model *m, int n_tokens)
     return carve_prefill(*m, n_tokens, nullptr).total;
 }
 
-int qkn_prefill(cudaStream_t st, const smol_b200_qkn_model *mp, const int *tokens, int n, int start,
-                uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows, const int64_t *layer_row0,
+int qkn_prefill(cudaStream_t st, const smol_b200_qkn_model *mp, const int *tokens, const float *x_in, int n,
+                int start, uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows, const int64_t *layer_row0,
                 const float *rope_cos, const float *rope_sin, void *workspace, size_t workspace_bytes)
 {
     if (n <= 0) return SMOL_B200_OK;
-    if (!model_ok(mp) || !tokens || !k_pool || !v_pool || !layer_row0 || !rope_cos || !rope_sin || start < 0)
+    if (!model_ok(mp) || (!tokens == !x_in) || !k_pool || !v_pool || !layer_row0 || !rope_cos || !rope_sin || start < 0)
         return SMOL_B200_ERR_ARGS;
     const smol_b200_qkn_model &m = *mp;
     const int hd = m.head_dim;
@@ -798,7 +807,7 @@ int qkn_prefill(cudaStream_t st, const smol_b200_qkn_model *mp, const int *token
     };
     // embedding rows, scaled by the Gemma normaliser when set (qkn_decoder.c:408-419)
     if (launch_kernel(embed_kernel, dim3(n), dim3(256), 0, st, w.x, tokens, m.tok_embeddings, H, m.vocab,
-                      m.embed_normalizer, err) != cudaSuccess)
+                      m.embed_normalizer, err, x_in) != cudaSuccess)
         return SMOL_B200_ERR_CUDA;
     int rc = SMOL_B200_OK;
     for (int l = 0; l < m.n_layers && rc == SMOL_B200_OK; ++l) {
@@ -872,12 +881,13 @@ size_t qkn_step_workspace_bytes(const smol_b200_qkn_model *m, int n_seqs, int ma
 }
 
 int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *mp, int n_seqs, const int *tokens_in,
-                    int *tokens_out, uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows,
+                    const float *x_in, int *tokens_out, uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows,
                     const int64_t *layer_row0, int *kv_len, int max_kv_len, const float *rope_cos,
-                    const float *rope_sin, int advance, void *workspace, size_t workspace_bytes)
+                    const float *rope_sin, int advance, void *workspace, size_t workspace_bytes,
+                    float *x_normed_out)
 {
     if (n_seqs <= 0) return SMOL_B200_OK;
-    if (!model_ok(mp) || !tokens_in || !tokens_out || !k_pool || !v_pool || !layer_row0 || !kv_len || !rope_cos ||
+    if (!model_ok(mp) || (!tokens_in == !x_in) || !tokens_out || !k_pool || !v_pool || !layer_row0 || !kv_len || !rope_cos ||
         !rope_sin || max_kv_len < 0)
         return SMOL_B200_ERR_ARGS;
     const smol_b200_qkn_model &m = *mp;
@@ -895,7 +905,7 @@ int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *mp, int n_seqs, 
     if (launch_kernel(step_index_kernel, dim3((n_idx + 255) / 256), dim3(256), 0, st, w.positions, w.kv_next, w.slots,
                       layer_row0, static_cast<const int *>(kv_len), n_seqs, m.n_layers) != cudaSuccess ||
         launch_kernel(embed_kernel, dim3(n_seqs), dim3(256), 0, st, w.x, tokens_in, m.tok_embeddings, H, m.vocab,
-                      m.embed_normalizer, err) != cudaSuccess)
+                      m.embed_normalizer, err, x_in) != cudaSuccess)
         return SMOL_B200_ERR_CUDA;
 
     const int gate_mode = m.activation == 1 ? 3 : 2;   // GeGLU / SwiGLU (qkn_decoder.c:695-698)
@@ -973,6 +983,10 @@ int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *mp, int n_seqs, 
     rc = run_argmax(st, tokens_out, w.x, H, m.lm_head ? m.lm_head : m.tok_embeddings, m.vocab, H, n_seqs, w.argmax_ws,
                     w.argmax_ws_bytes, m.final_norm, m.eps, w.xn);
     if (rc != SMOL_B200_OK) return rc;
+    if (x_normed_out && !cuda_check(cudaMemcpyAsync(x_normed_out, w.xn, static_cast<size_t>(n_seqs) * H * sizeof(float),
+                                                    cudaMemcpyDeviceToDevice, st),
+                                    "cudaMemcpyAsync(x_normed)"))
+        return SMOL_B200_ERR_CUDA;
     if (advance && launch_kernel(advance_kernel, dim3((n_seqs + 255) / 256), dim3(256), 0, st, kv_len, n_seqs) !=
                        cudaSuccess)
         return SMOL_B200_ERR_CUDA;

@@ -131,12 +131,14 @@ int argmax_bf16(cudaStream_t st, int *tokens_out, const float *x, int64_t ldx, c
 size_t argmax_workspace_bytes(int n_seqs, int vocab);
 size_t qkn_step_workspace_bytes(const smol_b200_qkn_model *m, int n_seqs, int max_kv_len);
 int qkn_decode_step(cudaStream_t st, const smol_b200_qkn_model *m, int n_seqs, const int *tokens_in,
-                    int *tokens_out, uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows,
+                    const float *x_in, int *tokens_out, uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows,
                     const int64_t *layer_row0, int *kv_len, int max_kv_len, const float *rope_cos,
-                    const float *rope_sin, int advance, void *workspace, size_t workspace_bytes);
+                    const float *rope_sin, int advance, void *workspace, size_t workspace_bytes,
+                    float *x_normed_out = nullptr);
 
 size_t qkn_prefill_workspace_bytes(const smol_b200_qkn_model *m, int n_tokens);
-int qkn_prefill(cudaStream_t st, const smol_b200_qkn_model *m, const int *tokens, int n_tokens, int start,
+int qkn_prefill(cudaStream_t st, const smol_b200_qkn_model *m, const int *tokens, const float *x_in, int n_tokens,
+                int start,
                 uint16_t *k_pool, uint16_t *v_pool, int64_t pool_rows, const int64_t *layer_row0,
                 const float *rope_cos, const float *rope_sin, void *workspace, size_t workspace_bytes);
 

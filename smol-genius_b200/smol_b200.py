@@ -83,6 +83,14 @@ _SIGNATURES = {
     # Part 4 (device-resident decoder step)
     "smol_b200_qkn_step_workspace_bytes": (_c_size, [_c_void, _c_int, _c_int]),
     "smol_b200_qkn_prefill_workspace_bytes": (_c_size, [_c_void, _c_int]),
+    "smol_b200_qkn_prefill_embeds": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_void, _c_void, _c_i64,
+                                              _c_void, _c_void, _c_void, _c_void, _c_size]),
+    "smol_b200_qkn_decode_step_embeds": (
+        _c_int, [_c_void, _c_void, _c_int, _c_void, _c_void, _c_void, _c_void, _c_i64, _c_void, _c_void, _c_int,
+                 _c_void, _c_void, _c_int, _c_void, _c_size, _c_void]),
+    "smol_b200_device_alloc": (_c_void, [_c_size]),
+    "smol_b200_device_free": (None, [_c_void]),
+    "smol_b200_copy": (_c_int, [_c_void, _c_void, _c_size]),
     "smol_b200_qkn_prefill": (_c_int, [_c_void, _c_void, _c_void, _c_int, _c_int, _c_void, _c_void, _c_i64, _c_void,
                                        _c_void, _c_void, _c_void, _c_size]),
     "smol_b200_qkn_decode_step": (

@@ -237,6 +237,11 @@ int main(int argc, char **argv)
         for (int k = 0; k < HIDDEN; k++) x[k] = from_bf16(d->tok_embeddings_bf16[(size_t)tok * HIDDEN + k]);
         tok = qkn_decoder_forward(ctx, x);
         printf("%d%c", tok, s + 1 < steps ? ' ' : '\n');
+        if (tok < 0 || tok >= VOCAB) {   /* a failure sentinel (qkn_decoder.c:605-611), not a token */
+            printf("\n");
+            fprintf(stderr, "forward returned %d at step %d\n", tok, s);
+            return 3;
+        }
         double top1 = -INFINITY, top2 = -INFINITY;
         for (int v = 0; v < VOCAB; v++) {
             double dot = 0.0;

@@ -172,7 +172,7 @@ def test_binding_signatures_match_header():
     protos = re.findall(r"SMOL_B200_API\s+([\w\s\*]+?)\b(\w+)\s*\(([^;]*?)\)\s*;", text, flags=re.S)
     assert len(protos) == len(smol_b200.header_symbols())
     kinds = {"void": None, "int": ctypes.c_int, "size_t": ctypes.c_size_t, "unsigned": ctypes.c_uint,
-             "const char *": ctypes.c_char_p}
+             "const char *": ctypes.c_char_p, "void *": ctypes.c_void_p}
     for ret, name, args in protos:
         args = args.strip()
         n_args = 0 if args in ("", "void") else len(args.split(","))

@@ -37,3 +37,18 @@ def test_storage_precision_keeps_decisive_stream():
 def test_storage_precision_flips_near_tie_of_random_readout():
     args = (512, 128, 1, 3, 4, 1, 0)
     assert first_divergence(tokens("ref", args), tokens("emul", args)) == 116
+
+
+def test_device_decoder_dropin_fails_loudly_without_a_device():
+    """The decoder-level drop-in has no CPU path: without a GPU the prefill and the forward
+    say why on stderr and the forward returns the reference's allocation-failure
+    sentinel (151645), which the driver reports and stops on."""
+    import torch
+    device_bin = os.path.join(ROOT, "oracle", "_ref", "qkn_dropin_device")
+    if not os.path.exists(device_bin):
+        pytest.skip("qkn_dropin_device not built")
+    if torch.cuda.is_available():
+        pytest.skip("a CUDA device is present")
+    p = subprocess.run([device_bin, "32", "3"], capture_output=True, text=True, timeout=120)
+    assert p.returncode == 3 and p.stdout.split() == ["151645"], (p.returncode, p.stdout)
+    assert "qkn_decoder_prefill (device)" in p.stderr and "qkn_decoder_forward (device)" in p.stderr
