@@ -1,0 +1,196 @@
+/*
+ * device_decoder.c -- see device_decoder.h.
+ */
+#include "device_decoder.h"
+
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "smol_kernels.h"
+
+static void *upload(const void *host, size_t bytes)
+{
+    if (!host) return NULL;
+    void *d = smol_b200_device_alloc(bytes);
+    if (d && smol_b200_copy(d, host, bytes) != SMOL_B200_OK) {
+        smol_b200_device_free(d);
+        return NULL;
+    }
+    return d;
+}
+
+/* RoPE tables for positions [0, rows): the formula of qkn_decoder.c:261-311 and
+ * smol_compute_rope_* (rope.c:27-66) -- 1/powf(theta, 2d/hd), cosf / sinf of pos * f. */
+static int rope_tables(float **cos_d, float **sin_d, int rows, int head_dim, float theta, int interleaved)
+{
+    int *pos = (int *)malloc(sizeof(int) * (size_t)rows);
+    float *c = (float *)malloc(sizeof(float) * (size_t)rows * head_dim);
+    float *s = (float *)malloc(sizeof(float) * (size_t)rows * head_dim);
+    int ok = pos && c && s;
+    if (ok) {
+        for (int i = 0; i < rows; i++) pos[i] = i;
+        if (interleaved)
+            smol_compute_rope_interleaved(c, s, pos, rows, head_dim, theta);
+        else
+            smol_compute_rope_neox(c, s, pos, rows, head_dim, theta);
+        smol_b200_device_free(*cos_d);
+        smol_b200_device_free(*sin_d);
+        *cos_d = (float *)upload(c, sizeof(float) * (size_t)rows * head_dim);
+        *sin_d = (float *)upload(s, sizeof(float) * (size_t)rows * head_dim);
+        ok = *cos_d && *sin_d;
+    }
+    free(pos);
+    free(c);
+    free(s);
+    return ok;
+}
+
+int dd_setup(dd_state *st, const dd_config *c, const dd_layer *layers, const uint16_t *tok_embeddings,
+             const float *final_norm, const uint16_t *lm_head)
+{
+    if (c->layers < 1 || c->layers > DD_MAX_LAYERS) return -1;
+    memset(st, 0, sizeof(*st));
+    st->cfg = *c;
+    const size_t H = (size_t)c->hidden, I = (size_t)c->intermediate, HD = (size_t)c->head_dim;
+    const size_t qd = (size_t)c->heads * HD, kvd = (size_t)c->kv_heads * HD;
+    for (int l = 0; l < c->layers; l++) {
+        const dd_layer *ly = &layers[l];
+        smol_b200_qkn_layer *o = &st->layers[l];
+        o->wq = (const uint16_t *)upload(ly->wq, qd * H * 2);
+        o->wk = (const uint16_t *)upload(ly->wk, kvd * H * 2);
+        o->wv = (const uint16_t *)upload(ly->wv, kvd * H * 2);
+        o->wo = (const uint16_t *)upload(ly->wo, H * qd * 2);
+        o->gate_up = (const uint16_t *)upload(ly->gate_up, 2 * I * H * 2);
+        o->down = (const uint16_t *)upload(ly->down, H * I * 2);
+        o->input_norm = (const float *)upload(ly->input_norm, H * 4);
+        o->post_attn_norm = (const float *)upload(ly->post_attn_norm, H * 4);
+        o->q_norm = (const float *)upload(ly->q_norm, HD * 4);
+        o->k_norm = (const float *)upload(ly->k_norm, HD * 4);
+        o->pre_ffn_norm = (const float *)upload(ly->pre_ffn_norm, H * 4);
+        o->post_ffn_norm = (const float *)upload(ly->post_ffn_norm, H * 4);
+        o->is_sliding = ly->is_sliding;
+        if (!o->wq || !o->wk || !o->wv || !o->wo || !o->gate_up || !o->down || !o->input_norm || !o->post_attn_norm)
+            return -1;
+    }
+    smol_b200_qkn_model *m = &st->model;
+    m->hidden = c->hidden;
+    m->n_layers = c->layers;
+    m->n_heads = c->heads;
+    m->n_kv_heads = c->kv_heads;
+    m->head_dim = c->head_dim;
+    m->intermediate = c->intermediate;
+    m->vocab = c->vocab;
+    m->eps = c->eps;
+    m->rope_interleaved = c->interleaved;
+    m->tok_embeddings = (const uint16_t *)upload(tok_embeddings, (size_t)c->vocab * H * 2);
+    m->final_norm = (const float *)upload(final_norm, H * 4);
+    m->lm_head = (const uint16_t *)upload(lm_head, (size_t)c->vocab * H * 2);
+    m->layers = st->layers;
+    m->activation = c->geglu ? 1 : 0;
+    m->embed_normalizer = c->embed_normalizer;
+    m->attn_softcap = c->attn_softcap;
+    m->sliding_window = c->sliding_window;
+    st->kv_len_dev = (int *)smol_b200_device_alloc(sizeof(int));
+    st->token_dev = (int *)smol_b200_device_alloc(sizeof(int));
+    st->xn_dev = (float *)smol_b200_device_alloc(H * 4);
+    if (!m->tok_embeddings || !m->final_norm || (lm_head && !m->lm_head) || !st->kv_len_dev || !st->token_dev ||
+        !st->xn_dev)
+        return -1;
+    st->ready = 1;
+    return 0;
+}
+
+/* Pools, tables and buffers for positions [0, need) and n_in input rows; `cached`
+ * positions are kept when the pool grows (rows copied on the device). */
+static int ensure_capacity(dd_state *st, int need, int cached, int n_in)
+{
+    const dd_config *c = &st->cfg;
+    const size_t H = (size_t)c->hidden, kvd = (size_t)c->kv_heads * c->head_dim;
+    const int L = c->layers;
+    if (need > st->cap) {
+        const int64_t cap = need + 1024 > 2 * st->cap ? need + 1024 : 2 * st->cap;
+        uint16_t *k = (uint16_t *)smol_b200_device_alloc((size_t)L * cap * kvd * 2);
+        uint16_t *v = (uint16_t *)smol_b200_device_alloc((size_t)L * cap * kvd * 2);
+        if (!k || !v) {
+            smol_b200_device_free(k);
+            smol_b200_device_free(v);
+            return 0;
+        }
+        const int keep = cached < st->cap ? cached : (int)st->cap;
+        for (int l = 0; l < L && st->k_pool && keep > 0; l++) {
+            if (smol_b200_copy(k + (size_t)l * cap * kvd, st->k_pool + (size_t)l * st->cap * kvd,
+                               (size_t)keep * kvd * 2) != SMOL_B200_OK ||
+                smol_b200_copy(v + (size_t)l * cap * kvd, st->v_pool + (size_t)l * st->cap * kvd,
+                               (size_t)keep * kvd * 2) != SMOL_B200_OK)
+                return 0;
+        }
+        smol_b200_device_free(st->k_pool);
+        smol_b200_device_free(st->v_pool);
+        st->k_pool = k;
+        st->v_pool = v;
+        st->cap = cap;
+        for (int l = 0; l < L; l++) st->row0_host[l] = (int64_t)l * cap;
+        smol_b200_device_free(st->row0_dev);
+        st->row0_dev = (int64_t *)upload(st->row0_host, sizeof(int64_t) * (size_t)L);
+        smol_b200_device_free(st->step_ws);
+        st->step_ws_bytes = smol_b200_qkn_step_workspace_bytes(&st->model, 1, (int)cap - 1);
+        st->step_ws = smol_b200_device_alloc(st->step_ws_bytes);
+        if (!st->row0_dev || !st->step_ws) return 0;
+    }
+    if (need > st->rope_cap) {
+        const int rows = (int)st->cap;
+        if (!rope_tables(&st->cos, &st->sin, rows, c->head_dim, c->theta, c->interleaved)) return 0;
+        /* sliding layers' own theta (qkn_decoder.c:313-340) */
+        if (c->local_theta > 0.0f && c->local_theta != c->theta) {
+            if (!rope_tables(&st->cos_local, &st->sin_local, rows, c->head_dim, c->local_theta, c->interleaved))
+                return 0;
+            st->model.rope_cos_local = st->cos_local;
+            st->model.rope_sin_local = st->sin_local;
+        }
+        st->rope_cap = rows;
+    }
+    if (n_in > st->x_cap) {
+        smol_b200_device_free(st->x_dev);
+        st->x_dev = (float *)smol_b200_device_alloc((size_t)n_in * H * 4);
+        if (!st->x_dev) return 0;
+        st->x_cap = n_in;
+    }
+    return 1;
+}
+
+int dd_prefill(dd_state *st, const float *embeds, int n, int start)
+{
+    if (n <= 0) return 0;
+    if (!st->ready || !ensure_capacity(st, start + n + 1, start, n)) return -1;
+    if (n > st->prefill_cap) {
+        smol_b200_device_free(st->prefill_ws);
+        st->prefill_ws_bytes = smol_b200_qkn_prefill_workspace_bytes(&st->model, n);
+        st->prefill_ws = smol_b200_device_alloc(st->prefill_ws_bytes);
+        st->prefill_cap = st->prefill_ws ? n : 0;
+    }
+    if (!st->prefill_ws ||
+        smol_b200_copy(st->x_dev, embeds, (size_t)n * st->cfg.hidden * 4) != SMOL_B200_OK ||
+        smol_b200_qkn_prefill_embeds(NULL, &st->model, st->x_dev, n, start, st->k_pool, st->v_pool,
+                                     (int64_t)st->cfg.layers * st->cap, st->row0_host, st->cos, st->sin,
+                                     st->prefill_ws, st->prefill_ws_bytes) != SMOL_B200_OK)
+        return -1;
+    return 0;
+}
+
+int dd_forward(dd_state *st, const float *embed, int pos, float *x_normed)
+{
+    int token = -1;
+    const size_t H = (size_t)st->cfg.hidden;
+    if (!st->ready || !ensure_capacity(st, pos + 2, pos, 1) ||
+        smol_b200_copy(st->x_dev, embed, H * 4) != SMOL_B200_OK ||
+        smol_b200_copy(st->kv_len_dev, &pos, sizeof(int)) != SMOL_B200_OK ||
+        smol_b200_qkn_decode_step_embeds(NULL, &st->model, 1, st->x_dev, st->token_dev, st->k_pool, st->v_pool,
+                                         (int64_t)st->cfg.layers * st->cap, st->row0_dev, st->kv_len_dev,
+                                         (int)st->cap - 1, st->cos, st->sin, 0, st->step_ws, st->step_ws_bytes,
+                                         st->xn_dev) != SMOL_B200_OK ||
+        smol_b200_copy(&token, st->token_dev, sizeof(int)) != SMOL_B200_OK ||
+        (x_normed && smol_b200_copy(x_normed, st->xn_dev, H * 4) != SMOL_B200_OK))
+        return -1;
+    return token;
+}
