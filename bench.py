@@ -61,11 +61,12 @@ def parse_args():
     ap.add_argument("--no-decode", action="store_true", help="prefill measurement only (profiling helper)")
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg 1/3/4 block")
     ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4", "decoder", "audio", "siglip", "gemma",
-                                              "prefill"],
+                                              "prefill", "dropin"],
                     default=None,
                     help="run one of the other measurements alone: cfg 1/3/4, the decoder step, or (not in the "
                          "default run yet) the audio-encoder windows, the whole SigLIP encoder, the Gemma-"
-                         "configured decoder step or the device prefill")
+                         "configured decoder step, the device prefill, or the decoder-level drop-in against the "
+                         "reference decoder on the host")
     ap.add_argument("--images", type=int, default=None, help="cfg 3 image count override")
     ap.add_argument("--prefill-shape", default=None, help="B,L override of the cfg 5 prefill shape")
     return ap.parse_args()
@@ -807,6 +808,32 @@ def run_decoder_prefill(pk, n_tokens: int = 2048) -> dict:
             "frac_of_bf16_peak": round(fl / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 4)}
 
 
+def run_decoder_dropin(layers: int = 2) -> dict:
+    """The reference's decoder driver (tests/dropin/qkn_dropin_main.c: Qwen3-shaped,
+    hidden 1024, 16/8 heads, `layers` layers) through the reference's own
+    qkn_decoder_prefill / _forward on the host cores (oracle/_ref/qkn_dropin_ref) and
+    through the decoder-level drop-in on the device (oracle/_ref/qkn_dropin_device):
+    wall-clock time of the calls with host buffers in and out, and token identity."""
+    ref_dir = os.path.join(ROOT, "oracle", "_ref")
+    args = ["512", "128", "2", "4", "2", str(layers), "1"]
+    res = {}
+    for kind in ("ref", "device"):
+        exe = os.path.join(ref_dir, f"qkn_dropin_{kind}")
+        if not os.path.exists(exe):
+            return {"unavailable": f"{exe} not built"}
+        p = subprocess.run([exe, *args], capture_output=True, text=True, timeout=900)
+        if p.returncode != 0:
+            return {"error": f"{kind}: exit {p.returncode}: {p.stderr[-300:]}"}
+        t = p.stderr.split("prefill_ms")[1].split()
+        res[kind] = {"prefill_ms": float(t[0]), "forward_ms_per_step": float(t[2]), "tokens": p.stdout.split()}
+    return {"workload": f"reference decoder driver, hidden 1024, {layers} layers, prefill 511 + 128 steps",
+            "reference_cpu": {k: v for k, v in res["ref"].items() if k != "tokens"},
+            "device_dropin": {k: v for k, v in res["device"].items() if k != "tokens"},
+            "forward_speedup": round(res["ref"]["forward_ms_per_step"] / res["device"]["forward_ms_per_step"], 1),
+            "prefill_speedup": round(res["ref"]["prefill_ms"] / res["device"]["prefill_ms"], 1),
+            "tokens_equal": res["ref"]["tokens"] == res["device"]["tokens"]}
+
+
 def run_other_configs(pk) -> dict:
     """The remaining BASELINE configs on one GPU (latency- or tensor-bound; not the headline).
 
@@ -1016,7 +1043,8 @@ def main():
               "audio": lambda: run_audio_windows(pk),
               "siglip": lambda: run_siglip_encoder(pk, args.images),
               "gemma": lambda: [run_gemma_decoder(pk, 1), run_gemma_decoder(pk, 8)],
-              "prefill": lambda: run_decoder_prefill(pk)}[args.only_config]
+              "prefill": lambda: run_decoder_prefill(pk),
+              "dropin": run_decoder_dropin}[args.only_config]
         print(json.dumps({args.only_config: fn()}))
         return
     run_ours(args)

@@ -3,15 +3,19 @@
  * of tmzt/smol-genius) through qkn_decoder_prefill / qkn_decoder_forward with a seeded,
  * synthetic Qwen3-shaped model, and prints the greedy tokens.
  *
- * oracle/Makefile links this file three times:
- *   qkn_dropin_ref   -- with every reference kernel object (the baseline);
- *   qkn_dropin_b200  -- with the reference objects minus attention.o, rope.o and
- *                       rmsnorm.o, and with libsmol_b200.so in their place, exactly as
- *                       a maintainer links the exports (those three sources
- *                       filtered out of libsmol.a's list, -lsmol_b200 added);
- *   qkn_dropin_emul  -- with every reference object and smol_causal_attention wrapped
- *                       (cache_precision_wrap.c) to attend over bf16 K / fp16 V values.
- * The tests compare the token streams.  Nothing in the reference changes.
+ * oracle/Makefile links this file four times:
+ *   qkn_dropin_ref    -- with every reference kernel object (the baseline);
+ *   qkn_dropin_b200   -- with the reference objects minus attention.o, rope.o and
+ *                        rmsnorm.o, and with libsmol_b200.so in their place, exactly as
+ *                        a maintainer links the exports (those three sources
+ *                        filtered out of libsmol.a's list, -lsmol_b200 added);
+ *   qkn_dropin_device -- with qkn_decoder_prefill / qkn_decoder_forward taken from
+ *                        smol-genius_b200/dropin/qkn_decoder_device.c (the whole decoder
+ *                        on the device; qkn_decoder.c compiled with the two renamed);
+ *   qkn_dropin_emul   -- with every reference object and smol_causal_attention wrapped
+ *                        (cache_precision_wrap.c) to attend over bf16 K / fp16 V values.
+ * The tests compare the token streams; stderr also carries the wall-clock time of the
+ * prefill call and the mean of the forward calls.  Nothing in the reference changes.
  *
  * Usage: qkn_dropin_xxx [prefill_len=512] [steps=128] [seed=2] [qk_gain=4] [vo_gain=2] [layers=1] [copy=1]
  *
@@ -38,6 +42,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <time.h>
 
 #include "qkn_decoder.h"
 #include "smol_kernels.h"
@@ -223,7 +228,12 @@ int main(int argc, char **argv)
     for (int i = 0; i < prefill; i++)
         for (int k = 0; k < HIDDEN; k++)
             embeds[(size_t)i * HIDDEN + k] = from_bf16(d->tok_embeddings_bf16[(size_t)prompt[i] * HIDDEN + k]);
+    struct timespec t0, t1;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
     qkn_decoder_prefill(ctx, embeds, prefill - 1);
+    clock_gettime(CLOCK_MONOTONIC, &t1);
+    const double prefill_ms = (t1.tv_sec - t0.tv_sec) * 1e3 + (t1.tv_nsec - t0.tv_nsec) * 1e-6;
+    double forward_ms = 0.0;
 
     /* qkn_decoder_forward leaves the final-normed hidden state in ctx->dec_x
      * (qkn_decoder.c:584, :709-713), so the top-1 / top-2 logit margin of each step is
@@ -235,7 +245,10 @@ int main(int argc, char **argv)
     int min_step = -1;
     for (int s = 0; s < steps; s++) {
         for (int k = 0; k < HIDDEN; k++) x[k] = from_bf16(d->tok_embeddings_bf16[(size_t)tok * HIDDEN + k]);
+        clock_gettime(CLOCK_MONOTONIC, &t0);
         tok = qkn_decoder_forward(ctx, x);
+        clock_gettime(CLOCK_MONOTONIC, &t1);
+        forward_ms += (t1.tv_sec - t0.tv_sec) * 1e3 + (t1.tv_nsec - t0.tv_nsec) * 1e-6;
         printf("%d%c", tok, s + 1 < steps ? ' ' : '\n');
         if (tok < 0 || tok >= VOCAB) {   /* a failure sentinel (qkn_decoder.c:605-611), not a token */
             printf("\n");
@@ -253,6 +266,8 @@ int main(int argc, char **argv)
         if (top1 - top2 < min_margin) { min_margin = top1 - top2; min_step = s; }
     }
     fflush(stdout);
+    /* wall-clock time of the decoder calls themselves (host buffers in and out) */
+    fprintf(stderr, "prefill_ms %.3f forward_ms_per_step %.4f\n", prefill_ms, steps > 0 ? forward_ms / steps : 0.0);
     fprintf(stderr, "min top-2 margin %.4f at step %d\nmargins:", min_margin, min_step);
     for (int s = 0; s < steps; s++) fprintf(stderr, " %.5f", margins[s]);
     fprintf(stderr, "\n");
