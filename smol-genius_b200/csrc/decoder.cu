@@ -37,6 +37,13 @@ const int g_gemv_warps_per_sm = [] {
     const int v = e ? atoi(e) : 0;
     return v > 0 ? v : 8;
 }();
+// Cap on the CTAs of one projection per SM (SMOL_GEMV_CTAS_PER_SM, measurement knob):
+// fewer resident CTAs leave room for the next kernel of the step to start early.
+const int g_gemv_ctas_per_sm = [] {
+    const char *e = getenv("SMOL_GEMV_CTAS_PER_SM");
+    const int v = e ? atoi(e) : 0;
+    return v > 0 ? v : 16;
+}();
 
 struct GemvSeg {
     const uint16_t *w;
@@ -545,7 +552,7 @@ int launch_gemv_nb(cudaStream_t st, GemvParams &p)
     p.ksplit = S;
     const int G = kGemvWarps / S;
     long long grid = (groups + G - 1) / G;
-    if (grid > 148LL * 16) grid = 148LL * 16;
+    if (grid > 148LL * g_gemv_ctas_per_sm) grid = 148LL * g_gemv_ctas_per_sm;
     return launch_kernel(gemv_bf16_kernel<NB, R>, dim3(static_cast<unsigned>(grid)), dim3(kGemvThreads), smem, st,
                          p) == cudaSuccess
                ? SMOL_B200_OK
