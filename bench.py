@@ -244,6 +244,49 @@ def cpu_reference_decode(lens: np.ndarray, seconds: float) -> dict:
     return ref.run(seconds)
 
 
+def cpu_reference_prefill() -> dict:
+    """The compiled reference (oracle/_ref) on the host cores for the tensor-bound configs,
+    one bounded sample each, reported as GFLOP/s of visible pairs (4 * hd FLOPs per pair
+    and head) so it scales to the full workloads:
+      cfg 3: smol_bidirectional_attention (single-threaded in the reference) on one image
+             and one layer (1024 patches, 12 heads, hd 64, window {0, 1024});
+      cfg 5: smol_causal_attention on one sequence of 4096 tokens, 16 / 8 heads, hd 128
+             (the full 32768-token layer is 64x the pairs)."""
+    import ctypes
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle
+    path = pyoracle.ref_path()
+    if path is None:
+        return {"unavailable": "compiled reference (oracle/_ref) not present"}
+    lib = ctypes.CDLL(path)
+    lib.smol_set_threads(ctypes.c_int(min(os.cpu_count() or 1, 16)))
+    threads = int(lib.smol_get_thread_count())
+    rng = np.random.default_rng(11)
+    p = lambda a: ctypes.c_void_p(a.ctypes.data)   # noqa: E731
+    out = {}
+    N, h, hd = 1024, 12, 64
+    q, k, v = (rng.standard_normal((N, h * hd), dtype=np.float32) for _ in range(3))
+    o = np.zeros_like(q)
+    ws = np.array([0, N], np.int32)
+    t0 = time.perf_counter()
+    lib.smol_bidirectional_attention(p(o), p(q), p(k), p(v), ctypes.c_int(N), ctypes.c_int(h), ctypes.c_int(hd),
+                                     ctypes.c_float(0.125), p(ws), ctypes.c_int(1))
+    t = time.perf_counter() - t0
+    out["cfg3"] = {"gflops": round(workload.full_flops(N, h, hd) / t / 1e9, 2), "cores": 1,
+                   "sample": "smol_bidirectional_attention, 1 image x 1 layer (1024 patches, 12 heads, hd 64)"}
+    L, hq, hkv, hd = 4096, 16, 8, 128
+    q = rng.standard_normal((L, hq * hd), dtype=np.float32)
+    k, v = (rng.standard_normal((L, hkv * hd), dtype=np.float32) for _ in range(2))
+    o = np.zeros_like(q)
+    t0 = time.perf_counter()
+    lib.smol_causal_attention(p(o), p(q), p(k), p(v), ctypes.c_int(L), ctypes.c_int(L), ctypes.c_int(hq),
+                              ctypes.c_int(hkv), ctypes.c_int(hd), ctypes.c_float(1 / np.sqrt(hd)), ctypes.c_int(0))
+    t = time.perf_counter() - t0
+    out["cfg5"] = {"gflops": round(workload.causal_flops_square(L, hq, hd) / t / 1e9, 2), "cores": threads,
+                   "sample": "smol_causal_attention, 1 sequence of 4096 tokens, 16/8 heads, hd 128 (causal)"}
+    return out
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -998,6 +1041,11 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_reference_decode(lens, args.cpu_seconds)
+        if prefill is not None or others is not None:   # the tensor-bound configs' CPU reference too
+            try:
+                cpu["other_configs"] = cpu_reference_prefill()
+            except Exception as e:   # a missing or failing reference must not cost the headline
+                cpu["other_configs"] = {"error": str(e)[:200]}
 
     if rank != 0:
         return
