@@ -46,6 +46,34 @@ static int rope_tables(float **cos_d, float **sin_d, int rows, int head_dim, flo
     return ok;
 }
 
+void dd_release(dd_state *st)
+{
+    for (int l = 0; l < DD_MAX_LAYERS; l++) {
+        smol_b200_qkn_layer *o = &st->layers[l];
+        const void *bufs[] = {o->wq, o->wk, o->wv, o->wo, o->gate_up, o->down, o->input_norm, o->post_attn_norm,
+                              o->q_norm, o->k_norm, o->pre_ffn_norm, o->post_ffn_norm};
+        for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++) smol_b200_device_free((void *)bufs[i]);
+    }
+    const void *bufs[] = {st->model.tok_embeddings, st->model.final_norm, st->model.lm_head, st->k_pool, st->v_pool,
+                          st->row0_dev, st->cos, st->sin, st->cos_local, st->sin_local, st->kv_len_dev,
+                          st->token_dev, st->x_dev, st->xn_dev, st->step_ws, st->prefill_ws};
+    for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++) smol_b200_device_free((void *)bufs[i]);
+    memset(st, 0, sizeof(*st));
+}
+
+uint64_t dd_fingerprint(const dd_config *c, const uint16_t *tok_embeddings, const uint16_t *wq0)
+{
+    uint64_t h = 1469598103934665603ull;   /* FNV-1a over the addresses, the shape and a few values */
+    const uint64_t words[] = {(uint64_t)(uintptr_t)tok_embeddings, (uint64_t)(uintptr_t)wq0, (uint64_t)c->hidden,
+                              (uint64_t)c->layers, (uint64_t)c->vocab};
+    for (size_t i = 0; i < sizeof(words) / sizeof(words[0]); i++) h = (h ^ words[i]) * 1099511628211ull;
+    for (int i = 0; i < 32 && tok_embeddings && wq0; i++) {
+        h = (h ^ tok_embeddings[i]) * 1099511628211ull;
+        h = (h ^ wq0[i]) * 1099511628211ull;
+    }
+    return h;
+}
+
 int dd_setup(dd_state *st, const dd_config *c, const dd_layer *layers, const uint16_t *tok_embeddings,
              const float *final_norm, const uint16_t *lm_head)
 {
@@ -70,8 +98,10 @@ int dd_setup(dd_state *st, const dd_config *c, const dd_layer *layers, const uin
         o->pre_ffn_norm = (const float *)upload(ly->pre_ffn_norm, H * 4);
         o->post_ffn_norm = (const float *)upload(ly->post_ffn_norm, H * 4);
         o->is_sliding = ly->is_sliding;
-        if (!o->wq || !o->wk || !o->wv || !o->wo || !o->gate_up || !o->down || !o->input_norm || !o->post_attn_norm)
+        if (!o->wq || !o->wk || !o->wv || !o->wo || !o->gate_up || !o->down || !o->input_norm || !o->post_attn_norm) {
+            dd_release(st);
             return -1;
+        }
     }
     smol_b200_qkn_model *m = &st->model;
     m->hidden = c->hidden;
@@ -95,8 +125,10 @@ int dd_setup(dd_state *st, const dd_config *c, const dd_layer *layers, const uin
     st->token_dev = (int *)smol_b200_device_alloc(sizeof(int));
     st->xn_dev = (float *)smol_b200_device_alloc(H * 4);
     if (!m->tok_embeddings || !m->final_norm || (lm_head && !m->lm_head) || !st->kv_len_dev || !st->token_dev ||
-        !st->xn_dev)
+        !st->xn_dev) {
+        dd_release(st);
         return -1;
+    }
     st->ready = 1;
     return 0;
 }

@@ -55,6 +55,13 @@ typedef struct {
 int dd_setup(dd_state *st, const dd_config *cfg, const dd_layer *layers, const uint16_t *tok_embeddings,
              const float *final_norm, const uint16_t *lm_head);
 
+/* Frees every device buffer of a state (set up or partly set up). */
+void dd_release(dd_state *st);
+
+/* A fingerprint of a decoder's host weights (their addresses and a few values): a context
+ * freed and allocated again at the same address is recognised as a different model. */
+uint64_t dd_fingerprint(const dd_config *cfg, const uint16_t *tok_embeddings, const uint16_t *wq0);
+
 /* Prefill n host embeddings at positions start.. (the positions before `start` are
  * kept when the pool grows).  0 on success. */
 int dd_prefill(dd_state *st, const float *embeds, int n, int start);

@@ -25,6 +25,7 @@
  * -Dqkn_decoder_forward=qkn_decoder_forward_host, add this file and device_decoder.c,
  * and -lsmol_b200.
  */
+#include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -37,17 +38,30 @@
 
 static struct {
     const qkn_ctx_t *ctx;
+    uint64_t fingerprint;   /* of the weights it was set up from */
     dd_state st;
 } g_slots[MAX_CONTEXTS];
 
 static dd_state *state_for(qkn_ctx_t *ctx)
 {
+    if (ctx->config.dec_layers < 1 || ctx->config.dec_layers > DD_MAX_LAYERS) return NULL;
+    dd_config probe;
+    memset(&probe, 0, sizeof(probe));
+    probe.hidden = ctx->config.dec_hidden;
+    probe.layers = ctx->config.dec_layers;
+    probe.vocab = ctx->config.vocab_size;
+    const uint64_t fp = dd_fingerprint(&probe, ctx->decoder.tok_embeddings_bf16, ctx->decoder.layers[0].wq_weight_bf16);
     int free_slot = -1;
     for (int i = 0; i < MAX_CONTEXTS; i++) {
-        if (g_slots[i].ctx == ctx) return &g_slots[i].st;
+        if (g_slots[i].ctx == ctx) {
+            if (g_slots[i].fingerprint == fp) return &g_slots[i].st;
+            /* the same address now holds another model: start over */
+            dd_release(&g_slots[i].st);
+            g_slots[i].ctx = NULL;
+        }
         if (!g_slots[i].ctx && free_slot < 0) free_slot = i;
     }
-    if (free_slot < 0 || ctx->config.dec_layers > DD_MAX_LAYERS) return NULL;
+    if (free_slot < 0) return NULL;
     const qkn_config_t *c = &ctx->config;
     const qkn_decoder_t *d = &ctx->decoder;
     dd_config cfg;
@@ -77,6 +91,7 @@ static dd_state *state_for(qkn_ctx_t *ctx)
     }
     if (dd_setup(&g_slots[free_slot].st, &cfg, layers, d->tok_embeddings_bf16, d->norm, NULL) != 0) return NULL;
     g_slots[free_slot].ctx = ctx;
+    g_slots[free_slot].fingerprint = fp;
     return &g_slots[free_slot].st;
 }
 
