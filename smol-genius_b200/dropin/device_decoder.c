@@ -144,18 +144,19 @@ static int ensure_capacity(dd_state *st, int need, int cached, int n_in)
         const int64_t cap = need + 1024 > 2 * st->cap ? need + 1024 : 2 * st->cap;
         uint16_t *k = (uint16_t *)smol_b200_device_alloc((size_t)L * cap * kvd * 2);
         uint16_t *v = (uint16_t *)smol_b200_device_alloc((size_t)L * cap * kvd * 2);
-        if (!k || !v) {
-            smol_b200_device_free(k);
-            smol_b200_device_free(v);
-            return 0;
-        }
         const int keep = cached < st->cap ? cached : (int)st->cap;
-        for (int l = 0; l < L && st->k_pool && keep > 0; l++) {
+        int ok = k && v;
+        for (int l = 0; l < L && ok && st->k_pool && keep > 0; l++) {
             if (smol_b200_copy(k + (size_t)l * cap * kvd, st->k_pool + (size_t)l * st->cap * kvd,
                                (size_t)keep * kvd * 2) != SMOL_B200_OK ||
                 smol_b200_copy(v + (size_t)l * cap * kvd, st->v_pool + (size_t)l * st->cap * kvd,
                                (size_t)keep * kvd * 2) != SMOL_B200_OK)
-                return 0;
+                ok = 0;
+        }
+        if (!ok) {   /* the old pools stay as they were */
+            smol_b200_device_free(k);
+            smol_b200_device_free(v);
+            return 0;
         }
         smol_b200_device_free(st->k_pool);
         smol_b200_device_free(st->v_pool);
@@ -191,10 +192,18 @@ static int ensure_capacity(dd_state *st, int need, int cached, int n_in)
     return 1;
 }
 
+/* Positions past the ones written would be attended as uninitialised rows. */
+static int position_held(const dd_state *st, int pos)
+{
+    if (pos >= 0 && pos <= st->held) return 1;
+    fprintf(stderr, "device decoder: position %d is past the %d positions held on the device\n", pos, st->held);
+    return 0;
+}
+
 int dd_prefill(dd_state *st, const float *embeds, int n, int start)
 {
     if (n <= 0) return 0;
-    if (!st->ready || !ensure_capacity(st, start + n + 1, start, n)) return -1;
+    if (!st->ready || !position_held(st, start) || !ensure_capacity(st, start + n + 1, start, n)) return -1;
     if (n > st->prefill_cap) {
         smol_b200_device_free(st->prefill_ws);
         st->prefill_ws_bytes = smol_b200_qkn_prefill_workspace_bytes(&st->model, n);
@@ -207,6 +216,7 @@ int dd_prefill(dd_state *st, const float *embeds, int n, int start)
                                      (int64_t)st->cfg.layers * st->cap, st->row0_host, st->cos, st->sin,
                                      st->prefill_ws, st->prefill_ws_bytes) != SMOL_B200_OK)
         return -1;
+    st->held = start + n;
     return 0;
 }
 
@@ -214,7 +224,7 @@ int dd_forward(dd_state *st, const float *embed, int pos, float *x_normed)
 {
     int token = -1;
     const size_t H = (size_t)st->cfg.hidden;
-    if (!st->ready || !ensure_capacity(st, pos + 2, pos, 1) ||
+    if (!st->ready || !position_held(st, pos) || !ensure_capacity(st, pos + 2, pos, 1) ||
         smol_b200_copy(st->x_dev, embed, H * 4) != SMOL_B200_OK ||
         smol_b200_copy(st->kv_len_dev, &pos, sizeof(int)) != SMOL_B200_OK ||
         smol_b200_qkn_decode_step_embeds(NULL, &st->model, 1, st->x_dev, st->token_dev, st->k_pool, st->v_pool,
@@ -224,5 +234,6 @@ int dd_forward(dd_state *st, const float *embed, int pos, float *x_normed)
         smol_b200_copy(&token, st->token_dev, sizeof(int)) != SMOL_B200_OK ||
         (x_normed && smol_b200_copy(x_normed, st->xn_dev, H * 4) != SMOL_B200_OK))
         return -1;
+    st->held = pos + 1;
     return token;
 }

@@ -38,6 +38,7 @@ typedef struct {
     smol_b200_qkn_layer layers[DD_MAX_LAYERS];
     smol_b200_qkn_model model;
     int64_t cap;                        /* positions per layer in the pools */
+    int held;                           /* positions [0, held) hold written K / V rows */
     uint16_t *k_pool, *v_pool;
     int64_t row0_host[DD_MAX_LAYERS];
     int64_t *row0_dev;
@@ -63,11 +64,13 @@ void dd_release(dd_state *st);
 uint64_t dd_fingerprint(const dd_config *cfg, const uint16_t *tok_embeddings, const uint16_t *wq0);
 
 /* Prefill n host embeddings at positions start.. (the positions before `start` are
- * kept when the pool grows).  0 on success. */
+ * kept when the pool grows).  0 on success; -1 also when start is past the positions
+ * the device holds (their rows were never written). */
 int dd_prefill(dd_state *st, const float *embeds, int n, int start);
 
-/* One decode step at position pos (= cached positions): returns the greedy token and
- * writes the final normalised state to x_normed (host, may be NULL), or -1. */
+/* One decode step at position pos (= cached positions, at most the positions held):
+ * returns the greedy token and writes the final normalised state to x_normed (host,
+ * may be NULL), or -1. */
 int dd_forward(dd_state *st, const float *embed, int pos, float *x_normed);
 
 #endif /* SMOL_B200_DEVICE_DECODER_H */

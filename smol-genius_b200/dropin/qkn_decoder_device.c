@@ -118,3 +118,20 @@ int qkn_decoder_forward(qkn_ctx_t *ctx, const float *input_embed)
     ctx->kv_cache_len += 1;
     return token;
 }
+
+/* Frees the device weights, cache and workspaces held for ctx (a no-op for a context
+ * never passed here) and sets ctx->kv_cache_len to 0: the cached positions are gone.
+ * The reference has no call that frees a context (exports free its fields directly),
+ * so device memory otherwise stays until the process exits; a context freed and
+ * allocated again at the same address with other weights is recognised by the
+ * fingerprint and set up afresh. */
+void qkn_decoder_device_release(qkn_ctx_t *ctx)
+{
+    for (int i = 0; i < MAX_CONTEXTS; i++) {
+        if (g_slots[i].ctx != ctx) continue;
+        dd_release(&g_slots[i].st);
+        g_slots[i].ctx = NULL;
+        g_slots[i].fingerprint = 0;
+        ctx->kv_cache_len = 0;
+    }
+}

@@ -11,7 +11,9 @@
  *                        filtered out of libsmol.a's list, -lsmol_b200 added);
  *   qkn_dropin_device -- with qkn_decoder_prefill / qkn_decoder_forward taken from
  *                        smol-genius_b200/dropin/qkn_decoder_device.c (the whole decoder
- *                        on the device; qkn_decoder.c compiled with the two renamed);
+ *                        on the device; qkn_decoder.c compiled with the two renamed;
+ *                        SMOL_DROPIN_DEVICE defined: SMOL_DROPIN_RERUN=1 in the
+ *                        environment also checks qkn_decoder_device_release);
  *   qkn_dropin_emul   -- with every reference object and smol_causal_attention wrapped
  *                        (cache_precision_wrap.c) to attend over bf16 K / fp16 V values.
  * The tests compare the token streams; stderr also carries the wall-clock time of the
@@ -156,6 +158,69 @@ static void copy_readout(qkn_dec_layer_t *l, double gain)
     }
 }
 
+#ifdef SMOL_DROPIN_DEVICE
+/* smol-genius_b200/dropin/qkn_decoder_device.c */
+void qkn_decoder_device_release(qkn_ctx_t *ctx);
+#endif
+
+/* Prefill all but the last prompt token (as the exports do, e.g. qwen_asr.c:695-703),
+ * then decode `steps` tokens from the last one, printing them on one stdout line.
+ * With `report`, stderr gets the call times and the top-1 / top-2 logit margins.
+ * Returns 3 when a forward call returns a failure sentinel instead of a token. */
+static int generate(qkn_ctx_t *ctx, const int *prompt, const float *embeds, int prefill, int steps, int report)
+{
+    const qkn_decoder_t *d = &ctx->decoder;
+    struct timespec t0, t1;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
+    qkn_decoder_prefill(ctx, embeds, prefill - 1);
+    clock_gettime(CLOCK_MONOTONIC, &t1);
+    const double prefill_ms = (t1.tv_sec - t0.tv_sec) * 1e3 + (t1.tv_nsec - t0.tv_nsec) * 1e-6;
+    double forward_ms = 0.0;
+
+    /* qkn_decoder_forward leaves the final-normed hidden state in ctx->dec_x
+     * (qkn_decoder.c:584, :709-713), so the top-1 / top-2 logit margin of each step is
+     * recomputed from it here and the smallest one printed on stderr. */
+    float *x = (float *)malloc(sizeof(float) * HIDDEN);
+    int tok = prompt[prefill - 1];
+    double min_margin = INFINITY;
+    double *margins = (double *)malloc(sizeof(double) * (size_t)(steps > 0 ? steps : 1));
+    int min_step = -1;
+    for (int s = 0; s < steps; s++) {
+        for (int k = 0; k < HIDDEN; k++) x[k] = from_bf16(d->tok_embeddings_bf16[(size_t)tok * HIDDEN + k]);
+        clock_gettime(CLOCK_MONOTONIC, &t0);
+        tok = qkn_decoder_forward(ctx, x);
+        clock_gettime(CLOCK_MONOTONIC, &t1);
+        forward_ms += (t1.tv_sec - t0.tv_sec) * 1e3 + (t1.tv_nsec - t0.tv_nsec) * 1e-6;
+        printf("%d%c", tok, s + 1 < steps ? ' ' : '\n');
+        if (tok < 0 || tok >= VOCAB) {   /* a failure sentinel (qkn_decoder.c:605-611), not a token */
+            printf("\n");
+            fprintf(stderr, "forward returned %d at step %d\n", tok, s);
+            return 3;
+        }
+        double top1 = -INFINITY, top2 = -INFINITY;
+        for (int v = 0; v < VOCAB; v++) {
+            double dot = 0.0;
+            for (int k = 0; k < HIDDEN; k++)
+                dot += (double)from_bf16(d->tok_embeddings_bf16[(size_t)v * HIDDEN + k]) * ctx->dec_x[k];
+            if (dot > top1) { top2 = top1; top1 = dot; } else if (dot > top2) top2 = dot;
+        }
+        margins[s] = top1 - top2;
+        if (top1 - top2 < min_margin) { min_margin = top1 - top2; min_step = s; }
+    }
+    fflush(stdout);
+    if (report) {
+        /* wall-clock time of the decoder calls themselves (host buffers in and out) */
+        fprintf(stderr, "prefill_ms %.3f forward_ms_per_step %.4f\n", prefill_ms,
+                steps > 0 ? forward_ms / steps : 0.0);
+        fprintf(stderr, "min top-2 margin %.4f at step %d\nmargins:", min_margin, min_step);
+        for (int s = 0; s < steps; s++) fprintf(stderr, " %.5f", margins[s]);
+        fprintf(stderr, "\n");
+    }
+    free(x);
+    free(margins);
+    return 0;
+}
+
 int main(int argc, char **argv)
 {
     int prefill = argc > 1 ? atoi(argv[1]) : 512;
@@ -228,48 +293,22 @@ int main(int argc, char **argv)
     for (int i = 0; i < prefill; i++)
         for (int k = 0; k < HIDDEN; k++)
             embeds[(size_t)i * HIDDEN + k] = from_bf16(d->tok_embeddings_bf16[(size_t)prompt[i] * HIDDEN + k]);
-    struct timespec t0, t1;
-    clock_gettime(CLOCK_MONOTONIC, &t0);
-    qkn_decoder_prefill(ctx, embeds, prefill - 1);
-    clock_gettime(CLOCK_MONOTONIC, &t1);
-    const double prefill_ms = (t1.tv_sec - t0.tv_sec) * 1e3 + (t1.tv_nsec - t0.tv_nsec) * 1e-6;
-    double forward_ms = 0.0;
-
-    /* qkn_decoder_forward leaves the final-normed hidden state in ctx->dec_x
-     * (qkn_decoder.c:584, :709-713), so the top-1 / top-2 logit margin of each step is
-     * recomputed from it here and the smallest one printed on stderr. */
-    float *x = (float *)malloc(sizeof(float) * HIDDEN);
-    int tok = prompt[prefill - 1];
-    double min_margin = INFINITY;
-    double *margins = (double *)malloc(sizeof(double) * (size_t)(steps > 0 ? steps : 1));
-    int min_step = -1;
-    for (int s = 0; s < steps; s++) {
-        for (int k = 0; k < HIDDEN; k++) x[k] = from_bf16(d->tok_embeddings_bf16[(size_t)tok * HIDDEN + k]);
-        clock_gettime(CLOCK_MONOTONIC, &t0);
-        tok = qkn_decoder_forward(ctx, x);
-        clock_gettime(CLOCK_MONOTONIC, &t1);
-        forward_ms += (t1.tv_sec - t0.tv_sec) * 1e3 + (t1.tv_nsec - t0.tv_nsec) * 1e-6;
-        printf("%d%c", tok, s + 1 < steps ? ' ' : '\n');
-        if (tok < 0 || tok >= VOCAB) {   /* a failure sentinel (qkn_decoder.c:605-611), not a token */
-            printf("\n");
-            fprintf(stderr, "forward returned %d at step %d\n", tok, s);
-            return 3;
+    int rc = generate(ctx, prompt, embeds, prefill, steps, 1);
+#ifdef SMOL_DROPIN_DEVICE
+    /* SMOL_DROPIN_RERUN=1: release the device state, run the same prompt again on the
+     * same context (a second line of tokens), then ask for a position past the ones the
+     * device holds, which must come back as the failure sentinel. */
+    const char *rerun = getenv("SMOL_DROPIN_RERUN");
+    if (rc == 0 && rerun && atoi(rerun)) {
+        qkn_decoder_device_release(ctx);
+        if (ctx->kv_cache_len != 0) return 4;
+        rc = generate(ctx, prompt, embeds, prefill, steps, 0);
+        if (rc == 0) {
+            for (int k = 0; k < HIDDEN; k++) embeds[k] = from_bf16(d->tok_embeddings_bf16[k]);
+            ctx->kv_cache_len += 5;
+            fprintf(stderr, "past_held_token %d\n", qkn_decoder_forward(ctx, embeds));
         }
-        double top1 = -INFINITY, top2 = -INFINITY;
-        for (int v = 0; v < VOCAB; v++) {
-            double dot = 0.0;
-            for (int k = 0; k < HIDDEN; k++)
-                dot += (double)from_bf16(d->tok_embeddings_bf16[(size_t)v * HIDDEN + k]) * ctx->dec_x[k];
-            if (dot > top1) { top2 = top1; top1 = dot; } else if (dot > top2) top2 = dot;
-        }
-        margins[s] = top1 - top2;
-        if (top1 - top2 < min_margin) { min_margin = top1 - top2; min_step = s; }
     }
-    fflush(stdout);
-    /* wall-clock time of the decoder calls themselves (host buffers in and out) */
-    fprintf(stderr, "prefill_ms %.3f forward_ms_per_step %.4f\n", prefill_ms, steps > 0 ? forward_ms / steps : 0.0);
-    fprintf(stderr, "min top-2 margin %.4f at step %d\nmargins:", min_margin, min_step);
-    for (int s = 0; s < steps; s++) fprintf(stderr, " %.5f", margins[s]);
-    fprintf(stderr, "\n");
-    return 0;
+#endif
+    return rc;
 }

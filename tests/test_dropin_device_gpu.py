@@ -37,6 +37,25 @@ def test_device_decoder_tokens_equal_unmodified_reference(cuda):
     assert d is None, f"diverged at step {d}: {out['ref'][d:d + 4]} vs {out['device'][d:d + 4]}"
 
 
+@pytest.mark.skipif(not all(os.path.exists(b) for b in BIN.values()),
+                    reason="drop-in binaries not built (reference checkout absent at build time)")
+def test_device_decoder_release_and_position_guard(cuda):
+    """qkn_decoder_device_release frees the context's device state and zeroes
+    kv_cache_len; the same context then runs the same prompt again from scratch (weights
+    uploaded again) with the same tokens.  A kv_cache_len past the positions the device
+    holds returns the failure sentinel 151645 instead of attending unwritten rows."""
+    args = list(map(str, (DECISIVE[0], 32) + DECISIVE[2:]))   # the decisive stream's first 32 steps
+    ref = subprocess.run([BIN["ref"], *args], capture_output=True, text=True, timeout=600, check=True)
+    p = subprocess.run([BIN["device"], *args], capture_output=True, text=True, timeout=600,
+                       env={**os.environ, "SMOL_DROPIN_RERUN": "1"})
+    assert p.returncode == 0, p.stderr
+    lines = [[int(t) for t in ln.split()] for ln in p.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 2 and len(lines[0]) == 32, p.stdout
+    assert lines[0] == lines[1] == [int(t) for t in ref.stdout.split()]
+    assert "past_held_token 151645" in p.stderr, p.stderr
+    assert "past the" in p.stderr
+
+
 @pytest.mark.skipif(not os.path.exists(SMOLVLM_BIN), reason="smolvlm_weights_device not built")
 def test_smolvlm_device_decoder_matches_oracle(cuda, tmp_path):
     """SmolVLM's decoder-level drop-in (smol-genius_b200/dropin/smolvlm_decoder_device.c)
