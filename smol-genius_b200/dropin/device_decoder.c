@@ -7,8 +7,6 @@
 #include <stdlib.h>
 #include <string.h>
 
-#include "smol_kernels.h"
-
 static void *upload(const void *host, size_t bytes)
 {
     if (!host) return NULL;
@@ -61,17 +59,64 @@ void dd_release(dd_state *st)
     memset(st, 0, sizeof(*st));
 }
 
-uint64_t dd_fingerprint(const dd_config *c, const uint16_t *tok_embeddings, const uint16_t *wq0)
+uint64_t dd_fingerprint(int hidden, int layers, int vocab, const uint16_t *tok_embeddings, const uint16_t *wq0)
 {
     uint64_t h = 1469598103934665603ull;   /* FNV-1a over the addresses, the shape and a few values */
-    const uint64_t words[] = {(uint64_t)(uintptr_t)tok_embeddings, (uint64_t)(uintptr_t)wq0, (uint64_t)c->hidden,
-                              (uint64_t)c->layers, (uint64_t)c->vocab};
+    const uint64_t words[] = {(uint64_t)(uintptr_t)tok_embeddings, (uint64_t)(uintptr_t)wq0, (uint64_t)hidden,
+                              (uint64_t)layers, (uint64_t)vocab};
     for (size_t i = 0; i < sizeof(words) / sizeof(words[0]); i++) h = (h ^ words[i]) * 1099511628211ull;
     for (int i = 0; i < 32 && tok_embeddings && wq0; i++) {
         h = (h ^ tok_embeddings[i]) * 1099511628211ull;
         h = (h ^ wq0[i]) * 1099511628211ull;
     }
     return h;
+}
+
+static struct {
+    const void *ctx;
+    uint64_t fingerprint;
+    dd_state st;
+} g_slots[DD_MAX_CONTEXTS];
+
+dd_state *dd_slot_find(const void *ctx, uint64_t fingerprint, int *ready)
+{
+    int free_slot = -1;
+    *ready = 0;
+    for (int i = 0; i < DD_MAX_CONTEXTS; i++) {
+        if (g_slots[i].ctx == ctx) {
+            if (g_slots[i].fingerprint == fingerprint) {
+                *ready = 1;
+                return &g_slots[i].st;
+            }
+            /* the same address now holds another model: start over */
+            dd_release(&g_slots[i].st);
+            g_slots[i].ctx = NULL;
+        }
+        if (!g_slots[i].ctx && free_slot < 0) free_slot = i;
+    }
+    return free_slot < 0 ? NULL : &g_slots[free_slot].st;
+}
+
+void dd_slot_claim(dd_state *st, const void *ctx, uint64_t fingerprint)
+{
+    for (int i = 0; i < DD_MAX_CONTEXTS; i++) {
+        if (&g_slots[i].st != st) continue;
+        g_slots[i].ctx = ctx;
+        g_slots[i].fingerprint = fingerprint;
+    }
+}
+
+int dd_slot_release(const void *ctx)
+{
+    int found = 0;
+    for (int i = 0; i < DD_MAX_CONTEXTS; i++) {
+        if (!ctx || g_slots[i].ctx != ctx) continue;
+        dd_release(&g_slots[i].st);
+        g_slots[i].ctx = NULL;
+        g_slots[i].fingerprint = 0;
+        found = 1;
+    }
+    return found;
 }
 
 int dd_setup(dd_state *st, const dd_config *c, const dd_layer *layers, const uint16_t *tok_embeddings,
@@ -98,7 +143,10 @@ int dd_setup(dd_state *st, const dd_config *c, const dd_layer *layers, const uin
         o->pre_ffn_norm = (const float *)upload(ly->pre_ffn_norm, H * 4);
         o->post_ffn_norm = (const float *)upload(ly->post_ffn_norm, H * 4);
         o->is_sliding = ly->is_sliding;
-        if (!o->wq || !o->wk || !o->wv || !o->wo || !o->gate_up || !o->down || !o->input_norm || !o->post_attn_norm) {
+        /* the optional norms are absent only when the host has none (a failed upload is a failure) */
+        if (!o->wq || !o->wk || !o->wv || !o->wo || !o->gate_up || !o->down || !o->input_norm || !o->post_attn_norm ||
+            (ly->q_norm && !o->q_norm) || (ly->k_norm && !o->k_norm) || (ly->pre_ffn_norm && !o->pre_ffn_norm) ||
+            (ly->post_ffn_norm && !o->post_ffn_norm)) {
             dd_release(st);
             return -1;
         }
@@ -164,12 +212,21 @@ static int ensure_capacity(dd_state *st, int need, int cached, int n_in)
         st->v_pool = v;
         st->cap = cap;
         for (int l = 0; l < L; l++) st->row0_host[l] = (int64_t)l * cap;
+        /* both depend on the capacity: made again below */
         smol_b200_device_free(st->row0_dev);
-        st->row0_dev = (int64_t *)upload(st->row0_host, sizeof(int64_t) * (size_t)L);
+        st->row0_dev = NULL;
         smol_b200_device_free(st->step_ws);
-        st->step_ws_bytes = smol_b200_qkn_step_workspace_bytes(&st->model, 1, (int)cap - 1);
+        st->step_ws = NULL;
+    }
+    /* (also retried here after a failed allocation of an earlier call) */
+    if (!st->row0_dev) {
+        st->row0_dev = (int64_t *)upload(st->row0_host, sizeof(int64_t) * (size_t)L);
+        if (!st->row0_dev) return 0;
+    }
+    if (!st->step_ws) {
+        st->step_ws_bytes = smol_b200_qkn_step_workspace_bytes(&st->model, 1, (int)st->cap - 1);
         st->step_ws = smol_b200_device_alloc(st->step_ws_bytes);
-        if (!st->row0_dev || !st->step_ws) return 0;
+        if (!st->step_ws) return 0;
     }
     if (need > st->rope_cap) {
         const int rows = (int)st->cap;
@@ -183,11 +240,12 @@ static int ensure_capacity(dd_state *st, int need, int cached, int n_in)
         }
         st->rope_cap = rows;
     }
-    if (n_in > st->x_cap) {
+    if (n_in > st->x_cap || !st->x_dev) {
+        const int rows = n_in > st->x_cap ? n_in : st->x_cap;
         smol_b200_device_free(st->x_dev);
-        st->x_dev = (float *)smol_b200_device_alloc((size_t)n_in * H * 4);
+        st->x_dev = (float *)smol_b200_device_alloc((size_t)rows * H * 4);
+        st->x_cap = st->x_dev ? rows : 0;
         if (!st->x_dev) return 0;
-        st->x_cap = n_in;
     }
     return 1;
 }

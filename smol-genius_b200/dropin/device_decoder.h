@@ -59,9 +59,25 @@ int dd_setup(dd_state *st, const dd_config *cfg, const dd_layer *layers, const u
 /* Frees every device buffer of a state (set up or partly set up). */
 void dd_release(dd_state *st);
 
-/* A fingerprint of a decoder's host weights (their addresses and a few values): a context
- * freed and allocated again at the same address is recognised as a different model. */
-uint64_t dd_fingerprint(const dd_config *cfg, const uint16_t *tok_embeddings, const uint16_t *wq0);
+/* The side table of device states the drop-ins keep for the reference's contexts (up
+ * to DD_MAX_CONTEXTS), keyed by the context's address and a fingerprint of its weights
+ * (their host addresses, the shape and a few values), so that a context freed and
+ * allocated again at the same address with another model is set up afresh. */
+#define DD_MAX_CONTEXTS 8
+
+/* The fingerprint of a decoder's host weights. */
+uint64_t dd_fingerprint(int hidden, int layers, int vocab, const uint16_t *tok_embeddings, const uint16_t *wq0);
+
+/* The state of ctx when it was set up from weights with this fingerprint (*ready = 1);
+ * otherwise a free slot for dd_setup (*ready = 0; a state ctx held for other weights is
+ * released first), or NULL when every slot is taken. */
+dd_state *dd_slot_find(const void *ctx, uint64_t fingerprint, int *ready);
+
+/* Records that st (from dd_slot_find) now holds ctx's weights. */
+void dd_slot_claim(dd_state *st, const void *ctx, uint64_t fingerprint);
+
+/* Releases the state held for ctx, if any; returns 1 when there was one. */
+int dd_slot_release(const void *ctx);
 
 /* Prefill n host embeddings at positions start.. (the positions before `start` are
  * kept when the pool grows).  0 on success; -1 also when start is past the positions

@@ -34,34 +34,15 @@
 #include "qkn_decoder.h"
 
 #define DEVICE_TOKEN_ON_ERROR 151645   /* SMOL_TOKEN_IM_END, qkn_decoder.c:20 */
-#define MAX_CONTEXTS 8
-
-static struct {
-    const qkn_ctx_t *ctx;
-    uint64_t fingerprint;   /* of the weights it was set up from */
-    dd_state st;
-} g_slots[MAX_CONTEXTS];
 
 static dd_state *state_for(qkn_ctx_t *ctx)
 {
     if (ctx->config.dec_layers < 1 || ctx->config.dec_layers > DD_MAX_LAYERS) return NULL;
-    dd_config probe;
-    memset(&probe, 0, sizeof(probe));
-    probe.hidden = ctx->config.dec_hidden;
-    probe.layers = ctx->config.dec_layers;
-    probe.vocab = ctx->config.vocab_size;
-    const uint64_t fp = dd_fingerprint(&probe, ctx->decoder.tok_embeddings_bf16, ctx->decoder.layers[0].wq_weight_bf16);
-    int free_slot = -1;
-    for (int i = 0; i < MAX_CONTEXTS; i++) {
-        if (g_slots[i].ctx == ctx) {
-            if (g_slots[i].fingerprint == fp) return &g_slots[i].st;
-            /* the same address now holds another model: start over */
-            dd_release(&g_slots[i].st);
-            g_slots[i].ctx = NULL;
-        }
-        if (!g_slots[i].ctx && free_slot < 0) free_slot = i;
-    }
-    if (free_slot < 0) return NULL;
+    const uint64_t fp = dd_fingerprint(ctx->config.dec_hidden, ctx->config.dec_layers, ctx->config.vocab_size,
+                                       ctx->decoder.tok_embeddings_bf16, ctx->decoder.layers[0].wq_weight_bf16);
+    int ready;
+    dd_state *st = dd_slot_find(ctx, fp, &ready);
+    if (!st || ready) return st;
     const qkn_config_t *c = &ctx->config;
     const qkn_decoder_t *d = &ctx->decoder;
     dd_config cfg;
@@ -89,10 +70,9 @@ static dd_state *state_for(qkn_ctx_t *ctx)
                                ly->q_norm_weight, ly->k_norm_weight, ly->pre_ffn_norm, ly->post_ffn_norm,
                                ly->is_sliding};
     }
-    if (dd_setup(&g_slots[free_slot].st, &cfg, layers, d->tok_embeddings_bf16, d->norm, NULL) != 0) return NULL;
-    g_slots[free_slot].ctx = ctx;
-    g_slots[free_slot].fingerprint = fp;
-    return &g_slots[free_slot].st;
+    if (dd_setup(st, &cfg, layers, d->tok_embeddings_bf16, d->norm, NULL) != 0) return NULL;
+    dd_slot_claim(st, ctx, fp);
+    return st;
 }
 
 void qkn_decoder_prefill(qkn_ctx_t *ctx, const float *input_embeds, int seq_len)
@@ -127,11 +107,5 @@ int qkn_decoder_forward(qkn_ctx_t *ctx, const float *input_embed)
  * fingerprint and set up afresh. */
 void qkn_decoder_device_release(qkn_ctx_t *ctx)
 {
-    for (int i = 0; i < MAX_CONTEXTS; i++) {
-        if (g_slots[i].ctx != ctx) continue;
-        dd_release(&g_slots[i].st);
-        g_slots[i].ctx = NULL;
-        g_slots[i].fingerprint = 0;
-        ctx->kv_cache_len = 0;
-    }
+    if (ctx && dd_slot_release(ctx)) ctx->kv_cache_len = 0;
 }

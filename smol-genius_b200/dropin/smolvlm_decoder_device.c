@@ -25,34 +25,15 @@
 #include "smolvlm.h"
 
 #define DEVICE_TOKEN_ON_ERROR 49154   /* SMOLVLM_TOKEN_EOS, smolvlm.h:54 */
-#define MAX_CONTEXTS 8
-
-static struct {
-    const smolvlm_ctx_t *ctx;
-    uint64_t fingerprint;   /* of the weights it was set up from */
-    dd_state st;
-} g_slots[MAX_CONTEXTS];
 
 static dd_state *state_for(smolvlm_ctx_t *ctx)
 {
     if (ctx->config.dec_layers < 1 || ctx->config.dec_layers > DD_MAX_LAYERS) return NULL;
-    dd_config probe;
-    memset(&probe, 0, sizeof(probe));
-    probe.hidden = ctx->config.dec_hidden;
-    probe.layers = ctx->config.dec_layers;
-    probe.vocab = ctx->config.vocab_size;
-    const uint64_t fp = dd_fingerprint(&probe, ctx->decoder.tok_embeddings_bf16, ctx->decoder.layers[0].wq_weight_bf16);
-    int free_slot = -1;
-    for (int i = 0; i < MAX_CONTEXTS; i++) {
-        if (g_slots[i].ctx == ctx) {
-            if (g_slots[i].fingerprint == fp) return &g_slots[i].st;
-            /* the same address now holds another model: start over */
-            dd_release(&g_slots[i].st);
-            g_slots[i].ctx = NULL;
-        }
-        if (!g_slots[i].ctx && free_slot < 0) free_slot = i;
-    }
-    if (free_slot < 0) return NULL;
+    const uint64_t fp = dd_fingerprint(ctx->config.dec_hidden, ctx->config.dec_layers, ctx->config.vocab_size,
+                                       ctx->decoder.tok_embeddings_bf16, ctx->decoder.layers[0].wq_weight_bf16);
+    int ready;
+    dd_state *st = dd_slot_find(ctx, fp, &ready);
+    if (!st || ready) return st;
     const smolvlm_config_t *c = &ctx->config;
     const smolvlm_decoder_t *d = &ctx->decoder;
     dd_config cfg;
@@ -73,11 +54,10 @@ static dd_state *state_for(smolvlm_ctx_t *ctx)
                                ly->gate_up_fused_bf16, ly->down_weight_bf16, ly->input_norm, ly->post_attn_norm,
                                NULL, NULL, NULL, NULL, 0};
     }
-    if (dd_setup(&g_slots[free_slot].st, &cfg, layers, d->tok_embeddings_bf16, d->norm, d->lm_head_bf16) != 0)
+    if (dd_setup(st, &cfg, layers, d->tok_embeddings_bf16, d->norm, d->lm_head_bf16) != 0)
         return NULL;
-    g_slots[free_slot].ctx = ctx;
-    g_slots[free_slot].fingerprint = fp;
-    return &g_slots[free_slot].st;
+    dd_slot_claim(st, ctx, fp);
+    return st;
 }
 
 void smolvlm_decoder_prefill(smolvlm_ctx_t *ctx, const float *input_embeds, int seq_len)
@@ -112,11 +92,5 @@ int smolvlm_decoder_forward(smolvlm_ctx_t *ctx, const float *input_embed)
  * fingerprint and set up afresh. */
 void smolvlm_decoder_device_release(smolvlm_ctx_t *ctx)
 {
-    for (int i = 0; i < MAX_CONTEXTS; i++) {
-        if (g_slots[i].ctx != ctx) continue;
-        dd_release(&g_slots[i].st);
-        g_slots[i].ctx = NULL;
-        g_slots[i].fingerprint = 0;
-        ctx->kv_cache_len = 0;
-    }
+    if (ctx && dd_slot_release(ctx)) ctx->kv_cache_len = 0;
 }
