@@ -147,6 +147,37 @@ def test_siglip_workspace_sizes_and_shape_checks():
     assert smol_b200.siglip_workspace_bytes(_siglip_model(patch_w=None), 1) == 0
 
 
+def test_gemm_argument_rules():
+    """smol_b200_gemm_bf16 refuses what its kernel cannot take before touching a device
+    (1 = SMOL_B200_ERR_ARGS): activations out of range, gated pairs with an odd N or a
+    residual add, unaligned operands or strides, K <= 0, short leading dimensions.  A
+    well-formed call gets as far as the device (3 = SMOL_B200_ERR_NO_DEVICE here)."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("the addresses below are placeholders: never hand them to a device")
+    L = smol_b200.lib()
+    base = 1 << 20   # 16-byte aligned placeholder addresses, never dereferenced without a device
+
+    def gemm(**over):
+        kw = dict(out=base, ldo=256, out_kind=smol_b200.GEMM_OUT_F32, a=base, lda=128, w=base, ldw=128, bias=None,
+                  add=None, ld_add=0, add_rows=0, m=64, n=256, k=128, act=smol_b200.ACT_NONE)
+        kw.update(over)
+        return L.smol_b200_gemm_bf16(None, *kw.values())
+
+    assert gemm() == 3
+    assert gemm(act=smol_b200.ACT_GEGLU_PAIRS, out_kind=smol_b200.GEMM_OUT_BF16, ldo=128) == 3
+    assert gemm(act=4) == 1 and gemm(act=-1) == 1
+    assert gemm(act=smol_b200.ACT_SWIGLU_PAIRS, n=255) == 1                         # odd N
+    assert gemm(act=smol_b200.ACT_SWIGLU_PAIRS, out_kind=smol_b200.GEMM_OUT_F32_ADD) == 1
+    assert gemm(act=smol_b200.ACT_SWIGLU_PAIRS, add=base, ld_add=256, add_rows=1) == 1
+    assert gemm(a=base + 8) == 1 and gemm(w=base + 4) == 1                          # TMA base alignment
+    assert gemm(lda=132) == 1 and gemm(ldw=120) == 1                                # strides
+    assert gemm(k=0) == 1 and gemm(ldo=255) == 1
+    assert gemm(add=base, ld_add=256, add_rows=0) == 1
+    assert gemm(m=0) == 0                                                           # nothing to do
+    smol_b200.clear_error()
+
+
 def test_no_device_fails_loudly():
     import torch
     if torch.cuda.is_available():
