@@ -120,6 +120,31 @@ def test_dropin_bidirectional_audio_encoder_windows(cuda):
     assert_close(out, want, "audio encoder windows")
 
 
+@pytest.mark.new_on_gpu
+def test_dropin_bidirectional_nomic_batch(cuda):
+    # nomic's embedder (exports/nomic/nomic.c:176-182, :438-447): a batch of sequences of
+    # different lengths packed end to end, each sequence one window, 12 heads of hd 64,
+    # RoPE positions restarting at 0 in every sequence -- windows from 1 token to several
+    # 128-row query tiles, starting anywhere inside a tile
+    rng = np.random.default_rng(7)
+    h, hd = 12, 64
+    lens = [1, 37, 128, 300, 5, 129, 64]
+    ws = [0] + np.cumsum(lens).tolist()
+    seq = ws[-1]
+    pos = np.concatenate([np.arange(n) for n in lens]).astype(np.int32)
+    cos, sin = (np.zeros((seq, hd), np.float32) for _ in range(2))
+    smol_b200.compute_rope(cos, sin, pos, seq, hd, 1000.0)
+    q, k, v = (rnd_bf16(rng, seq, h * hd) for _ in range(3))
+    for x in (q, k):
+        smol_b200.apply_rope(x, cos, sin, seq, h, hd)
+    q, k = pyoracle.round_bf16(q), pyoracle.round_bf16(k)   # the parity protocol's bf16-exact inputs
+    out = np.zeros((seq, h * hd), np.float32)
+    smol_b200.bidirectional_attention(out, q, k, v, seq, h, hd, 0.125, ws)
+    no_error()
+    want = pyoracle.oracle().bidirectional_attention(q, k, v, seq, h, hd, 0.125, ws)
+    assert_close(out, want, "nomic batch windows")
+
+
 def test_dropin_rope_and_norm_golden(golden, cuda):
     for name in ("rope_neox", "rope_interleaved", "rope_neox_odd"):
         hd, inter = (int(x) for x in golden[f"{name}/meta"])
