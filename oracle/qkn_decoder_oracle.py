@@ -12,6 +12,11 @@ The attention, QK-norm, RoPE and cache append go through the C restatement
 fp16), so both sides attend over identical values.  Weights are bf16 (kept as the
 rounded fp32 values and as the raw bits to upload).
 
+Pinned to the reference decoder itself: PIN_CASES below run through qkn_decoder.c (and
+SmolVLM's decoder.c) on the same weights, live in tests/test_decoder_oracle_e2e.py and
+as the committed outputs of tests/golden/decoder_cases.npz; its pieces are pinned to the
+reference's own kernels in tests/test_decoder_oracle.py.
+
 Only tests/ import this module.
 """
 from __future__ import annotations

@@ -14,6 +14,11 @@ fp16; patch pixels bf16), so that the device path is compared on identical opera
 `False` is the reference's all-fp32 arithmetic.  Matrices are bf16-valued (stored as
 the rounded fp32 values), biases and norm weights fp32.
 
+Pinned to the reference's siglip_forward itself (SIGLIP_PIN_CASES below, run by the
+compiled reference on the same weights): tests/test_siglip_oracle.py, live and against
+tests/golden/siglip_cases.npz; the windowed encoder-layer composition in
+tests/test_encoder_layers_oracle.py.
+
 Only tests/ import this module.
 """
 from __future__ import annotations
