@@ -147,6 +147,36 @@ def test_siglip_workspace_sizes_and_shape_checks():
     assert smol_b200.siglip_workspace_bytes(_siglip_model(patch_w=None), 1) == 0
 
 
+def test_host_tables_match_oracle_and_reference():
+    """The RoPE tables and sinusoidal embeddings of Part 1 are built on the host (every
+    device path only indexes them): bit for bit the oracle's, and the reference's golden
+    tables within the one-ulp frequency difference of its -ffast-math build
+    (2e-6 + 1.2e-7 * position)."""
+    import pyoracle
+    golden = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "reference_cases.npz"))
+    o = pyoracle.oracle()
+    pos = np.arange(4096, dtype=np.int32)
+    for inter in (False, True):
+        for hd, theta in ((128, 1e6), (256, 1e4), (80, 1e4)):
+            c = np.zeros((len(pos), hd), np.float32)
+            s = np.zeros_like(c)
+            smol_b200.compute_rope(c, s, pos, len(pos), hd, theta, interleaved=inter)
+            c2, s2 = o.compute_rope(pos, hd, theta, interleaved=inter)
+            assert np.array_equal(c, c2) and np.array_equal(s, s2), (inter, hd)
+    for name in ("rope_neox", "rope_interleaved", "rope_neox_odd"):
+        hd, inter = (int(x) for x in golden[f"{name}/meta"])
+        p = golden[f"{name}/pos"].astype(np.int32)
+        c = np.zeros((len(p), hd), np.float32)
+        s = np.zeros_like(c)
+        smol_b200.compute_rope(c, s, p, len(p), hd, float(golden[f"{name}/fmeta"][0]), interleaved=bool(inter))
+        bound = (2e-6 + 1.2e-7 * p.astype(np.float64))[:, None]
+        assert np.all(np.abs(c - golden[f"{name}/cos"]) <= bound) and np.all(np.abs(s - golden[f"{name}/sin"]) <= bound)
+    pe = np.zeros((9, 32), np.float32)
+    smol_b200.sinusoidal_pe(pe, 9, 32)
+    assert np.allclose(pe, golden["sinusoidal/out"], rtol=1e-6, atol=1e-6)
+    assert smol_b200.last_error() == 0
+
+
 def test_gemm_argument_rules():
     """smol_b200_gemm_bf16 refuses what its kernel cannot take before touching a device
     (1 = SMOL_B200_ERR_ARGS): activations out of range, gated pairs with an odd N or a
