@@ -287,7 +287,8 @@ int dd_forward(dd_state *st, const float *embed, int pos, float *x_normed)
         smol_b200_copy(st->kv_len_dev, &pos, sizeof(int)) != SMOL_B200_OK ||
         smol_b200_qkn_decode_step_embeds(NULL, &st->model, 1, st->x_dev, st->token_dev, st->k_pool, st->v_pool,
                                          (int64_t)st->cfg.layers * st->cap, st->row0_dev, st->kv_len_dev,
-                                         (int)st->cap - 1, st->cos, st->sin, 0, st->step_ws, st->step_ws_bytes,
+                                         pos /* the split-KV plan follows the actual length */, st->cos, st->sin, 0,
+                                         st->step_ws, st->step_ws_bytes,
                                          st->xn_dev) != SMOL_B200_OK ||
         smol_b200_copy(&token, st->token_dev, sizeof(int)) != SMOL_B200_OK ||
         (x_normed && smol_b200_copy(x_normed, st->xn_dev, H * 4) != SMOL_B200_OK))
