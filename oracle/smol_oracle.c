@@ -209,6 +209,12 @@ void oracle_decode_batched(float *out, const float *Q, const uint16_t *K_bf16,
         int L = kv_len[b];
         float *k = (float *)malloc(sizeof(float) * (size_t)(L > 0 ? L : 1) * kv_dim);
         float *v = (float *)malloc(sizeof(float) * (size_t)(L > 0 ? L : 1) * kv_dim);
+        if (!k || !v) {   /* out of host memory: NaN rows fail every comparison */
+            for (long i = 0; i < q_dim; i++) out[b * q_dim + i] = NAN;
+            free(k);
+            free(v);
+            continue;
+        }
         oracle_bf16_to_f32(k, K_bf16 + row0[b] * kv_dim, (int64_t)L * kv_dim);
         oracle_f16_to_f32(v, V_f16 + row0[b] * kv_dim, (int64_t)L * kv_dim);
         /* qkn_decoder.c:658-677: seq_q=1, seq_k=pos+1, q_offset=pos */
@@ -265,6 +271,10 @@ void oracle_fill_rope_table(float *cos_tab, float *sin_tab, int n_pos, int head_
 {
     int half = head_dim / 2;
     float *inv = (float *)malloc(sizeof(float) * (size_t)(half > 0 ? half : 1));
+    if (!inv) {   /* out of host memory: NaN tables fail every comparison */
+        for (long i = 0; i < (long)n_pos * head_dim; i++) cos_tab[i] = sin_tab[i] = NAN;
+        return;
+    }
     for (int d = 0; d < half; d++)
         inv[d] = 1.0f / powf(theta, (float)(2 * d) / (float)head_dim);
     for (int pos = 0; pos < n_pos; pos++) {
