@@ -178,14 +178,6 @@ __device__ __forceinline__ float gate_act(float g, int mode)
     return g / (1.0f + expf(-g));
 }
 
-// Pull a weight row into L2 ahead of the dependency wait (weights never change).
-__device__ __forceinline__ void prefetch_row_l2(const uint16_t *row, int k_dim, int lane)
-{
-    const char *p = reinterpret_cast<const char *>(row);
-    for (int off = lane * 128; off < k_dim * 2; off += 32 * 128)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
-}
-
 // Row `r` of the concatenated segments: its weights and its output column.
 struct RowRef {
     const uint16_t *w;
