@@ -10,8 +10,10 @@
  *                  (no QK-norm, untied output head).
  * The library calls are the fakes of fake_smol_b200.c; the model struct the fakes last
  * received is compared field by field and weight by weight with the context.  Also:
- * kv_cache_len and dec_x after prefill / forward, the failure sentinel for a position
- * past the ones the device holds, release, and a context whose weights changed.
+ * kv_cache_len and dec_x after prefill / forward, a chunked prefill and a cache reset
+ * (the fake prefill checks each chunk's inputs arrive at their positions), the failure
+ * sentinel for a position past the ones the device holds, release, and a context whose
+ * weights changed.
  *
  * Exit status 0 when every check passes; otherwise 1, with the failing check on stderr.
  */
@@ -155,6 +157,18 @@ int main(void)
     CHECK(!m->rope_cos_local && !m->rope_sin_local);
     CHECK(same(m->lm_head, ctx->decoder.lm_head_bf16, (size_t)VOCAB * HID * 2));
 #endif
+
+    /* chunked prefill continues at kv_cache_len; a cache reset (qkn_kv_cache_reset sets
+     * kv_cache_len = 0, qkn_decoder.h:165-167) starts again at position 0 */
+    float more[3 * HID];
+    for (int t = 0; t < 3; t++)
+        for (int i = 0; i < HID; i++) more[t * HID + i] = (float)(6 + t);
+    PREFILL(ctx, more, 3);
+    CHECK(ctx->kv_cache_len == 9 && g_prefills == 2);
+    ctx->kv_cache_len = 0;
+    PREFILL(ctx, embeds, 5);
+    CHECK(ctx->kv_cache_len == 5 && g_prefills == 3);
+    CHECK(FORWARD(ctx, embeds + 5 * HID) == 5 % VOCAB && ctx->kv_cache_len == 6);
 
     /* a position past the ones the device holds: the export's failure sentinel */
     ctx->kv_cache_len = 9;
