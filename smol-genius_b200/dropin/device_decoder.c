@@ -181,8 +181,9 @@ int dd_setup(dd_state *st, const dd_config *c, const dd_layer *layers, const uin
     return 0;
 }
 
-/* Pools, tables and buffers for positions [0, need) and n_in input rows; `cached`
- * positions are kept when the pool grows (rows copied on the device). */
+/* Pools, tables and buffers for positions [0, need) and n_in input rows; the first
+ * `cached` positions (all the held ones) are kept when the pool grows (rows copied on
+ * the device), so a call that fails after a growth loses none of them. */
 static int ensure_capacity(dd_state *st, int need, int cached, int n_in)
 {
     const dd_config *c = &st->cfg;
@@ -228,11 +229,16 @@ static int ensure_capacity(dd_state *st, int need, int cached, int n_in)
         st->step_ws = smol_b200_device_alloc(st->step_ws_bytes);
         if (!st->step_ws) return 0;
     }
-    if (need > st->rope_cap) {
+    /* sliding layers' own theta (qkn_decoder.c:313-340) */
+    const int want_local = c->local_theta > 0.0f && c->local_theta != c->theta;
+    if (need > st->rope_cap || !st->cos || !st->sin || (want_local && (!st->cos_local || !st->sin_local))) {
+        /* until both sets are made again, nothing refers to the old ones */
+        st->rope_cap = 0;
+        st->model.rope_cos_local = NULL;
+        st->model.rope_sin_local = NULL;
         const int rows = (int)st->cap;
         if (!rope_tables(&st->cos, &st->sin, rows, c->head_dim, c->theta, c->interleaved)) return 0;
-        /* sliding layers' own theta (qkn_decoder.c:313-340) */
-        if (c->local_theta > 0.0f && c->local_theta != c->theta) {
+        if (want_local) {
             if (!rope_tables(&st->cos_local, &st->sin_local, rows, c->head_dim, c->local_theta, c->interleaved))
                 return 0;
             st->model.rope_cos_local = st->cos_local;
@@ -258,22 +264,32 @@ static int position_held(const dd_state *st, int pos)
     return 0;
 }
 
+/* After a call that failed inside the library the rows from `pos` on may hold a partial
+ * write: only the positions before it stay trusted.  (A failed allocation before the
+ * call leaves every held row in place: pool growth copies all of them.) */
+static void distrust_from(dd_state *st, int pos)
+{
+    if (st->held > pos) st->held = pos;
+}
+
 int dd_prefill(dd_state *st, const float *embeds, int n, int start)
 {
     if (n <= 0) return 0;
-    if (!st->ready || !position_held(st, start) || !ensure_capacity(st, start + n + 1, start, n)) return -1;
+    if (!st->ready || !position_held(st, start) || !ensure_capacity(st, start + n + 1, st->held, n)) return -1;
     if (n > st->prefill_cap) {
         smol_b200_device_free(st->prefill_ws);
         st->prefill_ws_bytes = smol_b200_qkn_prefill_workspace_bytes(&st->model, n);
         st->prefill_ws = smol_b200_device_alloc(st->prefill_ws_bytes);
         st->prefill_cap = st->prefill_ws ? n : 0;
     }
-    if (!st->prefill_ws ||
-        smol_b200_copy(st->x_dev, embeds, (size_t)n * st->cfg.hidden * 4) != SMOL_B200_OK ||
-        smol_b200_qkn_prefill_embeds(NULL, &st->model, st->x_dev, n, start, st->k_pool, st->v_pool,
-                                     (int64_t)st->cfg.layers * st->cap, st->row0_host, st->cos, st->sin,
-                                     st->prefill_ws, st->prefill_ws_bytes) != SMOL_B200_OK)
+    if (!st->prefill_ws || smol_b200_copy(st->x_dev, embeds, (size_t)n * st->cfg.hidden * 4) != SMOL_B200_OK)
         return -1;
+    if (smol_b200_qkn_prefill_embeds(NULL, &st->model, st->x_dev, n, start, st->k_pool, st->v_pool,
+                                     (int64_t)st->cfg.layers * st->cap, st->row0_host, st->cos, st->sin,
+                                     st->prefill_ws, st->prefill_ws_bytes) != SMOL_B200_OK) {
+        distrust_from(st, start);
+        return -1;
+    }
     st->held = start + n;
     return 0;
 }
@@ -282,17 +298,19 @@ int dd_forward(dd_state *st, const float *embed, int pos, float *x_normed)
 {
     int token = -1;
     const size_t H = (size_t)st->cfg.hidden;
-    if (!st->ready || !position_held(st, pos) || !ensure_capacity(st, pos + 2, pos, 1) ||
+    if (!st->ready || !position_held(st, pos) || !ensure_capacity(st, pos + 2, st->held, 1) ||
         smol_b200_copy(st->x_dev, embed, H * 4) != SMOL_B200_OK ||
-        smol_b200_copy(st->kv_len_dev, &pos, sizeof(int)) != SMOL_B200_OK ||
-        smol_b200_qkn_decode_step_embeds(NULL, &st->model, 1, st->x_dev, st->token_dev, st->k_pool, st->v_pool,
+        smol_b200_copy(st->kv_len_dev, &pos, sizeof(int)) != SMOL_B200_OK)
+        return -1;
+    if (smol_b200_qkn_decode_step_embeds(NULL, &st->model, 1, st->x_dev, st->token_dev, st->k_pool, st->v_pool,
                                          (int64_t)st->cfg.layers * st->cap, st->row0_dev, st->kv_len_dev,
                                          pos /* the split-KV plan follows the actual length */, st->cos, st->sin, 0,
-                                         st->step_ws, st->step_ws_bytes,
-                                         st->xn_dev) != SMOL_B200_OK ||
+                                         st->step_ws, st->step_ws_bytes, st->xn_dev) != SMOL_B200_OK ||
         smol_b200_copy(&token, st->token_dev, sizeof(int)) != SMOL_B200_OK ||
-        (x_normed && smol_b200_copy(x_normed, st->xn_dev, H * 4) != SMOL_B200_OK))
+        (x_normed && smol_b200_copy(x_normed, st->xn_dev, H * 4) != SMOL_B200_OK)) {
+        distrust_from(st, pos);
         return -1;
+    }
     st->held = pos + 1;
     return token;
 }

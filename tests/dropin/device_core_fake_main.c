@@ -234,6 +234,89 @@ static void check_failed_uploads(int gemma)
     CHECK(dd_slot_release(&ctxs[0]) == 1 && g_live == 0);
 }
 
+/* A seeded random sequence of prefills, decode steps, truncations, cache resets,
+ * releases, single failed allocations and failures inside the library calls, against a
+ * model of what each must do: a call succeeds exactly when its position is within the
+ * ones held and nothing was made to fail; after a failure inside the library the rows
+ * from the call's position on are no longer held; and every call checks, through the
+ * fakes, that all rows written before are still where the library reads them. */
+static void check_random_operations(void)
+{
+    host_model h;
+    make_model(&h, 1, 900);
+    int ctx_r;
+    uint64_t rng = 12345;
+    int held = 0, failures_seen = 0, ok_ops = 0, max_held = 0;
+    float xn[HID];
+    dd_state *st = set_up(&ctx_r, &h);
+    CHECK(st != NULL);
+    for (int op = 0; op < 3000 && st; op++) {
+        rng = rng * 6364136223846793005ull + 1442695040888963407ull;
+        const unsigned r = (unsigned)(rng >> 33);
+        const int inject = r % 7 == 0;                   /* one allocation of this call fails */
+        const int fail_call = !inject && r % 23 == 0;    /* the library call itself fails */
+        if (inject) g_fail_at = g_allocs + (int)((r >> 8) % 5);
+        g_fail_call = fail_call;
+        int want_ok, rc;
+        const unsigned kind = (r >> 4) % 100;   /* 25 % prefill, 60 % decode, 10 % truncate, 3 % reset, 2 % release */
+        if (kind < 25) {   /* prefill at a position near the end of what is held */
+            const int start = held - (int)((r >> 12) % 4) + (int)((r >> 16) % 3) - 1;
+            const int n = 1 + (int)((r >> 20) % 300);
+            want_ok = start >= 0 && start <= held;
+            rc = start >= 0 ? prefill(st, start, n) : -1;
+            if (rc == 0) held = start + n;
+            if (fail_call && want_ok) {
+                CHECK(rc == -1);
+                held = start < held ? start : held;
+                want_ok = 0;
+            }
+        } else if (kind < 95) {   /* a decode step at the end (or just past it), or after a truncation */
+            int pos = held + ((r >> 12) % 16 == 0 ? 1 : 0);
+            if (kind >= 85) pos = held > 0 ? (int)((r >> 16) % (unsigned)held) : 0;
+            want_ok = pos <= held;
+            const int tok = step(st, pos, xn);
+            rc = tok < 0 ? -1 : 0;
+            if (rc == 0) {
+                CHECK(tok == pos % VOCAB);
+                held = pos + 1;
+            }
+            if (fail_call && want_ok) {
+                CHECK(rc == -1);
+                held = pos < held ? pos : held;
+                want_ok = 0;
+            }
+        } else if (kind < 98) {   /* a cache reset: prefill from 0 */
+            const int n = 1 + (int)((r >> 12) % 50);
+            want_ok = !fail_call;
+            rc = prefill(st, 0, n);
+            if (rc == 0) held = n;
+            if (fail_call) held = 0;
+        } else {   /* release and set up again */
+            g_fail_at = -1;
+            g_fail_call = 0;
+            CHECK(dd_slot_release(&ctx_r) == 1);
+            st = set_up(&ctx_r, &h);
+            CHECK(st != NULL);
+            held = 0;
+            continue;
+        }
+        g_fail_at = -1;
+        g_fail_call = 0;
+        if (inject && want_ok && rc != 0) {
+            failures_seen++;   /* the failed allocation hit this call: the next calls must still work */
+            continue;
+        }
+        CHECK((rc == 0) == want_ok);
+        CHECK(st->held == held);
+        ok_ops += rc == 0;
+        max_held = held > max_held ? held : max_held;
+    }
+    CHECK(failures_seen > 10 && ok_ops > 1500 && max_held > 2100);   /* at least two pool growths */
+    CHECK(dd_slot_release(&ctx_r) == 1 && g_live == 0);
+    printf("random operations: %d succeeded, %d failed allocations, up to %d positions\n", ok_ops, failures_seen,
+           max_held);
+}
+
 int main(void)
 {
     check_decoder(0);
@@ -241,6 +324,7 @@ int main(void)
     check_slots();
     check_failed_uploads(0);
     check_failed_uploads(1);
+    check_random_operations();
     printf("prefills %d steps %d failures %d\n", g_prefills, g_steps, g_failures);
     return g_failures ? 1 : 0;
 }

@@ -9,7 +9,8 @@
  * earlier still holds its tag at the row the library would read it from
  * (layer_row0[l] + position), then tag the rows they write; the decode returns token
  * position % vocab and writes embed + 0.5 as the normalised state.  Both keep a copy of
- * the model struct they were given (g_last_model).
+ * the model struct they were given (g_last_model).  With g_fail_call set, the next of
+ * them corrupts the first row it wrote and fails (a failure inside the library).
  */
 #include <stdint.h>
 #include <stdio.h>
@@ -114,7 +115,7 @@ void smol_compute_rope_interleaved(float *c, float *s, const int *pos, int seq, 
 uint16_t tag_k(int l, int p) { return (uint16_t)(1 + l * 2003 + p); }
 uint16_t tag_v(int l, int p) { return (uint16_t)(tag_k(l, p) ^ 0x8000u); }
 
-int g_prefills = 0, g_steps = 0, g_check_embeds = 1;
+int g_prefills = 0, g_steps = 0, g_check_embeds = 1, g_fail_call = 0;
 smol_b200_qkn_model g_last_model;
 static smol_b200_qkn_layer g_last_layers[DD_MAX_LAYERS];
 
@@ -186,7 +187,13 @@ int smol_b200_qkn_prefill_embeds(void *stream, const smol_b200_qkn_model *m, con
         return SMOL_B200_ERR_ARGS;
     for (int t = 0; t < n && g_check_embeds; t++)
         if (embeds[(size_t)t * H] != (float)(start + t)) return SMOL_B200_ERR_ARGS;
-    return check_and_tag(m, k_pool, v_pool, pool_rows, row0_host, start, start, n) ? SMOL_B200_OK : SMOL_B200_ERR_ARGS;
+    if (!check_and_tag(m, k_pool, v_pool, pool_rows, row0_host, start, start, n)) return SMOL_B200_ERR_ARGS;
+    if (g_fail_call) {   /* a failure inside the library after a partial write */
+        g_fail_call = 0;
+        k_pool[(size_t)(row0_host[0] + start) * m->n_kv_heads * m->head_dim] = 0xdead;
+        return SMOL_B200_ERR_CUDA;
+    }
+    return SMOL_B200_OK;
 }
 
 int smol_b200_qkn_decode_step_embeds(void *stream, const smol_b200_qkn_model *m, int n_seqs, const float *embeds,
@@ -209,6 +216,11 @@ int smol_b200_qkn_decode_step_embeds(void *stream, const smol_b200_qkn_model *m,
         return SMOL_B200_ERR_ARGS;
     if (m->rope_cos_local && dev_bytes_from(m->rope_cos_local) < (size_t)(pos + 1) * hd * 4) return SMOL_B200_ERR_ARGS;
     if (!check_and_tag(m, k_pool, v_pool, pool_rows, layer_row0, pos, pos, 1)) return SMOL_B200_ERR_ARGS;
+    if (g_fail_call) {   /* a failure inside the library after a partial write */
+        g_fail_call = 0;
+        k_pool[(size_t)(layer_row0[0] + pos) * m->n_kv_heads * m->head_dim] = 0xdead;
+        return SMOL_B200_ERR_CUDA;
+    }
     tokens_out[0] = pos % m->vocab;
     if (x_normed_out)
         for (size_t i = 0; i < H; i++) x_normed_out[i] = embeds[i] + 0.5f;

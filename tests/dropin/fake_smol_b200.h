@@ -11,6 +11,7 @@
 extern int g_failures;                     /* failed CHECKs (and frees of foreign pointers) */
 extern int g_live, g_allocs, g_fail_at;    /* live allocations, allocations made, the one to fail */
 extern int g_prefills, g_steps, g_check_embeds;
+extern int g_fail_call;                    /* the next prefill / decode call fails after a partial write */
 extern smol_b200_qkn_model g_last_model;   /* as passed to the last prefill / decode call */
 
 #define CHECK(cond)                                                                   \
