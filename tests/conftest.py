@@ -48,10 +48,14 @@ def pytest_configure(config):
 
 
 def pytest_collection_modifyitems(config, items):
-    """Tests marked new_on_gpu run last (the sort is stable), so that under -x a failure
-    in one of them cannot keep the established tests from running; among them by
-    `stage` (default 0): unit tests of a new kernel before the tests built on it."""
+    """Tests marked new_on_gpu run after the established ones (the sort is stable), so
+    that under -x a failure in one of them cannot keep the established tests from
+    running; among them by `stage` (default 0): unit tests of a new kernel before the
+    tests built on it.  test_zz_no_alloc.py stays the very last file: the
+    allocation-free entry point's tests must find every other test already run."""
     def key(item):
+        if os.path.basename(str(item.fspath)) == "test_zz_no_alloc.py":
+            return (2, 0)
         mark = item.get_closest_marker("new_on_gpu")
         return (0, 0) if mark is None else (1, mark.kwargs.get("stage", 0))
     items.sort(key=key)
