@@ -193,7 +193,9 @@ SMOL_B200_API int smol_b200_decode_attention(
  * Every call shares the one array and leaves its contents behind: two calls whose
  * kernels overlap on the GPU (different streams, or different host threads) race
  * on it, so serialise them.  Arguments and results are those of
- * smol_b200_decode_attention. */
+ * smol_b200_decode_attention.  A wait that timed out inside its kernels is reported
+ * by smol_cuda_device_error(), which in a process that uses no other entry point reads
+ * a word of the same array and allocates nothing; smol_cuda_clear_error() resets it. */
 SMOL_B200_API int smol_b200_decode_attention_noalloc(
     void *stream, float *out, const void *q, int q_is_bf16, const uint16_t *k_pool,
     const uint16_t *v_pool, int64_t pool_rows, const int64_t *seq_row0, const int *kv_len,

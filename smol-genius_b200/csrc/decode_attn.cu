@@ -804,6 +804,44 @@ int launch_decode_noalloc(cudaStream_t st, int dev, uint8_t *scratch, float *out
 
 }  // namespace
 
+// Whether the allocation-free entry point has set up its array on the current device.
+bool noalloc_in_use()
+{
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) {
+        cudaGetLastError();
+        return false;
+    }
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    return g_noalloc_ptr[dev] != nullptr;
+}
+
+// Watchdog bits the allocation-free kernels left in word 0 of the array on the current
+// device (they go there when no device error word had been created); `clear` resets
+// the word.  0 when the entry point has not run on this device.  Copies, never
+// allocates.
+unsigned noalloc_watchdog_bits(bool clear)
+{
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) {
+        cudaGetLastError();
+        return 0;
+    }
+    void *ptr = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        ptr = g_noalloc_ptr[dev];
+    }
+    if (!ptr) return 0;
+    unsigned v = 0;
+    if (cudaMemcpy(&v, ptr, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return 0xffffffffu;
+    }
+    if (clear && v && cudaMemset(ptr, 0, sizeof(unsigned)) != cudaSuccess) cudaGetLastError();
+    return v;
+}
+
 }  // namespace smolb200
 
 // Part 3 of smol_b200.h: the allocation-free entry point (declared there).

@@ -296,23 +296,28 @@ void smol_cuda_clear_error(void)
         cudaMemset(smolb200::g_ctx[dev].err_word, 0, sizeof(unsigned));
         cudaDeviceSynchronize();
     }
+    smolb200::noalloc_watchdog_bits(true);   // the allocation-free entry point's word, if it ran here
     cudaGetLastError();
 }
 
 unsigned smol_cuda_device_error(void)
 {
-    unsigned *w = smolb200::device_error_word();
-    if (!w) return 0;
+    // A process that only uses the allocation-free entry point has no error word and
+    // gets none here (making it allocates); that entry point's kernels leave their bits
+    // in word 0 of its own array, read below.
+    const bool noalloc = smolb200::noalloc_in_use();
+    unsigned *w = noalloc ? smolb200::device_error_word_if_created() : smolb200::device_error_word();
+    if (!w && !noalloc) return 0;
     unsigned v = 0;
     if (cudaDeviceSynchronize() != cudaSuccess) {
         cudaGetLastError();
         return 0xffffffffu;
     }
-    if (cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) {
+    if (w && cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) {
         cudaGetLastError();
         return 0xffffffffu;
     }
-    return v;
+    return v | smolb200::noalloc_watchdog_bits(false);
 }
 
 }  // extern "C"

@@ -21,6 +21,9 @@ bool cuda_check(cudaError_t e, const char *what);   // records SMOL_B200_ERR_CUD
 unsigned *device_error_word();
 // The same word if this device's context already exists, else NULL; never allocates.
 unsigned *device_error_word_if_created();
+// decode_attn.cu: the allocation-free entry point's array on the current device
+bool noalloc_in_use();
+unsigned noalloc_watchdog_bits(bool clear);
 // Stream used by the drop-in (Part 1) entry points of the current device.
 cudaStream_t legacy_stream();
 // Grow-only device scratch of the current device for the drop-in entry points.
