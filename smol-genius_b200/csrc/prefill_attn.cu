@@ -66,13 +66,16 @@ constexpr int kMaxExtraOuts = 7;   // further copies of the output (peers of an 
 
 struct PrefillParams {
     CUtensorMap tq, tk, tv;
-    CUtensorMap to;                 // fp32 output, box 32 x 32 rows, 128B swizzle (v2 epilogue)
-    // Further destinations of every output row (v2), same strides as `out`: plain
-    // 16-byte stores, so a peer GPU's buffer mapped through CUDA IPC receives its copy
-    // over NVLink while later tiles compute.
-    float *out_more[kMaxExtraOuts];
+    // Output for the v2 epilogue's TMA stores, 128B swizzle: fp32 boxes of 32 columns x
+    // 32 rows, or bf16 boxes of 64 columns x 32 rows when out_bf16.
+    CUtensorMap to;
+    // Further destinations of every output row (v2), same strides and type as `out`:
+    // plain 16-byte stores, so a peer GPU's buffer mapped through CUDA IPC receives its
+    // copy over NVLink while later tiles compute.
+    void *out_more[kMaxExtraOuts];
     int n_more;
-    float *out;
+    int out_bf16;                   // output elements: 0 fp32, 1 bf16 (round to nearest even)
+    void *out;
     long long out_row_stride, out_batch_stride;
     const int *window_starts;
     unsigned *err;
@@ -96,6 +99,32 @@ __device__ __forceinline__ float fast_exp2(float x)
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 32 consecutive output values of one row (rr scaled by inv), as fp32 or bf16, to `dst`
+// (element offset `off` of an output buffer) with 16-byte stores.
+__device__ __forceinline__ void store_row32(void *dst, long long off, const uint32_t (&rr)[32], float inv,
+                                            bool bf16)
+{
+    if (bf16) {
+        uint16_t *o = static_cast<uint16_t *>(dst) + off;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv);
+            v.y = pack_bf16x2(__uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
+            v.z = pack_bf16x2(__uint_as_float(rr[i + 4]) * inv, __uint_as_float(rr[i + 5]) * inv);
+            v.w = pack_bf16x2(__uint_as_float(rr[i + 6]) * inv, __uint_as_float(rr[i + 7]) * inv);
+            *reinterpret_cast<uint4 *>(o + i) = v;
+        }
+    } else {
+        float *o = static_cast<float *>(dst) + off;
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4 *>(o + i) =
+                make_float4(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv,
+                            __uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
+    }
 }
 
 // Keys [lo, hi) visible to query row i; written=false for rows no window covers
@@ -129,6 +158,20 @@ __device__ __forceinline__ void row_range(const PrefillParams &p, int i, int &lo
     if (p.window > 0 && pos >= p.window) lo = max(lo, pos - p.window + 1);   // attention.c:194-196
     if (lo < 0) lo = 0;
     if (hi < lo) hi = lo;
+}
+
+// First key of a work item's key tiles, given the lowest key `lo` any of its rows sees.
+// Under a sliding window `lo` moves with the item's first row, so it is rounded down to
+// a multiple of BN in absolute key index: a query row then meets the same key-tile
+// boundaries -- hence the same online-softmax rescale points and the same fp16
+// rounding of P -- whichever chunk of a chunked prefill (q_offset) it falls in.  The
+// extra keys in front are masked for every row, and a fully masked tile changes
+// neither the running maximum nor O (its P is exactly 0).  Causal and prefix-LM rows
+// start at key 0 already; window masks are never chunked and keep their exact start.
+template <int BN>
+__device__ __forceinline__ int first_key_tile(const PrefillParams &p, int lo)
+{
+    return p.window > 0 ? (lo / BN) * BN : lo;
 }
 
 // Work item k of a v1 launch: (query tile qt, head h, batch b), query tiles fastest --
@@ -165,8 +208,8 @@ __device__ __forceinline__ Item1 item1_geometry(const PrefillParams &p, int k)
         row_range(p, a, lo_a, hi_a, w);
         row_range(p, z, lo_z, hi_z, w);
         if (hi_z > lo_a) {
-            it.lo_min = lo_a;
-            it.n_tiles = (hi_z - lo_a + BN - 1) / BN;
+            it.lo_min = first_key_tile<BN>(p, lo_a);
+            it.n_tiles = (hi_z - it.lo_min + BN - 1) / BN;
         }
     }
     return it;
@@ -446,9 +489,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                                                                  p.err, kErrWaitMma));
             tc_fence_after();
             const bool store = ok && row_valid && my_written;
-            float *orow = p.out + static_cast<long long>(it.b) * p.out_batch_stride +
-                          static_cast<long long>(store ? row : 0) * p.out_row_stride +
-                          static_cast<long long>(it.h) * HD;
+            const long long orow = static_cast<long long>(it.b) * p.out_batch_stride +
+                                   static_cast<long long>(store ? row : 0) * p.out_row_stride +
+                                   static_cast<long long>(it.h) * HD;
             const float inv = l > 0.f ? 1.f / l : 0.f;
             uint32_t rr[32];
 #pragma unroll
@@ -460,14 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 #pragma unroll
                     for (int i = 0; i < 32; ++i) rr[i] = 0u;
                 }
-                if (store) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        float4 v = make_float4(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv,
-                                               __uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
-                        *reinterpret_cast<float4 *>(orow + c * 32 + i) = v;
-                    }
-                }
+                if (store) store_row32(p.out, orow + c * 32, rr, inv, p.out_bf16 != 0);
             }
             g0 += n_tiles;
         }
@@ -657,8 +693,8 @@ __device__ __forceinline__ Item2 item_geometry(const PrefillParams &p, int k)
         row_range(p, a, lo_a, hi_a, w);
         row_range(p, z, lo_z, hi_z, w);
         if (hi_z > lo_a) {
-            it.lo_min = lo_a;
-            it.n_tiles = (hi_z - lo_a + BN - 1) / BN;
+            it.lo_min = first_key_tile<BN>(p, lo_a);
+            it.n_tiles = (hi_z - it.lo_min + BN - 1) / BN;
         }
     }
     return it;
@@ -1007,6 +1043,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                                             : (tile == 0 ? sK : sV) + (warp & 3) * (32 * HD * 4);
                 if (lane == 0 && stores_pending) bulk_wait_read0();   // previous store read its staging
                 __syncwarp();
+                const bool bf = p.out_bf16 != 0;
                 uint32_t rr[32];
 #pragma unroll
                 for (int c = 0; c < HD / 32; ++c) {
@@ -1017,52 +1054,71 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
 #pragma unroll
                         for (int i = 0; i < 32; ++i) rr[i] = 0u;
                     }
-                    uint8_t *box = stage + c * (32 * 128);
+                    if (bf) {
+                        // bf16 boxes are 64 columns (128 B) wide: columns [32c, 32c+32) are the
+                        // 16-byte units 4(c%2) .. 4(c%2)+3 of box c/2
+                        uint8_t *box = stage + (c / 2) * (32 * 128);
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        float4 v = make_float4(__uint_as_float(rr[4 * q]) * inv, __uint_as_float(rr[4 * q + 1]) * inv,
-                                               __uint_as_float(rr[4 * q + 2]) * inv,
-                                               __uint_as_float(rr[4 * q + 3]) * inv);
-                        *reinterpret_cast<float4 *>(box + sw128_offset(lane, q)) = v;
+                        for (int u = 0; u < 4; ++u) {
+                            uint4 v;
+                            v.x = pack_bf16x2(__uint_as_float(rr[8 * u]) * inv, __uint_as_float(rr[8 * u + 1]) * inv);
+                            v.y = pack_bf16x2(__uint_as_float(rr[8 * u + 2]) * inv,
+                                              __uint_as_float(rr[8 * u + 3]) * inv);
+                            v.z = pack_bf16x2(__uint_as_float(rr[8 * u + 4]) * inv,
+                                              __uint_as_float(rr[8 * u + 5]) * inv);
+                            v.w = pack_bf16x2(__uint_as_float(rr[8 * u + 6]) * inv,
+                                              __uint_as_float(rr[8 * u + 7]) * inv);
+                            *reinterpret_cast<uint4 *>(box + sw128_offset(lane, (c % 2) * 4 + u)) = v;
+                        }
+                    } else {
+                        uint8_t *box = stage + c * (32 * 128);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) {
+                            float4 v = make_float4(__uint_as_float(rr[4 * q]) * inv,
+                                                   __uint_as_float(rr[4 * q + 1]) * inv,
+                                                   __uint_as_float(rr[4 * q + 2]) * inv,
+                                                   __uint_as_float(rr[4 * q + 3]) * inv);
+                            *reinterpret_cast<float4 *>(box + sw128_offset(lane, q)) = v;
+                        }
                     }
                 }
                 __syncwarp();
                 if (p.n_more > 0) {
                     // Further destinations (a peer GPU's buffer over NVLink): the warp copies its
-                    // 32 staged rows one row per instruction -- lane l takes the 16 bytes at
-                    // column 4l (16-byte unit l%8 of box l/8) -- so each store is a contiguous
-                    // run of the row, not 32 scattered 16-byte pieces.
+                    // 32 staged rows one row per instruction -- lane l takes 16-byte unit l of the
+                    // row (unit u%8 of box u/8) -- so each store is a contiguous run of the row,
+                    // not 32 scattered 16-byte pieces.
                     const int y0 = it.row0[tile] + (warp & 3) * 32;
-                    constexpr int kLanesPerRow = HD / 4;          // 16 (hd 64) or 32 (hd 128)
-                    constexpr int kRowsPerStep = 32 / kLanesPerRow;
-                    const int sub = lane / kLanesPerRow, col4 = lane % kLanesPerRow;
-                    for (int r0 = 0; r0 < 32; r0 += kRowsPerStep) {
+                    const int lanes_per_row = bf ? HD / 8 : HD / 4;   // 16-byte units per row
+                    const int rows_per_step = 32 / lanes_per_row;
+                    const int sub = lane / lanes_per_row, u = lane % lanes_per_row;
+                    const int elems = bf ? 8 : 4;                     // per 16-byte unit
+                    for (int r0 = 0; r0 < 32; r0 += rows_per_step) {
                         const int rr_ = r0 + sub, grow = y0 + rr_;
                         if (grow >= p.seq_q) break;   // rows past the end exist only in the staging
-                        const float4 v = *reinterpret_cast<const float4 *>(stage + (col4 / 8) * (32 * 128) +
-                                                                           sw128_offset(rr_, col4 % 8));
+                        const uint4 v = *reinterpret_cast<const uint4 *>(stage + (u / 8) * (32 * 128) +
+                                                                         sw128_offset(rr_, u % 8));
                         const long long off = static_cast<long long>(it.b) * p.out_batch_stride +
                                               static_cast<long long>(grow) * p.out_row_stride +
-                                              static_cast<long long>(head) * HD + col4 * 4;
-                        for (int o = 0; o < p.n_more; ++o) *reinterpret_cast<float4 *>(p.out_more[o] + off) = v;
+                                              static_cast<long long>(head) * HD + u * elems;
+                        const long long boff = off * (bf ? 2 : 4);
+                        for (int o = 0; o < p.n_more; ++o)
+                            *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(p.out_more[o]) + boff) = v;
                     }
                 }
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
                     const int y = it.row0[tile] + (warp & 3) * 32;
-#pragma unroll
-                    for (int c = 0; c < HD / 32; ++c)
-                        tma_store_3d(&p.to, smem_u32(stage + c * (32 * 128)), head * HD + c * 32, y, it.b);
+                    const int box_cols = bf ? 64 : 32;
+                    for (int c = 0; c < HD / box_cols; ++c)
+                        tma_store_3d(&p.to, smem_u32(stage + c * (32 * 128)), head * HD + c * box_cols, y, it.b);
                     bulk_commit();
                     stores_pending = true;
                 }
                 __syncwarp();
             } else if (ok) {
                 const bool store = row_valid && my_written;
-                float *orow = p.out + static_cast<long long>(it.b) * p.out_batch_stride +
-                              static_cast<long long>(store ? row : 0) * p.out_row_stride +
-                              static_cast<long long>(head) * HD;
                 uint32_t rr[32];
 #pragma unroll
                 for (int c = 0; c < HD / 32; ++c) {
@@ -1077,13 +1133,8 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                         const long long off = static_cast<long long>(it.b) * p.out_batch_stride +
                                               static_cast<long long>(row) * p.out_row_stride +
                                               static_cast<long long>(head) * HD + c * 32;
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4) {
-                            float4 v = make_float4(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv,
-                                                   __uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
-                            *reinterpret_cast<float4 *>(orow + c * 32 + i) = v;
-                            for (int o = 0; o < p.n_more; ++o) *reinterpret_cast<float4 *>(p.out_more[o] + off + i) = v;
-                        }
+                        store_row32(p.out, off, rr, inv, p.out_bf16 != 0);
+                        for (int o = 0; o < p.n_more; ++o) store_row32(p.out_more[o], off, rr, inv, p.out_bf16 != 0);
                     }
                 }
             }
@@ -1154,12 +1205,12 @@ int prepare_v2(int dev)
 }
 
 template <int HD>
-int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t out_batch_stride,
+int launch_prefill(cudaStream_t st, void *out, int64_t out_row_stride, int64_t out_batch_stride,
                    const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride, const uint16_t *k,
                    int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
                    int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads, int n_kv_heads,
                    float scale, int mask_kind, int q_offset, int prefix_len, int window, float softcap,
-                   const int *window_starts, int n_windows, float *const *more_outs, int n_more)
+                   const int *window_starts, int n_windows, void *const *more_outs, int n_more, int out_bf16)
 {
     using S = PrefillShape<HD>;
     PrefillParams p;
@@ -1183,9 +1234,15 @@ int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t 
         return SMOL_B200_ERR_CUDA;
     {
         const int64_t ob = batch > 1 ? out_batch_stride : static_cast<int64_t>(seq_q) * out_row_stride;
-        if (!make_tmap_3d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, static_cast<int64_t>(n_heads) * HD, seq_q,
-                          batch, out_row_stride, ob, 32, 32, 4))
-            return SMOL_B200_ERR_CUDA;
+        const bool ok = out_bf16
+                            ? make_tmap_3d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                           static_cast<int64_t>(n_heads) * HD, seq_q, batch, out_row_stride, ob, 64,
+                                           32, 2)
+                            : make_tmap_3d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                           static_cast<int64_t>(n_heads) * HD, seq_q, batch, out_row_stride, ob, 32,
+                                           32, 4);
+        if (!ok) return SMOL_B200_ERR_CUDA;
+        p.out_bf16 = out_bf16 ? 1 : 0;
         p.n_more = n_more;
         for (int i = 0; i < n_more; ++i) p.out_more[i] = more_outs[i];
     }
@@ -1258,12 +1315,13 @@ int launch_prefill(cudaStream_t st, float *out, int64_t out_row_stride, int64_t 
 
 }  // namespace
 
-int prefill_attention(cudaStream_t st, float *out, int64_t out_row_stride, int64_t out_batch_stride,
+int prefill_attention(cudaStream_t st, void *out, int64_t out_row_stride, int64_t out_batch_stride,
                       const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride, const uint16_t *k,
                       int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
                       int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads, int n_kv_heads,
                       int head_dim, float scale, int mask_kind, int q_offset, int prefix_len, int window,
-                      float softcap, const int *window_starts, int n_windows, float *const *more_outs, int n_more)
+                      float softcap, const int *window_starts, int n_windows, void *const *more_outs, int n_more,
+                      int out_bf16)
 {
     if (batch <= 0 || seq_q <= 0) return SMOL_B200_OK;
     if (n_more < 0 || n_more > kMaxExtraOuts || (n_more > 0 && (!more_outs || head_dim == 256)))
@@ -1280,7 +1338,9 @@ int prefill_attention(cudaStream_t st, float *out, int64_t out_row_stride, int64
     if (align & 15) return SMOL_B200_ERR_ARGS;
     if ((q_row_stride | k_row_stride | v_row_stride) & 7) return SMOL_B200_ERR_ARGS;
     if (batch > 1 && ((q_batch_stride | k_batch_stride | v_batch_stride) & 7)) return SMOL_B200_ERR_ARGS;
-    if ((out_row_stride & 3) || (batch > 1 && (out_batch_stride & 3))) return SMOL_B200_ERR_ARGS;
+    // output rows and batches start on 16 bytes: 4 fp32 or 8 bf16 elements
+    const int64_t out_align = out_bf16 ? 7 : 3;
+    if ((out_row_stride & out_align) || (batch > 1 && (out_batch_stride & out_align))) return SMOL_B200_ERR_ARGS;
     if (q_row_stride < static_cast<int64_t>(n_heads) * head_dim ||
         k_row_stride < static_cast<int64_t>(n_kv_heads) * head_dim ||
         v_row_stride < static_cast<int64_t>(n_kv_heads) * head_dim)
@@ -1288,7 +1348,7 @@ int prefill_attention(cudaStream_t st, float *out, int64_t out_row_stride, int64
 #define SMOL_PREFILL_ARGS                                                                                      \
     st, out, out_row_stride, out_batch_stride, q, q_row_stride, q_batch_stride, k, k_row_stride, k_batch_stride, \
         v, v_row_stride, v_batch_stride, batch, seq_q, seq_k, n_heads, n_kv_heads, scale,      \
-        mask_kind, q_offset, prefix_len, window, softcap, window_starts, n_windows, more_outs, n_more
+        mask_kind, q_offset, prefix_len, window, softcap, window_starts, n_windows, more_outs, n_more, out_bf16
     switch (head_dim) {
     case 64: return launch_prefill<64>(SMOL_PREFILL_ARGS);
     case 128: return launch_prefill<128>(SMOL_PREFILL_ARGS);

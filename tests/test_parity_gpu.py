@@ -270,6 +270,40 @@ def test_qknorm_rope_append_matches_oracle(cuda):
         assert np.array_equal(vc.view(torch.int16).cpu().numpy().view(np.uint16), vc_o)
 
 
+def test_fp16_v_overflow_is_reported(cuda):
+    # The V cache is fp16 (largest finite 65504): a V value it cannot hold sets bit 6 of
+    # the device error word instead of being stored silently as infinity; the drop-in
+    # attention (which stages V as fp16) fails with SMOL_B200_ERR_RANGE and zeroes out.
+    n, hq, hkv, hd = 4, 2, 1, 64
+    q, k = torch.randn((n, hq * hd), device=cuda), torch.randn((n, hkv * hd), device=cuda)
+    v = torch.randn((n, hkv * hd), device=cuda)
+    kc = torch.zeros((n, hkv * hd), dtype=torch.bfloat16, device=cuda)
+    vc = torch.zeros((n, hkv * hd), dtype=torch.float16, device=cuda)
+    pos = torch.arange(n, dtype=torch.int32, device=cuda)
+    args = (n, hq, hkv, hd, None, None, 1e-6, None, None, False, pos, pos.to(torch.int64), None, None, kc, vc, n)
+    smol_b200.qknorm_rope_append(q, k, v, *args)
+    torch.cuda.synchronize()
+    assert smol_b200.device_error() == 0
+    v[2, 7] = 65519.0                                   # rounds to 65504: still fits
+    smol_b200.qknorm_rope_append(q, k, v, *args)
+    torch.cuda.synchronize()
+    assert smol_b200.device_error() == 0
+    v[1, 3] = -7.0e4
+    smol_b200.qknorm_rope_append(q, k, v, *args)
+    torch.cuda.synchronize()
+    assert smol_b200.device_error() == smol_b200.DEVERR_VALUE_RANGE
+    smol_b200.clear_error()
+    assert smol_b200.device_error() == 0
+    Q = np.ones((3, hq * hd), np.float32)
+    K = np.ones((3, hkv * hd), np.float32)
+    V = np.ones((3, hkv * hd), np.float32)
+    V[1, 0] = 1.0e5
+    out = np.full((3, hq * hd), 9.0, np.float32)
+    smol_b200.causal_attention(out, Q, K, V, 3, 3, hq, hkv, hd, 0.125, 0)
+    assert smol_b200.last_error() == 7 and not out.any()
+    smol_b200.clear_error()
+
+
 # ---------------------------------------------------------------------------
 # Batched split-KV decode
 # ---------------------------------------------------------------------------
@@ -445,6 +479,94 @@ def test_prefill_edges_vs_oracle(cuda, sq, sk, qo, hq, hkv, hd, win, cap):
     got = run_prefill(cuda, q, k, v, 1, sq, sk, hq, hkv, hd, 0.1, q_offset=qo, window=win, softcap=cap)
     want = pyoracle.oracle().causal_attention(q, k, v, sq, sk, hq, hkv, hd, 0.1, qo, window=win, cap=cap)
     assert_close(got[0], want, f"prefill {sq}x{sk} qo={qo} win={win} cap={cap}")
+
+
+@pytest.mark.parametrize("sq,cut,qo,hq,hkv,hd,win,cap", [
+    (299, 150, 0, 8, 1, 256, 64, 50.0),    # Gemma-2 shape: MQA hd 256 (v1 kernel), window + softcap
+    (400, 173, 37, 16, 8, 128, 64, 0.0),   # hd 128 (v2 kernel, paired heads), q_offset > 0
+    (333, 100, 5, 3, 1, 64, 100, 0.0),     # hd 64, odd GQA group (v2, consecutive row blocks)
+])
+def test_prefill_window_chunk_invariant(cuda, sq, cut, qo, hq, hkv, hd, win, cap):
+    # A chunked prefill under a sliding window (the second chunk continues at
+    # q_offset + cut) must write exactly what one call writes: streaming prefix reuse
+    # truncates the cache and prefills only the delta (qwen_asr.c:1599-1614).
+    rng = np.random.default_rng(sq + cut)
+    sk = qo + sq
+    q, k, v = rnd_bf16(rng, sq, hq * hd), rnd_bf16(rng, sk, hkv * hd), rnd_bf16(rng, sk, hkv * hd)
+    one = run_prefill(cuda, q, k, v, 1, sq, sk, hq, hkv, hd, 0.1, q_offset=qo, window=win, softcap=cap)[0]
+    a = run_prefill(cuda, q[:cut], k, v, 1, cut, qo + cut, hq, hkv, hd, 0.1, q_offset=qo, window=win,
+                    softcap=cap)[0]
+    b = run_prefill(cuda, q[cut:], k, v, 1, sq - cut, sk, hq, hkv, hd, 0.1, q_offset=qo + cut, window=win,
+                    softcap=cap)[0]
+    two = np.concatenate([a, b])
+    diff = np.abs(two - one)
+    assert np.array_equal(two, one), f"chunked != one call: max |d| {diff.max():.3e} at row {diff.max(1).argmax()}"
+    want = pyoracle.oracle().causal_attention(q, k, v, sq, sk, hq, hkv, hd, 0.1, qo, window=win, cap=cap)
+    assert_close(one, want, f"prefill window {win} qo={qo}")
+
+
+@pytest.mark.parametrize("hd,hq,hkv,mask", [(64, 4, 4, "windows"), (128, 8, 4, "causal"), (128, 3, 1, "full"),
+                                             (256, 8, 1, "prefix")])
+def test_prefill_bf16_output_is_rounded_fp32_output(cuda, hd, hq, hkv, mask):
+    # smol_b200_prefill_attention_bf16: the same result rounded to bf16 (nearest even),
+    # bit for bit, in a strided output; rows no window covers stay untouched.
+    rng = np.random.default_rng(hd + hq)
+    B, S = 2, 333
+    q, k, v = rnd_bf16(rng, B, S, hq * hd), rnd_bf16(rng, B, S, hkv * hd), rnd_bf16(rng, B, S, hkv * hd)
+    kw = {}
+    kind = {"windows": smol_b200.MASK_WINDOWS, "causal": smol_b200.MASK_CAUSAL, "full": smol_b200.MASK_FULL,
+            "prefix": smol_b200.MASK_PREFIX_LM}[mask]
+    if mask == "windows":
+        kw["window_starts"] = torch.tensor([5, 104, 208, 300], dtype=torch.int32, device=cuda)
+    if mask == "prefix":
+        kw["prefix_len"] = 200
+    ow = hq * hd + 8
+    strides = ((ow, S * ow), (hq * hd, S * hq * hd), (hkv * hd, S * hkv * hd), (hkv * hd, S * hkv * hd))
+    args = (dev_bf16(q, cuda), dev_bf16(k, cuda), dev_f16(v, cuda), B, S, S, hq, hkv, hd, 0.09)
+    out32 = torch.full((B, S, ow), 5.0, device=cuda)
+    smol_b200.prefill_attention(out32, *args, mask_kind=kind, strides=strides, **kw)
+    out16 = torch.full((B, S, ow), 5.0, device=cuda, dtype=torch.bfloat16)
+    smol_b200.prefill_attention(out16, *args, mask_kind=kind, strides=strides, **kw)
+    torch.cuda.synchronize()
+    no_error()
+    want = out32.to(torch.bfloat16)
+    assert torch.equal(out16.view(torch.int16), want.view(torch.int16)), \
+        float((out16.float() - want.float()).abs().max())
+    if mask == "windows":
+        assert bool((out16[:, :5].float() == 5.0).all()) and bool((out16[:, 300:].float() == 5.0).all())
+
+
+def test_bf16_decoder_reference_second_oracle(cuda):
+    # The reference's own bf16-cache attention (qkn_bf16_decoder.c:120-233: fp32 scores,
+    # two-pass softmax, output truncated to bf16; fixtures from
+    # tests/golden/make_bf16_golden.py) on the device path: seq_q > 1 through the tcgen05
+    # prefill, seq_q == 1 through the split-KV decode over a pool, with the PaliGemma
+    # decoder's settings (MQA 8/1, head dim 256, softcap 50, sliding window).  V goes in
+    # as fp16 (every bf16 value of these inputs is exact in fp16).  The device's fp32
+    # result must lie within 2e-3 relative (P in fp16, ex2.approx) or 1e-4 absolute of the
+    # interval each truncated reference value stands for.
+    import os
+
+    from conftest import assert_within_bf16_truncation
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "bf16_decoder_cases.npz"))
+    for name in sorted({k.split("/")[0] for k in g.files}):
+        sq, sk, hq, hkv, hd, qo, win = (int(x) for x in g[f"{name}/meta"])
+        scale, cap = (float(x) for x in g[f"{name}/fmeta"])
+        q, k, v = (pyoracle.bf16_to_f32(g[f"{name}/{t}_bf16"]) for t in ("q", "k", "v"))
+        if sq > 1:
+            got = run_prefill(cuda, q, k, v, 1, sq, sk, hq, hkv, hd, scale, q_offset=qo, window=win, softcap=cap)[0]
+        else:
+            assert qo == sk - 1
+            out = torch.zeros((1, hq * hd), device=cuda)
+            ws = torch.empty(smol_b200.decode_workspace_bytes(1, sk, hq, hkv, hd), dtype=torch.uint8, device=cuda)
+            smol_b200.decode_attention(out, dev_bf16(q, cuda), dev_bf16(k, cuda), dev_f16(v, cuda), sk,
+                                       torch.zeros(1, dtype=torch.int64, device=cuda),
+                                       torch.full((1,), sk, dtype=torch.int32, device=cuda), 1, sk, hq, hkv, hd,
+                                       scale, ws, window=win, softcap=cap)
+            torch.cuda.synchronize()
+            no_error()
+            got = out.cpu().numpy()
+        assert_within_bf16_truncation(got, g[f"{name}/out_bf16"], rel_tol=2e-3, abs_tol=1e-4, what=name)
 
 
 def test_prefill_batched_strided(cuda):
