@@ -667,15 +667,29 @@ int launch_decode(cudaStream_t st, float *out, const void *q, int q_is_bf16, con
 
 }  // namespace
 
+// Partials for any call whose max_kv_len is at most `max_kv_len`.  The chunk count of a
+// call, ceil(L / decode_chunk_size(L)), is not monotonic in L (the chunk grows in steps
+// of 64 keys), so the size is that of the largest count over [1, max_kv_len]:
+//   chunk == 64 (lower clamp)      count = ceil(L/64)       <= ceil(max/64)
+//   64 <= chunk < 2048             chunk >= W*L/1184, so count <= ceil(1184/W)
+//   chunk == SMOL_DECODE_MAX_CHUNK count = ceil(L/2048)     <= ceil(max/2048)
+// with W = n_seqs * n_kv_heads * Q-head groups (the work per key); the first two cases
+// together give min(ceil(max/64), ceil(1184/W)).  A workspace sized for max_kv_len
+// therefore serves every shorter call, as a decoder that sizes it once for its cache
+// capacity relies on.
 size_t decode_workspace_bytes(int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, int head_dim)
 {
     if (n_seqs <= 0 || n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0) return 0;
     const int group = n_heads / n_kv_heads;
-    const int nq = (group + 7) / 8;
-    const int chunk = decode_chunk_size(n_seqs, max_kv_len, n_kv_heads, nq);
-    int max_chunks = (max_kv_len + chunk - 1) / chunk;
+    const long long w = static_cast<long long>(n_seqs) * n_kv_heads * ((group + 7) / 8);
+    const long long len = max_kv_len > 0 ? max_kv_len : 1;
+    long long small = (len + kKeysPerTile - 1) / kKeysPerTile;
+    const long long by_work = (148 * 8 + w - 1) / w;
+    if (small > by_work) small = by_work;
+    const long long big = (len + SMOL_DECODE_MAX_CHUNK - 1) / SMOL_DECODE_MAX_CHUNK;
+    long long max_chunks = small > big ? small : big;
     if (max_chunks < 1) max_chunks = 1;
-    const size_t n_items = static_cast<size_t>(n_seqs) * n_heads * max_chunks;
+    const size_t n_items = static_cast<size_t>(n_seqs) * n_heads * static_cast<size_t>(max_chunks);
     return n_items * (static_cast<size_t>(head_dim) + 2) * sizeof(float);
 }
 

@@ -4,6 +4,7 @@
 // (common/kernels/threading.c:26-47).  The equivalent here is one context per
 // CUDA device holding the stream and the grow-only scratch the drop-in entry
 // points stage through, plus the device error word that bounded waits write.
+#include <atomic>
 #include <mutex>
 #include <stdio.h>
 #include <stdlib.h>
@@ -26,7 +27,9 @@ constexpr int kMaxDevices = 16;
 constexpr int kScratchSlots = 8;
 
 struct DeviceCtx {
-    bool init = false;
+    // Set (release) after err_word and stream; read (acquire) without the lock, so a
+    // reader that sees it set also sees both.
+    std::atomic<bool> init{false};
     unsigned *err_word = nullptr;
     cudaStream_t stream = nullptr;
     void *scratch[kScratchSlots] = {};
@@ -53,14 +56,14 @@ DeviceCtx *ctx_for_current()
     const int dev = current_device();
     if (dev < 0) return nullptr;
     DeviceCtx &c = g_ctx[dev];
-    if (!c.init) {
+    if (!c.init.load(std::memory_order_acquire)) {
         std::lock_guard<std::mutex> lock(g_mutex);
-        if (!c.init) {
+        if (!c.init.load(std::memory_order_relaxed)) {
             if (!cuda_check(cudaMalloc(&c.err_word, sizeof(unsigned)), "cudaMalloc(error word)")) return nullptr;
             if (!cuda_check(cudaMemset(c.err_word, 0, sizeof(unsigned)), "cudaMemset(error word)")) return nullptr;
             if (!cuda_check(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking), "cudaStreamCreate"))
                 return nullptr;
-            c.init = true;
+            c.init.store(true, std::memory_order_release);
         }
     }
     return &c;
@@ -180,7 +183,7 @@ unsigned *device_error_word_if_created()
         cudaGetLastError();
         return nullptr;
     }
-    return g_ctx[dev].init ? g_ctx[dev].err_word : nullptr;
+    return g_ctx[dev].init.load(std::memory_order_acquire) ? g_ctx[dev].err_word : nullptr;
 }
 
 cudaStream_t legacy_stream()
@@ -282,6 +285,7 @@ const char *smol_cuda_error_string(int code)
     case SMOL_B200_ERR_OOM: return "device out of memory";
     case SMOL_B200_ERR_WATCHDOG: return "a kernel wait ran out of time";
     case SMOL_B200_ERR_WORKSPACE: return "workspace too small";
+    case SMOL_B200_ERR_RANGE: return "a value outside the range of its storage format";
     default: return "unknown error";
     }
 }
@@ -292,7 +296,7 @@ void smol_cuda_clear_error(void)
     smolb200::g_reported = false;
     int dev = -1;
     if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < smolb200::kMaxDevices &&
-        smolb200::g_ctx[dev].init) {
+        smolb200::g_ctx[dev].init.load(std::memory_order_acquire)) {
         cudaMemset(smolb200::g_ctx[dev].err_word, 0, sizeof(unsigned));
         cudaDeviceSynchronize();
     }

@@ -72,10 +72,14 @@ def test_dropin_prototypes_match_reference():
         assert ours.get(name) == sig, (name, ours.get(name), sig)
 
 
-@pytest.mark.skipif(not os.path.exists("/root/reference/common/kernels/smol_kernels.h"),
-                    reason="reference checkout not present")
+REF_HEADER = os.path.join(os.environ.get("SMOL_REFERENCE_DIR") or
+                          os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                                       "reference"), "common", "kernels", "smol_kernels.h")
+
+
+@pytest.mark.skipif(not os.path.exists(REF_HEADER), reason="reference checkout not present ($SMOL_REFERENCE_DIR)")
 def test_dropin_prototypes_match_reference_header_file():
-    ref = prototypes(open("/root/reference/common/kernels/smol_kernels.h").read())
+    ref = prototypes(open(REF_HEADER).read())
     ours = prototypes(open(smol_b200.HEADER_PATH).read())
     for name in prototypes(REFERENCE_PROTOTYPES):
         assert ours[name] == ref[name], name
@@ -83,7 +87,7 @@ def test_dropin_prototypes_match_reference_header_file():
 
 def test_error_strings():
     lib = smol_b200.lib()
-    for code in range(7):
+    for code in range(8):
         assert lib.smol_cuda_error_string(code)
     assert lib.smol_cuda_error_string(0) == b"ok"
 
@@ -94,6 +98,30 @@ def test_workspace_sizes():
     assert 0 < a < b
     assert smol_b200.decode_workspace_bytes(1, 0, 16, 8, 128) > 0
     assert smol_b200.decode_step_scratch_bytes(256, 8192, 16, 8, 128) > a
+
+
+def _decode_call_bytes(n_seqs, L, n_heads, n_kv_heads, hd):
+    """Partials one decode call of max_kv_len L writes: the library's chunk rule (about
+    8 CTAs per SM of 148, multiples of 64 keys, at most 2048) restated."""
+    w = n_seqs * n_kv_heads * ((n_heads // n_kv_heads + 7) // 8)
+    c = -(-w * max(L, 1) // (148 * 8))
+    c = min(max(-(-c // 64) * 64, 64), 2048)
+    return n_seqs * n_heads * max(-(-L // c), 1) * (hd + 2) * 4
+
+
+@pytest.mark.parametrize("n_seqs,n_heads,n_kv_heads,hd", [(1, 16, 8, 128), (1, 8, 1, 256), (3, 12, 12, 64),
+                                                          (256, 16, 8, 128)])
+def test_decode_workspace_never_shrinks(n_seqs, n_heads, n_kv_heads, hd):
+    """A workspace sized once for a cache capacity must serve every shorter call: the
+    chunk grows in steps of 64 keys, so a call's own partial count is not monotonic in
+    its length (Qwen3 shapes, one sequence: 9409 keys need more than 9600 would)."""
+    prev = 0
+    lens = list(range(1, 20001, 7)) + [9409, 9472, 9600, 20000, 65536, 300000]
+    for L in sorted(set(lens)):
+        got = smol_b200.decode_workspace_bytes(n_seqs, L, n_heads, n_kv_heads, hd)
+        assert got >= prev, (L, got, prev)
+        assert got >= _decode_call_bytes(n_seqs, L, n_heads, n_kv_heads, hd), L
+        prev = got
 
 
 def _siglip_model(**over):
@@ -136,10 +164,11 @@ def test_siglip_workspace_sizes_and_shape_checks():
     call would return SMOL_B200_ERR_ARGS) for shapes the device path does not take."""
     one = smol_b200.siglip_workspace_bytes(_siglip_model(), 1)
     assert one > 0 and smol_b200.siglip_workspace_bytes(_siglip_model(), 4) > 3 * one
-    # per image: unfolded patches, 4 bf16 activations and a bf16 copy of the attention
-    # output, the fp32 attention output, the bf16 fc1 output (1024 patches)
+    # per image: unfolded patches, 4 bf16 activations and the bf16 attention output (the
+    # prefill kernel writes it in bf16 for the output projection), the bf16 fc1 output
+    # (1024 patches)
     T = 1024
-    assert one >= T * (768 * 2 + 5 * 768 * 2 + 768 * 4 + 3072 * 2)
+    assert one >= T * (768 * 2 + 5 * 768 * 2 + 3072 * 2)
     assert smol_b200.siglip_workspace_bytes(_siglip_model(heads=16), 1) == 0           # head dim 48
     assert smol_b200.siglip_workspace_bytes(_siglip_model(num_positions=1000), 1) == 0  # fewer positions than patches
     assert smol_b200.siglip_workspace_bytes(_siglip_model(patch_ld=770), 1) == 0       # stride not a multiple of 8
