@@ -2,23 +2,29 @@
 """bench.py -- decode-attention KV GB/s of BASELINE cfg 2 on 1..8 B200s (+ prefill TFLOP/s).
 
 Workload: one batched decode step of a Qwen3-ASR-1.7B-shaped
-decoder over 28 layers -- 256 independent sequences per GPU, KV lengths drawn
-uniformly from [1024, 8192] (seed 0), 16 Q / 8 KV heads, head_dim 128, RoPE theta 1e6,
-bf16 K / fp16 V cache ~N(0,1).  Per layer the step runs the fused QK-RMSNorm + RoPE +
+decoder over 28 layers -- 256 independent sequences, KV lengths drawn uniformly from
+[1024, 8192] (seed 0), 16 Q / 8 KV heads, head_dim 128, RoPE theta 1e6, bf16 K / fp16 V
+cache ~N(0,1).  With N GPUs the fixed batch of 256 is split by KV bytes (greedy
+longest-first, workload.shard_by_bytes): strong scaling, `value` = all 256 sequences'
+KV bytes / the slowest rank's step time.  Per layer the step runs the fused QK-RMSNorm + RoPE +
 cache-append kernel for the new token of every sequence and the split-KV decode
 attention over [0, L+1).  Synthetic data; the cache (~135 GB) is far larger than L2,
 so no flush is needed between steps.
 
 Arms
-  default            libsmol_b200 on N GPUs (one process per GPU; weak scaling: every
-                     rank owns its own 256 sequences, no collective on the data path)
+  default            libsmol_b200 on N GPUs (one process per GPU; the 256 sequences are
+                     sharded across the ranks, no collective on the data path;
+                     --scaling weak gives every rank its own 256 instead)
   --impl reference   the reference's own CPU implementation (oracle/_ref, compiled
                      from the reference sources) on the host cores, rank 0 only
 
 The JSON line carries `value` (device-timed, inputs resident), `e2e` (the same step
 through the C ABI with host buffers: H2D of q/k/v and D2H of the output inside the
-timed region), `roofline` of the decode kernel pair, `cpu_baseline`, `clocks`, and a
-`prefill` block with the cfg 5 causal prefill TFLOP/s (one layer, batch 4 x 32768).
+timed region), `roofline` of the decode kernel pair, `cpu_baseline`, `clocks`, a
+`prefill` block with the cfg 5 causal prefill TFLOP/s (one layer, batch 4 x 32768,
+KV heads split across the ranks with one all-gather of the outputs), and
+`other_configs`: cfg 3 (128 images split by image) and cfg 4 (32 sequences split by
+sequence) at every N, and at N = 1 also cfg 1 and the device decoder step.
 """
 from __future__ import annotations
 
@@ -56,7 +62,10 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline sample budget in seconds (--impl reference: the cap per step)")
-    ap.add_argument("--seqs", type=int, default=workload.CFG2["n_seqs"], help="sequences per GPU")
+    ap.add_argument("--seqs", type=int, default=workload.CFG2["n_seqs"],
+                    help="sequences of the cfg 2 batch (split across the GPUs; per GPU with --scaling weak)")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="strong: one fixed batch split across the GPUs (BASELINE cfg 2); weak: every GPU its own")
     ap.add_argument("--layers", type=int, default=workload.CFG2["layers"])
     ap.add_argument("--no-decode", action="store_true", help="prefill measurement only (profiling helper)")
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg 1/3/4 block")
@@ -307,7 +316,7 @@ def run_reference(args):
             vals.append(cb["value"])
     v = statistics.median(vals)
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": args.scaling,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "cfg2 batched decode attention (reference CPU, sampled sequences)",
                        "lengths": "U[1024,8192] seed 0", "heads": "16/8", "head_dim": 128},
@@ -347,8 +356,10 @@ def run_prefill(args, world, rank, pk):
     q = torch.randn((B, L, hq_r * hd), device="cuda", generator=g).to(torch.bfloat16)
     k = torch.randn((B, L, hkv_r * hd), device="cuda", generator=g).to(torch.bfloat16)
     v = torch.randn((B, L, hkv_r * hd), device="cuda", generator=g).to(torch.float16)
-    out = torch.empty((B, L, hq_r * hd), device="cuda")
-    gathered = torch.empty((world,) + tuple(out.shape), device="cuda") if world > 1 else None
+    # bf16 output: the consumer (the output projection) takes bf16 operands, and the
+    # all-gather moves 2 bytes per element
+    out = torch.empty((B, L, hq_r * hd), device="cuda", dtype=torch.bfloat16)
+    gathered = torch.empty((world,) + tuple(out.shape), device="cuda", dtype=out.dtype) if world > 1 else None
     stream = torch.cuda.current_stream()
     scale = 1 / np.sqrt(hd)
     # Measured on one box (ms per layer, fused vs NCCL): 4 GPUs 4.37 vs 5.56, 8 GPUs 2.72 vs 3.71.
@@ -365,7 +376,7 @@ def run_prefill(args, world, rank, pk):
         allmeta = torch.empty(world * 72, dtype=torch.uint8, device="cuda")
         dist.all_gather_into_tensor(allmeta, meta)
         allmeta = allmeta.cpu().numpy().reshape(world, 72)
-        slot = out.numel() * 4
+        slot = out.numel() * out.element_size()
         bases = []
         for peer in range(world):
             if peer == rank:
@@ -379,7 +390,7 @@ def run_prefill(args, world, rank, pk):
     def layer():
         if fused:
             smol_b200.prefill_attention_multi(outs, hq_r * hd, L * hq_r * hd, q, k, v, B, L, L, hq_r, hkv_r, hd, scale,
-                                              stream=stream)
+                                              stream=stream, bf16=True)
             dist.all_reduce(sync_t)   # device-side barrier: every rank's stores have landed
         else:
             smol_b200.prefill_attention(out, q, k, v, B, L, L, hq_r, hkv_r, hd, scale, stream=stream)
@@ -418,8 +429,10 @@ def run_prefill(args, world, rank, pk):
               (f", KV heads split over {world} GPUs; outputs all-gathered inside the prefill kernel (every output "
                "row stored to each peer's buffer over NVLink, CUDA IPC)" if fused
                else f", KV heads split over {world} GPUs + NCCL all-gather"))
-    return {"workload": f"cfg5 causal prefill, 1 layer, batch {B} x {L}, GQA 16/8, hd 128" + gather,
+    return {"workload": f"cfg5 causal prefill, 1 layer, batch {B} x {L}, GQA 16/8, hd 128, bf16 output" + gather,
             "gather_matches_nccl": check,
+            "gather_bytes_per_layer": (world - 1) * world * out.numel() * out.element_size(),
+            "gather_bytes_per_gpu_out": (world - 1) * out.numel() * out.element_size(),
             "tflops": round(tf, 1), "ms_per_layer": round(ms, 3), "flops_per_layer": flops,
             "frac_of_bf16_peak": round(tf / world / pk["bf16_tflops"], 4), "per_gpu_tflops": round(tf / world, 1),
             "peak": pk["bf16_tflops"], "peak_source": pk["source"], "kernel": "tcgen05 prefill2_kernel<128>"}
@@ -518,19 +531,23 @@ def run_cfg1() -> dict:
                     "loop (append + split + combine per step) each replayed as one CUDA graph"}
 
 
-def run_cfg3(pk, images: int | None = None, layers: int | None = None) -> dict:
-    """cfg 3: SigLIP attention, 128 images x 12 layers, 1024 patches, 12 heads, hd 64."""
+def run_cfg3(pk, images: int | None = None, layers: int | None = None, world: int = 1, rank: int = 0) -> dict:
+    """cfg 3: SigLIP attention, 128 images x 12 layers, 1024 patches, 12 heads, hd 64.
+    With N GPUs rank r attends images workload.shard_evenly(128, N, r); the time is the
+    slowest rank's and the TFLOP/s count all 128 images."""
     import torch
 
     import smol_b200
     ev = _ev
-    g = torch.Generator(device="cuda").manual_seed(13)
+    g = torch.Generator(device="cuda").manual_seed(13 + rank)
     c = dict(workload.CFG3)
     if images:
         c["images"] = images
     if layers:
         c["layers"] = layers
-    B, N, h3, hd3 = c["images"], c["patches"], c["n_heads"], c["head_dim"]
+    total_images = c["images"]
+    B = len(workload.shard_evenly(total_images, world, rank))
+    N, h3, hd3 = c["patches"], c["n_heads"], c["head_dim"]
     q3 = torch.randn((B, N, h3 * hd3), device="cuda", generator=g).to(torch.bfloat16)
     k3 = torch.randn((B, N, h3 * hd3), device="cuda", generator=g).to(torch.bfloat16)
     v3 = torch.randn((B, N, h3 * hd3), device="cuda", generator=g).to(torch.float16)
@@ -542,15 +559,19 @@ def run_cfg3(pk, images: int | None = None, layers: int | None = None) -> dict:
         for _ in range(c["layers"]):
             smol_b200.prefill_attention(o3, q3, k3, v3, B, N, N, h3, h3, hd3, 1 / 8.0, mask_kind=smol_b200.MASK_FULL)
     siglip()
+    torch.cuda.synchronize()
+    barrier(world)
     a.record()
     siglip()
     b.record()
     torch.cuda.synchronize()
-    ms3 = a.elapsed_time(b)
-    fl3 = workload.full_flops(N, h3, hd3) * B * c["layers"]
-    return {"workload": f"{B} images x {c['layers']} layers", "ms": round(ms3, 3),
-            "tflops": round(fl3 / (ms3 * 1e-3) / 1e12, 1),
-            "frac_of_bf16_peak": round(fl3 / (ms3 * 1e-3) / 1e12 / pk["bf16_tflops"], 4),
+    ms3 = allreduce_max(a.elapsed_time(b), world)
+    fl3 = workload.full_flops(N, h3, hd3) * total_images * c["layers"]
+    tf = fl3 / (ms3 * 1e-3) / 1e12
+    return {"workload": f"{total_images} images x {c['layers']} layers" +
+                        (f", {B} images per GPU on {world} GPUs (split by image, no collective)" if world > 1 else ""),
+            "ms": round(ms3, 3), "tflops": round(tf, 1),
+            "frac_of_bf16_peak": round(tf / world / pk["bf16_tflops"], 4),
             "flops": fl3, "kernel": "prefill2_kernel<64> (full mask)"}
 
 
@@ -635,16 +656,19 @@ def run_siglip_encoder(pk, images: int | None = None) -> dict:
             "kernels": "gemm_bf16_kernel (tcgen05), prefill2_kernel<64>, layer_norm_kernel, unfold / convert"}
 
 
-def run_cfg4() -> dict:
-    """cfg 4: PaliGemma prefix-LM, batch 32, 18 layers, MQA 8/1, hd 256; 128-step suffix."""
+def run_cfg4(pk=None, world: int = 1, rank: int = 0) -> dict:
+    """cfg 4: PaliGemma prefix-LM, batch 32, 18 layers, MQA 8/1, hd 256; 128-step suffix.
+    With N GPUs rank r owns sequences workload.shard_evenly(32, N, r); times are the
+    slowest rank's, FLOPs and bytes count all 32 sequences."""
     import torch
 
     import smol_b200
     ev = _ev
-    g = torch.Generator(device="cuda").manual_seed(17)
+    g = torch.Generator(device="cuda").manual_seed(17 + rank)
     c = workload.CFG4
-    B4, P4, S4, h4, hkv4, hd4, L4 = c["batch"], c["prefix"], c["suffix"], c["n_heads"], c["n_kv_heads"], \
-        c["head_dim"], c["layers"]
+    P4, S4, h4, hkv4, hd4, L4 = c["prefix"], c["suffix"], c["n_heads"], c["n_kv_heads"], c["head_dim"], c["layers"]
+    B_all = c["batch"]
+    B4 = len(workload.shard_evenly(B_all, world, rank))
     tot = P4 + S4
     kv4 = hkv4 * hd4
     q4 = torch.randn((B4, P4, h4 * hd4), device="cuda", generator=g).to(torch.bfloat16)
@@ -663,12 +687,14 @@ def run_cfg4() -> dict:
                                         strides=((h4 * hd4, P4 * h4 * hd4), (h4 * hd4, P4 * h4 * hd4),
                                                  (kv4, tot * kv4), (kv4, tot * kv4)))
     prefix()
+    torch.cuda.synchronize()
+    barrier(world)
     a.record()
     prefix()
     b.record()
     torch.cuda.synchronize()
-    ms4 = a.elapsed_time(b)
-    fl4 = workload.prefix_lm_flops(P4, P4, h4, hd4) * B4 * L4
+    ms4 = allreduce_max(a.elapsed_time(b), world)
+    fl4 = workload.prefix_lm_flops(P4, P4, h4, hd4) * B_all * L4
     qd = torch.randn((B4, h4 * hd4), device="cuda", generator=g)
     od = torch.empty_like(qd)
     r04 = [torch.arange(B4, dtype=torch.int64, device="cuda") * tot + layer * B4 * tot for layer in range(L4)]
@@ -680,14 +706,26 @@ def run_cfg4() -> dict:
             for layer in range(L4):
                 smol_b200.decode_attention(od, qd, kp4, vp4, L4 * B4 * tot, r04[layer], lens4[t], B4, tot, h4, hkv4,
                                            hd4, 1 / 16.0, ws4)
-    ms_s = _time_graph(_graph(suffix), 3)
-    suf_bytes = sum(B4 * (P4 + t + 1) * kv4 * 2 * 2 for t in range(S4)) * L4
+    graph = _graph(suffix)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms_s = allreduce_max(_time_graph(graph, 3), world)
+    del graph
+    suf_bytes = sum(B_all * (P4 + t + 1) * kv4 * 2 * 2 for t in range(S4)) * L4
     smol_b200.check(smol_b200.last_error(), "cfg4")
-    return {"prefix_ms_18_layers": round(ms4, 3), "prefix_tflops": round(fl4 / (ms4 * 1e-3) / 1e12, 1),
-            "suffix_128_steps_ms": round(ms_s, 2), "suffix_step_us": round(ms_s * 1e3 / S4, 1),
-            "suffix_kv_gbs": round(suf_bytes / (ms_s * 1e-3) / 1e9, 1),
-            "kernels": "prefill_kernel<256> (prefix-LM mask) + decode_split_kernel<256> (MQA group 8); "
-                       "the 128-step x 18-layer suffix replayed as one CUDA graph"}
+    tf = fl4 / (ms4 * 1e-3) / 1e12
+    gbs = suf_bytes / (ms_s * 1e-3) / 1e9
+    res = {"prefix_ms_18_layers": round(ms4, 3), "prefix_tflops": round(tf, 1),
+           "suffix_128_steps_ms": round(ms_s, 2), "suffix_step_us": round(ms_s * 1e3 / S4, 1),
+           "suffix_kv_gbs": round(gbs, 1),
+           "kernels": "prefill_kernel<256> (prefix-LM mask) + decode_split_kernel<256> (MQA group 8); "
+                      "the 128-step x 18-layer suffix replayed as one CUDA graph"}
+    if pk is not None:
+        res["prefix_frac_of_bf16_peak"] = round(tf / world / pk["bf16_tflops"], 4)
+        res["suffix_hbm_frac"] = round(gbs / world / pk["hbm_gbs"], 4)
+    if world > 1:
+        res["workload"] = f"{B_all} sequences, {B4} per GPU on {world} GPUs (split by sequence, no collective)"
+    return res
 
 
 def run_decoder(pk, batch: int = 1, steps: int = 50) -> dict:
@@ -877,14 +915,20 @@ def run_decoder_dropin(layers: int = 2) -> dict:
             "tokens_equal": res["ref"]["tokens"] == res["device"]["tokens"]}
 
 
-def run_other_configs(pk) -> dict:
-    """The remaining BASELINE configs on one GPU (latency- or tensor-bound; not the headline).
+def run_other_configs(pk, world: int = 1, rank: int = 0) -> dict:
+    """The remaining BASELINE configs (latency- or tensor-bound; not the headline).
 
-    Each runs on its own: a library error in one is reported in its entry ("error")
-    and does not stop the others or the headline measurement."""
+    cfg 3 and cfg 4 shard across the ranks (by image, by sequence) and report the
+    slowest rank's time; cfg 1 (batch 1, replicas only) and the decoder step run at
+    N = 1 only.  Each runs on its own: a library error in one is reported in its entry
+    ("error") and does not stop the others or the headline measurement.  Every rank
+    runs the same list, so the collectives inside line up."""
     import smol_b200
-    runs = {"cfg1": run_cfg1, "cfg3": lambda: run_cfg3(pk), "cfg4": run_cfg4,
-            "decoder_step_b1": lambda: run_decoder(pk, 1), "decoder_step_b8": lambda: run_decoder(pk, 8)}
+    runs = {"cfg3": lambda: run_cfg3(pk, world=world, rank=rank),
+            "cfg4": lambda: run_cfg4(pk, world=world, rank=rank)}
+    if world == 1:
+        runs = {"cfg1": run_cfg1, **runs,
+                "decoder_step_b1": lambda: run_decoder(pk, 1), "decoder_step_b8": lambda: run_decoder(pk, 8)}
     res = {}
     for name, fn in runs.items():
         smol_b200.clear_error()
@@ -906,18 +950,27 @@ def run_ours(args):
     cfg = workload.CFG2
     hq, hkv, hd, layers = cfg["n_heads"], cfg["n_kv_heads"], cfg["head_dim"], args.layers
     kv_dim = hkv * hd
-    n = args.seqs
-    lens = workload.decode_lengths(n, cfg["len_lo"], cfg["len_hi"], seed=0)   # same per rank: equal work
+    lens_all = workload.decode_lengths(args.seqs, cfg["len_lo"], cfg["len_hi"], seed=0)
+    if args.scaling == "strong":
+        # BASELINE cfg 2: one batch of 256 split by KV bytes; no data crosses ranks
+        mine = workload.shard_by_bytes(lens_all, world)[rank]
+        job_lens = lens_all
+    else:
+        mine = np.arange(args.seqs)
+        job_lens = np.tile(lens_all, world)
+    lens = lens_all[mine]
+    n = len(lens)
     lay = workload.pool_layout(lens, layers, reserve=1)
     max_len = int(lens.max())
+    kv_bytes_job = workload.pool_layout(job_lens, layers, reserve=1).kv_bytes(kv_dim, extra_tokens=1)
 
     prefill = None
     if not args.no_prefill:
         prefill = run_prefill(args, world, rank, pk)
         torch.cuda.empty_cache()
     others = None
-    if world == 1 and not args.no_configs and not args.no_decode:
-        others = run_other_configs(pk)
+    if not args.no_configs and not args.no_decode:
+        others = run_other_configs(pk, world, rank)
         torch.cuda.empty_cache()
     if args.no_decode:
         if rank == 0:
@@ -990,7 +1043,22 @@ def run_ours(args):
         raise SystemExit(f"kernel error: device word {dev_err}, last error {smol_b200.last_error()}")
 
     kv_bytes_rank = lay.kv_bytes(kv_dim, extra_tokens=1)          # attends L+1 per layer
-    value = world * kv_bytes_rank / (ms_step * 1e-3) / 1e9
+    value = kv_bytes_job / (ms_step * 1e-3) / 1e9                  # whole job / slowest rank
+    ms_rank = ms_total / args.steps                                 # this rank's own step time
+    rank_ms = [0.0] * world
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.zeros(world, dtype=torch.float64, device="cuda")
+        t[rank] = ms_rank
+        dist.all_reduce(t)
+        rank_ms = [float(x) for x in t.cpu()]
+        rank_bytes = torch.zeros(world, dtype=torch.float64, device="cuda")
+        rank_bytes[rank] = float(kv_bytes_rank)
+        dist.all_reduce(rank_bytes)
+        rank_bytes = [float(x) for x in rank_bytes.cpu()]
+    else:
+        rank_ms = [ms_rank]
+        rank_bytes = [float(kv_bytes_rank)]
     # roofline of the decode kernel pair (split-KV + combine), live CUDA events
     dec_ms = statistics.mean(a.elapsed_time(b) for a, b in kv_events)
     qo_bytes = n * hq * hd * 4 * 2                                 # fp32 q read + fp32 out write
@@ -1031,10 +1099,11 @@ def run_ours(args):
         e1.record(stream)
         torch.cuda.synchronize()
         e2e_ms = allreduce_max(e0.elapsed_time(e1) / args.steps, world)
-        e2e = {"value": round(world * kv_bytes_rank / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
+        e2e = {"value": round(kv_bytes_job / (e2e_ms * 1e-3) / 1e9, 2), "unit": UNIT,
                "ms_per_step": round(e2e_ms, 3),
-               "h2d_bytes_per_step": layers * (qh.numel() + kh.numel() + vh.numel()) * 4,
-               "d2h_bytes_per_step": layers * oh.numel() * 4,
+               "h2d_bytes_per_step": world * layers * (qh.numel() + kh.numel() + vh.numel()) * 4 if
+               args.scaling == "weak" else len(lens_all) * layers * (hq * hd + 2 * kv_dim) * 4,
+               "d2h_bytes_per_step": (world * n if args.scaling == "weak" else len(lens_all)) * layers * hq * hd * 4,
                "api": "smol_b200_decode_step_host (pinned host q/k/v in, host out; 28 calls per step)"}
         smol_b200.check(smol_b200.last_error(), "e2e")
 
@@ -1049,24 +1118,33 @@ def run_ours(args):
 
     if rank != 0:
         return
+    strong = args.scaling == "strong"
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "cfg2: batched decode attention step, 28 layers x 256 sequences per GPU, "
-                               "KV len ~U[1024,8192] seed 0, GQA 16/8, hd 128, theta 1e6, QK-norm+RoPE+append fused",
-                   "global_batch": n * world, "layers": layers, "kv_cache": "K bf16 / V fp16, pooled in HBM",
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+        "scaling": args.scaling, "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": ("cfg2: batched decode attention step, 28 layers x 256 sequences "
+                                + ("split across the GPUs by KV bytes" if strong else "per GPU")
+                                + ", KV len ~U[1024,8192] seed 0, GQA 16/8, hd 128, theta 1e6, "
+                                  "QK-norm+RoPE+append fused"),
+                   "global_batch": len(job_lens), "layers": layers, "kv_cache": "K bf16 / V fp16, pooled in HBM",
                    "parallelism": f"dp{world} (sequences sharded, no collective)",
                    "l2": "cache of %.1f GB per GPU >> 126 MB L2: no flush needed" % (2 * lay.rows * kv_dim * 2 / 1e9)},
-        "kv_bytes_per_step": world * kv_bytes_rank,
+        "kv_bytes_per_step": kv_bytes_job,
         "hbm_frac": round(value / world / pk["hbm_gbs"], 4),
+        "shards": {"sequences_per_rank": ([len(x) for x in workload.shard_by_bytes(lens_all, world)] if strong
+                                          else [len(lens_all)] * world), "rank_ms_per_step": [round(x, 4) for x in rank_ms],
+                   "rank_kv_bytes": [int(x) for x in rank_bytes],
+                   "balance": round(min(rank_bytes) / max(rank_bytes), 4),
+                   "limit": ("slowest rank: the byte split leaves at most one sequence's bytes of imbalance, and "
+                             "each rank keeps the per-layer fixed cost of its launches")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": int(traffic_launch),
                      "traffic_source": "ncu dram bytes of the 16-seq 1-layer case x (full / small algorithmic bytes)",
                      "kernel": "decode_split_kernel<128> + decode_combine_kernel<128> (per layer)",
                      "alg_bytes_per_launch": int(alg_bytes_launch), "ms_per_launch": round(dec_ms, 4),
                      "peak_source": pk["source"]},
-        "gpu_launches": args.steps * layers * 3,
+        "gpu_launches": args.steps * layers * 3,   # append + split + combine per layer (n >= 32 never clusters)
         "e2e": e2e,
         "cpu_baseline": None if cpu is None else {k: (round(v, 3) if isinstance(v, float) else v)
                                                   for k, v in cpu.items()},

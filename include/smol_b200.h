@@ -113,15 +113,23 @@ enum {
     SMOL_B200_ERR_NO_DEVICE = 3,     /* no sm_100 device visible                       */
     SMOL_B200_ERR_OOM = 4,           /* device allocation failed                       */
     SMOL_B200_ERR_WATCHDOG = 5,      /* a kernel's bounded wait ran out (see device word) */
-    SMOL_B200_ERR_WORKSPACE = 6      /* caller's workspace smaller than required        */
+    SMOL_B200_ERR_WORKSPACE = 6,     /* caller's workspace smaller than required        */
+    SMOL_B200_ERR_RANGE = 7          /* a value too large for fp16 V storage (see device word) */
 };
 
 /* Last error recorded by any call on this thread's process (sticky until cleared). */
 SMOL_B200_API int smol_cuda_last_error(void);
 SMOL_B200_API const char *smol_cuda_error_string(int code);
 SMOL_B200_API void smol_cuda_clear_error(void);
-/* Device error word of the current device: bits set by kernels whose bounded waits
- * ran out (0 = none).  Synchronises the device.  Cleared by smol_cuda_clear_error. */
+/* Device error word of the current device (0 = none), bits set by kernels:
+ *   bits 0-4  a bounded wait ran out (TMA tile, free stage, tcgen05 commit, P / O,
+ *             drain);
+ *   bit 5     a kernel saw arguments its host wrapper should have rejected;
+ *   bit 6     a value stored as fp16 (the V cache, fp16 GEMM outputs) had
+ *             |x| >= 65520 and became infinity.
+ * Synchronises the device.  Cleared by smol_cuda_clear_error.  The drop-in entry
+ * points of Part 1 read it after every call (SMOL_B200_ERR_RANGE for bit 6 alone,
+ * SMOL_B200_ERR_WATCHDOG otherwise). */
 SMOL_B200_API unsigned smol_cuda_device_error(void);
 /* Self test of the bounded waits: launches one kernel that waits on an mbarrier
  * nothing arrives on.  After about 2 s the wait gives up, sets bit 0 of the device
@@ -227,6 +235,28 @@ SMOL_B200_API int smol_b200_prefill_attention(
  * out_list is a host array.  Head dims 64 and 128 (the tcgen05 two-tile kernel). */
 SMOL_B200_API int smol_b200_prefill_attention_multi(
     void *stream, float *const *out_list, int n_out, int64_t out_row_stride,
+    int64_t out_batch_stride, const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride,
+    const uint16_t *k, int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v,
+    int64_t v_row_stride, int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads,
+    int n_kv_heads, int head_dim, float scale, int mask_kind, int q_offset, int prefix_len,
+    int window, float softcap, const int *window_starts, int n_windows);
+
+/* The two calls above with a bf16 output (rounded to nearest even from the fp32
+ * result) instead of fp32: out / out_list[i] hold bf16 elements, and their row and
+ * batch strides must be multiples of 8 elements.  For a consumer that takes the
+ * attention output as a bf16 GEMM operand (an output projection), and for the
+ * KV-head-split prefill, whose all-gather then moves 2 bytes per element instead of
+ * 4.  No counterpart in the reference (its attention writes fp32,
+ * common/kernels/attention.c:79-170). */
+SMOL_B200_API int smol_b200_prefill_attention_bf16(
+    void *stream, uint16_t *out, int64_t out_row_stride, int64_t out_batch_stride,
+    const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride, const uint16_t *k,
+    int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
+    int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads, int n_kv_heads,
+    int head_dim, float scale, int mask_kind, int q_offset, int prefix_len, int window,
+    float softcap, const int *window_starts, int n_windows);
+SMOL_B200_API int smol_b200_prefill_attention_multi_bf16(
+    void *stream, uint16_t *const *out_list, int n_out, int64_t out_row_stride,
     int64_t out_batch_stride, const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride,
     const uint16_t *k, int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v,
     int64_t v_row_stride, int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads,

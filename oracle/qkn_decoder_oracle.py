@@ -134,13 +134,19 @@ class QknOracle:
         """One decoder layer over tokens at positions pos0.. (qkn_decoder.c:431-563 / :622-705).
         device_formats: round what the device prefill keeps in bf16 -- the RMSNorm outputs,
         the rotated Q, the attention output and the gated activation (GEMM / attention
-        operands) -- the same way."""
+        operands) -- the same way; the Q / K / V projections take the input RMSNorm output
+        as two bf16 operands, hi = bf16(x) and lo = bf16(x - hi), summed in fp32."""
         r16 = pyoracle.round_bf16 if device_formats else (lambda a: a)
         lw, n = self.layers[l], x.shape[0]
         sliding = self.sliding[l] and self.sliding_window > 0
         cos, sin = (self.cos_local, self.sin_local) if self.has_local and self.sliding[l] else (self.cos, self.sin)
-        xn = r16(rms_norm(x, lw["input_norm"], self.eps))
-        q, k, v = xn @ lw["wq"].T, xn @ lw["wk"].T, xn @ lw["wv"].T
+        xn = rms_norm(x, lw["input_norm"], self.eps)
+        if device_formats:
+            hi = r16(xn)
+            lo = r16((xn - hi).astype(np.float32))
+            q, k, v = ((hi @ lw[w].T).astype(np.float32) + (lo @ lw[w].T).astype(np.float32) for w in ("wq", "wk", "wv"))
+        else:
+            q, k, v = xn @ lw["wq"].T, xn @ lw["wk"].T, xn @ lw["wv"].T
         pos = np.arange(pos0, pos0 + n, dtype=np.int32)
         q_rot = pyoracle.qknorm_rope_append(q, k, v, self.HQ, self.HKV, self.HD, lw.get("q_norm"), lw.get("k_norm"),
                                             self.eps, cos, sin, self.interleaved, pos, pos.astype(np.int64),

@@ -15,6 +15,7 @@
 #include <mutex>
 #include <vector>
 
+#include "b200_common.cuh"
 #include "runtime.h"
 
 using namespace smolb200;
@@ -45,7 +46,10 @@ bool finish(cudaStream_t st)
     unsigned *w = device_error_word();
     unsigned v = 0;
     if (w && cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost) == cudaSuccess && v != 0) {
-        set_error(SMOL_B200_ERR_WATCHDOG, "device error word set by a kernel");
+        if (v == kErrValueRange)
+            set_error(SMOL_B200_ERR_RANGE, "a value does not fit the fp16 V format (|v| >= 65520)");
+        else
+            set_error(SMOL_B200_ERR_WATCHDOG, "device error word set by a kernel");
         return false;
     }
     return true;
@@ -185,7 +189,9 @@ void legacy_attention(float *out, const float *Q, const float *K, const float *V
         cuda_check(cudaMemcpyAsync(out + static_cast<int64_t>(row_lo) * q_w, dst, static_cast<size_t>(nrows) * q_w * 4,
                                    cudaMemcpyDeviceToHost, st),
                    "copy result to host");
-    finish(st);
+    // a kernel that reported through the device word (a wait that ran out, a V value fp16
+    // cannot hold) leaves no trustworthy rows: the caller gets zeros, as for other failures
+    if (!finish(st)) zero_host_or_device(out, out_n);
 }
 
 // In-place fp32 op on x (host or device): stage, run `fn` on the device copy, copy back.
@@ -593,8 +599,43 @@ int smol_b200_prefill_attention_multi(void *stream, float *const *out_list, int 
                                     q, q_row_stride, q_batch_stride, k, k_row_stride, k_batch_stride, v, v_row_stride,
                                     v_batch_stride, batch, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale,
                                     mask_kind, q_offset, prefix_len, window, softcap, window_starts, n_windows,
-                                    out_list + 1, n_out - 1),
+                                    reinterpret_cast<void *const *>(out_list + 1), n_out - 1),
                   "smol_b200_prefill_attention_multi");
+}
+
+int smol_b200_prefill_attention_bf16(void *stream, uint16_t *out, int64_t out_row_stride, int64_t out_batch_stride,
+                                     const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride,
+                                     const uint16_t *k, int64_t k_row_stride, int64_t k_batch_stride,
+                                     const uint16_t *v, int64_t v_row_stride, int64_t v_batch_stride, int batch,
+                                     int seq_q, int seq_k, int n_heads, int n_kv_heads, int head_dim, float scale,
+                                     int mask_kind, int q_offset, int prefix_len, int window, float softcap,
+                                     const int *window_starts, int n_windows)
+{
+    return record(prefill_attention(static_cast<cudaStream_t>(stream), out, out_row_stride, out_batch_stride, q,
+                                    q_row_stride, q_batch_stride, k, k_row_stride, k_batch_stride, v, v_row_stride,
+                                    v_batch_stride, batch, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale,
+                                    mask_kind, q_offset, prefix_len, window, softcap, window_starts, n_windows,
+                                    nullptr, 0, 1),
+                  "smol_b200_prefill_attention_bf16");
+}
+
+int smol_b200_prefill_attention_multi_bf16(void *stream, uint16_t *const *out_list, int n_out,
+                                           int64_t out_row_stride, int64_t out_batch_stride, const uint16_t *q,
+                                           int64_t q_row_stride, int64_t q_batch_stride, const uint16_t *k,
+                                           int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v,
+                                           int64_t v_row_stride, int64_t v_batch_stride, int batch, int seq_q,
+                                           int seq_k, int n_heads, int n_kv_heads, int head_dim, float scale,
+                                           int mask_kind, int q_offset, int prefix_len, int window, float softcap,
+                                           const int *window_starts, int n_windows)
+{
+    if (!out_list || n_out < 1 || n_out > 8)
+        return record(SMOL_B200_ERR_ARGS, "smol_b200_prefill_attention_multi_bf16");
+    return record(prefill_attention(static_cast<cudaStream_t>(stream), out_list[0], out_row_stride, out_batch_stride,
+                                    q, q_row_stride, q_batch_stride, k, k_row_stride, k_batch_stride, v, v_row_stride,
+                                    v_batch_stride, batch, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale,
+                                    mask_kind, q_offset, prefix_len, window, softcap, window_starts, n_windows,
+                                    reinterpret_cast<void *const *>(out_list + 1), n_out - 1, 1),
+                  "smol_b200_prefill_attention_multi_bf16");
 }
 
 int smol_b200_ipc_get_handle(const void *dev_ptr, void *handle64, size_t *offset)

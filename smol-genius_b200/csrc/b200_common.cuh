@@ -30,7 +30,12 @@ enum : unsigned {
     kErrWaitSoftmax   = 1u << 3,   // MMA issuer gave up waiting for P / O-ready
     kErrDrain         = 1u << 4,   // draining in-flight copies after an abort timed out
     kErrBadArgs       = 1u << 5,   // a kernel saw arguments its host wrapper should have rejected
+    kErrValueRange    = 1u << 6,   // a value too large for fp16 storage (|x| >= 65520) became infinity
 };
+
+// Round-to-nearest-even into fp16 gives infinity from |x| >= 65520 on (65504 is the
+// largest finite fp16 and 65520 the midpoint to the next power of two).
+__device__ __forceinline__ bool f16_overflows(float x) { return fabsf(x) >= 65520.f; }
 
 // Bounded waits give up after this many nanoseconds of %globaltimer.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s

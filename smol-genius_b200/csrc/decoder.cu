@@ -479,9 +479,11 @@ __global__ void step_index_kernel(int *positions, int *kv_next, int64_t *slots, 
 // (rmsnorm.c:17-70), one warp per row, as the operand of the next GEMM.
 constexpr int kRowNormWarps = 8;
 
-__global__ void __launch_bounds__(kRowNormWarps * 32) rms_norm_rows_bf16_kernel(uint16_t *out, const float *x,
-                                                                                const float *w, int rows, int hidden,
-                                                                                float eps)
+// out = bf16(rmsnorm(x) * w); with out_lo also the residual bf16(y - out), so that a
+// GEMM over out and then out_lo (added) sees y to ~2^-17 relative instead of 2^-9.
+__global__ void __launch_bounds__(kRowNormWarps * 32) rms_norm_rows_bf16_kernel(uint16_t *out, uint16_t *out_lo,
+                                                                                const float *x, const float *w,
+                                                                                int rows, int hidden, float eps)
 {
     const int row = blockIdx.x * kRowNormWarps + threadIdx.x / 32, lane = threadIdx.x % 32;
     if (row >= rows) return;
@@ -490,9 +492,15 @@ __global__ void __launch_bounds__(kRowNormWarps * 32) rms_norm_rows_bf16_kernel(
     for (int i = lane; i < hidden; i += 32) ss += xr[i] * xr[i];
     const float r = 1.0f / sqrtf(warp_sum(ss) / static_cast<float>(hidden) + eps);
     uint16_t *o = out + static_cast<long long>(row) * hidden;
+    uint16_t *ol = out_lo ? out_lo + static_cast<long long>(row) * hidden : nullptr;
     for (int i = lane; i < hidden; i += 32) {
-        __nv_bfloat16 b = __float2bfloat16_rn(xr[i] * w[i] * r);
+        const float y = xr[i] * w[i] * r;
+        __nv_bfloat16 b = __float2bfloat16_rn(y);
         o[i] = *reinterpret_cast<uint16_t *>(&b);
+        if (ol) {
+            __nv_bfloat16 bl = __float2bfloat16_rn(y - __bfloat162float(b));
+            ol[i] = *reinterpret_cast<uint16_t *>(&bl);
+        }
     }
 }
 
@@ -728,8 +736,8 @@ size_t argmax_workspace_bytes(int n_seqs, int vocab)
 
 // Workspace of one prefill of n tokens, carved in 256-byte aligned pieces.
 struct PrefillWs {
-    float *x, *q, *k, *v, *attn, *sub;
-    uint16_t *xn, *qb, *attn16, *act;
+    float *x, *q, *k, *v, *sub;
+    uint16_t *xn, *xn_lo, *qb, *attn16, *act;
     int *positions;
     int64_t *slots;
     size_t total;
@@ -751,9 +759,9 @@ static PrefillWs carve_prefill(const smol_b200_qkn_model &m, int n, uint8_t *bas
     w.q = reinterpret_cast<float *>(take(T * qd * 4));
     w.k = reinterpret_cast<float *>(take(T * kvd * 4));
     w.v = reinterpret_cast<float *>(take(T * kvd * 4));
-    w.attn = reinterpret_cast<float *>(take(T * qd * 4));
     w.sub = reinterpret_cast<float *>(take(T * H * 4));
     w.xn = reinterpret_cast<uint16_t *>(take(T * H * 2));
+    w.xn_lo = reinterpret_cast<uint16_t *>(take(T * H * 2));
     w.qb = reinterpret_cast<uint16_t *>(take(T * qd * 2));
     w.attn16 = reinterpret_cast<uint16_t *>(take(T * qd * 2));
     w.act = reinterpret_cast<uint16_t *>(take(T * I * 2));
@@ -790,10 +798,11 @@ int qkn_prefill(cudaStream_t st, const smol_b200_qkn_model *mp, const int *token
     const float scale = 1.0f / sqrtf(static_cast<float>(hd));            // qkn_decoder.c:430
     const int gate = m.activation == 1 ? 3 : 2;                         // GeGLU / SwiGLU (:548-551)
     const unsigned rows_grid = static_cast<unsigned>((n + kRowNormWarps - 1) / kRowNormWarps);
-    auto rms_bf16 = [&](const float *norm_w) {
+    auto rms_bf16 = [&](const float *norm_w, bool with_lo = false) {
         if (!norm_w) return SMOL_B200_ERR_ARGS;
         return launch_kernel(rms_norm_rows_bf16_kernel, dim3(rows_grid), dim3(kRowNormWarps * 32), 0, st, w.xn,
-                             static_cast<const float *>(w.x), norm_w, n, H, m.eps) == cudaSuccess
+                             with_lo ? w.xn_lo : nullptr, static_cast<const float *>(w.x), norm_w, n, H,
+                             m.eps) == cudaSuccess
                    ? SMOL_B200_OK
                    : SMOL_B200_ERR_CUDA;
     };
@@ -815,14 +824,24 @@ int qkn_prefill(cudaStream_t st, const smol_b200_qkn_model *mp, const int *token
         const int window = L.is_sliding && m.sliding_window > 0 ? m.sliding_window : 0;
         const float softcap = m.attn_softcap > 0.f ? m.attn_softcap : 0.f;
         const int64_t row0 = layer_row0[l];
-        // input RMSNorm, Q / K / V projections (qkn_decoder.c:470-476)
-        rc = rms_bf16(L.input_norm);
-        if (rc == SMOL_B200_OK)
-            rc = gemm_bf16(st, w.q, qd, SMOL_B200_GEMM_OUT_F32, w.xn, H, L.wq, H, nullptr, nullptr, 0, 0, n, qd, H, 0);
-        if (rc == SMOL_B200_OK)
-            rc = gemm_bf16(st, w.k, kvd, SMOL_B200_GEMM_OUT_F32, w.xn, H, L.wk, H, nullptr, nullptr, 0, 0, n, kvd, H, 0);
-        if (rc == SMOL_B200_OK)
-            rc = gemm_bf16(st, w.v, kvd, SMOL_B200_GEMM_OUT_F32, w.xn, H, L.wv, H, nullptr, nullptr, 0, 0, n, kvd, H, 0);
+        // input RMSNorm, Q / K / V projections (qkn_decoder.c:470-476).  These feed the KV
+        // cache, so their input keeps fp32 accuracy as two bf16 operands: W x = W hi + W lo
+        // (the second product added into the first's fp32 result).  With sharp attention a
+        // bf16-rounded input (2^-9 relative) moves cached keys enough to change a later
+        // greedy token that the reference's fp32 projection keeps.
+        rc = rms_bf16(L.input_norm, true);
+        struct Proj {
+            float *out;
+            const uint16_t *wt;
+            int n_out;
+        } const proj[3] = {{w.q, L.wq, qd}, {w.k, L.wk, kvd}, {w.v, L.wv, kvd}};
+        for (int j = 0; j < 3 && rc == SMOL_B200_OK; ++j) {
+            rc = gemm_bf16(st, proj[j].out, proj[j].n_out, SMOL_B200_GEMM_OUT_F32, w.xn, H, proj[j].wt, H, nullptr,
+                           nullptr, 0, 0, n, proj[j].n_out, H, 0);
+            if (rc == SMOL_B200_OK)
+                rc = gemm_bf16(st, proj[j].out, proj[j].n_out, SMOL_B200_GEMM_OUT_F32_ADD, w.xn_lo, H, proj[j].wt, H,
+                               nullptr, nullptr, 0, 0, n, proj[j].n_out, H, 0);
+        }
         // QK-norm, RoPE at positions start.., K / V into the pool (qkn_decoder.c:486-503)
         if (rc == SMOL_B200_OK &&
             launch_kernel(prefill_index_kernel, dim3((n + 255) / 256), dim3(256), 0, st, l == 0 ? w.positions : nullptr,
@@ -836,12 +855,11 @@ int qkn_prefill(cudaStream_t st, const smol_b200_qkn_model *mp, const int *token
         // causal attention over the layer's cached rows [0, start + n) (qkn_decoder.c:505-531)
         if (rc == SMOL_B200_OK) {
             const uint16_t *kl = k_pool + row0 * kvd, *vl = v_pool + row0 * kvd;
-            rc = prefill_attention(st, w.attn, qd, static_cast<int64_t>(n) * qd, w.qb, qd, static_cast<int64_t>(n) * qd,
+            rc = prefill_attention(st, w.attn16, qd, static_cast<int64_t>(n) * qd, w.qb, qd, static_cast<int64_t>(n) * qd,
                                    kl, kvd, static_cast<int64_t>(L_k) * kvd, vl, kvd, static_cast<int64_t>(L_k) * kvd,
                                    1, n, L_k, m.n_heads, m.n_kv_heads, hd, scale, SMOL_MASK_CAUSAL, start, 0, window,
-                                   softcap, nullptr, 0);
+                                   softcap, nullptr, 0, nullptr, 0, 1 /* bf16 output: the o_proj GEMM's operand */);
         }
-        if (rc == SMOL_B200_OK) rc = convert_f32_to_bf16(st, w.attn16, w.attn, static_cast<long long>(n) * qd);
         // output projection and residual, then the MLP input norm (qkn_decoder.c:530-543)
         if (rc == SMOL_B200_OK) {
             if (L.pre_ffn_norm) {

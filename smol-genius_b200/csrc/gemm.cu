@@ -129,6 +129,12 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int row, int nb
     if (p.out_kind == SMOL_B200_GEMM_OUT_BF16 || p.out_kind == SMOL_B200_GEMM_OUT_F16) {
         uint16_t *o = static_cast<uint16_t *>(p.out) + static_cast<long long>(row) * p.ldo + nb;
         const bool h = p.out_kind == SMOL_B200_GEMM_OUT_F16;
+        if (h) {   // an fp16 output (SigLIP's V) reports values it cannot hold instead of storing inf
+            bool over = false;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) over |= nb + i < p.N && f16_overflows(v[i]);
+            if (over) atomicOr(p.err, kErrValueRange);
+        }
         if (full) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {

@@ -568,7 +568,14 @@ struct Prefill2Shape {
     static constexpr int kSmemBytes = kUsed > 118 * 1024 ? kUsed : 118 * 1024;
     static constexpr int kTileCols = 256;
     static constexpr int kTmO = BN;
+    // Look-ahead (head dim 64): P gets its own 64 columns after O instead of overwriting
+    // S, so S of the next key tile can be computed while the softmax still works on
+    // this one (S 128 + O 64 + P 64 = 256 columns per Q tile).  Head dim 128 has no room
+    // (S 128 + O 128) and writes P over the first half of S.
+    static constexpr bool kLookAhead = HD == 64;
+    static constexpr int kTmP = kLookAhead ? BN + HD : 0;
     static_assert(kTmO + HD <= kTileCols, "TMEM budget");
+    static_assert(!kLookAhead || kTmP + BN / 2 <= kTileCols, "TMEM budget (P region)");
     static_assert(kStages * kKvBytes >= kBM * HD * 4, "epilogue staging must fit a K or V ring");
 };
 
@@ -577,6 +584,7 @@ struct Barriers2 {
     uint64_t q_full, q_empty;
     uint64_t k_full[kMaxStages2], k_empty[kMaxStages2], v_full[kMaxStages2], v_empty[kMaxStages2];
     uint64_t s_full[2], p_full[2], o_done[2];
+    uint64_t s_free[2];   // look-ahead: the softmax warps of a tile have read its S
     uint64_t mma_done;
     uint32_t tmem_base;
 };
@@ -729,6 +737,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
             mbar_init(smem_u32(&bars->s_full[t]), 1);
             mbar_init(smem_u32(&bars->p_full[t]), kSoftmaxThreads);
             mbar_init(smem_u32(&bars->o_done[t]), 1);
+            mbar_init(smem_u32(&bars->s_free[t]), 4);   // one arrival per softmax warp
         }
         mbar_init(smem_u32(&bars->mma_done), 1);
         fence_mbar_init();
@@ -828,7 +837,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
             // O_t (+)= P_t V for key tile g; `first` starts the accumulation of an item.
             auto issue_pv = [&](int t, int g, bool first) {
                 const uint32_t v_addr = smem_u32(sV + (g % ST) * S::kKvBytes);
-                const uint32_t p_col = tmem + t * S::kTileCols;
+                const uint32_t p_col = tmem + t * S::kTileCols + S::kTmP;
                 const uint32_t o_col = tmem + t * S::kTileCols + S::kTmO;
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
@@ -842,7 +851,56 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
             };
             int qit = 0, g0 = 0;
             bool ok = true;
-            for (int r = 0; r < n_rounds && ok; ++r) {
+            // Look-ahead order per key tile g: S0(g+1), S1(g+1) as soon as each tile's
+            // softmax has read S(g) (s_free), then PV0(g), PV1(g) once P(g) is written.
+            auto wait_s_free = [&](int t, int g) {   // softmax of tile t has read S(g)
+                return g < 0 || mbar_wait(smem_u32(&bars->s_free[t]), g & 1, p.err, kErrWaitSoftmax);
+            };
+            if constexpr (S::kLookAhead) {
+                for (int r = 0; r < n_rounds && ok; ++r) {
+                    const int k = item_index(p, r);
+                    if (k >= n_items) break;
+                    const Item2 it = item_geometry<BN>(p, k);
+                    const int n = it.n_tiles;
+                    if (n == 0) continue;
+                    ok = mbar_wait(smem_u32(&bars->q_full), qit & 1, p.err, kErrWaitTmaFull) && wait_k(g0);
+                    for (int t = 0; t < 2 && ok; ++t) {
+                        if (!(ok = wait_s_free(t, g0 - 1))) break;
+                        tc_fence_after();
+                        issue_s(t, g0);
+                    }
+                    if (!ok) break;
+                    umma_commit(smem_u32(&bars->k_empty[g0 % ST]));
+                    if (n == 1) umma_commit(smem_u32(&bars->q_empty));
+                    for (int j = 0; j < n && ok; ++j) {
+                        const int g = g0 + j;
+                        if (j + 1 < n) {
+                            if (!(ok = wait_k(g + 1))) break;
+                            for (int t = 0; t < 2 && ok; ++t) {
+                                if (!(ok = wait_s_free(t, g))) break;
+                                tc_fence_after();
+                                issue_s(t, g + 1);
+                            }
+                            if (!ok) break;
+                            umma_commit(smem_u32(&bars->k_empty[(g + 1) % ST]));
+                            if (j + 2 == n) umma_commit(smem_u32(&bars->q_empty));   // last S of the item
+                        }
+                        if (!(ok = mbar_wait(smem_u32(&bars->v_full[g % ST]), (g / ST) & 1, p.err, kErrWaitTmaFull)))
+                            break;
+                        // O_t is overwritten by the item's first PV: its readers (the previous
+                        // item's epilogue) are the threads whose p_full arrival that PV waits for.
+                        for (int t = 0; t < 2 && ok; ++t) {
+                            if (!(ok = mbar_wait(smem_u32(&bars->p_full[t]), g & 1, p.err, kErrWaitSoftmax))) break;
+                            tc_fence_after();
+                            issue_pv(t, g, j == 0);
+                        }
+                        if (ok) umma_commit(smem_u32(&bars->v_empty[g % ST]));
+                    }
+                    g0 += n;
+                    ++qit;
+                }
+            }
+            for (int r = 0; r < n_rounds && ok && !S::kLookAhead; ++r) {
                 const int k = item_index(p, r);
                 if (k >= n_items) break;
                 const Item2 it = item_geometry<BN>(p, k);
@@ -905,6 +963,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
         const uint32_t s_full = smem_u32(&bars->s_full[tile]);
         const uint32_t p_full = smem_u32(&bars->p_full[tile]);
         const uint32_t o_done = smem_u32(&bars->o_done[tile]);
+        const uint32_t s_free = smem_u32(&bars->s_free[tile]);
         bool stores_pending = false;   // lane 0: a TMA store from this warp's staging area
         int g0 = 0;
         bool ok = true;
@@ -922,7 +981,8 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
             float l = 0.f;
             for (int j = 0; j < n_tiles; ++j) {
                 const int g = g0 + j;
-                const uint32_t s_base = lane_base;   // S of this key tile; P overwrites it
+                const uint32_t s_base = lane_base;                // S of this key tile
+                const uint32_t p_base = lane_base + S::kTmP;      // P: its own columns, or over S
                 ok = __all_sync(0xffffffffu, mbar_wait(s_full, g & 1, p.err, kErrWaitMma));
                 if (!ok) break;
                 tc_fence_after();
@@ -937,6 +997,11 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     for (int c = 0; c < BN / 32; ++c)
 #pragma unroll
                         for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(rr[c][i]);
+                }
+                if constexpr (S::kLookAhead) {   // S is in registers: the next S may overwrite it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(s_free);
                 }
                 const int key0 = it.lo_min + j * BN;
                 const bool full_tile = row_valid && key0 >= my_lo && key0 + BN <= my_hi;
@@ -990,6 +1055,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                 const uint64_t vmul = f2_pack(mul, mul);
                 const uint64_t vneg = f2_pack(live ? -m : 0.f, live ? -m : 0.f);
                 uint64_t acc[4] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+                bool p_free = true;   // look-ahead: PV(g-1) has read the P columns
                 {
                     uint32_t rr[32];
 #pragma unroll
@@ -1008,8 +1074,21 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                             acc[i & 3] = f2_add(acc[i & 3], f2_pack(e0, e1));   // 4 independent sums
                             rr[i] = pack_f16x2(e0, e1);
                         }
-                        tmem_st32(s_base + c * 32, rr);
+                        if constexpr (S::kLookAhead) {
+                            // P(g-1) in the same columns is read by PV(g-1): wait for it only now,
+                            // after half of this tile's exponentials (the first P of an item follows
+                            // the previous item's epilogue, which waited for that item's last PV)
+                            if (c == 0 && j > 0) {
+                                p_free = __all_sync(0xffffffffu, mbar_wait(o_done, (g - 1) & 1, p.err, kErrWaitMma));
+                                tc_fence_after();
+                            }
+                        }
+                        if (p_free) tmem_st32(p_base + c * 32, rr);
                     }
+                }
+                if (!p_free) {
+                    ok = false;
+                    break;
                 }
                 const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
                 const uint64_t a = f2_add(a01, a23);

@@ -174,17 +174,21 @@ __global__ void qknorm_rope_append_kernel(const float *__restrict__ q_in, const 
     if (!is_q) {
         const float *vs = v_in + (tok * heads + h) * hd;
         uint16_t *vd = v_cache + (slot * heads + h) * hd;
+        bool over = false;
         for (int d = lane; d < hd; d += 32) {
             __half hv = __float2half_rn(vs[d]);
             vd[d] = *reinterpret_cast<uint16_t *>(&hv);
+            over |= f16_overflows(vs[d]);
         }
+        // the V cache is fp16: a value it cannot hold is reported, not stored silently as inf
+        if (__any_sync(0xffffffffu, over) && lane == 0 && err) atomicOr(err, kErrValueRange);
     }
 }
 
 // dst[r, hh*padded_hd + d] = convert(src[r, hh*head_dim + d]) for d < head_dim, 0 for the padding.
 __global__ void pack_rows_kernel(uint16_t *dst, long long dst_stride, int dst_width, const float *src,
                                  long long src_stride, int src_heads, int head_dim, int padded_hd, long long rows,
-                                 int to_f16)
+                                 int to_f16, unsigned *err)
 {
     const long long total = rows * dst_width;
     for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -198,6 +202,7 @@ __global__ void pack_rows_kernel(uint16_t *dst, long long dst_stride, int dst_wi
         if (to_f16) {
             __half x = __float2half_rn(v);
             bits = *reinterpret_cast<uint16_t *>(&x);
+            if (f16_overflows(v) && err) atomicOr(err, kErrValueRange);
         } else {
             __nv_bfloat16 x = __float2bfloat16_rn(v);
             bits = *reinterpret_cast<uint16_t *>(&x);
@@ -311,7 +316,8 @@ int launch_pack_rows(cudaStream_t st, uint16_t *dst, int64_t dst_stride, int dst
 {
     if (rows <= 0 || dst_width <= 0) return SMOL_B200_OK;
     pack_rows_kernel<<<grid_for(rows * dst_width, 256), 256, 0, st>>>(dst, dst_stride, dst_width, src, src_stride,
-                                                                       src_heads, head_dim, padded_hd, rows, to_f16);
+                                                                       src_heads, head_dim, padded_hd, rows, to_f16,
+                                                                       to_f16 ? device_error_word() : nullptr);
     return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
 }
 

@@ -53,13 +53,14 @@ int decode_attention(cudaStream_t st, float *out, const void *q, int q_is_bf16, 
                      int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, int head_dim, float scale,
                      int window, float softcap, void *workspace, size_t workspace_bytes);
 
-int prefill_attention(cudaStream_t st, float *out, int64_t out_row_stride, int64_t out_batch_stride,
+// out (and each of more_outs) holds fp32 elements, or bf16 when out_bf16.
+int prefill_attention(cudaStream_t st, void *out, int64_t out_row_stride, int64_t out_batch_stride,
                       const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride, const uint16_t *k,
                       int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
                       int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads, int n_kv_heads,
                       int head_dim, float scale, int mask_kind, int q_offset, int prefix_len, int window,
-                      float softcap, const int *window_starts, int n_windows, float *const *more_outs = nullptr,
-                      int n_more = 0);
+                      float softcap, const int *window_starts, int n_windows, void *const *more_outs = nullptr,
+                      int n_more = 0, int out_bf16 = 0);
 
 int qknorm_rope_append(cudaStream_t st, const float *q_in, const float *k_in, const float *v_in, int n_tokens,
                        int n_heads, int n_kv_heads, int head_dim, const float *q_norm_w, const float *k_norm_w,
@@ -152,7 +153,6 @@ int launch_decode_step_index(cudaStream_t st, int *positions, int64_t *slots, in
 int gemm_bf16(cudaStream_t st, void *out, int64_t ldo, int out_kind, const uint16_t *a, int64_t lda,
               const uint16_t *w, int64_t ldw, const float *bias, const float *add, int64_t ld_add, int add_rows,
               int M, int N, int K, int gelu, int gate = 0);
-int convert_f32_to_bf16(cudaStream_t st, uint16_t *dst, const float *src, long long n);
 int layer_norm(cudaStream_t st, void *out, int out_bf16, const float *x, const float *w, const float *b, int rows,
                int hidden, float eps);
 size_t encoder_workspace_bytes(int n_tokens, int hidden, int ffn);

@@ -84,16 +84,6 @@ __global__ void unfold_patches_kernel(uint16_t *a, long long lda, const float *i
     }
 }
 
-// dst = bf16(src), n a multiple of 4 (the attention output as the next GEMM's operand)
-__global__ void f32_to_bf16_kernel(uint16_t *dst, const float *src, long long n4)
-{
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
-         i += static_cast<long long>(gridDim.x) * blockDim.x) {
-        const float4 v = reinterpret_cast<const float4 *>(src)[i];
-        reinterpret_cast<uint2 *>(dst)[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
-    }
-}
-
 unsigned grid_for(long long work, int block)
 {
     const long long g = (work + block - 1) / block;
@@ -103,7 +93,6 @@ unsigned grid_for(long long work, int block)
 // Workspace of the encoder layers for T tokens (256-byte aligned pieces).
 struct EncoderWs {
     uint16_t *xn, *q, *k, *v, *attn16, *h;
-    float *attn;
     size_t total;
 };
 
@@ -121,7 +110,6 @@ EncoderWs carve_encoder(size_t T, size_t H, size_t F, uint8_t *base)
     w.q = reinterpret_cast<uint16_t *>(take(T * H * 2));
     w.k = reinterpret_cast<uint16_t *>(take(T * H * 2));
     w.v = reinterpret_cast<uint16_t *>(take(T * H * 2));
-    w.attn = reinterpret_cast<float *>(take(T * H * 4));
     w.attn16 = reinterpret_cast<uint16_t *>(take(T * H * 2));
     w.h = reinterpret_cast<uint16_t *>(take(T * F * 2));
     w.total = off;
@@ -185,17 +173,6 @@ bool model_ok(const smol_b200_siglip_model *m)
 
 }  // namespace
 
-int convert_f32_to_bf16(cudaStream_t st, uint16_t *dst, const float *src, long long n)
-{
-    if (n <= 0) return SMOL_B200_OK;
-    if (!dst || !src || (n & 3) || (reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 7))
-        return SMOL_B200_ERR_ARGS;
-    const long long n4 = n / 4;
-    return launch_kernel(f32_to_bf16_kernel, dim3(grid_for(n4, 256)), dim3(256), 0, st, dst, src, n4) == cudaSuccess
-               ? SMOL_B200_OK
-               : SMOL_B200_ERR_CUDA;
-}
-
 int layer_norm(cudaStream_t st, void *out, int out_bf16, const float *x, const float *w, const float *b, int rows,
                int hidden, float eps)
 {
@@ -241,9 +218,9 @@ int encoder_layers(cudaStream_t st, float *x, int batch, int seq, const smol_b20
         // bidirectional attention: all tokens of a batch element (siglip.c:104-127) or the
         // tokens of each window (encoder.c:426-435, :462-464)
         if (rc == SMOL_B200_OK)
-            rc = prefill_attention(st, w.attn, H, bs, w.q, H, bs, w.k, H, bs, w.v, H, bs, batch, seq, seq, heads, heads,
-                                   hd, scale, mask, 0, 0, 0, 0.f, window_starts, n_windows);
-        if (rc == SMOL_B200_OK) rc = convert_f32_to_bf16(st, w.attn16, w.attn, static_cast<long long>(T) * H);
+            rc = prefill_attention(st, w.attn16, H, bs, w.q, H, bs, w.k, H, bs, w.v, H, bs, batch, seq, seq, heads,
+                                   heads, hd, scale, mask, 0, 0, 0, 0.f, window_starts, n_windows, nullptr, 0,
+                                   1 /* bf16 output: the o_proj GEMM's operand */);
         if (rc == SMOL_B200_OK)
             rc = gemm_bf16(st, x, H, SMOL_B200_GEMM_OUT_F32_ADD, w.attn16, H, L.wo, H, L.bo, nullptr, 0, 0, T, H, H, 0);
         if (rc == SMOL_B200_OK) rc = layer_norm(st, w.xn, 1, x, L.ln2_w, L.ln2_b, T, H, eps);

@@ -24,7 +24,8 @@ HEADER_PATH = os.path.join(os.path.dirname(HERE), "include", "smol_b200.h")
 
 MASK_CAUSAL, MASK_PREFIX_LM, MASK_WINDOWS, MASK_FULL = 0, 1, 2, 3
 
-ERR_NAMES = {0: "ok", 1: "args", 2: "cuda", 3: "no_device", 4: "oom", 5: "watchdog", 6: "workspace"}
+ERR_NAMES = {0: "ok", 1: "args", 2: "cuda", 3: "no_device", 4: "oom", 5: "watchdog", 6: "workspace", 7: "range"}
+DEVERR_VALUE_RANGE = 1 << 6   # device error word: a value stored as fp16 had |x| >= 65520
 
 
 class SmolB200Error(RuntimeError):
@@ -75,6 +76,10 @@ _SIGNATURES = {
         _c_int, [_c_void, _c_void, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void, _c_i64,
                  _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _c_int, _c_int, _c_int,
                  _c_float, _c_void, _c_int]),
+    "smol_b200_prefill_attention_bf16": (
+        _c_int, [_c_void, _c_void, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void, _c_i64,
+                 _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _c_int, _c_int, _c_int,
+                 _c_float, _c_void, _c_int]),
     "smol_b200_decode_step_scratch_bytes": (_c_size, [_c_int] * 5),
     "smol_b200_decode_step_host": (
         _c_int, [_c_void, _c_void, _c_void, _c_void, _c_void, _c_int, _c_int, _c_int, _c_int, _c_void, _c_void,
@@ -102,6 +107,10 @@ _SIGNATURES = {
                                        _c_size]),
     "smol_b200_argmax_workspace_bytes": (_c_size, [_c_int, _c_int]),
     "smol_b200_prefill_attention_multi": (
+        _c_int, [_c_void, _c_void, _c_int, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void,
+                 _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _c_int, _c_int,
+                 _c_int, _c_float, _c_void, _c_int]),
+    "smol_b200_prefill_attention_multi_bf16": (
         _c_int, [_c_void, _c_void, _c_int, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void, _c_i64, _c_i64, _c_void,
                  _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_int, _c_int, _c_int,
                  _c_int, _c_float, _c_void, _c_int]),
@@ -281,17 +290,20 @@ def prefill_attention(out, q, k, v, batch, seq_q, seq_k, n_heads, n_kv_heads, he
                       q_offset=0, prefix_len=0, window=0, softcap=0.0, window_starts=None, stream=None,
                       strides=None):
     """q/k: bf16 [batch, seq, heads*hd]; v: fp16; out: fp32 [batch, seq_q, n_heads*hd] (contiguous unless
-    `strides` = ((out_row, out_batch), (q_row, q_batch), (k_row, k_batch), (v_row, v_batch)) in elements)."""
+    `strides` = ((out_row, out_batch), (q_row, q_batch), (k_row, k_batch), (v_row, v_batch)) in elements).
+    A bf16 `out` selects smol_b200_prefill_attention_bf16."""
+    import torch
     if strides is None:
         qw, kw = n_heads * head_dim, n_kv_heads * head_dim
         strides = ((qw, seq_q * qw), (qw, seq_q * qw), (kw, seq_k * kw), (kw, seq_k * kw))
     (ors, obs), (qrs, qbs), (krs, kbs), (vrs, vbs) = strides
     nw = 0 if window_starts is None else window_starts.numel() - 1
-    rc = lib().smol_b200_prefill_attention(
+    name = "smol_b200_prefill_attention_bf16" if out.dtype == torch.bfloat16 else "smol_b200_prefill_attention"
+    rc = getattr(lib(), name)(
         _stream(stream), _ptr(out), ors, obs, _ptr(q), qrs, qbs, _ptr(k), krs, kbs, _ptr(v), vrs, vbs, batch, seq_q,
         seq_k, n_heads, n_kv_heads, head_dim, scale, mask_kind, q_offset, prefix_len, window, softcap,
         _ptr(window_starts), nw)
-    check(rc, "smol_b200_prefill_attention")
+    check(rc, name)
 
 
 def decode_step_scratch_bytes(n_seqs, max_kv_len, n_heads, n_kv_heads, head_dim) -> int:
@@ -401,18 +413,20 @@ def argmax_bf16(tokens_out, x, ldx, emb, vocab, k_dim, n_seqs, workspace, stream
 # ---------------------------------------------------------------------------
 def prefill_attention_multi(out_ptrs, row_stride, batch_stride, q, k, v, batch, seq_q, seq_k, n_heads, n_kv_heads,
                             head_dim, scale, mask_kind=MASK_CAUSAL, q_offset=0, prefix_len=0, window=0, softcap=0.0,
-                            strides=None, stream=None):
-    """out_ptrs: device addresses (ints) of every destination, same strides (elements)."""
+                            strides=None, stream=None, bf16=False):
+    """out_ptrs: device addresses (ints) of every destination, same strides (elements); fp32 elements, or bf16
+    with bf16=True (smol_b200_prefill_attention_multi_bf16)."""
     if strides is None:
         strides = ((n_heads * head_dim, seq_q * n_heads * head_dim), (n_kv_heads * head_dim, seq_k * n_kv_heads * head_dim),
                    (n_kv_heads * head_dim, seq_k * n_kv_heads * head_dim))
     (qs, qb), (ks, kb), (vs, vb) = strides
     arr = (ctypes.c_void_p * len(out_ptrs))(*out_ptrs)
-    rc = lib().smol_b200_prefill_attention_multi(
+    name = "smol_b200_prefill_attention_multi_bf16" if bf16 else "smol_b200_prefill_attention_multi"
+    rc = getattr(lib(), name)(
         _stream(stream), ctypes.cast(arr, ctypes.c_void_p), len(out_ptrs), row_stride, batch_stride, _ptr(q), qs, qb,
         _ptr(k), ks, kb, _ptr(v), vs, vb, batch, seq_q, seq_k, n_heads, n_kv_heads, head_dim, scale, mask_kind,
         q_offset, prefix_len, window, softcap, None, 0)
-    check(rc, "smol_b200_prefill_attention_multi")
+    check(rc, name)
 
 
 def ipc_handle(t) -> tuple[bytes, int]:

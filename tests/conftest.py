@@ -84,3 +84,26 @@ def assert_close(got, want, what=""):
     m = float(np.abs(got - want).max()) if got.size else 0.0
     assert e <= REL_L2_TOL and m <= MAX_ABS_TOL, f"{what}: rel-L2 {e:.3e} (tol {REL_L2_TOL}), max-abs {m:.3e}"
     return e, m
+
+
+def assert_within_bf16_truncation(got, ref_bits, rel_tol, abs_tol=1e-6, what=""):
+    """The reference's bf16 decoder truncates its fp32 results toward zero
+    (qkn_bf16_decoder.c:30-35), so the value it computed lies in [|t|, |t| + ulp(t)) with
+    t's sign, t the stored bf16.  `got` (fp32) passes when its distance to that interval
+    is at most rel_tol * |got| + abs_tol everywhere.  Returns the largest distance
+    relative to |got| + 1e-30."""
+    got = np.asarray(got, np.float64)
+    bits = np.asarray(ref_bits, np.uint16).astype(np.uint32)
+    t = (bits << 16).view(np.float32).astype(np.float64)
+    exp = (bits >> 7) & 0xFF
+    ulp = np.where(exp > 0, np.ldexp(1.0, exp.astype(np.int64) - 127 - 7), np.ldexp(1.0, -133))
+    lo, hi = np.abs(t), np.abs(t) + ulp
+    same = (np.sign(got) == np.sign(t)) | (t == 0) | (got == 0)
+    a = np.abs(got)
+    dist = np.where(same, np.maximum(0.0, np.maximum(lo - a, a - hi)), a + np.abs(t))
+    bad = dist > rel_tol * a + abs_tol
+    if bad.any():
+        i = int(np.argmax(np.where(bad, dist - rel_tol * a, -1.0)))
+        raise AssertionError(f"{what}: {int(bad.sum())} of {bad.size} outside the truncation interval; worst at "
+                             f"{i}: got {got.flat[i]:.6g}, reference {t.flat[i]:.6g}, distance {dist.flat[i]:.3e}")
+    return float((dist / (a + 1e-30)).max())

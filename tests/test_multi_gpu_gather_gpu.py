@@ -5,7 +5,7 @@ the causal prefill for its Q heads and the per-rank outputs are all-gathered.  W
 smol_b200_prefill_attention_multi every output tile is stored to this rank's slot in
 each rank's gather buffer (a CUDA IPC mapping for the peer) by the prefill kernel
 itself.  The gathered tensor must equal prefill + NCCL all-gather bit for bit on every
-rank.  Ranks are child processes with NCCL over 127.0.0.1 and a short process-group
+rank, with fp32 and with bf16 outputs.  Ranks are child processes with NCCL over 127.0.0.1 and a short process-group
 timeout; NVLS is off so no multicast object is involved.
 """
 import os
@@ -26,7 +26,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, B, L, q_err):
+def _rank_main(rank, world, port, B, L, bf16, q_err):
     import datetime
 
     import torch.distributed as dist
@@ -43,14 +43,15 @@ def _rank_main(rank, world, port, B, L, q_err):
         q = torch.randn((B, L, hq_r * hd), device="cuda", generator=g).to(torch.bfloat16)
         k = torch.randn((B, L, hkv_r * hd), device="cuda", generator=g).to(torch.bfloat16)
         v = torch.randn((B, L, hkv_r * hd), device="cuda", generator=g).to(torch.float16)
-        out = torch.empty((B, L, hq_r * hd), device="cuda")
-        gathered = torch.full((world, B, L, hq_r * hd), float("nan"), device="cuda")
+        dt = torch.bfloat16 if bf16 else torch.float32
+        out = torch.empty((B, L, hq_r * hd), device="cuda", dtype=dt)
+        gathered = torch.full((world, B, L, hq_r * hd), float("nan"), device="cuda", dtype=dt)
         handle, off = smol_b200.ipc_handle(gathered)
         meta = torch.tensor(list(handle) + list(off.to_bytes(8, "little")), dtype=torch.uint8, device="cuda")
         allmeta = torch.empty(world * 72, dtype=torch.uint8, device="cuda")
         dist.all_gather_into_tensor(allmeta, meta)
         allmeta = allmeta.cpu().numpy().reshape(world, 72)
-        slot = out.numel() * 4
+        slot = out.numel() * out.element_size()
         bases, opened = [], []
         for peer in range(world):
             if peer == rank:
@@ -62,7 +63,8 @@ def _rank_main(rank, world, port, B, L, q_err):
         outs = [bases[rank] + rank * slot] + [bases[p] + rank * slot for p in range(world) if p != rank]
         dist.barrier()
         scale = 1 / np.sqrt(hd)
-        smol_b200.prefill_attention_multi(outs, hq_r * hd, L * hq_r * hd, q, k, v, B, L, L, hq_r, hkv_r, hd, scale)
+        smol_b200.prefill_attention_multi(outs, hq_r * hd, L * hq_r * hd, q, k, v, B, L, L, hq_r, hkv_r, hd, scale,
+                                          bf16=bf16)
         torch.cuda.synchronize()
         dist.barrier()                 # every rank's kernel (and its stores) has finished
         fused = gathered.clone()
@@ -82,13 +84,13 @@ def _rank_main(rank, world, port, B, L, q_err):
         raise
 
 
-@pytest.mark.parametrize("B,L", [(2, 1024), (1, 1000)])
-def test_fused_allgather_matches_nccl(B, L):
+@pytest.mark.parametrize("B,L,bf16", [(2, 1024, False), (1, 1000, False), (2, 1024, True), (1, 1000, True)])
+def test_fused_allgather_matches_nccl(B, L, bf16):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q_err = ctx.SimpleQueue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, B, L, q_err)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, B, L, bf16, q_err)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

@@ -131,3 +131,25 @@ def test_restatement_vs_live_reference_random():
         a = o.causal_attention(q, k, v, sq, sk, hq, hkv, hd, 0.3, qo, window=win, cap=cap)
         b = r.causal_attention(q, k, v, sq, sk, hq, hkv, hd, 0.3, qo, window=win, cap=cap)
         assert pyoracle.rel_l2(a, b) < TIGHT
+
+
+def test_oracle_matches_reference_bf16_decoder_attention():
+    """Second oracle for the bf16-cache path: the reference's own bf16 decoder attention
+    (qkn_bf16_decoder.c:120-233, fp32 two-pass softmax, output truncated to bf16;
+    fixtures from tests/golden/make_bf16_golden.py).  The restatement's fp32 result must
+    lie within fp32 rounding of the interval the truncated value stands for: relative
+    2e-5, and absolute 1e-5 for outputs that nearly cancel (the reference sums up to 200
+    weighted |v| <= ~5 in fp32 in its own order, ~1e-6 apart from ours)."""
+    import os
+
+    from conftest import assert_within_bf16_truncation
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "bf16_decoder_cases.npz"))
+    o = pyoracle.oracle()
+    names = sorted({k.split("/")[0] for k in g.files})
+    assert len(names) == 7
+    for name in names:
+        sq, sk, hq, hkv, hd, qo, win = (int(x) for x in g[f"{name}/meta"])
+        scale, cap = (float(x) for x in g[f"{name}/fmeta"])
+        q, k, v = (pyoracle.bf16_to_f32(g[f"{name}/{t}_bf16"]) for t in ("q", "k", "v"))
+        got = o.causal_attention(q, k, v, sq, sk, hq, hkv, hd, scale, qo, window=win, cap=cap)
+        assert_within_bf16_truncation(got, g[f"{name}/out_bf16"], rel_tol=2e-5, abs_tol=1e-5, what=name)

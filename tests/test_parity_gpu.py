@@ -543,8 +543,9 @@ def test_bf16_decoder_reference_second_oracle(cuda):
     # prefill, seq_q == 1 through the split-KV decode over a pool, with the PaliGemma
     # decoder's settings (MQA 8/1, head dim 256, softcap 50, sliding window).  V goes in
     # as fp16 (every bf16 value of these inputs is exact in fp16).  The device's fp32
-    # result must lie within 2e-3 relative (P in fp16, ex2.approx) or 1e-4 absolute of the
-    # interval each truncated reference value stands for.
+    # result must lie within 2e-3 relative or 4e-4 absolute of the interval each truncated
+    # reference value stands for: P in fp16 (2^-11 relative per weight) moves an output of
+    # ~0.1, an average of ~70 values ~N(0,1), by up to ~2e-4.
     import os
 
     from conftest import assert_within_bf16_truncation
@@ -566,7 +567,7 @@ def test_bf16_decoder_reference_second_oracle(cuda):
             torch.cuda.synchronize()
             no_error()
             got = out.cpu().numpy()
-        assert_within_bf16_truncation(got, g[f"{name}/out_bf16"], rel_tol=2e-3, abs_tol=1e-4, what=name)
+        assert_within_bf16_truncation(got, g[f"{name}/out_bf16"], rel_tol=2e-3, abs_tol=4e-4, what=name)
 
 
 def test_prefill_batched_strided(cuda):
