@@ -62,6 +62,7 @@ struct GemmParams {
     int gelu;
     int gate;                 // 0, or 2 / 3: columns (2j, 2j+1) -> out[j] = act(c[2j]) * c[2j+1], act SiLU / GELU-tanh
     int vec_ok;               // rows of `out` (and `add`) are 16-byte aligned
+    int bias_vec, add_vec;    // bias / rows of `add` are 16-byte aligned: 16-byte loads
     unsigned *err;
 };
 
@@ -86,15 +87,44 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int row, int nb
     if (row >= p.M || nb >= p.N) return;
     float v[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-        const int n = nb + i;
-        float x = __uint_as_float(r[i]);
-        if (n < p.N) {
-            if (p.bias) x += p.bias[n];
-            if (p.add) x += p.add[static_cast<long long>(row % p.add_rows) * p.ld_add + n];
-            if (p.gelu) x = gelu_tanh(x);
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    const bool whole = nb + 32 <= p.N;
+    if (p.bias) {
+        if (whole && p.bias_vec) {   // the same 32 values for every row: 8 broadcast 16-byte loads
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 b4 = __ldg(reinterpret_cast<const float4 *>(p.bias + nb) + q);
+                v[4 * q] += b4.x;
+                v[4 * q + 1] += b4.y;
+                v[4 * q + 2] += b4.z;
+                v[4 * q + 3] += b4.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (nb + i < p.N) v[i] += p.bias[nb + i];
         }
-        v[i] = x;
+    }
+    if (p.add) {
+        const float *ar = p.add + static_cast<long long>(row % p.add_rows) * p.ld_add + nb;
+        if (whole && p.add_vec) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const float4 a4 = __ldg(reinterpret_cast<const float4 *>(ar) + q);
+                v[4 * q] += a4.x;
+                v[4 * q + 1] += a4.y;
+                v[4 * q + 2] += a4.z;
+                v[4 * q + 3] += a4.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (nb + i < p.N) v[i] += ar[i];
+        }
+    }
+    if (p.gelu) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
     }
     const bool full = p.vec_ok && nb + 32 <= p.N;
     if (p.gate) {   // 16 outputs from the 32 columns: out[nb/2 + j]
@@ -283,35 +313,43 @@ __global__ void __launch_bounds__(kGemmThreads, 2) gemm_bf16_kernel(const __grid
 }
 
 // ---------------------------------------------------------------------------
-// Persistent form (SMOL_GEMM_PERSISTENT=1): one CTA per SM walks the output tiles
-// (N fastest, so CTAs running together share A rows in L2), a 4-stage ring runs on
-// across tiles, and two TMEM accumulators (2 x 128 columns) let the MMAs of the next
-// tile run while the epilogue warps drain the previous one.
+// Wide persistent form: one CTA per SM walks output tiles of 128 x 256 (N fastest, so
+// the CTAs running together share A rows in L2).  A 128 x 128 tile streams 32 KB from
+// L2 per 2.1 MFLOP (64 FLOP/B), which at the full tensor rate asks ~26 TB/s of L2;
+// 128 x 256 streams 48 KB per 4.2 MFLOP (87 FLOP/B).  A 4-stage ring of 48 KB stages
+// runs on across tiles, and two 256-column TMEM accumulators let the MMAs of tile i+1
+// run while the epilogue warps drain tile i (tcgen05.mma kind::f16, M = 128, N = 256).
 // ---------------------------------------------------------------------------
-constexpr int kPStages = 4;
+constexpr int kWBN = 256;
+constexpr int kWStages = 4;
+constexpr int kWBBytes = kWBN * kBK * 2;                  // 32 KB
+constexpr int kWStageBytes = kABytes + kWBBytes;          // 48 KB
+constexpr int kWTmemCols = 2 * kWBN;                      // two accumulators
+constexpr uint32_t kWIdesc = umma_idesc_f16(kBM, kWBN, true, false);
 
-struct PersistentBarriers {
-    uint64_t full[kPStages], empty[kPStages];
+struct WideBarriers {
+    uint64_t full[kWStages], empty[kWStages];
     uint64_t acc_full[2], acc_empty[2];
     uint64_t mma_done;
     uint32_t tmem_base;
     int abort;
 };
 
-constexpr int kPSmemBytes = 1024 + kPStages * kStageBytes + 256;
+constexpr int kWSmemBytes = 1024 + kWStages * kWStageBytes + 256;
+static_assert(kWSmemBytes <= 227 * 1024, "shared memory");
 
-__global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_persistent_kernel(const __grid_constant__ GemmParams p)
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_wide_kernel(const __grid_constant__ GemmParams p)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    PersistentBarriers *bars = reinterpret_cast<PersistentBarriers *>(smem + kPStages * kStageBytes);
+    WideBarriers *bars = reinterpret_cast<WideBarriers *>(smem + kWStages * kWStageBytes);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int n_kb = (p.K + kBK - 1) / kBK;
-    const int tiles_n = (p.N + kBN - 1) / kBN;
+    const int tiles_n = (p.N + kWBN - 1) / kWBN;
     const int n_tiles = tiles_n * ((p.M + kBM - 1) / kBM);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kPStages; ++s) {
+        for (int s = 0; s < kWStages; ++s) {
             mbar_init(smem_u32(&bars->full[s]), 1);
             mbar_init(smem_u32(&bars->empty[s]), 1);
         }
@@ -324,7 +362,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_persistent_kernel(c
         fence_mbar_init();
     }
     if (warp == kMmaWarp) {
-        tmem_alloc(smem_u32(&bars->tmem_base), 2 * kTmemCols);
+        tmem_alloc(smem_u32(&bars->tmem_base), kWTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -339,26 +377,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_persistent_kernel(c
             int g = 0;   // k blocks issued so far (the ring's running index)
             bool ok = true;
             for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-                const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kBN;
+                const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kWBN;
                 for (int kb = 0; kb < n_kb; ++kb, ++g) {
-                    const int st = g % kPStages;
-                    if ((g >= kPStages &&
-                         !mbar_wait(smem_u32(&bars->empty[st]), ((g / kPStages) - 1) & 1, p.err, kErrWaitTmaEmpty)) ||
+                    const int st = g % kWStages;
+                    if ((g >= kWStages &&
+                         !mbar_wait(smem_u32(&bars->empty[st]), ((g / kWStages) - 1) & 1, p.err, kErrWaitTmaEmpty)) ||
                         atomicAdd(&bars->abort, 0)) {
                         atomicExch(&bars->abort, 1);
                         ok = false;
                         break;
                     }
                     const uint32_t full = smem_u32(&bars->full[st]);
-                    const uint32_t sa = smem_u32(smem + st * kStageBytes);
-                    mbar_arrive_expect_tx(full, kStageBytes);
+                    const uint32_t sa = smem_u32(smem + st * kWStageBytes);
+                    mbar_arrive_expect_tx(full, kWStageBytes);
                     tma_load_2d(sa, &p.ta, full, kb * kBK, m0);
                     tma_load_2d(sa + kABytes, &p.tw, full, kb * kBK, n0);
                 }
             }
             // every issued copy lands before the CTA may exit
-            for (int q = g > kPStages ? g - kPStages : 0; q < g; ++q)
-                mbar_wait(smem_u32(&bars->full[q % kPStages]), (q / kPStages) & 1, p.err, kErrDrain);
+            for (int q = g > kWStages ? g - kWStages : 0; q < g; ++q)
+                mbar_wait(smem_u32(&bars->full[q % kWStages]), (q / kWStages) & 1, p.err, kErrDrain);
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
@@ -366,7 +404,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_persistent_kernel(c
             bool ok = true;
             for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x, ++i) {
                 const int b = i & 1;
-                const uint32_t acc = tmem + b * kTmemCols;
+                const uint32_t acc = tmem + b * kWBN;
                 // the epilogue has drained this accumulator (tile i - 2)
                 if (i >= 2 && !mbar_wait(smem_u32(&bars->acc_empty[b]), ((i >> 1) - 1) & 1, p.err, kErrWaitSoftmax)) {
                     atomicExch(&bars->abort, 1);
@@ -374,20 +412,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_persistent_kernel(c
                 }
                 tc_fence_after();
                 for (int kb = 0; kb < n_kb; ++kb, ++g) {
-                    const int st = g % kPStages;
-                    if (!mbar_wait(smem_u32(&bars->full[st]), (g / kPStages) & 1, p.err, kErrWaitTmaFull) ||
+                    const int st = g % kWStages;
+                    if (!mbar_wait(smem_u32(&bars->full[st]), (g / kWStages) & 1, p.err, kErrWaitTmaFull) ||
                         atomicAdd(&bars->abort, 0)) {
                         atomicExch(&bars->abort, 1);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t sa = smem_u32(smem + st * kStageBytes);
+                    const uint32_t sa = smem_u32(smem + st * kWStageBytes);
 #pragma unroll
-                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                    for (int kk = 0; kk < kBK / 16; ++kk) {   // 16 bf16 = 32 bytes along K inside the swizzled row
                         const uint64_t adesc = umma_sdesc_sw128(sa + kk * 32, 16, 1024);
                         const uint64_t bdesc = umma_sdesc_sw128(sa + kABytes + kk * 32, 16, 1024);
-                        umma_ss(acc, adesc, bdesc, kIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                        umma_ss(acc, adesc, bdesc, kWIdesc, (kb > 0 || kk > 0) ? 1u : 0u);
                     }
                     umma_commit(smem_u32(&bars->empty[st]));
                 }
@@ -401,21 +439,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_persistent_kernel(c
         int i = 0;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
             const int b = i & 1;
-            const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kBN;
+            const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kWBN;
             const int row = m0 + quarter * 32 + lane;
             const bool waited = mbar_wait(smem_u32(&bars->acc_full[b]), (i >> 1) & 1, p.err, kErrWaitMma);
             tc_fence_after();
             if (!__all_sync(0xffffffffu, waited && atomicAdd(&bars->abort, 0) == 0)) break;
-            const uint32_t taddr = tmem + b * kTmemCols + (static_cast<uint32_t>(quarter * 32) << 16);
-            for (int c = 0; c < kBN / 32; ++c) {
+            const uint32_t taddr = tmem + b * kWBN + (static_cast<uint32_t>(quarter * 32) << 16);
+            const int n_chunks = min(kWBN, p.N - n0 + 31) / 32;   // chunks holding columns < N
+            for (int c = 0; c < kWBN / 32; ++c) {
                 uint32_t r[32];
-                tmem_ld32(taddr + c * 32, r);
-                tmem_ld_wait();
-                if (c == kBN / 32 - 1) {   // the accumulator is free for tile i + 2
+                if (c < n_chunks) {
+                    tmem_ld32(taddr + c * 32, r);
+                    tmem_ld_wait();
+                }
+                if (c == kWBN / 32 - 1) {   // the accumulator is free for tile i + 2
                     tc_fence_before();
                     mbar_arrive(smem_u32(&bars->acc_empty[b]));
                 }
-                store_chunk(p, row, n0 + c * 32, r);
+                if (c < n_chunks) store_chunk(p, row, n0 + c * 32, r);
             }
         }
     }
@@ -424,13 +465,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_persistent_kernel(c
     __syncthreads();
     if (warp == kMmaWarp) {
         tc_fence_after();
-        tmem_dealloc(tmem, 2 * kTmemCols);
+        tmem_dealloc(tmem, kWTmemCols);
     }
 }
 
-const bool g_gemm_persistent = [] {
-    const char *e = getenv("SMOL_GEMM_PERSISTENT");
-    return e && atoi(e) != 0;
+// SMOL_GEMM_WIDE=0 in the environment keeps every GEMM on the one-tile-per-CTA
+// 128 x 128 form (measurement knob).
+const bool g_gemm_wide = [] {
+    const char *e = getenv("SMOL_GEMM_WIDE");
+    return !(e && e[0] == '0');
 }();
 
 int sm_count()
@@ -472,10 +515,15 @@ int gemm_bf16(cudaStream_t st, void *out, int64_t ldo, int out_kind, const uint1
             return SMOL_B200_ERR_CUDA;
         raised[dev] = true;
     }
+    // The wide persistent form when its 128 x 256 tiles fill at least one wave of SMs;
+    // narrow outputs and small batches keep one 128 x 128 tile per CTA (more CTAs).
+    const int sms = sm_count();
+    const long long wide_tiles = static_cast<long long>((N + kWBN - 1) / kWBN) * ((M + kBM - 1) / kBM);
+    const bool wide = g_gemm_wide && N >= kWBN && wide_tiles >= sms;
     GemmParams p;
     memset(&p, 0, sizeof(p));
     if (!make_tmap_2d(&p.ta, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, M, kBK, kBM, lda) ||
-        !make_tmap_2d(&p.tw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, N, kBK, kBN, ldw))
+        !make_tmap_2d(&p.tw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, K, N, kBK, wide ? kWBN : kBN, ldw))
         return SMOL_B200_ERR_CUDA;
     const int esz = out_kind == SMOL_B200_GEMM_OUT_BF16 || out_kind == SMOL_B200_GEMM_OUT_F16 ? 2 : 4;
     p.out = out;
@@ -491,18 +539,19 @@ int gemm_bf16(cudaStream_t st, void *out, int64_t ldo, int out_kind, const uint1
     p.gelu = gelu ? 1 : 0;
     p.gate = gate;
     p.vec_ok = (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (ldo * esz) % 16 == 0;
+    p.bias_vec = bias && reinterpret_cast<uintptr_t>(bias) % 16 == 0;
+    p.add_vec = add && reinterpret_cast<uintptr_t>(add) % 16 == 0 && ld_add % 4 == 0;
     p.err = err;
-    if (g_gemm_persistent) {
-        static bool raised_p[64] = {};
-        if (!raised_p[dev]) {
-            if (cudaFuncSetAttribute(gemm_bf16_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kPSmemBytes) != cudaSuccess)
+    if (wide) {
+        static bool raised_w[64] = {};
+        if (!raised_w[dev]) {
+            if (cudaFuncSetAttribute(gemm_bf16_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kWSmemBytes) != cudaSuccess)
                 return SMOL_B200_ERR_CUDA;
-            raised_p[dev] = true;
+            raised_w[dev] = true;
         }
-        const long long tiles = static_cast<long long>((N + kBN - 1) / kBN) * ((M + kBM - 1) / kBM);
-        const unsigned grid = static_cast<unsigned>(tiles < sm_count() ? tiles : sm_count());
-        return launch_kernel(gemm_bf16_persistent_kernel, dim3(grid), dim3(kGemmThreads), kPSmemBytes, st, p) ==
+        const unsigned grid = static_cast<unsigned>(wide_tiles < sms ? wide_tiles : sms);
+        return launch_kernel(gemm_bf16_wide_kernel, dim3(grid), dim3(kGemmThreads), kWSmemBytes, st, p) ==
                        cudaSuccess
                    ? SMOL_B200_OK
                    : SMOL_B200_ERR_CUDA;

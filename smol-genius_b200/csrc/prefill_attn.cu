@@ -605,6 +605,25 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b)
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+// The same two operations on float pairs: the pairs are formed and split with mov.b64
+// inside the asm, which the register allocator maps onto register pairs, instead of
+// 64-bit shifts and ors in C++ that can cost integer instructions per element.
+__device__ __forceinline__ void fma2(float &d0, float &d1, float a0, float a1, float b0, float b1, float c0, float c1)
+{
+    asm("{\n\t.reg .b64 a, b, c, d;\n\t"
+        "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+        "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void add2(float &d0, float &d1, float a0, float a1, float b0, float b1)
+{
+    asm("{\n\t.reg .b64 a, b, d;\n\t"
+        "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+        "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
 // 2^x for a pair of floats on the FMA pipe instead of MUFU (Cody-Waite range reduction
 // + polynomial): n = round(x) via the 1.5*2^23 constant, f = x - n in [-1/2, 1/2],
 // 2^f from a degree-3 polynomial fitted for relative error (max 7.5e-5 on the interval;
@@ -1052,9 +1071,10 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                 // P = exp2(s*scale_log2 - m): one packed FMA per two scores, then ex2.
                 const bool live = m != -INFINITY;
                 const float mul = cap > 0.f ? 1.f : sl2;
-                const uint64_t vmul = f2_pack(mul, mul);
-                const uint64_t vneg = f2_pack(live ? -m : 0.f, live ? -m : 0.f);
-                uint64_t acc[4] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+                // A row with no visible key yet (m = -inf) has every score at -inf, so with
+                // -m replaced by 0 its exponentials are exactly 0: no per-element select.
+                const float negm = live ? -m : 0.f;
+                float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};   // 4 independent pair sums
                 bool p_free = true;   // look-ahead: PV(g-1) has read the P columns
                 {
                     uint32_t rr[32];
@@ -1062,16 +1082,15 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     for (int c = 0; c < BN / 64; ++c) {
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
-                            const uint64_t x = f2_fma(f2_pack(t[c * 64 + 2 * i], t[c * 64 + 2 * i + 1]), vmul, vneg);
-                            float e0, e1;
+                            float x0, x1, e0, e1;
+                            fma2(x0, x1, t[c * 64 + 2 * i], t[c * 64 + 2 * i + 1], mul, mul, negm, negm);
                             if ((i & 7) < PolyPairs8) {   // this pair on the FMA pipe
-                                exp2_poly_pair(x, e0, e1);
+                                exp2_poly_pair(f2_pack(x0, x1), e0, e1);
                             } else {                      // this pair on MUFU
-                                e0 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x)));
-                                e1 = fast_exp2(__uint_as_float(static_cast<uint32_t>(x >> 32)));
+                                e0 = fast_exp2(x0);
+                                e1 = fast_exp2(x1);
                             }
-                            if (!live) e0 = e1 = 0.f;
-                            acc[i & 3] = f2_add(acc[i & 3], f2_pack(e0, e1));   // 4 independent sums
+                            add2(acc0[i & 3], acc1[i & 3], acc0[i & 3], acc1[i & 3], e0, e1);
                             rr[i] = pack_f16x2(e0, e1);
                         }
                         if constexpr (S::kLookAhead) {
@@ -1090,9 +1109,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     ok = false;
                     break;
                 }
-                const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
-                const uint64_t a = f2_add(a01, a23);
-                l += __uint_as_float(static_cast<uint32_t>(a)) + __uint_as_float(static_cast<uint32_t>(a >> 32));
+                l += ((acc0[0] + acc0[1]) + (acc0[2] + acc0[3])) + ((acc1[0] + acc1[1]) + (acc1[2] + acc1[3]));
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(p_full);

@@ -105,45 +105,62 @@ def test_gemm_bf16_gated_pairs(cuda, M, I, K):
         assert pyoracle.rel_l2(yb.float().cpu().numpy(), fn(c)) < 4e-3
 
 
-_PERSISTENT_CHECK = """
-import sys, numpy as np, torch
-sys.path[:0] = [{oracle!r}, {pkg!r}]
-import pyoracle, smol_b200
-rng = np.random.default_rng(5)
-for M, N, K in ((1000, 768, 768), (4500, 640, 200), (8192, 1024, 256), (130, 520, 588)):
+@pytest.mark.new_on_gpu(stage=1)
+@pytest.mark.parametrize("M,N,K", [(4096, 1280, 768), (8192, 1024, 256), (20000, 768, 200), (37000, 520, 588)])
+def test_gemm_bf16_wide_form(cuda, M, N, K):
+    """Shapes whose 128 x 256 tiles fill a wave of SMs run the wide persistent GEMM: more
+    tiles than SMs (both TMEM accumulators reused), ragged M, N and K tails; fp32 with
+    bias + GELU, fp32 added into C, bf16 out; against float64 numpy on sampled rows."""
+    rng = np.random.default_rng(M + N)
+    t = _dev(cuda)
     lda = (K + 7) // 8 * 8
     A = pyoracle.round_bf16(rng.standard_normal((M, K)).astype(np.float32))
     W = pyoracle.round_bf16((rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float32))
-    Ap = np.zeros((M, lda), np.float32); Ap[:, :K] = A
-    Wp = np.zeros((N, lda), np.float32); Wp[:, :K] = W
+    Ap = np.zeros((M, lda), np.float32)
+    Ap[:, :K] = A
+    Wp = np.zeros((N, lda), np.float32)
+    Wp[:, :K] = W
     bias = rng.standard_normal(N).astype(np.float32)
-    y = torch.zeros((M, N), device="cuda")
-    smol_b200.gemm_bf16(y, N, smol_b200.GEMM_OUT_F32, torch.from_numpy(pyoracle.bf16_bits(Ap)).cuda(), lda,
-                        torch.from_numpy(pyoracle.bf16_bits(Wp)).cuda(), lda, M, N, K, bias=torch.from_numpy(bias).cuda(),
-                        gelu=True)
+    a_d, w_d, b_d = t(pyoracle.bf16_bits(Ap)), t(pyoracle.bf16_bits(Wp)), t(bias)
+    rows = np.unique(np.concatenate([np.arange(0, 300), rng.integers(0, M, 700), np.arange(M - 300, M)]))
+    base = (A[rows].astype(np.float64) @ W.T.astype(np.float64)).astype(np.float32)
+
+    y = torch.zeros((M, N), device=cuda)
+    smol_b200.gemm_bf16(y, N, smol_b200.GEMM_OUT_F32, a_d, lda, w_d, ldw=lda, m=M, n=N, k=K, bias=b_d, gelu=True)
     torch.cuda.synchronize()
-    assert smol_b200.last_error() == 0 and smol_b200.device_error() == 0
-    from siglip_oracle import gelu_tanh
-    want = gelu_tanh(((A.astype(np.float64) @ W.T.astype(np.float64)) + bias).astype(np.float32))
-    e = pyoracle.rel_l2(y.cpu().numpy(), want)
-    assert e < 1e-5, (M, N, K, e)
-print("persistent ok")
-"""
+    _no_error()
+    assert pyoracle.rel_l2(y.cpu().numpy()[rows], gelu_tanh(base + bias)) < 1e-5
+
+    y0 = torch.randn((M, N), device=cuda)
+    y = y0.clone()
+    smol_b200.gemm_bf16(y, N, smol_b200.GEMM_OUT_F32_ADD, a_d, lda, w_d, ldw=lda, m=M, n=N, k=K, bias=b_d)
+    torch.cuda.synchronize()
+    assert pyoracle.rel_l2(y.cpu().numpy()[rows], y0.cpu().numpy()[rows] + base + bias) < 1e-5
+
+    yb = torch.zeros((M, N), dtype=torch.bfloat16, device=cuda)
+    smol_b200.gemm_bf16(yb, N, smol_b200.GEMM_OUT_BF16, a_d, lda, w_d, ldw=lda, m=M, n=N, k=K, bias=b_d)
+    torch.cuda.synchronize()
+    _no_error()
+    assert pyoracle.rel_l2(yb.float().cpu().numpy()[rows], base + bias) < 4e-3
 
 
 @pytest.mark.new_on_gpu(stage=1)
-def test_gemm_bf16_persistent_form(cuda):
-    """The persistent GEMM (SMOL_GEMM_PERSISTENT=1, read when the library loads, so it
-    runs in a child process): more tiles than SMs (up to 4 per CTA, so both accumulators
-    are reused), ragged tails, bias + GELU."""
-    import subprocess
-    import sys
-    here = os.path.dirname(os.path.abspath(__file__))
-    root = os.path.dirname(here)
-    code = _PERSISTENT_CHECK.format(oracle=os.path.join(root, "oracle"), pkg=os.path.join(root, "smol-genius_b200"))
-    env = dict(os.environ, SMOL_GEMM_PERSISTENT="1")
-    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, env=env)
-    assert r.returncode == 0 and "persistent ok" in r.stdout, r.stdout + r.stderr
+def test_gemm_bf16_wide_gated_pairs(cuda):
+    """The gated gate/up epilogue on the wide form: 4096 rows x 2*1536 interleaved columns."""
+    from qkn_decoder_oracle import swiglu
+    M, I, K = 4096, 1536, 1024
+    rng = np.random.default_rng(9)
+    t = _dev(cuda)
+    A = pyoracle.round_bf16(rng.standard_normal((M, K)).astype(np.float32))
+    W = pyoracle.round_bf16((rng.standard_normal((2 * I, K)) / np.sqrt(K)).astype(np.float32))
+    rows = rng.integers(0, M, 400)
+    c = (A[rows].astype(np.float64) @ W.T.astype(np.float64)).astype(np.float32)
+    yb = torch.zeros((M, I), dtype=torch.bfloat16, device=cuda)
+    smol_b200.gemm_bf16(yb, I, smol_b200.GEMM_OUT_BF16, t(pyoracle.bf16_bits(A)), K, t(pyoracle.bf16_bits(W)), K, M,
+                        2 * I, K, act=smol_b200.ACT_SWIGLU_PAIRS)
+    torch.cuda.synchronize()
+    _no_error()
+    assert pyoracle.rel_l2(yb.float().cpu().numpy()[rows], swiglu(c)) < 4e-3
 
 
 @pytest.mark.new_on_gpu(stage=1)
