@@ -52,8 +52,12 @@ struct PrefillShape {
     static constexpr int kOffQ = 0;
     static constexpr int kOffK = kOffQ + kQBytes;
     static constexpr int kOffV = kOffK + kStages * kKvBytes;
-    static constexpr int kOffBar = kOffV + kStages * kKvBytes;
+    // Epilogue staging: 8 KB per softmax warp (two 32-row x 128-byte TMA store boxes).
+    static constexpr int kStageWarpBytes = 2 * 32 * 128;
+    static constexpr int kOffStage = kOffV + kStages * kKvBytes;
+    static constexpr int kOffBar = kOffStage + 4 * kStageWarpBytes;
     static constexpr int kUsed = kOffBar + 256 + 1024;
+    static_assert(kUsed <= 227 * 1024, "shared memory");
     // At least ~116 KB so that a single CTA is resident per SM: every CTA
     // allocates all 512 TMEM columns.
     static constexpr int kSmemBytes = kUsed > 118 * 1024 ? kUsed : 118 * 1024;
@@ -81,6 +85,9 @@ struct PrefillParams {
     unsigned *err;
     int n_windows;
     int seq_q, seq_k, n_heads, group, mask_kind, q_offset, prefix_len, window;
+    // v1: query rows per position in a tile -- the `pack` heads of a KV group that share
+    // its keys (row r of a tile is position r / pack of head h + r % pack); 1 = one head
+    int pack;
     float scale, scale_log2, softcap;
     // v2 work items: n_qblocks x n_ygroups (head pairs or heads) x batch
     int n_qblocks, n_ygroups, batch, pair_heads, heavy_first;
@@ -180,7 +187,7 @@ __device__ __forceinline__ int first_key_tile(const PrefillParams &p, int lo)
 // of rounds r = 0, 1, ... at positions blockIdx.x (even rounds) and gridDim.x-1-blockIdx.x
 // (odd rounds).
 struct Item1 {
-    int qt, h, b, q0;
+    int qt, h, b, q0;      // h: first head of the tile; q0: first packed row (position q0 / pack)
     int lo_min, n_tiles;   // key tiles [lo_min, lo_min + n_tiles*BN) cover every row's keys
 };
 
@@ -191,11 +198,12 @@ __device__ __forceinline__ Item1 item1_geometry(const PrefillParams &p, int k)
     const int nq = p.n_qblocks;
     it.qt = p.heavy_first ? nq - 1 - k % nq : k % nq;
     const int r = k / nq;
-    it.h = r % p.n_ygroups;
+    it.h = (r % p.n_ygroups) * p.pack;
     it.b = r / p.n_ygroups;
     it.q0 = it.qt * kBM;
-    // every mask's [lo, hi) is non-decreasing in the row: first row -> lowest key, last row -> highest
-    int a = it.q0, z = min(it.q0 + kBM, p.seq_q) - 1;
+    // every mask's [lo, hi) is non-decreasing in the position: first position -> lowest
+    // key, last position -> highest
+    int a = it.q0 / p.pack, z = (min(it.q0 + kBM, p.seq_q * p.pack) - 1) / p.pack;
     if (p.mask_kind == SMOL_MASK_WINDOWS) {
         a = max(a, p.window_starts[0]);
         z = min(z, p.window_starts[p.n_windows] - 1);
@@ -287,8 +295,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 const uint32_t qb = smem_u32(&bars->q_full);
                 mbar_arrive_expect_tx(qb, S::kQBytes);
 #pragma unroll
-                for (int sub = 0; sub < S::kSub; ++sub)
-                    tma_load_3d(smem_u32(sQ + sub * S::kQSubBytes), &p.tq, qb, it.h * HD + sub * 64, it.q0, it.b);
+                for (int sub = 0; sub < S::kSub; ++sub)   // box: 64 columns x pack heads x 128/pack positions
+                    tma_load_4d(smem_u32(sQ + sub * S::kQSubBytes), &p.tq, qb, sub * 64, it.h, it.q0 / p.pack, it.b);
                 ++qit;
                 const int kvh = it.h / p.group;
                 for (int j = 0; j < it.n_tiles; ++j, ++g) {
@@ -390,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         const float cap = p.softcap;
         const float inv_cap = cap > 0.f ? 1.f / cap : 0.f;
         const float kLog2e = 1.4426950408889634f;
+        bool stores_pending = false;   // lane 0: a TMA store from this warp's staging area
         int g0 = 0;
         bool ok = true;
         for (int r = 0; r < n_rounds && ok; ++r) {
@@ -397,7 +406,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             if (k >= n_items) break;
             const Item1 it = item1_geometry<BN>(p, k);
             const int n_tiles = it.n_tiles;
-            const int row = it.q0 + threadIdx.x;
+            const int vrow = it.q0 + static_cast<int>(threadIdx.x);   // packed row of this thread
+            const int row = vrow / p.pack;                            // its position
+            const int head = it.h + vrow % p.pack;
             const bool row_valid = row < p.seq_q;
             int my_lo = 0, my_hi = 0;
             bool my_written = false;
@@ -488,25 +499,89 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 have_o = ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done), (g0 + n_tiles - 1) & 1,
                                                                  p.err, kErrWaitMma));
             tc_fence_after();
-            const bool store = ok && row_valid && my_written;
-            const long long orow = static_cast<long long>(it.b) * p.out_batch_stride +
-                                   static_cast<long long>(store ? row : 0) * p.out_row_stride +
-                                   static_cast<long long>(it.h) * HD;
             const float inv = l > 0.f ? 1.f / l : 0.f;
-            uint32_t rr[32];
+            // Staged epilogue: the warp's 32 rows (32/pack positions x pack heads) go through
+            // shared memory in 128B-swizzled boxes, two at a time, and leave with TMA tensor
+            // stores, so the output is written as whole sectors instead of 16-byte pieces of
+            // 32 rows.  Rows no window covers must stay untouched: such warps store rows.
+            const bool staged = ok && __all_sync(0xffffffffu, my_written || !row_valid);
+            if (staged) {
+                const bool bf = p.out_bf16 != 0;
+                const int box_cols = bf ? 64 : 32;
+                uint8_t *stage = smem + S::kOffStage + warp * S::kStageWarpBytes;
+                const int pos0 = (it.q0 + warp * 32) / p.pack;
+                for (int c0 = 0; c0 < HD; c0 += 2 * box_cols) {   // two boxes per round
+                    if (lane == 0 && stores_pending) bulk_wait_read0();   // the staging is free again
+                    __syncwarp();
+                    for (int c = c0; c < c0 + 2 * box_cols; c += 32) {    // 32 TMEM columns at a time
+                        uint32_t rr[32];
+                        if (have_o) {
+                            tmem_ld32(lane_base + S::kTmO + c, rr);
+                            tmem_ld_wait();
+                        } else {
 #pragma unroll
-            for (int c = 0; c < HD / 32; ++c) {
-                if (have_o) {
-                    tmem_ld32(lane_base + S::kTmO + c * 32, rr);
-                    tmem_ld_wait();
-                } else {
+                            for (int i = 0; i < 32; ++i) rr[i] = 0u;
+                        }
+                        uint8_t *box = stage + ((c - c0) / box_cols) * (32 * 128);
+                        if (bf) {
+                            const int u0 = ((c - c0) % 64) / 8;   // first 16-byte unit of these columns
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) rr[i] = 0u;
+                            for (int u = 0; u < 4; ++u) {
+                                uint4 v;
+                                v.x = pack_bf16x2(__uint_as_float(rr[8 * u]) * inv, __uint_as_float(rr[8 * u + 1]) * inv);
+                                v.y = pack_bf16x2(__uint_as_float(rr[8 * u + 2]) * inv,
+                                                  __uint_as_float(rr[8 * u + 3]) * inv);
+                                v.z = pack_bf16x2(__uint_as_float(rr[8 * u + 4]) * inv,
+                                                  __uint_as_float(rr[8 * u + 5]) * inv);
+                                v.w = pack_bf16x2(__uint_as_float(rr[8 * u + 6]) * inv,
+                                                  __uint_as_float(rr[8 * u + 7]) * inv);
+                                *reinterpret_cast<uint4 *>(box + sw128_offset(lane, u0 + u)) = v;
+                            }
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 8; ++q) {
+                                float4 v = make_float4(__uint_as_float(rr[4 * q]) * inv,
+                                                       __uint_as_float(rr[4 * q + 1]) * inv,
+                                                       __uint_as_float(rr[4 * q + 2]) * inv,
+                                                       __uint_as_float(rr[4 * q + 3]) * inv);
+                                *reinterpret_cast<float4 *>(box + sw128_offset(lane, q)) = v;
+                            }
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+#pragma unroll
+                        for (int bx = 0; bx < 2; ++bx)
+                            tma_store_4d(&p.to, smem_u32(stage + bx * (32 * 128)), c0 + bx * box_cols, it.h, pos0,
+                                         it.b);
+                        bulk_commit();
+                        stores_pending = true;
+                    }
+                    __syncwarp();
                 }
-                if (store) store_row32(p.out, orow + c * 32, rr, inv, p.out_bf16 != 0);
+            } else if (ok) {
+                const bool store = row_valid && my_written;
+                const long long orow = static_cast<long long>(it.b) * p.out_batch_stride +
+                                       static_cast<long long>(store ? row : 0) * p.out_row_stride +
+                                       static_cast<long long>(head) * HD;
+                uint32_t rr[32];
+#pragma unroll
+                for (int c = 0; c < HD / 32; ++c) {
+                    if (have_o) {
+                        tmem_ld32(lane_base + S::kTmO + c * 32, rr);
+                        tmem_ld_wait();
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) rr[i] = 0u;
+                    }
+                    if (store) store_row32(p.out, orow + c * 32, rr, inv, p.out_bf16 != 0);
+                }
             }
             g0 += n_tiles;
         }
+        if (lane == 0 && stores_pending) bulk_wait_read0();   // staging read before the CTA exits
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -1316,9 +1391,21 @@ int launch_prefill(cudaStream_t st, void *out, int64_t out_row_stride, int64_t o
     const int64_t qb = batch > 1 ? q_batch_stride : static_cast<int64_t>(seq_q) * q_row_stride;
     const int64_t kb = batch > 1 ? k_batch_stride : static_cast<int64_t>(kv_rows) * k_row_stride;
     const int64_t vb = batch > 1 ? v_batch_stride : static_cast<int64_t>(kv_rows) * v_row_stride;
-    if (!make_tmap_3d(&p.tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<int64_t>(n_heads) * HD, seq_q, batch,
-                      q_row_stride, qb, 64, kBM))
+    // v1 (head dim 256) packs the heads of a KV group into the rows of a query tile when
+    // the group is a power of two up to 32: each K/V tile then serves all of them, and a
+    // short prefix fills whole tiles (MQA 8/1: 16 positions x 8 heads per tile).
+    const int group = n_heads / n_kv_heads;
+    const int pack = (HD == 256 && group <= 32 && (group & (group - 1)) == 0) ? group : 1;
+    if (HD == 256) {
+        // Q as (column, head, position, batch): box 64 columns x pack heads x 128/pack positions
+        if (!make_tmap_4d(&p.tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HD, n_heads, seq_q, batch, HD, q_row_stride,
+                          qb, 64, pack, kBM / pack))
+            return SMOL_B200_ERR_CUDA;
+    } else if (!make_tmap_3d(&p.tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<int64_t>(n_heads) * HD, seq_q,
+                             batch, q_row_stride, qb, 64, kBM)) {
         return SMOL_B200_ERR_CUDA;
+    }
+    p.pack = pack;
     // K/V boxes are one key tile high: the tile height of the kernel that will run
     // (v1 for head dim 256, v2 otherwise) -- the producer's expect_tx counts on it.
     constexpr int kv_box_rows = KvTileRows<HD>::value;
@@ -1330,13 +1417,18 @@ int launch_prefill(cudaStream_t st, void *out, int64_t out_row_stride, int64_t o
         return SMOL_B200_ERR_CUDA;
     {
         const int64_t ob = batch > 1 ? out_batch_stride : static_cast<int64_t>(seq_q) * out_row_stride;
-        const bool ok = out_bf16
-                            ? make_tmap_3d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                                           static_cast<int64_t>(n_heads) * HD, seq_q, batch, out_row_stride, ob, 64,
-                                           32, 2)
-                            : make_tmap_3d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                                           static_cast<int64_t>(n_heads) * HD, seq_q, batch, out_row_stride, ob, 32,
-                                           32, 4);
+        bool ok;
+        if (HD == 256)   // v1: (column, head, position, batch), box 32 rows = 32/pack positions x pack heads
+            ok = out_bf16 ? make_tmap_4d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HD, n_heads, seq_q, batch,
+                                         HD, out_row_stride, ob, 64, pack, 32 / pack)
+                          : make_tmap_4d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, HD, n_heads, seq_q, batch,
+                                         HD, out_row_stride, ob, 32, pack, 32 / pack);
+        else
+            ok = out_bf16 ? make_tmap_3d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                                         static_cast<int64_t>(n_heads) * HD, seq_q, batch, out_row_stride, ob, 64, 32, 2)
+                          : make_tmap_3d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                         static_cast<int64_t>(n_heads) * HD, seq_q, batch, out_row_stride, ob, 32, 32,
+                                         4);
         if (!ok) return SMOL_B200_ERR_CUDA;
         p.out_bf16 = out_bf16 ? 1 : 0;
         p.n_more = n_more;
@@ -1370,12 +1462,15 @@ int launch_prefill(cudaStream_t st, void *out, int64_t out_row_stride, int64_t o
                 return SMOL_B200_ERR_CUDA;
             attr_set[dev] = true;
         }
-        // work items (query tile, head, batch), query tiles fastest; persistent CTAs
-        p.n_qblocks = (seq_q + kBM - 1) / kBM;
-        p.n_ygroups = n_heads;
+        // work items (query tile of packed rows, head group, batch), query tiles fastest;
+        // persistent CTAs
+        const long long rows = static_cast<long long>(seq_q) * pack;
+        if (rows > 0x7fffffffLL - kBM) return SMOL_B200_ERR_ARGS;
+        p.n_qblocks = static_cast<int>((rows + kBM - 1) / kBM);
+        p.n_ygroups = n_heads / pack;
         p.batch = batch;
         p.heavy_first = (mask_kind == SMOL_MASK_CAUSAL || mask_kind == SMOL_MASK_PREFIX_LM) ? 1 : 0;
-        const long long n_items = static_cast<long long>(p.n_qblocks) * n_heads * batch;
+        const long long n_items = static_cast<long long>(p.n_qblocks) * p.n_ygroups * batch;
         if (n_items > 0x7fffffffLL) return SMOL_B200_ERR_ARGS;
         int grid = static_cast<int>(n_items);
         const int sms = sm_count();

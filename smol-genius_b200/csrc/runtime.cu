@@ -266,6 +266,28 @@ bool make_tmap_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype,
     return true;
 }
 
+bool make_tmap_4d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes, int64_t inner,
+                  int64_t d1, int64_t d2, int64_t d3, int64_t s1, int64_t s2, int64_t s3, int b0, int b1, int b2)
+{
+    if (!encode_fn()) return false;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(d1), static_cast<cuuint64_t>(d2),
+                          static_cast<cuuint64_t>(d3)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(s1) * elem_bytes, static_cast<cuuint64_t>(s2) * elem_bytes,
+                             static_cast<cuuint64_t>(s3) * elem_bytes};
+    cuuint32_t box[4] = {static_cast<cuuint32_t>(b0), static_cast<cuuint32_t>(b1), static_cast<cuuint32_t>(b2), 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = g_encode(map, dtype, 4, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        char buf[128];
+        snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled(4d) failed with %d", static_cast<int>(r));
+        set_error(SMOL_B200_ERR_CUDA, buf);
+        return false;
+    }
+    return true;
+}
+
 }  // namespace smolb200
 
 // ---------------------------------------------------------------------------

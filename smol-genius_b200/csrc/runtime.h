@@ -45,6 +45,10 @@ bool make_tmap_2d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype,
 bool make_tmap_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int64_t inner,
                   int64_t rows, int64_t outer, int64_t row_stride, int64_t outer_stride, int box_inner,
                   int box_rows, int elem_bytes = 2);
+// 4-D tiled map over (inner, d1, d2, d3) with element strides s1, s2, s3 of d1..d3 and
+// box (b0, b1, b2, 1), 128-byte swizzle.
+bool make_tmap_4d(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem_bytes, int64_t inner,
+                  int64_t d1, int64_t d2, int64_t d3, int64_t s1, int64_t s2, int64_t s3, int b0, int b1, int b2);
 
 // ---- kernels (implemented in the .cu files) ----
 size_t decode_workspace_bytes(int n_seqs, int max_kv_len, int n_heads, int n_kv_heads, int head_dim);
