@@ -472,6 +472,9 @@ def test_prefill_golden_prefix_lm(golden, cuda):
     (300, 700, 400, 8, 2, 64, 128, 25.0),
     (64, 0, 0, 2, 1, 128, 0, 0.0),
     (40, 30, -20, 2, 1, 128, 0, 0.0),
+    (64, 0, 0, 8, 1, 256, 0, 0.0),        # head dim 256, packed MQA rows: no keys at all
+    (40, 30, -20, 8, 1, 256, 0, 0.0),     # rows before the first key are zero
+    (300, 300, 0, 4, 2, 256, 40, 30.0),   # packed GQA pairs, window + softcap
 ])
 def test_prefill_edges_vs_oracle(cuda, sq, sk, qo, hq, hkv, hd, win, cap):
     rng = np.random.default_rng(sq * 7 + sk)
