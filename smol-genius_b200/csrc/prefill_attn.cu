@@ -108,6 +108,69 @@ __device__ __forceinline__ float fast_exp2(float x)
     return y;
 }
 
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi)
+{
+    return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c)
+{
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b)
+{
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// The same two operations on float pairs: the pairs are formed and split with mov.b64
+// inside the asm, which the register allocator maps onto register pairs, instead of
+// 64-bit shifts and ors in C++ that can cost integer instructions per element.
+__device__ __forceinline__ void fma2(float &d0, float &d1, float a0, float a1, float b0, float b1, float c0, float c1)
+{
+    asm("{\n\t.reg .b64 a, b, c, d;\n\t"
+        "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+        "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+__device__ __forceinline__ void add2(float &d0, float &d1, float a0, float a1, float b0, float b1)
+{
+    asm("{\n\t.reg .b64 a, b, d;\n\t"
+        "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+        "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+// 2^x for a pair of floats on the FMA pipe instead of MUFU (Cody-Waite range reduction
+// + polynomial): n = round(x) via the 1.5*2^23 constant, f = x - n in [-1/2, 1/2],
+// 2^f from a degree-3 polynomial fitted for relative error (max 7.5e-5 on the interval;
+// coefficients fitted for this kernel), and n added to the exponent field.  x is
+// clamped to >= -126 so the result stays a normal float (2^-126 rounds to 0 in fp16).
+__device__ __forceinline__ void exp2_poly_pair(uint64_t x, float &e0, float &e1)
+{
+    constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+    const float x0 = fmaxf(__uint_as_float(static_cast<uint32_t>(x)), -126.f);
+    const float x1 = fmaxf(__uint_as_float(static_cast<uint32_t>(x >> 32)), -126.f);
+    const uint64_t xx = f2_pack(x0, x1);
+    const uint64_t j = f2_add(xx, f2_pack(kMagic, kMagic));
+    const uint64_t r = f2_add(j, f2_pack(-kMagic, -kMagic));
+    const uint64_t f = f2_fma(r, f2_pack(-1.f, -1.f), xx);
+    uint64_t p = f2_fma(f2_pack(0.05517166f, 0.05517166f), f, f2_pack(0.24261113f, 0.24261113f));
+    p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
+    p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
+    e0 = __uint_as_float(static_cast<uint32_t>(p) + (static_cast<uint32_t>(j) << 23));
+    e1 = __uint_as_float(static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(j >> 32) << 23));
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c)
+{
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // 32 consecutive output values of one row (rr scaled by inv), as fp32 or bf16, to `dst`
 // (element offset `off` of an output buffer) with 16-byte stores.
 __device__ __forceinline__ void store_row32(void *dst, long long off, const uint32_t (&rr)[32], float inv,
@@ -425,30 +488,42 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 const uint32_t s_col = lane_base + (st ? S::kTmS1 : S::kTmS0);
                 float t[BN];
                 {
-                    uint32_t rr[32];
+                    // all column groups in flight before one wait
+                    uint32_t rr[BN / 32][32];
 #pragma unroll
-                    for (int c = 0; c < BN / 32; ++c) {
-                        tmem_ld32(s_col + c * 32, rr);
-                        tmem_ld_wait();
+                    for (int c = 0; c < BN / 32; ++c) tmem_ld32(s_col + c * 32, rr[c]);
+                    tmem_ld_wait();
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(rr[i]);
-                    }
+                    for (int c = 0; c < BN / 32; ++c)
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) t[c * 32 + i] = __uint_as_float(rr[c][i]);
                 }
                 const int key0 = it.lo_min + j * BN;
                 const bool full_tile = row_valid && key0 >= my_lo && key0 + BN <= my_hi;
-                float mx = -INFINITY;
+                if (cap > 0.f) {   // softcapped scores in log2 units; raw scores are scaled below
 #pragma unroll
-                for (int c = 0; c < BN; ++c) {
-                    float x = t[c];
-                    if (cap > 0.f) x = cap * tanhf(x * p.scale * inv_cap) * kLog2e;
-                    else x = x * p.scale_log2;
-                    if (!full_tile) {
-                        const int key = key0 + c;
-                        if (!row_valid || key < my_lo || key >= my_hi) x = -INFINITY;
-                    }
-                    t[c] = x;
-                    mx = fmaxf(mx, x);
+                    for (int c = 0; c < BN; ++c) t[c] = cap * tanhf(t[c] * p.scale * inv_cap) * kLog2e;
                 }
+                if (!full_tile) {
+#pragma unroll
+                    for (int c = 0; c < BN; ++c) {
+                        const int key = key0 + c;
+                        if (!row_valid || key < my_lo || key >= my_hi) t[c] = -INFINITY;
+                    }
+                }
+                // Row max as 8 independent chains of 3-input maxima and a short tree.
+                float mx;
+                {
+                    float pm[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) pm[q] = fmaxf(t[2 * q], t[2 * q + 1]);
+#pragma unroll
+                    for (int c = 16; c < BN; c += 16)
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) pm[q] = max3f(pm[q], t[c + 2 * q], t[c + 2 * q + 1]);
+                    mx = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
+                }
+                if (cap <= 0.f) mx *= p.scale_log2;
                 // The running maximum moves only when the row maximum grew by > 2^8 (or on the
                 // first tile with a visible key, when O of this row is still zero).
                 const bool need = m != -INFINITY && mx > m + kRescaleThreshold;
@@ -470,31 +545,41 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     l *= f;
                 }
                 if (need || (m == -INFINITY && mx > -INFINITY)) m = mx;
-                // P = exp2(t - m) as fp16 pairs over the first BN/2 columns of this S buffer.
-                float psum = 0.f;
+                // P = exp2(t*mul - m) as fp16 pairs over the first BN/2 columns of this S buffer,
+                // one packed FMA per two scores.  A row with no visible key yet (m = -inf) has
+                // every t at -inf, so with -m replaced by 0 its exponentials are exactly 0.
+                const float mul = cap > 0.f ? 1.f : p.scale_log2;
+                const float negm = m != -INFINITY ? -m : 0.f;
+                float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};   // independent pair sums
                 {
-                    const bool live = m != -INFINITY;
                     uint32_t rr[32];
 #pragma unroll
                     for (int c = 0; c < BN / 64; ++c) {
 #pragma unroll
                         for (int i = 0; i < 32; ++i) {
-                            const float e0 = live ? fast_exp2(t[c * 64 + 2 * i] - m) : 0.f;
-                            const float e1 = live ? fast_exp2(t[c * 64 + 2 * i + 1] - m) : 0.f;
-                            psum += e0 + e1;
+                            float x0, x1;
+                            fma2(x0, x1, t[c * 64 + 2 * i], t[c * 64 + 2 * i + 1], mul, mul, negm, negm);
+                            const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+                            add2(acc0[i & 3], acc1[i & 3], acc0[i & 3], acc1[i & 3], e0, e1);
                             rr[i] = pack_f16x2(e0, e1);
                         }
                         tmem_st32(s_col + c * 32, rr);
                     }
                 }
-                l += psum;
+                l += ((acc0[0] + acc0[1]) + (acc0[2] + acc0[3])) + ((acc1[0] + acc1[1]) + (acc1[2] + acc1[3]));
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(smem_u32(&bars->p_full[st]));
             }
             if (!ok) break;
-            // ---- epilogue: O / l -> out (fp32) ----
+            // ---- epilogue: O / l -> out ----
+            // The last S of an item is issued before its second-to-last PV, so o_done can
+            // still be two phases short of the last PV here: wait for both, in order (a
+            // parity wait is only exact one phase ahead).
             bool have_o = n_tiles > 0;
+            if (have_o && n_tiles >= 2)
+                have_o = ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done), (g0 + n_tiles - 2) & 1,
+                                                                 p.err, kErrWaitMma));
             if (have_o)
                 have_o = ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done), (g0 + n_tiles - 1) & 1,
                                                                  p.err, kErrWaitMma));
@@ -664,68 +749,6 @@ struct Barriers2 {
     uint32_t tmem_base;
 };
 
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi)
-{
-    return static_cast<uint64_t>(__float_as_uint(lo)) | (static_cast<uint64_t>(__float_as_uint(hi)) << 32);
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c)
-{
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b)
-{
-    uint64_t d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-// The same two operations on float pairs: the pairs are formed and split with mov.b64
-// inside the asm, which the register allocator maps onto register pairs, instead of
-// 64-bit shifts and ors in C++ that can cost integer instructions per element.
-__device__ __forceinline__ void fma2(float &d0, float &d1, float a0, float a1, float b0, float b1, float c0, float c1)
-{
-    asm("{\n\t.reg .b64 a, b, c, d;\n\t"
-        "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
-        "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
-        : "=f"(d0), "=f"(d1)
-        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
-}
-__device__ __forceinline__ void add2(float &d0, float &d1, float a0, float a1, float b0, float b1)
-{
-    asm("{\n\t.reg .b64 a, b, d;\n\t"
-        "mov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
-        "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
-        : "=f"(d0), "=f"(d1)
-        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-// 2^x for a pair of floats on the FMA pipe instead of MUFU (Cody-Waite range reduction
-// + polynomial): n = round(x) via the 1.5*2^23 constant, f = x - n in [-1/2, 1/2],
-// 2^f from a degree-3 polynomial fitted for relative error (max 7.5e-5 on the interval;
-// coefficients fitted for this kernel), and n added to the exponent field.  x is
-// clamped to >= -126 so the result stays a normal float (2^-126 rounds to 0 in fp16).
-__device__ __forceinline__ void exp2_poly_pair(uint64_t x, float &e0, float &e1)
-{
-    constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
-    const float x0 = fmaxf(__uint_as_float(static_cast<uint32_t>(x)), -126.f);
-    const float x1 = fmaxf(__uint_as_float(static_cast<uint32_t>(x >> 32)), -126.f);
-    const uint64_t xx = f2_pack(x0, x1);
-    const uint64_t j = f2_add(xx, f2_pack(kMagic, kMagic));
-    const uint64_t r = f2_add(j, f2_pack(-kMagic, -kMagic));
-    const uint64_t f = f2_fma(r, f2_pack(-1.f, -1.f), xx);
-    uint64_t p = f2_fma(f2_pack(0.05517166f, 0.05517166f), f, f2_pack(0.24261113f, 0.24261113f));
-    p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
-    p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
-    e0 = __uint_as_float(static_cast<uint32_t>(p) + (static_cast<uint32_t>(j) << 23));
-    e1 = __uint_as_float(static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(j >> 32) << 23));
-}
-
-__device__ __forceinline__ float max3f(float a, float b, float c)
-{
-    float d;
-    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-    return d;
-}
 
 // Exponentials per row and key tile: PolyPairs8 of every 8 pairs go to the FMA-pipe
 // polynomial, the rest to MUFU ex2.  Measured on cfg 5 (hd 128) and cfg 3 (hd 64):
