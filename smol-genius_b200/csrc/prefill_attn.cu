@@ -144,24 +144,26 @@ __device__ __forceinline__ void add2(float &d0, float &d1, float a0, float a1, f
         : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 // 2^x for a pair of floats on the FMA pipe instead of MUFU (Cody-Waite range reduction
-// + polynomial): n = round(x) via the 1.5*2^23 constant, f = x - n in [-1/2, 1/2],
-// 2^f from a degree-3 polynomial fitted for relative error (max 7.5e-5 on the interval;
-// coefficients fitted for this kernel), and n added to the exponent field.  x is
-// clamped to >= -126 so the result stays a normal float (2^-126 rounds to 0 in fp16).
-__device__ __forceinline__ void exp2_poly_pair(uint64_t x, float &e0, float &e1)
+// + polynomial, the published method FlashAttention-4 applies to this bottleneck):
+// n = round(x) via the 1.5*2^23 constant, f = x - n in [-1/2, 1/2], 2^f from a degree-3
+// polynomial fitted here for relative error (max 7.5e-5 on the interval, below the fp16
+// rounding of P), and n added to the exponent field.  x is clamped to >= -126 so the
+// result stays a normal float (2^-126 rounds to 0 in fp16).  Pairs go through f32x2
+// adds and FMAs on register pairs.
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float &e0, float &e1)
 {
-    constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
-    const float x0 = fmaxf(__uint_as_float(static_cast<uint32_t>(x)), -126.f);
-    const float x1 = fmaxf(__uint_as_float(static_cast<uint32_t>(x >> 32)), -126.f);
-    const uint64_t xx = f2_pack(x0, x1);
-    const uint64_t j = f2_add(xx, f2_pack(kMagic, kMagic));
-    const uint64_t r = f2_add(j, f2_pack(-kMagic, -kMagic));
-    const uint64_t f = f2_fma(r, f2_pack(-1.f, -1.f), xx);
-    uint64_t p = f2_fma(f2_pack(0.05517166f, 0.05517166f), f, f2_pack(0.24261113f, 0.24261113f));
-    p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
-    p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
-    e0 = __uint_as_float(static_cast<uint32_t>(p) + (static_cast<uint32_t>(j) << 23));
-    e1 = __uint_as_float(static_cast<uint32_t>(p >> 32) + (static_cast<uint32_t>(j >> 32) << 23));
+    constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23: x + kMagic holds round(x) in its low bits
+    x0 = fmaxf(x0, -126.f);
+    x1 = fmaxf(x1, -126.f);
+    float j0, j1, r0, r1, f0, f1, p0, p1;
+    add2(j0, j1, x0, x1, kMagic, kMagic);
+    add2(r0, r1, j0, j1, -kMagic, -kMagic);          // r = round(x)
+    fma2(f0, f1, r0, r1, -1.f, -1.f, x0, x1);        // f = x - r in [-1/2, 1/2]
+    fma2(p0, p1, 0.05517166f, 0.05517166f, f0, f1, 0.24261113f, 0.24261113f);
+    fma2(p0, p1, p0, p1, f0, f1, 0.69326097f, 0.69326097f);
+    fma2(p0, p1, p0, p1, f0, f1, 0.99992806f, 0.99992806f);
+    e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(j0) << 23));
+    e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(j1) << 23));
 }
 
 __device__ __forceinline__ float max3f(float a, float b, float c)
@@ -751,11 +753,12 @@ struct Barriers2 {
 
 
 // Exponentials per row and key tile: PolyPairs8 of every 8 pairs go to the FMA-pipe
-// polynomial, the rest to MUFU ex2.  Measured on cfg 5 (hd 128) and cfg 3 (hd 64):
-// every share above 0 was slower (issue slots, not MUFU, bound the softmax), so the
-// default keeps all exponentials on MUFU; the share stays a build-time knob.
+// polynomial, the rest to MUFU ex2.  Measured on cfg 3 (hd 64, 128 images x 12 layers,
+// two runs each): 0/8 8.72 ms, 1/8 8.42, 2/8 8.32, 3/8 8.48, 4/8 8.73 -- the default
+// for head dim 64 is 2/8.  Head dim 128 keeps all on MUFU.  The share is a build-time
+// knob.
 #ifndef SMOL_POLY8_HD64
-#define SMOL_POLY8_HD64 0
+#define SMOL_POLY8_HD64 2
 #endif
 #ifndef SMOL_POLY8_HD128
 #define SMOL_POLY8_HD128 0
@@ -1183,7 +1186,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                             float x0, x1, e0, e1;
                             fma2(x0, x1, t[c * 64 + 2 * i], t[c * 64 + 2 * i + 1], mul, mul, negm, negm);
                             if ((i & 7) < PolyPairs8) {   // this pair on the FMA pipe
-                                exp2_poly_pair(f2_pack(x0, x1), e0, e1);
+                                exp2_poly2(x0, x1, e0, e1);
                             } else {                      // this pair on MUFU
                                 e0 = fast_exp2(x0);
                                 e1 = fast_exp2(x1);
