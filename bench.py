@@ -71,11 +71,11 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=workload.CFG2["layers"])
     ap.add_argument("--no-decode", action="store_true", help="prefill measurement only (profiling helper)")
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg 1/3/4 block")
-    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4", "decoder", "audio", "siglip", "gemma",
-                                              "prefill", "dropin"],
+    ap.add_argument("--only-config", choices=["cfg1", "cfg3", "cfg4", "decoder", "audio", "siglip", "so400m",
+                                              "gemma", "prefill", "dropin"],
                     default=None,
-                    help="run one of the other measurements alone: cfg 1/3/4, the decoder step, or (not in the "
-                         "default run yet) the audio-encoder windows, the whole SigLIP encoder, the Gemma-"
+                    help="run one of the other measurements alone: cfg 1/3/4, the decoder step, the audio-encoder "
+                         "windows, the whole SigLIP encoder, the So400m (head dim 72) attention, the Gemma-"
                          "configured decoder step, the device prefill, or the decoder-level drop-in against the "
                          "reference decoder on the host")
     ap.add_argument("--images", type=int, default=None, help="cfg 3 image count override")
@@ -611,6 +611,41 @@ def run_audio_windows(pk, segments: int = 64) -> dict:
             "kernel": "prefill2_kernel<64> (window mask)"}
 
 
+def run_so400m_attention(pk, images: int = 128, layers: int = 27) -> dict:
+    """SmolVLM's vision tower attention (SigLIP-So400m: 729 patches of a 378-pixel tile,
+    16 heads of 72, 27 layers): bidirectional, one call per layer over 128 tiles.  The
+    72-column heads run the 128-wide kernel (columns past 72 read as zero), and FLOPs
+    count the real head dim, so that padding shows in the fraction."""
+    import torch
+
+    import smol_b200
+    g = torch.Generator(device="cuda").manual_seed(29)
+    N, h, hd = 729, 16, 72
+    q = torch.randn((images, N, h * hd), device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn((images, N, h * hd), device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn((images, N, h * hd), device="cuda", generator=g).to(torch.float16)
+    o = torch.empty((images, N, h * hd), device="cuda", dtype=torch.bfloat16)
+
+    def tower():
+        for _ in range(layers):
+            smol_b200.prefill_attention(o, q, k, v, images, N, N, h, h, hd, 1 / hd ** 0.5,
+                                        mask_kind=smol_b200.MASK_FULL)
+    tower()
+    a, b = _ev(), _ev()
+    torch.cuda.synchronize()
+    a.record()
+    tower()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b)
+    fl = workload.full_flops(N, h, hd) * images * layers
+    tf = fl / (ms * 1e-3) / 1e12
+    return {"workload": f"SigLIP-So400m attention, {images} tiles x {layers} layers, 729 patches, 16 heads of 72, "
+                        "bf16 output (q/k/v 215 MB each, more than L2)",
+            "ms": round(ms, 3), "tflops": round(tf, 1), "frac_of_bf16_peak": round(tf / pk["bf16_tflops"], 4),
+            "flops": fl, "kernel": "prefill2_kernel<128> on 72-column heads (full mask)"}
+
+
 def run_siglip_encoder(pk, images: int | None = None) -> dict:
     """The whole SigLIP-base encoder on the device (siglip_forward, Part 5): cfg 3's 128
     images of 512 x 512 (1024 patches of 16 x 16), 12 layers, hidden 768, 12 heads, ffn
@@ -940,7 +975,8 @@ def run_other_configs(pk, world: int = 1, rank: int = 0) -> dict:
                 # the rows beside the attention path: whole SigLIP encoder, the audio encoder's
                 # window shape, the device prefill, the Gemma-configured step, and the
                 # reference decoder driver against its decoder-level drop-in
-                "siglip_encoder": lambda: run_siglip_encoder(pk), "audio_windows": lambda: run_audio_windows(pk),
+                "siglip_encoder": lambda: run_siglip_encoder(pk), "so400m_attention": lambda: run_so400m_attention(pk),
+                "audio_windows": lambda: run_audio_windows(pk),
                 "device_prefill": lambda: run_decoder_prefill(pk),
                 "gemma_step_b1": lambda: run_gemma_decoder(pk, 1), "gemma_step_b8": lambda: run_gemma_decoder(pk, 8),
                 "decoder_dropin": run_decoder_dropin}
@@ -1189,6 +1225,7 @@ def main():
               "cfg4": run_cfg4, "decoder": lambda: [run_decoder(pk, 1), run_decoder(pk, 8)],
               "audio": lambda: run_audio_windows(pk),
               "siglip": lambda: run_siglip_encoder(pk, args.images),
+              "so400m": lambda: run_so400m_attention(pk),
               "gemma": lambda: [run_gemma_decoder(pk, 1), run_gemma_decoder(pk, 8)],
               "prefill": lambda: run_decoder_prefill(pk),
               "dropin": run_decoder_dropin}[args.only_config]

@@ -85,6 +85,7 @@ struct PrefillParams {
     unsigned *err;
     int n_windows;
     int seq_q, seq_k, n_heads, group, mask_kind, q_offset, prefix_len, window;
+    int hd;   // the caller's head dim (<= the kernel's HD: columns past it are zero on load, not stored)
     // v1: query rows per position in a tile -- the `pack` heads of a KV group that share
     // its keys (row r of a tile is position r / pack of head h + r % pack); 1 = one head
     int pack;
@@ -173,15 +174,17 @@ __device__ __forceinline__ float max3f(float a, float b, float c)
     return d;
 }
 
-// 32 consecutive output values of one row (rr scaled by inv), as fp32 or bf16, to `dst`
-// (element offset `off` of an output buffer) with 16-byte stores.
+// The first `ncols` (a multiple of 8, <= 32) of 32 consecutive output values of one row
+// (rr scaled by inv), as fp32 or bf16, to `dst` (element offset `off` of an output
+// buffer) with 16-byte stores.
 __device__ __forceinline__ void store_row32(void *dst, long long off, const uint32_t (&rr)[32], float inv,
-                                            bool bf16)
+                                            bool bf16, int ncols = 32)
 {
     if (bf16) {
         uint16_t *o = static_cast<uint16_t *>(dst) + off;
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
+            if (i >= ncols) break;
             uint4 v;
             v.x = pack_bf16x2(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv);
             v.y = pack_bf16x2(__uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
@@ -193,7 +196,8 @@ __device__ __forceinline__ void store_row32(void *dst, long long off, const uint
         float *o = static_cast<float *>(dst) + off;
 #pragma unroll
         for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4 *>(o + i) =
+            if (i < ncols)
+                *reinterpret_cast<float4 *>(o + i) =
                 make_float4(__uint_as_float(rr[i]) * inv, __uint_as_float(rr[i + 1]) * inv,
                             __uint_as_float(rr[i + 2]) * inv, __uint_as_float(rr[i + 3]) * inv);
     }
@@ -374,8 +378,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     mbar_arrive_expect_tx(kb, S::kKvBytes);
 #pragma unroll
                     for (int sub = 0; sub < S::kSub; ++sub)
-                        tma_load_3d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb,
-                                    kvh * HD + sub * 64, key0, it.b);
+                        tma_load_4d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb, sub * 64,
+                                    kvh, key0, it.b);
                     if (g >= 2 &&
                         !(ok = mbar_wait(smem_u32(&bars->v_empty[st]), ((g >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty)))
                         break;
@@ -383,8 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     mbar_arrive_expect_tx(vb, S::kKvBytes);
 #pragma unroll
                     for (int sub = 0; sub < S::kSub; ++sub)
-                        tma_load_3d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb,
-                                    kvh * HD + sub * 64, key0, it.b);
+                        tma_load_4d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb, sub * 64,
+                                    kvh, key0, it.b);
                 }
             }
             // Drain: whatever was issued must land before the CTA can exit.
@@ -639,9 +643,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     __syncwarp();
                     if (lane == 0) {
 #pragma unroll
-                        for (int bx = 0; bx < 2; ++bx)
-                            tma_store_4d(&p.to, smem_u32(stage + bx * (32 * 128)), c0 + bx * box_cols, it.h, pos0,
-                                         it.b);
+                        for (int bx = 0; bx < 2; ++bx)   // boxes wholly past the caller's head dim: none
+                            if (c0 + bx * box_cols < p.hd)
+                                tma_store_4d(&p.to, smem_u32(stage + bx * (32 * 128)), c0 + bx * box_cols, it.h,
+                                             pos0, it.b);
                         bulk_commit();
                         stores_pending = true;
                     }
@@ -651,7 +656,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 const bool store = row_valid && my_written;
                 const long long orow = static_cast<long long>(it.b) * p.out_batch_stride +
                                        static_cast<long long>(store ? row : 0) * p.out_row_stride +
-                                       static_cast<long long>(head) * HD;
+                                       static_cast<long long>(head) * p.hd;
                 uint32_t rr[32];
 #pragma unroll
                 for (int c = 0; c < HD / 32; ++c) {
@@ -662,7 +667,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 #pragma unroll
                         for (int i = 0; i < 32; ++i) rr[i] = 0u;
                     }
-                    if (store) store_row32(p.out, orow + c * 32, rr, inv, p.out_bf16 != 0);
+                    if (store && c * 32 < p.hd)
+                        store_row32(p.out, orow + c * 32, rr, inv, p.out_bf16 != 0, min(32, p.hd - c * 32));
                 }
             }
             g0 += n_tiles;
@@ -902,8 +908,8 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                 for (int t = 0; t < 2; ++t)
 #pragma unroll
                     for (int sub = 0; sub < S::kSub; ++sub)
-                        tma_load_3d(smem_u32(sQ + t * S::kQBytes + sub * S::kQSubBytes), &p.tq, qbar,
-                                    it.head[t] * HD + sub * 64, it.row0[t], it.b);
+                        tma_load_4d(smem_u32(sQ + t * S::kQBytes + sub * S::kQSubBytes), &p.tq, qbar, sub * 64,
+                                    it.head[t], it.row0[t], it.b);
                 ++qit;
                 const int kvh = it.head[0] / p.group;
                 for (int j = 0; j < it.n_tiles; ++j, ++g) {
@@ -916,8 +922,8 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     mbar_arrive_expect_tx(kb, S::kKvBytes);
 #pragma unroll
                     for (int sub = 0; sub < S::kSub; ++sub)
-                        tma_load_3d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb,
-                                    kvh * HD + sub * 64, key0, it.b);
+                        tma_load_4d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb, sub * 64,
+                                    kvh, key0, it.b);
                     if (g >= ST &&
                         !(ok = mbar_wait(smem_u32(&bars->v_empty[st]), ((g / ST) - 1) & 1, p.err, kErrWaitTmaEmpty)))
                         break;
@@ -925,8 +931,8 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     mbar_arrive_expect_tx(vb, S::kKvBytes);
 #pragma unroll
                     for (int sub = 0; sub < S::kSub; ++sub)
-                        tma_load_3d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb,
-                                    kvh * HD + sub * 64, key0, it.b);
+                        tma_load_4d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb, sub * 64,
+                                    kvh, key0, it.b);
                 }
             }
             // Drain: the last Q and the last ST key tiles must have landed before exit.
@@ -1297,7 +1303,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                                                                          sw128_offset(rr_, u % 8));
                         const long long off = static_cast<long long>(it.b) * p.out_batch_stride +
                                               static_cast<long long>(grow) * p.out_row_stride +
-                                              static_cast<long long>(head) * HD + u * elems;
+                                              static_cast<long long>(head) * p.hd + u * elems;
                         const long long boff = off * (bf ? 2 : 4);
                         for (int o = 0; o < p.n_more; ++o)
                             *reinterpret_cast<uint4 *>(static_cast<uint8_t *>(p.out_more[o]) + boff) = v;
@@ -1309,7 +1315,8 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     const int y = it.row0[tile] + (warp & 3) * 32;
                     const int box_cols = bf ? 64 : 32;
                     for (int c = 0; c < HD / box_cols; ++c)
-                        tma_store_3d(&p.to, smem_u32(stage + c * (32 * 128)), head * HD + c * box_cols, y, it.b);
+                        if (c * box_cols < p.hd)   // boxes wholly past the caller's head dim: none
+                            tma_store_4d(&p.to, smem_u32(stage + c * (32 * 128)), c * box_cols, head, y, it.b);
                     bulk_commit();
                     stores_pending = true;
                 }
@@ -1326,12 +1333,14 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
 #pragma unroll
                         for (int i = 0; i < 32; ++i) rr[i] = 0u;
                     }
-                    if (store) {
+                    if (store && c * 32 < p.hd) {
                         const long long off = static_cast<long long>(it.b) * p.out_batch_stride +
                                               static_cast<long long>(row) * p.out_row_stride +
-                                              static_cast<long long>(head) * HD + c * 32;
-                        store_row32(p.out, off, rr, inv, p.out_bf16 != 0);
-                        for (int o = 0; o < p.n_more; ++o) store_row32(p.out_more[o], off, rr, inv, p.out_bf16 != 0);
+                                              static_cast<long long>(head) * p.hd + c * 32;
+                        const int nc = min(32, p.hd - c * 32);
+                        store_row32(p.out, off, rr, inv, p.out_bf16 != 0, nc);
+                        for (int o = 0; o < p.n_more; ++o)
+                            store_row32(p.out_more[o], off, rr, inv, p.out_bf16 != 0, nc);
                     }
                 }
             }
@@ -1407,7 +1416,8 @@ int launch_prefill(cudaStream_t st, void *out, int64_t out_row_stride, int64_t o
                    int64_t k_row_stride, int64_t k_batch_stride, const uint16_t *v, int64_t v_row_stride,
                    int64_t v_batch_stride, int batch, int seq_q, int seq_k, int n_heads, int n_kv_heads,
                    float scale, int mask_kind, int q_offset, int prefix_len, int window, float softcap,
-                   const int *window_starts, int n_windows, void *const *more_outs, int n_more, int out_bf16)
+                   const int *window_starts, int n_windows, void *const *more_outs, int n_more, int out_bf16,
+                   int hd)
 {
     using S = PrefillShape<HD>;
     PrefillParams p;
@@ -1417,44 +1427,36 @@ int launch_prefill(cudaStream_t st, void *out, int64_t out_row_stride, int64_t o
     const int64_t qb = batch > 1 ? q_batch_stride : static_cast<int64_t>(seq_q) * q_row_stride;
     const int64_t kb = batch > 1 ? k_batch_stride : static_cast<int64_t>(kv_rows) * k_row_stride;
     const int64_t vb = batch > 1 ? v_batch_stride : static_cast<int64_t>(kv_rows) * v_row_stride;
-    // v1 (head dim 256) packs the heads of a KV group into the rows of a query tile when
-    // the group is a power of two up to 32: each K/V tile then serves all of them, and a
-    // short prefix fills whole tiles (MQA 8/1: 16 positions x 8 heads per tile).
+    // Every operand is described as (column, head, row, batch) with the caller's head dim
+    // `hd` <= HD: the kernel's 64-column boxes past `hd` read zeros (outside the tensor),
+    // which change no score and no output column, and its stores there are clipped or
+    // skipped -- so a head dim such as SigLIP-So400m's 72 runs the 128-wide kernel without
+    // a padded copy.  v1 (head dim 256) packs the heads of a KV group into the rows of a
+    // query tile when the group is a power of two up to 32: each K/V tile then serves all
+    // of them, and a short prefix fills whole tiles (MQA 8/1: 16 positions x 8 heads).
     const int group = n_heads / n_kv_heads;
     const int pack = (HD == 256 && group <= 32 && (group & (group - 1)) == 0) ? group : 1;
-    if (HD == 256) {
-        // Q as (column, head, position, batch): box 64 columns x pack heads x 128/pack positions
-        if (!make_tmap_4d(&p.tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HD, n_heads, seq_q, batch, HD, q_row_stride,
-                          qb, 64, pack, kBM / pack))
-            return SMOL_B200_ERR_CUDA;
-    } else if (!make_tmap_3d(&p.tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<int64_t>(n_heads) * HD, seq_q,
-                             batch, q_row_stride, qb, 64, kBM)) {
+    // Q: box 64 columns x pack heads x 128/pack positions
+    if (!make_tmap_4d(&p.tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hd, n_heads, seq_q, batch, hd, q_row_stride, qb,
+                      64, pack, kBM / pack))
         return SMOL_B200_ERR_CUDA;
-    }
     p.pack = pack;
+    p.hd = hd;
     // K/V boxes are one key tile high: the tile height of the kernel that will run
     // (v1 for head dim 256, v2 otherwise) -- the producer's expect_tx counts on it.
     constexpr int kv_box_rows = KvTileRows<HD>::value;
-    if (!make_tmap_3d(&p.tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, static_cast<int64_t>(n_kv_heads) * HD, kv_rows,
-                      batch, k_row_stride, kb, 64, kv_box_rows))
-        return SMOL_B200_ERR_CUDA;
-    if (!make_tmap_3d(&p.tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, static_cast<int64_t>(n_kv_heads) * HD, kv_rows,
-                      batch, v_row_stride, vb, 64, kv_box_rows))
+    if (!make_tmap_4d(&p.tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hd, n_kv_heads, kv_rows, batch, hd, k_row_stride,
+                      kb, 64, 1, kv_box_rows) ||
+        !make_tmap_4d(&p.tv, v, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, hd, n_kv_heads, kv_rows, batch, hd, v_row_stride,
+                      vb, 64, 1, kv_box_rows))
         return SMOL_B200_ERR_CUDA;
     {
+        // output boxes: 32 rows (32/pack positions x pack heads) x 128 bytes
         const int64_t ob = batch > 1 ? out_batch_stride : static_cast<int64_t>(seq_q) * out_row_stride;
-        bool ok;
-        if (HD == 256)   // v1: (column, head, position, batch), box 32 rows = 32/pack positions x pack heads
-            ok = out_bf16 ? make_tmap_4d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, HD, n_heads, seq_q, batch,
-                                         HD, out_row_stride, ob, 64, pack, 32 / pack)
-                          : make_tmap_4d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, HD, n_heads, seq_q, batch,
-                                         HD, out_row_stride, ob, 32, pack, 32 / pack);
-        else
-            ok = out_bf16 ? make_tmap_3d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
-                                         static_cast<int64_t>(n_heads) * HD, seq_q, batch, out_row_stride, ob, 64, 32, 2)
-                          : make_tmap_3d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
-                                         static_cast<int64_t>(n_heads) * HD, seq_q, batch, out_row_stride, ob, 32, 32,
-                                         4);
+        const bool ok = out_bf16 ? make_tmap_4d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hd, n_heads, seq_q,
+                                                batch, hd, out_row_stride, ob, 64, pack, 32 / pack)
+                                 : make_tmap_4d(&p.to, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, hd, n_heads, seq_q,
+                                                batch, hd, out_row_stride, ob, 32, pack, 32 / pack);
         if (!ok) return SMOL_B200_ERR_CUDA;
         p.out_bf16 = out_bf16 ? 1 : 0;
         p.n_more = n_more;
@@ -1541,7 +1543,10 @@ int prefill_attention(cudaStream_t st, void *out, int64_t out_row_stride, int64_
                       int out_bf16)
 {
     if (batch <= 0 || seq_q <= 0) return SMOL_B200_OK;
-    if (n_more < 0 || n_more > kMaxExtraOuts || (n_more > 0 && (!more_outs || head_dim == 256)))
+    // the kernel's head dim: 64, 128 or 256, the smallest that holds head_dim
+    const int kernel_hd = head_dim <= 64 ? 64 : head_dim <= 128 ? 128 : 256;
+    if (n_more < 0 || n_more > kMaxExtraOuts ||
+        (n_more > 0 && (!more_outs || head_dim == 256 || head_dim != kernel_hd)))
         return SMOL_B200_ERR_ARGS;
     for (int i = 0; i < n_more; ++i)
         if (!more_outs[i] || (reinterpret_cast<uintptr_t>(more_outs[i]) & 15)) return SMOL_B200_ERR_ARGS;
@@ -1549,7 +1554,7 @@ int prefill_attention(cudaStream_t st, void *out, int64_t out_row_stride, int64_
         batch > 65535 || n_heads > 65535 || mask_kind < 0 || mask_kind > SMOL_MASK_FULL)
         return SMOL_B200_ERR_ARGS;
     if (mask_kind == SMOL_MASK_WINDOWS && (!window_starts || n_windows <= 0)) return SMOL_B200_ERR_ARGS;
-    if (head_dim != 64 && head_dim != 128 && head_dim != 256) return SMOL_B200_ERR_ARGS;
+    if (head_dim <= 0 || head_dim > 256 || head_dim % 8) return SMOL_B200_ERR_ARGS;   // 16-byte head rows
     const uintptr_t align = reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) |
                             reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(out);
     if (align & 15) return SMOL_B200_ERR_ARGS;
@@ -1565,8 +1570,9 @@ int prefill_attention(cudaStream_t st, void *out, int64_t out_row_stride, int64_
 #define SMOL_PREFILL_ARGS                                                                                      \
     st, out, out_row_stride, out_batch_stride, q, q_row_stride, q_batch_stride, k, k_row_stride, k_batch_stride, \
         v, v_row_stride, v_batch_stride, batch, seq_q, seq_k, n_heads, n_kv_heads, scale,      \
-        mask_kind, q_offset, prefix_len, window, softcap, window_starts, n_windows, more_outs, n_more, out_bf16
-    switch (head_dim) {
+        mask_kind, q_offset, prefix_len, window, softcap, window_starts, n_windows, more_outs, n_more, out_bf16, \
+        head_dim
+    switch (kernel_hd) {
     case 64: return launch_prefill<64>(SMOL_PREFILL_ARGS);
     case 128: return launch_prefill<128>(SMOL_PREFILL_ARGS);
     default: return launch_prefill<256>(SMOL_PREFILL_ARGS);

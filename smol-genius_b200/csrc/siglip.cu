@@ -156,8 +156,10 @@ bool layers_ok(const smol_b200_siglip_layer *layers, int n_layers)
 bool encoder_shape_ok(int hidden, int heads, int ffn)
 {
     if (hidden <= 0 || heads <= 0 || hidden % heads || ffn <= 0 || hidden % 8 || ffn % 8) return false;
+    // any head dim the prefill kernel takes: a multiple of 8 up to 256 (SigLIP-base 64,
+    // SigLIP-So400m 72)
     const int hd = hidden / heads;
-    return hd == 64 || hd == 128 || hd == 256;
+    return hd % 8 == 0 && hd <= 256;
 }
 
 bool model_ok(const smol_b200_siglip_model *m)

@@ -169,7 +169,13 @@ def test_siglip_workspace_sizes_and_shape_checks():
     # (1024 patches)
     T = 1024
     assert one >= T * (768 * 2 + 5 * 768 * 2 + 3072 * 2)
-    assert smol_b200.siglip_workspace_bytes(_siglip_model(heads=16), 1) == 0           # head dim 48
+    # head dims: any multiple of 8 up to 256 (the prefill kernel zero-fills the columns
+    # up to its own 64/128/256), so 48 and SigLIP-So400m's 72 run; 12 and 153.6 do not
+    assert smol_b200.siglip_workspace_bytes(_siglip_model(heads=16), 1) > 0            # head dim 48
+    assert smol_b200.siglip_workspace_bytes(_siglip_model(heads=64), 1) == 0           # head dim 12
+    assert smol_b200.siglip_workspace_bytes(_siglip_model(heads=5), 1) == 0            # 768 / 5
+    so400m = dict(hidden=1152, heads=16, ffn=4304, patch=14, image_size=378, num_positions=729, patch_ld=592)
+    assert smol_b200.siglip_workspace_bytes(_siglip_model(**so400m), 1) > 0             # head dim 72
     assert smol_b200.siglip_workspace_bytes(_siglip_model(num_positions=1000), 1) == 0  # fewer positions than patches
     assert smol_b200.siglip_workspace_bytes(_siglip_model(patch_ld=770), 1) == 0       # stride not a multiple of 8
     assert smol_b200.siglip_workspace_bytes(_siglip_model(ffn=3070), 1) == 0

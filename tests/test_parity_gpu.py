@@ -475,6 +475,9 @@ def test_prefill_golden_prefix_lm(golden, cuda):
     (64, 0, 0, 8, 1, 256, 0, 0.0),        # head dim 256, packed MQA rows: no keys at all
     (40, 30, -20, 8, 1, 256, 0, 0.0),     # rows before the first key are zero
     (300, 300, 0, 4, 2, 256, 40, 30.0),   # packed GQA pairs, window + softcap
+    (129, 200, 71, 4, 2, 72, 0, 0.0),     # head dim 72 (SigLIP-So400m) on the 128-wide kernel
+    (150, 150, 0, 2, 2, 40, 0, 20.0),     # head dim 40 on the 64-wide kernel
+    (100, 140, 40, 8, 1, 136, 50, 0.0),   # head dim 136 on the 256-wide kernel, packed MQA rows
 ])
 def test_prefill_edges_vs_oracle(cuda, sq, sk, qo, hq, hkv, hd, win, cap):
     rng = np.random.default_rng(sq * 7 + sk)
@@ -537,6 +540,31 @@ def test_prefill_bf16_output_is_rounded_fp32_output(cuda, hd, hq, hkv, mask):
         float((out16.float() - want.float()).abs().max())
     if mask == "windows":
         assert bool((out16[:, :5].float() == 5.0).all()) and bool((out16[:, 300:].float() == 5.0).all())
+
+
+def test_prefill_siglip_so400m_head_dim_72(cuda):
+    # SmolVLM's vision tower (SigLIP-So400m: 729 patches, 16 heads of 72) -- bidirectional
+    # attention per image on the 128-wide kernel with the caller's 72-column rows: the
+    # columns past 72 are read as zero and never written, so the output rows (and the
+    # 8 columns of padding the strided output keeps between them) stay exact.
+    rng = np.random.default_rng(729)
+    B, N, h, hd = 2, 729, 16, 72
+    q, k, v = rnd_bf16(rng, B, N, h * hd), rnd_bf16(rng, B, N, h * hd), rnd_bf16(rng, B, N, h * hd)
+    ow = h * hd + 8
+    strides = ((ow, N * ow), (h * hd, N * h * hd), (h * hd, N * h * hd), (h * hd, N * h * hd))
+    args = (dev_bf16(q, cuda), dev_bf16(k, cuda), dev_f16(v, cuda), B, N, N, h, h, hd, 1 / np.sqrt(hd))
+    out32 = torch.full((B, N, ow), 5.0, device=cuda)
+    smol_b200.prefill_attention(out32, *args, mask_kind=smol_b200.MASK_FULL, strides=strides)
+    out16 = torch.full((B, N, ow), 5.0, device=cuda, dtype=torch.bfloat16)
+    smol_b200.prefill_attention(out16, *args, mask_kind=smol_b200.MASK_FULL, strides=strides)
+    torch.cuda.synchronize()
+    no_error()
+    got = out32.cpu().numpy()
+    assert bool((got[:, :, h * hd:] == 5.0).all())
+    for b in range(B):
+        want = pyoracle.oracle().bidirectional_attention(q[b], k[b], v[b], N, h, hd, 1 / np.sqrt(hd), [0, N])
+        assert_close(got[b, :, :h * hd], want, f"so400m image {b}")
+    assert torch.equal(out16.view(torch.int16), out32.to(torch.bfloat16).view(torch.int16))
 
 
 def test_bf16_decoder_reference_second_oracle(cuda):

@@ -220,6 +220,23 @@ def test_siglip_forward_matches_oracle_and_reference(cuda, case):
     print(f"{case}: rel-L2 {e:.2e} vs the device-format oracle, {pyoracle.rel_l2(got, ref):.2e} vs the reference")
 
 
+def test_siglip_forward_head_dim_72(cuda):
+    """SmolVLM's SigLIP-So400m layer shape (hidden 1152, 16 heads of 72) through the whole
+    device forward: the attention runs the 128-wide prefill kernel on 72-column heads.
+    Two layers, a 224-pixel image of 16-pixel patches (196 patches) and a shorter MLP
+    keep the oracle quick; the head dim is what this checks."""
+    m = SiglipOracle(hidden=1152, heads=16, ffn=1536, layers=2, patch=16, image=224, seed=11)
+    images = m.images(2, 13)
+    model, keep = _upload(m, cuda)
+    ws = torch.zeros(smol_b200.siglip_workspace_bytes(model, 2), dtype=torch.uint8, device=cuda)
+    out = torch.zeros((2, m.n_pos, m.H), device=cuda)
+    smol_b200.siglip_forward(out, _dev(cuda)(images), 2, model, ws)
+    torch.cuda.synchronize()
+    _no_error()
+    e = pyoracle.rel_l2(out.cpu().numpy(), m.forward(images, device_formats=True))
+    assert e < 5e-3, e
+
+
 def test_encoder_layers_with_windows(cuda):
     """The layer stack alone with attention windows -- the Qwen3-ASR audio encoder's form
     (encoder.c:449-484, eps 1e-5): ten 104-token windows, the last ragged, 4 heads of 64
