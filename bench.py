@@ -1225,7 +1225,7 @@ def main():
               "cfg4": run_cfg4, "decoder": lambda: [run_decoder(pk, 1), run_decoder(pk, 8)],
               "audio": lambda: run_audio_windows(pk),
               "siglip": lambda: run_siglip_encoder(pk, args.images),
-              "so400m": lambda: run_so400m_attention(pk),
+              "so400m": lambda: run_so400m_attention(pk, args.images or 128, 1 if args.images else 27),
               "gemma": lambda: [run_gemma_decoder(pk, 1), run_gemma_decoder(pk, 8)],
               "prefill": lambda: run_decoder_prefill(pk),
               "dropin": run_decoder_dropin}[args.only_config]

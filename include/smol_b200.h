@@ -214,7 +214,9 @@ SMOL_B200_API int smol_b200_decode_attention_noalloc(
  * of head h attends the keys the mask allows (see SMOL_MASK_*), further limited to
  * [pos-window+1, ...] when window > 0 and capped by softcap when softcap > 0.
  * q, k: bf16; v: fp16; out: fp32.  Strides are in elements; row strides must be
- * multiples of 8 and pointers 16-byte aligned.  head_dim: 64, 128 or 256.
+ * multiples of 8 and pointers 16-byte aligned.  head_dim: any multiple of 8 up to 256
+ * (the kernel for 64, 128 or 256 columns runs, reading the columns past head_dim as
+ * zero: SigLIP-So400m's 72 takes the 128-wide kernel without a padded copy).
  * window_starts (device, n_windows+1 entries) is read for SMOL_MASK_WINDOWS only.
  * GQA: head h reads KV head h / (n_heads/n_kv_heads). */
 SMOL_B200_API int smol_b200_prefill_attention(
@@ -232,7 +234,7 @@ SMOL_B200_API int smol_b200_prefill_attention(
  * all-gather of its output become one kernel: every output row leaves the CTA for this
  * GPU (TMA store) and, as plain stores over NVLink, for every peer, while later tiles
  * compute.
- * out_list is a host array.  Head dims 64 and 128 (the tcgen05 two-tile kernel). */
+ * out_list is a host array.  Head dims exactly 64 or 128 (the tcgen05 two-tile kernel). */
 SMOL_B200_API int smol_b200_prefill_attention_multi(
     void *stream, float *const *out_list, int n_out, int64_t out_row_stride,
     int64_t out_batch_stride, const uint16_t *q, int64_t q_row_stride, int64_t q_batch_stride,

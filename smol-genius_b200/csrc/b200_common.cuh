@@ -125,6 +125,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigne
     }
 }
 
+// The same wait by every lane of a converged warp, with one answer for all of them.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, unsigned *err, unsigned code)
+{
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, code));
+}
+
 // ---------------------------------------------------------------------------
 // TMA (tensor copies, global -> shared, completion on an mbarrier).  No cluster
 // multicast is used anywhere in this library.
@@ -313,6 +319,40 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
         "{ .reg .pred p; setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p; }" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+        : "memory");
+}
+
+// Warp-collective forms for an MMA warp that runs converged: every lane computes the
+// (warp-uniform) operands and elect.sync picks the one lane that issues, so the
+// operands stay in the uniform datapath instead of being moved there for each MMA by
+// a single divergent thread.
+__device__ __forceinline__ void umma_ss_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate)
+{
+    const uint32_t z = 0;
+    asm volatile(
+        "{ .reg .pred p, e; .reg .b32 l; elect.sync l|e, 0xffffffff; setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p; }" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate)
+{
+    const uint32_t z = 0;
+    asm volatile(
+        "{ .reg .pred p, e; .reg .b32 l; elect.sync l|e, 0xffffffff; setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p; }" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit_elect(uint32_t bar)
+{
+    asm volatile(
+        "{ .reg .pred e; .reg .b32 l; elect.sync l|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0]; }" ::"r"(bar)
         : "memory");
 }
 

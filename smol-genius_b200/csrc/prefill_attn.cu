@@ -39,6 +39,9 @@ constexpr int kSoftmaxThreads = 128;
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
 constexpr float kRescaleThreshold = 8.0f;   // log2 units
+// prefill2: a tile's row sum of exponentials against the row's reference point may
+// reach 2^15 before the row moves its reference (each P value then fits fp16)
+constexpr float kSpecSumLimit = 32768.0f;
 
 template <int HD>
 struct PrefillShape {
@@ -399,26 +402,27 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             }
         }
     } else if (warp == kMmaWarp) {
-        // ================= tcgen05 issuer (one thread) =================
-        if (lane == 0) {
+        // ================= tcgen05 issuer: the whole warp, converged; one elected
+        // lane issues each MMA and commit =================
+        {
             constexpr uint32_t idesc_s = umma_idesc_f16(kBM, BN, true, false);
             constexpr uint32_t idesc_pv = umma_idesc_f16(kBM, HD, false, true);
             const uint32_t q_addr = smem_u32(sQ);
             // O += P(g) V(g); `first` starts the accumulation of an item
             auto issue_pv = [&](int g, bool first) -> bool {
                 const int st = g & 1;
-                if (!mbar_wait(smem_u32(&bars->p_full[st]), (g >> 1) & 1, p.err, kErrWaitSoftmax)) return false;
-                if (!mbar_wait(smem_u32(&bars->v_full[st]), (g >> 1) & 1, p.err, kErrWaitTmaFull)) return false;
+                if (!mbar_wait_warp(smem_u32(&bars->p_full[st]), (g >> 1) & 1, p.err, kErrWaitSoftmax)) return false;
+                if (!mbar_wait_warp(smem_u32(&bars->v_full[st]), (g >> 1) & 1, p.err, kErrWaitTmaFull)) return false;
                 tc_fence_after();
                 const uint32_t v_addr = smem_u32(sV + st * S::kKvBytes);
                 const uint32_t p_col = tmem + (st ? S::kTmS1 : S::kTmS0);
 #pragma unroll
                 for (int kk = 0; kk < BN / 16; ++kk) {
                     const uint64_t bdesc = umma_sdesc_sw128(v_addr + kk * 16 * 128, S::kKvSubBytes, 1024);
-                    umma_ts(tmem + S::kTmO, p_col + kk * 8, bdesc, idesc_pv, (!first || kk > 0) ? 1u : 0u);
+                    umma_ts_elect(tmem + S::kTmO, p_col + kk * 8, bdesc, idesc_pv, (!first || kk > 0) ? 1u : 0u);
                 }
-                umma_commit(smem_u32(&bars->o_done));
-                umma_commit(smem_u32(&bars->v_empty[st]));
+                umma_commit_elect(smem_u32(&bars->o_done));
+                umma_commit_elect(smem_u32(&bars->v_empty[st]));
                 return true;
             };
             int qit = 0, g0 = 0;
@@ -429,13 +433,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 const Item1 it = item1_geometry<BN>(p, k);
                 const int n = it.n_tiles;
                 if (n == 0) continue;
-                ok = mbar_wait(smem_u32(&bars->q_full), qit & 1, p.err, kErrWaitTmaFull);
+                ok = mbar_wait_warp(smem_u32(&bars->q_full), qit & 1, p.err, kErrWaitTmaFull);
                 // O is overwritten by the item's first PV: its readers (the previous item's
                 // epilogue) are the threads whose p_full arrival that PV waits for.
                 for (int j = 0; j < n && ok; ++j) {
                     const int g = g0 + j;
                     const int st = g & 1;
-                    if (!(ok = mbar_wait(smem_u32(&bars->k_full[st]), (g >> 1) & 1, p.err, kErrWaitTmaFull))) break;
+                    if (!(ok = mbar_wait_warp(smem_u32(&bars->k_full[st]), (g >> 1) & 1, p.err, kErrWaitTmaFull))) break;
                     tc_fence_after();
                     const uint32_t k_addr = smem_u32(sK + st * S::kKvBytes);
                     const uint32_t s_col = tmem + (st ? S::kTmS1 : S::kTmS0);
@@ -444,11 +448,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                         const uint32_t off = (kk & 3) * 32;   // 16 halves = 32 B along K
                         const uint64_t adesc = umma_sdesc_sw128(q_addr + (kk >> 2) * S::kQSubBytes + off, 16, 1024);
                         const uint64_t bdesc = umma_sdesc_sw128(k_addr + (kk >> 2) * S::kKvSubBytes + off, 16, 1024);
-                        umma_ss(s_col, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+                        umma_ss_elect(s_col, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
                     }
-                    umma_commit(smem_u32(&bars->s_full[st]));
-                    umma_commit(smem_u32(&bars->k_empty[st]));
-                    if (j + 1 == n) umma_commit(smem_u32(&bars->q_empty));   // the item's last S read Q
+                    umma_commit_elect(smem_u32(&bars->s_full[st]));
+                    umma_commit_elect(smem_u32(&bars->k_empty[st]));
+                    if (j + 1 == n) umma_commit_elect(smem_u32(&bars->q_empty));   // the item's last S read Q
                     if (j >= 1 && !(ok = issue_pv(g - 1, j == 1))) break;
                 }
                 if (ok) ok = issue_pv(g0 + n - 1, n == 1);
@@ -456,8 +460,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 ++qit;
             }
             // Every MMA must be complete before TMEM is released.
-            umma_commit(smem_u32(&bars->mma_done));
-            mbar_wait(smem_u32(&bars->mma_done), 0, p.err, kErrDrain);
+            umma_commit_elect(smem_u32(&bars->mma_done));
+            mbar_wait_warp(smem_u32(&bars->mma_done), 0, p.err, kErrDrain);
         }
     } else {
         // ================= softmax: thread owns query row `row` =================
@@ -717,7 +721,9 @@ template <int HD>
 struct Prefill2Shape {
     static constexpr int BN = 128;
     static constexpr int kNSB = 1;                         // S/P buffers per Q tile
-    static constexpr int kStages = 2;                      // K and V ring depth
+    // K and V ring depth: 4 for head dim 64 (the rings, two Q tiles and the epilogue's
+    // own staging fill 224 KB), 2 for head dim 128 (the 32 KB tiles leave no room)
+    static constexpr int kStages = HD == 64 ? 4 : 2;
     static constexpr int kSub = HD / 64;
     static constexpr int kQSubBytes = kBM * 128;
     static constexpr int kQBytes = kSub * kQSubBytes;      // one tile
@@ -840,6 +846,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
     using S = Prefill2Shape<HD>;
     constexpr int BN = S::BN;
     constexpr int ST = S::kStages;
+    static_assert(ST <= kMaxStages2 && S::kUsed <= 227 * 1024, "ring depth / shared memory");
     // One item per CTA (grid = items) unless Persistent: then rounds until items run out.
     const int n_items = p.n_qblocks * p.n_ygroups * p.batch;
     const int n_rounds = Persistent ? (n_items + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x) : 1;
@@ -943,44 +950,48 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
             }
         }
     } else if (warp == kMmaWarp2) {
-        if (lane == 0) {
+        {   // the whole warp, converged: one elected lane issues each MMA and commit
             constexpr uint32_t idesc_s = umma_idesc_f16(kBM, BN, true, false);
             constexpr uint32_t idesc_pv = umma_idesc_f16(kBM, HD, false, true);
+            // A shared-memory descriptor is linear in its address (bits [0,14) hold
+            // address / 16, and every address here is below 256 KB), so each MMA's operand
+            // descriptors are a per-tile base plus a compile-time constant.
+            const uint64_t q_desc0 = umma_sdesc_sw128(smem_u32(sQ), 16, 1024);
+            const uint64_t k_desc0 = umma_sdesc_sw128(smem_u32(sK), 16, 1024);
+            const uint64_t v_desc0 = umma_sdesc_sw128(smem_u32(sV), S::kKvSubBytes, 1024);
             // S of Q tile t for global key tile g; K/V of key tile g sit in ring slot g % ST.
             auto issue_s = [&](int t, int g) {
-                const uint32_t q_addr = smem_u32(sQ + t * S::kQBytes);
-                const uint32_t k_addr = smem_u32(sK + (g % ST) * S::kKvBytes);
+                const uint64_t qd = q_desc0 + static_cast<uint32_t>(t * (S::kQBytes >> 4));
+                const uint64_t kd = k_desc0 + static_cast<uint32_t>((g % ST) * (S::kKvBytes >> 4));
                 const uint32_t s_col = tmem + t * S::kTileCols;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk) {
-                    const uint32_t off = (kk & 3) * 32;
-                    const uint64_t adesc = umma_sdesc_sw128(q_addr + (kk >> 2) * S::kQSubBytes + off, 16, 1024);
-                    const uint64_t bdesc = umma_sdesc_sw128(k_addr + (kk >> 2) * S::kKvSubBytes + off, 16, 1024);
-                    umma_ss(s_col, adesc, bdesc, idesc_s, kk > 0 ? 1u : 0u);
+                    const uint32_t aoff = ((kk >> 2) * S::kQSubBytes + (kk & 3) * 32) >> 4;
+                    const uint32_t boff = ((kk >> 2) * S::kKvSubBytes + (kk & 3) * 32) >> 4;
+                    umma_ss_elect(s_col, qd + aoff, kd + boff, idesc_s, kk > 0 ? 1u : 0u);
                 }
-                umma_commit(smem_u32(&bars->s_full[t]));
+                umma_commit_elect(smem_u32(&bars->s_full[t]));
             };
             // O_t (+)= P_t V for key tile g; `first` starts the accumulation of an item.
             auto issue_pv = [&](int t, int g, bool first) {
-                const uint32_t v_addr = smem_u32(sV + (g % ST) * S::kKvBytes);
+                const uint64_t vd = v_desc0 + static_cast<uint32_t>((g % ST) * (S::kKvBytes >> 4));
                 const uint32_t p_col = tmem + t * S::kTileCols + S::kTmP;
                 const uint32_t o_col = tmem + t * S::kTileCols + S::kTmO;
 #pragma unroll
-                for (int kk = 0; kk < BN / 16; ++kk) {
-                    const uint64_t bdesc = umma_sdesc_sw128(v_addr + kk * 16 * 128, S::kKvSubBytes, 1024);
-                    umma_ts(o_col, p_col + kk * 8, bdesc, idesc_pv, (!first || kk > 0) ? 1u : 0u);
-                }
-                umma_commit(smem_u32(&bars->o_done[t]));
+                for (int kk = 0; kk < BN / 16; ++kk)
+                    umma_ts_elect(o_col, p_col + kk * 8, vd + ((kk * 16 * 128) >> 4), idesc_pv,
+                                  (!first || kk > 0) ? 1u : 0u);
+                umma_commit_elect(smem_u32(&bars->o_done[t]));
             };
             auto wait_k = [&](int g) {
-                return mbar_wait(smem_u32(&bars->k_full[g % ST]), (g / ST) & 1, p.err, kErrWaitTmaFull);
+                return mbar_wait_warp(smem_u32(&bars->k_full[g % ST]), (g / ST) & 1, p.err, kErrWaitTmaFull);
             };
             int qit = 0, g0 = 0;
             bool ok = true;
             // Look-ahead order per key tile g: S0(g+1), S1(g+1) as soon as each tile's
             // softmax has read S(g) (s_free), then PV0(g), PV1(g) once P(g) is written.
             auto wait_s_free = [&](int t, int g) {   // softmax of tile t has read S(g)
-                return g < 0 || mbar_wait(smem_u32(&bars->s_free[t]), g & 1, p.err, kErrWaitSoftmax);
+                return g < 0 || mbar_wait_warp(smem_u32(&bars->s_free[t]), g & 1, p.err, kErrWaitSoftmax);
             };
             if constexpr (S::kLookAhead) {
                 for (int r = 0; r < n_rounds && ok; ++r) {
@@ -989,15 +1000,15 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     const Item2 it = item_geometry<BN>(p, k);
                     const int n = it.n_tiles;
                     if (n == 0) continue;
-                    ok = mbar_wait(smem_u32(&bars->q_full), qit & 1, p.err, kErrWaitTmaFull) && wait_k(g0);
+                    ok = mbar_wait_warp(smem_u32(&bars->q_full), qit & 1, p.err, kErrWaitTmaFull) && wait_k(g0);
                     for (int t = 0; t < 2 && ok; ++t) {
                         if (!(ok = wait_s_free(t, g0 - 1))) break;
                         tc_fence_after();
                         issue_s(t, g0);
                     }
                     if (!ok) break;
-                    umma_commit(smem_u32(&bars->k_empty[g0 % ST]));
-                    if (n == 1) umma_commit(smem_u32(&bars->q_empty));
+                    umma_commit_elect(smem_u32(&bars->k_empty[g0 % ST]));
+                    if (n == 1) umma_commit_elect(smem_u32(&bars->q_empty));
                     for (int j = 0; j < n && ok; ++j) {
                         const int g = g0 + j;
                         if (j + 1 < n) {
@@ -1008,19 +1019,19 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                                 issue_s(t, g + 1);
                             }
                             if (!ok) break;
-                            umma_commit(smem_u32(&bars->k_empty[(g + 1) % ST]));
-                            if (j + 2 == n) umma_commit(smem_u32(&bars->q_empty));   // last S of the item
+                            umma_commit_elect(smem_u32(&bars->k_empty[(g + 1) % ST]));
+                            if (j + 2 == n) umma_commit_elect(smem_u32(&bars->q_empty));   // last S of the item
                         }
-                        if (!(ok = mbar_wait(smem_u32(&bars->v_full[g % ST]), (g / ST) & 1, p.err, kErrWaitTmaFull)))
+                        if (!(ok = mbar_wait_warp(smem_u32(&bars->v_full[g % ST]), (g / ST) & 1, p.err, kErrWaitTmaFull)))
                             break;
                         // O_t is overwritten by the item's first PV: its readers (the previous
                         // item's epilogue) are the threads whose p_full arrival that PV waits for.
                         for (int t = 0; t < 2 && ok; ++t) {
-                            if (!(ok = mbar_wait(smem_u32(&bars->p_full[t]), g & 1, p.err, kErrWaitSoftmax))) break;
+                            if (!(ok = mbar_wait_warp(smem_u32(&bars->p_full[t]), g & 1, p.err, kErrWaitSoftmax))) break;
                             tc_fence_after();
                             issue_pv(t, g, j == 0);
                         }
-                        if (ok) umma_commit(smem_u32(&bars->v_empty[g % ST]));
+                        if (ok) umma_commit_elect(smem_u32(&bars->v_empty[g % ST]));
                     }
                     g0 += n;
                     ++qit;
@@ -1035,20 +1046,20 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                 // Prologue: S of the item's first key tile for both Q tiles.  (The
                 // previous item's last PV read P from the same TMEM columns; MMAs of
                 // this thread run in issue order.)
-                ok = mbar_wait(smem_u32(&bars->q_full), qit & 1, p.err, kErrWaitTmaFull) && wait_k(g0);
+                ok = mbar_wait_warp(smem_u32(&bars->q_full), qit & 1, p.err, kErrWaitTmaFull) && wait_k(g0);
                 if (!ok) break;
                 tc_fence_after();
                 issue_s(0, g0);
                 issue_s(1, g0);
-                umma_commit(smem_u32(&bars->k_empty[g0 % ST]));
-                if (n == 1) umma_commit(smem_u32(&bars->q_empty));
+                umma_commit_elect(smem_u32(&bars->k_empty[g0 % ST]));
+                if (n == 1) umma_commit_elect(smem_u32(&bars->q_empty));
                 // O_t is overwritten by the item's first PV: its readers (the previous
                 // item's epilogue) are the threads whose p_full arrival that PV waits for.
                 for (int j = 0; j < n && ok; ++j) {
                     const int g = g0 + j;
                     const int st = g % ST;
-                    ok = mbar_wait(smem_u32(&bars->p_full[0]), g & 1, p.err, kErrWaitSoftmax) &&
-                         mbar_wait(smem_u32(&bars->v_full[st]), (g / ST) & 1, p.err, kErrWaitTmaFull);
+                    ok = mbar_wait_warp(smem_u32(&bars->p_full[0]), g & 1, p.err, kErrWaitSoftmax) &&
+                         mbar_wait_warp(smem_u32(&bars->v_full[st]), (g / ST) & 1, p.err, kErrWaitTmaFull);
                     if (!ok) break;
                     tc_fence_after();
                     issue_pv(0, g, j == 0);
@@ -1059,22 +1070,22 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                         tc_fence_after();
                         issue_s(0, g + 1);
                     }
-                    ok = mbar_wait(smem_u32(&bars->p_full[1]), g & 1, p.err, kErrWaitSoftmax);
+                    ok = mbar_wait_warp(smem_u32(&bars->p_full[1]), g & 1, p.err, kErrWaitSoftmax);
                     if (!ok) break;
                     tc_fence_after();
                     issue_pv(1, g, j == 0);
-                    umma_commit(smem_u32(&bars->v_empty[st]));
+                    umma_commit_elect(smem_u32(&bars->v_empty[st]));
                     if (more) {
                         issue_s(1, g + 1);
-                        umma_commit(smem_u32(&bars->k_empty[(g + 1) % ST]));
-                        if (j + 2 == n) umma_commit(smem_u32(&bars->q_empty));   // last S of the item
+                        umma_commit_elect(smem_u32(&bars->k_empty[(g + 1) % ST]));
+                        if (j + 2 == n) umma_commit_elect(smem_u32(&bars->q_empty));   // last S of the item
                     }
                 }
                 g0 += n;
                 ++qit;
             }
-            umma_commit(smem_u32(&bars->mma_done));
-            mbar_wait(smem_u32(&bars->mma_done), 0, p.err, kErrDrain);
+            umma_commit_elect(smem_u32(&bars->mma_done));
+            mbar_wait_warp(smem_u32(&bars->mma_done), 0, p.err, kErrDrain);
         }
     }
     } else {
@@ -1143,9 +1154,9 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     }
                 }
                 // Row max as 8 independent chains of 3-input maxima and a short tree (a single
-                // chain over BN scores would serialise BN/2 dependent instructions).
-                float mx;
-                {
+                // chain over BN scores would serialise BN/2 dependent instructions), in log2
+                // units (scores are raw, scale applied here, unless softcapped).
+                auto row_max_log2 = [&]() -> float {
                     float pm[8];
 #pragma unroll
                     for (int q = 0; q < 8; ++q) pm[q] = fmaxf(t[2 * q], t[2 * q + 1]);
@@ -1153,37 +1164,34 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                     for (int c = 16; c < BN; c += 16)
 #pragma unroll
                         for (int q = 0; q < 8; ++q) pm[q] = max3f(pm[q], t[c + 2 * q], t[c + 2 * q + 1]);
-                    mx = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
+                    const float mx =
+                        max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
+                    return cap > 0.f ? mx : mx * sl2;
+                };
+                // The reference point m of the exponentials.  A row that has none yet (no
+                // visible key so far) takes this tile's exact maximum.  Every other row keeps
+                // its m and computes the exponentials straight away; the tile's sum then
+                // tells whether any of them passed 2^15 (its scores grew by more than 15 in
+                // log2 units), and only such a row takes the tile's maximum, rescales O and
+                // l and recomputes.  A P value thus stays below 2^15 (fp16 holds it) and no
+                // row pays for a row maximum on a tile whose scores did not jump.  Each
+                // decision depends on the row's own scores alone, so a row's result does not
+                // depend on which rows share its warp (a chunked prefill stays bit-exact).
+                const bool fresh = m == -INFINITY && row_valid && key0 < my_hi && key0 + BN > my_lo;
+                if (__any_sync(0xffffffffu, fresh)) {
+                    const float mxs = row_max_log2();
+                    if (fresh) m = mxs;
                 }
-                // scores are raw (scale applied below) unless softcapped (already in log2 units)
-                const float mxs = cap > 0.f ? mx : mx * sl2;
-                const bool need = m != -INFINITY && mxs > m + kRescaleThreshold;   // only when j > 0
-                if (__any_sync(0xffffffffu, need)) {
-                    ok = __all_sync(0xffffffffu, mbar_wait(o_done, (g - 1) & 1, p.err, kErrWaitMma));
-                    if (!ok) break;
-                    tc_fence_after();
-                    const float f = need ? fast_exp2(m - mxs) : 1.f;
-                    uint32_t rr[32];
-#pragma unroll
-                    for (int c = 0; c < HD / 32; ++c) {
-                        tmem_ld32(lane_base + S::kTmO + c * 32, rr);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * f);
-                        tmem_st32(lane_base + S::kTmO + c * 32, rr);
-                    }
-                    l *= f;
-                }
-                if (need || (m == -INFINITY && mxs > -INFINITY)) m = mxs;
-                // P = exp2(s*scale_log2 - m): one packed FMA per two scores, then ex2.
-                const bool live = m != -INFINITY;
                 const float mul = cap > 0.f ? 1.f : sl2;
-                // A row with no visible key yet (m = -inf) has every score at -inf, so with
-                // -m replaced by 0 its exponentials are exactly 0: no per-element select.
-                const float negm = live ? -m : 0.f;
-                float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};   // 4 independent pair sums
-                bool p_free = true;   // look-ahead: PV(g-1) has read the P columns
-                {
+                float lt = 0.f;        // this tile's row sum
+                bool p_free = true;    // look-ahead: PV(g-1) has read the P columns
+#pragma unroll
+                for (int pass = 0; pass < 2; ++pass) {   // unrolled: each pass scheduled on its own
+                    // P = exp2(s*scale_log2 - m): one packed FMA per two scores, then ex2.
+                    // A row with no visible key yet (m = -inf) has every score at -inf, so with
+                    // -m replaced by 0 its exponentials are exactly 0: no per-element select.
+                    const float negm = m != -INFINITY ? -m : 0.f;
+                    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};   // 4 pair sums
                     uint32_t rr[32];
 #pragma unroll
                     for (int c = 0; c < BN / 64; ++c) {
@@ -1204,19 +1212,46 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                             // P(g-1) in the same columns is read by PV(g-1): wait for it only now,
                             // after half of this tile's exponentials (the first P of an item follows
                             // the previous item's epilogue, which waited for that item's last PV)
-                            if (c == 0 && j > 0) {
+                            if (pass == 0 && c == 0 && j > 0) {
                                 p_free = __all_sync(0xffffffffu, mbar_wait(o_done, (g - 1) & 1, p.err, kErrWaitMma));
                                 tc_fence_after();
                             }
                         }
                         if (p_free) tmem_st32(p_base + c * 32, rr);
                     }
+                    if (!p_free) break;
+                    lt = ((acc0[0] + acc0[1]) + (acc0[2] + acc0[3])) + ((acc1[0] + acc1[1]) + (acc1[2] + acc1[3]));
+                    const bool over = !(lt <= kSpecSumLimit);   // also NaN / inf
+                    if (pass == 1 || !__any_sync(0xffffffffu, over)) break;
+                    // Rows whose sum passed the limit: this tile's maximum becomes m; O (the
+                    // earlier tiles' PV, complete: waited for above or, without look-ahead,
+                    // before this S) and l are scaled by 2^(m_old - m_new).  The other rows
+                    // recompute the same values.
+                    const float mxs = row_max_log2();
+                    const float f = over ? fast_exp2(m - mxs) : 1.f;
+                    if (over) m = mxs;
+                    if (j > 0) {
+                        if (!(p_free = __all_sync(0xffffffffu, mbar_wait(o_done, (g - 1) & 1, p.err, kErrWaitMma))))
+                            break;
+                        tc_fence_after();
+                        uint32_t ro[32];
+#pragma unroll
+                        for (int c = 0; c < HD / 32; ++c) {
+                            tmem_ld32(lane_base + S::kTmO + c * 32, ro);
+                            tmem_ld_wait();
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) ro[i] = __float_as_uint(__uint_as_float(ro[i]) * f);
+                            tmem_st32(lane_base + S::kTmO + c * 32, ro);
+                        }
+                    }
+                    l *= f;
+                    tmem_st_wait();
                 }
                 if (!p_free) {
                     ok = false;
                     break;
                 }
-                l += ((acc0[0] + acc0[1]) + (acc0[2] + acc0[3])) + ((acc1[0] + acc1[1]) + (acc1[2] + acc1[3]));
+                l += lt;
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(p_full);
