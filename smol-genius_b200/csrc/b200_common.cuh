@@ -187,6 +187,8 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, uint32_t sr
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until every committed bulk store of this thread has finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// At most one bulk group of this thread still reading its shared-memory source.
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // Order this thread's generic-proxy shared-memory writes before later async-proxy reads.
 __device__ __forceinline__ void fence_proxy_async_smem()
 {

@@ -472,6 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         const float inv_cap = cap > 0.f ? 1.f / cap : 0.f;
         const float kLog2e = 1.4426950408889634f;
         bool stores_pending = false;   // lane 0: a TMA store from this warp's staging area
+        int slot = 0;                  // staging slot of the warp's next box (alternates across items)
         int g0 = 0;
         bool ok = true;
         for (int r = 0; r < n_rounds && ok; ++r) {
@@ -596,19 +597,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             tc_fence_after();
             const float inv = l > 0.f ? 1.f / l : 0.f;
             // Staged epilogue: the warp's 32 rows (32/pack positions x pack heads) go through
-            // shared memory in 128B-swizzled boxes, two at a time, and leave with TMA tensor
-            // stores, so the output is written as whole sectors instead of 16-byte pieces of
-            // 32 rows.  Rows no window covers must stay untouched: such warps store rows.
+            // shared memory in 128B-swizzled boxes and leave with TMA tensor stores, so the
+            // output is written as whole sectors instead of 16-byte pieces of 32 rows.  The
+            // warp's two box slots alternate: box k is written while the store of box k-1
+            // still reads the other slot (one bulk group in flight).  Rows no window covers
+            // must stay untouched: such warps store rows.
             const bool staged = ok && __all_sync(0xffffffffu, my_written || !row_valid);
             if (staged) {
                 const bool bf = p.out_bf16 != 0;
                 const int box_cols = bf ? 64 : 32;
                 uint8_t *stage = smem + S::kOffStage + warp * S::kStageWarpBytes;
                 const int pos0 = (it.q0 + warp * 32) / p.pack;
-                for (int c0 = 0; c0 < HD; c0 += 2 * box_cols) {   // two boxes per round
-                    if (lane == 0 && stores_pending) bulk_wait_read0();   // the staging is free again
+                for (int c0 = 0; c0 < HD; c0 += box_cols, slot ^= 1) {   // one box per round
+                    if (c0 >= p.hd) break;                                 // boxes wholly past the head dim
+                    if (lane == 0 && stores_pending) bulk_wait_read1();    // this slot's last store read it
                     __syncwarp();
-                    for (int c = c0; c < c0 + 2 * box_cols; c += 32) {    // 32 TMEM columns at a time
+                    for (int c = c0; c < c0 + box_cols; c += 32) {         // 32 TMEM columns at a time
                         uint32_t rr[32];
                         if (have_o) {
                             tmem_ld32(lane_base + S::kTmO + c, rr);
@@ -617,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
 #pragma unroll
                             for (int i = 0; i < 32; ++i) rr[i] = 0u;
                         }
-                        uint8_t *box = stage + ((c - c0) / box_cols) * (32 * 128);
+                        uint8_t *box = stage + slot * (32 * 128);
                         if (bf) {
                             const int u0 = ((c - c0) % 64) / 8;   // first 16-byte unit of these columns
 #pragma unroll
@@ -646,11 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-#pragma unroll
-                        for (int bx = 0; bx < 2; ++bx)   // boxes wholly past the caller's head dim: none
-                            if (c0 + bx * box_cols < p.hd)
-                                tma_store_4d(&p.to, smem_u32(stage + bx * (32 * 128)), c0 + bx * box_cols, it.h,
-                                             pos0, it.b);
+                        tma_store_4d(&p.to, smem_u32(stage + slot * (32 * 128)), c0, it.h, pos0, it.b);
                         bulk_commit();
                         stores_pending = true;
                     }

@@ -542,6 +542,35 @@ def test_prefill_bf16_output_is_rounded_fp32_output(cuda, hd, hq, hkv, mask):
         assert bool((out16[:, :5].float() == 5.0).all()) and bool((out16[:, 300:].float() == 5.0).all())
 
 
+@pytest.mark.parametrize("hd,hq,hkv,mask", [(64, 4, 4, "full"), (64, 2, 1, "causal"), (128, 4, 2, "causal"),
+                                             (72, 2, 2, "full"), (256, 8, 1, "causal")])
+def test_prefill_scores_growing_across_key_tiles(cuda, hd, hq, hkv, mask):
+    # Even rows' scores grow by ~20 (natural units) from one 128-key tile to the next and
+    # odd rows' fall: an even row's exponentials against its first tile's maximum would
+    # pass fp16 on every later tile, so its reference maximum must move (the rescale
+    # path), while the odd rows of the same warp keep theirs.
+    rng = np.random.default_rng(hd * 3 + hq)
+    S = 600
+    scale = 1 / np.sqrt(hd)
+    B = 8.0
+    u = np.ones(hd, np.float32) / np.sqrt(hd)
+    a = np.arange(S, dtype=np.float32) * (20.0 / (128 * B * scale))
+    sign = np.where(np.arange(S) % 2 == 0, 1.0, -1.0).astype(np.float32)
+    q = (sign[:, None, None] * B * u[None, None, :] + 0.05 * rng.standard_normal((S, hq, hd))).reshape(S, hq * hd)
+    k = (a[:, None, None] * u[None, None, :] + 0.05 * rng.standard_normal((S, hkv, hd))).reshape(S, hkv * hd)
+    q, k = pyoracle.round_bf16(q.astype(np.float32)), pyoracle.round_bf16(k.astype(np.float32))
+    v = rnd_bf16(rng, S, hkv * hd)
+    o = pyoracle.oracle()
+    if mask == "full":
+        got = run_prefill(cuda, q, k, v, 1, S, S, hq, hkv, hd, scale, mask=smol_b200.MASK_FULL)
+        want = o.bidirectional_attention(q, k, v, S, hq, hd, scale, [0, S])
+    else:
+        got = run_prefill(cuda, q, k, v, 1, S, S, hq, hkv, hd, scale)
+        want = o.causal_attention(q, k, v, S, S, hq, hkv, hd, scale, 0)
+    assert np.isfinite(got).all()
+    assert_close(got[0], want, f"growing scores hd {hd} {mask}")
+
+
 def test_prefill_siglip_so400m_head_dim_72(cuda):
     # SmolVLM's vision tower (SigLIP-So400m: 729 patches, 16 heads of 72) -- bidirectional
     # attention per image on the 128-wide kernel with the caller's 72-column rows: the
