@@ -840,6 +840,70 @@ __device__ __forceinline__ Item2 item_geometry(const PrefillParams &p, int k)
     return it;
 }
 
+// The TMA producer of the two-tile kernels (one thread): an item's two Q tiles, then
+// its K and V tiles through the ST-deep rings.  Barrier phases run on across items:
+// q_full / q_empty once per item with key tiles (count qit), the rings once per key
+// tile (global count g over all items of this CTA).
+template <typename S, typename Bars>
+__device__ __forceinline__ void produce_two_tiles(const PrefillParams &p, Bars *bars, uint8_t *sQ, uint8_t *sK,
+                                                  uint8_t *sV, int n_items, int n_rounds)
+{
+    constexpr int BN = S::BN;
+    constexpr int ST = S::kStages;
+    tma_prefetch_desc(&p.tq);
+    tma_prefetch_desc(&p.tk);
+    tma_prefetch_desc(&p.tv);
+    int qit = 0, g = 0;
+    bool ok = true;
+    for (int r = 0; r < n_rounds && ok; ++r) {
+        const int k = item_index(p, r);
+        if (k >= n_items) break;
+        const Item2 it = item_geometry<BN>(p, k);
+        if (it.n_tiles == 0) continue;
+        // Q of this item overwrites the last one's: wait for its final S MMAs.
+        if (qit > 0 && !(ok = mbar_wait(smem_u32(&bars->q_empty), (qit - 1) & 1, p.err, kErrWaitTmaEmpty)))
+            break;
+        const uint32_t qbar = smem_u32(&bars->q_full);
+        mbar_arrive_expect_tx(qbar, 2 * S::kQBytes);
+#pragma unroll
+        for (int t = 0; t < 2; ++t)
+#pragma unroll
+            for (int sub = 0; sub < S::kSub; ++sub)
+                tma_load_4d(smem_u32(sQ + t * S::kQBytes + sub * S::kQSubBytes), &p.tq, qbar, sub * 64,
+                            it.head[t], it.row0[t], it.b);
+        ++qit;
+        const int kvh = it.head[0] / p.group;
+        for (int j = 0; j < it.n_tiles; ++j, ++g) {
+            const int st = g % ST;
+            const int key0 = it.lo_min + j * BN;
+            if (g >= ST &&
+                !(ok = mbar_wait(smem_u32(&bars->k_empty[st]), ((g / ST) - 1) & 1, p.err, kErrWaitTmaEmpty)))
+                break;
+            const uint32_t kb = smem_u32(&bars->k_full[st]);
+            mbar_arrive_expect_tx(kb, S::kKvBytes);
+#pragma unroll
+            for (int sub = 0; sub < S::kSub; ++sub)
+                tma_load_4d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb, sub * 64,
+                            kvh, key0, it.b);
+            if (g >= ST &&
+                !(ok = mbar_wait(smem_u32(&bars->v_empty[st]), ((g / ST) - 1) & 1, p.err, kErrWaitTmaEmpty)))
+                break;
+            const uint32_t vb = smem_u32(&bars->v_full[st]);
+            mbar_arrive_expect_tx(vb, S::kKvBytes);
+#pragma unroll
+            for (int sub = 0; sub < S::kSub; ++sub)
+                tma_load_4d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb, sub * 64,
+                            kvh, key0, it.b);
+        }
+    }
+    // Drain: the last Q and the last ST key tiles must have landed before exit.
+    if (qit > 0) mbar_wait(smem_u32(&bars->q_full), (qit - 1) & 1, p.err, kErrDrain);
+    for (int j = max(0, g - ST); j < g; ++j) {
+        if (!mbar_wait(smem_u32(&bars->k_full[j % ST]), (j / ST) & 1, p.err, kErrDrain)) break;
+        if (!mbar_wait(smem_u32(&bars->v_full[j % ST]), (j / ST) & 1, p.err, kErrDrain)) break;
+    }
+}
+
 template <int HD, bool Persistent, int PolyPairs8 = PolyShare<HD>::kPairs8>
 __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_constant__ PrefillParams p)
 {
@@ -895,60 +959,7 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
     // warpgroup 2 (producer, MMA issuer, two idle warps) hands registers to the softmax
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsOther2));
     if (warp == kProducerWarp2) {
-        if (lane == 0) {
-            tma_prefetch_desc(&p.tq);
-            tma_prefetch_desc(&p.tk);
-            tma_prefetch_desc(&p.tv);
-            int qit = 0, g = 0;
-            bool ok = true;
-            for (int r = 0; r < n_rounds && ok; ++r) {
-                const int k = item_index(p, r);
-                if (k >= n_items) break;
-                const Item2 it = item_geometry<BN>(p, k);
-                if (it.n_tiles == 0) continue;
-                // Q of this item overwrites the last one's: wait for its final S MMAs.
-                if (qit > 0 && !(ok = mbar_wait(smem_u32(&bars->q_empty), (qit - 1) & 1, p.err, kErrWaitTmaEmpty)))
-                    break;
-                const uint32_t qbar = smem_u32(&bars->q_full);
-                mbar_arrive_expect_tx(qbar, 2 * S::kQBytes);
-#pragma unroll
-                for (int t = 0; t < 2; ++t)
-#pragma unroll
-                    for (int sub = 0; sub < S::kSub; ++sub)
-                        tma_load_4d(smem_u32(sQ + t * S::kQBytes + sub * S::kQSubBytes), &p.tq, qbar, sub * 64,
-                                    it.head[t], it.row0[t], it.b);
-                ++qit;
-                const int kvh = it.head[0] / p.group;
-                for (int j = 0; j < it.n_tiles; ++j, ++g) {
-                    const int st = g % ST;
-                    const int key0 = it.lo_min + j * BN;
-                    if (g >= ST &&
-                        !(ok = mbar_wait(smem_u32(&bars->k_empty[st]), ((g / ST) - 1) & 1, p.err, kErrWaitTmaEmpty)))
-                        break;
-                    const uint32_t kb = smem_u32(&bars->k_full[st]);
-                    mbar_arrive_expect_tx(kb, S::kKvBytes);
-#pragma unroll
-                    for (int sub = 0; sub < S::kSub; ++sub)
-                        tma_load_4d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb, sub * 64,
-                                    kvh, key0, it.b);
-                    if (g >= ST &&
-                        !(ok = mbar_wait(smem_u32(&bars->v_empty[st]), ((g / ST) - 1) & 1, p.err, kErrWaitTmaEmpty)))
-                        break;
-                    const uint32_t vb = smem_u32(&bars->v_full[st]);
-                    mbar_arrive_expect_tx(vb, S::kKvBytes);
-#pragma unroll
-                    for (int sub = 0; sub < S::kSub; ++sub)
-                        tma_load_4d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb, sub * 64,
-                                    kvh, key0, it.b);
-                }
-            }
-            // Drain: the last Q and the last ST key tiles must have landed before exit.
-            if (qit > 0) mbar_wait(smem_u32(&bars->q_full), (qit - 1) & 1, p.err, kErrDrain);
-            for (int j = max(0, g - ST); j < g; ++j) {
-                if (!mbar_wait(smem_u32(&bars->k_full[j % ST]), (j / ST) & 1, p.err, kErrDrain)) break;
-                if (!mbar_wait(smem_u32(&bars->v_full[j % ST]), (j / ST) & 1, p.err, kErrDrain)) break;
-            }
-        }
+        if (lane == 0) produce_two_tiles<S>(p, bars, sQ, sK, sV, n_items, n_rounds);
     } else if (warp == kMmaWarp2) {
         {   // the whole warp, converged: one elected lane issues each MMA and commit
             constexpr uint32_t idesc_s = umma_idesc_f16(kBM, BN, true, false);
