@@ -38,9 +38,8 @@ constexpr int kThreads = 192;
 constexpr int kSoftmaxThreads = 128;
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
-constexpr float kRescaleThreshold = 8.0f;   // log2 units
-// prefill2: a tile's row sum of exponentials against the row's reference point may
-// reach 2^15 before the row moves its reference (each P value then fits fp16)
+// A tile's row sum of exponentials against the row's reference point may reach 2^15
+// before the row moves its reference (each P value then fits fp16)
 constexpr float kSpecSumLimit = 32768.0f;
 
 template <int HD>
@@ -522,9 +521,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                         if (!row_valid || key < my_lo || key >= my_hi) t[c] = -INFINITY;
                     }
                 }
-                // Row max as 8 independent chains of 3-input maxima and a short tree.
-                float mx;
-                {
+                // Row max (log2 units) as 8 independent chains of 3-input maxima and a short tree.
+                auto row_max_log2 = [&]() -> float {
                     float pm[8];
 #pragma unroll
                     for (int q = 0; q < 8; ++q) pm[q] = fmaxf(t[2 * q], t[2 * q + 1]);
@@ -532,52 +530,72 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     for (int c = 16; c < BN; c += 16)
 #pragma unroll
                         for (int q = 0; q < 8; ++q) pm[q] = max3f(pm[q], t[c + 2 * q], t[c + 2 * q + 1]);
-                    mx = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
+                    const float mx =
+                        max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
+                    return cap > 0.f ? mx : mx * p.scale_log2;
+                };
+                // The reference point m of the exponentials: a row that has none yet (no
+                // visible key so far) takes this tile's exact maximum; every other row keeps
+                // its m until this tile's sum of exponentials passes 2^15 (then P would no
+                // longer fit fp16), and only then takes the tile's maximum, rescales O and l
+                // and recomputes.  Each decision depends on the row's own scores alone.
+                const bool fresh = m == -INFINITY && row_valid && key0 < my_hi && key0 + BN > my_lo;
+                if (__any_sync(0xffffffffu, fresh)) {
+                    const float mxs = row_max_log2();
+                    if (fresh) m = mxs;
                 }
-                if (cap <= 0.f) mx *= p.scale_log2;
-                // The running maximum moves only when the row maximum grew by > 2^8 (or on the
-                // first tile with a visible key, when O of this row is still zero).
-                const bool need = m != -INFINITY && mx > m + kRescaleThreshold;
-                if (__any_sync(0xffffffffu, need)) {
-                    // O holds P_0..P_{j-1} V: wait for the item's previous PV, then rescale.
-                    ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done), (g - 1) & 1, p.err, kErrWaitMma));
-                    if (!ok) break;
-                    tc_fence_after();
-                    const float f = need ? fast_exp2(m - mx) : 1.f;
-                    uint32_t rr[32];
-#pragma unroll
-                    for (int c = 0; c < HD / 32; ++c) {
-                        tmem_ld32(lane_base + S::kTmO + c * 32, rr);
-                        tmem_ld_wait();
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * f);
-                        tmem_st32(lane_base + S::kTmO + c * 32, rr);
-                    }
-                    l *= f;
-                }
-                if (need || (m == -INFINITY && mx > -INFINITY)) m = mx;
                 // P = exp2(t*mul - m) as fp16 pairs over the first BN/2 columns of this S buffer,
                 // one packed FMA per two scores.  A row with no visible key yet (m = -inf) has
                 // every t at -inf, so with -m replaced by 0 its exponentials are exactly 0.
                 const float mul = cap > 0.f ? 1.f : p.scale_log2;
-                const float negm = m != -INFINITY ? -m : 0.f;
-                float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};   // independent pair sums
-                {
-                    uint32_t rr[32];
+                float lt = 0.f;   // this tile's row sum
 #pragma unroll
-                    for (int c = 0; c < BN / 64; ++c) {
+                for (int pass = 0; pass < 2; ++pass) {
+                    const float negm = m != -INFINITY ? -m : 0.f;
+                    float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};   // independent pair sums
+                    {
+                        uint32_t rr[32];
 #pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            float x0, x1;
-                            fma2(x0, x1, t[c * 64 + 2 * i], t[c * 64 + 2 * i + 1], mul, mul, negm, negm);
-                            const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
-                            add2(acc0[i & 3], acc1[i & 3], acc0[i & 3], acc1[i & 3], e0, e1);
-                            rr[i] = pack_f16x2(e0, e1);
+                        for (int c = 0; c < BN / 64; ++c) {
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) {
+                                float x0, x1;
+                                fma2(x0, x1, t[c * 64 + 2 * i], t[c * 64 + 2 * i + 1], mul, mul, negm, negm);
+                                const float e0 = fast_exp2(x0), e1 = fast_exp2(x1);
+                                add2(acc0[i & 3], acc1[i & 3], acc0[i & 3], acc1[i & 3], e0, e1);
+                                rr[i] = pack_f16x2(e0, e1);
+                            }
+                            tmem_st32(s_col + c * 32, rr);
                         }
-                        tmem_st32(s_col + c * 32, rr);
                     }
+                    lt = ((acc0[0] + acc0[1]) + (acc0[2] + acc0[3])) + ((acc1[0] + acc1[1]) + (acc1[2] + acc1[3]));
+                    const bool over = !(lt <= kSpecSumLimit);   // also NaN / inf
+                    if (pass == 1 || !__any_sync(0xffffffffu, over)) break;
+                    // O holds P_0..P_{j-1} V: wait for the item's previous PV, then rescale the
+                    // rows that move their reference; the other rows recompute the same P.
+                    const float mxs = row_max_log2();
+                    const float f = over ? fast_exp2(m - mxs) : 1.f;
+                    if (over) m = mxs;
+                    if (j > 0) {
+                        ok = __all_sync(0xffffffffu,
+                                        mbar_wait(smem_u32(&bars->o_done), (g - 1) & 1, p.err, kErrWaitMma));
+                        if (!ok) break;
+                        tc_fence_after();
+                        uint32_t ro[32];
+#pragma unroll
+                        for (int c = 0; c < HD / 32; ++c) {
+                            tmem_ld32(lane_base + S::kTmO + c * 32, ro);
+                            tmem_ld_wait();
+#pragma unroll
+                            for (int i = 0; i < 32; ++i) ro[i] = __float_as_uint(__uint_as_float(ro[i]) * f);
+                            tmem_st32(lane_base + S::kTmO + c * 32, ro);
+                        }
+                    }
+                    l *= f;
+                    tmem_st_wait();
                 }
-                l += ((acc0[0] + acc0[1]) + (acc0[2] + acc0[3])) + ((acc1[0] + acc1[1]) + (acc1[2] + acc1[3]));
+                if (!ok) break;
+                l += lt;
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(smem_u32(&bars->p_full[st]));
@@ -766,11 +784,11 @@ struct Barriers2 {
 
 // Exponentials per row and key tile: PolyPairs8 of every 8 pairs go to the FMA-pipe
 // polynomial, the rest to MUFU ex2.  Measured on cfg 3 (hd 64, 128 images x 12 layers,
-// two runs each): 0/8 8.72 ms, 1/8 8.42, 2/8 8.32, 3/8 8.48, 4/8 8.73 -- the default
-// for head dim 64 is 2/8.  Head dim 128 keeps all on MUFU.  The share is a build-time
-// knob.
+// two runs each) with the row-maximum-free softmax: 1/8 8.07 ms, 2/8 8.21, 3/8 8.60 --
+// the default for head dim 64 is 1/8.  Head dim 128 keeps all on MUFU (2/8 on the
+// So400m attention: 23.6 ms against 22.7).  The share is a build-time knob.
 #ifndef SMOL_POLY8_HD64
-#define SMOL_POLY8_HD64 2
+#define SMOL_POLY8_HD64 1
 #endif
 #ifndef SMOL_POLY8_HD128
 #define SMOL_POLY8_HD128 0
