@@ -184,7 +184,18 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, uint32_t sr
                  "r"(src), "r"(x), "r"(y), "r"(z), "r"(w)
                  : "memory");
 }
+// Shared -> global element-wise add (fp32) of a tensor box, done by the TMA unit in L2.
+__device__ __forceinline__ void tma_reduce_add_4d(const CUtensorMap *map, uint32_t src, int x, int y, int z, int w)
+{
+    asm volatile(
+        "cp.reduce.async.bulk.tensor.4d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(src), "r"(x), "r"(y), "r"(z), "r"(w)
+        : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until every committed bulk operation of this thread has completed (writes done).
+__device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 // Wait until every committed bulk store of this thread has finished reading shared memory.
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // At most one bulk group of this thread still reading its shared-memory source.

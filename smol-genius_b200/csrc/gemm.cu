@@ -51,6 +51,8 @@ constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;   // alignment sl
 
 struct GemmParams {
     CUtensorMap ta, tw;
+    CUtensorMap to;           // the output as a 32-row box map (wide form's staged epilogue)
+    int tma_out;              // 1: the wide form stores through `to` (TMA store, or reduce-add for F32_ADD)
     void *out;
     long long ldo;
     const float *bias;        // [N] or null
@@ -81,13 +83,9 @@ __device__ __forceinline__ float gated(float g, float u, int gate)
     return (gate == 3 ? gelu_tanh(g) : g / (1.0f + expf(-g))) * u;
 }
 
-// Epilogue of one 32-column chunk of one row: bias, addend, activation, store.
-__device__ __forceinline__ void store_chunk(const GemmParams &p, int row, int nb, const uint32_t (&r)[32])
+// Epilogue math of one 32-column chunk of one row: bias, addend, activation (in place).
+__device__ __forceinline__ void chunk_math(const GemmParams &p, int row, int nb, float (&v)[32])
 {
-    if (row >= p.M || nb >= p.N) return;
-    float v[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
     const bool whole = nb + 32 <= p.N;
     if (p.bias) {
         if (whole && p.bias_vec) {   // the same 32 values for every row: 8 broadcast 16-byte loads
@@ -126,6 +124,16 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int row, int nb
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(v[i]);
     }
+}
+
+// Epilogue of one 32-column chunk of one row: bias, addend, activation, store.
+__device__ __forceinline__ void store_chunk(const GemmParams &p, int row, int nb, const uint32_t (&r)[32])
+{
+    if (row >= p.M || nb >= p.N) return;
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+    chunk_math(p, row, nb, v);
     const bool full = p.vec_ok && nb + 32 <= p.N;
     if (p.gate) {   // 16 outputs from the 32 columns: out[nb/2 + j]
         float gv[16];
@@ -335,14 +343,17 @@ struct WideBarriers {
     int abort;
 };
 
-constexpr int kWSmemBytes = 1024 + kWStages * kWStageBytes + 256;
+// Epilogue staging: per epilogue warp two 4 KB boxes (32 rows x 128 bytes), alternating.
+constexpr int kWStageOut = 4 * 2 * 4096;
+constexpr int kWSmemBytes = 1024 + kWStages * kWStageBytes + 256 + kWStageOut;
 static_assert(kWSmemBytes <= 227 * 1024, "shared memory");
 
 __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_wide_kernel(const __grid_constant__ GemmParams p)
 {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    WideBarriers *bars = reinterpret_cast<WideBarriers *>(smem + kWStages * kWStageBytes);
+    uint8_t *stage_out = smem + kWStages * kWStageBytes;   // 1024-aligned: the epilogue's swizzled boxes
+    WideBarriers *bars = reinterpret_cast<WideBarriers *>(stage_out + kWStageOut);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int n_kb = (p.K + kBK - 1) / kBK;
     const int tiles_n = (p.N + kWBN - 1) / kWBN;
@@ -436,11 +447,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_wide_kernel(const _
         }
     } else {
         const int quarter = warp & 3;
+        // staged epilogue (p.tma_out): this warp's 32 rows leave through two alternating
+        // 4 KB boxes (32 rows x 128 bytes, 128B-swizzled) as TMA tensor stores -- or, for an
+        // fp32 output that is added to, as TMA reduce-adds, so the residual is never read
+        // into the SM -- with one box in flight while the next is written
+        uint8_t *my_stage = stage_out + quarter * 2 * 4096;
+        int boxes = 0;   // boxes this warp has issued (lane 0 commits one bulk group per box)
+        const bool f32 = p.out_kind == SMOL_B200_GEMM_OUT_F32 || p.out_kind == SMOL_B200_GEMM_OUT_F32_ADD;
         int i = 0;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
             const int b = i & 1;
             const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kWBN;
             const int row = m0 + quarter * 32 + lane;
+            // An fp32 output that is added to (the residual stream) is read back by this
+            // thread's row: start its 1 KB on the way to L2 while the tile's MMAs run, so the
+            // epilogue's read-add-write does not wait on HBM once per 32-column chunk.
+            if (p.out_kind == SMOL_B200_GEMM_OUT_F32_ADD && row < p.M) {
+                const char *orow = reinterpret_cast<const char *>(static_cast<const float *>(p.out) +
+                                                                  static_cast<long long>(row) * p.ldo + n0);
+                const int bytes = min(kWBN, p.N - n0) * 4;
+                for (int off = 0; off < bytes; off += 128) asm volatile("prefetch.global.L2 [%0];" ::"l"(orow + off));
+            }
             const bool waited = mbar_wait(smem_u32(&bars->acc_full[b]), (i >> 1) & 1, p.err, kErrWaitMma);
             tc_fence_after();
             if (!__all_sync(0xffffffffu, waited && atomicAdd(&bars->abort, 0) == 0)) break;
@@ -456,9 +483,67 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_wide_kernel(const _
                     tc_fence_before();
                     mbar_arrive(smem_u32(&bars->acc_empty[b]));
                 }
-                if (c < n_chunks) store_chunk(p, row, n0 + c * 32, r);
+                if (c >= n_chunks) continue;
+                if (!p.tma_out) {
+                    store_chunk(p, row, n0 + c * 32, r);
+                    continue;
+                }
+                float v[32];
+#pragma unroll
+                for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
+                chunk_math(p, row, n0 + c * 32, v);
+                // fp32: one box per chunk; 16-bit: chunks 2j, 2j+1 share a box (64 columns)
+                const bool first_half = f32 || (c & 1) == 0;
+                uint8_t *box = my_stage + (boxes & 1) * 4096;
+                if (first_half) {
+                    if (lane == 0 && boxes >= 1) bulk_wait_read1();   // this slot's previous store read it
+                    __syncwarp();
+                }
+                if (f32) {
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        *reinterpret_cast<float4 *>(box + sw128_offset(lane, q)) =
+                            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                } else {
+                    const bool h = p.out_kind == SMOL_B200_GEMM_OUT_F16;
+                    if (h) {   // an fp16 output reports values it cannot hold instead of storing inf
+                        bool over = false;
+#pragma unroll
+                        for (int k = 0; k < 32; ++k) over |= row < p.M && n0 + c * 32 + k < p.N && f16_overflows(v[k]);
+                        if (over) atomicOr(p.err, kErrValueRange);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        uint4 w4;
+                        uint32_t *wp = reinterpret_cast<uint32_t *>(&w4);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const float x0 = v[u * 8 + 2 * j], x1 = v[u * 8 + 2 * j + 1];
+                            wp[j] = h ? pack_f16x2(x0, x1) : pack_bf16x2(x0, x1);
+                        }
+                        *reinterpret_cast<uint4 *>(box + sw128_offset(lane, (c & 1) * 4 + u)) = w4;
+                    }
+                }
+                // a box leaves when full: every fp32 chunk, every second 16-bit chunk, or the
+                // last chunk holding columns < N (columns past N are clipped by the store)
+                if (f32 || (c & 1) == 1 || c == n_chunks - 1) {
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        const int x = n0 + (f32 ? c : (c & ~1)) * 32, y = m0 + quarter * 32;
+                        if (p.out_kind == SMOL_B200_GEMM_OUT_F32_ADD)
+                            tma_reduce_add_4d(&p.to, smem_u32(box), x, y, 0, 0);
+                        else
+                            tma_store_4d(&p.to, smem_u32(box), x, y, 0, 0);
+                        bulk_commit();
+                    }
+                    __syncwarp();
+                    ++boxes;
+                }
             }
         }
+        if (lane == 0 && boxes > 0) bulk_wait_all0();   // the stores have completed before the CTA exits
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -468,6 +553,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_wide_kernel(const _
         tmem_dealloc(tmem, kWTmemCols);
     }
 }
+
+// SMOL_GEMM_TMA_OUT=0 in the environment keeps the wide form's per-row stores
+// (measurement knob).
+const bool g_gemm_tma_out = [] {
+    const char *e = getenv("SMOL_GEMM_TMA_OUT");
+    return !(e && e[0] == '0');
+}();
 
 // SMOL_GEMM_WIDE=0 in the environment keeps every GEMM on the one-tile-per-CTA
 // 128 x 128 form (measurement knob).
@@ -542,6 +634,18 @@ int gemm_bf16(cudaStream_t st, void *out, int64_t ldo, int out_kind, const uint1
     p.bias_vec = bias && reinterpret_cast<uintptr_t>(bias) % 16 == 0;
     p.add_vec = add && reinterpret_cast<uintptr_t>(add) % 16 == 0 && ld_add % 4 == 0;
     p.err = err;
+    // The wide form stages its epilogue through TMA stores when the output rows are
+    // 16-byte aligned and there is no gated pairing (whose 16 outputs per 32 columns keep
+    // the row stores): 32-row boxes of 128 bytes (32 fp32 / 64 bf16 or fp16 columns).
+    if (wide && p.vec_ok && !gate && g_gemm_tma_out) {
+        const CUtensorMapDataType dt = out_kind == SMOL_B200_GEMM_OUT_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                       : out_kind == SMOL_B200_GEMM_OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+        const long long plane = static_cast<long long>(ldo) * M;
+        if (!make_tmap_4d(&p.to, out, dt, esz, N, M, 1, 1, ldo, plane, plane, esz == 4 ? 32 : 64, 32, 1))
+            return SMOL_B200_ERR_CUDA;
+        p.tma_out = 1;
+    }
     if (wide) {
         static bool raised_w[64] = {};
         if (!raised_w[dev]) {
