@@ -51,8 +51,8 @@ constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 256;   // alignment sl
 
 struct GemmParams {
     CUtensorMap ta, tw;
-    CUtensorMap to;           // the output as a 32-row box map (wide form's staged epilogue)
-    int tma_out;              // 1: the wide form stores through `to` (TMA store, or reduce-add for F32_ADD)
+    CUtensorMap to;           // the output as a 32-row box map (staged epilogue)
+    int tma_out;              // 1: the epilogue stores through `to` (TMA store, or reduce-add for F32_ADD)
     void *out;
     long long ldo;
     const float *bias;        // [N] or null
@@ -217,6 +217,70 @@ __device__ __forceinline__ void store_chunk(const GemmParams &p, int row, int nb
     }
 }
 
+// Staged epilogue of one 32-column chunk (columns n0 + 32c) of a warp's 32 rows (from
+// y0): the values go into one of the warp's two alternating 4 KB boxes (32 rows x 128
+// bytes, 128B-swizzled) in `stage`, and a full box leaves as a TMA tensor store -- or,
+// for an fp32 output that is added to, as a TMA reduce-add, so the residual is added in
+// L2 and never read into the SM -- with one box in flight while the next is written.
+// fp32: one box per chunk; 16-bit: chunks 2j and 2j+1 share a box of 64 columns.
+__device__ __forceinline__ void staged_chunk(const GemmParams &p, uint8_t *stage, int &boxes, int row, int y0, int n0,
+                                             int c, int n_chunks, int lane, const uint32_t (&r)[32])
+{
+    const bool f32 = p.out_kind == SMOL_B200_GEMM_OUT_F32 || p.out_kind == SMOL_B200_GEMM_OUT_F32_ADD;
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
+    chunk_math(p, row, n0 + c * 32, v);
+    // fp32: one box per chunk; 16-bit: chunks 2j, 2j+1 share a box (64 columns)
+    const bool first_half = f32 || (c & 1) == 0;
+    uint8_t *box = stage + (boxes & 1) * 4096;
+    if (first_half) {
+        if (lane == 0 && boxes >= 1) bulk_wait_read1();   // this slot's previous store read it
+        __syncwarp();
+    }
+    if (f32) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4 *>(box + sw128_offset(lane, q)) =
+                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    } else {
+        const bool h = p.out_kind == SMOL_B200_GEMM_OUT_F16;
+        if (h) {   // an fp16 output reports values it cannot hold instead of storing inf
+            bool over = false;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) over |= row < p.M && n0 + c * 32 + k < p.N && f16_overflows(v[k]);
+            if (over) atomicOr(p.err, kErrValueRange);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            uint4 w4;
+            uint32_t *wp = reinterpret_cast<uint32_t *>(&w4);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float x0 = v[u * 8 + 2 * j], x1 = v[u * 8 + 2 * j + 1];
+                wp[j] = h ? pack_f16x2(x0, x1) : pack_bf16x2(x0, x1);
+            }
+            *reinterpret_cast<uint4 *>(box + sw128_offset(lane, (c & 1) * 4 + u)) = w4;
+        }
+    }
+    // a box leaves when full: every fp32 chunk, every second 16-bit chunk, or the
+    // last chunk holding columns < N (columns past N are clipped by the store)
+    if (f32 || (c & 1) == 1 || c == n_chunks - 1) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            const int x = n0 + (f32 ? c : (c & ~1)) * 32, y = y0;
+            if (p.out_kind == SMOL_B200_GEMM_OUT_F32_ADD)
+                tma_reduce_add_4d(&p.to, smem_u32(box), x, y, 0, 0);
+            else
+                tma_store_4d(&p.to, smem_u32(box), x, y, 0, 0);
+            bulk_commit();
+        }
+        __syncwarp();
+        ++boxes;
+    }
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 2) gemm_bf16_kernel(const __grid_constant__ GemmParams p)
 {
     extern __shared__ uint8_t smem_raw[];
@@ -303,12 +367,22 @@ __global__ void __launch_bounds__(kGemmThreads, 2) gemm_bf16_kernel(const __grid
         // warp-uniform: tcgen05.ld is a warp-collective instruction
         if (__all_sync(0xffffffffu, waited && atomicAdd(&bars->abort, 0) == 0)) {
             const uint32_t taddr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+            // staged epilogue (p.tma_out) in the first ring stage, free once the last MMA
+            // completed: two alternating 4 KB boxes per warp, as in the wide form
+            static_assert(kStageBytes >= 4 * 2 * 4096, "epilogue staging in ring stage 0");
+            uint8_t *my_stage = smem + quarter * 2 * 4096;
+            int boxes = 0;
+            const int n_chunks = min(kBN, p.N - n0 + 31) / 32;
             for (int c = 0; c < kBN / 32; ++c) {
+                if (c >= n_chunks) break;
                 uint32_t r[32];
                 tmem_ld32(taddr + c * 32, r);
                 tmem_ld_wait();
-                store_chunk(p, row, n0 + c * 32, r);
+                if (p.tma_out) staged_chunk(p, my_stage, boxes, row, m0 + quarter * 32, n0, c, n_chunks, lane, r);
+                else store_chunk(p, row, n0 + c * 32, r);
             }
+            if (lane == 0 && boxes > 0) bulk_wait_all0();   // the stores have completed before the CTA exits
+            __syncwarp();
         }
     }
 
@@ -453,7 +527,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_wide_kernel(const _
         // into the SM -- with one box in flight while the next is written
         uint8_t *my_stage = stage_out + quarter * 2 * 4096;
         int boxes = 0;   // boxes this warp has issued (lane 0 commits one bulk group per box)
-        const bool f32 = p.out_kind == SMOL_B200_GEMM_OUT_F32 || p.out_kind == SMOL_B200_GEMM_OUT_F32_ADD;
         int i = 0;
         for (int t = blockIdx.x; t < n_tiles; t += gridDim.x, ++i) {
             const int b = i & 1;
@@ -488,58 +561,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_wide_kernel(const _
                     store_chunk(p, row, n0 + c * 32, r);
                     continue;
                 }
-                float v[32];
-#pragma unroll
-                for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(r[k]);
-                chunk_math(p, row, n0 + c * 32, v);
-                // fp32: one box per chunk; 16-bit: chunks 2j, 2j+1 share a box (64 columns)
-                const bool first_half = f32 || (c & 1) == 0;
-                uint8_t *box = my_stage + (boxes & 1) * 4096;
-                if (first_half) {
-                    if (lane == 0 && boxes >= 1) bulk_wait_read1();   // this slot's previous store read it
-                    __syncwarp();
-                }
-                if (f32) {
-#pragma unroll
-                    for (int q = 0; q < 8; ++q)
-                        *reinterpret_cast<float4 *>(box + sw128_offset(lane, q)) =
-                            make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-                } else {
-                    const bool h = p.out_kind == SMOL_B200_GEMM_OUT_F16;
-                    if (h) {   // an fp16 output reports values it cannot hold instead of storing inf
-                        bool over = false;
-#pragma unroll
-                        for (int k = 0; k < 32; ++k) over |= row < p.M && n0 + c * 32 + k < p.N && f16_overflows(v[k]);
-                        if (over) atomicOr(p.err, kErrValueRange);
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        uint4 w4;
-                        uint32_t *wp = reinterpret_cast<uint32_t *>(&w4);
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            const float x0 = v[u * 8 + 2 * j], x1 = v[u * 8 + 2 * j + 1];
-                            wp[j] = h ? pack_f16x2(x0, x1) : pack_bf16x2(x0, x1);
-                        }
-                        *reinterpret_cast<uint4 *>(box + sw128_offset(lane, (c & 1) * 4 + u)) = w4;
-                    }
-                }
-                // a box leaves when full: every fp32 chunk, every second 16-bit chunk, or the
-                // last chunk holding columns < N (columns past N are clipped by the store)
-                if (f32 || (c & 1) == 1 || c == n_chunks - 1) {
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        const int x = n0 + (f32 ? c : (c & ~1)) * 32, y = m0 + quarter * 32;
-                        if (p.out_kind == SMOL_B200_GEMM_OUT_F32_ADD)
-                            tma_reduce_add_4d(&p.to, smem_u32(box), x, y, 0, 0);
-                        else
-                            tma_store_4d(&p.to, smem_u32(box), x, y, 0, 0);
-                        bulk_commit();
-                    }
-                    __syncwarp();
-                    ++boxes;
-                }
+                staged_chunk(p, my_stage, boxes, row, m0 + quarter * 32, n0, c, n_chunks, lane, r);
             }
         }
         if (lane == 0 && boxes > 0) bulk_wait_all0();   // the stores have completed before the CTA exits
@@ -634,10 +656,10 @@ int gemm_bf16(cudaStream_t st, void *out, int64_t ldo, int out_kind, const uint1
     p.bias_vec = bias && reinterpret_cast<uintptr_t>(bias) % 16 == 0;
     p.add_vec = add && reinterpret_cast<uintptr_t>(add) % 16 == 0 && ld_add % 4 == 0;
     p.err = err;
-    // The wide form stages its epilogue through TMA stores when the output rows are
-    // 16-byte aligned and there is no gated pairing (whose 16 outputs per 32 columns keep
-    // the row stores): 32-row boxes of 128 bytes (32 fp32 / 64 bf16 or fp16 columns).
-    if (wide && p.vec_ok && !gate && g_gemm_tma_out) {
+    // The epilogue stages through TMA stores when the output rows are 16-byte aligned and
+    // there is no gated pairing (whose 16 outputs per 32 columns keep the row stores):
+    // 32-row boxes of 128 bytes (32 fp32 / 64 bf16 or fp16 columns).
+    if (p.vec_ok && !gate && g_gemm_tma_out) {
         const CUtensorMapDataType dt = out_kind == SMOL_B200_GEMM_OUT_BF16   ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                        : out_kind == SMOL_B200_GEMM_OUT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
