@@ -62,6 +62,52 @@ __global__ void __launch_bounds__(kLnWarps * 32) layer_norm_kernel(void *out, in
     }
 }
 
+// The same for rows of a multiple of 128 floats up to 2048 (SigLIP-base 768, So400m
+// 1152): the warp reads its row once as float4 pieces kept in registers (lane l holds
+// elements 4l..4l+3 of every 128-float block), both reductions run on those registers,
+// and the output leaves as 8-byte (bf16) or 16-byte (fp32) pieces.
+constexpr int kLnMaxVec = 16;   // float4 pieces per lane: hidden <= 16 * 128
+__global__ void __launch_bounds__(kLnWarps * 32) layer_norm_vec_kernel(void *out, int out_bf16, const float *x,
+                                                                       const float *w, const float *b, int rows,
+                                                                       int hidden, float eps)
+{
+    const int row = blockIdx.x * kLnWarps + threadIdx.x / 32, lane = threadIdx.x % 32;
+    if (row >= rows) return;
+    const int nv = hidden / 128;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + static_cast<long long>(row) * hidden);
+    float4 v[kLnMaxVec];
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < kLnMaxVec; ++i)
+        if (i < nv) {
+            v[i] = xr[i * 32 + lane];
+            s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        }
+    const float mean = warp_sum(s) / static_cast<float>(hidden);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kLnMaxVec; ++i)
+        if (i < nv) {
+            const float a = v[i].x - mean, c = v[i].y - mean, d = v[i].z - mean, e = v[i].w - mean;
+            ss += (a * a + c * c) + (d * d + e * e);
+        }
+    const float inv = 1.0f / sqrtf(warp_sum(ss) / static_cast<float>(hidden) + eps);
+    const float4 *w4 = reinterpret_cast<const float4 *>(w), *b4 = reinterpret_cast<const float4 *>(b);
+#pragma unroll
+    for (int i = 0; i < kLnMaxVec; ++i) {
+        if (i >= nv) break;
+        const float4 wv = __ldg(w4 + i * 32 + lane), bv = __ldg(b4 + i * 32 + lane);
+        const float y0 = (v[i].x - mean) * inv * wv.x + bv.x, y1 = (v[i].y - mean) * inv * wv.y + bv.y;
+        const float y2 = (v[i].z - mean) * inv * wv.z + bv.z, y3 = (v[i].w - mean) * inv * wv.w + bv.w;
+        const long long e = static_cast<long long>(row) * hidden + i * 128 + 4 * lane;
+        if (out_bf16)
+            *reinterpret_cast<uint2 *>(static_cast<uint16_t *>(out) + e) = make_uint2(pack_bf16x2(y0, y1),
+                                                                                       pack_bf16x2(y2, y3));
+        else
+            *reinterpret_cast<float4 *>(static_cast<float *>(out) + e) = make_float4(y0, y1, y2, y3);
+    }
+}
+
 // a[img * n_patches + py * pw + px][(c * patch + ky) * patch + kx] =
 //     bf16(image[img][c][py * patch + ky][px * patch + kx]); columns [kin, lda) zero.
 __global__ void unfold_patches_kernel(uint16_t *a, long long lda, const float *images, int n_images, int size,
@@ -181,8 +227,11 @@ int layer_norm(cudaStream_t st, void *out, int out_bf16, const float *x, const f
     if (rows <= 0) return SMOL_B200_OK;
     if (!out || !x || !w || !b || hidden <= 0) return SMOL_B200_ERR_ARGS;
     const unsigned grid = static_cast<unsigned>((rows + kLnWarps - 1) / kLnWarps);
-    return launch_kernel(layer_norm_kernel, dim3(grid), dim3(kLnWarps * 32), 0, st, out, out_bf16, x, w, b, rows,
-                         hidden, eps) == cudaSuccess
+    const uintptr_t al = reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(x) |
+                         reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(b);
+    const bool vec = hidden % 128 == 0 && hidden <= kLnMaxVec * 128 && (al & 15) == 0;
+    return launch_kernel(vec ? layer_norm_vec_kernel : layer_norm_kernel, dim3(grid), dim3(kLnWarps * 32), 0, st,
+                         out, out_bf16, x, w, b, rows, hidden, eps) == cudaSuccess
                ? SMOL_B200_OK
                : SMOL_B200_ERR_CUDA;
 }
