@@ -532,9 +532,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_bf16_wide_kernel(const _
             const int b = i & 1;
             const int m0 = (t / tiles_n) * kBM, n0 = (t % tiles_n) * kWBN;
             const int row = m0 + quarter * 32 + lane;
-            // An fp32 output that is added to (the residual stream) is read back by this
-            // thread's row: start its 1 KB on the way to L2 while the tile's MMAs run, so the
-            // epilogue's read-add-write does not wait on HBM once per 32-column chunk.
+            // An fp32 output that is added to (the residual stream): start this thread's row
+            // of it (1 KB) on the way to L2 while the tile's MMAs run, where the epilogue's
+            // TMA reduce-adds (or, without them, its read-add-writes) will find it.
             if (p.out_kind == SMOL_B200_GEMM_OUT_F32_ADD && row < p.M) {
                 const char *orow = reinterpret_cast<const char *>(static_cast<const float *>(p.out) +
                                                                   static_cast<long long>(row) * p.ldo + n0);
