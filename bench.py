@@ -713,13 +713,16 @@ def run_cfg4(pk=None, world: int = 1, rank: int = 0) -> dict:
     kp4 = torch.randn((L4 * B4 * tot, kv4), device="cuda", generator=g).to(torch.bfloat16)
     vp4 = torch.randn((L4 * B4 * tot, kv4), device="cuda", generator=g).to(torch.float16)
     o4 = torch.empty((B4, P4, h4 * hd4), device="cuda")
+    # the same prefix with a bf16 output (the o-projection's operand type): half the
+    # output bytes, which a layer writes in one burst at the end of every work item
+    o4h = torch.empty((B4, P4, h4 * hd4), device="cuda", dtype=torch.bfloat16)
 
     a, b = ev(), ev()
 
-    def prefix():
+    def prefix(out=o4):
         for layer in range(L4):
             base = layer * B4 * tot
-            smol_b200.prefill_attention(o4, q4, kp4[base:], vp4[base:], B4, P4, P4, h4, hkv4, hd4, 1 / 16.0,
+            smol_b200.prefill_attention(out, q4, kp4[base:], vp4[base:], B4, P4, P4, h4, hkv4, hd4, 1 / 16.0,
                                         mask_kind=smol_b200.MASK_PREFIX_LM, prefix_len=P4,
                                         strides=((h4 * hd4, P4 * h4 * hd4), (h4 * hd4, P4 * h4 * hd4),
                                                  (kv4, tot * kv4), (kv4, tot * kv4)))
@@ -731,6 +734,14 @@ def run_cfg4(pk=None, world: int = 1, rank: int = 0) -> dict:
     b.record()
     torch.cuda.synchronize()
     ms4 = allreduce_max(a.elapsed_time(b), world)
+    prefix(o4h)
+    torch.cuda.synchronize()
+    barrier(world)
+    a.record()
+    prefix(o4h)
+    b.record()
+    torch.cuda.synchronize()
+    ms4h = allreduce_max(a.elapsed_time(b), world)
     fl4 = workload.prefix_lm_flops(P4, P4, h4, hd4) * B_all * L4
     qd = torch.randn((B4, h4 * hd4), device="cuda", generator=g)
     od = torch.empty_like(qd)
@@ -753,12 +764,14 @@ def run_cfg4(pk=None, world: int = 1, rank: int = 0) -> dict:
     tf = fl4 / (ms4 * 1e-3) / 1e12
     gbs = suf_bytes / (ms_s * 1e-3) / 1e9
     res = {"prefix_ms_18_layers": round(ms4, 3), "prefix_tflops": round(tf, 1),
+           "prefix_bf16_out_ms": round(ms4h, 3), "prefix_bf16_out_tflops": round(fl4 / (ms4h * 1e-3) / 1e12, 1),
            "suffix_128_steps_ms": round(ms_s, 2), "suffix_step_us": round(ms_s * 1e3 / S4, 1),
            "suffix_kv_gbs": round(gbs, 1),
            "kernels": "prefill_kernel<256> (prefix-LM mask) + decode_split_kernel<256> (MQA group 8); "
                       "the 128-step x 18-layer suffix replayed as one CUDA graph"}
     if pk is not None:
         res["prefix_frac_of_bf16_peak"] = round(tf / world / pk["bf16_tflops"], 4)
+        res["prefix_bf16_out_frac_of_bf16_peak"] = round(fl4 / (ms4h * 1e-3) / 1e12 / world / pk["bf16_tflops"], 4)
         res["suffix_hbm_frac"] = round(gbs / world / pk["hbm_gbs"], 4)
     if world > 1:
         res["workload"] = f"{B_all} sequences, {B4} per GPU on {world} GPUs (split by sequence, no collective)"
@@ -1222,7 +1235,7 @@ def main():
         torch.cuda.set_device(0)
         pk = peaks()
         fn = {"cfg1": run_cfg1, "cfg3": lambda: run_cfg3(pk, args.images, 1 if args.images else None),
-              "cfg4": run_cfg4, "decoder": lambda: [run_decoder(pk, 1), run_decoder(pk, 8)],
+              "cfg4": lambda: run_cfg4(pk), "decoder": lambda: [run_decoder(pk, 1), run_decoder(pk, 8)],
               "audio": lambda: run_audio_windows(pk),
               "siglip": lambda: run_siglip_encoder(pk, args.images),
               "so400m": lambda: run_so400m_attention(pk, args.images or 128, 1 if args.images else 27),
