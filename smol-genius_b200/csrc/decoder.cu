@@ -203,7 +203,7 @@ __device__ __forceinline__ RowRef row_ref(const GemvParams &p, int r, int k_dim)
 // warps, each warp streaming every S-th 256-element piece of K, and the S partial
 // sums meet in shared memory -- so a projection with few rows still spreads over
 // enough warps to keep HBM busy.
-template <int NB, int R>
+template <int NB, int R, bool Pre>
 __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_constant__ GemvParams p)
 {
     extern __shared__ float xs[];   // [nb][k_dim]
@@ -213,16 +213,29 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_co
     const int S = p.ksplit, G = kGemvWarps / S;
     const int slice = warp % S, grp = warp / S;
     const int n_groups = (p.total_rows + R - 1) / R;
+    const int k_first = (slice * 32 + lane) * 8, k_step = S * 256;
+    // Small products at small batches (Pre, R <= 2): the first kPre weight pieces of this
+    // warp's first rows are loaded into registers before the wait -- most warps own one
+    // row group, so its weights are in flight while the previous kernel finishes, and the
+    // product after the wait waits only for the staged activations.  (Large products keep
+    // the registers for occupancy: they are bound by HBM, not by the wait.)
+    constexpr int kPre = !Pre ? 0 : R == 1 ? 8 : R == 2 ? 6 : 0;
+    uint4 pre[R][kPre > 0 ? kPre : 1];
     {   // this warp's first rows stream from HBM while the previous kernel finishes
         const int rg = blockIdx.x * G + grp;
         if (rg < n_groups) {
 #pragma unroll
             for (int i = 0; i < R; ++i) {
                 if (rg * R + i >= p.total_rows) break;
-                // this warp reads the 512-byte pieces slice, slice+S, ... of the row: lane l
-                // takes 128-byte line l%4 of piece slice + (l/4)*S, 8 pieces per pass
-                const char *row = reinterpret_cast<const char *>(row_ref(p, rg * R + i, k_dim).w);
-                for (int off = (slice + (lane / 4) * S) * 512 + (lane % 4) * 128; off < k_dim * 2;
+                const uint16_t *wrow = row_ref(p, rg * R + i, k_dim).w;
+#pragma unroll
+                for (int n = 0; n < kPre; ++n)
+                    if (k_first + n * k_step < k_dim) pre[i][n] = ldg_stream(wrow + k_first + n * k_step);
+                // the rest of the row (past the preloaded pieces) on its way to L2: this warp
+                // reads the 512-byte pieces slice, slice+S, ... of the row: lane l takes
+                // 128-byte line l%4 of piece slice + (l/4)*S, 8 pieces per pass
+                const char *row = reinterpret_cast<const char *>(wrow);
+                for (int off = (slice + (lane / 4) * S) * 512 + (lane % 4) * 128 + kPre * S * 512; off < k_dim * 2;
                      off += 8 * S * 512)
                     asm volatile("prefetch.global.L2 [%0];" ::"l"(row + off));
             }
@@ -249,12 +262,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_co
         for (int i = 0; i < R; ++i)
 #pragma unroll
             for (int b = 0; b < NB; ++b) acc[i][b] = 0.f;
-#pragma unroll 2
-        for (int k = (slice * 32 + lane) * 8; k < k_dim; k += S * 256) {
+        // acc[i][b] += dot(8 weights of row i at k, x[b][k..k+8))
+        auto consume = [&](int k, const uint4 (&wv)[R]) {
             float wf[R][8];
 #pragma unroll
             for (int i = 0; i < R; ++i) {
-                const uint4 w = valid[i] ? ldg_stream(rr[i].w + k) : make_uint4(0, 0, 0, 0);
+                const uint4 w = wv[i];
                 const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -277,6 +290,24 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_co
                     }
                 }
             }
+        };
+        int k = k_first;
+        if (kPre > 0 && base == blockIdx.x * G) {   // the first row group: its preloaded pieces
+#pragma unroll
+            for (int n = 0; n < kPre; ++n, k += k_step) {
+                if (k >= k_dim) break;
+                uint4 wv[R];
+#pragma unroll
+                for (int i = 0; i < R; ++i) wv[i] = valid[i] ? pre[i][n] : make_uint4(0, 0, 0, 0);
+                consume(k, wv);
+            }
+        }
+#pragma unroll 2
+        for (; k < k_dim; k += k_step) {
+            uint4 wv[R];
+#pragma unroll
+            for (int i = 0; i < R; ++i) wv[i] = valid[i] ? ldg_stream(rr[i].w + k) : make_uint4(0, 0, 0, 0);
+            consume(k, wv);
         }
         if (S == 1) {   // the warp holds whole rows: write from lane 0, no CTA barrier
 #pragma unroll
@@ -527,22 +558,35 @@ int gemv_smem_bytes(int nb, int k_dim)
     return nb * k_dim * static_cast<int>(sizeof(float));
 }
 
-template <int NB, int R>
-int launch_gemv_nb(cudaStream_t st, GemvParams &p)
+// Products of at most this many weight bytes take the register preload (latency-bound
+// at small batches); larger ones keep the registers for occupancy.
+constexpr long long kGemvPreMaxBytes = 32ll << 20;
+
+template <int NB, int R, bool Pre>
+int launch_gemv_pre(cudaStream_t st, const GemvParams &p, long long grid, int smem)
 {
-    const int smem = gemv_smem_bytes(p.nb, p.k_dim);
     if (smem > 48 * 1024) {
         static bool raised[64] = {};
         const int dev = current_device();
         if (dev < 0 || dev >= 64) return SMOL_B200_ERR_CUDA;
         if (!raised[dev]) {
             // dynamic + static (the norm partials) must stay within the 227 KB per block
-            if (cudaFuncSetAttribute(gemv_bf16_kernel<NB, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            if (cudaFuncSetAttribute(gemv_bf16_kernel<NB, R, Pre>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      kMaxXsBytes) != cudaSuccess)
                 return SMOL_B200_ERR_CUDA;
             raised[dev] = true;
         }
     }
+    return launch_kernel(gemv_bf16_kernel<NB, R, Pre>, dim3(static_cast<unsigned>(grid)), dim3(kGemvThreads), smem,
+                         st, p) == cudaSuccess
+               ? SMOL_B200_OK
+               : SMOL_B200_ERR_CUDA;
+}
+
+template <int NB, int R>
+int launch_gemv_nb(cudaStream_t st, GemvParams &p)
+{
+    const int smem = gemv_smem_bytes(p.nb, p.k_dim);
     // K slices per row group: enough warps in flight for HBM (~16 per SM), while each
     // slice keeps at least one 256-element piece per lane.
     const long long groups = (p.total_rows + R - 1) / R;
@@ -553,10 +597,9 @@ int launch_gemv_nb(cudaStream_t st, GemvParams &p)
     const int G = kGemvWarps / S;
     long long grid = (groups + G - 1) / G;
     if (grid > 148LL * g_gemv_ctas_per_sm) grid = 148LL * g_gemv_ctas_per_sm;
-    return launch_kernel(gemv_bf16_kernel<NB, R>, dim3(static_cast<unsigned>(grid)), dim3(kGemvThreads), smem, st,
-                         p) == cudaSuccess
-               ? SMOL_B200_OK
-               : SMOL_B200_ERR_CUDA;
+    if (static_cast<long long>(p.total_rows) * p.k_dim * 2 <= kGemvPreMaxBytes)
+        return launch_gemv_pre<NB, R, true>(st, p, grid, smem);
+    return launch_gemv_pre<NB, R, false>(st, p, grid, smem);
 }
 
 // Rows per warp: 1 for a single sequence (most warps in flight), 2 for two, 4 from four
