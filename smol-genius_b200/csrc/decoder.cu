@@ -203,9 +203,16 @@ __device__ __forceinline__ RowRef row_ref(const GemvParams &p, int r, int k_dim)
 // warps, each warp streaming every S-th 256-element piece of K, and the S partial
 // sums meet in shared memory -- so a projection with few rows still spreads over
 // enough warps to keep HBM busy.
-template <int NB, int R, bool Pre>
+// XReg (one sequence, at most kXPieces 256-element pieces of K per lane, and the norm
+// only where one warp covers all of K): the activations never go through shared memory
+// -- each lane loads the pieces it multiplies straight into registers after the wait,
+// the warp's lanes together hold all of x for the RMSNorm, and no CTA barrier is needed.
+constexpr int kXPieces = 4;
+
+template <int NB, int R, bool Pre, bool XReg = false>
 __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_constant__ GemvParams p)
 {
+    static_assert(!XReg || NB == 1, "register activations: one sequence");
     extern __shared__ float xs[];   // [nb][k_dim]
     __shared__ float part[kGemvWarps][R][NB];
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -219,7 +226,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_co
     // row group, so its weights are in flight while the previous kernel finishes, and the
     // product after the wait waits only for the staged activations.  (Large products keep
     // the registers for occupancy: they are bound by HBM, not by the wait.)
-    constexpr int kPre = !Pre ? 0 : R == 1 ? 8 : R == 2 ? 6 : 0;
+    constexpr int kPre = !Pre ? 0 : XReg ? kXPieces : R == 1 ? 8 : R == 2 ? 6 : 0;
     uint4 pre[R][kPre > 0 ? kPre : 1];
     {   // this warp's first rows stream from HBM while the previous kernel finishes
         const int rg = blockIdx.x * G + grp;
@@ -243,9 +250,53 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_co
     }
     griddep_wait();
     griddep_trigger();   // one successor may start (and prefetch) while this one works
-    stage_x<NB>(xs, p.x, p.ldx, k_dim, p.nb, p.norm_w, p.eps);
-    if (p.x_normed && blockIdx.x == 0)
-        for (int i = threadIdx.x; i < p.nb * k_dim; i += blockDim.x) p.x_normed[(i / k_dim) * p.ldx + i % k_dim] = xs[i];
+    float xr[XReg ? kXPieces : 1][8];   // XReg: this lane's pieces of x (k = k_first + n * k_step)
+    if constexpr (XReg) {
+        float ss = 0.f;
+#pragma unroll
+        for (int n = 0; n < kXPieces; ++n) {
+            const int k = k_first + n * k_step;
+            if (k < k_dim) {
+                const float4 a = *reinterpret_cast<const float4 *>(p.x + k);
+                const float4 c = *reinterpret_cast<const float4 *>(p.x + k + 4);
+                xr[n][0] = a.x, xr[n][1] = a.y, xr[n][2] = a.z, xr[n][3] = a.w;
+                xr[n][4] = c.x, xr[n][5] = c.y, xr[n][6] = c.z, xr[n][7] = c.w;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) ss += xr[n][j] * xr[n][j];
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) xr[n][j] = 0.f;
+            }
+        }
+        if (p.norm_w) {   // smol_rms_norm's (x * w) * 1/sqrtf(mean(x^2) + eps); one warp holds all of x
+            const float r = 1.0f / sqrtf(warp_sum(ss) / static_cast<float>(k_dim) + p.eps);
+#pragma unroll
+            for (int n = 0; n < kXPieces; ++n) {
+                const int k = k_first + n * k_step;
+                if (k < k_dim) {
+                    const float4 a = __ldg(reinterpret_cast<const float4 *>(p.norm_w + k));
+                    const float4 c = __ldg(reinterpret_cast<const float4 *>(p.norm_w + k + 4));
+                    const float wn[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) xr[n][j] = xr[n][j] * wn[j] * r;
+                }
+            }
+        }
+        if (p.x_normed && blockIdx.x == 0 && warp == 0) {
+#pragma unroll
+            for (int n = 0; n < kXPieces; ++n) {
+                const int k = k_first + n * k_step;
+                if (k < k_dim)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) p.x_normed[k + j] = xr[n][j];
+            }
+        }
+    } else {
+        stage_x<NB>(xs, p.x, p.ldx, k_dim, p.nb, p.norm_w, p.eps);
+        if (p.x_normed && blockIdx.x == 0)
+            for (int i = threadIdx.x; i < p.nb * k_dim; i += blockDim.x)
+                p.x_normed[(i / k_dim) * p.ldx + i % k_dim] = xs[i];
+    }
     // every warp runs the same number of rounds (the CTA meets at the partial-sum barriers)
     for (int base = blockIdx.x * G; base < n_groups; base += gridDim.x * G) {
         const int rg = base + grp;
@@ -291,8 +342,30 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_bf16_kernel(const __grid_co
                 }
             }
         };
-        int k = k_first;
-        if (kPre > 0 && base == blockIdx.x * G) {   // the first row group: its preloaded pieces
+        if constexpr (XReg) {   // x in registers: piece n of every row against xr[n]
+            const bool first = base == blockIdx.x * G;
+#pragma unroll
+            for (int n = 0; n < kXPieces; ++n) {
+                const int k = k_first + n * k_step;
+                if (k >= k_dim) break;
+#pragma unroll
+                for (int i = 0; i < R; ++i) {
+                    const uint4 w = !valid[i]               ? make_uint4(0, 0, 0, 0)
+                                    : (first && n < kPre) ? pre[i][n < kPre ? n : 0]
+                                                          : ldg_stream(rr[i].w + k);
+                    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+                    float a = acc[i][0];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        a = fmaf(bf16lo_f32(u[j]), xr[n][2 * j], a);
+                        a = fmaf(bf16hi_f32(u[j]), xr[n][2 * j + 1], a);
+                    }
+                    acc[i][0] = a;
+                }
+            }
+        }
+        int k = XReg ? k_dim : k_first;
+        if (!XReg && kPre > 0 && base == blockIdx.x * G) {   // the first row group: its preloaded pieces
 #pragma unroll
             for (int n = 0; n < kPre; ++n, k += k_step) {
                 if (k >= k_dim) break;
@@ -558,6 +631,13 @@ int gemv_smem_bytes(int nb, int k_dim)
     return nb * k_dim * static_cast<int>(sizeof(float));
 }
 
+// SMOL_GEMV_XREG=0 in the environment stages the activations in shared memory for every
+// product (measurement knob).
+const bool g_gemv_xreg = [] {
+    const char *e = getenv("SMOL_GEMV_XREG");
+    return !(e && e[0] == '0');
+}();
+
 // Products of at most this many weight bytes take the register preload (latency-bound
 // at small batches); larger ones keep the registers for occupancy.
 constexpr long long kGemvPreMaxBytes = 32ll << 20;
@@ -565,6 +645,16 @@ constexpr long long kGemvPreMaxBytes = 32ll << 20;
 template <int NB, int R, bool Pre>
 int launch_gemv_pre(cudaStream_t st, const GemvParams &p, long long grid, int smem)
 {
+    if constexpr (NB == 1 && Pre) {
+        // one sequence, a small product whose K fits kXPieces pieces per lane, with the
+        // norm only where a warp covers all of K: activations in registers
+        const int pieces = (p.k_dim + p.ksplit * 256 - 1) / (p.ksplit * 256);
+        if (g_gemv_xreg && pieces <= kXPieces && (p.ksplit == 1 || !p.norm_w))
+            return launch_kernel(gemv_bf16_kernel<NB, R, Pre, true>, dim3(static_cast<unsigned>(grid)),
+                                 dim3(kGemvThreads), 0, st, p) == cudaSuccess
+                       ? SMOL_B200_OK
+                       : SMOL_B200_ERR_CUDA;
+    }
     if (smem > 48 * 1024) {
         static bool raised[64] = {};
         const int dev = current_device();
