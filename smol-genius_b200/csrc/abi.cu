@@ -507,6 +507,15 @@ size_t smol_b200_decode_step_scratch_bytes(int n_seqs, int max_kv_len, int n_hea
     return step_layout(n_seqs, max_kv_len, n_heads, n_kv_heads, head_dim).total;
 }
 
+// SMOL_STEP_CHUNKS=n in the environment sets the number of sequence chunks of
+// smol_b200_decode_step_host (measurement knob; 0 or unset: by batch size, at most 4,
+// at most kMaxChunks).
+static const int g_step_chunks = [] {
+    const char *e = getenv("SMOL_STEP_CHUNKS");
+    const int v = e ? atoi(e) : 0;
+    return v > 0 ? (v < smolb200::StepPipe::kMaxChunks ? v : smolb200::StepPipe::kMaxChunks) : 0;
+}();
+
 int smol_b200_decode_step_host(void *stream, float *out_host, const float *q_host, const float *k_host,
                                const float *v_host, int n_seqs, int n_heads, int n_kv_heads, int head_dim,
                                const float *q_norm_w, const float *k_norm_w, float eps, const float *rope_cos,
@@ -532,18 +541,24 @@ int smol_b200_decode_step_host(void *stream, float *out_host, const float *q_hos
     StepPipe *P = step_pipe();
     if (!P) return record(SMOL_B200_ERR_CUDA, "smol_b200_decode_step_host");
     std::lock_guard<std::mutex> lock(*P->mu);
-    // The batch goes in up to four chunks of sequences: the inputs of chunk c+1 copy in
-    // and the result of chunk c-1 copies out while chunk c computes (three streams).
-    const int chunks = n_seqs >= 128 ? 4 : (n_seqs >= 64 ? 2 : 1);
+    // The batch goes in two chunks of sequences from 64 on: the inputs of the second copy
+    // in and the result of the first copies out while the other computes (three streams).
+    // More, smaller chunks measured slower end to end (cfg 2: 4 chunks 5686 GB/s, 8
+    // chunks 5142, 2 chunks 5843-5916): each chunk's attention launch fills the GPU less.
+    int chunks = n_seqs >= 64 ? 2 : 1;
+    if (g_step_chunks > 0) chunks = g_step_chunks < n_seqs ? g_step_chunks : n_seqs;
+    auto bound = [&](int c) {   // first sequence of chunk c
+        return static_cast<int>(static_cast<long long>(n_seqs) * c / chunks);
+    };
     const size_t qw = static_cast<size_t>(n_heads) * head_dim, kw = static_cast<size_t>(n_kv_heads) * head_dim;
     bool ok = cuda_check(cudaEventRecord(P->start, st), "record") &&          // after the caller's prior work
               cuda_check(cudaStreamWaitEvent(P->h2d, P->start, 0), "wait") &&
               cuda_check(cudaStreamWaitEvent(P->compute, P->start, 0), "wait");
     int rc = SMOL_B200_OK;
     for (int c = 0; c < chunks && ok && rc == SMOL_B200_OK; ++c) {
-        const int s0 = static_cast<int>(static_cast<long long>(n_seqs) * c / chunks);
-        const int s1 = static_cast<int>(static_cast<long long>(n_seqs) * (c + 1) / chunks);
+        const int s0 = bound(c), s1 = bound(c + 1);
         const int nc = s1 - s0;
+        if (nc <= 0) continue;
         ok = cuda_check(cudaMemcpyAsync(q + s0 * qw, q_host + s0 * qw, nc * qw * 4, cudaMemcpyHostToDevice, P->h2d),
                         "copy q") &&
              cuda_check(cudaMemcpyAsync(k + s0 * kw, k_host + s0 * kw, nc * kw * 4, cudaMemcpyHostToDevice, P->h2d),

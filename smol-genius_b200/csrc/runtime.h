@@ -95,7 +95,7 @@ int launch_watchdog_selftest(cudaStream_t st);
 // (smol_b200_decode_step_host): inputs in on h2d, kernels on compute, results out on
 // d2h.  One per device, created on first use; `mu` serialises its users.
 struct StepPipe {
-    static constexpr int kMaxChunks = 4;
+    static constexpr int kMaxChunks = 8;
     cudaStream_t h2d = nullptr, compute = nullptr, d2h = nullptr;
     cudaEvent_t start = nullptr, in[kMaxChunks] = {}, done[kMaxChunks] = {};
     std::mutex *mu = nullptr;
