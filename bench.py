@@ -944,7 +944,11 @@ def run_decoder_dropin(layers: int = 1) -> dict:
     hidden 1024, 16/8 heads, `layers` layers) through the reference's own
     qkn_decoder_prefill / _forward on the host cores (oracle/_ref/qkn_dropin_ref) and
     through the decoder-level drop-in on the device (oracle/_ref/qkn_dropin_device):
-    wall-clock time of the calls with host buffers in and out, and token identity."""
+    wall-clock time of the calls with host buffers in and out, and token identity.
+    Each program runs twice: as a process's first generation (`first_run`: the device
+    context, module loading and the weight upload fall inside the first calls) and with
+    SMOL_DROPIN_WARM=1 (the same generation after one unreported run and a cache reset:
+    the steady state a serving process sees); the speed-ups compare the warm runs."""
     ref_dir = os.path.join(ROOT, "oracle", "_ref")
     # the decisive copy model of tests/test_dropin_device_gpu.py (smallest top-2 logit margin
     # ~9): with more layers the reference itself changes tokens once its cache is rounded
@@ -955,20 +959,35 @@ def run_decoder_dropin(layers: int = 1) -> dict:
         exe = os.path.join(ref_dir, f"qkn_dropin_{kind}")
         if not os.path.exists(exe):
             return {"unavailable": f"{exe} not built"}
-        p = subprocess.run([exe, *args], capture_output=True, text=True, timeout=900)
-        if p.returncode != 0:
-            return {"error": f"{kind}: exit {p.returncode}: {p.stderr[-300:]}"}
-        t = p.stderr.split("prefill_ms")[1].split()
-        res[kind] = {"prefill_ms": float(t[0]), "forward_ms_per_step": float(t[2]), "tokens": p.stdout.split()}
-    return {"workload": f"reference decoder driver, hidden 1024, {layers} layer(s), prefill 511 + 128 steps",
-            "reference_cpu": {k: v for k, v in res["ref"].items() if k != "tokens"},
-            "device_dropin": {k: v for k, v in res["device"].items() if k != "tokens"},
-            "forward_speedup": round(res["ref"]["forward_ms_per_step"] / res["device"]["forward_ms_per_step"], 1),
-            "prefill_speedup": round(res["ref"]["prefill_ms"] / res["device"]["prefill_ms"], 1),
-            "tokens_equal": res["ref"]["tokens"] == res["device"]["tokens"],
-            "first_differing_step": next((i for i, (x, y) in enumerate(zip(res["ref"]["tokens"], res["device"]["tokens"]))
+        for warm in (0, 1):
+            p = subprocess.run([exe, *args], capture_output=True, text=True, timeout=900,
+                               env={**os.environ, "SMOL_DROPIN_WARM": str(warm)})
+            if p.returncode != 0:
+                return {"error": f"{kind} (warm={warm}): exit {p.returncode}: {p.stderr[-300:]}"}
+            t = p.stderr.split("prefill_ms")[1].split()
+            res[(kind, warm)] = {"prefill_ms": float(t[0]), "forward_ms_per_step": float(t[2]),
+                                 "tokens": p.stdout.split()}
+
+    def times(kind):
+        warm, first = res[(kind, 1)], res[(kind, 0)]
+        return {"prefill_ms": warm["prefill_ms"], "forward_ms_per_step": warm["forward_ms_per_step"],
+                "first_run": {"prefill_ms": first["prefill_ms"], "forward_ms_per_step": first["forward_ms_per_step"]}}
+
+    ref, dev = res[("ref", 1)], res[("device", 1)]
+    streams = [res[(k, w)]["tokens"] for k in ("ref", "device") for w in (0, 1)]
+    return {"workload": f"reference decoder driver, hidden 1024, {layers} layer(s), vocab 4096, "
+                        "prefill 511 + 128 steps",
+            "reference_cpu": times("ref"),
+            "device_dropin": times("device"),
+            "forward_speedup": round(ref["forward_ms_per_step"] / dev["forward_ms_per_step"], 2),
+            "prefill_speedup": round(ref["prefill_ms"] / dev["prefill_ms"], 2),
+            "tokens_equal": all(x == streams[0] for x in streams),
+            "first_differing_step": next((i for i, (x, y) in enumerate(zip(ref["tokens"], dev["tokens"]))
                                           if x != y), None),
-            "note": "device prefill_ms includes the first call's upload of the weights"}
+            "note": "warm runs (one unreported generation first); first_run = a process's first generation, "
+                    "whose first device call includes context creation and the weight upload; the device "
+                    "prefill call returns once its work is queued (about 0.15 ms of GPU time at this size), "
+                    "which the first forward call's copy then waits for"}
 
 
 def run_other_configs(pk, world: int = 1, rank: int = 0) -> dict:

@@ -53,9 +53,11 @@ void dd_release(dd_state *st)
         for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++) smol_b200_device_free((void *)bufs[i]);
     }
     const void *bufs[] = {st->model.tok_embeddings, st->model.final_norm, st->model.lm_head, st->k_pool, st->v_pool,
-                          st->row0_dev, st->cos, st->sin, st->cos_local, st->sin_local, st->kv_len_dev,
-                          st->token_dev, st->x_dev, st->xn_dev, st->step_ws, st->prefill_ws};
+                          st->row0_dev, st->cos, st->sin, st->cos_local, st->sin_local, st->step_in_dev,
+                          st->step_out_dev, st->x_dev, st->step_ws, st->prefill_ws};
     for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++) smol_b200_device_free((void *)bufs[i]);
+    free(st->step_in_host);
+    free(st->step_out_host);
     memset(st, 0, sizeof(*st));
 }
 
@@ -169,11 +171,12 @@ int dd_setup(dd_state *st, const dd_config *c, const dd_layer *layers, const uin
     m->embed_normalizer = c->embed_normalizer;
     m->attn_softcap = c->attn_softcap;
     m->sliding_window = c->sliding_window;
-    st->kv_len_dev = (int *)smol_b200_device_alloc(sizeof(int));
-    st->token_dev = (int *)smol_b200_device_alloc(sizeof(int));
-    st->xn_dev = (float *)smol_b200_device_alloc(H * 4);
-    if (!m->tok_embeddings || !m->final_norm || (lm_head && !m->lm_head) || !st->kv_len_dev || !st->token_dev ||
-        !st->xn_dev) {
+    st->step_in_dev = (float *)smol_b200_device_alloc((H + 1) * 4);
+    st->step_out_dev = (float *)smol_b200_device_alloc((H + 1) * 4);
+    st->step_in_host = (float *)malloc((H + 1) * 4);
+    st->step_out_host = (float *)malloc((H + 1) * 4);
+    if (!m->tok_embeddings || !m->final_norm || (lm_head && !m->lm_head) || !st->step_in_dev || !st->step_out_dev ||
+        !st->step_in_host || !st->step_out_host) {
         dd_release(st);
         return -1;
     }
@@ -298,19 +301,21 @@ int dd_forward(dd_state *st, const float *embed, int pos, float *x_normed)
 {
     int token = -1;
     const size_t H = (size_t)st->cfg.hidden;
-    if (!st->ready || !position_held(st, pos) || !ensure_capacity(st, pos + 2, st->held, 1) ||
-        smol_b200_copy(st->x_dev, embed, H * 4) != SMOL_B200_OK ||
-        smol_b200_copy(st->kv_len_dev, &pos, sizeof(int)) != SMOL_B200_OK)
-        return -1;
-    if (smol_b200_qkn_decode_step_embeds(NULL, &st->model, 1, st->x_dev, st->token_dev, st->k_pool, st->v_pool,
-                                         (int64_t)st->cfg.layers * st->cap, st->row0_dev, st->kv_len_dev,
+    if (!st->ready || !position_held(st, pos) || !ensure_capacity(st, pos + 2, st->held, 1)) return -1;
+    memcpy(st->step_in_host, embed, H * 4);
+    memcpy(st->step_in_host + H, &pos, sizeof(int));
+    if (smol_b200_copy(st->step_in_dev, st->step_in_host, (H + 1) * 4) != SMOL_B200_OK) return -1;
+    if (smol_b200_qkn_decode_step_embeds(NULL, &st->model, 1, st->step_in_dev, (int *)(st->step_out_dev + H),
+                                         st->k_pool, st->v_pool, (int64_t)st->cfg.layers * st->cap, st->row0_dev,
+                                         (int *)(st->step_in_dev + H),
                                          pos /* the split-KV plan follows the actual length */, st->cos, st->sin, 0,
-                                         st->step_ws, st->step_ws_bytes, st->xn_dev) != SMOL_B200_OK ||
-        smol_b200_copy(&token, st->token_dev, sizeof(int)) != SMOL_B200_OK ||
-        (x_normed && smol_b200_copy(x_normed, st->xn_dev, H * 4) != SMOL_B200_OK)) {
+                                         st->step_ws, st->step_ws_bytes, st->step_out_dev) != SMOL_B200_OK ||
+        smol_b200_copy(st->step_out_host, st->step_out_dev, (H + 1) * 4) != SMOL_B200_OK) {
         distrust_from(st, pos);
         return -1;
     }
+    memcpy(&token, st->step_out_host + H, sizeof(int));
+    if (x_normed) memcpy(x_normed, st->step_out_host, H * 4);
     st->held = pos + 1;
     return token;
 }

@@ -44,8 +44,13 @@ typedef struct {
     int64_t *row0_dev;
     int rope_cap;
     float *cos, *sin, *cos_local, *sin_local;
-    int *kv_len_dev, *token_dev;
-    float *x_dev, *xn_dev;
+    /* A decode step's input and output, each one block so that a step makes one copy
+     * each way: [hidden] embedding + the position (an int in the last slot), and
+     * [hidden] final normalised state + the greedy token (likewise); the host staging
+     * buffers have the same layout. */
+    float *step_in_dev, *step_out_dev;
+    float *step_in_host, *step_out_host;
+    float *x_dev;   /* prefill input rows */
     int x_cap;
     void *step_ws, *prefill_ws;
     size_t step_ws_bytes, prefill_ws_bytes;
