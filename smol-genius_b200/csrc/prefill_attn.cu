@@ -34,10 +34,15 @@ namespace smolb200 {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kThreads = 192;
+// v1 warps: 0-3 softmax (one query row per thread), 4 TMA producer, 5 MMA issuer, 6-9
+// epilogue (each reads the TMEM lanes of warp index % 4, i.e. the rows of softmax warp
+// index % 4), so an item's output leaves while the next item's scores are computed.
+constexpr int kThreads = 320;
 constexpr int kSoftmaxThreads = 128;
 constexpr int kProducerWarp = 4;
 constexpr int kMmaWarp = 5;
+constexpr int kEpiWarp0 = 6;
+constexpr int kEpiWarps = 4;
 // A tile's row sum of exponentials against the row's reference point may reach 2^15
 // before the row moves its reference (each P value then fits fp16)
 constexpr float kSpecSumLimit = 32768.0f;
@@ -57,15 +62,19 @@ struct PrefillShape {
     // Epilogue staging: 8 KB per softmax warp (two 32-row x 128-byte TMA store boxes).
     static constexpr int kStageWarpBytes = 2 * 32 * 128;
     static constexpr int kOffStage = kOffV + kStages * kKvBytes;
-    static constexpr int kOffBar = kOffStage + 4 * kStageWarpBytes;
+    static constexpr int kOffBar = kOffStage + kEpiWarps * kStageWarpBytes;
     static constexpr int kUsed = kOffBar + 256 + 1024;
     static_assert(kUsed <= 227 * 1024, "shared memory");
     // At least ~116 KB so that a single CTA is resident per SM: every CTA
     // allocates all 512 TMEM columns.
     static constexpr int kSmemBytes = kUsed > 118 * 1024 ? kUsed : 118 * 1024;
     static constexpr int kTmS0 = 0, kTmS1 = BN, kTmO = 2 * BN;
+    // Two columns after O hold each row's sum of exponentials for the epilogue warps,
+    // by item parity (an item's sum is written while the epilogue may still read the
+    // previous item's).
+    static constexpr int kTmL = 2 * BN + HD;
     static constexpr int kTmCols = 512;
-    static_assert(2 * BN + HD <= 512, "TMEM budget");
+    static_assert(kTmL + 2 <= 512, "TMEM budget");
 };
 
 constexpr int kMaxExtraOuts = 7;   // further copies of the output (peers of an all-gather)
@@ -101,6 +110,8 @@ struct Barriers {
     uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
     uint64_t s_full[2], p_full[2];
     uint64_t o_done, mma_done;
+    uint64_t o_final;   // an item's last PV is complete (O and its row sums are final)
+    uint64_t o_free;    // the epilogue warps have read O (the next item's first PV may start)
     uint32_t tmem_base;
 };
 
@@ -332,6 +343,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         }
         mbar_init(smem_u32(&bars->o_done), 1);
         mbar_init(smem_u32(&bars->mma_done), 1);
+        mbar_init(smem_u32(&bars->o_final), 1);
+        mbar_init(smem_u32(&bars->o_free), kEpiWarps);
         fence_mbar_init();
     }
     if (warp == kMmaWarp) {
@@ -407,9 +420,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             constexpr uint32_t idesc_s = umma_idesc_f16(kBM, BN, true, false);
             constexpr uint32_t idesc_pv = umma_idesc_f16(kBM, HD, false, true);
             const uint32_t q_addr = smem_u32(sQ);
-            // O += P(g) V(g); `first` starts the accumulation of an item
+            int oit = 0;   // items with key tiles issued so far
+            // O += P(g) V(g); `first` starts the accumulation of an item, which overwrites O:
+            // the epilogue warps must have read the previous item's O first
             auto issue_pv = [&](int g, bool first) -> bool {
                 const int st = g & 1;
+                if (first && oit > 0 &&
+                    !mbar_wait_warp(smem_u32(&bars->o_free), (oit - 1) & 1, p.err, kErrWaitSoftmax))
+                    return false;
                 if (!mbar_wait_warp(smem_u32(&bars->p_full[st]), (g >> 1) & 1, p.err, kErrWaitSoftmax)) return false;
                 if (!mbar_wait_warp(smem_u32(&bars->v_full[st]), (g >> 1) & 1, p.err, kErrWaitTmaFull)) return false;
                 tc_fence_after();
@@ -433,8 +451,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 const int n = it.n_tiles;
                 if (n == 0) continue;
                 ok = mbar_wait_warp(smem_u32(&bars->q_full), qit & 1, p.err, kErrWaitTmaFull);
-                // O is overwritten by the item's first PV: its readers (the previous item's
-                // epilogue) are the threads whose p_full arrival that PV waits for.
                 for (int j = 0; j < n && ok; ++j) {
                     const int g = g0 + j;
                     const int st = g & 1;
@@ -455,14 +471,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     if (j >= 1 && !(ok = issue_pv(g - 1, j == 1))) break;
                 }
                 if (ok) ok = issue_pv(g0 + n - 1, n == 1);
+                if (ok) umma_commit_elect(smem_u32(&bars->o_final));
                 g0 += n;
                 ++qit;
+                ++oit;
             }
             // Every MMA must be complete before TMEM is released.
             umma_commit_elect(smem_u32(&bars->mma_done));
             mbar_wait_warp(smem_u32(&bars->mma_done), 0, p.err, kErrDrain);
         }
-    } else {
+    } else if (warp < kProducerWarp) {
         // ================= softmax: thread owns query row `row` =================
         // tcgen05.ld / tcgen05.st are warp-collective, so every branch around them is
         // made warp-uniform (votes) and per-row decisions only select values.
@@ -470,9 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
         const float cap = p.softcap;
         const float inv_cap = cap > 0.f ? 1.f / cap : 0.f;
         const float kLog2e = 1.4426950408889634f;
-        bool stores_pending = false;   // lane 0: a TMA store from this warp's staging area
-        int slot = 0;                  // staging slot of the warp's next box (alternates across items)
-        int g0 = 0;
+        int g0 = 0, oit = 0;
         bool ok = true;
         for (int r = 0; r < n_rounds && ok; ++r) {
             const int k = item1_index(r);
@@ -596,24 +612,51 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                 }
                 if (!ok) break;
                 l += lt;
+                // the item's row sums for the epilogue warps (read after the last PV, which
+                // waits for this arrival)
+                if (j + 1 == n_tiles) tmem_st1(lane_base + S::kTmL + (oit & 1), __float_as_uint(l));
                 tmem_st_wait();
                 tc_fence_before();
                 mbar_arrive(smem_u32(&bars->p_full[st]));
             }
             if (!ok) break;
-            // ---- epilogue: O / l -> out ----
-            // The last S of an item is issued before its second-to-last PV, so o_done can
-            // still be two phases short of the last PV here: wait for both, in order (a
-            // parity wait is only exact one phase ahead).
+            if (n_tiles > 0) ++oit;
+            g0 += n_tiles;
+        }
+    } else {
+        // ================= epilogue: O / l -> out, rows of TMEM lane quarter warp % 4 =================
+        const int quarter = warp % 4;
+        const uint32_t lane_base = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+        bool stores_pending = false;   // lane 0: a TMA store from this warp's staging area
+        int slot = 0;                  // staging slot of the warp's next box (alternates across items)
+        int oit = 0;
+        bool ok = true;
+        for (int r = 0; r < n_rounds && ok; ++r) {
+            const int k = item1_index(r);
+            if (k >= n_items) break;
+            const Item1 it = item1_geometry<BN>(p, k);
+            const int n_tiles = it.n_tiles;
+            const int vrow = it.q0 + quarter * 32 + lane;   // packed row of this thread
+            const int row = vrow / p.pack;                 // its position
+            const int head = it.h + vrow % p.pack;
+            const bool row_valid = row < p.seq_q;
+            int my_lo = 0, my_hi = 0;
+            bool my_written = false;
+            if (row_valid) row_range(p, row, my_lo, my_hi, my_written);
             bool have_o = n_tiles > 0;
-            if (have_o && n_tiles >= 2)
-                have_o = ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done), (g0 + n_tiles - 2) & 1,
-                                                                 p.err, kErrWaitMma));
-            if (have_o)
-                have_o = ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done), (g0 + n_tiles - 1) & 1,
-                                                                 p.err, kErrWaitMma));
-            tc_fence_after();
-            const float inv = l > 0.f ? 1.f / l : 0.f;
+            float inv = 0.f;
+            if (have_o) {
+                have_o = ok =
+                    __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_final), oit & 1, p.err, kErrWaitMma));
+                if (ok) {
+                    tc_fence_after();
+                    uint32_t lv;
+                    tmem_ld1(lane_base + S::kTmL + (oit & 1), lv);
+                    tmem_ld_wait();
+                    const float l = __uint_as_float(lv);
+                    inv = l > 0.f ? 1.f / l : 0.f;
+                }
+            }
             // Staged epilogue: the warp's 32 rows (32/pack positions x pack heads) go through
             // shared memory in 128B-swizzled boxes and leave with TMA tensor stores, so the
             // output is written as whole sectors instead of 16-byte pieces of 32 rows.  The
@@ -624,8 +667,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             if (staged) {
                 const bool bf = p.out_bf16 != 0;
                 const int box_cols = bf ? 64 : 32;
-                uint8_t *stage = smem + S::kOffStage + warp * S::kStageWarpBytes;
-                const int pos0 = (it.q0 + warp * 32) / p.pack;
+                uint8_t *stage = smem + S::kOffStage + (warp - kEpiWarp0) * S::kStageWarpBytes;
+                const int pos0 = (it.q0 + quarter * 32) / p.pack;
                 for (int c0 = 0; c0 < HD; c0 += box_cols, slot ^= 1) {   // one box per round
                     if (c0 >= p.hd) break;                                 // boxes wholly past the head dim
                     if (lane == 0 && stores_pending) bulk_wait_read1();    // this slot's last store read it
@@ -693,7 +736,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                         store_row32(p.out, orow + c * 32, rr, inv, p.out_bf16 != 0, min(32, p.hd - c * 32));
                 }
             }
-            g0 += n_tiles;
+            if (have_o) {   // every read of O has completed (tcgen05.wait::ld after each)
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&bars->o_free));
+                ++oit;
+            }
         }
         if (lane == 0 && stores_pending) bulk_wait_read0();   // staging read before the CTA exits
         __syncwarp();
