@@ -366,13 +366,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
             tma_prefetch_desc(&p.tq);
             tma_prefetch_desc(&p.tk);
             tma_prefetch_desc(&p.tv);
-            int qit = 0, g = 0;
+            int qit = 0, g = 0, gv = 0;            // Q, K and V tiles issued
+            int v_kvh = 0, v_key0 = 0, v_b = 0;   // V tile gv, owed until K tile gv + 1 is issued
             bool ok = true;
+            // Within an item V(t) follows K(t+1): K(t+1) then waits only for S(t-1), not
+            // behind V(t)'s wait for PV(t-2).  An item's last V goes before the next Q's wait.
+            auto load_v = [&]() -> bool {
+                const int st = gv & 1;
+                if (gv >= 2 &&
+                    !mbar_wait(smem_u32(&bars->v_empty[st]), ((gv >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty))
+                    return false;
+                const uint32_t vb = smem_u32(&bars->v_full[st]);
+                mbar_arrive_expect_tx(vb, S::kKvBytes);
+#pragma unroll
+                for (int sub = 0; sub < S::kSub; ++sub)
+                    tma_load_4d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb, sub * 64, v_kvh,
+                                v_key0, v_b);
+                ++gv;
+                return true;
+            };
             for (int r = 0; r < n_rounds && ok; ++r) {
                 const int k = item1_index(r);
                 if (k >= n_items) break;
                 const Item1 it = item1_geometry<BN>(p, k);
                 if (it.n_tiles == 0) continue;
+                if (gv < g && !(ok = load_v())) break;
                 // this item's Q overwrites the last one's: wait for its final S MMA
                 if (qit > 0 && !(ok = mbar_wait(smem_u32(&bars->q_empty), (qit - 1) & 1, p.err, kErrWaitTmaEmpty)))
                     break;
@@ -395,23 +413,19 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_const
                     for (int sub = 0; sub < S::kSub; ++sub)
                         tma_load_4d(smem_u32(sK + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tk, kb, sub * 64,
                                     kvh, key0, it.b);
-                    if (g >= 2 &&
-                        !(ok = mbar_wait(smem_u32(&bars->v_empty[st]), ((g >> 1) - 1) & 1, p.err, kErrWaitTmaEmpty)))
-                        break;
-                    const uint32_t vb = smem_u32(&bars->v_full[st]);
-                    mbar_arrive_expect_tx(vb, S::kKvBytes);
-#pragma unroll
-                    for (int sub = 0; sub < S::kSub; ++sub)
-                        tma_load_4d(smem_u32(sV + st * S::kKvBytes + sub * S::kKvSubBytes), &p.tv, vb, sub * 64,
-                                    kvh, key0, it.b);
+                    if (gv < g && !(ok = load_v())) break;
+                    v_kvh = kvh;
+                    v_key0 = key0;
+                    v_b = it.b;
                 }
             }
+            if (ok && gv < g) load_v();
             // Drain: whatever was issued must land before the CTA can exit.
             if (qit > 0) mbar_wait(smem_u32(&bars->q_full), (qit - 1) & 1, p.err, kErrDrain);
-            for (int j = max(0, g - 2); j < g; ++j) {
+            for (int j = max(0, g - 2); j < g; ++j)
                 if (!mbar_wait(smem_u32(&bars->k_full[j & 1]), (j >> 1) & 1, p.err, kErrDrain)) break;
+            for (int j = max(0, gv - 2); j < gv; ++j)
                 if (!mbar_wait(smem_u32(&bars->v_full[j & 1]), (j >> 1) & 1, p.err, kErrDrain)) break;
-            }
         }
     } else if (warp == kMmaWarp) {
         // ================= tcgen05 issuer: the whole warp, converged; one elected
