@@ -709,6 +709,9 @@ int decode_attention(cudaStream_t st, float *out, const void *q, int q_is_bf16, 
         return SMOL_B200_ERR_ARGS;
     const size_t need = decode_workspace_bytes(n_seqs, max_kv_len, n_heads, n_kv_heads, head_dim);
     if (!workspace || workspace_bytes < need) return SMOL_B200_ERR_WORKSPACE;
+    // The split (and merge) kernels wait (griddepcontrol.wait) before reading anything, so
+    // they may launch while the stream's previous kernel finishes.
+    PdlScope pdl(g_api_pdl);
     switch (head_dim) {
     case 64:
         return launch_decode<64>(st, out, q, q_is_bf16, k_pool, v_pool, pool_rows, seq_row0, kv_len, n_seqs,

@@ -304,6 +304,7 @@ int qknorm_rope_append(cudaStream_t st, const float *q_in, const float *k_in, co
     const long long warps = static_cast<long long>(n_tokens) * (n_heads + n_kv_heads);
     const long long blocks = (warps + kWarpsPerBlock - 1) / kWarpsPerBlock;
     if (blocks > 0x7fffffffLL) return SMOL_B200_ERR_ARGS;
+    PdlScope pdl(g_api_pdl);   // the kernel waits (griddepcontrol.wait) before reading its inputs
     const cudaError_t e = launch_kernel(
         qknorm_rope_append_kernel, dim3(static_cast<unsigned>(blocks)), dim3(kWarpsPerBlock * 32), 0, st, q_in, k_in,
         v_in, n_tokens, n_heads, n_kv_heads, head_dim, q_norm_w, k_norm_w, eps, rope_cos, rope_sin, rope_interleaved,

@@ -20,6 +20,10 @@ const bool g_pdl_enabled = [] {
     const char *e = getenv("SMOL_PDL");
     return !(e && e[0] == '0');
 }();
+const bool g_api_pdl = [] {
+    const char *e = getenv("SMOL_API_PDL");
+    return !(e && e[0] == '0');
+}();
 
 namespace {
 

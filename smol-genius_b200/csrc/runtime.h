@@ -107,9 +107,12 @@ StepPipe *step_pipe();
 // go through it call griddep_wait() before touching data of earlier kernels.
 extern thread_local bool g_pdl_scope;
 extern const bool g_pdl_enabled;
+extern const bool g_api_pdl;   // the attention entry points' own launches (SMOL_API_PDL=0: off)
 struct PdlScope {
     bool prev;
-    PdlScope() : prev(g_pdl_scope) { g_pdl_scope = g_pdl_enabled; }
+    // on: launches inside the scope use programmatic dependent launch (an enclosing scope's
+    // setting is kept when off)
+    explicit PdlScope(bool on = true) : prev(g_pdl_scope) { g_pdl_scope = prev || (on && g_pdl_enabled); }
     ~PdlScope() { g_pdl_scope = prev; }
 };
 template <typename... KArgs, typename... Args>
