@@ -515,6 +515,19 @@ static const int g_step_chunks = [] {
     const int v = e ? atoi(e) : 0;
     return v > 0 ? (v < smolb200::StepPipe::kMaxChunks ? v : smolb200::StepPipe::kMaxChunks) : 0;
 }();
+// SMOL_STEP_WEIGHTS="w0,w1,..." (measurement knob): relative chunk sizes, one per chunk.
+static const std::vector<int> g_step_weights = [] {
+    std::vector<int> w;
+    const char *e = getenv("SMOL_STEP_WEIGHTS");
+    for (const char *c = e; c && *c;) {
+        const int v = atoi(c);
+        if (v <= 0 || static_cast<int>(w.size()) >= smolb200::StepPipe::kMaxChunks) return std::vector<int>();
+        w.push_back(v);
+        while (*c && *c != ',') ++c;
+        if (*c == ',') ++c;
+    }
+    return w;
+}();
 
 int smol_b200_decode_step_host(void *stream, float *out_host, const float *q_host, const float *k_host,
                                const float *v_host, int n_seqs, int n_heads, int n_kv_heads, int head_dim,
@@ -545,10 +558,28 @@ int smol_b200_decode_step_host(void *stream, float *out_host, const float *q_hos
     // in and the result of the first copies out while the other computes (three streams).
     // More, smaller chunks measured slower end to end (cfg 2: 4 chunks 5686 GB/s, 8
     // chunks 5142, 2 chunks 5843-5916): each chunk's attention launch fills the GPU less.
+    // Two chunks, the first a quarter of the batch: only the first chunk's copy in and
+    // the last chunk's copy out are not overlapped with compute, and the copy in is twice
+    // the copy out (q, k, v against the output): cfg 2 end to end ~6.0 TB/s against
+    // ~5.8 with equal halves (weights 1,2 / 1,4 / 1,6 / 1,4,3 measured within 1 % of 1,3).
+    static const int kDefaultWeights[2] = {1, 3};
     int chunks = n_seqs >= 64 ? 2 : 1;
-    if (g_step_chunks > 0) chunks = g_step_chunks < n_seqs ? g_step_chunks : n_seqs;
+    const int *weights = chunks == 2 ? kDefaultWeights : nullptr;
+    if (g_step_chunks > 0) {
+        chunks = g_step_chunks < n_seqs ? g_step_chunks : n_seqs;
+        weights = nullptr;
+    }
+    if (!g_step_weights.empty() && static_cast<int>(g_step_weights.size()) <= n_seqs) {
+        chunks = static_cast<int>(g_step_weights.size());
+        weights = g_step_weights.data();
+    }
+    long long wsum = 0;
+    for (int c = 0; weights && c < chunks; ++c) wsum += weights[c];
     auto bound = [&](int c) {   // first sequence of chunk c
-        return static_cast<int>(static_cast<long long>(n_seqs) * c / chunks);
+        if (!weights) return static_cast<int>(static_cast<long long>(n_seqs) * c / chunks);
+        long long acc = 0;
+        for (int i = 0; i < c; ++i) acc += weights[i];
+        return static_cast<int>(static_cast<long long>(n_seqs) * acc / wsum);
     };
     const size_t qw = static_cast<size_t>(n_heads) * head_dim, kw = static_cast<size_t>(n_kv_heads) * head_dim;
     bool ok = cuda_check(cudaEventRecord(P->start, st), "record") &&          // after the caller's prior work
