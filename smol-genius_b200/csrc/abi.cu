@@ -556,12 +556,12 @@ int smol_b200_decode_step_host(void *stream, float *out_host, const float *q_hos
     std::lock_guard<std::mutex> lock(*P->mu);
     // The batch goes in two chunks of sequences from 64 on: the inputs of the second copy
     // in and the result of the first copies out while the other computes (three streams).
-    // More, smaller chunks measured slower end to end (cfg 2: 4 chunks 5686 GB/s, 8
-    // chunks 5142, 2 chunks 5843-5916): each chunk's attention launch fills the GPU less.
-    // Two chunks, the first a quarter of the batch: only the first chunk's copy in and
-    // the last chunk's copy out are not overlapped with compute, and the copy in is twice
-    // the copy out (q, k, v against the output): cfg 2 end to end ~6.0 TB/s against
-    // ~5.8 with equal halves (weights 1,2 / 1,4 / 1,6 / 1,4,3 measured within 1 % of 1,3).
+    // More, smaller chunks measured slower end to end (cfg 2 with equal chunks: 4 chunks
+    // 5686 GB/s, 8 chunks 5142, 2 chunks 5843-5916): each chunk's attention launch fills
+    // the GPU less.  The first chunk is a quarter of the batch: only its copy in and the
+    // last chunk's copy out are not overlapped with compute, and the copy in is twice the
+    // copy out (q, k, v against the output): cfg 2 end to end ~6.0 TB/s against ~5.8 with
+    // equal halves (weights 1,2 / 1,4 / 1,6 / 1,4,3 measured within 1 % of 1,3).
     static const int kDefaultWeights[2] = {1, 3};
     int chunks = n_seqs >= 64 ? 2 : 1;
     const int *weights = chunks == 2 ? kDefaultWeights : nullptr;
