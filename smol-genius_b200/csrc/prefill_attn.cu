@@ -318,6 +318,8 @@ __device__ __forceinline__ int item1_index(int r)
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p)
 {
+    griddep_wait();   // programmatic launch: nothing of earlier kernels is read before this
+    griddep_trigger();
     using S = PrefillShape<HD>;
     constexpr int BN = S::BN;
     const int n_items = p.n_qblocks * p.n_ygroups * p.batch;
@@ -987,6 +989,8 @@ __device__ __forceinline__ void produce_two_tiles(const PrefillParams &p, Bars *
 template <int HD, bool Persistent, int PolyPairs8 = PolyShare<HD>::kPairs8>
 __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_constant__ PrefillParams p)
 {
+    griddep_wait();   // programmatic launch: nothing of earlier kernels is read before this
+    griddep_trigger();
     using S = Prefill2Shape<HD>;
     constexpr int BN = S::BN;
     constexpr int ST = S::kStages;
@@ -1629,7 +1633,8 @@ int launch_prefill(cudaStream_t st, void *out, int64_t out_row_stride, int64_t o
         int grid = static_cast<int>(n_items);
         const int sms = sm_count();
         if (sms > 0 && grid > sms) grid = sms;
-        prefill_kernel<HD><<<grid, kThreads, S::kSmemBytes, st>>>(p);
+        if (launch_kernel(prefill_kernel<HD>, dim3(grid), dim3(kThreads), S::kSmemBytes, st, p) != cudaSuccess)
+            return SMOL_B200_ERR_CUDA;
     } else {
         using S2 = Prefill2Shape<HD>;
         p.pair_heads = (p.group % 2 == 0) ? 1 : 0;
@@ -1648,11 +1653,15 @@ int launch_prefill(cudaStream_t st, void *out, int64_t out_row_stride, int64_t o
             if (sms > 0 && grid > sms) grid = sms;
             const int rc = prepare_v2<HD, true>(dev);
             if (rc != SMOL_B200_OK) return rc;
-            prefill2_kernel<HD, true><<<grid, kThreads2, S2::kSmemBytes, st>>>(p);
+            if (launch_kernel(prefill2_kernel<HD, true>, dim3(grid), dim3(kThreads2), S2::kSmemBytes, st, p) !=
+                cudaSuccess)
+                return SMOL_B200_ERR_CUDA;
         } else {
             const int rc = prepare_v2<HD, false>(dev);
             if (rc != SMOL_B200_OK) return rc;
-            prefill2_kernel<HD, false><<<grid, kThreads2, S2::kSmemBytes, st>>>(p);
+            if (launch_kernel(prefill2_kernel<HD, false>, dim3(grid), dim3(kThreads2), S2::kSmemBytes, st, p) !=
+                cudaSuccess)
+                return SMOL_B200_ERR_CUDA;
         }
     }
     return cudaGetLastError() == cudaSuccess ? SMOL_B200_OK : SMOL_B200_ERR_CUDA;
@@ -1698,6 +1707,9 @@ int prefill_attention(cudaStream_t st, void *out, int64_t out_row_stride, int64_
         v, v_row_stride, v_batch_stride, batch, seq_q, seq_k, n_heads, n_kv_heads, scale,      \
         mask_kind, q_offset, prefix_len, window, softcap, window_starts, n_windows, more_outs, n_more, out_bf16, \
         head_dim
+    // the kernels wait (griddepcontrol.wait) before reading anything, so they may launch
+    // while the stream's previous kernel finishes
+    PdlScope pdl(g_api_pdl);
     switch (kernel_hd) {
     case 64: return launch_prefill<64>(SMOL_PREFILL_ARGS);
     case 128: return launch_prefill<128>(SMOL_PREFILL_ARGS);
