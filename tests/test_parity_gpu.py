@@ -682,7 +682,7 @@ def test_prefill_cfg5_full_length_sampled(cuda):
 # ---------------------------------------------------------------------------
 # The host-buffer decode step (the call bench.py's end-to-end number goes through)
 # ---------------------------------------------------------------------------
-@pytest.mark.parametrize("n", [6, 70, 130])   # 1, 2 and 4 pipelined chunks of sequences
+@pytest.mark.parametrize("n", [6, 70, 130])   # one chunk, and two pipelined chunks (a quarter, then the rest)
 def test_decode_step_host_vs_oracle(cuda, n):
     rng = np.random.default_rng(12 + n)
     hq, hkv, hd = 16, 8, 128
