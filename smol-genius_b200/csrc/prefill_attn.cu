@@ -1199,10 +1199,11 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
         bool stores_pending = false;   // lane 0: a TMA store from this warp's staging area
         int g0 = 0;
         bool ok = true;
+        int k = item_index(p, 0);
+        Item2 it_cur = k < n_items ? item_geometry<BN>(p, k) : Item2{};
         for (int r = 0; r < n_rounds && ok; ++r) {
-            const int k = item_index(p, r);
             if (k >= n_items) break;
-            const Item2 it = item_geometry<BN>(p, k);
+            const Item2 it = it_cur;
             const int n_tiles = it.n_tiles;
             const int row = it.row0[tile] + (threadIdx.x & 127);
             const bool row_valid = row < p.seq_q;
@@ -1352,6 +1353,10 @@ __global__ void __launch_bounds__(kThreads2, 1) prefill2_kernel(const __grid_con
                 mbar_arrive(p_full);
             }
             if (!ok) break;
+            // the next item's geometry while this item's last PV products run (its row
+            // ranges stay at the top of the loop: computing them here measured slower)
+            k = item_index(p, r + 1);
+            if (k < n_items) it_cur = item_geometry<BN>(p, k);
 
             // ---- epilogue: O / l -> out (fp32) ----
             bool have_o = n_tiles > 0;
