@@ -443,6 +443,22 @@ def test_prefill_cfg3_siglip_image(cuda):
     assert_close(got2[0], want, "cfg3 full mask")
 
 
+@pytest.mark.parametrize("hd", [256, 136])
+def test_prefill_windows_wide_heads_vs_oracle(cuda, hd):
+    # Window masks on the 256-wide kernel: its epilogue warps store row by row where a
+    # warp holds rows no window covers, and those rows stay untouched (attention.c:39-43).
+    rng = np.random.default_rng(hd)
+    S, h = 300, 2
+    q, k, v = (rnd_bf16(rng, S, h * hd) for _ in range(3))
+    starts = [7, 100, 230, 290]
+    ws = torch.tensor(starts, dtype=torch.int32, device=cuda)
+    got = run_prefill(cuda, q, k, v, 1, S, S, h, h, hd, 0.1, mask=smol_b200.MASK_WINDOWS, window_starts=ws)
+    want = pyoracle.oracle().bidirectional_attention(q, k, v, S, h, hd, 0.1, starts,
+                                                     out=np.full((S, h * hd), 9.0, np.float32))
+    assert_close(got[0], want, f"windows hd {hd}")
+    assert (got[0][:7] == 9.0).all() and (got[0][290:] == 9.0).all()
+
+
 def test_prefill_cfg4_prefix_lm(cuda):
     # cfg 4: prefix 320 (256 image + 64 text) bidirectional, then a causal suffix,
     # MQA 8/1, hd 256.  Oracle: the reference's two-call composition.
