@@ -59,7 +59,7 @@ struct PrefillShape {
     static constexpr int kOffQ = 0;
     static constexpr int kOffK = kOffQ + kQBytes;
     static constexpr int kOffV = kOffK + kStages * kKvBytes;
-    // Epilogue staging: 8 KB per softmax warp (two 32-row x 128-byte TMA store boxes).
+    // Epilogue staging: 8 KB per epilogue warp (two 32-row x 128-byte TMA store boxes).
     static constexpr int kStageWarpBytes = 2 * 32 * 128;
     static constexpr int kOffStage = kOffV + kStages * kKvBytes;
     static constexpr int kOffBar = kOffStage + kEpiWarps * kStageWarpBytes;
@@ -313,8 +313,9 @@ __device__ __forceinline__ int item1_index(int r)
 }
 
 // v1 (head dim 256): one 128-row query tile per work item; CTAs are persistent -- TMEM
-// is allocated once and every barrier's phase runs on across items (q_full / q_empty
-// once per item with key tiles, the K/V ring, S buffers and o_done once per key tile).
+// is allocated once and every barrier's phase runs on across items (q_full / q_empty,
+// o_final / o_free once per item with key tiles, the K/V ring, S buffers and o_done once
+// per key tile).
 template <int HD>
 __global__ void __launch_bounds__(kThreads, 1) prefill_kernel(const __grid_constant__ PrefillParams p)
 {
