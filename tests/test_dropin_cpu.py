@@ -18,8 +18,9 @@ pytestmark = pytest.mark.skipif(not all(os.path.exists(b) for b in BIN.values())
                                 reason="reference drop-in binaries not built (reference checkout absent)")
 
 
-def tokens(kind, args):
-    p = subprocess.run([BIN[kind], *map(str, args)], capture_output=True, text=True, timeout=300, check=True)
+def tokens(kind, args, env=None):
+    p = subprocess.run([BIN[kind], *map(str, args)], capture_output=True, text=True, timeout=300, check=True,
+                       env=None if env is None else {**os.environ, **env})
     return p.stdout.split()
 
 
@@ -32,6 +33,16 @@ def test_storage_precision_keeps_decisive_stream():
     ref, emul = tokens("ref", args), tokens("emul", args)
     assert len(ref) == 128 and len(set(ref)) >= 32
     assert ref == emul
+
+
+def test_warm_run_prints_the_same_stream():
+    """SMOL_DROPIN_WARM=1 (the bench's steady-state timing) runs the generation once
+    unreported, resets the cache with qkn_kv_cache_reset and prints the second run: the
+    same tokens as a first run, and only one line of them."""
+    args = (64, 16, 2, 4, 2, 1, 1)
+    cold = tokens("ref", args)
+    warm = tokens("ref", args, {"SMOL_DROPIN_WARM": "1"})
+    assert len(cold) == 16 and warm == cold
 
 
 def test_storage_precision_flips_near_tie_of_random_readout():
